@@ -1,0 +1,216 @@
+/*
+ * needle_cuda.h -- C-ABI of libneedle_cuda.so, the B200 (sm_100a) decode engine for Needle 2.
+ *
+ * The engine plugs in as a third needle.js backend: a TypeScript `CudaBackend implements
+ * InferenceBackend` (packages/needle.js/src/backends/backend.ts:83-110) whose
+ * createResidentSession() returns a `ResidentExecutionSession` (backend.ts:66-80) binds these
+ * functions through bun:ffi.  Plain C types only: no exceptions, no C++ or torch types.
+ *
+ * Conventions
+ *  - Every function returns a needle_status; the message of the last failure on the calling
+ *    thread is available from needle_cuda_last_error().
+ *  - Statuses 1..10 are NeedleErrorCode (packages/needle.js/src/errors.ts:1-11) in order, so the
+ *    adapter rethrows `new NeedleError(CODES[status - 1], needle_cuda_last_error())`.
+ *  - One context per GPU and one host thread per context.  Host pointers are borrowed for the
+ *    duration of the call only.  The context owns all device memory it allocates.
+ *  - Arithmetic follows the reference CPU backend: in NEEDLE_NUMERICS_EXACT every expression is
+ *    evaluated in binary64 in the reference's order and rounded to binary32 where the reference
+ *    stores into a Float32Array, so tokens and int8 KV codes match the CPU backend.
+ */
+#ifndef NEEDLE_CUDA_H
+#define NEEDLE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum needle_status {
+  NEEDLE_OK = 0,
+  NEEDLE_INVALID_CACT = 1,
+  NEEDLE_UNSUPPORTED_CACT = 2,
+  NEEDLE_WEIGHTS_NOT_FOUND = 3,
+  NEEDLE_WEIGHTS_INTEGRITY = 4,
+  NEEDLE_WEBGPU_UNAVAILABLE = 5,
+  NEEDLE_BACKEND_UNAVAILABLE = 6, /* also: CUDA errors, bad context, unsupported geometry */
+  NEEDLE_CONTEXT_OVERFLOW = 7,
+  NEEDLE_INVALID_TOOL_SCHEMA = 8,
+  NEEDLE_GRAMMAR_DEAD_END = 9,
+  NEEDLE_GENERATION_ABORTED = 10
+} needle_status;
+
+enum {
+  NEEDLE_NUMERICS_EXACT = 0, /* binary64 in reference order: bit-faithful to the CPU backend */
+  NEEDLE_KV_INT8 = 0,        /* RuntimeOptions.kvCache "int8" (runtime.ts:30-32) */
+};
+
+typedef struct needle_opts {
+  uint32_t struct_size; /* sizeof(needle_opts) */
+  int32_t device;       /* CUDA device ordinal */
+  int32_t max_seqs;     /* sequence slots (concurrent sequences) */
+  int32_t max_len;      /* largest maximumLength a slot accepts (<= geometry max sequence) */
+  int32_t max_sink;     /* largest sinkLength a slot accepts */
+  int32_t kv_mode;      /* NEEDLE_KV_INT8 */
+  int32_t numerics;     /* NEEDLE_NUMERICS_EXACT */
+  int32_t reserved[9];
+} needle_opts;
+
+typedef struct needle_ctx needle_ctx;
+
+/* Geometry of the opened archive (CactGeometry, packages/needle.js/src/model/cact.ts:15-35). */
+typedef struct needle_geometry {
+  int32_t vocabulary_size, model_dimension, heads, kv_heads, layers, head_dimension,
+      maximum_sequence_length, hadamard_dimension, mhc_lanes, engram_slots,
+      engram_sub_dimension, engram_tables, engram_taps, engram_dilation, kv_window, kv_bits;
+  int32_t engram_order_count, engram_orders[4], engram_site_count, engram_sites[4];
+  float rope_theta;
+  int32_t num_tensors;
+  int32_t kv_capacity; /* KV slots per sequence allocated by this context */
+} needle_geometry;
+
+/* One sequence's work in a batched step (NeedleRuntime.step / stepSelected, runtime.ts:257-583). */
+typedef struct needle_step_item {
+  int32_t seq;            /* slot in [0, max_seqs) prepared with needle_cuda_seq_reset */
+  int32_t token;          /* token consumed at the slot's current position;
+                             NEEDLE_TOKEN_PENDING takes the slot's last selected id */
+  int32_t select;         /* 1: select a token after this step (argmax / masked argmax) */
+  int32_t allowed_count;  /* -1: unmasked; >0: mask = allowed_ids[allowed_offset, +count) */
+  uint32_t allowed_offset;
+} needle_step_item;
+
+#define NEEDLE_TOKEN_PENDING (-1)
+
+/* SelectedToken (backend.ts:41-44). */
+typedef struct needle_selected {
+  int32_t id;
+  int32_t reserved;
+  double log_probability;
+} needle_selected;
+
+/* Last failure message of the calling thread ("" if none). */
+const char* needle_cuda_last_error(void);
+
+/* Fills *opts with defaults (device 0, 1 slot, max_len 2048, max_sink 160, int8, exact). */
+int needle_cuda_default_opts(needle_opts* opts);
+
+/* Parses a `.cact` archive (parseCact, cact.ts:189-562), checks the geometry this engine
+ * supports (the same gate as supportsResidentExecution, packages/needle.js/src/resident/
+ * compatibility.ts:4-40, except that kvWindow 0 is accepted), and uploads the weights to
+ * `opts->device`.  Replaces CpuBackend construction (packages/needle.js/src/backends/cpu.ts:
+ * 120-124) / createTypeGPUBackend. */
+int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, needle_ctx** out);
+
+/* InferenceBackend.dispose (backend.ts:109).  Frees every device allocation. */
+int needle_cuda_close(needle_ctx* ctx);
+
+int needle_cuda_geometry(const needle_ctx* ctx, needle_geometry* out);
+
+/* ResidentExecutionSession.reset / NeedleRuntime.reset (backend.ts:67, runtime.ts:150-225):
+ * position 0, empty history, sink = min(max(sink, 0), maximum_length).  Fails with
+ * CONTEXT_OVERFLOW when maximum_length is outside (0, geometry max] or above opts.max_len, and
+ * with BACKEND_UNAVAILABLE (the reference's "no resident execution") when sink + window exceeds
+ * the context's KV capacity. */
+int needle_cuda_seq_reset(needle_ctx* ctx, int32_t seq, int32_t maximum_length, int32_t sink_length);
+
+/* Position (tokens consumed) of a slot. */
+int needle_cuda_seq_position(const needle_ctx* ctx, int32_t seq, int32_t* position);
+
+/* One ragged batched decode step over n items (distinct slots).  For every item the slot's token
+ * runs through all layers at the slot's position, its K/V are appended to the int8 cache, and the
+ * position advances (runtime.ts:280-583).  Items with select=1 write out_selected[i]
+ * (selectToken, runtime.ts:880-899).  out_logits (n * vocabulary floats, row i for item i) may be
+ * NULL; when given, every item's logits are written (step with wantLogits).  The call is
+ * synchronous: results are in host memory on return. */
+int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n,
+                     const uint32_t* allowed_ids, size_t allowed_total,
+                     needle_selected* out_selected, float* out_logits);
+
+/* NeedleRuntime.prefill (runtime.ts:227-243) for one slot: n steps, logits of the last one
+ * written to out_logits (vocabulary floats) when non-NULL. */
+int needle_cuda_prefill(needle_ctx* ctx, int32_t seq, const int32_t* ids, int32_t n, float* out_logits);
+
+/* Copies one layer of a slot's int8 KV cache (layout of runtime.ts:666-677): codes
+ * [kv_heads][kv_allocation][head_dim], scales [kv_heads][kv_allocation], where kv_allocation is the
+ * slot's min(maximum_length, sink + window) (runtime.ts:166-170).  Any pointer may be NULL. */
+int needle_cuda_read_kv(const needle_ctx* ctx, int32_t seq, int32_t layer, int8_t* key_codes,
+                        int8_t* value_codes, float* key_scales, float* value_scales,
+                        int32_t* kv_allocation);
+
+/* Reads a slot's mHC lane state x (lanes * model_dimension floats) after its last step. */
+int needle_cuda_read_lanes(const needle_ctx* ctx, int32_t seq, float* lanes);
+
+/* InferenceBackend.matvec (backend.ts:89-93; CpuBackend.matvec cpu.ts:12-16): rows
+ * [row_start, row_start + row_count) of archive tensor `tensor` (a CQ matrix) times `batch` input
+ * vectors x (batch * input_size floats) into y (batch * row_count floats). */
+int needle_cuda_matvec(needle_ctx* ctx, int32_t tensor, int32_t row_start, int32_t row_count,
+                       const float* x, int32_t batch, float* y);
+
+/* InferenceBackend.row (backend.ts:107; dequantizeCqRow, cq.ts:243-295). */
+int needle_cuda_row(needle_ctx* ctx, int32_t tensor, int32_t row, float* out);
+
+/* ---- Device-pointer operators (isolated kernels; the caller owns every buffer). ---- */
+
+/* A Cactus-Quant matrix resident in device memory (CqMatrix, cact.ts:61-75). */
+typedef struct needle_cq_matrix {
+  const uint8_t* packed;  /* rows * row_bytes, 16-byte aligned */
+  const uint16_t* norms;  /* rows * (input_padded / group) fp16, 4-byte aligned */
+  int32_t rows;
+  int32_t input_size;
+  int32_t group_size;     /* 128 */
+  int32_t bits;           /* 2, 3, 4 or 5 (ternary record marker) */
+} needle_cq_matrix;
+
+/* cqMatvec (cq.ts:233-240) on device buffers: x is batch * input_size floats (row stride
+ * input_size), y is batch * rows floats.  `codebook` is 28 HOST floats (CQ2|CQ3|CQ4, the archive's
+ * shared codebook).  Runs on `stream` (a cudaStream_t; NULL = legacy default stream) without
+ * synchronising.  The prepared (Hadamard-rotated) activations go to a scratch buffer that the
+ * library owns, one per device, grown with cudaMalloc when a call needs more. */
+int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float* codebook, const float* x,
+                              int32_t batch, float* y, void* stream);
+
+/* Decode attention over an int8 cache with kvWindow = 0 semantics (runtime.ts:719-786) for a
+ * ragged batch, on device buffers:
+ *   q        [batch][heads * head_dim] floats
+ *   codes    [batch][kv_heads][capacity][head_dim] int8 (key_codes, value_codes)
+ *   scales   [batch][kv_heads][capacity] floats
+ *   counts   [batch] int32 visible positions (1..capacity)
+ *   out      [batch][heads * head_dim] floats
+ * heads = 8, kv_heads = 4, head_dim = 64 (the Needle 2 geometry). */
+int needle_cuda_attention_dev(const float* q, const int8_t* key_codes, const float* key_scales,
+                              const int8_t* value_codes, const float* value_scales,
+                              const int32_t* counts, int32_t batch, int32_t capacity, float* out,
+                              void* stream);
+
+/* ---- Benchmark / device-resident scheduling ---- */
+
+/* Returns the context's CUDA stream (a cudaStream_t) so callers can time on it. */
+void* needle_cuda_stream(const needle_ctx* ctx);
+
+/* Device-resident ragged decode (continuous batching without host round trips).  Loads a queue
+ * of sequences: prompt ids (concatenated, prompt_offsets has n_seqs + 1 entries) and the number
+ * of greedy tokens each generates; slots [0, min(n_slots, n_seqs)) admit the first sequences.
+ * Each needle_cuda_sched_step then runs one batched step over every busy slot: a slot consumes
+ * its next prompt token or, after the prompt, its last greedily selected token; a slot whose
+ * sequence has selected its last token admits the next queued sequence. */
+int needle_cuda_sched_load(needle_ctx* ctx, int32_t n_slots, const int32_t* prompt_offsets,
+                           const int32_t* prompt_ids, const int32_t* gen_steps, int32_t n_seqs);
+/* Enqueues `steps` device-resident steps on the context stream without synchronising. */
+int needle_cuda_sched_step(needle_ctx* ctx, int32_t steps);
+/* Synchronises and reports progress: tokens processed so far, sequences finished, and for every
+ * queued sequence its last selected token (n_seqs entries, -1 while unfinished; may be NULL). */
+int needle_cuda_sched_status(needle_ctx* ctx, int64_t* tokens_processed, int32_t* seqs_finished,
+                             int32_t* last_ids);
+
+/* Per-kernel-class timing with CUDA events on the context stream (off by default).  enable=1
+ * starts accumulating, enable=0 stops.  read fills up to n entries of (name, total ms, launches)
+ * and returns the number of classes through *count. */
+int needle_cuda_profile(needle_ctx* ctx, int32_t enable);
+int needle_cuda_profile_read(needle_ctx* ctx, int32_t n, const char** names, double* total_ms,
+                             int64_t* launches, int32_t* count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NEEDLE_CUDA_H */

@@ -1,0 +1,296 @@
+"""Host-side mirror of the needle.js backend interface over libneedle_cuda.so.
+
+needle.js is TypeScript and its runtime cannot run in this environment, so the adapter it would
+use (a bun:ffi `CudaBackend`) is mirrored here in Python with the same names,
+argument meanings and error behaviour:
+
+* `CudaBackend`         -- InferenceBackend (packages/needle.js/src/backends/backend.ts:83-110):
+                            matvec / matvec_batch / row / create_resident_session / dispose.
+                            CQ matrices are addressed by archive record index
+                            (CqMatrix.record.index, cact.ts:61-75).
+* `NeedleRuntime`       -- NeedleRuntime (packages/needle.js/src/model/runtime.ts:108-583):
+                            reset / prefill / prefill_selected / step / step_selected over one
+                            sequence slot of the engine, token loop entirely on the GPU.
+* `CudaEngine`          -- the batched engine itself: many slots stepped together (the ragged
+                            batch API that the single-sequence reference has no counterpart for).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import native
+from .native import NeedleError, check, lib, ptr
+
+
+@dataclass
+class StepRequest:
+    """One slot's work in a batched step."""
+    seq: int
+    token: int = native.TOKEN_PENDING
+    select: bool = False
+    allowed: Optional[np.ndarray] = None  # None: unmasked argmax
+
+
+class CudaEngine:
+    """One engine context on one GPU (needle_cuda_open .. needle_cuda_close)."""
+
+    def __init__(self, archive: bytes, device: int = 0, max_seqs: int = 1, max_len: int = 2048,
+                 max_sink: int = 160):
+        self._archive = np.frombuffer(archive, dtype=np.uint8)
+        opts = native.default_opts(device=device, max_seqs=max_seqs, max_len=max_len, max_sink=max_sink)
+        h = C.c_void_p()
+        check(lib().needle_cuda_open(ptr(self._archive), self._archive.size, C.byref(opts), C.byref(h)))
+        self.h = h
+        g = native.Geometry()
+        check(lib().needle_cuda_geometry(self.h, C.byref(g)))
+        self.geometry = g
+        self.vocab = g.vocabulary_size
+        self.layers = g.layers
+        self.max_seqs = max_seqs
+
+    def close(self):
+        if getattr(self, "h", None):
+            check(lib().needle_cuda_close(self.h))
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        return lib().needle_cuda_stream(self.h) or 0
+
+    def reset(self, seq: int, maximum_length: int, sink_length: int = 0):
+        check(lib().needle_cuda_seq_reset(self.h, seq, maximum_length, sink_length))
+
+    def position(self, seq: int) -> int:
+        p = C.c_int32()
+        check(lib().needle_cuda_seq_position(self.h, seq, C.byref(p)))
+        return p.value
+
+    def step(self, requests: Sequence[StepRequest], want_logits: bool = False):
+        """One batched step; returns (selected list of (id, logprob) or None per request, logits)."""
+        n = len(requests)
+        items = (native.StepItem * max(n, 1))()
+        allowed_parts, offset = [], 0
+        for i, r in enumerate(requests):
+            items[i].seq = r.seq
+            items[i].token = r.token
+            items[i].select = 1 if r.select else 0
+            if r.select and r.allowed is not None:
+                a = np.ascontiguousarray(r.allowed, dtype=np.uint32)
+                items[i].allowed_count = a.size
+                items[i].allowed_offset = offset
+                allowed_parts.append(a)
+                offset += a.size
+            else:
+                items[i].allowed_count = -1
+                items[i].allowed_offset = 0
+        allowed = np.concatenate(allowed_parts) if allowed_parts else None
+        sel = (native.Selected * max(n, 1))()
+        logits = np.zeros((n, self.vocab), dtype=np.float32) if want_logits else None
+        check(lib().needle_cuda_step(self.h, C.cast(items, C.c_void_p), n, ptr(allowed),
+                                     0 if allowed is None else allowed.size, C.cast(sel, C.c_void_p),
+                                     ptr(logits)))
+        out = [(sel[i].id, sel[i].log_probability) if r.select else None for i, r in enumerate(requests)]
+        return out, logits
+
+    def prefill(self, seq: int, ids, want_logits: bool = True):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        logits = np.zeros(self.vocab, dtype=np.float32) if want_logits else None
+        check(lib().needle_cuda_prefill(self.h, seq, ptr(ids), ids.size, ptr(logits)))
+        return logits
+
+    def read_kv(self, seq: int, layer: int):
+        g = self.geometry
+        alloc = C.c_int32()
+        check(lib().needle_cuda_read_kv(self.h, seq, layer, None, None, None, None, C.byref(alloc)))
+        a = alloc.value
+        kc = np.zeros((g.kv_heads, a, g.head_dimension), dtype=np.int8)
+        vc = np.zeros_like(kc)
+        ks = np.zeros((g.kv_heads, a), dtype=np.float32)
+        vs = np.zeros_like(ks)
+        check(lib().needle_cuda_read_kv(self.h, seq, layer, ptr(kc), ptr(vc), ptr(ks), ptr(vs), C.byref(alloc)))
+        return kc, vc, ks, vs
+
+    def read_lanes(self, seq: int):
+        out = np.zeros(self.geometry.mhc_lanes * self.geometry.model_dimension, dtype=np.float32)
+        check(lib().needle_cuda_read_lanes(self.h, seq, ptr(out)))
+        return out
+
+    def matvec(self, tensor: int, x, row_start: int = 0, row_count: Optional[int] = None):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        batch = 1 if x.ndim == 1 else x.shape[0]
+        if row_count is None:
+            raise ValueError("row_count is required")
+        y = np.zeros((batch, row_count), dtype=np.float32)
+        check(lib().needle_cuda_matvec(self.h, tensor, row_start, row_count, ptr(x), batch, ptr(y)))
+        return y[0] if x.ndim == 1 else y
+
+    def row(self, tensor: int, row: int, width: int):
+        out = np.zeros(width, dtype=np.float32)
+        check(lib().needle_cuda_row(self.h, tensor, row, ptr(out)))
+        return out
+
+    # device-resident continuous batching -------------------------------------------------
+    def sched_load(self, n_slots: int, prompts, gen_steps):
+        offsets = np.zeros(len(prompts) + 1, dtype=np.int32)
+        offsets[1:] = np.cumsum([len(p) for p in prompts])
+        flat = np.ascontiguousarray(np.concatenate(prompts) if prompts else np.zeros(0), dtype=np.int32)
+        steps = np.ascontiguousarray(gen_steps, dtype=np.int32)
+        check(lib().needle_cuda_sched_load(self.h, n_slots, ptr(offsets), ptr(flat), ptr(steps), len(prompts)))
+        self._n_seqs = len(prompts)
+
+    def sched_step(self, steps: int = 1):
+        check(lib().needle_cuda_sched_step(self.h, steps))
+
+    def sched_status(self):
+        tokens, finished = C.c_int64(), C.c_int32()
+        last = np.zeros(max(self._n_seqs, 1), dtype=np.int32)
+        check(lib().needle_cuda_sched_status(self.h, C.byref(tokens), C.byref(finished), ptr(last)))
+        return tokens.value, finished.value, last[:self._n_seqs]
+
+    # per-kernel-class event timing ----------------------------------------------------------
+    def profile(self, enable: bool):
+        check(lib().needle_cuda_profile(self.h, 1 if enable else 0))
+
+    def profile_read(self):
+        n = 16
+        names = (C.c_char_p * n)()
+        ms = (C.c_double * n)()
+        launches = (C.c_int64 * n)()
+        count = C.c_int32()
+        check(lib().needle_cuda_profile_read(self.h, n, names, ms, launches, C.byref(count)))
+        return {names[i].decode(): (ms[i], launches[i]) for i in range(count.value)}
+
+
+class CudaBackend:
+    """InferenceBackend over one engine context (backend.ts:83-110)."""
+
+    kind = "cuda"
+    name = "CUDA sm_100a (B200)"
+
+    def __init__(self, archive: bytes, device: int = 0, max_seqs: int = 1, max_len: int = 2048,
+                 max_sink: int = 160):
+        self.weights = archive
+        self.engine = CudaEngine(archive, device=device, max_seqs=max_seqs, max_len=max_len, max_sink=max_sink)
+        self._free = list(range(max_seqs))
+
+    def matvec(self, tensor: int, input, range: Optional[dict] = None):
+        """matvec(matrix, input, range?) with the matrix given by its archive record index."""
+        rows = self._rows(tensor)
+        start = (range or {}).get("rowStart", 0)
+        count = (range or {}).get("rowCount", rows - start)
+        return self.engine.matvec(tensor, input, start, count)
+
+    def matvec_batch(self, requests):
+        """matvecBatch(requests): one (tensor, input, range) per request."""
+        return [self.matvec(t, x, r) for (t, x, r) in requests]
+
+    def row(self, tensor: int, row: int):
+        return self.engine.row(tensor, row, self._width(tensor))
+
+    def create_resident_session(self) -> "CudaResidentSession":
+        if not self._free:
+            raise NeedleError("BACKEND_UNAVAILABLE", "all sequence slots of the CUDA backend are in use")
+        return CudaResidentSession(self, self._free.pop(0))
+
+    def dispose(self):
+        self.engine.close()
+
+    def _record(self, tensor):
+        import struct
+        a = self.weights
+        n, cbl = struct.unpack_from("<II", a, 4)
+        off = 120 + cbl * 4 + tensor * 44
+        dtype, rank = a[off], a[off + 1]
+        dims = struct.unpack_from("<4I", a, off + 4)
+        return dtype, dims[:rank]
+
+    def _rows(self, tensor):
+        return self._record(tensor)[1][0]
+
+    def _width(self, tensor):
+        return self._record(tensor)[1][1]
+
+
+class CudaResidentSession:
+    """ResidentExecutionSession (backend.ts:66-80) bound to one engine slot.  reset() returns True
+    for supported options and raises NeedleError(BACKEND_UNAVAILABLE) otherwise: unlike the
+    reference's optional sessions, this backend never hands the step back to a CPU loop."""
+
+    def __init__(self, backend: CudaBackend, slot: int):
+        self.backend = backend
+        self.engine = backend.engine
+        self.slot = slot
+
+    def reset(self, maximum_length: int, sink_length: int = 0, kv_cache: str = "int8",
+              collect_confidence: bool = False) -> bool:
+        if kv_cache != "int8":
+            raise NeedleError("BACKEND_UNAVAILABLE", "the CUDA backend implements the int8 KV cache")
+        self.engine.reset(self.slot, maximum_length, sink_length)
+        return True
+
+    def dispose(self):
+        self.backend._free.append(self.slot)
+
+
+class NeedleRuntime:
+    """NeedleRuntime (runtime.ts:108-583) over a CUDA resident session."""
+
+    def __init__(self, backend: CudaBackend):
+        self.backend = backend
+        self.session = backend.create_resident_session()
+        self.engine = backend.engine
+        self.slot = self.session.slot
+        self._max = 0
+
+    @property
+    def position(self) -> int:
+        return self.engine.position(self.slot)
+
+    @property
+    def maximum_length(self) -> int:
+        return self._max
+
+    def reset(self, maximum_length: int, sink_length: int = 0):
+        self.session.reset(maximum_length, sink_length)
+        self._max = maximum_length
+
+    def prefill(self, tokens) -> np.ndarray:
+        if len(tokens) == 0:
+            raise NeedleError("INVALID_CACT", "Cannot prefill an empty token sequence")
+        return self.engine.prefill(self.slot, tokens, want_logits=True)
+
+    def prefill_selected(self, tokens, allowed=None):
+        if len(tokens) == 0:
+            raise NeedleError("INVALID_CACT", "Cannot prefill an empty token sequence")
+        if len(tokens) > 1:
+            self.engine.prefill(self.slot, tokens[:-1], want_logits=False)
+        return self.step_selected(tokens[-1], allowed)
+
+    def step(self, token: int, want_logits: bool = True):
+        _, logits = self.engine.step([StepRequest(self.slot, int(token))], want_logits=want_logits)
+        return None if logits is None else logits[0]
+
+    def step_selected(self, token: int, allowed=None):
+        if allowed is not None and len(allowed) == 0:
+            raise NeedleError("INVALID_CACT", "Allowed token set is empty")
+        sel, _ = self.engine.step([StepRequest(self.slot, int(token), True, allowed)])
+        return sel[0]
+
+    def dispose(self):
+        self.session.dispose()

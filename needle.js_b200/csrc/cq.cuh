@@ -1,0 +1,86 @@
+// cq.cuh -- Cactus-Quant matrix kernels: activation prepare (per-group FWHT), batched
+// multi-matrix GEMV, and row dequantisation.
+#pragma once
+
+#include "common.cuh"
+
+namespace needle {
+
+// One matrix-times-batch job of a GEMV launch.  Rows [row_start, row_start + rows) of the matrix
+// multiply the prepared inputs x[i * x_stride ...] of every item i; row r of the job lands in
+// y[i * y_stride + r].
+struct CqJob {
+  const uint8_t* packed;   // row 0 of the matrix
+  const uint16_t* norms;   // fp16 norms of row 0
+  int32_t row_start;
+  int32_t rows;
+  int32_t in_pad;          // padded input length (multiple of 128)
+  int32_t bits;            // 2, 3, 4 or 5 (ternary)
+  int32_t row_bytes;
+  int32_t tile_begin;      // first 32-row tile of this job in the launch
+  const float* x;
+  int32_t x_stride;
+  int32_t y_stride;
+  float* y;
+};
+
+constexpr int kMaxJobs = 8;
+struct CqJobs {
+  CqJob job[kMaxJobs];
+  int32_t count;
+  int32_t total_tiles;
+};
+
+// Codebook (28 binary32 levels: CQ2 | CQ3 | CQ4) shared by every matrix of an archive.
+struct Codebook {
+  float v[28];
+};
+
+// Host launchers (cq.cu).  `n_dev` (device int, may be null) overrides `n_host` as item count so
+// that graphs and the device scheduler can size the batch on the device.
+cudaError_t launch_cq_prepare(const float* x, int32_t x_stride, int32_t input_size, int32_t in_pad,
+                              float* out, int32_t out_stride, int32_t n_host, const int32_t* n_dev,
+                              cudaStream_t s);
+cudaError_t launch_cq_gemv(const CqJobs& jobs, const Codebook& cb, int32_t n_host,
+                           const int32_t* n_dev, cudaStream_t s);
+cudaError_t launch_cq_rows(const uint8_t* packed, const uint16_t* norms, int32_t bits,
+                           int32_t row_bytes, int32_t in_pad, int32_t input_size,
+                           const int32_t* rows, int32_t n_rows, float* out, int32_t out_stride,
+                           const Codebook& cb, cudaStream_t s);
+
+// Device helpers shared with the fused per-sequence kernels ---------------------------------
+
+// Index of column `col` (within its row) of a packed CQ row (the bit layouts of
+// packages/needle.js/src/backends/cq.ts:270-284); ternary crumbs map to trit indices 3->0, 0->1,
+// 1->2, 2->3.
+__device__ __forceinline__ int cq_index(const uint8_t* rowp, int bits, int col) {
+  if (bits == 2 || bits == kTernaryBits) {
+    const int byte = rowp[col >> 2];
+    const int crumb = (byte >> ((col & 3) * 2)) & 3;
+    return bits == kTernaryBits ? (crumb == 3 ? 0 : crumb + 1) : crumb;
+  }
+  if (bits == 4) return (rowp[col >> 1] >> ((col & 1) * 4)) & 15;
+  // 3-bit bitstream: an index straddles two bytes only when its shift exceeds 5, and then the
+  // second byte lies inside the same row; otherwise the neighbour byte is masked off anyway.
+  const int bit = col * 3;
+  const int shift = bit & 7;
+  uint32_t word = rowp[bit >> 3];
+  if (shift > 5) word |= (uint32_t)rowp[(bit >> 3) + 1] << 8;
+  return (int)((word >> shift) & 7);
+}
+
+// Level of a dequantised index: the archive codebook, or for ternary rows the binary32 array
+// [-c/sqrt(g), 0, c/sqrt(g)] (cq.ts:259-262); index 3 of a ternary row reads past that array and
+// yields 0 (`codebook[index] ?? 0`).
+__device__ __forceinline__ double cq_level(const float* cb28, int bits, int index) {
+  if (bits == kTernaryBits) {
+    const double inv = 1.0 / sqrt((double)kGroup);
+    if (index == 0) return (double)f32(-kTernaryCentroid * inv);
+    if (index == 2) return (double)f32(kTernaryCentroid * inv);
+    return 0.0;
+  }
+  const int base = bits == 2 ? 0 : bits == 3 ? 4 : 12;
+  return (double)cb28[base + index];
+}
+
+}  // namespace needle

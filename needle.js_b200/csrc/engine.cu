@@ -1,0 +1,1193 @@
+// engine.cu -- host side of libneedle_cuda.so: `.cact` parsing, weight upload, per-slot state,
+// batched step orchestration, device scheduler, and the C-ABI of include/needle_cuda.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/needle_cuda.h"
+#include "engine.cuh"
+
+using namespace needle;
+
+namespace {
+
+thread_local std::string g_error;
+
+struct Failure {
+  int code;
+  std::string msg;
+};
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw Failure{code, msg}; }
+inline void require(bool ok, int code, const std::string& msg) {
+  if (!ok) fail(code, msg);
+}
+inline void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess)
+    fail(NEEDLE_BACKEND_UNAVAILABLE, std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
+}
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    return NEEDLE_OK;
+  } catch (const Failure& e) {
+    g_error = e.msg;
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    g_error = "host allocation failed";
+    return NEEDLE_BACKEND_UNAVAILABLE;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return NEEDLE_BACKEND_UNAVAILABLE;
+  }
+}
+
+// ------------------------------------------------------------------ archive view (host)
+
+inline uint32_t u32le(const uint8_t* p) {
+  return uint32_t(p[0]) | (uint32_t(p[1]) << 8) | (uint32_t(p[2]) << 16) | (uint32_t(p[3]) << 24);
+}
+inline uint64_t u64le(const uint8_t* p) { return uint64_t(u32le(p)) | (uint64_t(u32le(p + 4)) << 32); }
+inline float f32le(const uint8_t* p) {
+  uint32_t b = u32le(p);
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
+
+float half_to_float(uint16_t h) {  // exact binary16 -> binary32 widening
+  const uint32_t sign = uint32_t(h & 0x8000u) << 16;
+  int32_t exponent = (h >> 10) & 0x1f;
+  uint32_t mantissa = h & 0x3ffu, bits;
+  if (exponent == 0) {
+    if (mantissa == 0) {
+      bits = sign;
+    } else {
+      exponent = 127 - 15 + 1;
+      while ((mantissa & 0x400u) == 0) {
+        mantissa <<= 1;
+        exponent--;
+      }
+      bits = sign | (uint32_t(exponent) << 23) | ((mantissa & 0x3ffu) << 13);
+    }
+  } else if (exponent == 0x1f) {
+    bits = sign | 0x7f800000u | (mantissa << 13);
+  } else {
+    bits = sign | (uint32_t(exponent - 15 + 127) << 23) | (mantissa << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+struct Record {
+  int dtype = 0, rank = 0;
+  int64_t shape[4] = {0, 0, 0, 0};
+  uint64_t offset = 0, length = 0;
+  uint32_t group = 0, bits = 0;
+  // CQ derived
+  int64_t rows = 0, input = 0, in_pad = 0, row_bytes = 0, packed_bytes = 0;
+};
+
+struct Archive {
+  const uint8_t* b = nullptr;
+  size_t n = 0;
+  uint32_t hdr[30];
+  float rope_theta = 0;
+  std::vector<float> codebook;
+  std::vector<Record> rec;
+
+  std::vector<float> dense(int i) const {
+    const Record& r = rec[i];
+    int64_t count = 1;
+    for (int d = 0; d < r.rank; d++) count *= r.shape[d];
+    std::vector<float> out(count);
+    for (int64_t k = 0; k < count; k++) {
+      const uint8_t* p = b + r.offset + (r.dtype == 1 ? k * 2 : k * 4);
+      out[k] = r.dtype == 1 ? half_to_float(uint16_t(p[0] | (p[1] << 8))) : f32le(p);
+    }
+    return out;
+  }
+};
+
+// Parses and validates the archive like parseCact (packages/needle.js/src/model/cact.ts:189-401).
+void parse_archive(const uint8_t* b, size_t n, Archive& A) {
+  auto in_range = [&](uint64_t off, uint64_t len) { return off <= n && len <= n - off; };
+  require(in_range(0, 120), NEEDLE_INVALID_CACT,
+          "CACT header points outside the " + std::to_string(n) + "-byte archive");
+  A.b = b;
+  A.n = n;
+  for (int i = 0; i < 29; i++) A.hdr[i] = u32le(b + i * 4);
+  A.rope_theta = f32le(b + 29 * 4);
+  require(A.hdr[0] == 0x05e12a83u, NEEDLE_INVALID_CACT, "Invalid .cact tag");
+  const uint32_t tensors = A.hdr[1], cb_len = A.hdr[2];
+  require(tensors > 0, NEEDLE_INVALID_CACT, "The .cact archive has no tensors");
+  require(cb_len >= 28, NEEDLE_UNSUPPORTED_CACT,
+          "Needle 2 requires the CQ2/CQ3/CQ4 codebook (28 entries); archive has " + std::to_string(cb_len));
+  require(A.hdr[19] <= 4 && A.hdr[24] <= 4, NEEDLE_UNSUPPORTED_CACT,
+          "The current .cact format supports at most four engram orders and sites");
+  require(A.hdr[6] > 0 && A.hdr[5] > 0, NEEDLE_INVALID_CACT,
+          "Model geometry contains a zero-sized vocabulary or hidden dimension");
+  require(A.hdr[7] > 0 && A.hdr[8] > 0 && A.hdr[7] % A.hdr[8] == 0, NEEDLE_UNSUPPORTED_CACT,
+          "Attention heads must be a positive multiple of KV heads");
+  require((A.hdr[12] & (A.hdr[12] - 1)) == 0, NEEDLE_UNSUPPORTED_CACT, "Hadamard dimension must be a power of two");
+  require(in_range(120, uint64_t(cb_len) * 4), NEEDLE_INVALID_CACT, "CQ codebook points outside the archive");
+  A.codebook.resize(cb_len);
+  for (uint32_t i = 0; i < cb_len; i++) A.codebook[i] = f32le(b + 120 + i * 4);
+  const uint64_t dir = 120 + uint64_t(cb_len) * 4;
+  require(in_range(dir, uint64_t(tensors) * 44), NEEDLE_INVALID_CACT, "Tensor directory points outside the archive");
+  A.rec.resize(tensors);
+  for (uint32_t i = 0; i < tensors; i++) {
+    const uint8_t* r = b + dir + uint64_t(i) * 44;
+    Record& R = A.rec[i];
+    R.dtype = r[0];
+    R.rank = r[1];
+    require(R.rank <= 4, NEEDLE_UNSUPPORTED_CACT, "Tensor " + std::to_string(i) + " has more than four dimensions");
+    for (int d = 0; d < R.rank; d++) R.shape[d] = u32le(r + 4 + d * 4);
+    R.offset = u64le(r + 20);
+    R.length = u64le(r + 28);
+    R.group = u32le(r + 36);
+    R.bits = u32le(r + 40);
+    require(in_range(R.offset, R.length), NEEDLE_INVALID_CACT,
+            "Tensor " + std::to_string(i) + " points outside the archive");
+    int64_t count = 1;
+    for (int d = 0; d < R.rank; d++) count *= R.shape[d];
+    if (R.dtype == 1) {
+      require(R.length == uint64_t(count) * 2, NEEDLE_INVALID_CACT,
+              "FP16 tensor " + std::to_string(i) + " has an inconsistent byte length");
+    } else if (R.dtype == 2) {
+      require(R.length == uint64_t(count) * 4, NEEDLE_INVALID_CACT,
+              "FP32 tensor " + std::to_string(i) + " has an inconsistent byte length");
+    } else if (R.dtype == 3) {
+      require(R.rank == 2, NEEDLE_INVALID_CACT, "CQ tensor " + std::to_string(i) + " is not a matrix");
+      require(R.group > 0 && (R.group & (R.group - 1)) == 0, NEEDLE_UNSUPPORTED_CACT,
+              "CQ tensor " + std::to_string(i) + " has non-power-of-two group");
+      require(R.bits == 2 || R.bits == 3 || R.bits == 4 || R.bits == 5, NEEDLE_UNSUPPORTED_CACT,
+              "CQ tensor " + std::to_string(i) + " uses unsupported record width " + std::to_string(R.bits));
+      R.rows = R.shape[0];
+      R.input = R.shape[1];
+      R.in_pad = (R.input + R.group - 1) / R.group * R.group;
+      const int64_t pb = R.bits == 5 ? 2 : R.bits;
+      require((R.in_pad * pb) % 8 == 0, NEEDLE_INVALID_CACT, "CQ tensor has a fractional packed row size");
+      R.row_bytes = R.in_pad * pb / 8;
+      R.packed_bytes = R.rows * R.row_bytes;
+      const uint64_t norms = uint64_t(R.rows) * (R.in_pad / R.group);
+      require(R.length == uint64_t(R.packed_bytes) + norms * 2, NEEDLE_INVALID_CACT,
+              "CQ tensor " + std::to_string(i) + " has an inconsistent packed/norm length");
+    } else if (R.dtype != 4) {
+      fail(NEEDLE_UNSUPPORTED_CACT, "Tensor " + std::to_string(i) + " uses unknown dtype " + std::to_string(R.dtype));
+    }
+  }
+}
+
+// Canonical tensor order (cact.ts:403-536): embedding, 14 per layer, 9 mHC, 4 per engram site,
+// final norm, optional probe heads, RAW tokenizer.
+struct Roles {
+  int embedding = -1;
+  struct L {
+    int norm_input, q, k, v, qn, kn, gate, o, post, attn_gate, pre_had, d1, d2, d3;
+  };
+  std::vector<L> layers;
+  int a_pre, a_post, a_res, b_pre, b_post, b_res, phi_pre, phi_post, phi_res;
+  struct E {
+    int tables, k, v, taps;
+  };
+  std::vector<E> sites;
+  int final_norm;
+};
+
+Roles assign_roles(const Archive& A) {
+  Roles R;
+  size_t cur = 0;
+  auto take = [&](int want, const std::string& name) {
+    require(cur < A.rec.size(), NEEDLE_INVALID_CACT, "Archive ended before " + name);
+    const int i = int(cur++);
+    if (want == 3) require(A.rec[i].dtype == 3, NEEDLE_INVALID_CACT, name + " must be a Cactus-Quant matrix");
+    if (want == 1) require(A.rec[i].dtype == 1 || A.rec[i].dtype == 2, NEEDLE_INVALID_CACT, name + " must be an FP16/FP32 tensor");
+    return i;
+  };
+  R.embedding = take(3, "embedding");
+  const int L = int(A.hdr[9]);
+  for (int l = 0; l < L; l++) {
+    const std::string p = "layer " + std::to_string(l);
+    Roles::L x;
+    x.norm_input = take(1, p + " input norm");
+    x.q = take(3, p + " query projection");
+    x.k = take(3, p + " key projection");
+    x.v = take(3, p + " value projection");
+    x.qn = take(1, p + " query norm");
+    x.kn = take(1, p + " key norm");
+    x.gate = take(3, p + " gate projection");
+    x.o = take(3, p + " output projection");
+    x.post = take(1, p + " post-attention norm");
+    x.attn_gate = take(1, p + " attention gate");
+    x.pre_had = take(1, p + " pre-Hadamard norm");
+    x.d1 = take(1, p + " Hadamard d1");
+    x.d2 = take(1, p + " Hadamard d2");
+    x.d3 = take(1, p + " Hadamard d3");
+    R.layers.push_back(x);
+  }
+  R.a_pre = take(1, "mHC a_pre");
+  R.a_post = take(1, "mHC a_post");
+  R.a_res = take(1, "mHC a_res");
+  R.b_pre = take(1, "mHC b_pre");
+  R.b_post = take(1, "mHC b_post");
+  R.b_res = take(1, "mHC b_res");
+  R.phi_pre = take(3, "mHC phi_pre");
+  R.phi_post = take(3, "mHC phi_post");
+  R.phi_res = take(3, "mHC phi_res");
+  for (uint32_t s = 0; s < A.hdr[24]; s++) {
+    const std::string p = "engram " + std::to_string(s);
+    Roles::E e;
+    e.tables = take(3, p + " tables");
+    e.k = take(3, p + " key projection");
+    e.v = take(3, p + " value projection");
+    e.taps = take(1, p + " taps");
+    R.sites.push_back(e);
+  }
+  R.final_norm = take(1, "final norm");
+  bool tokenizer = false;
+  for (size_t i = cur; i < A.rec.size(); i++)
+    if (A.rec[i].dtype == 4) tokenizer = true;
+  require(tokenizer, NEEDLE_INVALID_CACT, "Archive does not contain its RAW SentencePiece tokenizer");
+  return R;
+}
+
+struct SlotHost {
+  bool ready = false;
+  int32_t max_len = 0, sink = 0, kv_alloc = 0, position = 0;
+};
+
+struct ProfEntry {
+  int cls;
+  cudaEvent_t a, b;
+};
+
+const char* kProfNames[] = {"embed", "gemv_engram", "layer", "gemv_qkvg", "attention", "gemv_o",
+                            "gemv_vocab", "finish", "sched", "copy"};
+constexpr int kProfClasses = 10;
+enum { P_EMBED, P_GEMV_ENGRAM, P_LAYER, P_GEMV_QKVG, P_ATTN, P_GEMV_O, P_GEMV_VOCAB, P_FINISH, P_SCHED, P_COPY };
+
+}  // namespace
+
+void needle::set_last_error(const char* msg) { g_error = msg ? msg : ""; }
+
+struct needle_ctx {
+  needle_opts opts{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<uint8_t> bytes;  // archive copy (host)
+  Archive A;
+  Roles roles;
+  std::vector<void*> allocs;
+  std::vector<CqMat> cq;  // per archive tensor (CQ tensors only)
+  ModelView mv{};
+  SlotView sv{};
+  StepView stv{};
+  std::vector<CqMat> lq, lk, lv, lg, lo;
+  std::vector<CqMat> ek, ev;
+  int32_t* d_counts = nullptr;  // [0] n_items, [1] n_select
+  std::vector<SlotHost> slots;
+  // pinned staging
+  DevItem* h_items = nullptr;
+  int32_t* h_counts = nullptr;
+  int32_t* h_ids = nullptr;
+  double* h_logprob = nullptr;
+  uint32_t* d_allowed = nullptr;
+  size_t allowed_cap = 0;
+  // scheduler
+  SchedView sched{};
+  bool sched_loaded = false;
+  std::vector<void*> sched_allocs;
+  // matvec API scratch
+  float* d_mv_x = nullptr;
+  float* d_mv_xp = nullptr;
+  float* d_mv_y = nullptr;
+  size_t mv_cap = 0;
+  int32_t* d_rows = nullptr;
+  float* d_row_out = nullptr;
+  // profiling
+  bool profiling = false;
+  std::vector<ProfEntry> prof_pending;
+  std::vector<cudaEvent_t> event_pool;
+  double prof_ms[kProfClasses] = {0};
+  int64_t prof_n[kProfClasses] = {0};
+
+  template <class T>
+  T* dalloc(size_t count, bool zero = true) {
+    void* p = nullptr;
+    cuda_check(cudaMalloc(&p, std::max<size_t>(count * sizeof(T), 16)), "cudaMalloc");
+    allocs.push_back(p);
+    if (zero) cuda_check(cudaMemset(p, 0, std::max<size_t>(count * sizeof(T), 16)), "cudaMemset");
+    return static_cast<T*>(p);
+  }
+
+  cudaEvent_t get_event() {
+    if (!event_pool.empty()) {
+      cudaEvent_t e = event_pool.back();
+      event_pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e;
+    cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+    return e;
+  }
+  void prof_drain() {
+    if (prof_pending.empty()) return;
+    cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+    for (auto& p : prof_pending) {
+      float ms = 0;
+      cuda_check(cudaEventElapsedTime(&ms, p.a, p.b), "cudaEventElapsedTime");
+      prof_ms[p.cls] += ms;
+      prof_n[p.cls] += 1;
+      event_pool.push_back(p.a);
+      event_pool.push_back(p.b);
+    }
+    prof_pending.clear();
+  }
+  // Runs `launch` bracketed by events when profiling.
+  template <class F>
+  void timed(int cls, F&& launch) {
+    if (!profiling) {
+      cuda_check(launch(), kProfNames[cls]);
+      return;
+    }
+    cudaEvent_t a = get_event(), b = get_event();
+    cuda_check(cudaEventRecord(a, stream), "cudaEventRecord");
+    cuda_check(launch(), kProfNames[cls]);
+    cuda_check(cudaEventRecord(b, stream), "cudaEventRecord");
+    prof_pending.push_back({cls, a, b});
+    if (prof_pending.size() > 4096) prof_drain();
+  }
+};
+
+namespace {
+
+CqMat upload_cq(needle_ctx& C, int i) {
+  const Record& R = C.A.rec[i];
+  CqMat m;
+  uint8_t* packed = C.dalloc<uint8_t>(size_t(R.packed_bytes) + 64);  // zero tail
+  uint16_t* norms = C.dalloc<uint16_t>(size_t(R.length - R.packed_bytes) / 2 + 8, false);
+  cuda_check(cudaMemcpy(packed, C.A.b + R.offset, R.packed_bytes, cudaMemcpyHostToDevice), "upload");
+  cuda_check(cudaMemcpy(norms, C.A.b + R.offset + R.packed_bytes, R.length - R.packed_bytes,
+                        cudaMemcpyHostToDevice), "upload");
+  m.packed = packed;
+  m.norms = norms;
+  m.rows = int32_t(R.rows);
+  m.input_size = int32_t(R.input);
+  m.in_pad = int32_t(R.in_pad);
+  m.bits = int32_t(R.bits);
+  m.row_bytes = int32_t(R.row_bytes);
+  return m;
+}
+
+const float* upload_floats(needle_ctx& C, const std::vector<float>& v) {
+  float* d = C.dalloc<float>(v.size(), false);
+  cuda_check(cudaMemcpy(d, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice), "upload");
+  return d;
+}
+
+std::vector<float> pack_layers(const needle_ctx& C, int Roles::L::*field, size_t expect) {
+  std::vector<float> out;
+  for (const auto& L : C.roles.layers) {
+    std::vector<float> v = C.A.dense(L.*field);
+    require(v.size() == expect, NEEDLE_UNSUPPORTED_CACT, "Unexpected dense tensor length");
+    out.insert(out.end(), v.begin(), v.end());
+  }
+  return out;
+}
+
+void check_geometry(const needle_ctx& C) {
+  const Archive& A = C.A;
+  const uint32_t* h = A.hdr;
+  auto gate = [&](bool ok, const std::string& what) {
+    require(ok, NEEDLE_BACKEND_UNAVAILABLE, "CUDA backend does not support this geometry: " + what);
+  };
+  gate(h[6] == kDim && h[10] == kHeadDim && h[7] == kHeads && h[8] == kKvHeads && h[13] == kLanes &&
+           h[12] == kHadamard,
+       "needs d=512, head_dim=64, 8 query / 4 KV heads, 4 lanes, Hadamard 512");
+  const Roles& R = C.roles;
+  auto cqr = [&](int i) -> const Record& { return A.rec[i]; };
+  for (const auto& L : R.layers) {
+    gate(cqr(L.q).rows == 512 && cqr(L.q).input == 512 && cqr(L.k).rows == 256 && cqr(L.k).input == 512 &&
+             cqr(L.v).rows == 256 && cqr(L.v).input == 512 && cqr(L.gate).rows == 512 &&
+             cqr(L.gate).input == 512 && cqr(L.o).rows == 512 && cqr(L.o).input == 512,
+         "projection shapes");
+    for (int t : {L.q, L.k, L.v, L.gate, L.o}) gate(cqr(t).group == kGroup, "CQ group size 128");
+  }
+  gate(cqr(R.embedding).group == kGroup, "CQ group size 128");
+  const int L = int(h[9]);
+  gate(cqr(R.phi_pre).rows == int64_t(L) * 4 && cqr(R.phi_pre).input == kLaneWidth &&
+           cqr(R.phi_post).rows == int64_t(L) * 4 && cqr(R.phi_post).input == kLaneWidth &&
+           cqr(R.phi_res).rows == int64_t(L) * 16 && cqr(R.phi_res).input == kLaneWidth,
+       "mHC phi shapes");
+  for (int t : {R.phi_pre, R.phi_post, R.phi_res}) gate(cqr(t).group == kGroup, "CQ group size 128");
+  if (!R.sites.empty()) {
+    gate(h[16] >= 1 && h[16] <= kMaxTables && h[15] == kGroup && h[16] * h[15] == kDim,
+         "engram tables x sub-dimension must be 512 with 128-wide rows");
+    gate(h[19] >= 1 && h[16] % h[19] == 0, "engram table count divisible by order count");
+    uint32_t mo = 1;
+    for (uint32_t i = 0; i < h[19]; i++) {
+      gate(h[20 + i] >= 1 && h[20 + i] <= 4, "engram orders in 1..4");
+      mo = std::max(mo, h[20 + i]);
+    }
+    gate((h[17] - 1) * mo + 1 <= 64 && h[17] >= 1, "engram ring depth");
+    for (const auto& e : R.sites) {
+      gate(cqr(e.tables).input == kGroup && cqr(e.tables).group == kGroup &&
+               cqr(e.tables).rows == int64_t(h[16]) * h[14],
+           "engram table shape");
+      gate(cqr(e.k).rows == 512 && cqr(e.k).input == 512 && cqr(e.v).rows == 512 && cqr(e.v).input == 512 &&
+               cqr(e.k).group == kGroup && cqr(e.v).group == kGroup,
+           "engram projection shape");
+    }
+    for (uint32_t s = 0; s < h[24]; s++) gate(h[25 + s] < uint32_t(L), "engram site layer");
+  }
+  gate(cqr(R.embedding).rows == h[5] && cqr(R.embedding).input == kDim, "embedding shape");
+}
+
+void build_model(needle_ctx& C) {
+  Archive& A = C.A;
+  const uint32_t* h = A.hdr;
+  const int L = int(h[9]);
+  C.cq.assign(A.rec.size(), CqMat{});
+  for (size_t i = 0; i < A.rec.size(); i++)
+    if (A.rec[i].dtype == 3) C.cq[i] = upload_cq(C, int(i));
+  ModelView& m = C.mv;
+  const Roles& R = C.roles;
+  m.embedding = C.cq[R.embedding];
+  m.phi_pre = C.cq[R.phi_pre];
+  m.phi_post = C.cq[R.phi_post];
+  m.phi_res = C.cq[R.phi_res];
+  m.layers = L;
+  m.vocab = int32_t(h[5]);
+  m.kv_window = int32_t(h[3]);
+  m.max_seq = int32_t(h[11]);
+  m.n_sites = int32_t(R.sites.size());
+  for (int s = 0; s < m.n_sites; s++) {
+    m.sites[s] = int32_t(h[25 + s]);
+    m.engram_tables[s] = C.cq[R.sites[s].tables];
+    C.ek.push_back(C.cq[R.sites[s].k]);
+    C.ev.push_back(C.cq[R.sites[s].v]);
+  }
+  m.n_orders = int32_t(h[19]);
+  m.max_order = 1;
+  for (int i = 0; i < m.n_orders; i++) {
+    m.orders[i] = int32_t(h[20 + i]);
+    m.max_order = std::max(m.max_order, m.orders[i]);
+  }
+  m.n_tables = int32_t(h[16]);
+  m.engram_slots = int32_t(h[14]);
+  m.engram_sub = int32_t(h[15]);
+  m.taps = int32_t(h[17]);
+  for (const auto& Lr : R.layers) {
+    C.lq.push_back(C.cq[Lr.q]);
+    C.lk.push_back(C.cq[Lr.k]);
+    C.lv.push_back(C.cq[Lr.v]);
+    C.lg.push_back(C.cq[Lr.gate]);
+    C.lo.push_back(C.cq[Lr.o]);
+  }
+  m.norm_input = upload_floats(C, pack_layers(C, &Roles::L::norm_input, kDim));
+  m.query_norm = upload_floats(C, pack_layers(C, &Roles::L::qn, kHeadDim));
+  m.key_norm = upload_floats(C, pack_layers(C, &Roles::L::kn, kHeadDim));
+  m.post_norm = upload_floats(C, pack_layers(C, &Roles::L::post, kDim));
+  m.pre_had_norm = upload_floats(C, pack_layers(C, &Roles::L::pre_had, kDim));
+  m.d1 = upload_floats(C, pack_layers(C, &Roles::L::d1, kHadamard));
+  m.d2 = upload_floats(C, pack_layers(C, &Roles::L::d2, kHadamard));
+  m.d3 = upload_floats(C, pack_layers(C, &Roles::L::d3, kHadamard));
+  {
+    std::vector<float> g;
+    for (const auto& Lr : R.layers) {
+      std::vector<float> v = A.dense(Lr.attn_gate);
+      g.push_back(v.empty() ? 0.0f : v[0]);
+    }
+    m.attn_gate = upload_floats(C, g);
+  }
+  auto dense_n = [&](int i, size_t n, const char* what) {
+    std::vector<float> v = A.dense(i);
+    require(v.size() >= n, NEEDLE_INVALID_CACT, std::string(what) + " is too short");
+    return v;
+  };
+  m.a_pre = upload_floats(C, dense_n(R.a_pre, L, "mHC a_pre"));
+  m.a_post = upload_floats(C, dense_n(R.a_post, L, "mHC a_post"));
+  m.a_res = upload_floats(C, dense_n(R.a_res, L, "mHC a_res"));
+  m.b_pre = upload_floats(C, dense_n(R.b_pre, size_t(L) * 4, "mHC b_pre"));
+  m.b_post = upload_floats(C, dense_n(R.b_post, size_t(L) * 4, "mHC b_post"));
+  m.b_res = upload_floats(C, dense_n(R.b_res, size_t(L) * 16, "mHC b_res"));
+  {
+    std::vector<float> taps;
+    for (const auto& e : R.sites) {
+      std::vector<float> v = dense_n(e.taps, size_t(m.taps) * kDim, "engram taps");
+      taps.insert(taps.end(), v.begin(), v.begin() + size_t(m.taps) * kDim);
+    }
+    if (taps.empty()) taps.push_back(0.0f);
+    m.taps_w = upload_floats(C, taps);
+  }
+  m.final_norm = upload_floats(C, dense_n(R.final_norm, kDim, "final norm"));
+  // RoPE angles in binary64 exactly as applyRope (math.ts:104-108) evaluates them.
+  {
+    const double theta = double(A.rope_theta);
+    std::vector<double> cs(size_t(m.max_seq) * 32), sn(size_t(m.max_seq) * 32);
+    for (int p = 0; p < m.max_seq; p++)
+      for (int d = 0; d < 32; d++) {
+        const double frequency = std::pow(theta, -(2.0 * d) / double(kHeadDim));
+        const double angle = double(p) * frequency;
+        cs[size_t(p) * 32 + d] = std::cos(angle);
+        sn[size_t(p) * 32 + d] = std::sin(angle);
+      }
+    double* dc = C.dalloc<double>(cs.size(), false);
+    double* ds = C.dalloc<double>(sn.size(), false);
+    cuda_check(cudaMemcpy(dc, cs.data(), cs.size() * 8, cudaMemcpyHostToDevice), "upload");
+    cuda_check(cudaMemcpy(ds, sn.data(), sn.size() * 8, cudaMemcpyHostToDevice), "upload");
+    m.rope_cos = dc;
+    m.rope_sin = ds;
+  }
+  for (int i = 0; i < 28; i++) m.cb.v[i] = A.codebook[i];
+}
+
+void build_state(needle_ctx& C) {
+  const needle_opts& o = C.opts;
+  const ModelView& m = C.mv;
+  const int S = o.max_seqs, L = m.layers;
+  const int window = m.kv_window;
+  const int capacity = window > 0 ? std::min(o.max_len, o.max_sink + window) : o.max_len;
+  SlotView& sv = C.sv;
+  sv.capacity = capacity;
+  sv.layers = L;
+  const int depth = (m.taps - 1) * m.max_order + 1;
+  sv.x = C.dalloc<float>(size_t(S) * kLaneWidth);
+  sv.ring = C.dalloc<float>(size_t(S) * std::max(1, m.n_sites) * depth * kDim);
+  const size_t heads = size_t(S) * L * kKvHeads * capacity;
+  sv.kcodes = C.dalloc<int8_t>(heads * kHeadDim);
+  sv.vcodes = C.dalloc<int8_t>(heads * kHeadDim);
+  sv.kscale = C.dalloc<float>(heads);
+  sv.vscale = C.dalloc<float>(heads);
+  sv.seq = C.dalloc<SeqState>(S);
+  C.slots.assign(S, SlotHost{});
+  StepView& st = C.stv;
+  const size_t B = size_t(S);
+  st.items = C.dalloc<DevItem>(B);
+  C.d_counts = C.dalloc<int32_t>(4);
+  st.n_items = C.d_counts;
+  st.n_select = C.d_counts + 1;
+  const int ns = std::max(1, m.n_sites);
+  st.prep_engram = C.dalloc<float>(B * ns * kDim);
+  st.engram_kv = C.dalloc<float>(B * ns * 2 * kDim);
+  st.engram_val = C.dalloc<float>(B * ns * kDim);
+  st.update = C.dalloc<float>(B * kDim);
+  st.block = C.dalloc<float>(B * kDim);
+  st.prep_a = C.dalloc<float>(B * kDim);
+  st.qkvg = C.dalloc<float>(B * 1536);
+  st.prep_o = C.dalloc<float>(B * kDim);
+  st.proj = C.dalloc<float>(B * kDim);
+  st.route = C.dalloc<float>(B * 20);
+  st.prep_f = C.dalloc<float>(B * kDim);
+  st.logits = C.dalloc<float>(B * size_t(m.vocab));
+  st.out_id = C.dalloc<int32_t>(B);
+  st.out_logprob = C.dalloc<double>(B);
+  C.allowed_cap = 1 << 16;
+  C.d_allowed = C.dalloc<uint32_t>(C.allowed_cap);
+  st.allowed = C.d_allowed;
+  cuda_check(cudaMallocHost(&C.h_items, B * sizeof(DevItem)), "cudaMallocHost");
+  cuda_check(cudaMallocHost(&C.h_counts, 4 * sizeof(int32_t)), "cudaMallocHost");
+  cuda_check(cudaMallocHost(&C.h_ids, B * sizeof(int32_t)), "cudaMallocHost");
+  cuda_check(cudaMallocHost(&C.h_logprob, B * sizeof(double)), "cudaMallocHost");
+  cuda_check(configure_step_kernels(capacity), "cudaFuncSetAttribute");
+}
+
+// Builds the GEMV job list for matrices sharing one input (same bits per launch).
+void add_job(CqJobs& J, const CqMat& M, int row_start, int rows, const float* x, int x_stride, float* y,
+             int y_stride) {
+  CqJob& j = J.job[J.count++];
+  j.packed = M.packed;
+  j.norms = M.norms;
+  j.row_start = row_start;
+  j.rows = rows;
+  j.in_pad = M.in_pad;
+  j.bits = M.bits;
+  j.row_bytes = M.row_bytes;
+  j.tile_begin = J.total_tiles;
+  j.x = x;
+  j.x_stride = x_stride;
+  j.y = y;
+  j.y_stride = y_stride;
+  J.total_tiles += (rows + 31) / 32;
+}
+
+struct JobSpec {
+  CqMat M;
+  int row_start, rows;
+  const float* x;
+  int x_stride;
+  float* y;
+  int y_stride;
+};
+
+// Launches the jobs grouped by record width (one GEMV launch per width present).
+void run_gemv(needle_ctx& C, int cls, const std::vector<JobSpec>& specs, int n_host, const int32_t* n_dev) {
+  for (int bits : {2, 3, 4, 5}) {
+    CqJobs J{};
+    for (const auto& s : specs)
+      if (s.M.bits == bits) {
+        require(J.count < kMaxJobs, NEEDLE_BACKEND_UNAVAILABLE, "too many GEMV jobs");
+        add_job(J, s.M, s.row_start, s.rows, s.x, s.x_stride, s.y, s.y_stride);
+      }
+    if (J.count == 0) continue;
+    C.timed(cls, [&] { return launch_cq_gemv(J, C.mv.cb, n_host, n_dev, C.stream); });
+  }
+}
+
+// The kernel sequence of one batched step for up to n_host items (device counts in d_counts).
+void enqueue_step(needle_ctx& C, int n_host, bool any_select, const SchedView* sched) {
+  const ModelView& m = C.mv;
+  const SlotView& sv = C.sv;
+  const StepView& st = C.stv;
+  const int32_t* n_dev = st.n_items;
+  C.timed(P_EMBED, [&] { return launch_embed(m, sv, st, n_host, C.stream); });
+  if (m.n_sites > 0) {
+    std::vector<JobSpec> jobs;
+    for (int s = 0; s < m.n_sites; s++) {
+      jobs.push_back({C.ek[s], 0, 512, st.prep_engram + s * kDim, m.n_sites * kDim,
+                      st.engram_kv + (s * 2) * kDim, m.n_sites * 2 * kDim});
+      jobs.push_back({C.ev[s], 0, 512, st.prep_engram + s * kDim, m.n_sites * kDim,
+                      st.engram_kv + (s * 2 + 1) * kDim, m.n_sites * 2 * kDim});
+    }
+    run_gemv(C, P_GEMV_ENGRAM, jobs, n_host, n_dev);
+  }
+  for (int l = 0; l <= m.layers; l++) {
+    C.timed(P_LAYER, [&] { return launch_layer(m, sv, st, l, n_host, C.stream); });
+    if (l == m.layers) break;
+    run_gemv(C, P_GEMV_QKVG,
+             {{C.lq[l], 0, 512, st.prep_a, kDim, st.qkvg, 1536},
+              {C.lk[l], 0, 256, st.prep_a, kDim, st.qkvg + 512, 1536},
+              {C.lv[l], 0, 256, st.prep_a, kDim, st.qkvg + 768, 1536},
+              {C.lg[l], 0, 512, st.prep_a, kDim, st.qkvg + 1024, 1536}},
+             n_host, n_dev);
+    C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, C.stream); });
+    run_gemv(C, P_GEMV_O, {{C.lo[l], 0, 512, st.prep_o, kDim, st.proj, kDim}}, n_host, n_dev);
+  }
+  if (any_select)
+    run_gemv(C, P_GEMV_VOCAB, {{m.embedding, 0, m.vocab, st.prep_f, kDim, st.logits, m.vocab}}, n_host,
+             st.n_select);
+  C.timed(P_FINISH, [&] { return launch_finish(m, sv, st, n_host, sched, C.stream); });
+}
+
+needle_ctx* ctx_of(needle_ctx* c) {
+  require(c != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null needle context");
+  cuda_check(cudaSetDevice(c->device), "cudaSetDevice");
+  return c;
+}
+
+void destroy(needle_ctx* C) {
+  if (!C) return;
+  cudaSetDevice(C->device);
+  if (C->stream) cudaStreamSynchronize(C->stream);
+  for (auto& p : C->prof_pending) {
+    cudaEventDestroy(p.a);
+    cudaEventDestroy(p.b);
+  }
+  for (auto e : C->event_pool) cudaEventDestroy(e);
+  for (void* p : C->sched_allocs) cudaFree(p);
+  for (void* p : C->allocs) cudaFree(p);
+  if (C->d_mv_x) cudaFree(C->d_mv_x);
+  if (C->d_mv_xp) cudaFree(C->d_mv_xp);
+  if (C->d_mv_y) cudaFree(C->d_mv_y);
+  if (C->d_rows) cudaFree(C->d_rows);
+  if (C->d_row_out) cudaFree(C->d_row_out);
+  if (C->h_items) cudaFreeHost(C->h_items);
+  if (C->h_counts) cudaFreeHost(C->h_counts);
+  if (C->h_ids) cudaFreeHost(C->h_ids);
+  if (C->h_logprob) cudaFreeHost(C->h_logprob);
+  if (C->stream) cudaStreamDestroy(C->stream);
+  delete C;
+}
+
+// Grows the matvec API buffers.
+void ensure_mv(needle_ctx& C, size_t floats) {
+  if (floats <= C.mv_cap) return;
+  for (float** p : {&C.d_mv_x, &C.d_mv_xp, &C.d_mv_y})
+    if (*p) {
+      cudaFree(*p);
+      *p = nullptr;
+    }
+  cuda_check(cudaMalloc(&C.d_mv_x, floats * 4), "cudaMalloc");
+  cuda_check(cudaMalloc(&C.d_mv_xp, floats * 4), "cudaMalloc");
+  cuda_check(cudaMalloc(&C.d_mv_y, floats * 4), "cudaMalloc");
+  C.mv_cap = floats;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ C-ABI
+
+extern "C" {
+
+const char* needle_cuda_last_error(void) { return g_error.c_str(); }
+
+int needle_cuda_default_opts(needle_opts* o) {
+  return guarded([&] {
+    require(o != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null options");
+    std::memset(o, 0, sizeof(*o));
+    o->struct_size = sizeof(needle_opts);
+    o->device = 0;
+    o->max_seqs = 1;
+    o->max_len = 2048;
+    o->max_sink = 160;
+    o->kv_mode = NEEDLE_KV_INT8;
+    o->numerics = NEEDLE_NUMERICS_EXACT;
+  });
+}
+
+int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, needle_ctx** out) {
+  needle_ctx* C = nullptr;
+  const int rc = guarded([&] {
+    require(out != nullptr && cact != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+    *out = nullptr;
+    C = new needle_ctx();
+    if (opts) {
+      require(opts->struct_size == sizeof(needle_opts), NEEDLE_BACKEND_UNAVAILABLE, "needle_opts size mismatch");
+      C->opts = *opts;
+    } else {
+      needle_cuda_default_opts(&C->opts);
+    }
+    const needle_opts& o = C->opts;
+    require(o.kv_mode == NEEDLE_KV_INT8, NEEDLE_BACKEND_UNAVAILABLE, "only the int8 KV cache is implemented");
+    require(o.numerics == NEEDLE_NUMERICS_EXACT, NEEDLE_BACKEND_UNAVAILABLE, "unknown numerics mode");
+    require(o.max_seqs >= 1 && o.max_seqs <= 65536, NEEDLE_BACKEND_UNAVAILABLE, "max_seqs out of range");
+    require(o.max_sink >= 0 && o.max_len >= 1, NEEDLE_BACKEND_UNAVAILABLE, "max_len / max_sink out of range");
+    int devices = 0;
+    cuda_check(cudaGetDeviceCount(&devices), "cudaGetDeviceCount");
+    require(o.device >= 0 && o.device < devices, NEEDLE_BACKEND_UNAVAILABLE,
+            "CUDA device " + std::to_string(o.device) + " is not available");
+    C->device = o.device;
+    cuda_check(cudaSetDevice(C->device), "cudaSetDevice");
+    cudaDeviceProp prop;
+    cuda_check(cudaGetDeviceProperties(&prop, C->device), "cudaGetDeviceProperties");
+    require(prop.major == 10 && prop.minor == 0, NEEDLE_BACKEND_UNAVAILABLE,
+            std::string("libneedle_cuda is built for sm_100a (B200); device is ") + prop.name);
+    C->bytes.assign(cact, cact + n);
+    parse_archive(C->bytes.data(), C->bytes.size(), C->A);
+    C->roles = assign_roles(C->A);
+    check_geometry(*C);
+    require(int64_t(o.max_len) <= int64_t(C->A.hdr[11]), NEEDLE_CONTEXT_OVERFLOW,
+            "max_len exceeds the model's maximum sequence length");
+    cuda_check(cudaStreamCreateWithFlags(&C->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    build_model(*C);
+    build_state(*C);
+    cuda_check(cudaDeviceSynchronize(), "upload");
+    *out = C;
+  });
+  if (rc != NEEDLE_OK && C) destroy(C);
+  return rc;
+}
+
+int needle_cuda_close(needle_ctx* ctx) {
+  return guarded([&] {
+    require(ctx != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null needle context");
+    destroy(ctx);
+  });
+}
+
+int needle_cuda_geometry(const needle_ctx* ctx, needle_geometry* g) {
+  return guarded([&] {
+    require(ctx && g, NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+    const uint32_t* h = ctx->A.hdr;
+    std::memset(g, 0, sizeof(*g));
+    g->kv_window = int32_t(h[3]);
+    g->kv_bits = int32_t(h[4]);
+    g->vocabulary_size = int32_t(h[5]);
+    g->model_dimension = int32_t(h[6]);
+    g->heads = int32_t(h[7]);
+    g->kv_heads = int32_t(h[8]);
+    g->layers = int32_t(h[9]);
+    g->head_dimension = int32_t(h[10]);
+    g->maximum_sequence_length = int32_t(h[11]);
+    g->hadamard_dimension = int32_t(h[12]);
+    g->mhc_lanes = int32_t(h[13]);
+    g->engram_slots = int32_t(h[14]);
+    g->engram_sub_dimension = int32_t(h[15]);
+    g->engram_tables = int32_t(h[16]);
+    g->engram_taps = int32_t(h[17]);
+    g->engram_dilation = int32_t(h[18]);
+    g->engram_order_count = int32_t(h[19]);
+    for (int i = 0; i < 4; i++) g->engram_orders[i] = int32_t(h[20 + i]);
+    g->engram_site_count = int32_t(h[24]);
+    for (int i = 0; i < 4; i++) g->engram_sites[i] = int32_t(h[25 + i]);
+    g->rope_theta = ctx->A.rope_theta;
+    g->num_tensors = int32_t(ctx->A.rec.size());
+    g->kv_capacity = ctx->sv.capacity;
+  });
+}
+
+int needle_cuda_seq_reset(needle_ctx* ctx, int32_t seq, int32_t maximum_length, int32_t sink_length) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    require(seq >= 0 && seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
+    require(maximum_length > 0 && maximum_length <= C.mv.max_seq, NEEDLE_CONTEXT_OVERFLOW,
+            "Runtime length " + std::to_string(maximum_length) + " is outside model limit " +
+                std::to_string(C.mv.max_seq));
+    require(maximum_length <= C.opts.max_len, NEEDLE_CONTEXT_OVERFLOW,
+            "Runtime length exceeds the context's max_len");
+    const int32_t sink = std::min(std::max(sink_length, 0), maximum_length);
+    const int window = C.mv.kv_window;
+    const int32_t kv_alloc = window > 0 ? std::min(maximum_length, sink + window) : maximum_length;
+    require(kv_alloc <= C.sv.capacity, NEEDLE_BACKEND_UNAVAILABLE,
+            "sink + window exceeds the context's KV capacity (raise max_sink / max_len)");
+    SeqState st{};
+    st.position = 0;
+    st.sink = sink;
+    st.max_len = maximum_length;
+    st.kv_alloc = kv_alloc;
+    cuda_check(cudaMemcpyAsync(C.sv.seq + seq, &st, sizeof(st), cudaMemcpyHostToDevice, C.stream), "reset");
+    cuda_check(cudaStreamSynchronize(C.stream), "reset");
+    SlotHost& h = C.slots[seq];
+    h.ready = true;
+    h.max_len = maximum_length;
+    h.sink = sink;
+    h.kv_alloc = kv_alloc;
+    h.position = 0;
+  });
+}
+
+int needle_cuda_seq_position(const needle_ctx* ctx, int32_t seq, int32_t* position) {
+  return guarded([&] {
+    require(ctx && position, NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+    require(seq >= 0 && seq < ctx->opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
+    *position = ctx->slots[seq].position;
+  });
+}
+
+int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, const uint32_t* allowed_ids,
+                     size_t allowed_total, needle_selected* out_selected, float* out_logits) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    require(n >= 0 && n <= C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "item count out of range");
+    if (n == 0) return;
+    require(items != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null items");
+    std::vector<char> seen(C.opts.max_seqs, 0);
+    const int V = C.mv.vocab;
+    int n_sel = 0;
+    bool any_sel = out_logits != nullptr;
+    for (int i = 0; i < n; i++) {
+      const needle_step_item& it = items[i];
+      require(it.seq >= 0 && it.seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
+      require(!seen[it.seq], NEEDLE_BACKEND_UNAVAILABLE, "a slot appears twice in one step");
+      seen[it.seq] = 1;
+      const SlotHost& h = C.slots[it.seq];
+      require(h.ready, NEEDLE_INVALID_CACT, "Call runtime.reset() before decoding");
+      require(h.position < h.max_len, NEEDLE_CONTEXT_OVERFLOW,
+              "Position " + std::to_string(h.position) + " reached runtime limit " + std::to_string(h.max_len));
+      require(it.token == NEEDLE_TOKEN_PENDING || (it.token >= 0 && it.token < V), NEEDLE_INVALID_CACT,
+              "Token " + std::to_string(it.token) + " is outside the vocabulary");
+      if (it.select) {
+        require(out_selected != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "selection requested without output");
+        if (it.allowed_count >= 0) {
+          require(it.allowed_count > 0, NEEDLE_INVALID_CACT, "Allowed token set is empty");
+          require(allowed_ids != nullptr && uint64_t(it.allowed_offset) + uint64_t(it.allowed_count) <= allowed_total,
+                  NEEDLE_INVALID_CACT, "allowed ids out of range");
+          for (int32_t k = 0; k < it.allowed_count; k++)
+            require(allowed_ids[it.allowed_offset + k] < uint32_t(V), NEEDLE_INVALID_CACT,
+                    "Token " + std::to_string(allowed_ids[it.allowed_offset + k]) + " is outside logits");
+        }
+        n_sel++;
+        any_sel = true;
+      }
+    }
+    // internal order: items that need logits first
+    const bool all_logits = out_logits != nullptr;
+    int pos_sel = 0, pos_rest = all_logits ? 0 : n_sel;
+    std::vector<int> order(n);
+    for (int i = 0; i < n; i++) {
+      const needle_step_item& it = items[i];
+      const bool first = all_logits || it.select;
+      const int k = all_logits ? pos_sel++ : (first ? pos_sel++ : pos_rest++);
+      order[i] = k;
+      DevItem d{};
+      d.slot = it.seq;
+      d.token = it.token;
+      d.select = it.select ? 1 : 0;
+      d.allowed_count = it.select ? it.allowed_count : -1;
+      d.allowed_offset = it.allowed_offset;
+      d.position = C.slots[it.seq].position;
+      d.out_index = i;
+      C.h_items[k] = d;
+    }
+    if (allowed_total > 0 && allowed_ids) {
+      if (allowed_total > C.allowed_cap) {
+        uint32_t* p = nullptr;
+        cuda_check(cudaMalloc(&p, allowed_total * 4), "cudaMalloc");
+        C.allocs.push_back(p);
+        C.d_allowed = p;
+        C.allowed_cap = allowed_total;
+        C.stv.allowed = p;
+      }
+      cuda_check(cudaMemcpyAsync(C.d_allowed, allowed_ids, allowed_total * 4, cudaMemcpyHostToDevice, C.stream),
+                 "allowed upload");
+    }
+    C.h_counts[0] = n;
+    C.h_counts[1] = all_logits ? n : n_sel;
+    C.timed(P_COPY, [&] {
+      cudaError_t e = cudaMemcpyAsync(C.stv.items, C.h_items, size_t(n) * sizeof(DevItem), cudaMemcpyHostToDevice,
+                                      C.stream);
+      if (e != cudaSuccess) return e;
+      return cudaMemcpyAsync(C.d_counts, C.h_counts, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, C.stream);
+    });
+    enqueue_step(C, n, any_sel, nullptr);
+    if (n_sel > 0 || all_logits) {
+      const int ns = all_logits ? n : n_sel;
+      cuda_check(cudaMemcpyAsync(C.h_ids, C.stv.out_id, size_t(ns) * 4, cudaMemcpyDeviceToHost, C.stream), "readback");
+      cuda_check(cudaMemcpyAsync(C.h_logprob, C.stv.out_logprob, size_t(ns) * 8, cudaMemcpyDeviceToHost, C.stream),
+                 "readback");
+    }
+    if (all_logits) {
+      for (int i = 0; i < n; i++)
+        cuda_check(cudaMemcpyAsync(out_logits + size_t(i) * V, C.stv.logits + size_t(order[i]) * V, size_t(V) * 4,
+                                   cudaMemcpyDeviceToHost, C.stream),
+                   "logits readback");
+    }
+    cuda_check(cudaStreamSynchronize(C.stream), "step");
+    for (int i = 0; i < n; i++) {
+      C.slots[items[i].seq].position++;
+      if (items[i].select) {
+        out_selected[i].id = C.h_ids[order[i]];
+        out_selected[i].reserved = 0;
+        out_selected[i].log_probability = C.h_logprob[order[i]];
+      }
+    }
+  });
+}
+
+int needle_cuda_prefill(needle_ctx* ctx, int32_t seq, const int32_t* ids, int32_t n, float* out_logits) {
+  return guarded([&] {
+    require(ids != nullptr && n > 0, NEEDLE_INVALID_CACT, "Cannot prefill an empty token sequence");
+    needle_ctx& C = *ctx_of(ctx);
+    require(seq >= 0 && seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
+    const SlotHost& h = C.slots[seq];
+    require(h.max_len - h.position >= n, NEEDLE_CONTEXT_OVERFLOW,
+            "Prompt has " + std::to_string(n) + " tokens but runtime holds " + std::to_string(h.max_len));
+    for (int32_t i = 0; i < n; i++) {
+      needle_step_item it{seq, ids[i], 0, -1, 0};
+      const bool last = i == n - 1 && out_logits != nullptr;
+      const int rc = needle_cuda_step(ctx, &it, 1, nullptr, 0, nullptr, last ? out_logits : nullptr);
+      if (rc != NEEDLE_OK) fail(rc, g_error);
+    }
+  });
+}
+
+int needle_cuda_read_kv(const needle_ctx* ctx, int32_t seq, int32_t layer, int8_t* key_codes, int8_t* value_codes,
+                        float* key_scales, float* value_scales, int32_t* kv_allocation) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(const_cast<needle_ctx*>(ctx));
+    require(seq >= 0 && seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
+    require(layer >= 0 && layer < C.mv.layers, NEEDLE_INVALID_CACT, "Layer out of range");
+    const SlotHost& h = C.slots[seq];
+    require(h.ready, NEEDLE_INVALID_CACT, "KV cache was not allocated");
+    if (kv_allocation) *kv_allocation = h.kv_alloc;
+    const int cap = C.sv.capacity;
+    for (int head = 0; head < kKvHeads; head++) {
+      const size_t base = ((size_t(seq) * C.mv.layers + layer) * kKvHeads + head) * cap;
+      if (key_codes)
+        cuda_check(cudaMemcpy(key_codes + size_t(head) * h.kv_alloc * kHeadDim, C.sv.kcodes + base * kHeadDim,
+                              size_t(h.kv_alloc) * kHeadDim, cudaMemcpyDeviceToHost), "read_kv");
+      if (value_codes)
+        cuda_check(cudaMemcpy(value_codes + size_t(head) * h.kv_alloc * kHeadDim, C.sv.vcodes + base * kHeadDim,
+                              size_t(h.kv_alloc) * kHeadDim, cudaMemcpyDeviceToHost), "read_kv");
+      if (key_scales)
+        cuda_check(cudaMemcpy(key_scales + size_t(head) * h.kv_alloc, C.sv.kscale + base, size_t(h.kv_alloc) * 4,
+                              cudaMemcpyDeviceToHost), "read_kv");
+      if (value_scales)
+        cuda_check(cudaMemcpy(value_scales + size_t(head) * h.kv_alloc, C.sv.vscale + base, size_t(h.kv_alloc) * 4,
+                              cudaMemcpyDeviceToHost), "read_kv");
+    }
+  });
+}
+
+int needle_cuda_read_lanes(const needle_ctx* ctx, int32_t seq, float* lanes) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(const_cast<needle_ctx*>(ctx));
+    require(seq >= 0 && seq < C.opts.max_seqs && lanes, NEEDLE_BACKEND_UNAVAILABLE, "bad argument");
+    cuda_check(cudaMemcpy(lanes, C.sv.x + size_t(seq) * kLaneWidth, kLaneWidth * 4, cudaMemcpyDeviceToHost),
+               "read_lanes");
+  });
+}
+
+int needle_cuda_matvec(needle_ctx* ctx, int32_t tensor, int32_t row_start, int32_t row_count, const float* x,
+                       int32_t batch, float* y) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    require(tensor >= 0 && size_t(tensor) < C.cq.size() && C.cq[tensor].packed, NEEDLE_INVALID_CACT,
+            "Tensor " + std::to_string(tensor) + " must be a Cactus-Quant matrix");
+    const CqMat& M = C.cq[tensor];
+    require(row_start >= 0 && row_count >= 0 && int64_t(row_start) + row_count <= M.rows, NEEDLE_INVALID_CACT,
+            "Invalid matrix row range " + std::to_string(row_start) + ":" + std::to_string(row_start + row_count));
+    require(batch >= 0 && (batch == 0 || (x && y)), NEEDLE_BACKEND_UNAVAILABLE, "bad batch");
+    require(C.A.rec[tensor].group == uint32_t(kGroup), NEEDLE_BACKEND_UNAVAILABLE, "CQ group size 128 only");
+    if (batch == 0 || row_count == 0) return;
+    const size_t need = std::max(size_t(batch) * M.in_pad, size_t(batch) * row_count);
+    ensure_mv(C, need);
+    cuda_check(cudaMemcpyAsync(C.d_mv_x, x, size_t(batch) * M.input_size * 4, cudaMemcpyHostToDevice, C.stream),
+               "matvec upload");
+    cuda_check(launch_cq_prepare(C.d_mv_x, M.input_size, M.input_size, M.in_pad, C.d_mv_xp, M.in_pad, batch, nullptr,
+                                 C.stream),
+               "prepare");
+    run_gemv(C, P_GEMV_VOCAB, {{M, row_start, row_count, C.d_mv_xp, M.in_pad, C.d_mv_y, row_count}}, batch, nullptr);
+    cuda_check(cudaMemcpyAsync(y, C.d_mv_y, size_t(batch) * row_count * 4, cudaMemcpyDeviceToHost, C.stream),
+               "matvec readback");
+    cuda_check(cudaStreamSynchronize(C.stream), "matvec");
+  });
+}
+
+int needle_cuda_row(needle_ctx* ctx, int32_t tensor, int32_t row, float* out) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    require(tensor >= 0 && size_t(tensor) < C.cq.size() && C.cq[tensor].packed, NEEDLE_INVALID_CACT,
+            "Tensor " + std::to_string(tensor) + " must be a Cactus-Quant matrix");
+    const CqMat& M = C.cq[tensor];
+    require(row >= 0 && row < M.rows, NEEDLE_INVALID_CACT, "Matrix row " + std::to_string(row) + " is out of range");
+    require(out != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null output");
+    require(C.A.rec[tensor].group == uint32_t(kGroup), NEEDLE_BACKEND_UNAVAILABLE, "CQ group size 128 only");
+    if (!C.d_rows) {
+      cuda_check(cudaMalloc(&C.d_rows, 16), "cudaMalloc");
+      cuda_check(cudaMalloc(&C.d_row_out, size_t(kLaneWidth) * 4 * 4), "cudaMalloc");
+    }
+    require(M.in_pad <= kLaneWidth * 4, NEEDLE_BACKEND_UNAVAILABLE, "row too wide");
+    cuda_check(cudaMemcpyAsync(C.d_rows, &row, 4, cudaMemcpyHostToDevice, C.stream), "row upload");
+    cuda_check(launch_cq_rows(M.packed, M.norms, M.bits, M.row_bytes, M.in_pad, M.input_size, C.d_rows, 1,
+                              C.d_row_out, M.in_pad, C.mv.cb, C.stream),
+               "row");
+    cuda_check(cudaMemcpyAsync(out, C.d_row_out, size_t(M.input_size) * 4, cudaMemcpyDeviceToHost, C.stream),
+               "row readback");
+    cuda_check(cudaStreamSynchronize(C.stream), "row");
+  });
+}
+
+void* needle_cuda_stream(const needle_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+int needle_cuda_sched_load(needle_ctx* ctx, int32_t n_slots, const int32_t* prompt_offsets, const int32_t* prompt_ids,
+                           const int32_t* gen_steps, int32_t n_seqs) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    require(n_slots >= 1 && n_slots <= C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "n_slots out of range");
+    require(n_seqs >= 0 && prompt_offsets && gen_steps && (n_seqs == 0 || prompt_ids), NEEDLE_BACKEND_UNAVAILABLE,
+            "bad queue");
+    const int window = C.mv.kv_window;
+    for (int s = 0; s < n_seqs; s++) {
+      const int len = prompt_offsets[s + 1] - prompt_offsets[s];
+      require(len >= 1 && gen_steps[s] >= 1, NEEDLE_INVALID_CACT, "empty prompt or generation");
+      const int max_len = len + gen_steps[s];
+      require(max_len <= C.mv.max_seq && max_len <= C.opts.max_len, NEEDLE_CONTEXT_OVERFLOW,
+              "sequence exceeds the maximum length");
+      const int kv_alloc = window > 0 ? std::min(max_len, window) : max_len;
+      require(kv_alloc <= C.sv.capacity, NEEDLE_BACKEND_UNAVAILABLE, "sequence exceeds the KV capacity");
+    }
+    for (int s = 0; s < n_seqs; s++)
+      for (int32_t k = prompt_offsets[s]; k < prompt_offsets[s + 1]; k++)
+        require(prompt_ids[k] >= 0 && prompt_ids[k] < C.mv.vocab, NEEDLE_INVALID_CACT, "prompt token outside vocabulary");
+    cuda_check(cudaStreamSynchronize(C.stream), "sched_load");
+    for (void* p : C.sched_allocs) cudaFree(p);
+    C.sched_allocs.clear();
+    auto alloc = [&](size_t bytes) {
+      void* p = nullptr;
+      cuda_check(cudaMalloc(&p, std::max<size_t>(bytes, 16)), "cudaMalloc");
+      C.sched_allocs.push_back(p);
+      return p;
+    };
+    const size_t total = size_t(prompt_offsets[n_seqs]);
+    int32_t* d_off = static_cast<int32_t*>(alloc(size_t(n_seqs + 1) * 4));
+    int32_t* d_ids = static_cast<int32_t*>(alloc(total * 4));
+    int32_t* d_gen = static_cast<int32_t*>(alloc(size_t(n_seqs) * 4));
+    int32_t* d_ctr = static_cast<int32_t*>(alloc(64));
+    int32_t* d_last = static_cast<int32_t*>(alloc(size_t(std::max(n_seqs, 1)) * 4));
+    cuda_check(cudaMemcpy(d_off, prompt_offsets, size_t(n_seqs + 1) * 4, cudaMemcpyHostToDevice), "sched upload");
+    if (total) cuda_check(cudaMemcpy(d_ids, prompt_ids, total * 4, cudaMemcpyHostToDevice), "sched upload");
+    cuda_check(cudaMemcpy(d_gen, gen_steps, size_t(n_seqs) * 4, cudaMemcpyHostToDevice), "sched upload");
+    cuda_check(cudaMemset(d_ctr, 0, 64), "sched init");
+    cuda_check(cudaMemset(d_last, 0xff, size_t(std::max(n_seqs, 1)) * 4), "sched init");
+    // all slots idle
+    cuda_check(cudaMemset(C.sv.seq, 0, size_t(C.opts.max_seqs) * sizeof(SeqState)), "sched init");
+    for (auto& h : C.slots) h = SlotHost{};
+    SchedView& q = C.sched;
+    q.prompt_offsets = d_off;
+    q.prompt_ids = d_ids;
+    q.gen_steps = d_gen;
+    q.n_seqs = n_seqs;
+    q.n_slots = n_slots;
+    q.next_seq = d_ctr;
+    q.finished = d_ctr + 1;
+    q.processed = reinterpret_cast<int64_t*>(d_ctr + 2);
+    q.last_ids = d_last;
+    C.sched_loaded = true;
+    cuda_check(launch_sched_admit(C.sv, q, window, C.stream), "admit");
+    cuda_check(cudaStreamSynchronize(C.stream), "sched_load");
+  });
+}
+
+int needle_cuda_sched_step(needle_ctx* ctx, int32_t steps) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    require(C.sched_loaded, NEEDLE_BACKEND_UNAVAILABLE, "no scheduler queue loaded");
+    for (int32_t k = 0; k < steps; k++) {
+      C.timed(P_SCHED, [&] {
+        cudaError_t e = launch_sched_admit(C.sv, C.sched, C.mv.kv_window, C.stream);
+        if (e != cudaSuccess) return e;
+        return launch_sched(C.sv, C.stv, C.sched, C.d_counts, C.d_counts + 1, C.stream);
+      });
+      enqueue_step(C, C.sched.n_slots, true, &C.sched);
+    }
+  });
+}
+
+int needle_cuda_sched_status(needle_ctx* ctx, int64_t* tokens_processed, int32_t* seqs_finished, int32_t* last_ids) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    require(C.sched_loaded, NEEDLE_BACKEND_UNAVAILABLE, "no scheduler queue loaded");
+    cuda_check(cudaStreamSynchronize(C.stream), "sched_status");
+    int32_t ctr[4];
+    cuda_check(cudaMemcpy(ctr, C.sched.next_seq, 16, cudaMemcpyDeviceToHost), "sched_status");
+    int64_t processed = 0;
+    std::memcpy(&processed, ctr + 2, 8);
+    if (tokens_processed) *tokens_processed = processed;
+    if (seqs_finished) *seqs_finished = ctr[1];
+    if (last_ids && C.sched.n_seqs > 0)
+      cuda_check(cudaMemcpy(last_ids, C.sched.last_ids, size_t(C.sched.n_seqs) * 4, cudaMemcpyDeviceToHost),
+                 "sched_status");
+  });
+}
+
+int needle_cuda_profile(needle_ctx* ctx, int32_t enable) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    if (enable && !C.profiling) {
+      C.prof_drain();
+      for (int i = 0; i < kProfClasses; i++) {
+        C.prof_ms[i] = 0;
+        C.prof_n[i] = 0;
+      }
+    }
+    C.profiling = enable != 0;
+  });
+}
+
+int needle_cuda_profile_read(needle_ctx* ctx, int32_t n, const char** names, double* total_ms, int64_t* launches,
+                             int32_t* count) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    C.prof_drain();
+    if (count) *count = kProfClasses;
+    for (int i = 0; i < std::min<int32_t>(n, kProfClasses); i++) {
+      if (names) names[i] = kProfNames[i];
+      if (total_ms) total_ms[i] = C.prof_ms[i];
+      if (launches) launches[i] = C.prof_n[i];
+    }
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,129 @@
+// engine.cuh -- device-side data layout of the decode engine and the launchers of its fused
+// per-sequence kernels (layer.cu).
+#pragma once
+
+#include <string>
+
+#include "cq.cuh"
+
+namespace needle {
+
+// A Cactus-Quant matrix in device memory (CqMatrix, packages/needle.js/src/model/cact.ts:61-75).
+struct CqMat {
+  const uint8_t* packed = nullptr;
+  const uint16_t* norms = nullptr;
+  int32_t rows = 0, input_size = 0, in_pad = 0, bits = 0, row_bytes = 0;
+};
+
+// Read-only model parameters (device pointers).  Per-layer dense vectors are packed [L][n].
+struct ModelView {
+  CqMat embedding, phi_pre, phi_post, phi_res;
+  CqMat engram_tables[kMaxSites];
+  int32_t layers, vocab, kv_window, max_seq;
+  int32_t n_sites, sites[kMaxSites];
+  int32_t n_orders, orders[4], max_order;
+  int32_t n_tables, engram_slots, engram_sub, taps;
+  const float *norm_input, *query_norm, *key_norm, *post_norm, *pre_had_norm;  // [L][512|64]
+  const float *d1, *d2, *d3;                                                    // [L][512]
+  const float* attn_gate;                                                       // [L]
+  const float *a_pre, *a_post, *a_res, *b_pre, *b_post, *b_res;
+  const float* taps_w;      // [sites][taps][512]
+  const float* final_norm;  // [512]
+  const double *rope_cos, *rope_sin;  // [max_seq][32], computed on the host in binary64
+  Codebook cb;
+};
+
+// Per-slot sequence state (NeedleRuntime fields, runtime.ts:113-133), device-authoritative.
+struct SeqState {
+  int32_t position;    // tokens consumed
+  int32_t sink;        // sinkLength
+  int32_t max_len;     // maximumLength
+  int32_t kv_alloc;    // min(maximumLength, sink + window) or maximumLength (runtime.ts:166-170)
+  int32_t pending;     // last selected token
+  int32_t hist[3];     // previous tokens, most recent first (engram n-grams, runtime.ts:788-818)
+  // device scheduler
+  int32_t busy, seq_id, prompt_off, prompt_len, gen_target, gen_done;
+};
+
+// Slot-indexed device state.
+struct SlotView {
+  int32_t capacity;     // KV positions per (slot, layer, kv head)
+  int32_t layers;
+  float* x;             // [S][4][512] mHC lanes
+  float* ring;          // [S][sites][10][512] engram value ring
+  int8_t* kcodes;       // [S][L][4][capacity][64]
+  int8_t* vcodes;
+  float* kscale;        // [S][L][4][capacity]
+  float* vscale;
+  SeqState* seq;        // [S]
+};
+
+// One resolved item of a step (internal order: selecting items first).
+struct DevItem {
+  int32_t slot;
+  int32_t token;            // >= 0, or NEEDLE_TOKEN_PENDING (-1) until k_embed resolves it
+  int32_t select;
+  int32_t allowed_count;    // -1 unmasked
+  uint32_t allowed_offset;
+  int32_t position;         // filled by k_embed
+  int32_t out_index;        // caller's index
+  int32_t pad;
+};
+
+// Step scratch, indexed by internal item index.
+struct StepView {
+  DevItem* items;
+  const int32_t* n_items;   // device count (all items)
+  const int32_t* n_select;  // device count of selecting items (a prefix of items)
+  const uint32_t* allowed;  // allowed ids
+  float* prep_engram;       // [B][sites][512]
+  float* engram_kv;         // [B][sites][2][512]  (K projection, V projection)
+  float* engram_val;        // [B][sites][512]      convolved values
+  float* update;            // [B][512]
+  float* block;             // [B][512]
+  float* prep_a;            // [B][512]  prepared attention input
+  float* qkvg;              // [B][1536] q | k | v | gate
+  float* prep_o;            // [B][512]  prepared output-projection input
+  float* proj;              // [B][512]
+  float* route;             // [B][20]   hPost[4] | routing[16]
+  float* prep_f;            // [B][512]  prepared vocabulary input
+  float* logits;            // [B][vocab]
+  int32_t* out_id;          // [B]
+  double* out_logprob;      // [B]
+};
+
+// Device scheduler queue (needle_cuda_sched_*).
+struct SchedView {
+  const int32_t* prompt_offsets;  // [n_seqs + 1]
+  const int32_t* prompt_ids;
+  const int32_t* gen_steps;       // [n_seqs]
+  int32_t n_seqs;
+  int32_t n_slots;
+  int32_t* next_seq;              // queue head
+  int32_t* finished;              // finished count
+  int64_t* processed;             // tokens processed
+  int32_t* last_ids;              // [n_seqs]
+};
+
+cudaError_t launch_embed(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
+                         cudaStream_t s);
+cudaError_t launch_layer(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
+                         int n_host, cudaStream_t s);
+cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
+                             int n_host, cudaStream_t s);
+cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
+                          const SchedView* sched, cudaStream_t s);
+cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* n_items,
+                         int32_t* n_select, cudaStream_t s);
+cudaError_t launch_sched_admit(const SlotView& sv, const SchedView& q, int window, cudaStream_t s);
+cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
+                                 const float* vs, const int32_t* counts, int32_t batch,
+                                 int32_t capacity, float* out, cudaStream_t s);
+size_t attention_smem_bytes(int32_t capacity, bool ring);
+// Records the message returned by needle_cuda_last_error() on this thread (engine.cu).
+void set_last_error(const char* msg);
+inline void set_last_error(const std::string& msg) { set_last_error(msg.c_str()); }
+// Sets the dynamic shared-memory limits of the step kernels on the current device.
+cudaError_t configure_step_kernels(int32_t capacity);
+
+}  // namespace needle

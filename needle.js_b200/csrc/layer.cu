@@ -1,0 +1,896 @@
+// layer.cu -- fused per-sequence kernels of one decode step (exact numerics).
+//
+// Each kernel runs one CTA per sequence item (attention: one per item and KV head) and restates a
+// contiguous stretch of NeedleRuntime.step (packages/needle.js/src/model/runtime.ts:280-583)
+// between two quantised matvecs:
+//
+//   k_embed     embedding row x sqrt(512) into four lanes; engram n-gram hashes and table-row
+//               gathers, prepared for the engram key/value projections (runtime.ts:305-324,
+//               788-843)
+//   k_layer     [layer > 0]  output-side of layer-1: post-norm, sigmoid(attention gate) residual,
+//               Hadamard MLP, delta (runtime.ts:585-611), mHC post routing nextX (509-542)
+//               [layer < L]  input-side of layer: rmsUnit lanes, phi matvecs, h_pre, update
+//               input, engram injection, input RMSNorm, prepared Q/K/V/gate input (385-441);
+//               h_post and the 20-step Sinkhorn routing for the output side
+//               [layer == L] final lane mean, RMSNorm, prepared vocabulary input (570-577)
+//   k_attention per-head Q/K RMSNorm, RoPE, int8 KV store, attention over the visible window,
+//               sigmoid gate, prepared output-projection input (471-504, 679-786)
+//   k_finish    selectToken / argmax + logSoftmaxAt (880-899), position advance, scheduler
+//               bookkeeping
+//
+// Every binary64 expression keeps the reference's operand order; sums the reference runs as a
+// loop are run by one thread in loop order.  Values the reference stores in a Float32Array are
+// rounded with f32().
+#include "engine.cuh"
+
+namespace needle {
+
+namespace {
+
+constexpr int kThreads = 512;
+constexpr uint32_t kEngramSeed = 0x9e3779b9u;   // runtime.ts:22
+constexpr uint32_t kEngramPrime = 0x01000193u;  // runtime.ts:23
+
+__device__ __forceinline__ double silu_d(double v) { return v * sigmoid_d(v); }  // math.ts:12-14
+
+// roundTiesToEven, runtime.ts:901-907.
+__device__ __forceinline__ int round_ties_even(double value) {
+  const double lower = floor(value);
+  const double fraction = value - lower;
+  if (fraction < 0.5) return (int)lower;
+  if (fraction > 0.5) return (int)lower + 1;
+  return (((long long)lower) & 1) == 0 ? (int)lower : (int)lower + 1;
+}
+
+// Exact dot of one 128-group of a CQ row with binary64 inputs, in the reference's chunk order
+// (cq.ts:132-230).  `lut` holds the matrix's levels as binary64 (ternary: crumbs [0, c, 0, -c]).
+__device__ double group_dot_exact(const uint8_t* __restrict__ rowp, int bits, int g,
+                                  const double* lut, const double* xg) {
+  double dot = 0.0;
+  if (bits == 2 || bits == kTernaryBits) {
+    const uint8_t* p = rowp + g * 32;
+    for (int i = 0; i < 32; i++) {
+      const int byte = __ldg(p + i);
+      const double a0 = lut[byte & 3], a1 = lut[(byte >> 2) & 3];
+      const double a2 = lut[(byte >> 4) & 3], a3 = lut[(byte >> 6) & 3];
+      const double* x = xg + i * 4;
+      double s = a0 * x[0];
+      if (bits == 2) {
+        s = fma(a1, x[1], s);
+        s = fma(a2, x[2], s);
+        s = fma(a3, x[3], s);
+      } else {
+        s = s + a1 * x[1];
+        s = s + a2 * x[2];
+        s = s + a3 * x[3];
+      }
+      dot = dot + s;
+    }
+  } else if (bits == 4) {
+    const uint8_t* p = rowp + g * 64;
+    for (int i = 0; i < 64; i++) {
+      const int byte = __ldg(p + i);
+      double s = lut[byte & 15] * xg[2 * i];
+      s = fma(lut[byte >> 4], xg[2 * i + 1], s);
+      dot = dot + s;
+    }
+  } else {
+    for (int c = 0; c < kGroup; c++) dot = fma(lut[cq_index(rowp, 3, g * kGroup + c)], xg[c], dot);
+  }
+  return dot;
+}
+
+__device__ void fill_lut(double* lut, const float* cb28, int bits) {
+  for (int t = threadIdx.x; t < 16; t += blockDim.x) {
+    double v = 0.0;
+    if (bits == kTernaryBits) {
+      const double coefficient = kTernaryCentroid / sqrt((double)kGroup);
+      v = (t == 1) ? coefficient : (t == 3) ? -coefficient : 0.0;
+    } else if (t < (1 << bits)) {
+      v = (double)cb28[(bits == 2 ? 0 : bits == 3 ? 4 : 12) + t];
+    }
+    lut[t] = v;
+  }
+}
+
+// One thread's sequential sum of squares -> 1 / sqrt(s / n + 1e-6) (rmsNorm / rmsUnit).
+__device__ __forceinline__ double inverse_rms(const float* v, int n) {
+  const double s = sum_squares_seq(v, n);
+  return 1.0 / sqrt(s / (double)n + 1e-6);
+}
+
+// ------------------------------------------------------------------ k_embed
+
+__global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const SlotView sv, const StepView st) {
+  __shared__ float v[kDim];
+  __shared__ uint32_t eidx[kMaxTables];
+  __shared__ int evalid[kMaxTables];
+  __shared__ int s_token, s_pos;
+  const int b = blockIdx.x;
+  if (b >= *st.n_items) return;
+  const int tid = threadIdx.x;
+  DevItem it = st.items[b];
+  SeqState* q = sv.seq + it.slot;
+  if (tid == 0) {
+    const int p = q->position;
+    const int token = it.token >= 0 ? it.token : q->pending;
+    s_token = token;
+    s_pos = p;
+    st.items[b].token = token;
+    st.items[b].position = p;
+  }
+  __syncthreads();
+  const int token = s_token, p = s_pos;
+
+  // #engramLookup (runtime.ts:788-818): history = [..., hist[1], hist[0], token].
+  if (tid < m.n_tables && m.n_sites > 0) {
+    const int heads_per_order = m.n_tables / m.n_orders;
+    const int oi = tid / heads_per_order, head = tid - oi * heads_per_order;
+    const int order = m.orders[oi];
+    uint32_t hash = kEngramSeed * (uint32_t)(oi * heads_per_order + head + 1);
+    for (int off = 0; off < order; off++) {
+      const uint32_t tok = off > p ? 0u : off == 0 ? (uint32_t)token : (uint32_t)q->hist[off - 1];
+      hash = (hash ^ tok) * kEngramPrime;
+    }
+    hash = hash ^ (hash >> 15);
+    eidx[tid] = hash % (uint32_t)m.engram_slots;
+    evalid[tid] = (order - 1) <= p;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    q->hist[2] = q->hist[1];
+    q->hist[1] = q->hist[0];
+    q->hist[0] = token;
+  }
+
+  // Embedding: dequantizeCqRow(embedding, token) * sqrt(512), broadcast to the lanes (305-313).
+  {
+    const CqMat& E = m.embedding;
+    const int c = tid;
+    const int g = c / kGroup;
+    const uint8_t* rowp = E.packed + (int64_t)token * E.row_bytes;
+    const double nrm = norm16(E.norms, (int64_t)token * (E.in_pad / kGroup) + g);
+    v[c] = f32(cq_level(m.cb.v, E.bits, cq_index(rowp, E.bits, c)) * nrm);
+    __syncthreads();
+    fwht_smem(v, kGroup, kDim / kGroup);
+    const double inverse_root = 1.0 / sqrt((double)kGroup);
+    const float e = f32((double)v[c] * inverse_root);
+    const float scaled = f32((double)e * sqrt((double)kDim));
+    float* x = sv.x + (int64_t)it.slot * kLaneWidth;
+#pragma unroll
+    for (int lane = 0; lane < kLanes; lane++) x[lane * kDim + c] = scaled;
+    __syncthreads();
+  }
+
+  // Engram gathers (#engramStep, runtime.ts:825-841): concatenated table rows, then the
+  // prepareCqActivation of the key/value projections.
+  for (int si = 0; si < m.n_sites; si++) {
+    const CqMat& T = m.engram_tables[si];
+    const int c = tid;
+    const int t = c / m.engram_sub, col = c - t * m.engram_sub;
+    float val = 0.0f;
+    if (evalid[t]) {
+      const int64_t row = (int64_t)t * m.engram_slots + eidx[t];
+      const uint8_t* rowp = T.packed + row * T.row_bytes;
+      const int g = col / kGroup;
+      const double nrm = norm16(T.norms, row * (T.in_pad / kGroup) + g);
+      val = f32(cq_level(m.cb.v, T.bits, cq_index(rowp, T.bits, col)) * nrm);
+    }
+    v[c] = val;
+    __syncthreads();
+    const double inverse_root = 1.0 / sqrt((double)kGroup);
+    fwht_smem(v, kGroup, kDim / kGroup);  // dequantizeCqRow's FWHT of each 128-wide table row
+    v[c] = f32((double)v[c] * inverse_root);
+    __syncthreads();
+    fwht_smem(v, kGroup, kDim / kGroup);  // prepareCqActivation of the 512-wide concatenation
+    st.prep_engram[((int64_t)b * m.n_sites + si) * kDim + c] = f32((double)v[c] * inverse_root);
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ k_layer
+
+struct LayerSmem {
+  float xl[kLaneWidth];     // lanes x
+  float work[kLaneWidth];   // rmsUnit lanes / prepared phi input
+  double xd[kLaneWidth];    // prepared phi input in binary64
+  double dots[24 * 16];     // phi (row, group) dots
+  double lut[3][16];
+  float a[kDim], bvec[kDim], c[kDim], d[kDim];
+  float phi[24];
+  float hpre[kLanes], hpost[kLanes], routing[16];
+  double red[4];
+  double sk[16];            // Sinkhorn working copy (Float64Array)
+};
+
+__device__ void engram_mix(const ModelView& m, const SlotView& sv, const StepView& st, int b,
+                           int slot, int p) {
+  // #engramStep ring write and causal tap convolution (runtime.ts:854-873).  The engram position
+  // equals the token position: both start at 0 on reset and advance once per step.
+  const int c = threadIdx.x;
+  const int depth = (m.taps - 1) * m.max_order + 1;
+  for (int si = 0; si < m.n_sites; si++) {
+    const float now = st.engram_kv[(((int64_t)b * m.n_sites + si) * 2 + 1) * kDim + c];
+    float* ring = sv.ring + ((int64_t)slot * m.n_sites + si) * depth * kDim;
+    ring[(p % depth) * kDim + c] = now;
+    float mixed = 0.0f;
+    for (int tap = 0; tap < m.taps; tap++) {
+      const int prev = p - tap * m.max_order;
+      if (prev < 0) continue;
+      const float value = tap == 0 ? now : ring[(prev % depth) * kDim + c];
+      mixed = f32((double)mixed + (double)m.taps_w[((int64_t)si * m.taps + tap) * kDim + c] * (double)value);
+    }
+    st.engram_val[((int64_t)b * m.n_sites + si) * kDim + c] = mixed;
+  }
+}
+
+// 20 log-space Sinkhorn iterations on a 4x4 matrix (sinkhorn, math.ts:63-92), run by one full
+// warp (lanes 0-3 do the row / column passes); lanes 0-15 then write exp(values) as binary32.
+__device__ void sinkhorn4(double* v, float* out, int lane) {
+  for (int it = 0; it < 20; it++) {
+    if (lane < 4) {
+      const int o = lane * 4;
+      double mx = v[o];
+      for (int c = 1; c < 4; c++) mx = fmax(mx, v[o + c]);
+      double sum = 0.0;
+      for (int c = 0; c < 4; c++) sum = sum + exp(v[o + c] - mx);
+      const double log_sum = log(sum) + mx;
+      for (int c = 0; c < 4; c++) v[o + c] = v[o + c] - log_sum;
+    }
+    __syncwarp();
+    if (lane < 4) {
+      double mx = v[lane];
+      for (int r = 1; r < 4; r++) mx = fmax(mx, v[r * 4 + lane]);
+      double sum = 0.0;
+      for (int r = 0; r < 4; r++) sum = sum + exp(v[r * 4 + lane] - mx);
+      const double log_sum = log(sum) + mx;
+      for (int r = 0; r < 4; r++) v[r * 4 + lane] = v[r * 4 + lane] - log_sum;
+    }
+    __syncwarp();
+  }
+  if (lane < 16) out[lane] = f32(exp(v[lane]));
+}
+
+__global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const SlotView sv, const StepView st,
+                                                  int layer) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  LayerSmem& S = *reinterpret_cast<LayerSmem*>(smem_raw);
+  const int b = blockIdx.x;
+  if (b >= *st.n_items) return;
+  const int tid = threadIdx.x;
+  const DevItem it = st.items[b];
+  const int slot = it.slot, p = it.position;
+  float* xg = sv.x + (int64_t)slot * kLaneWidth;
+  for (int i = tid; i < kLaneWidth; i += kThreads) S.xl[i] = xg[i];
+  if (layer == 0 && m.n_sites > 0) engram_mix(m, sv, st, b, slot, p);
+  __syncthreads();
+
+  const double inv_root_128 = 1.0 / sqrt((double)kGroup);
+  const int c = tid;
+
+  if (layer > 0) {
+    // ---------------- output side of layer l = layer - 1
+    const int l = layer - 1;
+    const float upd = st.update[(int64_t)b * kDim + c];
+    const float blk = st.block[(int64_t)b * kDim + c];
+    S.a[c] = st.proj[(int64_t)b * kDim + c];
+    if (tid < 20) {
+      const float r = st.route[(int64_t)b * 20 + tid];
+      if (tid < 4) S.hpost[tid] = r;
+      else S.routing[tid - 4] = r;
+    }
+    __syncthreads();
+    if (tid == 0) S.red[0] = inverse_rms(S.a, kDim);
+    __syncthreads();
+    // #attentionDelta (runtime.ts:585-611)
+    const float normalized =
+        f32((1.0 + (double)m.post_norm[(int64_t)l * kDim + c]) * (double)S.a[c] * S.red[0]);
+    const double attention_scale = sigmoid_d((double)m.attn_gate[l]);
+    const float after = f32((double)blk + attention_scale * (double)normalized);
+    S.bvec[c] = after;
+    __syncthreads();
+    if (tid == 0) S.red[1] = inverse_rms(S.bvec, kDim);
+    __syncthreads();
+    const float pre = f32((1.0 + (double)m.pre_had_norm[(int64_t)l * kDim + c]) * (double)after * S.red[1]);
+    // hadamardMlp (math.ts:117-138)
+    S.c[c] = f32((double)pre * (double)m.d1[(int64_t)l * kHadamard + c]);
+    __syncthreads();
+    fwht_smem(S.c, kHadamard, 1);
+    const double inv_root_h = 1.0 / sqrt((double)kHadamard);
+    S.c[c] = f32(silu_d((double)S.c[c] * inv_root_h * (double)m.d2[(int64_t)l * kHadamard + c]));
+    __syncthreads();
+    fwht_smem(S.c, kHadamard, 1);
+    const float mlp = f32((double)S.c[c] * inv_root_h * (double)m.d3[(int64_t)l * kHadamard + c]);
+    const float delta = f32((double)after + (double)mlp - (double)upd);
+    // nextX (runtime.ts:530-541)
+    float nx[kLanes];
+#pragma unroll
+    for (int lane = 0; lane < kLanes; lane++) {
+      double sum = 0.0;
+#pragma unroll
+      for (int src = 0; src < kLanes; src++)
+        sum = fma((double)S.routing[lane * kLanes + src], (double)S.xl[src * kDim + c], sum);
+      nx[lane] = f32(sum + (double)S.hpost[lane] * (double)delta);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int lane = 0; lane < kLanes; lane++) {
+      S.xl[lane * kDim + c] = nx[lane];
+      xg[lane * kDim + c] = nx[lane];
+    }
+    __syncthreads();
+  }
+
+  if (layer == m.layers) {
+    // ---------------- final: lane mean, RMSNorm, prepared vocabulary input (runtime.ts:570-577)
+    double sum = 0.0;
+#pragma unroll
+    for (int lane = 0; lane < kLanes; lane++) sum = sum + (double)S.xl[lane * kDim + c];
+    S.a[c] = f32(sum / (double)kLanes);
+    __syncthreads();
+    if (tid == 0) S.red[0] = inverse_rms(S.a, kDim);
+    __syncthreads();
+    S.c[c] = f32((1.0 + (double)m.final_norm[c]) * (double)S.a[c] * S.red[0]);
+    __syncthreads();
+    fwht_smem(S.c, kGroup, kDim / kGroup);
+    st.prep_f[(int64_t)b * kDim + c] = f32((double)S.c[c] * inv_root_128);
+    return;
+  }
+
+  // ---------------- input side of layer l
+  const int l = layer;
+  if (tid == 0) S.red[2] = inverse_rms(S.xl, kLaneWidth);  // rmsUnit(x), runtime.ts:385
+  fill_lut(S.lut[0], m.cb.v, m.phi_pre.bits);
+  if (tid >= 16 && tid < 32) {
+    double* lut1 = S.lut[1];
+    double* lut2 = S.lut[2];
+    const int t = tid - 16;
+    // (same construction as fill_lut, for the phi_post / phi_res matrices)
+    for (int k = 0; k < 2; k++) {
+      const int bits = k == 0 ? m.phi_post.bits : m.phi_res.bits;
+      double v = 0.0;
+      if (bits == kTernaryBits) {
+        const double coefficient = kTernaryCentroid / sqrt((double)kGroup);
+        v = (t == 1) ? coefficient : (t == 3) ? -coefficient : 0.0;
+      } else if (t < (1 << bits)) {
+        v = (double)m.cb.v[(bits == 2 ? 0 : bits == 3 ? 4 : 12) + t];
+      }
+      (k == 0 ? lut1 : lut2)[t] = v;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < kLaneWidth; i += kThreads) S.work[i] = f32((double)S.xl[i] * S.red[2]);
+  __syncthreads();
+  fwht_smem(S.work, kGroup, kLaneWidth / kGroup);
+  for (int i = tid; i < kLaneWidth; i += kThreads) S.xd[i] = (double)f32((double)S.work[i] * inv_root_128);
+  __syncthreads();
+
+  // phi matvecs (matvecBatch, runtime.ts:386-402): rows 4l..4l+3 of phi_pre / phi_post and
+  // 16l..16l+15 of phi_res; 24 rows x 16 groups, one (row, group) per thread.
+  const int phi_groups = kLaneWidth / kGroup;
+  if (tid < 24 * phi_groups) {
+    const int rr = tid / phi_groups, g = tid - rr * phi_groups;
+    const CqMat& M = rr < 4 ? m.phi_pre : rr < 8 ? m.phi_post : m.phi_res;
+    const int64_t row = rr < 4 ? (int64_t)l * 4 + rr : rr < 8 ? (int64_t)l * 4 + rr - 4 : (int64_t)l * 16 + rr - 8;
+    const double* lut = S.lut[rr < 4 ? 0 : rr < 8 ? 1 : 2];
+    S.dots[tid] = group_dot_exact(M.packed + row * M.row_bytes, M.bits, g, lut, S.xd + g * kGroup);
+  }
+  __syncthreads();
+  if (tid < 24) {
+    const int rr = tid;
+    const CqMat& M = rr < 4 ? m.phi_pre : rr < 8 ? m.phi_post : m.phi_res;
+    const int64_t row = rr < 4 ? (int64_t)l * 4 + rr : rr < 8 ? (int64_t)l * 4 + rr - 4 : (int64_t)l * 16 + rr - 8;
+    double total = 0.0;
+    for (int g = 0; g < phi_groups; g++)
+      total = total + norm16(M.norms, row * phi_groups + g) * S.dots[rr * phi_groups + g];
+    S.phi[rr] = f32(total);
+  }
+  __syncthreads();
+  const int own = l % kLanes;
+  if (tid < 4) {
+    // h_pre (runtime.ts:404-413)
+    const double offset = tid == own ? 4.0 : -4.0;
+    S.hpre[tid] = f32(sigmoid_d((double)m.a_pre[l] * (double)S.phi[tid] +
+                                (double)m.b_pre[(int64_t)l * 4 + tid] + offset));
+  } else if (tid < 8) {
+    // h_post (runtime.ts:512-522)
+    const int lane = tid - 4;
+    const double offset = lane == own ? 0.0 : -4.0;
+    S.hpost[lane] = f32(2.0 * sigmoid_d((double)m.a_post[l] * (double)S.phi[tid] +
+                                        (double)m.b_post[(int64_t)l * 4 + lane] + offset));
+  } else if (tid < 24) {
+    // routing logits (runtime.ts:523-528), Float32Array then Float64Array(logits)
+    const int i = tid - 8;
+    S.sk[i] = (double)f32((double)m.a_res[l] * (double)S.phi[tid] + (double)m.b_res[(int64_t)l * 16 + i]);
+  }
+  __syncthreads();
+
+  // updateInput (runtime.ts:414-420)
+  double sum = 0.0;
+#pragma unroll
+  for (int lane = 0; lane < kLanes; lane++) sum = fma((double)S.hpre[lane], (double)S.xl[lane * kDim + c], sum);
+  const float upd = f32(sum);
+  S.a[c] = upd;
+  float blk = upd;
+  int site = -1;
+  for (int k = 0; k < m.n_sites; k++)
+    if (m.sites[k] == l) site = k;
+  if (site >= 0) {
+    // engram injection (runtime.ts:423-438)
+    const float key = st.engram_kv[(((int64_t)b * m.n_sites + site) * 2) * kDim + c];
+    S.bvec[c] = key;
+    __syncthreads();
+    if (tid == 0) S.red[0] = inverse_rms(S.a, kDim);
+    if (tid == 32) S.red[1] = inverse_rms(S.bvec, kDim);
+    __syncthreads();
+    S.c[c] = f32((double)upd * S.red[0]);
+    S.d[c] = f32((double)key * S.red[1]);
+    __syncthreads();
+    if (tid == 0) {
+      double dot = 0.0;
+      for (int i = 0; i < kDim; i++) dot = fma((double)S.c[i], (double)S.d[i], dot);
+      S.red[3] = sigmoid_d(dot / sqrt((double)kDim));
+    }
+    __syncthreads();
+    const float value = st.engram_val[((int64_t)b * m.n_sites + site) * kDim + c];
+    blk = f32((double)upd + S.red[3] * (double)value);
+    __syncthreads();
+  }
+  S.bvec[c] = blk;
+  st.update[(int64_t)b * kDim + c] = upd;
+  st.block[(int64_t)b * kDim + c] = blk;
+  __syncthreads();
+  if (tid == 0) S.red[0] = inverse_rms(S.bvec, kDim);
+  if (tid >= 32 && tid < 64) sinkhorn4(S.sk, S.routing, tid - 32);  // warp 1, beside thread 0
+  __syncthreads();
+  // rmsNorm(blockInput, normInput) then prepareCqActivation for Q/K/V/gate (runtime.ts:441, 465)
+  S.c[c] = f32((1.0 + (double)m.norm_input[(int64_t)l * kDim + c]) * (double)blk * S.red[0]);
+  __syncthreads();
+  fwht_smem(S.c, kGroup, kDim / kGroup);
+  st.prep_a[(int64_t)b * kDim + c] = f32((double)S.c[c] * inv_root_128);
+  if (tid < 4) st.route[(int64_t)b * 20 + tid] = S.hpost[tid];
+  else if (tid < 20) st.route[(int64_t)b * 20 + tid] = S.routing[tid - 4];
+}
+
+// ------------------------------------------------------------------ k_attention
+
+constexpr int kAttnThreads = 128;
+
+// Cache addressing of the engine (ring = window/sink slots) or of the isolated operator
+// (contiguous positions 0..count-1).
+struct CacheRef {
+  const int8_t* kc;
+  const int8_t* vc;
+  const float* ks;
+  const float* vs;
+};
+
+// Attention of query heads 2h, 2h+1 over one KV head (the #attention loops of runtime.ts:732-784
+// for one kvHead).  q: smem binary32 [2][64]; e: smem binary64 [2][count]; slot_of(t) maps the
+// t-th visible position to its cache row.  Leaves the gated outputs in out[2][64] (smem).
+template <class SlotOf>
+__device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const float* q, double* e,
+                            const float* gate, float* out, double* red) {
+  const int tid = threadIdx.x;
+  // scores[t] = f32((sum_i q_i * code_i * keyScale) / 8)  (runtime.ts:736-757)
+  for (int t = tid; t < count; t += kAttnThreads) {
+    const int sl = slot_of(t);
+    const double ks = (double)C.ks[sl];
+    const uint4* kr = reinterpret_cast<const uint4*>(C.kc + (int64_t)sl * kHeadDim);
+    double d0 = 0.0, d1 = 0.0;
+#pragma unroll
+    for (int w4 = 0; w4 < 4; w4++) {
+      const uint4 u = __ldg(kr + w4);
+      const uint32_t words[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        const int i = w4 * 16 + k;
+        const double code = (double)(int8_t)((words[k >> 2] >> ((k & 3) * 8)) & 0xff);
+        d0 = d0 + ((double)q[i] * code) * ks;
+        d1 = d1 + ((double)q[kHeadDim + i] * code) * ks;
+      }
+    }
+    const double inverse_root = 1.0 / sqrt((double)kHeadDim);
+    e[t] = (double)f32(d0 * inverse_root);
+    e[count + t] = (double)f32(d1 * inverse_root);
+  }
+  __syncthreads();
+  // softmaxInPlace (math.ts:46-60): max (order-free), exp in parallel, sequential total.
+  {
+    const int hh = tid >> 6, lane64 = tid & 63;
+    double mx = -INFINITY;
+    for (int t = lane64; t < count; t += 64) mx = fmax(mx, e[hh * count + t]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = fmax(red[hh * 2], red[hh * 2 + 1]);
+    __syncthreads();
+    for (int t = lane64; t < count; t += 64) e[hh * count + t] = exp(e[hh * count + t] - mx);
+    __syncthreads();
+    if (lane64 == 0) {
+      double total = 0.0;
+      for (int t = 0; t < count; t++) total = total + e[hh * count + t];
+      red[4 + hh] = total > 0.0 ? 1.0 / total : 0.0;
+    }
+    __syncthreads();
+  }
+  // output[i] += weight * code * valueScale, sequentially in t with binary32 storage (760-782).
+  {
+    const int hh = tid >> 6, i = tid & 63;
+    const double inverse = red[4 + hh];
+    const double* eh = e + hh * count;
+    float o = 0.0f;
+    for (int t = 0; t < count; t++) {
+      const int sl = slot_of(t);
+      const double w = (double)f32((double)f32(eh[t]) * inverse);
+      const double code = (double)C.vc[(int64_t)sl * kHeadDim + i];
+      o = f32((double)o + w * code * (double)C.vs[sl]);
+    }
+    // attentionOutput * sigmoid(gate) (runtime.ts:503-504)
+    out[hh * kHeadDim + i] = gate ? f32((double)o * sigmoid_d((double)gate[hh * kHeadDim + i])) : o;
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, const SlotView sv,
+                                                           const StepView st, int l) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float qv[2 * kHeadDim], kv[kHeadDim], vv[kHeadDim], gt[2 * kHeadDim], outv[2 * kHeadDim];
+  __shared__ double red[8];
+  __shared__ double amax[8];
+  const int b = blockIdx.x, h = blockIdx.y;
+  if (b >= *st.n_items) return;
+  const int tid = threadIdx.x;
+  const DevItem it = st.items[b];
+  const int slot = it.slot, p = it.position;
+  const SeqState seq = sv.seq[slot];
+  const float* qkvg = st.qkvg + (int64_t)b * 1536;
+  qv[tid] = qkvg[2 * h * kHeadDim + tid];
+  gt[tid] = qkvg[1024 + 2 * h * kHeadDim + tid];
+  if (tid < kHeadDim) {
+    kv[tid] = qkvg[512 + h * kHeadDim + tid];
+    vv[tid] = qkvg[768 + h * kHeadDim + tid];
+  }
+  __syncthreads();
+  // #rmsNormSlice on the two query heads and the key head (runtime.ts:471-486, 647-657)
+  if (tid == 0) red[0] = inverse_rms(qv, kHeadDim);
+  if (tid == 32) red[1] = inverse_rms(qv + kHeadDim, kHeadDim);
+  if (tid == 64) red[2] = inverse_rms(kv, kHeadDim);
+  __syncthreads();
+  {
+    const int i = tid & 63;
+    qv[tid] = f32((1.0 + (double)m.query_norm[(int64_t)l * kHeadDim + i]) * (double)qv[tid] * red[tid >> 6]);
+    if (tid < kHeadDim) kv[tid] = f32((1.0 + (double)m.key_norm[(int64_t)l * kHeadDim + tid]) * (double)kv[tid] * red[2]);
+  }
+  __syncthreads();
+  // applyRope (math.ts:94-115) with host-computed binary64 cos/sin of position * theta^(-2d/64)
+  if (tid < 96) {
+    const int which = tid >> 5, d = tid & 31;
+    float* vec = which < 2 ? qv + which * kHeadDim : kv;
+    const double cs = m.rope_cos[(int64_t)p * 32 + d], sn = m.rope_sin[(int64_t)p * 32 + d];
+    const double first = vec[d], second = vec[d + 32];
+    vec[d] = f32(first * cs - second * sn);
+    vec[d + 32] = f32(second * cs + first * sn);
+  }
+  __syncthreads();
+  // #storeKV (runtime.ts:679-717): abs-max (order-free), scale = max / 127, codes = RNE(x / scale).
+  const int window = m.kv_window;
+  const int sink = seq.sink;
+  auto kv_slot = [&](int pos) {
+    if (window == 0) return pos;
+    if (pos < sink) return pos;
+    return sink + (pos - sink) % window;
+  };
+  const int64_t head_base = (((int64_t)slot * sv.layers + l) * kKvHeads + h) * sv.capacity;
+  {
+    double mk = 0.0, mv = 0.0;
+    if (tid < kHeadDim) {
+      mk = fabs((double)kv[tid]);
+      mv = fabs((double)vv[tid]);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      mk = fmax(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+      mv = fmax(mv, __shfl_xor_sync(0xffffffffu, mv, o));
+    }
+    if ((tid & 31) == 0) {
+      amax[tid >> 5] = mk;
+      amax[4 + (tid >> 5)] = mv;
+    }
+    __syncthreads();
+    const double key_scale = fmax(1e-12, fmax(amax[0], amax[1])) / 127.0;
+    const double value_scale = fmax(1e-12, fmax(amax[4], amax[5])) / 127.0;
+    const int sl = kv_slot(p);
+    if (tid < kHeadDim) {
+      sv.kcodes[(head_base + sl) * kHeadDim + tid] = (int8_t)round_ties_even((double)kv[tid] / key_scale);
+      sv.vcodes[(head_base + sl) * kHeadDim + tid] = (int8_t)round_ties_even((double)vv[tid] / value_scale);
+    }
+    if (tid == 0) {
+      sv.kscale[head_base + sl] = f32(key_scale);
+      sv.vscale[head_base + sl] = f32(value_scale);
+    }
+    __syncthreads();
+  }
+  // Visible positions (runtime.ts:723-728): [0, prefix) U [recentLow, p].
+  const int prefix = min(sink, p + 1);
+  const int recent_low = window > 0 ? max(prefix, p + 1 - window) : prefix;
+  const int count = prefix + (p - recent_low + 1);
+  CacheRef C{sv.kcodes + head_base * kHeadDim, sv.vcodes + head_base * kHeadDim, sv.kscale + head_base,
+             sv.vscale + head_base};
+  double* e = reinterpret_cast<double*>(smem_raw);
+  auto slot_of = [&](int t) { return kv_slot(t < prefix ? t : recent_low + (t - prefix)); };
+  attend_pair(C, count, slot_of, qv, e, gt, outv, red);
+  // prepareCqActivation of the output projection: heads 2h, 2h+1 are exactly input group h.
+  fwht_smem(outv, kGroup, 1);
+  st.prep_o[(int64_t)b * kDim + h * kGroup + tid] = f32((double)outv[tid] * (1.0 / sqrt((double)kGroup)));
+}
+
+// Isolated decode attention (needle_cuda_attention_dev): kvWindow = 0, positions 0..count-1,
+// query already normalised and rotated, no gate.
+__global__ void __launch_bounds__(kAttnThreads) k_attention_dev(const float* __restrict__ q,
+                                                               const int8_t* kc, const float* ks,
+                                                               const int8_t* vc, const float* vs,
+                                                               const int32_t* counts, int32_t capacity,
+                                                               float* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float qv[2 * kHeadDim], outv[2 * kHeadDim];
+  __shared__ double red[8];
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x;
+  qv[tid] = q[(int64_t)b * kHeads * kHeadDim + 2 * h * kHeadDim + tid];
+  __syncthreads();
+  const int count = min(max(counts[b], 0), capacity);
+  const int64_t head_base = ((int64_t)b * kKvHeads + h) * capacity;
+  CacheRef C{kc + head_base * kHeadDim, vc + head_base * kHeadDim, ks + head_base, vs + head_base};
+  double* e = reinterpret_cast<double*>(smem_raw);
+  auto slot_of = [](int t) { return t; };
+  attend_pair(C, count, slot_of, qv, e, nullptr, outv, red);
+  out[(int64_t)b * kHeads * kHeadDim + 2 * h * kHeadDim + tid] = outv[tid];
+}
+
+// ------------------------------------------------------------------ k_finish
+
+constexpr int kFinishThreads = 256;
+
+__device__ __forceinline__ bool better(float v, int k, float bv, int bk) {
+  // strictly greater wins; equal values keep the earlier candidate (runtime.ts:889-896)
+  return v > bv || (v == bv && k < bk);
+}
+
+__global__ void __launch_bounds__(kFinishThreads) k_finish(const ModelView m, const SlotView sv,
+                                                         const StepView st, const SchedView q,
+                                                         int has_sched) {
+  __shared__ float sv_[kFinishThreads / 32];
+  __shared__ int sk_[kFinishThreads / 32];
+  __shared__ double sd_[kFinishThreads / 32];
+  __shared__ int s_id;
+  __shared__ double s_max;
+  const int b = blockIdx.x;
+  if (b >= *st.n_items) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const DevItem it = st.items[b];
+  SeqState* seq = sv.seq + it.slot;
+  const bool selecting = b < *st.n_select && it.select;
+  int chosen = -1;
+  if (selecting) {
+    const float* lg = st.logits + (int64_t)b * m.vocab;
+    // masked argmax / argmax (selectToken, runtime.ts:880-899; argmax, math.ts:140-151)
+    const bool masked = it.allowed_count >= 0;
+    const int n = masked ? it.allowed_count : m.vocab;
+    float bv = -INFINITY;
+    int bk = 0x7fffffff;
+    for (int k = tid; k < n; k += kFinishThreads) {
+      const int id = masked ? (int)st.allowed[it.allowed_offset + k] : k;
+      const float v = lg[id];
+      if (bk == 0x7fffffff || v > bv) {  // ascending k: strict > keeps the earliest
+        bv = v;
+        bk = k;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      if (ok != 0x7fffffff && (bk == 0x7fffffff || better(ov, ok, bv, bk))) {
+        bv = ov;
+        bk = ok;
+      }
+    }
+    if (lane == 0) {
+      sv_[warp] = bv;
+      sk_[warp] = bk;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float v0 = sv_[0];
+      int k0 = sk_[0];
+      for (int w = 1; w < kFinishThreads / 32; w++)
+        if (sk_[w] != 0x7fffffff && (k0 == 0x7fffffff || better(sv_[w], sk_[w], v0, k0))) {
+          v0 = sv_[w];
+          k0 = sk_[w];
+        }
+      s_id = masked ? (int)st.allowed[it.allowed_offset + k0] : k0;
+    }
+    // logSoftmaxAt (math.ts:153-160): max, then sum of exp(logit - max) as a binary64 tree sum.
+    double mx = -INFINITY;
+    for (int k = tid; k < m.vocab; k += kFinishThreads) mx = fmax(mx, (double)lg[k]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) sd_[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+      double v = sd_[0];
+      for (int w = 1; w < kFinishThreads / 32; w++) v = fmax(v, sd_[w]);
+      s_max = v;
+    }
+    __syncthreads();
+    double sum = 0.0;
+    for (int k = tid; k < m.vocab; k += kFinishThreads) sum += exp((double)lg[k] - s_max);
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) sd_[warp] = sum;
+    __syncthreads();
+    if (tid == 0) {
+      double total = 0.0;
+      for (int w = 0; w < kFinishThreads / 32; w++) total += sd_[w];
+      chosen = s_id;
+      st.out_id[b] = chosen;
+      st.out_logprob[b] = (double)lg[chosen] - s_max - log(total);
+      seq->pending = chosen;
+    }
+  }
+  if (tid == 0) {
+    seq->position = it.position + 1;
+    if (has_sched) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(q.processed), 1ull);
+      if (selecting) {
+        const int done = seq->gen_done + 1;
+        seq->gen_done = done;
+        if (done >= seq->gen_target) {
+          q.last_ids[seq->seq_id] = chosen;
+          atomicAdd(q.finished, 1);
+          seq->busy = 0;
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ device scheduler
+
+// Admission: every idle slot takes the next queued sequence (reset as runtime.ts:150-225 with
+// sink 0 and maximumLength = prompt + generated tokens).
+__global__ void k_sched_admit(const SlotView sv, const SchedView q, int window) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= q.n_slots) return;
+  SeqState* seq = sv.seq + s;
+  if (seq->busy) return;
+  const int id = atomicAdd(q.next_seq, 1);
+  if (id >= q.n_seqs) return;
+  const int off = q.prompt_offsets[id];
+  const int len = q.prompt_offsets[id + 1] - off;
+  const int gen = q.gen_steps[id];
+  const int max_len = len + gen;
+  seq->position = 0;
+  seq->sink = 0;
+  seq->max_len = max_len;
+  seq->kv_alloc = window > 0 ? min(max_len, window) : max_len;
+  seq->pending = 0;
+  seq->hist[0] = seq->hist[1] = seq->hist[2] = 0;
+  seq->seq_id = id;
+  seq->prompt_off = off;
+  seq->prompt_len = len;
+  seq->gen_target = gen;
+  seq->gen_done = 0;
+  seq->busy = 1;
+}
+
+// Builds the step's item list from the busy slots: selecting items (the last prompt token and
+// every decode step) first, then prefill items.  One CTA.
+__global__ void __launch_bounds__(1024) k_sched(const SlotView sv, const StepView st, const SchedView q,
+                                              int32_t* n_items, int32_t* n_select) {
+  __shared__ int s_sel;
+  const int tid = threadIdx.x;
+  if (tid == 0) s_sel = 0;
+  __syncthreads();
+  // pass 1: count selecting items
+  for (int s = tid; s < q.n_slots; s += blockDim.x) {
+    const SeqState& seq = sv.seq[s];
+    if (seq.busy && seq.position >= seq.prompt_len - 1) atomicAdd(&s_sel, 1);
+  }
+  __syncthreads();
+  const int n_sel = s_sel;
+  __shared__ int c_sel, c_pre;
+  if (tid == 0) {
+    c_sel = 0;
+    c_pre = 0;
+  }
+  __syncthreads();
+  for (int s = tid; s < q.n_slots; s += blockDim.x) {
+    const SeqState& seq = sv.seq[s];
+    if (!seq.busy) continue;
+    const bool sel = seq.position >= seq.prompt_len - 1;
+    const int idx = sel ? atomicAdd(&c_sel, 1) : n_sel + atomicAdd(&c_pre, 1);
+    DevItem it;
+    it.slot = s;
+    it.token = seq.position < seq.prompt_len ? q.prompt_ids[seq.prompt_off + seq.position] : -1;
+    it.select = sel ? 1 : 0;
+    it.allowed_count = -1;
+    it.allowed_offset = 0;
+    it.position = seq.position;
+    it.out_index = idx;
+    it.pad = 0;
+    st.items[idx] = it;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    *n_items = c_sel + c_pre;
+    *n_select = c_sel;
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ launchers
+
+cudaError_t launch_embed(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
+                         cudaStream_t s) {
+  if (n_host <= 0) return cudaSuccess;
+  k_embed<<<n_host, kThreads, 0, s>>>(m, sv, st);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layer(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
+                         int n_host, cudaStream_t s) {
+  if (n_host <= 0) return cudaSuccess;
+  const size_t smem = sizeof(LayerSmem);
+  k_layer<<<n_host, kThreads, smem, s>>>(m, sv, st, layer);
+  return cudaGetLastError();
+}
+
+size_t attention_smem_bytes(int32_t capacity, bool) { return sizeof(double) * 2 * (size_t)capacity; }
+
+cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
+                             int n_host, cudaStream_t s) {
+  if (n_host <= 0) return cudaSuccess;
+  const size_t smem = attention_smem_bytes(sv.capacity, true);
+  k_attention<<<dim3(n_host, kKvHeads), kAttnThreads, smem, s>>>(m, sv, st, layer);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
+                                 const float* vs, const int32_t* counts, int32_t batch,
+                                 int32_t capacity, float* out, cudaStream_t s) {
+  if (batch <= 0) return cudaSuccess;
+  const size_t smem = attention_smem_bytes(capacity, false);
+  cudaError_t e = cudaFuncSetAttribute(k_attention_dev, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k_attention_dev<<<dim3(batch, kKvHeads), kAttnThreads, smem, s>>>(q, kc, ks, vc, vs, counts, capacity, out);
+  return cudaGetLastError();
+}
+
+cudaError_t configure_step_kernels(int32_t capacity) {
+  cudaError_t e = cudaFuncSetAttribute(k_layer, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(LayerSmem));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)attention_smem_bytes(capacity, true));
+}
+
+cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
+                          const SchedView* sched, cudaStream_t s) {
+  if (n_host <= 0) return cudaSuccess;
+  SchedView q{};
+  if (sched) q = *sched;
+  k_finish<<<n_host, kFinishThreads, 0, s>>>(m, sv, st, q, sched ? 1 : 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sched_admit(const SlotView& sv, const SchedView& q, int window, cudaStream_t s) {
+  k_sched_admit<<<(q.n_slots + 255) / 256, 256, 0, s>>>(sv, q, window);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* n_items,
+                         int32_t* n_select, cudaStream_t s) {
+  k_sched<<<1, 1024, 0, s>>>(sv, st, q, n_items, n_select);
+  return cudaGetLastError();
+}
+
+}  // namespace needle

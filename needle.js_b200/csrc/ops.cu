@@ -1,0 +1,109 @@
+// ops.cu -- stateless device-pointer operators of the C-ABI (isolated matvec and attention).
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/needle_cuda.h"
+#include "engine.cuh"
+
+using namespace needle;
+
+namespace {
+
+// Library-owned scratch for prepared activations, one growable buffer per device.
+struct DeviceScratch {
+  float* ptr = nullptr;
+  size_t floats = 0;
+};
+std::mutex g_scratch_mu;
+std::vector<DeviceScratch> g_scratch;
+
+cudaError_t scratch_for(int device, size_t floats, float** out) {
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (int(g_scratch.size()) <= device) g_scratch.resize(device + 1);
+  DeviceScratch& s = g_scratch[device];
+  if (s.floats < floats) {
+    if (s.ptr) {
+      cudaError_t e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) return e;
+      cudaFree(s.ptr);
+      s.ptr = nullptr;
+      s.floats = 0;
+    }
+    cudaError_t e = cudaMalloc(&s.ptr, floats * sizeof(float));
+    if (e != cudaSuccess) return e;
+    s.floats = floats;
+  }
+  *out = s.ptr;
+  return cudaSuccess;
+}
+
+int op_fail(int code, const std::string& msg) {
+  set_last_error(msg);
+  return code;
+}
+
+}  // namespace
+
+extern "C" int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float* codebook, const float* x,
+                                         int32_t batch, float* y, void* stream) {
+  if (!m || !codebook || (batch > 0 && (!x || !y)))
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+  if (m->group_size != kGroup) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "CQ group size 128 only");
+  if (!(m->bits == 2 || m->bits == 3 || m->bits == 4 || m->bits == 5))
+    return op_fail(NEEDLE_UNSUPPORTED_CACT, "unsupported CQ record width");
+  if (m->rows < 0 || m->input_size <= 0 || batch < 0) return op_fail(NEEDLE_INVALID_CACT, "bad matrix shape");
+  if ((reinterpret_cast<uintptr_t>(m->packed) & 15) != 0)
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "packed rows must be 16-byte aligned");
+  if (batch == 0 || m->rows == 0) return NEEDLE_OK;
+  const int in_pad = (m->input_size + kGroup - 1) / kGroup * kGroup;
+  const int pb = m->bits == 5 ? 2 : m->bits;
+  const int row_bytes = in_pad * pb / 8;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Codebook cb{};
+  for (int i = 0; i < 28; i++) cb.v[i] = codebook[i];
+  int device = 0;
+  cudaGetDevice(&device);
+  float* xp = nullptr;
+  cudaError_t e = scratch_for(device, size_t(batch) * in_pad, &xp);
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  e = launch_cq_prepare(x, m->input_size, m->input_size, in_pad, xp, in_pad, batch, nullptr, s);
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  // Split rows into <= kMaxJobs jobs only to keep every job inside one launch; one job suffices.
+  CqJobs J{};
+  CqJob& j = J.job[0];
+  j.packed = m->packed;
+  j.norms = m->norms;
+  j.row_start = 0;
+  j.rows = m->rows;
+  j.in_pad = in_pad;
+  j.bits = m->bits;
+  j.row_bytes = row_bytes;
+  j.tile_begin = 0;
+  j.x = xp;
+  j.x_stride = in_pad;
+  j.y = y;
+  j.y_stride = m->rows;
+  J.count = 1;
+  J.total_tiles = (m->rows + 31) / 32;
+  e = launch_cq_gemv(J, cb, batch, nullptr, s);
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  return NEEDLE_OK;
+}
+
+extern "C" int needle_cuda_attention_dev(const float* q, const int8_t* key_codes, const float* key_scales,
+                                         const int8_t* value_codes, const float* value_scales, const int32_t* counts,
+                                         int32_t batch, int32_t capacity, float* out, void* stream) {
+  if (batch < 0 || capacity <= 0) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "bad batch / capacity");
+  if (batch == 0) return NEEDLE_OK;
+  if (!q || !key_codes || !key_scales || !value_codes || !value_scales || !counts || !out)
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+  if (attention_smem_bytes(capacity, false) > 200 * 1024)
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "capacity too large for the exact attention kernel");
+  cudaError_t e = launch_attention_dev(q, key_codes, key_scales, value_codes, value_scales, counts, batch, capacity,
+                                       out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  return NEEDLE_OK;
+}
