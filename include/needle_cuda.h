@@ -198,10 +198,14 @@ int needle_cuda_sched_load(needle_ctx* ctx, int32_t n_slots, const int32_t* prom
                            const int32_t* prompt_ids, const int32_t* gen_steps, int32_t n_seqs);
 /* Enqueues `steps` device-resident steps on the context stream without synchronising. */
 int needle_cuda_sched_step(needle_ctx* ctx, int32_t steps);
-/* Synchronises and reports progress: tokens processed so far, sequences finished, and for every
- * queued sequence its last selected token (n_seqs entries, -1 while unfinished; may be NULL). */
-int needle_cuda_sched_status(needle_ctx* ctx, int64_t* tokens_processed, int32_t* seqs_finished,
-                             int32_t* last_ids);
+/* Synchronises and reports progress: tokens processed (steps taken, prompt and generated tokens
+ * alike), tokens generated (greedy selections), sequences finished, and for every queued
+ * sequence its last selected token (n_seqs entries, -1 while unfinished; may be NULL). */
+int needle_cuda_sched_status(needle_ctx* ctx, int64_t* tokens_processed, int64_t* tokens_generated,
+                             int32_t* seqs_finished, int32_t* last_ids);
+
+/* Number of CUDA kernels this context has launched so far (for launch accounting). */
+int needle_cuda_kernel_launches(const needle_ctx* ctx, int64_t* count);
 
 /* Per-kernel-class timing with CUDA events on the context stream (off by default).  enable=1
  * starts accumulating, enable=0 stops.  read fills up to n entries of (name, total ms, launches)

@@ -158,10 +158,17 @@ class CudaEngine:
         check(lib().needle_cuda_sched_step(self.h, steps))
 
     def sched_status(self):
-        tokens, finished = C.c_int64(), C.c_int32()
+        """(tokens processed, tokens generated, sequences finished, last ids per sequence)."""
+        tokens, generated, finished = C.c_int64(), C.c_int64(), C.c_int32()
         last = np.zeros(max(self._n_seqs, 1), dtype=np.int32)
-        check(lib().needle_cuda_sched_status(self.h, C.byref(tokens), C.byref(finished), ptr(last)))
-        return tokens.value, finished.value, last[:self._n_seqs]
+        check(lib().needle_cuda_sched_status(self.h, C.byref(tokens), C.byref(generated), C.byref(finished),
+                                             ptr(last)))
+        return tokens.value, generated.value, finished.value, last[:self._n_seqs]
+
+    def kernel_launches(self) -> int:
+        n = C.c_int64()
+        check(lib().needle_cuda_kernel_launches(self.h, C.byref(n)))
+        return n.value
 
     # per-kernel-class event timing ----------------------------------------------------------
     def profile(self, enable: bool):

@@ -71,6 +71,30 @@ __device__ __forceinline__ void fwht_smem(float* v, int len, int groups) {
   }
 }
 
+// In-place FWHTs of consecutive blocks of `len` values (power of two, >= 32), one value per thread:
+// threads [0, active) hold the values (active a multiple of len).  Strides below 32 run in
+// registers with warp shuffles, larger strides through shared memory `v` (>= active floats).
+// Same butterflies, same binary32 results as fwht_smem.  Every thread of the block calls it.
+__device__ __forceinline__ float fwht_reg(float mine, float* v, int len, int active) {
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+#pragma unroll
+  for (int stride = 1; stride < 32; stride <<= 1) {
+    const float other = __shfl_xor_sync(0xffffffffu, mine, stride);
+    mine = (lane & stride) ? __fsub_rn(other, mine) : __fadd_rn(mine, other);
+  }
+  for (int stride = 32; stride < len; stride <<= 1) {
+    if (t < active) v[t] = mine;
+    __syncthreads();
+    if (t < active) {
+      const float other = v[t ^ stride];
+      mine = (t & stride) ? __fsub_rn(other, mine) : __fadd_rn(mine, other);
+    }
+    __syncthreads();
+  }
+  return mine;
+}
+
 // Sequential binary64 sum of squares (the `sumSquares += value * value` loops of rmsNorm /
 // rmsUnit, math.ts:16-44) run by one thread.  value*value is exact in binary64, so each step is
 // fma(v, v, s) == round(s + v*v).
@@ -82,6 +106,56 @@ __device__ __forceinline__ double sum_squares_seq(const float* v, int n) {
     s = fma(x, x, s);
   }
   return s;
+}
+
+// Sequential binary64 sum of n precomputed terms, in index order (one thread).  The terms are
+// staged in shared memory by the whole block first, so the dependent chain is one add per term;
+// the next eight terms are loaded while the current eight are added.
+__device__ __forceinline__ double sum_seq(const double* terms, int n) {
+  double s = 0.0;
+  int i = 0;
+  if (n >= 8) {
+    double2 a = *reinterpret_cast<const double2*>(terms);
+    double2 b = *reinterpret_cast<const double2*>(terms + 2);
+    double2 c = *reinterpret_cast<const double2*>(terms + 4);
+    double2 d = *reinterpret_cast<const double2*>(terms + 6);
+#pragma unroll 1
+    for (; i + 16 <= n; i += 8) {
+      const double2 na = *reinterpret_cast<const double2*>(terms + i + 8);
+      const double2 nb = *reinterpret_cast<const double2*>(terms + i + 10);
+      const double2 nc = *reinterpret_cast<const double2*>(terms + i + 12);
+      const double2 nd = *reinterpret_cast<const double2*>(terms + i + 14);
+      s = s + a.x;
+      s = s + a.y;
+      s = s + b.x;
+      s = s + b.y;
+      s = s + c.x;
+      s = s + c.y;
+      s = s + d.x;
+      s = s + d.y;
+      a = na;
+      b = nb;
+      c = nc;
+      d = nd;
+    }
+    s = s + a.x;
+    s = s + a.y;
+    s = s + b.x;
+    s = s + b.y;
+    s = s + c.x;
+    s = s + c.y;
+    s = s + d.x;
+    s = s + d.y;
+    i += 8;
+  }
+  for (; i < n; i++) s = s + terms[i];
+  return s;
+}
+
+// Exact binary64 value of a small integer (|v| < 2^31) through the FP64 add pipe instead of the
+// conversion unit: the bit pattern 0x4338000000000000 + v is the double 2^52 + 2^51 + v.
+__device__ __forceinline__ double int_to_double_exact(int v) {
+  return __longlong_as_double(0x4338000000000000LL + (long long)v) - 6755399441055744.0;
 }
 
 }  // namespace needle

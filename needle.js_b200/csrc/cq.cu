@@ -12,6 +12,9 @@
 // memory is a broadcast.  Groups are consumed in chunks of four (512 inputs), each chunk's dots
 // are folded into the per-(row, item) totals in group order, which keeps the reference's
 // summation order for any input length.
+#include <algorithm>
+#include <atomic>
+
 #include "cq.cuh"
 
 namespace needle {
@@ -56,72 +59,108 @@ struct GroupBytes {
   static constexpr int value = BITS == 4 ? 64 : BITS == 3 ? 48 : 32;  // 128 columns
 };
 
-// Dot products of one (row, group) against kBT items; xs holds [kBT][512] binary64 inputs of the
-// current chunk, `xg` points at this warp's group inside item 0.
+constexpr int kRowsPerThread = 2;
+
+// Dot products of kRowsPerThread rows (same group) against kBT items.  xg points at this warp's
+// group inside item 0 of the staged [kBT][512] binary64 inputs; every x operand is loaded once
+// and used for both rows.
 template <int BITS>
-__device__ __forceinline__ void group_dots(const uint32_t* __restrict__ w, const double* lut,
-                                           const double* __restrict__ xg, int nb, double* dot) {
+__device__ __forceinline__ void group_dots(const uint32_t (&w)[kRowsPerThread][GroupBytes<BITS>::value / 4 + 1],
+                                           const double* lut, const double* __restrict__ xg, int nb,
+                                           double (&dot)[kRowsPerThread][kBT]) {
 #pragma unroll
-  for (int b = 0; b < kBT; b++) dot[b] = 0.0;
+  for (int r = 0; r < kRowsPerThread; r++)
+#pragma unroll
+    for (int b = 0; b < kBT; b++) dot[r][b] = 0.0;
   if constexpr (BITS == 2 || BITS == kTernaryBits) {
-    // 32 bytes: 4 columns per byte, low crumb first.  Fully unrolled so that every word index
-    // is a compile-time constant (the weights stay in registers).
+    // 32 bytes per row: 4 columns per byte, low crumb first.  Fully unrolled so every word index
+    // is a compile-time constant and the weights stay in registers.
 #pragma unroll
     for (int byte_i = 0; byte_i < 32; byte_i++) {
-      const uint32_t byte = (w[byte_i >> 2] >> ((byte_i & 3) * 8)) & 0xffu;
-      const double a0 = lut[byte & 3], a1 = lut[(byte >> 2) & 3];
-      const double a2 = lut[(byte >> 4) & 3], a3 = lut[(byte >> 6) & 3];
+      double a[kRowsPerThread][4];
+#pragma unroll
+      for (int r = 0; r < kRowsPerThread; r++) {
+        const uint32_t byte = (w[r][byte_i >> 2] >> ((byte_i & 3) * 8)) & 0xffu;
+        a[r][0] = lut[byte & 3];
+        a[r][1] = lut[(byte >> 2) & 3];
+        a[r][2] = lut[(byte >> 4) & 3];
+        a[r][3] = lut[(byte >> 6) & 3];
+      }
       const int c = byte_i * 4;
 #pragma unroll
       for (int b = 0; b < kBT; b++) {
         if (b < nb) {
           const double2 x01 = *reinterpret_cast<const double2*>(xg + b * 512 + c);
           const double2 x23 = *reinterpret_cast<const double2*>(xg + b * 512 + c + 2);
-          double s;
-          if constexpr (BITS == 2) {
-            // codebook levels are binary32: every product is exact, so fma == add(product)
-            s = a0 * x01.x;
-            s = fma(a1, x01.y, s);
-            s = fma(a2, x23.x, s);
-            s = fma(a3, x23.y, s);
-          } else {
-            // ternary levels are binary64 (1.2240064 / sqrt(g)): round every product
-            s = a0 * x01.x;
-            s = s + a1 * x01.y;
-            s = s + a2 * x23.x;
-            s = s + a3 * x23.y;
+#pragma unroll
+          for (int r = 0; r < kRowsPerThread; r++) {
+            double s;
+            if constexpr (BITS == 2) {
+              // codebook levels are binary32: every product is exact, so fma == add(product)
+              s = a[r][0] * x01.x;
+              s = fma(a[r][1], x01.y, s);
+              s = fma(a[r][2], x23.x, s);
+              s = fma(a[r][3], x23.y, s);
+            } else {
+              // ternary levels are binary64 (1.2240064 / sqrt(g)): round every product
+              s = a[r][0] * x01.x;
+              s = s + a[r][1] * x01.y;
+              s = s + a[r][2] * x23.x;
+              s = s + a[r][3] * x23.y;
+            }
+            dot[r][b] = dot[r][b] + s;
           }
-          dot[b] = dot[b] + s;
         }
       }
     }
   } else if constexpr (BITS == 4) {
 #pragma unroll
     for (int byte_i = 0; byte_i < 64; byte_i++) {
-      const uint32_t byte = (w[byte_i >> 2] >> ((byte_i & 3) * 8)) & 0xffu;
-      const double a0 = lut[byte & 15], a1 = lut[byte >> 4];
+      double a[kRowsPerThread][2];
+#pragma unroll
+      for (int r = 0; r < kRowsPerThread; r++) {
+        const uint32_t byte = (w[r][byte_i >> 2] >> ((byte_i & 3) * 8)) & 0xffu;
+        a[r][0] = lut[byte & 15];
+        a[r][1] = lut[byte >> 4];
+      }
       const int c = byte_i * 2;
 #pragma unroll
       for (int b = 0; b < kBT; b++) {
         if (b < nb) {
           const double2 x01 = *reinterpret_cast<const double2*>(xg + b * 512 + c);
-          double s = a0 * x01.x;
-          s = fma(a1, x01.y, s);
-          dot[b] = dot[b] + s;
+#pragma unroll
+          for (int r = 0; r < kRowsPerThread; r++) {
+            double s = a[r][0] * x01.x;
+            s = fma(a[r][1], x01.y, s);
+            dot[r][b] = dot[r][b] + s;
+          }
         }
       }
     }
-  } else {  // 3-bit: one column per step, dot = round(dot + level * x) with an exact product
+  } else {  // 3-bit: dot = round(dot + level * x) per column, exact products; two columns a step
 #pragma unroll
-    for (int c = 0; c < kGroup; c++) {
-      const int bit = c * 3;
-      const int wi = bit >> 5, sh = bit & 31;
-      uint32_t v = w[wi] >> sh;
-      if (sh > 29) v |= w[wi + 1] << (32 - sh);
-      const double a = lut[v & 7];
+    for (int c = 0; c < kGroup; c += 2) {
+      double a[kRowsPerThread][2];
+#pragma unroll
+      for (int r = 0; r < kRowsPerThread; r++)
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+          const int bit = (c + k) * 3;
+          const int wi = bit >> 5, sh = bit & 31;
+          uint32_t v = w[r][wi] >> sh;
+          if (sh > 29) v |= w[r][wi + 1] << (32 - sh);
+          a[r][k] = lut[v & 7];
+        }
 #pragma unroll
       for (int b = 0; b < kBT; b++)
-        if (b < nb) dot[b] = fma(a, xg[b * 512 + c], dot[b]);
+        if (b < nb) {
+          const double2 x = *reinterpret_cast<const double2*>(xg + b * 512 + c);
+#pragma unroll
+          for (int r = 0; r < kRowsPerThread; r++) {
+            dot[r][b] = fma(a[r][0], x.x, dot[r][b]);
+            dot[r][b] = fma(a[r][1], x.y, dot[r][b]);
+          }
+        }
     }
   }
 }
@@ -129,30 +168,17 @@ __device__ __forceinline__ void group_dots(const uint32_t* __restrict__ w, const
 template <int BITS>
 __global__ void __launch_bounds__(kGemvThreads)
 k_cq_gemv(const CqJobs jobs, const Codebook cb, int32_t n_host, const int32_t* n_dev) {
+  constexpr int kTileRows = kRowsPerTile * kRowsPerThread;  // 64
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  double* xs = reinterpret_cast<double*>(smem_raw);        // [kBT][512]
-  double* dsm = xs + kBT * 512;                            // [kBT][4][32]
-  double* lut = dsm + kBT * kGroupsPerChunk * kRowsPerTile;  // [16]
+  double* xs = reinterpret_cast<double*>(smem_raw);          // [kBT][512]
+  double* dsm = xs + kBT * 512;                              // [kBT][4][64]
+  double* lut = dsm + kBT * kGroupsPerChunk * kTileRows;     // [16]
 
   const int n = item_count(n_host, n_dev);
-  const int b0 = blockIdx.y * kBT;
-  if (b0 >= n) return;
-  const int nb = min(kBT, n - b0);
-
-  // Locate this tile's job.
-  int j = 0;
-#pragma unroll 1
-  for (int k = 1; k < jobs.count; k++)
-    if ((int)blockIdx.x >= jobs.job[k].tile_begin) j = k;
-  const CqJob& job = jobs.job[j];
-  const int tile = blockIdx.x - job.tile_begin;
+  const int item_tiles = (n + kBT - 1) / kBT;
+  const int units = jobs.total_tiles * item_tiles;
   const int lane = threadIdx.x & 31;
   const int gc = threadIdx.x >> 5;  // group within the chunk
-  const int r_local = tile * kRowsPerTile + lane;
-  const bool row_ok = r_local < job.rows;
-  const int64_t row = (int64_t)job.row_start + r_local;
-  const int groups = job.in_pad / kGroup;
-
   if (threadIdx.x < 16) {
     double v = 0.0;
     if (BITS == kTernaryBits) {
@@ -165,67 +191,93 @@ k_cq_gemv(const CqJobs jobs, const Codebook cb, int32_t n_host, const int32_t* n
     lut[threadIdx.x] = v;
   }
 
-  // Totals owned by this thread: pairs (row lane, item) = threadIdx.x + k * 128.
-  constexpr int kPairs = kRowsPerTile * kBT / kGemvThreads;  // 2
-  double total[kPairs];
-#pragma unroll
-  for (int k = 0; k < kPairs; k++) total[k] = 0.0;
+  // Persistent loop over (row tile, item tile) units; consecutive units share an item tile.
+#pragma unroll 1
+  for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+    const int gtile = unit % jobs.total_tiles;
+    const int b0 = (unit / jobs.total_tiles) * kBT;
+    const int nb = min(kBT, n - b0);
+    int j = 0;
+#pragma unroll 1
+    for (int k = 1; k < jobs.count; k++)
+      if (gtile >= jobs.job[k].tile_begin) j = k;
+    const CqJob& job = jobs.job[j];
+    const int tile = gtile - job.tile_begin;
+    const int groups = job.in_pad / kGroup;
 
-  for (int g0 = 0; g0 < groups; g0 += kGroupsPerChunk) {
-    const int gn = min(kGroupsPerChunk, groups - g0);
-    __syncthreads();  // previous chunk's xs / dsm fully consumed
-    // Stage the chunk's inputs as binary64 (exact widening).
-    for (int idx = threadIdx.x; idx < nb * gn * kGroup; idx += kGemvThreads) {
-      const int b = idx / (gn * kGroup);
-      const int c = idx - b * gn * kGroup;
-      xs[b * 512 + c] = (double)job.x[(int64_t)(b0 + b) * job.x_stride + g0 * kGroup + c];
-    }
-    __syncthreads();
-    double dot[kBT];
-    if (gc < gn && row_ok) {
-      constexpr int kWords = GroupBytes<BITS>::value / 4;
-      uint32_t w[kWords + 1];
-      const uint4* src = reinterpret_cast<const uint4*>(job.packed + row * job.row_bytes +
-                                                        (int64_t)(g0 + gc) * GroupBytes<BITS>::value);
+    // Totals owned by this thread: pairs (tile row, item) = threadIdx.x + k * 128.
+    constexpr int kPairs = kTileRows * kBT / kGemvThreads;  // 4
+    double total[kPairs];
 #pragma unroll
-      for (int q = 0; q < kWords / 4; q++) {
-        const uint4 u = __ldg(src + q);
-        w[4 * q] = u.x;
-        w[4 * q + 1] = u.y;
-        w[4 * q + 2] = u.z;
-        w[4 * q + 3] = u.w;
+    for (int k = 0; k < kPairs; k++) total[k] = 0.0;
+
+    for (int g0 = 0; g0 < groups; g0 += kGroupsPerChunk) {
+      const int gn = min(kGroupsPerChunk, groups - g0);
+      __syncthreads();  // previous chunk's xs / dsm fully consumed
+      // Stage the chunk's inputs as binary64 (exact widening).
+      for (int idx = threadIdx.x; idx < nb * gn * kGroup; idx += kGemvThreads) {
+        const int b = idx / (gn * kGroup);
+        const int c = idx - b * gn * kGroup;
+        xs[b * 512 + c] = (double)job.x[(int64_t)(b0 + b) * job.x_stride + g0 * kGroup + c];
       }
-      w[kWords] = 0;
-      group_dots<BITS>(w, lut, xs + gc * kGroup, nb, dot);
-    } else {
+      __syncthreads();
+      double dot[kRowsPerThread][kBT];
+      constexpr int kWords = GroupBytes<BITS>::value / 4;
+      uint32_t w[kRowsPerThread][kWords + 1];
+      bool any = false;
 #pragma unroll
-      for (int b = 0; b < kBT; b++) dot[b] = 0.0;
+      for (int r = 0; r < kRowsPerThread; r++) {
+        const int r_local = tile * kTileRows + r * 32 + lane;
+        const bool ok = gc < gn && r_local < job.rows;
+        any |= ok;
+        const uint4* src = reinterpret_cast<const uint4*>(
+            job.packed + ((int64_t)job.row_start + r_local) * job.row_bytes + (int64_t)(g0 + gc) * GroupBytes<BITS>::value);
+#pragma unroll
+        for (int q = 0; q < kWords / 4; q++) {
+          const uint4 u = ok ? __ldg(src + q) : make_uint4(0, 0, 0, 0);
+          w[r][4 * q] = u.x;
+          w[r][4 * q + 1] = u.y;
+          w[r][4 * q + 2] = u.z;
+          w[r][4 * q + 3] = u.w;
+        }
+        w[r][kWords] = 0;
+      }
+      if (any) {
+        group_dots<BITS>(w, lut, xs + gc * kGroup, nb, dot);
+      } else {
+#pragma unroll
+        for (int r = 0; r < kRowsPerThread; r++)
+#pragma unroll
+          for (int b = 0; b < kBT; b++) dot[r][b] = 0.0;
+      }
+#pragma unroll
+      for (int r = 0; r < kRowsPerThread; r++)
+#pragma unroll
+        for (int b = 0; b < kBT; b++) dsm[(b * kGroupsPerChunk + gc) * kTileRows + r * 32 + lane] = dot[r][b];
+      __syncthreads();
+      // total += norm * dot, group by group in order (cq.ts:151).
+#pragma unroll
+      for (int k = 0; k < kPairs; k++) {
+        const int pair = threadIdx.x + k * kGemvThreads;
+        const int rl = pair % kTileRows, b = pair / kTileRows;
+        const int64_t prow = (int64_t)job.row_start + tile * kTileRows + rl;
+        if (b < nb && tile * kTileRows + rl < job.rows) {
+          double t = total[k];
+          for (int q = 0; q < gn; q++) {
+            const double nrm = norm16(job.norms, prow * groups + g0 + q);
+            t = t + nrm * dsm[(b * kGroupsPerChunk + q) * kTileRows + rl];
+          }
+          total[k] = t;
+        }
+      }
     }
-#pragma unroll
-    for (int b = 0; b < kBT; b++) dsm[(b * kGroupsPerChunk + gc) * kRowsPerTile + lane] = dot[b];
-    __syncthreads();
-    // total += norm * dot, group by group in order (cq.ts:151).
 #pragma unroll
     for (int k = 0; k < kPairs; k++) {
       const int pair = threadIdx.x + k * kGemvThreads;
-      const int rl = pair & 31, b = pair >> 5;
-      const int64_t prow = (int64_t)job.row_start + tile * kRowsPerTile + rl;
-      if (b < nb && tile * kRowsPerTile + rl < job.rows) {
-        double t = total[k];
-        for (int q = 0; q < gn; q++) {
-          const double nrm = norm16(job.norms, prow * groups + g0 + q);
-          t = t + nrm * dsm[(b * kGroupsPerChunk + q) * kRowsPerTile + rl];
-        }
-        total[k] = t;
-      }
+      const int rl = pair % kTileRows, b = pair / kTileRows;
+      const int r = tile * kTileRows + rl;
+      if (b < nb && r < job.rows) job.y[(int64_t)(b0 + b) * job.y_stride + r] = f32(total[k]);
     }
-  }
-#pragma unroll
-  for (int k = 0; k < kPairs; k++) {
-    const int pair = threadIdx.x + k * kGemvThreads;
-    const int rl = pair & 31, b = pair >> 5;
-    const int r = tile * kRowsPerTile + rl;
-    if (b < nb && r < job.rows) job.y[(int64_t)(b0 + b) * job.y_stride + r] = f32(total[k]);
   }
 }
 
@@ -267,16 +319,51 @@ cudaError_t launch_cq_prepare(const float* x, int32_t x_stride, int32_t input_si
 }
 
 static size_t gemv_smem() {
-  return sizeof(double) * (kBT * 512 + kBT * kGroupsPerChunk * kRowsPerTile + 16);
+  return sizeof(double) * (kBT * 512 + kBT * kGroupsPerChunk * kRowsPerTile * kRowsPerThread + 16);
+}
+
+// Opts the GEMV instantiations into more than 48 KB of dynamic shared memory, once per device.
+static cudaError_t configure_gemv() {
+  static std::atomic<uint64_t> done{0};
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (device & 63);
+  if (done.load() & bit) return cudaSuccess;
+  const int smem = (int)gemv_smem();
+  if ((e = cudaFuncSetAttribute(k_cq_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(k_cq_gemv<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(k_cq_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(k_cq_gemv<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+  done.fetch_or(bit);
+  return cudaSuccess;
+}
+
+// CTAs of k_cq_gemv that fit on the device at once (the persistent grid size).
+static int gemv_resident_ctas() {
+  static std::atomic<int> cached[64];
+  int device = 0;
+  cudaGetDevice(&device);
+  int v = cached[device & 63].load();
+  if (v > 0) return v;
+  int per_sm = 0, sms = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_cq_gemv<2>, kGemvThreads, gemv_smem());
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  v = std::max(1, per_sm) * std::max(1, sms);
+  cached[device & 63].store(v);
+  return v;
 }
 
 cudaError_t launch_cq_gemv(const CqJobs& jobs, const Codebook& cb, int32_t n_host,
                            const int32_t* n_dev, cudaStream_t s) {
   if (n_host <= 0 || jobs.count <= 0) return cudaSuccess;
+  cudaError_t ce = configure_gemv();
+  if (ce != cudaSuccess) return ce;
   const int bits = jobs.job[0].bits;
   for (int k = 1; k < jobs.count; k++)
     if (jobs.job[k].bits != bits) return cudaErrorInvalidValue;
-  dim3 grid(jobs.total_tiles, (n_host + kBT - 1) / kBT);
+  const int units = jobs.total_tiles * ((n_host + kBT - 1) / kBT);
+  dim3 grid(std::min(units, gemv_resident_ctas()));
   const size_t smem = gemv_smem();
   switch (bits) {
     case 2: k_cq_gemv<2><<<grid, kGemvThreads, smem, s>>>(jobs, cb, n_host, n_dev); break;

@@ -6,6 +6,9 @@
 
 namespace needle {
 
+// Rows of one GEMV tile (a CTA): tiles of consecutive rows are the unit of CqJob::tile_begin.
+constexpr int kGemvTileRows = 64;
+
 // One matrix-times-batch job of a GEMV launch.  Rows [row_start, row_start + rows) of the matrix
 // multiply the prepared inputs x[i * x_stride ...] of every item i; row r of the job lands in
 // y[i * y_stride + r].
@@ -17,7 +20,7 @@ struct CqJob {
   int32_t in_pad;          // padded input length (multiple of 128)
   int32_t bits;            // 2, 3, 4 or 5 (ternary)
   int32_t row_bytes;
-  int32_t tile_begin;      // first 32-row tile of this job in the launch
+  int32_t tile_begin;      // first kGemvTileRows-row tile of this job in the launch
   const float* x;
   int32_t x_stride;
   int32_t y_stride;

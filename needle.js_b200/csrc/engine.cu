@@ -273,9 +273,10 @@ struct ProfEntry {
 };
 
 const char* kProfNames[] = {"embed", "gemv_engram", "layer", "gemv_qkvg", "attention", "gemv_o",
-                            "gemv_vocab", "finish", "sched", "copy"};
-constexpr int kProfClasses = 10;
-enum { P_EMBED, P_GEMV_ENGRAM, P_LAYER, P_GEMV_QKVG, P_ATTN, P_GEMV_O, P_GEMV_VOCAB, P_FINISH, P_SCHED, P_COPY };
+                            "gemv_vocab", "finish", "sched", "copy", "route"};
+constexpr int kProfClasses = 11;
+enum { P_EMBED, P_GEMV_ENGRAM, P_LAYER, P_GEMV_QKVG, P_ATTN, P_GEMV_O, P_GEMV_VOCAB, P_FINISH, P_SCHED, P_COPY,
+       P_ROUTE };
 
 }  // namespace
 
@@ -285,6 +286,8 @@ struct needle_ctx {
   needle_opts opts{};
   int device = 0;
   cudaStream_t stream = nullptr;
+  cudaStream_t side = nullptr;             // routing (Sinkhorn) overlapped with attention
+  cudaEvent_t fork_ev[2] = {nullptr, nullptr}, join_ev[2] = {nullptr, nullptr};
   std::vector<uint8_t> bytes;  // archive copy (host)
   Archive A;
   Roles roles;
@@ -317,6 +320,7 @@ struct needle_ctx {
   float* d_row_out = nullptr;
   // profiling
   bool profiling = false;
+  int64_t launches = 0;  // kernels launched by this context
   std::vector<ProfEntry> prof_pending;
   std::vector<cudaEvent_t> event_pool;
   double prof_ms[kProfClasses] = {0};
@@ -357,6 +361,7 @@ struct needle_ctx {
   // Runs `launch` bracketed by events when profiling.
   template <class F>
   void timed(int cls, F&& launch) {
+    if (cls != P_COPY) launches += cls == P_SCHED ? 2 : 1;
     if (!profiling) {
       cuda_check(launch(), kProfNames[cls]);
       return;
@@ -619,7 +624,7 @@ void add_job(CqJobs& J, const CqMat& M, int row_start, int rows, const float* x,
   j.x_stride = x_stride;
   j.y = y;
   j.y_stride = y_stride;
-  J.total_tiles += (rows + 31) / 32;
+  J.total_tiles += (rows + kGemvTileRows - 1) / kGemvTileRows;
 }
 
 struct JobSpec {
@@ -663,8 +668,15 @@ void enqueue_step(needle_ctx& C, int n_host, bool any_select, const SchedView* s
     run_gemv(C, P_GEMV_ENGRAM, jobs, n_host, n_dev);
   }
   for (int l = 0; l <= m.layers; l++) {
+    if (l > 0) cuda_check(cudaStreamWaitEvent(C.stream, C.join_ev[(l - 1) & 1], 0), "join");
     C.timed(P_LAYER, [&] { return launch_layer(m, sv, st, l, n_host, C.stream); });
     if (l == m.layers) break;
+    // Sinkhorn routing of layer l on the side stream, joined before the next k_layer.
+    cuda_check(cudaEventRecord(C.fork_ev[l & 1], C.stream), "fork");
+    cuda_check(cudaStreamWaitEvent(C.side, C.fork_ev[l & 1], 0), "fork");
+    cuda_check(launch_route(st, n_host, C.side), "route");
+    C.launches++;
+    cuda_check(cudaEventRecord(C.join_ev[l & 1], C.side), "join");
     run_gemv(C, P_GEMV_QKVG,
              {{C.lq[l], 0, 512, st.prep_a, kDim, st.qkvg, 1536},
               {C.lk[l], 0, 256, st.prep_a, kDim, st.qkvg + 512, 1536},
@@ -706,6 +718,11 @@ void destroy(needle_ctx* C) {
   if (C->h_counts) cudaFreeHost(C->h_counts);
   if (C->h_ids) cudaFreeHost(C->h_ids);
   if (C->h_logprob) cudaFreeHost(C->h_logprob);
+  for (int k = 0; k < 2; k++) {
+    if (C->fork_ev[k]) cudaEventDestroy(C->fork_ev[k]);
+    if (C->join_ev[k]) cudaEventDestroy(C->join_ev[k]);
+  }
+  if (C->side) cudaStreamDestroy(C->side);
   if (C->stream) cudaStreamDestroy(C->stream);
   delete C;
 }
@@ -780,6 +797,11 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
     require(int64_t(o.max_len) <= int64_t(C->A.hdr[11]), NEEDLE_CONTEXT_OVERFLOW,
             "max_len exceeds the model's maximum sequence length");
     cuda_check(cudaStreamCreateWithFlags(&C->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    cuda_check(cudaStreamCreateWithFlags(&C->side, cudaStreamNonBlocking), "cudaStreamCreate");
+    for (int k = 0; k < 2; k++) {
+      cuda_check(cudaEventCreateWithFlags(&C->fork_ev[k], cudaEventDisableTiming), "cudaEventCreate");
+      cuda_check(cudaEventCreateWithFlags(&C->join_ev[k], cudaEventDisableTiming), "cudaEventCreate");
+    }
     build_model(*C);
     build_state(*C);
     cuda_check(cudaDeviceSynchronize(), "upload");
@@ -1123,6 +1145,7 @@ int needle_cuda_sched_load(needle_ctx* ctx, int32_t n_slots, const int32_t* prom
     q.next_seq = d_ctr;
     q.finished = d_ctr + 1;
     q.processed = reinterpret_cast<int64_t*>(d_ctr + 2);
+    q.generated = reinterpret_cast<int64_t*>(d_ctr + 4);
     q.last_ids = d_last;
     C.sched_loaded = true;
     cuda_check(launch_sched_admit(C.sv, q, window, C.stream), "admit");
@@ -1145,20 +1168,30 @@ int needle_cuda_sched_step(needle_ctx* ctx, int32_t steps) {
   });
 }
 
-int needle_cuda_sched_status(needle_ctx* ctx, int64_t* tokens_processed, int32_t* seqs_finished, int32_t* last_ids) {
+int needle_cuda_sched_status(needle_ctx* ctx, int64_t* tokens_processed, int64_t* tokens_generated,
+                             int32_t* seqs_finished, int32_t* last_ids) {
   return guarded([&] {
     needle_ctx& C = *ctx_of(ctx);
     require(C.sched_loaded, NEEDLE_BACKEND_UNAVAILABLE, "no scheduler queue loaded");
     cuda_check(cudaStreamSynchronize(C.stream), "sched_status");
-    int32_t ctr[4];
-    cuda_check(cudaMemcpy(ctr, C.sched.next_seq, 16, cudaMemcpyDeviceToHost), "sched_status");
-    int64_t processed = 0;
+    int32_t ctr[6];
+    cuda_check(cudaMemcpy(ctr, C.sched.next_seq, 24, cudaMemcpyDeviceToHost), "sched_status");
+    int64_t processed = 0, generated = 0;
     std::memcpy(&processed, ctr + 2, 8);
+    std::memcpy(&generated, ctr + 4, 8);
     if (tokens_processed) *tokens_processed = processed;
+    if (tokens_generated) *tokens_generated = generated;
     if (seqs_finished) *seqs_finished = ctr[1];
     if (last_ids && C.sched.n_seqs > 0)
       cuda_check(cudaMemcpy(last_ids, C.sched.last_ids, size_t(C.sched.n_seqs) * 4, cudaMemcpyDeviceToHost),
                  "sched_status");
+  });
+}
+
+int needle_cuda_kernel_launches(const needle_ctx* ctx, int64_t* count) {
+  return guarded([&] {
+    require(ctx && count, NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+    *count = ctx->launches;
   });
 }
 

@@ -102,6 +102,7 @@ struct SchedView {
   int32_t* next_seq;              // queue head
   int32_t* finished;              // finished count
   int64_t* processed;             // tokens processed
+  int64_t* generated;             // tokens selected (generated)
   int32_t* last_ids;              // [n_seqs]
 };
 
@@ -109,6 +110,8 @@ cudaError_t launch_embed(const ModelView& m, const SlotView& sv, const StepView&
                          cudaStream_t s);
 cudaError_t launch_layer(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
                          int n_host, cudaStream_t s);
+// Sinkhorn routing of the layer's items (reads and writes StepView::route[4..19]).
+cudaError_t launch_route(const StepView& st, int n_host, cudaStream_t s);
 cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
                              int n_host, cudaStream_t s);
 cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,

@@ -42,56 +42,7 @@ __device__ __forceinline__ int round_ties_even(double value) {
   return (((long long)lower) & 1) == 0 ? (int)lower : (int)lower + 1;
 }
 
-// Exact dot of one 128-group of a CQ row with binary64 inputs, in the reference's chunk order
-// (cq.ts:132-230).  `lut` holds the matrix's levels as binary64 (ternary: crumbs [0, c, 0, -c]).
-__device__ double group_dot_exact(const uint8_t* __restrict__ rowp, int bits, int g,
-                                  const double* lut, const double* xg) {
-  double dot = 0.0;
-  if (bits == 2 || bits == kTernaryBits) {
-    const uint8_t* p = rowp + g * 32;
-    for (int i = 0; i < 32; i++) {
-      const int byte = __ldg(p + i);
-      const double a0 = lut[byte & 3], a1 = lut[(byte >> 2) & 3];
-      const double a2 = lut[(byte >> 4) & 3], a3 = lut[(byte >> 6) & 3];
-      const double* x = xg + i * 4;
-      double s = a0 * x[0];
-      if (bits == 2) {
-        s = fma(a1, x[1], s);
-        s = fma(a2, x[2], s);
-        s = fma(a3, x[3], s);
-      } else {
-        s = s + a1 * x[1];
-        s = s + a2 * x[2];
-        s = s + a3 * x[3];
-      }
-      dot = dot + s;
-    }
-  } else if (bits == 4) {
-    const uint8_t* p = rowp + g * 64;
-    for (int i = 0; i < 64; i++) {
-      const int byte = __ldg(p + i);
-      double s = lut[byte & 15] * xg[2 * i];
-      s = fma(lut[byte >> 4], xg[2 * i + 1], s);
-      dot = dot + s;
-    }
-  } else {
-    for (int c = 0; c < kGroup; c++) dot = fma(lut[cq_index(rowp, 3, g * kGroup + c)], xg[c], dot);
-  }
-  return dot;
-}
 
-__device__ void fill_lut(double* lut, const float* cb28, int bits) {
-  for (int t = threadIdx.x; t < 16; t += blockDim.x) {
-    double v = 0.0;
-    if (bits == kTernaryBits) {
-      const double coefficient = kTernaryCentroid / sqrt((double)kGroup);
-      v = (t == 1) ? coefficient : (t == 3) ? -coefficient : 0.0;
-    } else if (t < (1 << bits)) {
-      v = (double)cb28[(bits == 2 ? 0 : bits == 3 ? 4 : 12) + t];
-    }
-    lut[t] = v;
-  }
-}
 
 // One thread's sequential sum of squares -> 1 / sqrt(s / n + 1e-6) (rmsNorm / rmsUnit).
 __device__ __forceinline__ double inverse_rms(const float* v, int n) {
@@ -192,15 +143,16 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
 
 struct LayerSmem {
   float xl[kLaneWidth];     // lanes x
-  float work[kLaneWidth];   // rmsUnit lanes / prepared phi input
+  double sq[kLaneWidth];    // terms of a sequential binary64 sum (squares / products)
+  double sq2[kDim];         // terms of a second, concurrent sum
   double xd[kLaneWidth];    // prepared phi input in binary64
+  float fw[kDim];           // FWHT exchange buffer
   double dots[24 * 16];     // phi (row, group) dots
   double lut[3][16];
-  float a[kDim], bvec[kDim], c[kDim], d[kDim];
   float phi[24];
   float hpre[kLanes], hpost[kLanes], routing[16];
   double red[4];
-  double sk[16];            // Sinkhorn working copy (Float64Array)
+  double sk[16];            // routing logits (Float64Array of the Float32Array, math.ts:64)
 };
 
 __device__ void engram_mix(const ModelView& m, const SlotView& sv, const StepView& st, int b,
@@ -251,6 +203,88 @@ __device__ void sinkhorn4(double* v, float* out, int lane) {
   if (lane < 16) out[lane] = f32(exp(v[lane]));
 }
 
+// Exact dot of one 128-group of a CQ row with binary64 inputs, in the reference's chunk order
+// (cq.ts:132-230).  `grp` is the group's 16-byte-aligned packed bytes; `lut` holds the matrix's
+// levels as binary64 (ternary: crumbs [0, c, 0, -c]).
+template <int BITS>
+__device__ double group_dot_t(const uint8_t* __restrict__ grp, const double* lut, const double* xg) {
+  constexpr int kWords = (BITS == 4 ? 64 : BITS == 3 ? 48 : 32) / 4;
+  uint32_t w[kWords + 1];
+#pragma unroll
+  for (int q = 0; q < kWords / 4; q++) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(grp) + q);
+    w[4 * q] = u.x;
+    w[4 * q + 1] = u.y;
+    w[4 * q + 2] = u.z;
+    w[4 * q + 3] = u.w;
+  }
+  w[kWords] = 0;
+  double dot = 0.0;
+  if constexpr (BITS == 2 || BITS == kTernaryBits) {
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      const uint32_t byte = (w[i >> 2] >> ((i & 3) * 8)) & 0xffu;
+      const double a0 = lut[byte & 3], a1 = lut[(byte >> 2) & 3];
+      const double a2 = lut[(byte >> 4) & 3], a3 = lut[(byte >> 6) & 3];
+      const double2 x01 = *reinterpret_cast<const double2*>(xg + 4 * i);
+      const double2 x23 = *reinterpret_cast<const double2*>(xg + 4 * i + 2);
+      double s = a0 * x01.x;
+      if constexpr (BITS == 2) {
+        s = fma(a1, x01.y, s);
+        s = fma(a2, x23.x, s);
+        s = fma(a3, x23.y, s);
+      } else {
+        s = s + a1 * x01.y;
+        s = s + a2 * x23.x;
+        s = s + a3 * x23.y;
+      }
+      dot = dot + s;
+    }
+  } else if constexpr (BITS == 4) {
+#pragma unroll
+    for (int i = 0; i < 64; i++) {
+      const uint32_t byte = (w[i >> 2] >> ((i & 3) * 8)) & 0xffu;
+      const double2 x01 = *reinterpret_cast<const double2*>(xg + 2 * i);
+      double s = lut[byte & 15] * x01.x;
+      s = fma(lut[byte >> 4], x01.y, s);
+      dot = dot + s;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < kGroup; c++) {
+      const int bit = c * 3, wi = bit >> 5, sh = bit & 31;
+      uint32_t v = w[wi] >> sh;
+      if (sh > 29) v |= w[wi + 1] << (32 - sh);
+      dot = fma(lut[v & 7], xg[c], dot);
+    }
+  }
+  return dot;
+}
+
+__device__ __forceinline__ double group_dot_exact(const uint8_t* grp, int bits, const double* lut,
+                                                  const double* xg) {
+  switch (bits) {
+    case 2: return group_dot_t<2>(grp, lut, xg);
+    case 3: return group_dot_t<3>(grp, lut, xg);
+    case 4: return group_dot_t<4>(grp, lut, xg);
+    default: return group_dot_t<kTernaryBits>(grp, lut, xg);
+  }
+}
+
+__device__ __forceinline__ double lut_level(const float* cb28, int bits, int t) {
+  if (bits == kTernaryBits) {
+    const double coefficient = kTernaryCentroid / sqrt((double)kGroup);
+    return (t == 1) ? coefficient : (t == 3) ? -coefficient : 0.0;
+  }
+  return t < (1 << bits) ? (double)cb28[(bits == 2 ? 0 : bits == 3 ? 4 : 12) + t] : 0.0;
+}
+
+// 1 / sqrt(sum / n + 1e-6) of rmsNorm / rmsUnit (math.ts:22-27), the sum being the sequential
+// binary64 sum of the staged terms.
+__device__ __forceinline__ double inverse_rms_of(const double* terms, int n) {
+  return 1.0 / sqrt(sum_seq(terms, n) / (double)n + 1e-6);
+}
+
 __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const SlotView sv, const StepView st,
                                                   int layer) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -263,7 +297,6 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
   float* xg = sv.x + (int64_t)slot * kLaneWidth;
   for (int i = tid; i < kLaneWidth; i += kThreads) S.xl[i] = xg[i];
   if (layer == 0 && m.n_sites > 0) engram_mix(m, sv, st, b, slot, p);
-  __syncthreads();
 
   const double inv_root_128 = 1.0 / sqrt((double)kGroup);
   const int c = tid;
@@ -273,36 +306,35 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
     const int l = layer - 1;
     const float upd = st.update[(int64_t)b * kDim + c];
     const float blk = st.block[(int64_t)b * kDim + c];
-    S.a[c] = st.proj[(int64_t)b * kDim + c];
+    const float projected = st.proj[(int64_t)b * kDim + c];
     if (tid < 20) {
       const float r = st.route[(int64_t)b * 20 + tid];
       if (tid < 4) S.hpost[tid] = r;
       else S.routing[tid - 4] = r;
     }
+    S.sq[c] = (double)projected * (double)projected;
     __syncthreads();
-    if (tid == 0) S.red[0] = inverse_rms(S.a, kDim);
+    if (tid == 0) S.red[0] = inverse_rms_of(S.sq, kDim);
     __syncthreads();
     // #attentionDelta (runtime.ts:585-611)
     const float normalized =
-        f32((1.0 + (double)m.post_norm[(int64_t)l * kDim + c]) * (double)S.a[c] * S.red[0]);
+        f32((1.0 + (double)m.post_norm[(int64_t)l * kDim + c]) * (double)projected * S.red[0]);
     const double attention_scale = sigmoid_d((double)m.attn_gate[l]);
     const float after = f32((double)blk + attention_scale * (double)normalized);
-    S.bvec[c] = after;
+    S.sq[c] = (double)after * (double)after;
     __syncthreads();
-    if (tid == 0) S.red[1] = inverse_rms(S.bvec, kDim);
+    if (tid == 0) S.red[1] = inverse_rms_of(S.sq, kDim);
     __syncthreads();
     const float pre = f32((1.0 + (double)m.pre_had_norm[(int64_t)l * kDim + c]) * (double)after * S.red[1]);
     // hadamardMlp (math.ts:117-138)
-    S.c[c] = f32((double)pre * (double)m.d1[(int64_t)l * kHadamard + c]);
-    __syncthreads();
-    fwht_smem(S.c, kHadamard, 1);
     const double inv_root_h = 1.0 / sqrt((double)kHadamard);
-    S.c[c] = f32(silu_d((double)S.c[c] * inv_root_h * (double)m.d2[(int64_t)l * kHadamard + c]));
-    __syncthreads();
-    fwht_smem(S.c, kHadamard, 1);
-    const float mlp = f32((double)S.c[c] * inv_root_h * (double)m.d3[(int64_t)l * kHadamard + c]);
+    float v = f32((double)pre * (double)m.d1[(int64_t)l * kHadamard + c]);
+    v = fwht_reg(v, S.fw, kHadamard, kThreads);
+    v = f32(silu_d((double)v * inv_root_h * (double)m.d2[(int64_t)l * kHadamard + c]));
+    v = fwht_reg(v, S.fw, kHadamard, kThreads);
+    const float mlp = f32((double)v * inv_root_h * (double)m.d3[(int64_t)l * kHadamard + c]);
     const float delta = f32((double)after + (double)mlp - (double)upd);
-    // nextX (runtime.ts:530-541)
+    // nextX (runtime.ts:530-541); thread c owns column c of every lane.
     float nx[kLanes];
 #pragma unroll
     for (int lane = 0; lane < kLanes; lane++) {
@@ -312,77 +344,79 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
         sum = fma((double)S.routing[lane * kLanes + src], (double)S.xl[src * kDim + c], sum);
       nx[lane] = f32(sum + (double)S.hpost[lane] * (double)delta);
     }
-    __syncthreads();
 #pragma unroll
     for (int lane = 0; lane < kLanes; lane++) {
       S.xl[lane * kDim + c] = nx[lane];
       xg[lane * kDim + c] = nx[lane];
     }
-    __syncthreads();
   }
+  __syncthreads();
 
   if (layer == m.layers) {
     // ---------------- final: lane mean, RMSNorm, prepared vocabulary input (runtime.ts:570-577)
     double sum = 0.0;
 #pragma unroll
     for (int lane = 0; lane < kLanes; lane++) sum = sum + (double)S.xl[lane * kDim + c];
-    S.a[c] = f32(sum / (double)kLanes);
+    const float mean = f32(sum / (double)kLanes);
+    S.sq[c] = (double)mean * (double)mean;
     __syncthreads();
-    if (tid == 0) S.red[0] = inverse_rms(S.a, kDim);
+    if (tid == 0) S.red[0] = inverse_rms_of(S.sq, kDim);
     __syncthreads();
-    S.c[c] = f32((1.0 + (double)m.final_norm[c]) * (double)S.a[c] * S.red[0]);
-    __syncthreads();
-    fwht_smem(S.c, kGroup, kDim / kGroup);
-    st.prep_f[(int64_t)b * kDim + c] = f32((double)S.c[c] * inv_root_128);
+    float f = f32((1.0 + (double)m.final_norm[c]) * (double)mean * S.red[0]);
+    f = fwht_reg(f, S.fw, kGroup, kThreads);
+    st.prep_f[(int64_t)b * kDim + c] = f32((double)f * inv_root_128);
     return;
   }
 
   // ---------------- input side of layer l
   const int l = layer;
-  if (tid == 0) S.red[2] = inverse_rms(S.xl, kLaneWidth);  // rmsUnit(x), runtime.ts:385
-  fill_lut(S.lut[0], m.cb.v, m.phi_pre.bits);
-  if (tid >= 16 && tid < 32) {
-    double* lut1 = S.lut[1];
-    double* lut2 = S.lut[2];
-    const int t = tid - 16;
-    // (same construction as fill_lut, for the phi_post / phi_res matrices)
-    for (int k = 0; k < 2; k++) {
-      const int bits = k == 0 ? m.phi_post.bits : m.phi_res.bits;
-      double v = 0.0;
-      if (bits == kTernaryBits) {
-        const double coefficient = kTernaryCentroid / sqrt((double)kGroup);
-        v = (t == 1) ? coefficient : (t == 3) ? -coefficient : 0.0;
-      } else if (t < (1 << bits)) {
-        v = (double)m.cb.v[(bits == 2 ? 0 : bits == 3 ? 4 : 12) + t];
-      }
-      (k == 0 ? lut1 : lut2)[t] = v;
-    }
+  // rmsUnit(x) over the 2048 lane values (runtime.ts:385)
+#pragma unroll
+  for (int k = 0; k < kLanes; k++) {
+    const double xv = (double)S.xl[c + k * kDim];
+    S.sq[c + k * kDim] = xv * xv;
+  }
+  if (tid >= 32 && tid < 80) {
+    const int t = tid - 32, which = t >> 4, lev = t & 15;
+    const int bits = which == 0 ? m.phi_pre.bits : which == 1 ? m.phi_post.bits : m.phi_res.bits;
+    S.lut[which][lev] = lut_level(m.cb.v, bits, lev);
   }
   __syncthreads();
-  for (int i = tid; i < kLaneWidth; i += kThreads) S.work[i] = f32((double)S.xl[i] * S.red[2]);
+  if (tid == 0) S.red[2] = inverse_rms_of(S.sq, kLaneWidth);
   __syncthreads();
-  fwht_smem(S.work, kGroup, kLaneWidth / kGroup);
-  for (int i = tid; i < kLaneWidth; i += kThreads) S.xd[i] = (double)f32((double)S.work[i] * inv_root_128);
+  // prepareCqActivation of the phi input: FWHT of each 128-group, * 1/sqrt(128)
+#pragma unroll
+  for (int k = 0; k < kLanes; k++) {
+    float nl = f32((double)S.xl[c + k * kDim] * S.red[2]);
+    nl = fwht_reg(nl, S.fw, kGroup, kThreads);
+    S.xd[c + k * kDim] = (double)f32((double)nl * inv_root_128);
+  }
   __syncthreads();
 
   // phi matvecs (matvecBatch, runtime.ts:386-402): rows 4l..4l+3 of phi_pre / phi_post and
   // 16l..16l+15 of phi_res; 24 rows x 16 groups, one (row, group) per thread.
-  const int phi_groups = kLaneWidth / kGroup;
-  if (tid < 24 * phi_groups) {
-    const int rr = tid / phi_groups, g = tid - rr * phi_groups;
+  // Thread t takes row t % 24 and group t / 24, so a warp reads the binary64 inputs of at most
+  // two groups (broadcasts) instead of sixteen (a 16-way bank conflict at the 1 KB group stride).
+  constexpr int kPhiGroups = kLaneWidth / kGroup;
+  if (tid < 24 * kPhiGroups) {
+    const int rr = tid % 24, g = tid / 24;
     const CqMat& M = rr < 4 ? m.phi_pre : rr < 8 ? m.phi_post : m.phi_res;
     const int64_t row = rr < 4 ? (int64_t)l * 4 + rr : rr < 8 ? (int64_t)l * 4 + rr - 4 : (int64_t)l * 16 + rr - 8;
-    const double* lut = S.lut[rr < 4 ? 0 : rr < 8 ? 1 : 2];
-    S.dots[tid] = group_dot_exact(M.packed + row * M.row_bytes, M.bits, g, lut, S.xd + g * kGroup);
+    const int gbytes = M.bits == 4 ? 64 : M.bits == 3 ? 48 : 32;
+    S.dots[rr * kPhiGroups + g] = group_dot_exact(M.packed + row * M.row_bytes + g * gbytes, M.bits,
+                                                  S.lut[rr < 4 ? 0 : rr < 8 ? 1 : 2], S.xd + g * kGroup);
   }
   __syncthreads();
   if (tid < 24) {
     const int rr = tid;
     const CqMat& M = rr < 4 ? m.phi_pre : rr < 8 ? m.phi_post : m.phi_res;
     const int64_t row = rr < 4 ? (int64_t)l * 4 + rr : rr < 8 ? (int64_t)l * 4 + rr - 4 : (int64_t)l * 16 + rr - 8;
+    double nrm[kPhiGroups];
+#pragma unroll
+    for (int g = 0; g < kPhiGroups; g++) nrm[g] = norm16(M.norms, row * kPhiGroups + g);
     double total = 0.0;
-    for (int g = 0; g < phi_groups; g++)
-      total = total + norm16(M.norms, row * phi_groups + g) * S.dots[rr * phi_groups + g];
+#pragma unroll
+    for (int g = 0; g < kPhiGroups; g++) total = total + nrm[g] * S.dots[rr * kPhiGroups + g];
     S.phi[rr] = f32(total);
   }
   __syncthreads();
@@ -410,46 +444,57 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
 #pragma unroll
   for (int lane = 0; lane < kLanes; lane++) sum = fma((double)S.hpre[lane], (double)S.xl[lane * kDim + c], sum);
   const float upd = f32(sum);
-  S.a[c] = upd;
   float blk = upd;
   int site = -1;
   for (int k = 0; k < m.n_sites; k++)
     if (m.sites[k] == l) site = k;
   if (site >= 0) {
-    // engram injection (runtime.ts:423-438)
+    // engram injection (runtime.ts:423-438): rmsUnit of both vectors, then their dot product
     const float key = st.engram_kv[(((int64_t)b * m.n_sites + site) * 2) * kDim + c];
-    S.bvec[c] = key;
+    S.sq[c] = (double)upd * (double)upd;
+    S.sq2[c] = (double)key * (double)key;
     __syncthreads();
-    if (tid == 0) S.red[0] = inverse_rms(S.a, kDim);
-    if (tid == 32) S.red[1] = inverse_rms(S.bvec, kDim);
+    if (tid == 0) S.red[0] = inverse_rms_of(S.sq, kDim);
+    if (tid == 32) S.red[1] = inverse_rms_of(S.sq2, kDim);
     __syncthreads();
-    S.c[c] = f32((double)upd * S.red[0]);
-    S.d[c] = f32((double)key * S.red[1]);
+    const float ni = f32((double)upd * S.red[0]);
+    const float nk = f32((double)key * S.red[1]);
+    S.sq[c] = (double)ni * (double)nk;
     __syncthreads();
-    if (tid == 0) {
-      double dot = 0.0;
-      for (int i = 0; i < kDim; i++) dot = fma((double)S.c[i], (double)S.d[i], dot);
-      S.red[3] = sigmoid_d(dot / sqrt((double)kDim));
-    }
+    if (tid == 0) S.red[3] = sigmoid_d(sum_seq(S.sq, kDim) / sqrt((double)kDim));
     __syncthreads();
     const float value = st.engram_val[((int64_t)b * m.n_sites + site) * kDim + c];
     blk = f32((double)upd + S.red[3] * (double)value);
-    __syncthreads();
   }
-  S.bvec[c] = blk;
   st.update[(int64_t)b * kDim + c] = upd;
   st.block[(int64_t)b * kDim + c] = blk;
+  S.sq[c] = (double)blk * (double)blk;
   __syncthreads();
-  if (tid == 0) S.red[0] = inverse_rms(S.bvec, kDim);
-  if (tid >= 32 && tid < 64) sinkhorn4(S.sk, S.routing, tid - 32);  // warp 1, beside thread 0
+  if (tid == 0) S.red[0] = inverse_rms_of(S.sq, kDim);
   __syncthreads();
   // rmsNorm(blockInput, normInput) then prepareCqActivation for Q/K/V/gate (runtime.ts:441, 465)
-  S.c[c] = f32((1.0 + (double)m.norm_input[(int64_t)l * kDim + c]) * (double)blk * S.red[0]);
-  __syncthreads();
-  fwht_smem(S.c, kGroup, kDim / kGroup);
-  st.prep_a[(int64_t)b * kDim + c] = f32((double)S.c[c] * inv_root_128);
+  float a = f32((1.0 + (double)m.norm_input[(int64_t)l * kDim + c]) * (double)blk * S.red[0]);
+  a = fwht_reg(a, S.fw, kGroup, kThreads);
+  st.prep_a[(int64_t)b * kDim + c] = f32((double)a * inv_root_128);
+  // h_post and the routing logits; k_route turns the logits into the Sinkhorn routing matrix
+  // while the attention half of the layer runs.
   if (tid < 4) st.route[(int64_t)b * 20 + tid] = S.hpost[tid];
-  else if (tid < 20) st.route[(int64_t)b * 20 + tid] = S.routing[tid - 4];
+  else if (tid < 20) st.route[(int64_t)b * 20 + tid] = (float)S.sk[tid - 4];
+}
+
+// Sinkhorn routing of one item (runtime.ts:523-529): one warp per item, in place on route[4..19].
+__global__ void __launch_bounds__(32) k_route(const StepView st) {
+  __shared__ double v[16];
+  __shared__ float out[16];
+  const int b = blockIdx.x;
+  if (b >= *st.n_items) return;
+  const int lane = threadIdx.x;
+  float* r = st.route + (int64_t)b * 20 + 4;
+  if (lane < 16) v[lane] = (double)r[lane];
+  __syncwarp();
+  sinkhorn4(v, out, lane);
+  __syncwarp();
+  if (lane < 16) r[lane] = out[lane];
 }
 
 // ------------------------------------------------------------------ k_attention
@@ -466,26 +511,32 @@ struct CacheRef {
 };
 
 // Attention of query heads 2h, 2h+1 over one KV head (the #attention loops of runtime.ts:732-784
-// for one kvHead).  q: smem binary32 [2][64]; e: smem binary64 [2][count]; slot_of(t) maps the
-// t-th visible position to its cache row.  Leaves the gated outputs in out[2][64] (smem).
+// for one kvHead).  q: smem binary32 [2][64]; e: smem binary64 [2][count]; tile: smem staging
+// area (kAttnTile value rows + scales + weights); slot_of(t) maps the t-th visible position to its
+// cache row.  Leaves the gated outputs in out[2][64] (smem).
+constexpr int kAttnTile = 256;
+constexpr size_t kAttnTileBytes = kAttnTile * (kHeadDim + 2 * 8);  // codes, 2 x weight*scale
+
 template <class SlotOf>
 __device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const float* q, double* e,
-                            const float* gate, float* out, double* red) {
+                            unsigned char* tile, const float* gate, float* out, double* red) {
   const int tid = threadIdx.x;
   // scores[t] = f32((sum_i q_i * code_i * keyScale) / 8)  (runtime.ts:736-757)
   for (int t = tid; t < count; t += kAttnThreads) {
     const int sl = slot_of(t);
     const double ks = (double)C.ks[sl];
     const uint4* kr = reinterpret_cast<const uint4*>(C.kc + (int64_t)sl * kHeadDim);
+    uint4 u[4];
+#pragma unroll
+    for (int w4 = 0; w4 < 4; w4++) u[w4] = __ldg(kr + w4);
     double d0 = 0.0, d1 = 0.0;
 #pragma unroll
     for (int w4 = 0; w4 < 4; w4++) {
-      const uint4 u = __ldg(kr + w4);
-      const uint32_t words[4] = {u.x, u.y, u.z, u.w};
+      const uint32_t words[4] = {u[w4].x, u[w4].y, u[w4].z, u[w4].w};
 #pragma unroll
       for (int k = 0; k < 16; k++) {
         const int i = w4 * 16 + k;
-        const double code = (double)(int8_t)((words[k >> 2] >> ((k & 3) * 8)) & 0xff);
+        const double code = int_to_double_exact((int)(int8_t)((words[k >> 2] >> ((k & 3) * 8)) & 0xff));
         d0 = d0 + ((double)q[i] * code) * ks;
         d1 = d1 + ((double)q[kHeadDim + i] * code) * ks;
       }
@@ -508,27 +559,46 @@ __device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const 
     for (int t = lane64; t < count; t += 64) e[hh * count + t] = exp(e[hh * count + t] - mx);
     __syncthreads();
     if (lane64 == 0) {
+      const double* eh = e + hh * count;
       double total = 0.0;
-      for (int t = 0; t < count; t++) total = total + e[hh * count + t];
+#pragma unroll 8
+      for (int t = 0; t < count; t++) total = total + eh[t];
       red[4 + hh] = total > 0.0 ? 1.0 / total : 0.0;
     }
     __syncthreads();
   }
   // output[i] += weight * code * valueScale, sequentially in t with binary32 storage (760-782).
-  {
-    const int hh = tid >> 6, i = tid & 63;
-    const double inverse = red[4 + hh];
-    const double* eh = e + hh * count;
-    float o = 0.0f;
-    for (int t = 0; t < count; t++) {
-      const int sl = slot_of(t);
-      const double w = (double)f32((double)f32(eh[t]) * inverse);
-      const double code = (double)C.vc[(int64_t)sl * kHeadDim + i];
-      o = f32((double)o + w * code * (double)C.vs[sl]);
+  // Value rows, scales and weights are staged tile by tile in shared memory so the sequential
+  // chain reads only shared memory.
+  // weight * code * valueScale == code * (weight * valueScale): weight (binary32) * valueScale
+  // (binary32) is exact in binary64, and weight * code is exact too, so both orders are one
+  // rounding of the same real product.
+  int8_t* vt = reinterpret_cast<int8_t*>(tile);                                   // [tile][64]
+  double* wvt = reinterpret_cast<double*>(tile + kAttnTile * kHeadDim);           // [2][tile]
+  const int hh = tid >> 6, i = tid & 63;
+  float o = 0.0f;
+  for (int t0 = 0; t0 < count; t0 += kAttnTile) {
+    const int n = min(kAttnTile, count - t0);
+    for (int k = tid; k < n * 4; k += kAttnThreads) {
+      const int t = k >> 2, part = k & 3;
+      const int sl = slot_of(t0 + t);
+      reinterpret_cast<uint4*>(vt + t * kHeadDim)[part] =
+          __ldg(reinterpret_cast<const uint4*>(C.vc + (int64_t)sl * kHeadDim) + part);
     }
-    // attentionOutput * sigmoid(gate) (runtime.ts:503-504)
-    out[hh * kHeadDim + i] = gate ? f32((double)o * sigmoid_d((double)gate[hh * kHeadDim + i])) : o;
+    for (int k = tid; k < 2 * n; k += kAttnThreads) {
+      const int h2 = k / n, t = k - h2 * n;
+      const double w = (double)f32((double)f32(e[h2 * count + t0 + t]) * red[4 + h2]);
+      wvt[h2 * kAttnTile + t] = w * (double)C.vs[slot_of(t0 + t)];
+    }
+    __syncthreads();
+    const double* wv = wvt + hh * kAttnTile;
+#pragma unroll 8
+    for (int t = 0; t < n; t++)
+      o = f32((double)o + int_to_double_exact(vt[t * kHeadDim + i]) * wv[t]);
+    __syncthreads();
   }
+  // attentionOutput * sigmoid(gate) (runtime.ts:503-504)
+  out[hh * kHeadDim + i] = gate ? f32((double)o * sigmoid_d((double)gate[hh * kHeadDim + i])) : o;
   __syncthreads();
 }
 
@@ -616,9 +686,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
   const int count = prefix + (p - recent_low + 1);
   CacheRef C{sv.kcodes + head_base * kHeadDim, sv.vcodes + head_base * kHeadDim, sv.kscale + head_base,
              sv.vscale + head_base};
-  double* e = reinterpret_cast<double*>(smem_raw);
+  unsigned char* tile = smem_raw;
+  double* e = reinterpret_cast<double*>(smem_raw + kAttnTileBytes);
   auto slot_of = [&](int t) { return kv_slot(t < prefix ? t : recent_low + (t - prefix)); };
-  attend_pair(C, count, slot_of, qv, e, gt, outv, red);
+  attend_pair(C, count, slot_of, qv, e, tile, gt, outv, red);
   // prepareCqActivation of the output projection: heads 2h, 2h+1 are exactly input group h.
   fwht_smem(outv, kGroup, 1);
   st.prep_o[(int64_t)b * kDim + h * kGroup + tid] = f32((double)outv[tid] * (1.0 / sqrt((double)kGroup)));
@@ -641,9 +712,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention_dev(const float* __r
   const int count = min(max(counts[b], 0), capacity);
   const int64_t head_base = ((int64_t)b * kKvHeads + h) * capacity;
   CacheRef C{kc + head_base * kHeadDim, vc + head_base * kHeadDim, ks + head_base, vs + head_base};
-  double* e = reinterpret_cast<double*>(smem_raw);
+  unsigned char* tile = smem_raw;
+  double* e = reinterpret_cast<double*>(smem_raw + kAttnTileBytes);
   auto slot_of = [](int t) { return t; };
-  attend_pair(C, count, slot_of, qv, e, nullptr, outv, red);
+  attend_pair(C, count, slot_of, qv, e, tile, nullptr, outv, red);
   out[(int64_t)b * kHeads * kHeadDim + 2 * h * kHeadDim + tid] = outv[tid];
 }
 
@@ -740,6 +812,7 @@ __global__ void __launch_bounds__(kFinishThreads) k_finish(const ModelView m, co
     if (has_sched) {
       atomicAdd(reinterpret_cast<unsigned long long*>(q.processed), 1ull);
       if (selecting) {
+        atomicAdd(reinterpret_cast<unsigned long long*>(q.generated), 1ull);
         const int done = seq->gen_done + 1;
         seq->gen_done = done;
         if (done >= seq->gen_target) {
@@ -844,7 +917,9 @@ cudaError_t launch_layer(const ModelView& m, const SlotView& sv, const StepView&
   return cudaGetLastError();
 }
 
-size_t attention_smem_bytes(int32_t capacity, bool) { return sizeof(double) * 2 * (size_t)capacity; }
+size_t attention_smem_bytes(int32_t capacity, bool) {
+  return kAttnTileBytes + sizeof(double) * 2 * (size_t)capacity;
+}
 
 cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
                              int n_host, cudaStream_t s) {
@@ -862,6 +937,12 @@ cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* 
   cudaError_t e = cudaFuncSetAttribute(k_attention_dev, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   k_attention_dev<<<dim3(batch, kKvHeads), kAttnThreads, smem, s>>>(q, kc, ks, vc, vs, counts, capacity, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route(const StepView& st, int n_host, cudaStream_t s) {
+  if (n_host <= 0) return cudaSuccess;
+  k_route<<<n_host, 32, 0, s>>>(st);
   return cudaGetLastError();
 }
 

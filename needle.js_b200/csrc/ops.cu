@@ -87,7 +87,7 @@ extern "C" int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float*
   j.y = y;
   j.y_stride = m->rows;
   J.count = 1;
-  J.total_tiles = (m->rows + 31) / 32;
+  J.total_tiles = (m->rows + kGemvTileRows - 1) / kGemvTileRows;
   e = launch_cq_gemv(J, cb, batch, nullptr, s);
   if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
   return NEEDLE_OK;

@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -1502,7 +1503,7 @@ int ref_generate_greedy(const ref_model* m, const int32_t* prompt, int32_t n_pro
 
 int ref_decode_many(const ref_model* m, int32_t n_seqs, const int32_t* prompt_offsets,
                     const int32_t* prompt_ids, const int32_t* gen_steps, int32_t n_threads,
-                    int32_t* out_last_ids, int64_t* tokens_processed) {
+                    int32_t* out_last_ids, int64_t* tokens_processed, double* out_seconds) {
   return guard([&] {
     invariant(n_threads > 0, INVALID_CACT, "n_threads must be positive");
     std::atomic<int32_t> next{0};
@@ -1520,6 +1521,7 @@ int ref_decode_many(const ref_model* m, int32_t n_seqs, const int32_t* prompt_of
           const int32_t s = next.fetch_add(1);
           if (s >= n_seqs) break;
           const int32_t p0 = prompt_offsets[s], n = prompt_offsets[s + 1] - p0, steps = gen_steps[s];
+          const auto t0 = std::chrono::steady_clock::now();
           rt.reset(int64_t(n) + steps, 0);
           int64_t local = 0;
           for (int32_t i = 0; i < n; i++, local++) rt.step(prompt_ids[p0 + i], i == n - 1, &logits);
@@ -1532,6 +1534,8 @@ int ref_decode_many(const ref_model* m, int32_t n_seqs, const int32_t* prompt_of
             }
           }
           if (out_last_ids) out_last_ids[s] = token;
+          if (out_seconds)
+            out_seconds[s] = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
           processed += local;
         }
       } catch (const RefError& e) {
@@ -1545,6 +1549,126 @@ int ref_decode_many(const ref_model* m, int32_t n_seqs, const int32_t* prompt_of
     *tokens_processed = processed.load();
   });
 }
+
+}  // extern "C"
+
+struct ref_sched {
+  const ref_model* M;
+  std::vector<int32_t> offsets, ids, gen;
+  int32_t n_seqs = 0, next = 0, finished = 0, n_threads = 1;
+  int64_t processed = 0, generated = 0;
+  std::vector<int32_t> last;
+  struct Slot {
+    std::unique_ptr<ref_runtime> rt;
+    bool busy = false;
+    int32_t seq = -1, pos = 0, len = 0, target = 0, done = 0, pending = 0;
+    std::vector<float> logits;
+  };
+  std::vector<Slot> slots;
+
+  void admit() {
+    for (auto& sl : slots) {
+      if (sl.busy || next >= n_seqs) continue;
+      const int32_t id = next++;
+      sl.seq = id;
+      sl.len = offsets[id + 1] - offsets[id];
+      sl.target = gen[id];
+      sl.pos = 0;
+      sl.done = 0;
+      sl.busy = true;
+      sl.rt->reset(int64_t(sl.len) + sl.target, 0);
+    }
+  }
+  // One token for one busy slot (the device scheduler's item for that slot).
+  void run(Slot& sl) {
+    const bool select = sl.pos >= sl.len - 1;
+    const int32_t token = sl.pos < sl.len ? ids[offsets[sl.seq] + sl.pos] : sl.pending;
+    sl.rt->step(token, select, &sl.logits);
+    sl.pos++;
+    if (select) sl.pending = argmaxF(sl.logits.data(), int64_t(sl.logits.size()));
+  }
+};
+
+extern "C" {
+
+int ref_sched_new(const ref_model* m, int32_t n_slots, const int32_t* prompt_offsets, const int32_t* prompt_ids,
+                  const int32_t* gen_steps, int32_t n_seqs, int32_t n_threads, ref_sched** out) {
+  return guard([&] {
+    invariant(n_slots > 0 && n_threads > 0 && n_seqs >= 0, INVALID_CACT, "bad scheduler arguments");
+    auto s = std::make_unique<ref_sched>();
+    s->M = m;
+    s->offsets.assign(prompt_offsets, prompt_offsets + n_seqs + 1);
+    s->ids.assign(prompt_ids, prompt_ids + (n_seqs ? prompt_offsets[n_seqs] : 0));
+    s->gen.assign(gen_steps, gen_steps + n_seqs);
+    s->n_seqs = n_seqs;
+    s->n_threads = n_threads;
+    s->last.assign(std::max(n_seqs, 1), -1);
+    s->slots.resize(n_slots);
+    for (auto& sl : s->slots) {
+      sl.rt = std::make_unique<ref_runtime>();
+      sl.rt->M = m;
+      sl.rt->kvMode = 0;
+      sl.rt->collectConfidence = false;
+    }
+    s->admit();
+    *out = s.release();
+  });
+}
+
+int ref_sched_step(ref_sched* s, int32_t steps) {
+  return guard([&] {
+    for (int32_t k = 0; k < steps; k++) {
+      std::vector<ref_sched::Slot*> busy;
+      for (auto& sl : s->slots)
+        if (sl.busy) busy.push_back(&sl);
+      if (busy.empty()) break;
+      std::vector<std::string> errors(s->n_threads);
+      std::atomic<size_t> cursor{0};
+      auto worker = [&](int tid) {
+        try {
+          for (;;) {
+            const size_t i = cursor.fetch_add(1);
+            if (i >= busy.size()) break;
+            s->run(*busy[i]);
+          }
+        } catch (const RefError& e) {
+          errors[tid] = e.msg;
+        }
+      };
+      std::vector<std::thread> pool;
+      const int nt = std::min<int>(s->n_threads, int(busy.size()));
+      for (int t = 1; t < nt; t++) pool.emplace_back(worker, t);
+      worker(0);
+      for (auto& th : pool) th.join();
+      for (auto& e : errors) invariant(e.empty(), BACKEND_UNAVAILABLE, e);
+      for (auto* sl : busy) {
+        s->processed++;
+        if (sl->pos - 1 >= sl->len - 1) {
+          s->generated++;
+          sl->done++;
+          if (sl->done >= sl->target) {
+            s->last[sl->seq] = sl->pending;
+            s->finished++;
+            sl->busy = false;
+          }
+        }
+      }
+      s->admit();
+    }
+  });
+}
+
+int ref_sched_status(const ref_sched* s, int64_t* tokens_processed, int64_t* tokens_generated, int32_t* seqs_finished,
+                     int32_t* last_ids) {
+  return guard([&] {
+    if (tokens_processed) *tokens_processed = s->processed;
+    if (tokens_generated) *tokens_generated = s->generated;
+    if (seqs_finished) *seqs_finished = s->finished;
+    if (last_ids) std::copy(s->last.begin(), s->last.begin() + s->n_seqs, last_ids);
+  });
+}
+
+void ref_sched_free(ref_sched* s) { delete s; }
 
 int ref_attention_int8(int32_t heads, int32_t kv_heads, int32_t head_dim, int32_t count,
                        const float* q, const int8_t* key_codes, const float* key_scales,

@@ -102,10 +102,25 @@ int ref_generate_greedy(const ref_model* m, const int32_t* prompt, int32_t n_pro
 
 /* Ragged CPU decode baseline: independent sequences spread over n_threads host threads; each
  * sequence runs prompt + greedy steps exactly as ref_generate_greedy.  Returns the number of
- * step() calls made (tokens processed) through *tokens_processed. */
+ * step() calls made (tokens processed) through *tokens_processed and, when out_seconds is not
+ * NULL, each sequence's own compute time on its thread. */
 int ref_decode_many(const ref_model* m, int32_t n_seqs, const int32_t* prompt_offsets,
                     const int32_t* prompt_ids, const int32_t* gen_steps, int32_t n_threads,
-                    int32_t* out_last_ids, int64_t* tokens_processed);
+                    int32_t* out_last_ids, int64_t* tokens_processed, double* out_seconds);
+
+/* Continuous batching on the host, the CPU counterpart of needle_cuda_sched_*: n_slots slots
+ * admit queued sequences (prompt ids concatenated, prompt_offsets has n_seqs + 1 entries;
+ * gen_steps greedy tokens each) in queue order into the lowest idle slot; every ref_sched_step
+ * runs one step for every busy slot -- its next prompt token or its last greedy token -- spread
+ * over n_threads host threads.  A sequence retires after selecting its last token. */
+typedef struct ref_sched ref_sched;
+int ref_sched_new(const ref_model* m, int32_t n_slots, const int32_t* prompt_offsets,
+                  const int32_t* prompt_ids, const int32_t* gen_steps, int32_t n_seqs,
+                  int32_t n_threads, ref_sched** out);
+int ref_sched_step(ref_sched* s, int32_t steps);
+int ref_sched_status(const ref_sched* s, int64_t* tokens_processed, int64_t* tokens_generated,
+                     int32_t* seqs_finished, int32_t* last_ids);
+void ref_sched_free(ref_sched* s);
 
 /* Decode attention over an int8 cache with kvWindow = 0 semantics (runtime.ts:719-786):
  * visible positions 0..count-1.  q: heads*hd; caches [kv_heads][count][hd]; scales

@@ -54,6 +54,7 @@ def lib():
         L.ref_runtime_kv_allocation.argtypes = [C.c_void_p]
         L.ref_model_close.argtypes = [C.c_void_p]
         L.ref_runtime_free.argtypes = [C.c_void_p]
+        L.ref_sched_free.argtypes = [C.c_void_p]
         _lib = L
     return _lib
 
@@ -183,15 +184,18 @@ class Model:
                                          C.c_int32(sink), _p(ids), _p(lp), _p(logits)))
         return ids, lp, logits
 
-    def decode_many(self, prompts, gen_steps, n_threads):
+    def decode_many(self, prompts, gen_steps, n_threads, seconds=False):
         offsets = np.zeros(len(prompts) + 1, dtype=np.int32)
         offsets[1:] = np.cumsum([len(p) for p in prompts])
         flat = np.ascontiguousarray(np.concatenate(prompts), dtype=np.int32)
         steps = np.ascontiguousarray(gen_steps, dtype=np.int32)
         last = np.zeros(len(prompts), dtype=np.int32)
+        secs = np.zeros(len(prompts), dtype=np.float64)
         processed = C.c_int64()
         _check(lib().ref_decode_many(self.h, C.c_int32(len(prompts)), _p(offsets), _p(flat), _p(steps),
-                                     C.c_int32(n_threads), _p(last), C.byref(processed)))
+                                     C.c_int32(n_threads), _p(last), C.byref(processed), _p(secs)))
+        if seconds:
+            return last, processed.value, secs
         return last, processed.value
 
 
@@ -276,3 +280,35 @@ def quantize_kv_head(x):
     s = C.c_float()
     _check(lib().ref_quantize_kv_head(_p(x), C.c_int32(x.size), _p(codes), C.byref(s)))
     return codes, s.value
+
+
+class Sched:
+    """Host continuous batching (ref_sched_*): the CPU counterpart of the device scheduler."""
+
+    def __init__(self, model: Model, n_slots, prompts, gen_steps, n_threads):
+        self.model = model
+        offsets = np.zeros(len(prompts) + 1, dtype=np.int32)
+        offsets[1:] = np.cumsum([len(p) for p in prompts])
+        flat = np.ascontiguousarray(np.concatenate(prompts) if len(prompts) else np.zeros(0), dtype=np.int32)
+        steps = np.ascontiguousarray(gen_steps, dtype=np.int32)
+        self.n_seqs = len(prompts)
+        h = C.c_void_p()
+        _check(lib().ref_sched_new(model.h, C.c_int32(n_slots), _p(offsets), _p(flat), _p(steps),
+                                   C.c_int32(len(prompts)), C.c_int32(n_threads), C.byref(h)))
+        self.h = h
+
+    def step(self, steps=1):
+        _check(lib().ref_sched_step(self.h, C.c_int32(steps)))
+
+    def status(self):
+        p, g, f = C.c_int64(), C.c_int64(), C.c_int32()
+        last = np.zeros(max(self.n_seqs, 1), dtype=np.int32)
+        _check(lib().ref_sched_status(self.h, C.byref(p), C.byref(g), C.byref(f), _p(last)))
+        return p.value, g.value, f.value, last[:self.n_seqs]
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().ref_sched_free(self.h)
+            self.h = None
+
+    __del__ = close

@@ -270,12 +270,13 @@ def test_device_scheduler_matches_oracle(engine, oracle, ref_model):
     total = int(sum(len(p) + g - 1 for p, g in zip(prompts, gens)))
     for _ in range(200):
         engine.sched_step(1)
-        tokens, finished, last = engine.sched_status()
+        tokens, generated, finished, last = engine.sched_status()
         if finished == len(prompts):
             break
     assert finished == len(prompts)
     np.testing.assert_array_equal(last, want)
     assert tokens == total == processed_ref
+    assert generated == int(gens.sum())
 
 
 def test_errors_follow_needle_error_codes(engine, ref_model):
