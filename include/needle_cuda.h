@@ -170,6 +170,24 @@ typedef struct needle_cq_matrix {
 int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float* codebook, const float* x,
                               int32_t batch, float* y, void* stream);
 
+/* Capacity, in floats, of the fixed scratch array used by needle_cuda_cq_matvec_dev_noalloc:
+ * batch * input_padded must not exceed it (4 MiB of device memory per GPU). */
+#define NEEDLE_NOALLOC_MAX_FLOATS (1 << 20)
+
+/* Same result as needle_cuda_cq_matvec_dev, but the call allocates no device memory.
+ * No counterpart in the reference: it exists for callers that cannot call cudaMalloc -- a host
+ * that hands all device memory to its own pool at start-up, or a latency-critical serving loop
+ * that must not take cudaMalloc's implicit device-wide synchronisation.  The rotated activations
+ * go to a statically sized array inside the library (NEEDLE_NOALLOC_MAX_FLOATS floats, reserved
+ * on every GPU that loads the library until the process exits); larger batch * input_padded is
+ * rejected with BACKEND_UNAVAILABLE.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream capture.  All calls
+ * share the one array and each call overwrites every element it reads, so no clearing is needed;
+ * calls whose executions overlap on the GPU (different streams, or host threads) race on it and
+ * must be serialised by the caller. */
+int needle_cuda_cq_matvec_dev_noalloc(const needle_cq_matrix* m, const float* codebook,
+                                      const float* x, int32_t batch, float* y, void* stream);
+
 /* Decode attention over an int8 cache with kvWindow = 0 semantics (runtime.ts:719-786) for a
  * ragged batch, on device buffers:
  *   q        [batch][heads * head_dim] floats

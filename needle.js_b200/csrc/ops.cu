@@ -93,6 +93,83 @@ extern "C" int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float*
   return NEEDLE_OK;
 }
 
+// ---- no-allocation variant of needle_cuda_cq_matvec_dev
+//
+// For callers that cannot call cudaMalloc (all device memory handed to their own pool, or a
+// serving loop that may not pay cudaMalloc's device-wide synchronisation): the rotated
+// activations live in this fixed array instead of a growable buffer.  Host code cannot use the
+// array's name as a device address, so the address is looked up once per device with
+// cudaGetSymbolAddress while that device is current.
+static __device__ __align__(256) float g_noalloc_prepared[NEEDLE_NOALLOC_MAX_FLOATS];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+cudaError_t noalloc_scratch(int device, float** out) {
+  if (device < 0 || device >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_prepared);
+    if (e != cudaSuccess) return e;
+    g_noalloc_addr[device] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_addr[device];
+  return cudaSuccess;
+}
+}  // namespace
+
+extern "C" int needle_cuda_cq_matvec_dev_noalloc(const needle_cq_matrix* m, const float* codebook, const float* x,
+                                                 int32_t batch, float* y, void* stream) {
+  if (!m || !codebook || (batch > 0 && (!x || !y)))
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+  if (m->group_size != kGroup) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "CQ group size 128 only");
+  if (!(m->bits == 2 || m->bits == 3 || m->bits == 4 || m->bits == 5))
+    return op_fail(NEEDLE_UNSUPPORTED_CACT, "unsupported CQ record width");
+  if (m->rows < 0 || m->input_size <= 0 || batch < 0) return op_fail(NEEDLE_INVALID_CACT, "bad matrix shape");
+  if ((reinterpret_cast<uintptr_t>(m->packed) & 15) != 0)
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "packed rows must be 16-byte aligned");
+  const int64_t in_pad = (int64_t(m->input_size) + kGroup - 1) / kGroup * kGroup;
+  if (int64_t(batch) * in_pad > NEEDLE_NOALLOC_MAX_FLOATS)
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE,
+                   "batch * padded input (" + std::to_string(int64_t(batch) * in_pad) +
+                       " floats) exceeds the no-allocation scratch of " + std::to_string(NEEDLE_NOALLOC_MAX_FLOATS) +
+                       " floats");
+  if (batch == 0 || m->rows == 0) return NEEDLE_OK;
+  const int pb = m->bits == 5 ? 2 : m->bits;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Codebook cb{};
+  for (int i = 0; i < 28; i++) cb.v[i] = codebook[i];
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  float* xp = nullptr;
+  if (e == cudaSuccess) e = noalloc_scratch(device, &xp);
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  e = launch_cq_prepare(x, m->input_size, m->input_size, int32_t(in_pad), xp, int32_t(in_pad), batch, nullptr, s);
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  CqJobs J{};
+  CqJob& j = J.job[0];
+  j.packed = m->packed;
+  j.norms = m->norms;
+  j.row_start = 0;
+  j.rows = m->rows;
+  j.in_pad = int32_t(in_pad);
+  j.bits = m->bits;
+  j.row_bytes = int32_t(in_pad * pb / 8);
+  j.tile_begin = 0;
+  j.x = xp;
+  j.x_stride = int32_t(in_pad);
+  j.y = y;
+  j.y_stride = m->rows;
+  J.count = 1;
+  J.total_tiles = (m->rows + kGemvTileRows - 1) / kGemvTileRows;
+  e = launch_cq_gemv(J, cb, batch, nullptr, s);
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  return NEEDLE_OK;
+}
+
 extern "C" int needle_cuda_attention_dev(const float* q, const int8_t* key_codes, const float* key_scales,
                                          const int8_t* value_codes, const float* value_scales, const int32_t* counts,
                                          int32_t batch, int32_t capacity, float* out, void* stream) {

@@ -18,6 +18,7 @@ CODES = ["INVALID_CACT", "UNSUPPORTED_CACT", "WEIGHTS_NOT_FOUND", "WEIGHTS_INTEG
          "WEBGPU_UNAVAILABLE", "BACKEND_UNAVAILABLE", "CONTEXT_OVERFLOW", "INVALID_TOOL_SCHEMA",
          "GRAMMAR_DEAD_END", "GENERATION_ABORTED"]
 TOKEN_PENDING = -1
+NOALLOC_MAX_FLOATS = 1 << 20  # NEEDLE_NOALLOC_MAX_FLOATS
 
 
 class NeedleError(RuntimeError):
@@ -78,6 +79,8 @@ EXPORTS = {
     "needle_cuda_row": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
     "needle_cuda_cq_matvec_dev": (C.c_int, [C.POINTER(CqMatrixDesc), C.c_void_p, C.c_void_p,
                                             C.c_int32, C.c_void_p, C.c_void_p]),
+    "needle_cuda_cq_matvec_dev_noalloc": (C.c_int, [C.POINTER(CqMatrixDesc), C.c_void_p, C.c_void_p,
+                                                    C.c_int32, C.c_void_p, C.c_void_p]),
     "needle_cuda_attention_dev": (C.c_int, [C.c_void_p] * 6 + [C.c_int32, C.c_int32, C.c_void_p,
                                                                 C.c_void_p]),
     "needle_cuda_stream": (C.c_void_p, [C.c_void_p]),
