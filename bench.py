@@ -168,8 +168,141 @@ def roofline_for(prof, n_items, peaks):
             "launch_ms": round(per_launch_ms, 5), "algorithmic_bytes_per_launch": int(bytes_)}
 
 
+QMATVEC_SHAPES = [  # (name, rows, inputs, record bits) -- every Needle 2 projection + the stress shape
+    ("query/gate 512x512 CQ2", 512, 512, 2), ("key/value 256x512 CQ2", 256, 512, 2),
+    ("output 512x512 CQ3", 512, 512, 3), ("phi_pre/post layer slice 4x2048 CQ4", 4, 2048, 4),
+    ("phi_res layer slice 16x2048 CQ4", 16, 2048, 4), ("phi_pre/post 108x2048 CQ4", 108, 2048, 4),
+    ("phi_res 432x2048 CQ4", 432, 2048, 4), ("engram key/value 512x512 ternary", 512, 512, 5),
+    ("vocabulary 8192x512 CQ4", 8192, 512, 4), ("stress 8192x8192 CQ4", 8192, 8192, 4)]
+ROTATE_BYTES = 256 << 20  # rotated operand sets exceed the 126 MB L2 twice over
+
+
+def _peak(peaks):
+    p = peaks.get("hbm_gbs") if peaks else None
+    return (p, "measured") if p else (6650.0, "fallback")
+
+
+def _time_calls(torch, stream, fn, n_sets, warmup, iters):
+    for i in range(warmup):
+        fn(i % n_sets)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(iters):
+        fn(i % n_sets)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def bench_qmatvec(args, peaks):
+    """isolated quantised matvec, every projection shape + 8192x8192, batch
+    1/8/32/128; indices uniform, fp16 norms |N(0,1)|*0.01, activations N(0,1) (seed 2)."""
+    import ctypes as C
+    import torch
+    from needle_b200 import native, synth
+    native.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    cb = synth.lloyd_max_codebook()
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    results, launches = [], 0
+    for name, rows, inputs, bits in QMATVEC_SHAPES:
+        pad = -(-inputs // 128) * 128
+        row_bytes = pad * (2 if bits == 5 else bits) // 8
+        mbytes = rows * row_bytes + rows * (pad // 128) * 2
+        n_sets = int(min(4096, max(4, -(-ROTATE_BYTES // mbytes))))
+        packed = torch.randint(0, 256, (n_sets, rows * row_bytes + 64), dtype=torch.uint8, device="cuda", generator=gen)
+        norms = (torch.randn((n_sets, rows * (pad // 128)), device="cuda", generator=gen).abs() * 0.01).half()
+        descs = [native.CqMatrixDesc(packed[i].data_ptr(), norms[i].data_ptr(), rows, inputs, 128, bits)
+                 for i in range(n_sets)]
+        for batch in (1, 8, 32, 128):
+            x = torch.randn((batch, inputs), device="cuda", generator=gen)
+            y = torch.empty((batch, rows), device="cuda")
+            lib = native.lib()
+
+            def call(i):
+                native.check(lib.needle_cuda_cq_matvec_dev(C.byref(descs[i]), native.ptr(cb), x.data_ptr(), batch,
+                                                           y.data_ptr(), stream.cuda_stream))
+            iters = max(20, min(args.steps, 200))
+            ms = _time_calls(torch, stream, call, n_sets, max(3, args.warmup), iters)
+            kernels = 3 if (batch <= 8 and pad // 128 >= 16) else 2
+            launches += kernels * iters
+            alg = mbytes + batch * 4 * (inputs + rows)
+            results.append({"shape": name, "batch": batch, "us": round(ms * 1e3, 3),
+                            "gbs": round(alg / (ms * 1e-3) / 1e9, 1), "bytes": alg, "kernels_per_call": kernels})
+        del packed, norms
+        torch.cuda.empty_cache()
+    head = next(r for r in results if r["shape"].startswith("stress") and r["batch"] == 1)
+    peak, src = _peak(peaks)
+    line = {"metric": "qmatvec HBM GB/s (exact numerics)", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
+            "steps": max(20, min(args.steps, 200)), "warmup": max(3, args.warmup), "ms_per_step": head["us"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "isolated quantised matvec (BASELINE config 2), headline 8192x8192 CQ4 batch 1",
+                       "l2": f"operand sets rotated over > {ROTATE_BYTES >> 20} MB", "cases": results},
+            "roofline": {"kernel": "k_cq_group_dots + k_cq_group_totals (split-group exact GEMV)", "bound": "hbm",
+                         "achieved": head["gbs"], "peak": peak, "peak_source": src, "unit": "GB/s",
+                         "frac": round(head["gbs"] / peak, 4), "traffic": None},
+            "gpu_launches": launches}
+    print(json.dumps(line), flush=True)
+
+
+def bench_attention(args, peaks):
+    """isolated int8-KV decode attention, batch 64, 8 query / 4 KV heads x 64,
+    visible counts uniform in [64, L] for L in {512, 2048, 8192}; codes uniform in [-127, 127],
+    scales |N(0,1)|*0.02, q N(0,1) (seed 3).  Exact and fast numerics."""
+    import torch
+    from needle_b200 import native
+    native.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    lib = native.lib()
+    results, launches = [], 0
+    for L in (512, 2048, 8192):
+        batch = 64
+        counts = torch.randint(64, L + 1, (batch,), dtype=torch.int32, device="cuda", generator=gen)
+        set_bytes = batch * 4 * L * (64 * 2 + 8)
+        n_sets = int(max(2, -(-ROTATE_BYTES // set_bytes)))
+        kc = torch.randint(-127, 128, (n_sets, batch, 4, L, 64), dtype=torch.int8, device="cuda", generator=gen)
+        vc = torch.randint(-127, 128, (n_sets, batch, 4, L, 64), dtype=torch.int8, device="cuda", generator=gen)
+        ks = torch.randn((n_sets, batch, 4, L), device="cuda", generator=gen).abs() * 0.02
+        vs = torch.randn((n_sets, batch, 4, L), device="cuda", generator=gen).abs() * 0.02
+        q = torch.randn((batch, 512), device="cuda", generator=gen)
+        out = torch.empty((batch, 512), device="cuda")
+        visible = int(counts.sum().item())
+        alg = visible * 4 * (64 * 2 + 8) + 2 * batch * 512 * 4 + batch * 4
+        for mode, fn, kernels in (("exact", lib.needle_cuda_attention_dev, 1),
+                                  ("fast", lib.needle_cuda_attention_dev_fast, 2)):
+            def call(i, fn=fn):
+                native.check(fn(q.data_ptr(), kc[i].data_ptr(), ks[i].data_ptr(), vc[i].data_ptr(), vs[i].data_ptr(),
+                                counts.data_ptr(), batch, L, out.data_ptr(), stream.cuda_stream))
+            iters = max(10, min(args.steps, 100))
+            ms = _time_calls(torch, stream, call, n_sets, max(3, args.warmup), iters)
+            launches += kernels * iters
+            results.append({"L": L, "numerics": mode, "us": round(ms * 1e3, 2),
+                            "gbs": round(alg / (ms * 1e-3) / 1e9, 1), "bytes": alg})
+        del kc, vc, ks, vs
+        torch.cuda.empty_cache()
+    head = next(r for r in results if r["L"] == 8192 and r["numerics"] == "fast")
+    peak, src = _peak(peaks)
+    line = {"metric": "int8-KV decode attention HBM GB/s", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
+            "steps": max(10, min(args.steps, 100)), "warmup": max(3, args.warmup), "ms_per_step": head["us"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fast) / f64 (exact)",
+            "data": "synthetic",
+            "config": {"workload": "isolated int8-KV decode attention (BASELINE config 3), headline L=8192 fast",
+                       "l2": f"KV sets rotated over > {ROTATE_BYTES >> 20} MB", "cases": results},
+            "roofline": {"kernel": "k_attention_fast (+ combine)", "bound": "hbm", "achieved": head["gbs"],
+                         "peak": peak, "peak_source": src, "unit": "GB/s", "frac": round(head["gbs"] / peak, 4),
+                         "traffic": None},
+            "gpu_launches": launches}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", choices=["decode", "qmatvec", "attention"], default="decode",
+                    help="decode: BASELINE config 4 (default); qmatvec / attention: configs 2 / 3 (1 GPU)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
@@ -189,6 +322,19 @@ def main():
                                         "of CQ weights stay L2-resident as in deployment",
               "parallelism": f"dp{args.gpus} (independent sequences per GPU, no collectives)"}
     metric, unit = "decode tokens/s", "tokens/s"
+
+    if args.workload != "decode" and args.impl == "cuda":
+        if rank != 0:
+            return
+        peaks = None
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except (OSError, ValueError):
+            pass
+        from needle_b200 import build as nbuild
+        nbuild.build()
+        (bench_qmatvec if args.workload == "qmatvec" else bench_attention)(args, peaks)
+        return
 
     if args.impl == "reference":
         if rank != 0:

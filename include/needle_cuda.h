@@ -201,6 +201,16 @@ int needle_cuda_attention_dev(const float* q, const int8_t* key_codes, const flo
                               const int32_t* counts, int32_t batch, int32_t capacity, float* out,
                               void* stream);
 
+/* The same attention in fast numerics: binary32 arithmetic, online softmax, positions split
+ * across CTAs and merged by max-rescaled sums (flash decoding).  Same arguments and layout as
+ * needle_cuda_attention_dev; results agree with the reference within binary32 rounding (not bit
+ * for bit).  capacity is unbounded.  Split partials go to a library-owned scratch buffer per
+ * device, grown with cudaMalloc when a call needs more. */
+int needle_cuda_attention_dev_fast(const float* q, const int8_t* key_codes, const float* key_scales,
+                                   const int8_t* value_codes, const float* value_scales,
+                                   const int32_t* counts, int32_t batch, int32_t capacity,
+                                   float* out, void* stream);
+
 /* ---- Benchmark / device-resident scheduling ---- */
 
 /* Returns the context's CUDA stream (a cudaStream_t) so callers can time on it. */

@@ -386,4 +386,136 @@ cudaError_t launch_cq_rows(const uint8_t* packed, const uint16_t* norms, int32_t
   return cudaGetLastError();
 }
 
+
+// ------------------------------------------------------------------ split-group GEMV (small batch)
+//
+// For few items and long rows a (row tile, item tile) unit is too coarse to fill the GPU: the
+// 8192 x 8192 stress matrix at batch 1 has 128 units for 148 SMs.  Here each unit is one
+// (64-row tile, 4-group chunk): its per-(row, group) dots go to scratch, and k_cq_group_totals then
+// forms every row's total over its groups in order -- the same operations, in the same order, as
+// the single-pass kernel.
+namespace {
+
+template <int BITS>
+__global__ void __launch_bounds__(kGemvThreads)
+k_cq_group_dots(const CqJob job, const Codebook cb, int32_t n, double* __restrict__ dots) {
+  constexpr int kTileRows = kRowsPerTile * kRowsPerThread;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  double* xs = reinterpret_cast<double*>(smem_raw);  // [kBT][512]
+  double* lut = xs + kBT * 512;                      // [16]
+  const int lane = threadIdx.x & 31, gc = threadIdx.x >> 5;
+  const int groups = job.in_pad / kGroup;
+  const int chunks = (groups + kGroupsPerChunk - 1) / kGroupsPerChunk;
+  const int tiles = (job.rows + kTileRows - 1) / kTileRows;
+  const int units = tiles * chunks;
+  if (threadIdx.x < 16) {
+    double v = 0.0;
+    if (BITS == kTernaryBits) {
+      const double coefficient = kTernaryCentroid / sqrt((double)kGroup);
+      const int t = threadIdx.x;
+      v = (t == 1) ? coefficient : (t == 3) ? -coefficient : 0.0;
+    } else if (threadIdx.x < (1 << BITS)) {
+      v = (double)cb.v[(BITS == 2 ? 0 : BITS == 3 ? 4 : 12) + threadIdx.x];
+    }
+    lut[threadIdx.x] = v;
+  }
+#pragma unroll 1
+  for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+    const int chunk = unit % chunks, tile = unit / chunks;  // neighbouring CTAs share rows
+    const int g0 = chunk * kGroupsPerChunk;
+    const int gn = min(kGroupsPerChunk, groups - g0);
+    const int nb = n;  // n <= kBT
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nb * gn * kGroup; idx += kGemvThreads) {
+      const int b = idx / (gn * kGroup);
+      const int c = idx - b * gn * kGroup;
+      xs[b * 512 + c] = (double)job.x[(int64_t)b * job.x_stride + g0 * kGroup + c];
+    }
+    __syncthreads();
+    if (gc >= gn) continue;
+    constexpr int kWords = GroupBytes<BITS>::value / 4;
+    uint32_t w[kRowsPerThread][kWords + 1];
+#pragma unroll
+    for (int r = 0; r < kRowsPerThread; r++) {
+      const int r_local = tile * kTileRows + r * 32 + lane;
+      const bool ok = r_local < job.rows;
+      const uint4* src = reinterpret_cast<const uint4*>(job.packed + ((int64_t)job.row_start + r_local) * job.row_bytes +
+                                                        (int64_t)(g0 + gc) * GroupBytes<BITS>::value);
+#pragma unroll
+      for (int q = 0; q < kWords / 4; q++) {
+        const uint4 u = ok ? __ldg(src + q) : make_uint4(0, 0, 0, 0);
+        w[r][4 * q] = u.x;
+        w[r][4 * q + 1] = u.y;
+        w[r][4 * q + 2] = u.z;
+        w[r][4 * q + 3] = u.w;
+      }
+      w[r][kWords] = 0;
+    }
+    double dot[kRowsPerThread][kBT];
+    group_dots<BITS>(w, lut, xs + gc * kGroup, nb, dot);
+#pragma unroll
+    for (int r = 0; r < kRowsPerThread; r++) {
+      const int r_local = tile * kTileRows + r * 32 + lane;
+      if (r_local >= job.rows) continue;
+#pragma unroll
+      for (int b = 0; b < kBT; b++)
+        if (b < nb) dots[((int64_t)b * job.rows + r_local) * groups + g0 + gc] = dot[r][b];
+    }
+  }
+}
+
+// total = sum_g norm[g] * dot[g] in group order (cq.ts:137-153), one thread per (row, item).
+__global__ void k_cq_group_totals(const CqJob job, int32_t n, const double* __restrict__ dots) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)n * job.rows) return;
+  const int b = int(idx / job.rows), r = int(idx - (int64_t)b * job.rows);
+  const int groups = job.in_pad / kGroup;
+  const double* d = dots + ((int64_t)b * job.rows + r) * groups;
+  const int64_t row = (int64_t)job.row_start + r;
+  double total = 0.0;
+  for (int g = 0; g < groups; g++) total = total + norm16(job.norms, row * groups + g) * d[g];
+  job.y[(int64_t)b * job.y_stride + r] = f32(total);
+}
+
+template <int BITS>
+cudaError_t split_launch(const CqJob& job, const Codebook& cb, int32_t n, double* scratch, cudaStream_t s) {
+  constexpr int kTileRows = kRowsPerTile * kRowsPerThread;
+  const size_t smem = sizeof(double) * (kBT * 512 + 16);
+  const int groups = job.in_pad / kGroup;
+  const int units = ((job.rows + kTileRows - 1) / kTileRows) * ((groups + kGroupsPerChunk - 1) / kGroupsPerChunk);
+  int per_sm = 0, sms = 0, device = 0;
+  cudaGetDevice(&device);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_cq_group_dots<BITS>, kGemvThreads, smem);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const int grid = std::min(units, std::max(1, per_sm) * std::max(1, sms));
+  k_cq_group_dots<BITS><<<grid, kGemvThreads, smem, s>>>(job, cb, n, scratch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int64_t threads = (int64_t)n * job.rows;
+  k_cq_group_totals<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(job, n, scratch);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t cq_gemv_split_scratch_bytes(const CqJob& job, int32_t n) {
+  return sizeof(double) * (size_t)n * job.rows * (job.in_pad / kGroup);
+}
+
+bool cq_gemv_prefers_split(const CqJob& job, int32_t n) {
+  return n >= 1 && n <= kBT && job.in_pad / kGroup >= 16;
+}
+
+cudaError_t launch_cq_gemv_split(const CqJob& job, const Codebook& cb, int32_t n, double* scratch, cudaStream_t s) {
+  if (n <= 0 || job.rows <= 0) return cudaSuccess;
+  if (n > kBT) return cudaErrorInvalidValue;
+  switch (job.bits) {
+    case 2: return split_launch<2>(job, cb, n, scratch, s);
+    case 3: return split_launch<3>(job, cb, n, scratch, s);
+    case 4: return split_launch<4>(job, cb, n, scratch, s);
+    case 5: return split_launch<5>(job, cb, n, scratch, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 }  // namespace needle

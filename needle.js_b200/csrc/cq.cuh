@@ -46,6 +46,11 @@ cudaError_t launch_cq_prepare(const float* x, int32_t x_stride, int32_t input_si
                               cudaStream_t s);
 cudaError_t launch_cq_gemv(const CqJobs& jobs, const Codebook& cb, int32_t n_host,
                            const int32_t* n_dev, cudaStream_t s);
+// Small-batch path for long rows (cq.cu): per-(row, group) dots of (row tile, group chunk) units
+// into `scratch` (cq_gemv_split_scratch_bytes), then ordered per-row totals.
+bool cq_gemv_prefers_split(const CqJob& job, int32_t n);
+size_t cq_gemv_split_scratch_bytes(const CqJob& job, int32_t n);
+cudaError_t launch_cq_gemv_split(const CqJob& job, const Codebook& cb, int32_t n, double* scratch, cudaStream_t s);
 cudaError_t launch_cq_rows(const uint8_t* packed, const uint16_t* norms, int32_t bits,
                            int32_t row_bytes, int32_t in_pad, int32_t input_size,
                            const int32_t* rows, int32_t n_rows, float* out, int32_t out_stride,

@@ -123,6 +123,11 @@ cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* 
                                  const float* vs, const int32_t* counts, int32_t batch,
                                  int32_t capacity, float* out, cudaStream_t s);
 size_t attention_smem_bytes(int32_t capacity, bool ring);
+// Fast-numerics attention (attn_fast.cu): scratch holds the split partials.
+size_t attention_fast_scratch_bytes(int32_t batch, int32_t capacity);
+cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
+                                  const float* vs, const int32_t* counts, int32_t batch, int32_t capacity,
+                                  float* out, void* scratch, cudaStream_t s);
 // Records the message returned by needle_cuda_last_error() on this thread (engine.cu).
 void set_last_error(const char* msg);
 inline void set_last_error(const std::string& msg) { set_last_error(msg.c_str()); }

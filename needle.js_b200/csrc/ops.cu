@@ -40,6 +40,30 @@ cudaError_t scratch_for(int device, size_t floats, float** out) {
   return cudaSuccess;
 }
 
+// Library-owned scratch for the split partials of the fast attention, one buffer per device.
+std::vector<DeviceScratch> g_attn_scratch;
+
+cudaError_t attn_scratch_for(int device, size_t bytes, void** out) {
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (int(g_attn_scratch.size()) <= device) g_attn_scratch.resize(device + 1);
+  DeviceScratch& s = g_attn_scratch[device];
+  const size_t floats = (bytes + 3) / 4;
+  if (s.floats < floats) {
+    if (s.ptr) {
+      cudaError_t e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) return e;
+      cudaFree(s.ptr);
+      s.ptr = nullptr;
+      s.floats = 0;
+    }
+    cudaError_t e = cudaMalloc(&s.ptr, floats * sizeof(float));
+    if (e != cudaSuccess) return e;
+    s.floats = floats;
+  }
+  *out = s.ptr;
+  return cudaSuccess;
+}
+
 int op_fail(int code, const std::string& msg) {
   set_last_error(msg);
   return code;
@@ -66,12 +90,18 @@ extern "C" int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float*
   for (int i = 0; i < 28; i++) cb.v[i] = codebook[i];
   int device = 0;
   cudaGetDevice(&device);
+  // Scratch: prepared activations, then (small batches of long rows) the per-group dots.
+  CqJob probe{};
+  probe.rows = m->rows;
+  probe.in_pad = in_pad;
+  const bool split = cq_gemv_prefers_split(probe, batch);
+  const size_t x_floats = (size_t(batch) * in_pad + 1) & ~size_t(1);  // keep the dots 8-byte aligned
+  const size_t dot_floats = split ? cq_gemv_split_scratch_bytes(probe, batch) / 4 : 0;
   float* xp = nullptr;
-  cudaError_t e = scratch_for(device, size_t(batch) * in_pad, &xp);
+  cudaError_t e = scratch_for(device, x_floats + dot_floats, &xp);
   if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
   e = launch_cq_prepare(x, m->input_size, m->input_size, in_pad, xp, in_pad, batch, nullptr, s);
   if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
-  // Split rows into <= kMaxJobs jobs only to keep every job inside one launch; one job suffices.
   CqJobs J{};
   CqJob& j = J.job[0];
   j.packed = m->packed;
@@ -88,7 +118,8 @@ extern "C" int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float*
   j.y_stride = m->rows;
   J.count = 1;
   J.total_tiles = (m->rows + kGemvTileRows - 1) / kGemvTileRows;
-  e = launch_cq_gemv(J, cb, batch, nullptr, s);
+  e = split ? launch_cq_gemv_split(j, cb, batch, reinterpret_cast<double*>(xp + x_floats), s)
+            : launch_cq_gemv(J, cb, batch, nullptr, s);
   if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
   return NEEDLE_OK;
 }
@@ -181,6 +212,27 @@ extern "C" int needle_cuda_attention_dev(const float* q, const int8_t* key_codes
     return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "capacity too large for the exact attention kernel");
   cudaError_t e = launch_attention_dev(q, key_codes, key_scales, value_codes, value_scales, counts, batch, capacity,
                                        out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  return NEEDLE_OK;
+}
+
+extern "C" int needle_cuda_attention_dev_fast(const float* q, const int8_t* key_codes, const float* key_scales,
+                                              const int8_t* value_codes, const float* value_scales,
+                                              const int32_t* counts, int32_t batch, int32_t capacity, float* out,
+                                              void* stream) {
+  if (batch < 0 || capacity <= 0) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "bad batch / capacity");
+  if (batch == 0) return NEEDLE_OK;
+  if (!q || !key_codes || !key_scales || !value_codes || !value_scales || !counts || !out)
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+  if ((reinterpret_cast<uintptr_t>(key_codes) & 15) != 0 || (reinterpret_cast<uintptr_t>(value_codes) & 15) != 0)
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "key/value codes must be 16-byte aligned");
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  void* scratch = nullptr;
+  if (e == cudaSuccess) e = attn_scratch_for(device, attention_fast_scratch_bytes(batch, capacity), &scratch);
+  if (e == cudaSuccess)
+    e = launch_attention_fast(q, key_codes, key_scales, value_codes, value_scales, counts, batch, capacity, out,
+                              scratch, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
   return NEEDLE_OK;
 }

@@ -83,6 +83,8 @@ EXPORTS = {
                                                     C.c_int32, C.c_void_p, C.c_void_p]),
     "needle_cuda_attention_dev": (C.c_int, [C.c_void_p] * 6 + [C.c_int32, C.c_int32, C.c_void_p,
                                                                 C.c_void_p]),
+    "needle_cuda_attention_dev_fast": (C.c_int, [C.c_void_p] * 6 + [C.c_int32, C.c_int32, C.c_void_p,
+                                                                     C.c_void_p]),
     "needle_cuda_stream": (C.c_void_p, [C.c_void_p]),
     "needle_cuda_sched_load": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_int32]),

@@ -78,6 +78,56 @@ def test_cq_matvec_dev_bit_exact(torch_cuda, oracle, bits, rows, inputs):
         np.testing.assert_array_equal(y[b], m.matvec(x[b]), err_msg=f"batch item {b}")
 
 
+@pytest.mark.parametrize("bits,batch", [(4, 1), (3, 1), (5, 3), (2, 8)])
+def test_cq_matvec_dev_long_rows_small_batch_bit_exact(torch_cuda, oracle, bits, batch):
+    """Small batches of long rows take the split-group path (per-group dots, then ordered totals)."""
+    torch = torch_cuda
+    from needle_b200 import native, synth
+    rows, inputs = 300, 8192 - 64  # a padded tail group too
+    packed, norms = synth.random_cq_matrix(rows, inputs, bits, seed=5)
+    cb = codebook()
+    x = synth.normal(5, batch * inputs, stream=9).astype(np.float32).reshape(batch, inputs)
+    d_packed = torch.from_numpy(packed.copy()).cuda()
+    d_norms = torch.from_numpy(norms.view(np.int16).copy()).cuda()
+    d_x = torch.from_numpy(x).cuda()
+    d_y = torch.zeros(batch, rows, dtype=torch.float32, device="cuda")
+    desc = native.CqMatrixDesc(d_packed.data_ptr(), d_norms.data_ptr(), rows, inputs, 128, bits)
+    native.check(native.lib().needle_cuda_cq_matvec_dev(C.byref(desc), native.ptr(cb), d_x.data_ptr(), batch,
+                                                        d_y.data_ptr(), None))
+    torch.cuda.synchronize()
+    m = oracle.CqMatrix(rows, inputs, 128, bits, packed, norms, cb[:4], cb[4:12], cb[12:])
+    y = d_y.cpu().numpy()
+    for b in range(batch):
+        np.testing.assert_array_equal(y[b], m.matvec(x[b]), err_msg=f"batch item {b}")
+
+
+def test_attention_dev_fast_within_tolerance(torch_cuda, oracle):
+    """Fast numerics (binary32, online softmax, split positions) vs the oracle's binary64 attention:
+    every output within 2e-4 of the largest output magnitude, including an 8192-position row."""
+    torch = torch_cuda
+    from needle_b200 import native
+    rng = np.random.default_rng(31)
+    batch, cap = 5, 8192
+    counts = np.array([1, 7, 1000, 1025, 8192], dtype=np.int32)
+    q = rng.standard_normal((batch, 512)).astype(np.float32)
+    kc = rng.integers(-127, 128, (batch, 4, cap, 64)).astype(np.int8)
+    vc = rng.integers(-127, 128, (batch, 4, cap, 64)).astype(np.int8)
+    ks = (np.abs(rng.standard_normal((batch, 4, cap))) * 0.02).astype(np.float32)
+    vs = (np.abs(rng.standard_normal((batch, 4, cap))) * 0.02).astype(np.float32)
+    d = {k: torch.from_numpy(v).cuda() for k, v in dict(q=q, kc=kc, vc=vc, ks=ks, vs=vs, n=counts).items()}
+    out = torch.zeros(batch, 512, dtype=torch.float32, device="cuda")
+    native.check(native.lib().needle_cuda_attention_dev_fast(
+        d["q"].data_ptr(), d["kc"].data_ptr(), d["ks"].data_ptr(), d["vc"].data_ptr(), d["vs"].data_ptr(),
+        d["n"].data_ptr(), batch, cap, out.data_ptr(), None))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for b in range(batch):
+        n = counts[b]
+        want = oracle.attention_int8(q[b], kc[b, :, :n], ks[b, :, :n], vc[b, :, :n], vs[b, :, :n])
+        err = np.max(np.abs(got[b].astype(np.float64) - want))
+        assert err <= 2e-4 * max(np.max(np.abs(want)), 1e-3), (b, n, err)
+
+
 def test_model_matvec_and_row_bit_exact(engine, ref_model):
     rng = np.random.default_rng(11)
     tensors = [0, 2, 3, 8, ref_model.num_tensors() - 3]
