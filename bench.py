@@ -183,15 +183,26 @@ def _peak(peaks):
 
 
 def _time_calls(torch, stream, fn, n_sets, warmup, iters):
+    """Device time per call: `iters` calls (rotating operand sets) captured once as a CUDA graph
+    after `warmup` eager calls, then the graph replayed between CUDA events, so host call overhead
+    stays out of the number.  fn(i, stream_handle) launches call i on the given stream."""
     for i in range(warmup):
-        fn(i % n_sets)
+        fn(i % n_sets, stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    with torch.cuda.graph(graph, stream=side):
+        cap = torch.cuda.current_stream().cuda_stream
+        for i in range(iters):
+            fn(i % n_sets, cap)
+    graph.replay()  # warm the graph
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(iters):
-        fn(i % n_sets)
+    graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
+    del graph
     return e0.elapsed_time(e1) / iters
 
 
@@ -220,27 +231,29 @@ def bench_qmatvec(args, peaks):
             x = torch.randn((batch, inputs), device="cuda", generator=gen)
             y = torch.empty((batch, rows), device="cuda")
             lib = native.lib()
-
-            def call(i):
-                native.check(lib.needle_cuda_cq_matvec_dev(C.byref(descs[i]), native.ptr(cb), x.data_ptr(), batch,
-                                                           y.data_ptr(), stream.cuda_stream))
-            iters = max(20, min(args.steps, 200))
-            ms = _time_calls(torch, stream, call, n_sets, max(3, args.warmup), iters)
-            kernels = 3 if (batch <= 8 and pad // 128 >= 16) else 2
-            launches += kernels * iters
-            alg = mbytes + batch * 4 * (inputs + rows)
-            results.append({"shape": name, "batch": batch, "us": round(ms * 1e3, 3),
-                            "gbs": round(alg / (ms * 1e-3) / 1e9, 1), "bytes": alg, "kernels_per_call": kernels})
+            modes = [("exact", lib.needle_cuda_cq_matvec_dev, 3 if (batch <= 8 and pad // 128 >= 16) else 2)]
+            if bits in (2, 4, 5):
+                modes.append(("fast", lib.needle_cuda_cq_matvec_dev_fast, 1 + -(-batch // 4)))
+            for mode, fn, kernels in modes:
+                def call(i, strm, fn=fn):
+                    native.check(fn(C.byref(descs[i]), native.ptr(cb), x.data_ptr(), batch, y.data_ptr(), strm))
+                iters = max(20, min(args.steps, 200))
+                ms = _time_calls(torch, stream, call, n_sets, max(3, args.warmup), iters)
+                launches += kernels * iters
+                alg = mbytes + batch * 4 * (inputs + rows)
+                results.append({"shape": name, "batch": batch, "numerics": mode, "us": round(ms * 1e3, 3),
+                                "gbs": round(alg / (ms * 1e-3) / 1e9, 1), "bytes": alg, "kernels_per_call": kernels})
         del packed, norms
         torch.cuda.empty_cache()
-    head = next(r for r in results if r["shape"].startswith("stress") and r["batch"] == 1)
+    head = next(r for r in results if r["shape"].startswith("stress") and r["batch"] == 1 and r["numerics"] == "fast")
     peak, src = _peak(peaks)
-    line = {"metric": "qmatvec HBM GB/s (exact numerics)", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
+    line = {"metric": "qmatvec HBM GB/s", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
             "steps": max(20, min(args.steps, 200)), "warmup": max(3, args.warmup), "ms_per_step": head["us"] / 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": "isolated quantised matvec (BASELINE config 2), headline 8192x8192 CQ4 batch 1",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fast) / f64 (exact)",
+            "data": "synthetic", "config": {"workload": "isolated quantised matvec (BASELINE config 2), headline 8192x8192 CQ4 batch 1, "
+                                   "fast numerics; exact-numerics rows alongside",
                        "l2": f"operand sets rotated over > {ROTATE_BYTES >> 20} MB", "cases": results},
-            "roofline": {"kernel": "k_cq_group_dots + k_cq_group_totals (split-group exact GEMV)", "bound": "hbm",
+            "roofline": {"kernel": "k_cq_gemv_fast (+ k_cq_prepare)", "bound": "hbm",
                          "achieved": head["gbs"], "peak": peak, "peak_source": src, "unit": "GB/s",
                          "frac": round(head["gbs"] / peak, 4), "traffic": None},
             "gpu_launches": launches}
@@ -274,9 +287,9 @@ def bench_attention(args, peaks):
         alg = visible * 4 * (64 * 2 + 8) + 2 * batch * 512 * 4 + batch * 4
         for mode, fn, kernels in (("exact", lib.needle_cuda_attention_dev, 1),
                                   ("fast", lib.needle_cuda_attention_dev_fast, 2)):
-            def call(i, fn=fn):
+            def call(i, strm, fn=fn):
                 native.check(fn(q.data_ptr(), kc[i].data_ptr(), ks[i].data_ptr(), vc[i].data_ptr(), vs[i].data_ptr(),
-                                counts.data_ptr(), batch, L, out.data_ptr(), stream.cuda_stream))
+                                counts.data_ptr(), batch, L, out.data_ptr(), strm))
             iters = max(10, min(args.steps, 100))
             ms = _time_calls(torch, stream, call, n_sets, max(3, args.warmup), iters)
             launches += kernels * iters

@@ -170,6 +170,13 @@ typedef struct needle_cq_matrix {
 int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float* codebook, const float* x,
                               int32_t batch, float* y, void* stream);
 
+/* The same matvec in fast numerics (binary32 FMAs, tree reductions; record widths 2, 4 and
+ * ternary): results agree with cqMatvec within binary32 rounding, not bit for bit.  Weights are
+ * streamed once with coalesced 16-byte loads.  Same arguments and scratch as
+ * needle_cuda_cq_matvec_dev; 3-bit matrices return UNSUPPORTED_CACT. */
+int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const float* codebook, const float* x,
+                                   int32_t batch, float* y, void* stream);
+
 /* Capacity, in floats, of the fixed scratch array used by needle_cuda_cq_matvec_dev_noalloc:
  * batch * input_padded must not exceed it (4 MiB of device memory per GPU). */
 #define NEEDLE_NOALLOC_MAX_FLOATS (1 << 20)

@@ -60,136 +60,178 @@ struct GroupBytes {
 };
 
 constexpr int kRowsPerThread = 2;
+constexpr int kTileRows = kRowsPerTile * kRowsPerThread;  // 64
 
-// Dot products of kRowsPerThread rows (same group) against kBT items.  xg points at this warp's
-// group inside item 0 of the staged [kBT][512] binary64 inputs; every x operand is loaded once
-// and used for both rows.
+// A (64-row, 4-group) weight tile staged in shared memory, [group][row][stride]; the stride is the
+// group's bytes + 4, an odd number of words, so the 32 rows a warp reads sit on distinct banks.
 template <int BITS>
-__device__ __forceinline__ void group_dots(const uint32_t (&w)[kRowsPerThread][GroupBytes<BITS>::value / 4 + 1],
-                                           const double* lut, const double* __restrict__ xg, int nb,
+struct Stage {
+  static constexpr int kBytes = GroupBytes<BITS>::value;
+  static constexpr int kStride = kBytes + 4;
+  static constexpr int kSize = kGroupsPerChunk * kTileRows * kStride;
+};
+
+template <int BITS>
+__device__ __forceinline__ void stage_weights(uint8_t* wt, const CqJob& job, int tile, int g0, int gn) {
+  constexpr int kWords = Stage<BITS>::kBytes / 4;
+  const int total = gn * kTileRows * kWords;
+  for (int idx = threadIdx.x; idx < total; idx += kGemvThreads) {
+    const int gq = idx / (kTileRows * kWords);
+    const int rem = idx - gq * kTileRows * kWords;
+    const int row = rem / kWords, w = rem - row * kWords;
+    const int r_local = tile * kTileRows + row;
+    uint32_t v = 0;
+    if (r_local < job.rows)
+      v = __ldg(reinterpret_cast<const uint32_t*>(job.packed + ((int64_t)job.row_start + r_local) * job.row_bytes +
+                                                  (int64_t)(g0 + gq) * Stage<BITS>::kBytes) + w);
+    *reinterpret_cast<uint32_t*>(wt + (gq * kTileRows + row) * Stage<BITS>::kStride + 4 * w) = v;
+  }
+}
+
+// Dot products of one (row pair, group) against kBT items, the chains interleaved across the
+// 2 x kBT (row, item) pairs so that independent binary64 operations issue back to back.  Each
+// chain is the reference's: per byte the 4 (2-bit, ternary) or 2 (4-bit) column products summed
+// left to right, then added to the group's dot; 3-bit rows add one product per column.
+// `wrow[r]` points at row r's staged group, `xg` at the group's columns of item 0 of the
+// [kBT][512] binary64 inputs.
+template <int BITS>
+__device__ __forceinline__ void group_dots(const uint8_t* wrow0, const uint8_t* wrow1, const double* lut,
+                                           const double* __restrict__ xg, int nb,
                                            double (&dot)[kRowsPerThread][kBT]) {
 #pragma unroll
   for (int r = 0; r < kRowsPerThread; r++)
 #pragma unroll
     for (int b = 0; b < kBT; b++) dot[r][b] = 0.0;
-  if constexpr (BITS == 2 || BITS == kTernaryBits) {
-    // 32 bytes per row: 4 columns per byte, low crumb first.  Fully unrolled so every word index
-    // is a compile-time constant and the weights stay in registers.
+  const uint8_t* wrow[kRowsPerThread] = {wrow0, wrow1};
+  if constexpr (BITS == 2 || BITS == kTernaryBits || BITS == 4) {
+    constexpr int kCols = BITS == 4 ? 2 : 4;  // columns per byte
+#pragma unroll 1
+    for (int wi = 0; wi < GroupBytes<BITS>::value / 4; wi++) {
+      uint32_t word[kRowsPerThread];
 #pragma unroll
-    for (int byte_i = 0; byte_i < 32; byte_i++) {
-      double a[kRowsPerThread][4];
+      for (int r = 0; r < kRowsPerThread; r++) word[r] = *reinterpret_cast<const uint32_t*>(wrow[r] + 4 * wi);
 #pragma unroll
-      for (int r = 0; r < kRowsPerThread; r++) {
-        const uint32_t byte = (w[r][byte_i >> 2] >> ((byte_i & 3) * 8)) & 0xffu;
-        a[r][0] = lut[byte & 3];
-        a[r][1] = lut[(byte >> 2) & 3];
-        a[r][2] = lut[(byte >> 4) & 3];
-        a[r][3] = lut[(byte >> 6) & 3];
-      }
-      const int c = byte_i * 4;
+      for (int byte_i = 0; byte_i < 4; byte_i++) {
+        const int c = (wi * 4 + byte_i) * kCols;
+        double a[kRowsPerThread][kCols];
 #pragma unroll
-      for (int b = 0; b < kBT; b++) {
-        if (b < nb) {
-          const double2 x01 = *reinterpret_cast<const double2*>(xg + b * 512 + c);
-          const double2 x23 = *reinterpret_cast<const double2*>(xg + b * 512 + c + 2);
+        for (int r = 0; r < kRowsPerThread; r++) {
+          const uint32_t byte = (word[r] >> (8 * byte_i)) & 0xffu;
 #pragma unroll
-          for (int r = 0; r < kRowsPerThread; r++) {
-            double s;
-            if constexpr (BITS == 2) {
-              // codebook levels are binary32: every product is exact, so fma == add(product)
-              s = a[r][0] * x01.x;
-              s = fma(a[r][1], x01.y, s);
-              s = fma(a[r][2], x23.x, s);
-              s = fma(a[r][3], x23.y, s);
-            } else {
-              // ternary levels are binary64 (1.2240064 / sqrt(g)): round every product
-              s = a[r][0] * x01.x;
-              s = s + a[r][1] * x01.y;
-              s = s + a[r][2] * x23.x;
-              s = s + a[r][3] * x23.y;
+          for (int k = 0; k < kCols; k++)
+            a[r][k] = BITS == 4 ? lut[(byte >> (4 * k)) & 15] : lut[(byte >> (2 * k)) & 3];
+        }
+        double x[kBT][kCols];
+#pragma unroll
+        for (int b = 0; b < kBT; b++) {
+          if (b < nb) {
+#pragma unroll
+            for (int k = 0; k < kCols; k += 2) {
+              const double2 v = *reinterpret_cast<const double2*>(xg + b * 512 + c + k);
+              x[b][k] = v.x;
+              x[b][k + 1] = v.y;
             }
-            dot[r][b] = dot[r][b] + s;
+          } else {
+#pragma unroll
+            for (int k = 0; k < kCols; k++) x[b][k] = 0.0;
           }
         }
+        double sacc[kRowsPerThread][kBT];
+#pragma unroll
+        for (int r = 0; r < kRowsPerThread; r++)
+#pragma unroll
+          for (int b = 0; b < kBT; b++) sacc[r][b] = a[r][0] * x[b][0];
+#pragma unroll
+        for (int k = 1; k < kCols; k++)
+#pragma unroll
+          for (int r = 0; r < kRowsPerThread; r++)
+#pragma unroll
+            for (int b = 0; b < kBT; b++) {
+              if constexpr (BITS == kTernaryBits)
+                sacc[r][b] = sacc[r][b] + a[r][k] * x[b][k];  // binary64 levels: rounded product
+              else
+                sacc[r][b] = fma(a[r][k], x[b][k], sacc[r][b]);  // binary32 levels: exact product
+            }
+#pragma unroll
+        for (int r = 0; r < kRowsPerThread; r++)
+#pragma unroll
+          for (int b = 0; b < kBT; b++) dot[r][b] = dot[r][b] + sacc[r][b];
       }
     }
-  } else if constexpr (BITS == 4) {
-#pragma unroll
-    for (int byte_i = 0; byte_i < 64; byte_i++) {
-      double a[kRowsPerThread][2];
-#pragma unroll
-      for (int r = 0; r < kRowsPerThread; r++) {
-        const uint32_t byte = (w[r][byte_i >> 2] >> ((byte_i & 3) * 8)) & 0xffu;
-        a[r][0] = lut[byte & 15];
-        a[r][1] = lut[byte >> 4];
-      }
-      const int c = byte_i * 2;
-#pragma unroll
-      for (int b = 0; b < kBT; b++) {
-        if (b < nb) {
-          const double2 x01 = *reinterpret_cast<const double2*>(xg + b * 512 + c);
-#pragma unroll
-          for (int r = 0; r < kRowsPerThread; r++) {
-            double s = a[r][0] * x01.x;
-            s = fma(a[r][1], x01.y, s);
-            dot[r][b] = dot[r][b] + s;
-          }
-        }
-      }
-    }
-  } else {  // 3-bit: dot = round(dot + level * x) per column, exact products; two columns a step
-#pragma unroll
-    for (int c = 0; c < kGroup; c += 2) {
-      double a[kRowsPerThread][2];
+  } else {
+    // 3-bit: 32 columns (three words, 96 bits) per outer step, one exact-product fma per column.
+#pragma unroll 1
+    for (int q = 0; q < 4; q++) {
+      uint32_t w[kRowsPerThread][3];
 #pragma unroll
       for (int r = 0; r < kRowsPerThread; r++)
 #pragma unroll
-        for (int k = 0; k < 2; k++) {
-          const int bit = (c + k) * 3;
-          const int wi = bit >> 5, sh = bit & 31;
-          uint32_t v = w[r][wi] >> sh;
-          if (sh > 29) v |= w[r][wi + 1] << (32 - sh);
-          a[r][k] = lut[v & 7];
-        }
+        for (int k = 0; k < 3; k++) w[r][k] = *reinterpret_cast<const uint32_t*>(wrow[r] + 12 * q + 4 * k);
 #pragma unroll
-      for (int b = 0; b < kBT; b++)
-        if (b < nb) {
-          const double2 x = *reinterpret_cast<const double2*>(xg + b * 512 + c);
+      for (int c2 = 0; c2 < 32; c2 += 2) {
+        double a[kRowsPerThread][2];
 #pragma unroll
-          for (int r = 0; r < kRowsPerThread; r++) {
-            dot[r][b] = fma(a[r][0], x.x, dot[r][b]);
-            dot[r][b] = fma(a[r][1], x.y, dot[r][b]);
+        for (int r = 0; r < kRowsPerThread; r++)
+#pragma unroll
+          for (int k = 0; k < 2; k++) {
+            const int bit = (c2 + k) * 3, wi = bit >> 5, sh = bit & 31;
+            uint32_t v = w[r][wi] >> sh;
+            if (sh > 29) v |= w[r][wi + 1] << (32 - sh);
+            a[r][k] = lut[v & 7];
+          }
+#pragma unroll
+        for (int b = 0; b < kBT; b++) {
+          if (b < nb) {
+            const double2 v = *reinterpret_cast<const double2*>(xg + b * 512 + 32 * q + c2);
+#pragma unroll
+            for (int r = 0; r < kRowsPerThread; r++) {
+              dot[r][b] = fma(a[r][0], v.x, dot[r][b]);
+              dot[r][b] = fma(a[r][1], v.y, dot[r][b]);
+            }
           }
         }
+      }
     }
+  }
+}
+
+__device__ __forceinline__ void fill_gemv_lut(double* lut, const Codebook& cb, int bits) {
+  if (threadIdx.x < 16) {
+    double v = 0.0;
+    if (bits == kTernaryBits) {
+      const double coefficient = kTernaryCentroid / sqrt((double)kGroup);
+      const int t = threadIdx.x;
+      v = (t == 1) ? coefficient : (t == 3) ? -coefficient : 0.0;  // crumbs [0, c, 0, -c]
+    } else if ((int)threadIdx.x < (1 << bits)) {
+      v = (double)cb.v[(bits == 2 ? 0 : bits == 3 ? 4 : 12) + threadIdx.x];
+    }
+    lut[threadIdx.x] = v;
+  }
+}
+
+// Stages the chunk's inputs of items [b0, b0 + nb) as binary64 (exact widening).
+__device__ __forceinline__ void stage_inputs(double* xs, const CqJob& job, int b0, int nb, int g0, int gn) {
+  for (int idx = threadIdx.x; idx < nb * gn * kGroup; idx += kGemvThreads) {
+    const int b = idx / (gn * kGroup);
+    const int c = idx - b * gn * kGroup;
+    xs[b * 512 + c] = (double)job.x[(int64_t)(b0 + b) * job.x_stride + g0 * kGroup + c];
   }
 }
 
 template <int BITS>
 __global__ void __launch_bounds__(kGemvThreads)
 k_cq_gemv(const CqJobs jobs, const Codebook cb, int32_t n_host, const int32_t* n_dev) {
-  constexpr int kTileRows = kRowsPerTile * kRowsPerThread;  // 64
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  double* xs = reinterpret_cast<double*>(smem_raw);          // [kBT][512]
-  double* dsm = xs + kBT * 512;                              // [kBT][4][64]
-  double* lut = dsm + kBT * kGroupsPerChunk * kTileRows;     // [16]
-
+  double* xs = reinterpret_cast<double*>(smem_raw);                   // [kBT][512]
+  double* dsm = xs + kBT * 512;                                       // [kBT][4][64]
+  double* lut = dsm + kBT * kGroupsPerChunk * kTileRows;              // [16]
+  uint8_t* wt = reinterpret_cast<uint8_t*>(lut + 16);                 // Stage<BITS>
   const int n = item_count(n_host, n_dev);
   const int item_tiles = (n + kBT - 1) / kBT;
   const int units = jobs.total_tiles * item_tiles;
   const int lane = threadIdx.x & 31;
   const int gc = threadIdx.x >> 5;  // group within the chunk
-  if (threadIdx.x < 16) {
-    double v = 0.0;
-    if (BITS == kTernaryBits) {
-      const double coefficient = kTernaryCentroid / sqrt((double)kGroup);
-      const int t = threadIdx.x;
-      v = (t == 1) ? coefficient : (t == 3) ? -coefficient : 0.0;  // crumbs [0, c, 0, -c]
-    } else if (threadIdx.x < (1 << BITS)) {
-      v = (double)cb.v[(BITS == 2 ? 0 : BITS == 3 ? 4 : 12) + threadIdx.x];
-    }
-    lut[threadIdx.x] = v;
-  }
+  fill_gemv_lut(lut, cb, BITS);
 
   // Persistent loop over (row tile, item tile) units; consecutive units share an item tile.
 #pragma unroll 1
@@ -213,47 +255,19 @@ k_cq_gemv(const CqJobs jobs, const Codebook cb, int32_t n_host, const int32_t* n
 
     for (int g0 = 0; g0 < groups; g0 += kGroupsPerChunk) {
       const int gn = min(kGroupsPerChunk, groups - g0);
-      __syncthreads();  // previous chunk's xs / dsm fully consumed
-      // Stage the chunk's inputs as binary64 (exact widening).
-      for (int idx = threadIdx.x; idx < nb * gn * kGroup; idx += kGemvThreads) {
-        const int b = idx / (gn * kGroup);
-        const int c = idx - b * gn * kGroup;
-        xs[b * 512 + c] = (double)job.x[(int64_t)(b0 + b) * job.x_stride + g0 * kGroup + c];
-      }
+      __syncthreads();  // previous chunk's xs / dsm / wt fully consumed
+      stage_inputs(xs, job, b0, nb, g0, gn);
+      stage_weights<BITS>(wt, job, tile, g0, gn);
       __syncthreads();
       double dot[kRowsPerThread][kBT];
-      constexpr int kWords = GroupBytes<BITS>::value / 4;
-      uint32_t w[kRowsPerThread][kWords + 1];
-      bool any = false;
-#pragma unroll
-      for (int r = 0; r < kRowsPerThread; r++) {
-        const int r_local = tile * kTileRows + r * 32 + lane;
-        const bool ok = gc < gn && r_local < job.rows;
-        any |= ok;
-        const uint4* src = reinterpret_cast<const uint4*>(
-            job.packed + ((int64_t)job.row_start + r_local) * job.row_bytes + (int64_t)(g0 + gc) * GroupBytes<BITS>::value);
-#pragma unroll
-        for (int q = 0; q < kWords / 4; q++) {
-          const uint4 u = ok ? __ldg(src + q) : make_uint4(0, 0, 0, 0);
-          w[r][4 * q] = u.x;
-          w[r][4 * q + 1] = u.y;
-          w[r][4 * q + 2] = u.z;
-          w[r][4 * q + 3] = u.w;
-        }
-        w[r][kWords] = 0;
-      }
-      if (any) {
-        group_dots<BITS>(w, lut, xs + gc * kGroup, nb, dot);
-      } else {
+      if (gc < gn) {
+        const uint8_t* w0 = wt + (gc * kTileRows + lane) * Stage<BITS>::kStride;
+        group_dots<BITS>(w0, w0 + 32 * Stage<BITS>::kStride, lut, xs + gc * kGroup, nb, dot);
 #pragma unroll
         for (int r = 0; r < kRowsPerThread; r++)
 #pragma unroll
-          for (int b = 0; b < kBT; b++) dot[r][b] = 0.0;
+          for (int b = 0; b < kBT; b++) dsm[(b * kGroupsPerChunk + gc) * kTileRows + r * 32 + lane] = dot[r][b];
       }
-#pragma unroll
-      for (int r = 0; r < kRowsPerThread; r++)
-#pragma unroll
-        for (int b = 0; b < kBT; b++) dsm[(b * kGroupsPerChunk + gc) * kTileRows + r * 32 + lane] = dot[r][b];
       __syncthreads();
       // total += norm * dot, group by group in order (cq.ts:151).
 #pragma unroll
@@ -319,7 +333,7 @@ cudaError_t launch_cq_prepare(const float* x, int32_t x_stride, int32_t input_si
 }
 
 static size_t gemv_smem() {
-  return sizeof(double) * (kBT * 512 + kBT * kGroupsPerChunk * kRowsPerTile * kRowsPerThread + 16);
+  return sizeof(double) * (kBT * 512 + kBT * kGroupsPerChunk * kTileRows + 16) + Stage<4>::kSize;
 }
 
 // Opts the GEMV instantiations into more than 48 KB of dynamic shared memory, once per device.
@@ -399,67 +413,36 @@ namespace {
 template <int BITS>
 __global__ void __launch_bounds__(kGemvThreads)
 k_cq_group_dots(const CqJob job, const Codebook cb, int32_t n, double* __restrict__ dots) {
-  constexpr int kTileRows = kRowsPerTile * kRowsPerThread;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   double* xs = reinterpret_cast<double*>(smem_raw);  // [kBT][512]
   double* lut = xs + kBT * 512;                      // [16]
+  uint8_t* wt = reinterpret_cast<uint8_t*>(lut + 16);
   const int lane = threadIdx.x & 31, gc = threadIdx.x >> 5;
   const int groups = job.in_pad / kGroup;
   const int chunks = (groups + kGroupsPerChunk - 1) / kGroupsPerChunk;
   const int tiles = (job.rows + kTileRows - 1) / kTileRows;
   const int units = tiles * chunks;
-  if (threadIdx.x < 16) {
-    double v = 0.0;
-    if (BITS == kTernaryBits) {
-      const double coefficient = kTernaryCentroid / sqrt((double)kGroup);
-      const int t = threadIdx.x;
-      v = (t == 1) ? coefficient : (t == 3) ? -coefficient : 0.0;
-    } else if (threadIdx.x < (1 << BITS)) {
-      v = (double)cb.v[(BITS == 2 ? 0 : BITS == 3 ? 4 : 12) + threadIdx.x];
-    }
-    lut[threadIdx.x] = v;
-  }
+  fill_gemv_lut(lut, cb, BITS);
 #pragma unroll 1
   for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
     const int chunk = unit % chunks, tile = unit / chunks;  // neighbouring CTAs share rows
     const int g0 = chunk * kGroupsPerChunk;
     const int gn = min(kGroupsPerChunk, groups - g0);
-    const int nb = n;  // n <= kBT
     __syncthreads();
-    for (int idx = threadIdx.x; idx < nb * gn * kGroup; idx += kGemvThreads) {
-      const int b = idx / (gn * kGroup);
-      const int c = idx - b * gn * kGroup;
-      xs[b * 512 + c] = (double)job.x[(int64_t)b * job.x_stride + g0 * kGroup + c];
-    }
+    stage_inputs(xs, job, 0, n, g0, gn);
+    stage_weights<BITS>(wt, job, tile, g0, gn);
     __syncthreads();
     if (gc >= gn) continue;
-    constexpr int kWords = GroupBytes<BITS>::value / 4;
-    uint32_t w[kRowsPerThread][kWords + 1];
-#pragma unroll
-    for (int r = 0; r < kRowsPerThread; r++) {
-      const int r_local = tile * kTileRows + r * 32 + lane;
-      const bool ok = r_local < job.rows;
-      const uint4* src = reinterpret_cast<const uint4*>(job.packed + ((int64_t)job.row_start + r_local) * job.row_bytes +
-                                                        (int64_t)(g0 + gc) * GroupBytes<BITS>::value);
-#pragma unroll
-      for (int q = 0; q < kWords / 4; q++) {
-        const uint4 u = ok ? __ldg(src + q) : make_uint4(0, 0, 0, 0);
-        w[r][4 * q] = u.x;
-        w[r][4 * q + 1] = u.y;
-        w[r][4 * q + 2] = u.z;
-        w[r][4 * q + 3] = u.w;
-      }
-      w[r][kWords] = 0;
-    }
     double dot[kRowsPerThread][kBT];
-    group_dots<BITS>(w, lut, xs + gc * kGroup, nb, dot);
+    const uint8_t* w0 = wt + (gc * kTileRows + lane) * Stage<BITS>::kStride;
+    group_dots<BITS>(w0, w0 + 32 * Stage<BITS>::kStride, lut, xs + gc * kGroup, n, dot);
 #pragma unroll
     for (int r = 0; r < kRowsPerThread; r++) {
       const int r_local = tile * kTileRows + r * 32 + lane;
       if (r_local >= job.rows) continue;
 #pragma unroll
       for (int b = 0; b < kBT; b++)
-        if (b < nb) dots[((int64_t)b * job.rows + r_local) * groups + g0 + gc] = dot[r][b];
+        if (b < n) dots[((int64_t)b * job.rows + r_local) * groups + g0 + gc] = dot[r][b];
     }
   }
 }
@@ -479,8 +462,19 @@ __global__ void k_cq_group_totals(const CqJob job, int32_t n, const double* __re
 
 template <int BITS>
 cudaError_t split_launch(const CqJob& job, const Codebook& cb, int32_t n, double* scratch, cudaStream_t s) {
-  constexpr int kTileRows = kRowsPerTile * kRowsPerThread;
-  const size_t smem = sizeof(double) * (kBT * 512 + 16);
+  const size_t smem = sizeof(double) * (kBT * 512 + 16) + Stage<BITS>::kSize;
+  static std::atomic<uint64_t> configured{0};  // per device: > 48 KB dynamic shared memory opt-in
+  {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(configured.load() & bit)) {
+      e = cudaFuncSetAttribute(k_cq_group_dots<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      configured.fetch_or(bit);
+    }
+  }
   const int groups = job.in_pad / kGroup;
   const int units = ((job.rows + kTileRows - 1) / kTileRows) * ((groups + kGroupsPerChunk - 1) / kGroupsPerChunk);
   int per_sm = 0, sms = 0, device = 0;

@@ -288,6 +288,14 @@ struct needle_ctx {
   cudaStream_t stream = nullptr;
   cudaStream_t side = nullptr;             // routing (Sinkhorn) overlapped with attention
   cudaEvent_t fork_ev[2] = {nullptr, nullptr}, join_ev[2] = {nullptr, nullptr};
+  // Second micro-batch of the device-scheduled step (its own main and routing streams).
+  cudaStream_t stream2 = nullptr, side2 = nullptr;
+  cudaEvent_t fork2_ev[2] = {nullptr, nullptr}, join2_ev[2] = {nullptr, nullptr};
+  cudaEvent_t split_ev = nullptr, merge_ev = nullptr;
+  // The device-scheduled step captured as a CUDA graph after one eager step.
+  cudaGraphExec_t sched_graph = nullptr;
+  int64_t graph_launches = 0;
+  int sched_eager_steps = 0;
   std::vector<uint8_t> bytes;  // archive copy (host)
   Archive A;
   Roles roles;
@@ -358,18 +366,19 @@ struct needle_ctx {
     }
     prof_pending.clear();
   }
-  // Runs `launch` bracketed by events when profiling.
+  // Runs `launch` (which enqueues on `s`) bracketed by events when profiling.
   template <class F>
-  void timed(int cls, F&& launch) {
+  void timed(int cls, F&& launch, cudaStream_t s = nullptr) {
+    if (!s) s = stream;
     if (cls != P_COPY) launches += cls == P_SCHED ? 2 : 1;
     if (!profiling) {
       cuda_check(launch(), kProfNames[cls]);
       return;
     }
     cudaEvent_t a = get_event(), b = get_event();
-    cuda_check(cudaEventRecord(a, stream), "cudaEventRecord");
+    cuda_check(cudaEventRecord(a, s), "cudaEventRecord");
     cuda_check(launch(), kProfNames[cls]);
-    cuda_check(cudaEventRecord(b, stream), "cudaEventRecord");
+    cuda_check(cudaEventRecord(b, s), "cudaEventRecord");
     prof_pending.push_back({cls, a, b});
     if (prof_pending.size() > 4096) prof_drain();
   }
@@ -580,7 +589,7 @@ void build_state(needle_ctx& C) {
   StepView& st = C.stv;
   const size_t B = size_t(S);
   st.items = C.dalloc<DevItem>(B);
-  C.d_counts = C.dalloc<int32_t>(4);
+  C.d_counts = C.dalloc<int32_t>(8);
   st.n_items = C.d_counts;
   st.n_select = C.d_counts + 1;
   const int ns = std::max(1, m.n_sites);
@@ -637,7 +646,9 @@ struct JobSpec {
 };
 
 // Launches the jobs grouped by record width (one GEMV launch per width present).
-void run_gemv(needle_ctx& C, int cls, const std::vector<JobSpec>& specs, int n_host, const int32_t* n_dev) {
+void run_gemv(needle_ctx& C, int cls, const std::vector<JobSpec>& specs, int n_host, const int32_t* n_dev,
+              cudaStream_t strm = nullptr) {
+  if (!strm) strm = C.stream;
   for (int bits : {2, 3, 4, 5}) {
     CqJobs J{};
     for (const auto& s : specs)
@@ -646,17 +657,52 @@ void run_gemv(needle_ctx& C, int cls, const std::vector<JobSpec>& specs, int n_h
         add_job(J, s.M, s.row_start, s.rows, s.x, s.x_stride, s.y, s.y_stride);
       }
     if (J.count == 0) continue;
-    C.timed(cls, [&] { return launch_cq_gemv(J, C.mv.cb, n_host, n_dev, C.stream); });
+    C.timed(cls, [&] { return launch_cq_gemv(J, C.mv.cb, n_host, n_dev, strm); }, strm);
   }
 }
 
-// The kernel sequence of one batched step for up to n_host items (device counts in d_counts).
-void enqueue_step(needle_ctx& C, int n_host, bool any_select, const SchedView* sched) {
+// The streams one micro-batch of a step runs on: its main stream and the side stream of its
+// Sinkhorn routing, with the events that fork and join them per layer.
+struct Lane {
+  cudaStream_t main, side;
+  cudaEvent_t* fork;
+  cudaEvent_t* join;
+};
+
+// A view of the step scratch for the items [offset, ...) with their own device counts.
+StepView half_view(const needle_ctx& C, int offset, const int32_t* n_items, const int32_t* n_select) {
+  const StepView& st = C.stv;
+  const int64_t o = offset, ns = C.mv.n_sites;
+  StepView v = st;
+  v.items = st.items + o;
+  v.n_items = n_items;
+  v.n_select = n_select;
+  v.prep_engram = st.prep_engram + o * ns * kDim;
+  v.engram_kv = st.engram_kv + o * ns * 2 * kDim;
+  v.engram_val = st.engram_val + o * ns * kDim;
+  v.update = st.update + o * kDim;
+  v.block = st.block + o * kDim;
+  v.prep_a = st.prep_a + o * kDim;
+  v.qkvg = st.qkvg + o * 1536;
+  v.prep_o = st.prep_o + o * kDim;
+  v.proj = st.proj + o * kDim;
+  v.route = st.route + o * 20;
+  v.prep_f = st.prep_f + o * kDim;
+  v.logits = st.logits + o * C.mv.vocab;
+  v.out_id = st.out_id + o;
+  v.out_logprob = st.out_logprob + o;
+  return v;
+}
+
+// The kernel sequence of one batched step for up to n_host items of view `st` (device counts in
+// st.n_items / st.n_select), on the lane's streams.
+void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select, const SchedView* sched,
+                  const Lane& lane) {
   const ModelView& m = C.mv;
   const SlotView& sv = C.sv;
-  const StepView& st = C.stv;
   const int32_t* n_dev = st.n_items;
-  C.timed(P_EMBED, [&] { return launch_embed(m, sv, st, n_host, C.stream); });
+  cudaStream_t s0 = lane.main;
+  C.timed(P_EMBED, [&] { return launch_embed(m, sv, st, n_host, s0); }, s0);
   if (m.n_sites > 0) {
     std::vector<JobSpec> jobs;
     for (int s = 0; s < m.n_sites; s++) {
@@ -665,31 +711,58 @@ void enqueue_step(needle_ctx& C, int n_host, bool any_select, const SchedView* s
       jobs.push_back({C.ev[s], 0, 512, st.prep_engram + s * kDim, m.n_sites * kDim,
                       st.engram_kv + (s * 2 + 1) * kDim, m.n_sites * 2 * kDim});
     }
-    run_gemv(C, P_GEMV_ENGRAM, jobs, n_host, n_dev);
+    run_gemv(C, P_GEMV_ENGRAM, jobs, n_host, n_dev, s0);
   }
   for (int l = 0; l <= m.layers; l++) {
-    if (l > 0) cuda_check(cudaStreamWaitEvent(C.stream, C.join_ev[(l - 1) & 1], 0), "join");
-    C.timed(P_LAYER, [&] { return launch_layer(m, sv, st, l, n_host, C.stream); });
+    if (l > 0) cuda_check(cudaStreamWaitEvent(s0, lane.join[(l - 1) & 1], 0), "join");
+    C.timed(P_LAYER, [&] { return launch_layer(m, sv, st, l, n_host, s0); }, s0);
     if (l == m.layers) break;
     // Sinkhorn routing of layer l on the side stream, joined before the next k_layer.
-    cuda_check(cudaEventRecord(C.fork_ev[l & 1], C.stream), "fork");
-    cuda_check(cudaStreamWaitEvent(C.side, C.fork_ev[l & 1], 0), "fork");
-    cuda_check(launch_route(st, n_host, C.side), "route");
+    cuda_check(cudaEventRecord(lane.fork[l & 1], s0), "fork");
+    cuda_check(cudaStreamWaitEvent(lane.side, lane.fork[l & 1], 0), "fork");
+    cuda_check(launch_route(st, n_host, lane.side), "route");
     C.launches++;
-    cuda_check(cudaEventRecord(C.join_ev[l & 1], C.side), "join");
+    cuda_check(cudaEventRecord(lane.join[l & 1], lane.side), "join");
     run_gemv(C, P_GEMV_QKVG,
              {{C.lq[l], 0, 512, st.prep_a, kDim, st.qkvg, 1536},
               {C.lk[l], 0, 256, st.prep_a, kDim, st.qkvg + 512, 1536},
               {C.lv[l], 0, 256, st.prep_a, kDim, st.qkvg + 768, 1536},
               {C.lg[l], 0, 512, st.prep_a, kDim, st.qkvg + 1024, 1536}},
-             n_host, n_dev);
-    C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, C.stream); });
-    run_gemv(C, P_GEMV_O, {{C.lo[l], 0, 512, st.prep_o, kDim, st.proj, kDim}}, n_host, n_dev);
+             n_host, n_dev, s0);
+    C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0); }, s0);
+    run_gemv(C, P_GEMV_O, {{C.lo[l], 0, 512, st.prep_o, kDim, st.proj, kDim}}, n_host, n_dev, s0);
   }
   if (any_select)
     run_gemv(C, P_GEMV_VOCAB, {{m.embedding, 0, m.vocab, st.prep_f, kDim, st.logits, m.vocab}}, n_host,
-             st.n_select);
-  C.timed(P_FINISH, [&] { return launch_finish(m, sv, st, n_host, sched, C.stream); });
+             st.n_select, s0);
+  C.timed(P_FINISH, [&] { return launch_finish(m, sv, st, n_host, sched, s0); }, s0);
+}
+
+Lane lane_a(needle_ctx& C) { return Lane{C.stream, C.side, C.fork_ev, C.join_ev}; }
+Lane lane_b(needle_ctx& C) { return Lane{C.stream2, C.side2, C.fork2_ev, C.join2_ev}; }
+
+// One device-scheduled step: admission and item list on the device, then the busy slots as two
+// micro-batches on two stream pairs so the latency-bound k_layer of one overlaps the GEMVs and
+// attention of the other (one batch when profiling, so per-kernel times stay unperturbed).
+void enqueue_sched_step(needle_ctx& C) {
+  const int S = C.sched.n_slots;
+  const bool split = S >= 64 && !C.profiling;
+  const int hA = split ? (S + 1) / 2 : S;
+  C.timed(P_SCHED, [&] {
+    cudaError_t e = launch_sched_admit(C.sv, C.sched, C.mv.kv_window, C.stream);
+    if (e != cudaSuccess) return e;
+    return launch_sched(C.sv, C.stv, C.sched, C.d_counts, hA, C.stream);
+  });
+  if (!split) {
+    enqueue_step(C, half_view(C, 0, C.d_counts, C.d_counts + 1), S, true, &C.sched, lane_a(C));
+    return;
+  }
+  cuda_check(cudaEventRecord(C.split_ev, C.stream), "split");
+  cuda_check(cudaStreamWaitEvent(C.stream2, C.split_ev, 0), "split");
+  enqueue_step(C, half_view(C, 0, C.d_counts + 2, C.d_counts + 3), hA, true, &C.sched, lane_a(C));
+  enqueue_step(C, half_view(C, hA, C.d_counts + 4, C.d_counts + 5), S - hA, true, &C.sched, lane_b(C));
+  cuda_check(cudaEventRecord(C.merge_ev, C.stream2), "merge");
+  cuda_check(cudaStreamWaitEvent(C.stream, C.merge_ev, 0), "merge");
 }
 
 needle_ctx* ctx_of(needle_ctx* c) {
@@ -722,6 +795,15 @@ void destroy(needle_ctx* C) {
     if (C->fork_ev[k]) cudaEventDestroy(C->fork_ev[k]);
     if (C->join_ev[k]) cudaEventDestroy(C->join_ev[k]);
   }
+  if (C->sched_graph) cudaGraphExecDestroy(C->sched_graph);
+  for (int k = 0; k < 2; k++) {
+    if (C->fork2_ev[k]) cudaEventDestroy(C->fork2_ev[k]);
+    if (C->join2_ev[k]) cudaEventDestroy(C->join2_ev[k]);
+  }
+  if (C->split_ev) cudaEventDestroy(C->split_ev);
+  if (C->merge_ev) cudaEventDestroy(C->merge_ev);
+  if (C->side2) cudaStreamDestroy(C->side2);
+  if (C->stream2) cudaStreamDestroy(C->stream2);
   if (C->side) cudaStreamDestroy(C->side);
   if (C->stream) cudaStreamDestroy(C->stream);
   delete C;
@@ -798,10 +880,16 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
             "max_len exceeds the model's maximum sequence length");
     cuda_check(cudaStreamCreateWithFlags(&C->stream, cudaStreamNonBlocking), "cudaStreamCreate");
     cuda_check(cudaStreamCreateWithFlags(&C->side, cudaStreamNonBlocking), "cudaStreamCreate");
+    cuda_check(cudaStreamCreateWithFlags(&C->stream2, cudaStreamNonBlocking), "cudaStreamCreate");
+    cuda_check(cudaStreamCreateWithFlags(&C->side2, cudaStreamNonBlocking), "cudaStreamCreate");
     for (int k = 0; k < 2; k++) {
       cuda_check(cudaEventCreateWithFlags(&C->fork_ev[k], cudaEventDisableTiming), "cudaEventCreate");
       cuda_check(cudaEventCreateWithFlags(&C->join_ev[k], cudaEventDisableTiming), "cudaEventCreate");
+      cuda_check(cudaEventCreateWithFlags(&C->fork2_ev[k], cudaEventDisableTiming), "cudaEventCreate");
+      cuda_check(cudaEventCreateWithFlags(&C->join2_ev[k], cudaEventDisableTiming), "cudaEventCreate");
     }
+    cuda_check(cudaEventCreateWithFlags(&C->split_ev, cudaEventDisableTiming), "cudaEventCreate");
+    cuda_check(cudaEventCreateWithFlags(&C->merge_ev, cudaEventDisableTiming), "cudaEventCreate");
     build_model(*C);
     build_state(*C);
     cuda_check(cudaDeviceSynchronize(), "upload");
@@ -962,7 +1050,7 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, 
       if (e != cudaSuccess) return e;
       return cudaMemcpyAsync(C.d_counts, C.h_counts, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, C.stream);
     });
-    enqueue_step(C, n, any_sel, nullptr);
+    enqueue_step(C, C.stv, n, any_sel, nullptr, lane_a(C));
     if (n_sel > 0 || all_logits) {
       const int ns = all_logits ? n : n_sel;
       cuda_check(cudaMemcpyAsync(C.h_ids, C.stv.out_id, size_t(ns) * 4, cudaMemcpyDeviceToHost, C.stream), "readback");
@@ -1114,6 +1202,11 @@ int needle_cuda_sched_load(needle_ctx* ctx, int32_t n_slots, const int32_t* prom
       for (int32_t k = prompt_offsets[s]; k < prompt_offsets[s + 1]; k++)
         require(prompt_ids[k] >= 0 && prompt_ids[k] < C.mv.vocab, NEEDLE_INVALID_CACT, "prompt token outside vocabulary");
     cuda_check(cudaStreamSynchronize(C.stream), "sched_load");
+    if (C.sched_graph) {
+      cudaGraphExecDestroy(C.sched_graph);
+      C.sched_graph = nullptr;
+    }
+    C.sched_eager_steps = 0;
     for (void* p : C.sched_allocs) cudaFree(p);
     C.sched_allocs.clear();
     auto alloc = [&](size_t bytes) {
@@ -1158,12 +1251,33 @@ int needle_cuda_sched_step(needle_ctx* ctx, int32_t steps) {
     needle_ctx& C = *ctx_of(ctx);
     require(C.sched_loaded, NEEDLE_BACKEND_UNAVAILABLE, "no scheduler queue loaded");
     for (int32_t k = 0; k < steps; k++) {
-      C.timed(P_SCHED, [&] {
-        cudaError_t e = launch_sched_admit(C.sv, C.sched, C.mv.kv_window, C.stream);
-        if (e != cudaSuccess) return e;
-        return launch_sched(C.sv, C.stv, C.sched, C.d_counts, C.d_counts + 1, C.stream);
-      });
-      enqueue_step(C, C.sched.n_slots, true, &C.sched);
+      if (C.profiling || C.sched_eager_steps < 1) {
+        enqueue_sched_step(C);
+        C.sched_eager_steps++;
+        continue;
+      }
+      if (!C.sched_graph) {
+        // Capture one step (kernels on both micro-batch lanes, joined on the main stream).
+        cuda_check(cudaStreamBeginCapture(C.stream, cudaStreamCaptureModeThreadLocal), "capture");
+        const int64_t l0 = C.launches;
+        try {
+          enqueue_sched_step(C);
+        } catch (...) {
+          cudaGraph_t broken = nullptr;
+          cudaStreamEndCapture(C.stream, &broken);
+          if (broken) cudaGraphDestroy(broken);
+          throw;
+        }
+        C.graph_launches = C.launches - l0;
+        C.launches = l0;
+        cudaGraph_t g = nullptr;
+        cuda_check(cudaStreamEndCapture(C.stream, &g), "capture");
+        const cudaError_t e = cudaGraphInstantiate(&C.sched_graph, g, 0);
+        cudaGraphDestroy(g);
+        cuda_check(e, "cudaGraphInstantiate");
+      }
+      cuda_check(cudaGraphLaunch(C.sched_graph, C.stream), "cudaGraphLaunch");
+      C.launches += C.graph_launches;
     }
   });
 }

@@ -116,8 +116,10 @@ cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepV
                              int n_host, cudaStream_t s);
 cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
                           const SchedView* sched, cudaStream_t s);
-cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* n_items,
-                         int32_t* n_select, cudaStream_t s);
+// Device scheduler: builds the step's item list and the counts [all, selecting, half A (all,
+// selecting), half B (all, selecting)] with half A = items [0, half).
+cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts, int half,
+                         cudaStream_t s);
 cudaError_t launch_sched_admit(const SlotView& sv, const SchedView& q, int window, cudaStream_t s);
 cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
                                  const float* vs, const int32_t* counts, int32_t batch,

@@ -856,8 +856,10 @@ __global__ void k_sched_admit(const SlotView sv, const SchedView q, int window) 
 
 // Builds the step's item list from the busy slots: selecting items (the last prompt token and
 // every decode step) first, then prefill items.  One CTA.
+// counts: [0] items, [1] selecting items, [2]/[3] the same for items [0, half), [4]/[5] for
+// items [half, n) -- the two micro-batches of the step.
 __global__ void __launch_bounds__(1024) k_sched(const SlotView sv, const StepView st, const SchedView q,
-                                              int32_t* n_items, int32_t* n_select) {
+                                              int32_t* counts, int half) {
   __shared__ int s_sel;
   const int tid = threadIdx.x;
   if (tid == 0) s_sel = 0;
@@ -893,14 +895,34 @@ __global__ void __launch_bounds__(1024) k_sched(const SlotView sv, const StepVie
   }
   __syncthreads();
   if (tid == 0) {
-    *n_items = c_sel + c_pre;
-    *n_select = c_sel;
+    const int n = c_sel + c_pre;
+    counts[0] = n;
+    counts[1] = c_sel;
+    counts[2] = min(n, half);
+    counts[3] = min(c_sel, half);
+    counts[4] = max(0, n - half);
+    counts[5] = max(0, c_sel - half);
   }
 }
 
 }  // namespace
 
 // ------------------------------------------------------------------ launchers
+
+// The dynamic shared-memory limit is an attribute of the function on the device, shared by every
+// context in the process, so it is raised to the device's opt-in maximum rather than to one
+// context's need (a smaller later context must not lower it under a larger one).
+static cudaError_t raise_smem_limit(const void* fn) {
+  int device = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  cudaFuncAttributes attr{};
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&attr, fn);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)attr.sharedSizeBytes);
+  return e;
+}
+
 
 cudaError_t launch_embed(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
                          cudaStream_t s) {
@@ -934,7 +956,7 @@ cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* 
                                  int32_t capacity, float* out, cudaStream_t s) {
   if (batch <= 0) return cudaSuccess;
   const size_t smem = attention_smem_bytes(capacity, false);
-  cudaError_t e = cudaFuncSetAttribute(k_attention_dev, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(k_attention_dev));
   if (e != cudaSuccess) return e;
   k_attention_dev<<<dim3(batch, kKvHeads), kAttnThreads, smem, s>>>(q, kc, ks, vc, vs, counts, capacity, out);
   return cudaGetLastError();
@@ -947,11 +969,13 @@ cudaError_t launch_route(const StepView& st, int n_host, cudaStream_t s) {
 }
 
 cudaError_t configure_step_kernels(int32_t capacity) {
-  cudaError_t e = cudaFuncSetAttribute(k_layer, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sizeof(LayerSmem));
+  if (sizeof(LayerSmem) > 200 * 1024 || attention_smem_bytes(capacity, true) > 200 * 1024)
+    return cudaErrorInvalidValue;
+  cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(k_layer));
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)attention_smem_bytes(capacity, true));
+  e = raise_smem_limit(reinterpret_cast<const void*>(k_attention));
+  if (e != cudaSuccess) return e;
+  return raise_smem_limit(reinterpret_cast<const void*>(k_attention_dev));
 }
 
 cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
@@ -968,9 +992,9 @@ cudaError_t launch_sched_admit(const SlotView& sv, const SchedView& q, int windo
   return cudaGetLastError();
 }
 
-cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* n_items,
-                         int32_t* n_select, cudaStream_t s) {
-  k_sched<<<1, 1024, 0, s>>>(sv, st, q, n_items, n_select);
+cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts, int half,
+                         cudaStream_t s) {
+  k_sched<<<1, 1024, 0, s>>>(sv, st, q, counts, half);
   return cudaGetLastError();
 }
 

@@ -236,3 +236,29 @@ extern "C" int needle_cuda_attention_dev_fast(const float* q, const int8_t* key_
   if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
   return NEEDLE_OK;
 }
+
+extern "C" int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const float* codebook, const float* x,
+                                              int32_t batch, float* y, void* stream) {
+  if (!m || !codebook || (batch > 0 && (!x || !y)))
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+  if (m->group_size != kGroup) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "CQ group size 128 only");
+  if (!cq_gemv_fast_supported(m->bits))
+    return op_fail(NEEDLE_UNSUPPORTED_CACT, "fast matvec supports record widths 2, 4 and ternary");
+  if (m->rows < 0 || m->input_size <= 0 || batch < 0) return op_fail(NEEDLE_INVALID_CACT, "bad matrix shape");
+  if ((reinterpret_cast<uintptr_t>(m->packed) & 15) != 0)
+    return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "packed rows must be 16-byte aligned");
+  if (batch == 0 || m->rows == 0) return NEEDLE_OK;
+  const int in_pad = (m->input_size + kGroup - 1) / kGroup * kGroup;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Codebook cb{};
+  for (int i = 0; i < 28; i++) cb.v[i] = codebook[i];
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  float* xp = nullptr;
+  if (e == cudaSuccess) e = scratch_for(device, size_t(batch) * in_pad, &xp);
+  if (e == cudaSuccess) e = launch_cq_prepare(x, m->input_size, m->input_size, in_pad, xp, in_pad, batch, nullptr, s);
+  if (e == cudaSuccess)
+    e = launch_cq_gemv_fast(m->packed, m->norms, m->rows, in_pad, m->bits, xp, batch, y, cb, s);
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  return NEEDLE_OK;
+}

@@ -79,6 +79,8 @@ EXPORTS = {
     "needle_cuda_row": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
     "needle_cuda_cq_matvec_dev": (C.c_int, [C.POINTER(CqMatrixDesc), C.c_void_p, C.c_void_p,
                                             C.c_int32, C.c_void_p, C.c_void_p]),
+    "needle_cuda_cq_matvec_dev_fast": (C.c_int, [C.POINTER(CqMatrixDesc), C.c_void_p, C.c_void_p,
+                                                 C.c_int32, C.c_void_p, C.c_void_p]),
     "needle_cuda_cq_matvec_dev_noalloc": (C.c_int, [C.POINTER(CqMatrixDesc), C.c_void_p, C.c_void_p,
                                                     C.c_int32, C.c_void_p, C.c_void_p]),
     "needle_cuda_attention_dev": (C.c_int, [C.c_void_p] * 6 + [C.c_int32, C.c_int32, C.c_void_p,

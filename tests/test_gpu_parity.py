@@ -329,6 +329,27 @@ def test_device_scheduler_matches_oracle(engine, oracle, ref_model):
     assert generated == int(gens.sum())
 
 
+def test_device_scheduler_two_microbatches_and_graph(torch_cuda, archive, oracle, ref_model):
+    """64+ slots: the step runs as two micro-batches on two stream pairs and, after the first
+    step, as a replayed CUDA graph; every sequence still matches the oracle."""
+    from needle_b200.backend import CudaEngine
+    rng = np.random.default_rng(8)
+    n = 90
+    prompts = [rng.integers(0, ref_model.vocab, int(k)).astype(np.int32) for k in rng.integers(1, 7, n)]
+    gens = rng.integers(1, 4, n).astype(np.int32)
+    want, processed_ref = ref_model.decode_many(prompts, gens, 8)
+    with CudaEngine(archive, device=0, max_seqs=64, max_len=64, max_sink=0) as eng:
+        eng.sched_load(64, prompts, gens)
+        for _ in range(100):
+            eng.sched_step(4)
+            tokens, generated, finished, last = eng.sched_status()
+            if finished == n:
+                break
+        assert finished == n
+        np.testing.assert_array_equal(last, want)
+        assert tokens == processed_ref and generated == int(gens.sum())
+
+
 def test_errors_follow_needle_error_codes(engine, ref_model):
     from needle_b200.backend import StepRequest
     from needle_b200.native import NeedleError
@@ -348,3 +369,29 @@ def test_errors_follow_needle_error_codes(engine, ref_model):
     with pytest.raises(NeedleError) as e:
         engine.step([StepRequest(1, 5, True, np.zeros(0, dtype=np.uint32))])
     assert e.value.code == "INVALID_CACT"
+
+
+@pytest.mark.parametrize("bits,rows,inputs,batch", [(4, 1000, 8192, 1), (2, 512, 512, 3), (5, 300, 2048, 6),
+                                                    (4, 64, 20000, 2)])
+def test_cq_matvec_dev_fast_within_tolerance(torch_cuda, oracle, bits, rows, inputs, batch):
+    """Fast numerics (binary32) vs the oracle's binary64 cqMatvec: |got - want| <= 1e-5 * sum of
+    |terms| bound, taken as 2e-6 * sqrt(inputs) * max|want| + 1e-6."""
+    torch = torch_cuda
+    from needle_b200 import native, synth
+    packed, norms = synth.random_cq_matrix(rows, inputs, bits, seed=6)
+    cb = codebook()
+    x = synth.normal(6, batch * inputs, stream=3).astype(np.float32).reshape(batch, inputs)
+    d_packed = torch.from_numpy(packed.copy()).cuda()
+    d_norms = torch.from_numpy(norms.view(np.int16).copy()).cuda()
+    d_x = torch.from_numpy(x).cuda()
+    d_y = torch.zeros(batch, rows, dtype=torch.float32, device="cuda")
+    desc = native.CqMatrixDesc(d_packed.data_ptr(), d_norms.data_ptr(), rows, inputs, 128, bits)
+    native.check(native.lib().needle_cuda_cq_matvec_dev_fast(C.byref(desc), native.ptr(cb), d_x.data_ptr(), batch,
+                                                             d_y.data_ptr(), None))
+    torch.cuda.synchronize()
+    y = d_y.cpu().numpy()
+    m = oracle.CqMatrix(rows, inputs, 128, bits, packed, norms, cb[:4], cb[4:12], cb[12:])
+    for b in range(batch):
+        want = m.matvec(x[b]).astype(np.float64)
+        tol = 2e-6 * np.sqrt(inputs) * np.max(np.abs(want)) + 1e-6
+        assert np.max(np.abs(y[b] - want)) <= tol, (b, np.max(np.abs(y[b] - want)), tol)
