@@ -233,7 +233,7 @@ def bench_qmatvec(args, peaks):
             lib = native.lib()
             modes = [("exact", lib.needle_cuda_cq_matvec_dev, 3 if (batch <= 8 and pad // 128 >= 16) else 2)]
             if bits in (2, 4, 5):
-                modes.append(("fast", lib.needle_cuda_cq_matvec_dev_fast, 1 + -(-batch // 4)))
+                modes.append(("fast", lib.needle_cuda_cq_matvec_dev_fast, -(-batch // 8)))
             for mode, fn, kernels in modes:
                 def call(i, strm, fn=fn):
                     native.check(fn(C.byref(descs[i]), native.ptr(cb), x.data_ptr(), batch, y.data_ptr(), strm))
@@ -253,7 +253,7 @@ def bench_qmatvec(args, peaks):
             "data": "synthetic", "config": {"workload": "isolated quantised matvec (BASELINE config 2), headline 8192x8192 CQ4 batch 1, "
                                    "fast numerics; exact-numerics rows alongside",
                        "l2": f"operand sets rotated over > {ROTATE_BYTES >> 20} MB", "cases": results},
-            "roofline": {"kernel": "k_cq_gemv_fast (+ k_cq_prepare)", "bound": "hbm",
+            "roofline": {"kernel": "k_cq_gemv_table", "bound": "hbm",
                          "achieved": head["gbs"], "peak": peak, "peak_source": src, "unit": "GB/s",
                          "frac": round(head["gbs"] / peak, 4), "traffic": None},
             "gpu_launches": launches}

@@ -51,11 +51,15 @@ cudaError_t launch_cq_gemv(const CqJobs& jobs, const Codebook& cb, int32_t n_hos
 bool cq_gemv_prefers_split(const CqJob& job, int32_t n);
 size_t cq_gemv_split_scratch_bytes(const CqJob& job, int32_t n);
 cudaError_t launch_cq_gemv_split(const CqJob& job, const Codebook& cb, int32_t n, double* scratch, cudaStream_t s);
-// Fast-numerics matvec (cq_fast.cu): binary32, record widths 2, 4 and ternary; x prepared.
+// Fast-numerics matvec (cq_fast.cu): binary32 table lookups, record widths 2, 4 and ternary; takes
+// the raw activation x [batch][input_size] (it prepares each group itself).  Scratch: per-group
+// partial sums (cq_gemv_fast_partial_floats); up to kFastMaxItems items per pass of two launches.
+constexpr int kFastMaxItems = 8;
 bool cq_gemv_fast_supported(int32_t bits);
-cudaError_t launch_cq_gemv_fast(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t in_pad,
-                                int32_t bits, const float* xp, int32_t batch, float* y, const Codebook& cb,
-                                cudaStream_t s);
+size_t cq_gemv_fast_partial_floats(int32_t rows, int32_t in_pad);
+cudaError_t launch_cq_gemv_fast(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
+                                int32_t bits, const float* x, int32_t batch, float* y, const Codebook& cb,
+                                float* partials, cudaStream_t s);
 cudaError_t launch_cq_rows(const uint8_t* packed, const uint16_t* norms, int32_t bits,
                            int32_t row_bytes, int32_t in_pad, int32_t input_size,
                            const int32_t* rows, int32_t n_rows, float* out, int32_t out_stride,

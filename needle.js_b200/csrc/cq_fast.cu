@@ -1,18 +1,37 @@
-// cq_fast.cu -- fast-numerics Cactus-Quant matvec (binary32 FMA, warp reductions).  Computes
-// cqMatvec (packages/needle.js/src/backends/cq.ts:233-240) like the exact kernel in cq.cu, but in
-// binary32 with a tree summation order, so results match the reference within binary32 rounding
-// instead of bit for bit.
+// cq_fast.cu -- fast-numerics Cactus-Quant matvec (binary32, table lookups).  Computes
+// cqMatvec (packages/needle.js/src/backends/cq.ts:233-240 = prepareCqActivation + cqMatvecPrepared,
+// cq.ts:30-46 and 107-231) in binary32 with its own summation order, so results match the
+// reference within binary32 rounding instead of bit for bit.  Record widths 4, 2 and ternary.
 //
-// Decomposition.  Weights are streamed once from HBM with fully coalesced 16-byte loads: a warp
-// owns a row, lane l reads the l-th, (l+32)-th, ... 16-byte chunk of it.  The rotated activation
-// (prepared per 128-group by k_cq_prepare) of up to kFastItems items sits in shared memory as
-// binary32, the 16 codebook levels in a 64-byte shared table (lanes with different indices hit
-// different banks).  Each chunk lies inside one 128-column group, so its partial dot is scaled
-// by that group's fp16 norm before it joins the lane's row sum; a butterfly shuffle finishes the
-// row.  A persistent grid walks rows; x is staged once per CTA in column tiles.
+// Why tables.  At batch 1 the matvec streams each weight byte once, so HBM sets the floor
+// (~5 us for 8192x8192 CQ4); a straightforward decode spends one codebook lookup plus one FMA per
+// weight, and the lookups alone (one shared-memory access each) cap the SM below the rate HBM
+// delivers.  The reference already works a byte at a time: for a 128-column group its inner step
+// adds lut[byte] . x[pair or quad] (cq.ts:146-152, 170-175, 192-197).  With x fixed per call that
+// whole term depends on the byte alone, so each CTA builds, for one group, the table
+//     T[b][j] = sum_i level(code_i(b)) * x'[j * codes_per_byte + i]      (b < 256)
+// (64 KB: 64 pairs for CQ4, 32 quads for CQ2 / ternary), and a byte of weights then costs one
+// table read and one add -- half or a quarter of a lookup per weight.
+//
+// Work: the (group, block of 32 rows) pairs in group-major order, a contiguous range per CTA, so a
+// CTA rebuilds its table only where its range crosses a group.  Each warp keeps its next block of
+// weights in flight in registers (the first one is issued before the table is built).  The group's activation slice is
+// prepared in the CTA (zero padding, FWHT in binary32 butterflies, scale by 1/sqrt(128) in
+// binary64 -- the same values k_cq_prepare produces), so a call is one launch.
+//
+// Lookup phase: one lane per row, streaming the row's 64 (CQ4) or 32 (CQ2) bytes of the group as
+// 16-byte loads (fully used sectors).  Table rows are 64 floats apart, so the bank of T[b][j] is
+// j mod 32 whatever b is; lanes walk their chunks and bytes from lane-specific starting points,
+// which makes the 32 lanes of every step read 32 different j -- no bank conflicts for any weights.
+//
+// Reduction: each block writes the group dot per (group, row) to scratch, and k_cq_fast_reduce --
+// a programmatic dependent launch, so its launch overlaps the GEMV's tail -- sums norm * dot over
+// the groups of every row in a fixed order; the result does not depend on scheduling.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "cq.cuh"
 
@@ -20,132 +39,336 @@ namespace needle {
 
 namespace {
 
-constexpr int kFastThreads = 256;  // 8 warps
-constexpr int kFastItems = 4;      // items per launch pass
-constexpr int kTileCols = 8192;    // columns of x staged per pass (kFastItems x 32 KB)
+constexpr int kTabThreads = 256;                 // 8 warps, two CTAs per SM
+constexpr int kTabStride = 64;                   // floats per table byte-row
+constexpr int kTabFloats = 256 * kTabStride;     // 64 KB
 
 template <int BITS>
-struct FastChunk {
-  // columns covered by one 16-byte chunk
-  static constexpr int cols = BITS == 4 ? 32 : BITS == 3 ? 0 : 64;
+struct TabGeom {
+  static constexpr int codes_per_byte = BITS == 4 ? 2 : 4;
+  static constexpr int group_bytes = kGroup / codes_per_byte;    // 64 or 32
+  static constexpr int chunks = group_bytes / 16;                // 16-byte chunks per group row: 4 or 2
 };
 
-// Levels of 16 codes packed in `w` (CQ4: 8 per word, 2 words -> 16 levels).
-template <int BITS>
-__device__ __forceinline__ float level_of(uint32_t word, int k, const float* lut) {
-  if constexpr (BITS == 4) return lut[(word >> (4 * k)) & 15];
-  else return lut[(word >> (2 * k)) & 3];
+// x' of one group: zero padding, FWHT (binary32 butterflies, strides 1, 2, 4, ...), times
+// 1/sqrt(128) in binary64 rounded to binary32 (prepareCqActivation, cq.ts:30-46).  Every warp
+// computes it (four values per lane: lane l holds x'[4l .. 4l+3]), so no barrier is needed.
+__device__ __forceinline__ void prepare_group(const float* __restrict__ x, int input_size, int g, float v[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int col = g * kGroup + 4 * lane + k;
+    v[k] = col < input_size ? __ldg(x + col) : 0.0f;
+  }
+  // strides 1 and 2 inside the lane
+  {
+    const float a0 = __fadd_rn(v[0], v[1]), a1 = __fsub_rn(v[0], v[1]);
+    const float a2 = __fadd_rn(v[2], v[3]), a3 = __fsub_rn(v[2], v[3]);
+    v[0] = __fadd_rn(a0, a2);
+    v[2] = __fsub_rn(a0, a2);
+    v[1] = __fadd_rn(a1, a3);
+    v[3] = __fsub_rn(a1, a3);
+  }
+  // strides 4 .. 64 across lanes
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[k], m);
+      v[k] = (lane & m) ? __fsub_rn(other, v[k]) : __fadd_rn(v[k], other);
+    }
+  }
+  const double inverse_root = 1.0 / sqrt((double)kGroup);
+#pragma unroll
+  for (int k = 0; k < 4; k++) v[k] = f32((double)v[k] * inverse_root);
 }
 
 template <int BITS>
-__global__ void __launch_bounds__(kFastThreads) k_cq_gemv_fast(const uint8_t* __restrict__ packed,
-                                                               const uint16_t* __restrict__ norms, int32_t rows,
-                                                               int32_t in_pad, int32_t row_bytes,
-                                                               const float* __restrict__ xp, int32_t nb,
-                                                               float* __restrict__ y, Codebook cb) {
-  extern __shared__ __align__(16) float xs[];  // [kFastItems][tile]
+__device__ __forceinline__ void build_table(const float v[4], const float* __restrict__ lut, float* __restrict__ T) {
+  const int t = threadIdx.x;
+  static_assert(kTabThreads == 256, "table build assumes 256 threads");
+  if constexpr (BITS == 4) {
+    const int j = t & 63, lo_blk = t >> 6;  // pair j; low nibbles 4 lo_blk .. 4 lo_blk + 3
+    // x'[2j] and x'[2j+1] live in lane j / 2 (elements 0, 1 or 2, 3)
+    const int src = j >> 1;
+    const float e0 = __shfl_sync(0xffffffffu, v[0], src), e1 = __shfl_sync(0xffffffffu, v[1], src);
+    const float e2 = __shfl_sync(0xffffffffu, v[2], src), e3 = __shfl_sync(0xffffffffu, v[3], src);
+    const float x0 = (j & 1) ? e2 : e0, x1 = (j & 1) ? e3 : e1;
+    float p0[4], p1[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) p0[k] = lut[4 * lo_blk + k] * x0;
+#pragma unroll
+    for (int h = 0; h < 16; h++) p1[h] = lut[h] * x1;
+    float* base = T + (4 * lo_blk) * kTabStride + j;
+#pragma unroll
+    for (int h = 0; h < 16; h++)
+#pragma unroll
+      for (int k = 0; k < 4; k++) base[(h * 16 + k) * kTabStride] = p0[k] + p1[h];
+  } else {
+    const int j = t & 31, hb = t >> 5;  // quad j = this lane; bytes 32 hb .. 32 hb + 31
+    const float x0 = v[0], x1 = v[1], x2 = v[2], x3 = v[3];
+    float p0[4], p1[4];
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      p0[c] = lut[c] * x0;
+      p1[c] = lut[c] * x1;
+    }
+    const float s3 = lut[hb >> 1] * x3;                     // code of bits 6-7 = hb >> 1
+    const float s23a = lut[(2 * hb) & 3] * x2 + s3;         // bits 4-5 for k < 16
+    const float s23b = lut[(2 * hb + 1) & 3] * x2 + s3;     // and for k >= 16
+    float* base = T + (32 * hb) * kTabStride + j;
+#pragma unroll
+    for (int k = 0; k < 32; k++) base[k * kTabStride] = (p0[k & 3] + p1[(k >> 2) & 3]) + (k < 16 ? s23a : s23b);
+  }
+}
+
+// Rotates the 16 bytes of c so that byte s of the result is byte (s + rot) & 15 of c
+// (selects and funnel shifts, no branches).
+__device__ __forceinline__ void rotate16(const uint4 c, int rot, uint32_t o[4]) {
+  const bool r1 = rot & 4, r2 = rot & 8;
+  const uint32_t b0 = r1 ? c.y : c.x, b1 = r1 ? c.z : c.y, b2 = r1 ? c.w : c.z, b3 = r1 ? c.x : c.w;
+  const uint32_t a0 = r2 ? b2 : b0, a1 = r2 ? b3 : b1, a2 = r2 ? b0 : b2, a3 = r2 ? b1 : b3;
+  const uint32_t sh = 8u * (rot & 3);
+  o[0] = __funnelshift_r(a0, a1, sh);
+  o[1] = __funnelshift_r(a1, a2, sh);
+  o[2] = __funnelshift_r(a2, a3, sh);
+  o[3] = __funnelshift_r(a3, a0, sh);
+}
+
+// Sum of T over the 16 bytes of a rotated chunk.  pk packs the 16 byte-row offsets of the steps,
+// three per word (the fourth byte is zero); one byte permute per step builds byte * 256 + offset.
+__device__ __forceinline__ float lookup16(const char* __restrict__ Tc, const uint32_t o[4], const uint32_t pk[6]) {
+  // two packed binary32 pairs (add.rn.f32x2) accumulate steps s and s + 1
+  unsigned long long acc[2] = {0ull, 0ull};
+#pragma unroll
+  for (int s = 0; s < 16; s += 2) {
+    float v[2];
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+      const int st = s + e;
+      // bytes of the offset: [offset of step st, weight byte st, 0, 0]
+      const uint32_t sel = 0x7700u | ((uint32_t)(st & 3) << 4) | (4u + (uint32_t)(st % 3));
+      const uint32_t at = __byte_perm(o[st >> 2], pk[st / 3], sel);
+      v[e] = *reinterpret_cast<const float*>(Tc + at);
+    }
+    unsigned long long pair;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(pair) : "f"(v[0]), "f"(v[1]));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(acc[(s >> 1) & 1]) : "l"(acc[(s >> 1) & 1]), "l"(pair));
+  }
+  unsigned long long t;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(acc[0]), "l"(acc[1]));
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(t));
+  return lo + hi;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kTabThreads, 2) k_cq_gemv_table(
+    const uint8_t* __restrict__ packed, int32_t rows, int32_t input_size, int32_t in_pad, int32_t row_bytes,
+    const float* __restrict__ x, int32_t x_stride, Codebook cb, float* __restrict__ partials) {
+  using G = TabGeom<BITS>;
+  constexpr int NCH = G::chunks;
+  constexpr int kWarps = kTabThreads / 32;
+  extern __shared__ __align__(16) float T[];  // kTabFloats
   __shared__ float lut[16];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int item = blockIdx.y;
+  const int groups = in_pad / kGroup;
+  const int nblk = (rows + 31) / 32;  // 32-row blocks per group
+  const int64_t total = (int64_t)groups * nblk;
+  const int64_t b_begin = total * blockIdx.x / gridDim.x, b_end = total * (blockIdx.x + 1) / gridDim.x;
+  x += (int64_t)item * x_stride;
+  float* part = partials + (int64_t)item * groups * rows;
   if (tid < 16) {
     float v = 0.0f;
-    if (BITS == kTernaryBits) {
-      const float coefficient = (float)(kTernaryCentroid / sqrt((double)kGroup));
-      v = (tid == 1) ? coefficient : (tid == 3) ? -coefficient : 0.0f;
-    } else if (tid < (1 << BITS)) {
-      v = cb.v[(BITS == 2 ? 0 : 12) + tid];
+    if constexpr (BITS == 4) {
+#pragma unroll
+      for (int k = 0; k < 16; k++) v = tid == k ? cb.v[12 + k] : v;  // static indices: cb stays in param space
+    } else if constexpr (BITS == 2) {
+#pragma unroll
+      for (int k = 0; k < 4; k++) v = tid == k ? cb.v[k] : v;
+    } else {
+      const float c = f32(kTernaryCentroid / sqrt((double)kGroup));
+      v = tid == 1 ? c : tid == 3 ? -c : 0.0f;
     }
     lut[tid] = v;
   }
-  constexpr int kCols = FastChunk<BITS>::cols;  // columns per 16-byte chunk
-  const int groups = in_pad / kGroup;
-  const int warps_total = gridDim.x * (kFastThreads / 32);
-  for (int c0 = 0; c0 < in_pad; c0 += kTileCols) {
-    const int tile = min(kTileCols, in_pad - c0);
-    __syncthreads();
-    for (int i = tid; i < nb * tile; i += kFastThreads) {
-      const int b = i / tile, c = i - b * tile;
-      xs[b * kTileCols + c] = xp[(int64_t)b * in_pad + c0 + c];
+
+  // The dependent reduction may be scheduled at once: its griddepcontrol.wait still waits for this
+  // whole grid to complete, and this grid is a single wave, so its CTAs only take spare slots.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  // Lane geometry (constant for the kernel).  Lane i owns row i of a 32-row block: its NCH 16-byte
+  // chunks of the group, walked in the order (i + p) mod NCH, each starting at byte rot = i / 2.
+  // The bank of T[b][j] is j mod 32 = 16 (chunk & 1) + position; at every step the lanes of either
+  // chunk parity hold the 16 distinct rotations, so the 32 lanes read 32 distinct banks.
+  const int rot = lane >> 1;
+  uint32_t pk[NCH][6];  // packed byte-row offsets (three per word) of every phase and step
+#pragma unroll
+  for (int ph = 0; ph < NCH; ph++)
+#pragma unroll
+    for (int m = 0; m < 6; m++) {
+      uint32_t w = 0;
+#pragma unroll
+      for (int e = 0; e < 3; e++) {
+        const int st = 3 * m + e;
+        if (st < 16) w |= (uint32_t)(16 * ((lane + ph) % NCH) + ((st + rot) & 15)) * 4u << (8 * e);
+      }
+      pk[ph][m] = w;
     }
+  const char* Tc = reinterpret_cast<const char*>(T);
+
+  // The CTA's blocks [b_begin, b_end) in group-major order, one segment per group.
+  for (int64_t seg = b_begin; seg < b_end;) {
+    const int g = (int)(seg / nblk);
+    const int64_t seg_end = min(b_end, (int64_t)(g + 1) * nblk);
+    const int rb0 = (int)(seg - (int64_t)g * nblk), nseg = (int)(seg_end - seg);
+    const uint8_t* gbase = packed + g * G::group_bytes;
+    // this lane's chunks of block k in walking order; the last block's missing rows read row
+    // rows - 1 (in bounds, never stored)
+    auto load = [&](int k, uint4* c) {
+      const int row = min((rb0 + k) * 32 + lane, rows - 1);
+      const uint4* src = reinterpret_cast<const uint4*>(gbase + (int64_t)row * row_bytes);
+#pragma unroll
+      for (int ph = 0; ph < NCH; ph++) c[ph] = __ldg(src + (lane + ph) % NCH);
+    };
+    auto process = [&](int k, const uint4* c) {
+      float sum = 0.0f;
+#pragma unroll
+      for (int ph = 0; ph < NCH; ph++) {
+        uint32_t o[4];
+        rotate16(c[ph], rot, o);
+        sum += lookup16(Tc, o, pk[ph]);
+      }
+      const int row = (rb0 + k) * 32 + lane;
+      if (row < rows) part[(int64_t)g * rows + row] = sum;
+    };
+    uint4 A[NCH], B[NCH];
+    int k = warp;
+    if (k < nseg) load(k, A);  // in flight during the table build
+    float xv[4];
+    prepare_group(x, input_size, g, xv);
+    __syncthreads();  // every warp is done with the previous table (and lut is written)
+    build_table<BITS>(xv, lut, T);
     __syncthreads();
-    const int chunks = tile / kCols;          // 16-byte chunks of this tile in a row
-    for (int row = blockIdx.x * (kFastThreads / 32) + warp; row < rows; row += warps_total) {
-      const uint4* src = reinterpret_cast<const uint4*>(packed + (int64_t)row * row_bytes + c0 / kCols * 16);
-      float acc[kFastItems] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 4
-      for (int ch = lane; ch < chunks; ch += 32) {
-        const uint4 u = __ldg(src + ch);
-        const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-        const int col = ch * kCols;  // within the tile
-        const float nrm = __half2float(__ushort_as_half(__ldg(norms + (int64_t)row * groups + (c0 + col) / kGroup)));
-        float part[kFastItems] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          constexpr int per_word = BITS == 4 ? 8 : 16;
-#pragma unroll
-          for (int k = 0; k < per_word; k++) {
-            const float a = level_of<BITS>(wv[q], k, lut);
-            const int c = col + q * per_word + k;
-#pragma unroll
-            for (int b = 0; b < kFastItems; b++)
-              if (b < nb) part[b] = fmaf(a, xs[b * kTileCols + c], part[b]);
-          }
-        }
-#pragma unroll
-        for (int b = 0; b < kFastItems; b++) acc[b] = fmaf(nrm, part[b], acc[b]);
-      }
-#pragma unroll
-      for (int b = 0; b < kFastItems; b++) {
-        float v = acc[b];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        acc[b] = v;
-      }
-      if (lane == 0) {
-        for (int b = 0; b < nb; b++) {
-          float* dst = y + (int64_t)b * rows + row;
-          *dst = c0 == 0 ? acc[b] : *dst + acc[b];
-        }
-      }
+    // two register buffers in turn: the next block is in flight while one is looked up
+    while (k < nseg) {
+      if (k + kWarps < nseg) load(k + kWarps, B);
+      process(k, A);
+      k += kWarps;
+      if (k >= nseg) break;
+      if (k + kWarps < nseg) load(k + kWarps, A);
+      process(k, B);
+      k += kWarps;
     }
+    seg = seg_end;
   }
+}
+
+// Row totals: y[row] = sum_g norm16[row][g] * partials[g][row], groups in a fixed order (four
+// interleaved chains combined in a fixed order).  Launched as a programmatic dependent of
+// k_cq_gemv_table: it is scheduled while that grid drains and waits for its completion before
+// reading.
+constexpr int kReduceRows = 64;
+constexpr int kReduceThreads = 256;
+__global__ void __launch_bounds__(kReduceThreads) k_cq_fast_reduce(const float* __restrict__ partials,
+                                                                   const uint16_t* __restrict__ norms, int32_t rows,
+                                                                   int32_t groups, float* __restrict__ y,
+                                                                   int32_t y_stride) {
+  __shared__ float red[kReduceThreads];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  constexpr int kSub = kReduceThreads / kReduceRows;
+  const int tid = threadIdx.x, item = blockIdx.y;
+  const int r = blockIdx.x * kReduceRows + (tid % kReduceRows), sub = tid / kReduceRows;
+  const float* part = partials + (int64_t)item * groups * rows;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (r < rows) {
+    const uint16_t* nr = norms + (int64_t)r * groups;
+    int gg = sub, k = 0;
+#pragma unroll 4
+    for (; gg < groups; gg += kSub, k++)
+      acc[k & 3] += __half2float(__ushort_as_half(__ldg(nr + gg))) * __ldcg(part + (int64_t)gg * rows + r);
+  }
+  red[tid] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  __syncthreads();
+  if (sub == 0 && r < rows) {
+    float v = red[tid];
+#pragma unroll
+    for (int k = 1; k < kSub; k++) v += red[tid + k * kReduceRows];
+    y[(int64_t)item * y_stride + r] = v;
+  }
+}
+
+template <int BITS>
+cudaError_t launch_table(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
+                         int32_t in_pad, const float* x, int32_t batch, float* y, const Codebook& cb,
+                         float* partials, cudaStream_t s) {
+  static std::atomic<uint64_t> configured{0};
+  static int per_sm[64] = {0};
+  int device = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return e;
+  const size_t smem = sizeof(float) * kTabFloats;
+  const uint64_t bit = 1ull << (device & 63);
+  if (!(configured.load() & bit)) {
+    e = cudaFuncSetAttribute(k_cq_gemv_table<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int n = 1;
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_cq_gemv_table<BITS>, kTabThreads, smem);
+    if (e != cudaSuccess) return e;
+    per_sm[device & 63] = std::max(1, n);
+    configured.fetch_or(bit);
+  }
+  const int groups = in_pad / kGroup;
+  const int64_t total = (int64_t)groups * ((rows + 31) / 32);
+  const int pb = BITS == kTernaryBits ? 2 : BITS;
+  const int row_bytes = in_pad * pb / 8;
+  for (int b0 = 0; b0 < batch; b0 += kFastMaxItems) {
+    const int nb = std::min(kFastMaxItems, batch - b0);
+    const int slots = sms * per_sm[device & 63];
+    // one wave of CTAs over the items of the pass; at least one CTA per group (one table build
+    // each) and, beyond that, at least one block per warp
+    const int64_t want = std::max<int64_t>(groups, (total + kTabThreads / 32 - 1) / (kTabThreads / 32));
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>({total, want, (int64_t)std::max(1, slots / nb)}));
+    float* yb = y + (int64_t)b0 * rows;
+    k_cq_gemv_table<BITS><<<dim3(grid, nb), kTabThreads, smem, s>>>(
+        packed, rows, input_size, in_pad, row_bytes, x + (int64_t)b0 * input_size, input_size, cb, partials);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((rows + kReduceRows - 1) / kReduceRows, nb);
+    cfg.blockDim = dim3(kReduceThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, k_cq_fast_reduce, (const float*)partials, norms, rows, groups, yb, rows);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace
 
 bool cq_gemv_fast_supported(int32_t bits) { return bits == 2 || bits == 4 || bits == kTernaryBits; }
 
-cudaError_t launch_cq_gemv_fast(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t in_pad,
-                                int32_t bits, const float* xp, int32_t batch, float* y, const Codebook& cb,
-                                cudaStream_t s) {
+size_t cq_gemv_fast_partial_floats(int32_t rows, int32_t in_pad) {
+  return (size_t)kFastMaxItems * (in_pad / kGroup) * rows;
+}
+
+cudaError_t launch_cq_gemv_fast(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
+                                int32_t bits, const float* x, int32_t batch, float* y, const Codebook& cb,
+                                float* partials, cudaStream_t s) {
   if (batch <= 0 || rows <= 0) return cudaSuccess;
-  const int pb = bits == kTernaryBits ? 2 : bits;
-  const int row_bytes = in_pad * pb / 8;
-  int device = 0, sms = 0;
-  cudaGetDevice(&device);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  for (int b0 = 0; b0 < batch; b0 += kFastItems) {
-    const int nb = std::min(kFastItems, batch - b0);
-    // x of nb items: shared memory sized to the pass, so batch-1 calls keep many CTAs per SM
-    const size_t smem = sizeof(float) * kTileCols * nb;
-    const float* xb = xp + (int64_t)b0 * in_pad;
-    float* yb = y + (int64_t)b0 * rows;
-    cudaError_t e = cudaSuccess;
-    int per_sm = 1;
-    auto run = [&](auto kernel) {
-      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sizeof(float) * kTileCols * kFastItems));
-      if (e != cudaSuccess) return;
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kFastThreads, smem);
-      const int grid = std::max(1, std::min((rows + 7) / 8, sms * std::max(1, per_sm)));
-      kernel<<<grid, kFastThreads, smem, s>>>(packed, norms, rows, in_pad, row_bytes, xb, nb, yb, cb);
-      e = cudaGetLastError();
-    };
-    if (bits == 4) run(k_cq_gemv_fast<4>);
-    else if (bits == 2) run(k_cq_gemv_fast<2>);
-    else if (bits == kTernaryBits) run(k_cq_gemv_fast<kTernaryBits>);
-    else return cudaErrorInvalidValue;
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  const int in_pad = (input_size + kGroup - 1) / kGroup * kGroup;
+  if (bits == 4) return launch_table<4>(packed, norms, rows, input_size, in_pad, x, batch, y, cb, partials, s);
+  if (bits == 2) return launch_table<2>(packed, norms, rows, input_size, in_pad, x, batch, y, cb, partials, s);
+  if (bits == kTernaryBits)
+    return launch_table<kTernaryBits>(packed, norms, rows, input_size, in_pad, x, batch, y, cb, partials, s);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace needle

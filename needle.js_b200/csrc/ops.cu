@@ -254,11 +254,10 @@ extern "C" int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const f
   for (int i = 0; i < 28; i++) cb.v[i] = codebook[i];
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
-  float* xp = nullptr;
-  if (e == cudaSuccess) e = scratch_for(device, size_t(batch) * in_pad, &xp);
-  if (e == cudaSuccess) e = launch_cq_prepare(x, m->input_size, m->input_size, in_pad, xp, in_pad, batch, nullptr, s);
+  float* partials = nullptr;
+  if (e == cudaSuccess) e = scratch_for(device, cq_gemv_fast_partial_floats(m->rows, in_pad), &partials);
   if (e == cudaSuccess)
-    e = launch_cq_gemv_fast(m->packed, m->norms, m->rows, in_pad, m->bits, xp, batch, y, cb, s);
+    e = launch_cq_gemv_fast(m->packed, m->norms, m->rows, m->input_size, m->bits, x, batch, y, cb, partials, s);
   if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
   return NEEDLE_OK;
 }

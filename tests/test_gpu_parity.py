@@ -101,14 +101,16 @@ def test_cq_matvec_dev_long_rows_small_batch_bit_exact(torch_cuda, oracle, bits,
         np.testing.assert_array_equal(y[b], m.matvec(x[b]), err_msg=f"batch item {b}")
 
 
-def test_attention_dev_fast_within_tolerance(torch_cuda, oracle):
+@pytest.mark.parametrize("cap", [8192, 8190])
+def test_attention_dev_fast_within_tolerance(torch_cuda, oracle, cap):
     """Fast numerics (binary32, online softmax, split positions) vs the oracle's binary64 attention:
-    every output within 2e-4 of the largest output magnitude, including an 8192-position row."""
+    every output within 2e-4 of the largest output magnitude, including a full 8192-position row.
+    A capacity that is a multiple of 4 takes the bulk-copy pipelined kernel, 8190 the direct-load one."""
     torch = torch_cuda
     from needle_b200 import native
     rng = np.random.default_rng(31)
-    batch, cap = 5, 8192
-    counts = np.array([1, 7, 1000, 1025, 8192], dtype=np.int32)
+    batch = 5
+    counts = np.array([1, 7, 1000, 1025, cap], dtype=np.int32)
     q = rng.standard_normal((batch, 512)).astype(np.float32)
     kc = rng.integers(-127, 128, (batch, 4, cap, 64)).astype(np.int8)
     vc = rng.integers(-127, 128, (batch, 4, cap, 64)).astype(np.int8)
@@ -372,7 +374,8 @@ def test_errors_follow_needle_error_codes(engine, ref_model):
 
 
 @pytest.mark.parametrize("bits,rows,inputs,batch", [(4, 1000, 8192, 1), (2, 512, 512, 3), (5, 300, 2048, 6),
-                                                    (4, 64, 20000, 2)])
+                                                    (4, 64, 20000, 2), (4, 700, 1000, 10), (2, 1500, 8192, 1),
+                                                    (4, 8192, 16384, 8)])
 def test_cq_matvec_dev_fast_within_tolerance(torch_cuda, oracle, bits, rows, inputs, batch):
     """Fast numerics (binary32) vs the oracle's binary64 cqMatvec: |got - want| <= 1e-5 * sum of
     |terms| bound, taken as 2e-6 * sqrt(inputs) * max|want| + 1e-6."""
