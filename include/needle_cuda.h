@@ -44,6 +44,7 @@ typedef enum needle_status {
 enum {
   NEEDLE_NUMERICS_EXACT = 0, /* binary64 in reference order: bit-faithful to the CPU backend */
   NEEDLE_KV_INT8 = 0,        /* RuntimeOptions.kvCache "int8" (runtime.ts:30-32) */
+  NEEDLE_KV_FLOAT32 = 1      /* RuntimeOptions.kvCache "float32": keys / values stored as given */
 };
 
 typedef struct needle_opts {
@@ -52,7 +53,7 @@ typedef struct needle_opts {
   int32_t max_seqs;     /* sequence slots (concurrent sequences) */
   int32_t max_len;      /* largest maximumLength a slot accepts (<= geometry max sequence) */
   int32_t max_sink;     /* largest sinkLength a slot accepts */
-  int32_t kv_mode;      /* NEEDLE_KV_INT8 */
+  int32_t kv_mode;      /* NEEDLE_KV_INT8 or NEEDLE_KV_FLOAT32, for every slot of the context */
   int32_t numerics;     /* NEEDLE_NUMERICS_EXACT */
   int32_t reserved[9];
 } needle_opts;
@@ -114,6 +115,17 @@ int needle_cuda_geometry(const needle_ctx* ctx, needle_geometry* out);
  * the context's KV capacity. */
 int needle_cuda_seq_reset(needle_ctx* ctx, int32_t seq, int32_t maximum_length, int32_t sink_length);
 
+/* needle_cuda_seq_reset with RuntimeOptions.collectConfidence (runtime.ts:36, 171-180): when
+ * collect_confidence is 1 and the archive has a confidence probe head, the slot keeps the online
+ * probe pool (OnlineProbePool, runtime.ts:48-105) over the scaled embedding and every layer's
+ * hidden state.  needle_cuda_seq_reset(ctx, s, m, k) is needle_cuda_seq_reset_ex(ctx, s, m, k, 0). */
+int needle_cuda_seq_reset_ex(needle_ctx* ctx, int32_t seq, int32_t maximum_length, int32_t sink_length,
+                             int32_t collect_confidence);
+
+/* NeedleRuntime.confidence (runtime.ts:634-645): sigmoid of the confidence head over the pooled
+ * probes, or NaN through *value when the slot does not collect or the archive has no head. */
+int needle_cuda_confidence(const needle_ctx* ctx, int32_t seq, double* value);
+
 /* Position (tokens consumed) of a slot. */
 int needle_cuda_seq_position(const needle_ctx* ctx, int32_t seq, int32_t* position);
 
@@ -137,6 +149,12 @@ int needle_cuda_prefill(needle_ctx* ctx, int32_t seq, const int32_t* ids, int32_
 int needle_cuda_read_kv(const needle_ctx* ctx, int32_t seq, int32_t layer, int8_t* key_codes,
                         int8_t* value_codes, float* key_scales, float* value_scales,
                         int32_t* kv_allocation);
+
+/* Copies one layer of a slot's float32 KV cache (contexts opened with NEEDLE_KV_FLOAT32): keys and
+ * values [kv_heads][kv_allocation][head_dim].  Either pointer may be NULL.  needle_cuda_read_kv
+ * fails with INVALID_CACT on such a context, and this call on an int8 one. */
+int needle_cuda_read_kv_f32(const needle_ctx* ctx, int32_t seq, int32_t layer, float* keys, float* values,
+                            int32_t* kv_allocation);
 
 /* Reads a slot's mHC lane state x (lanes * model_dimension floats) after its last step. */
 int needle_cuda_read_lanes(const needle_ctx* ctx, int32_t seq, float* lanes);

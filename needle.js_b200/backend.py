@@ -39,9 +39,13 @@ class CudaEngine:
     """One engine context on one GPU (needle_cuda_open .. needle_cuda_close)."""
 
     def __init__(self, archive: bytes, device: int = 0, max_seqs: int = 1, max_len: int = 2048,
-                 max_sink: int = 160):
+                 max_sink: int = 160, kv_cache: str = "int8"):
+        if kv_cache not in ("int8", "float32"):
+            raise NeedleError("BACKEND_UNAVAILABLE", f"unknown kvCache {kv_cache!r}")
         self._archive = np.frombuffer(archive, dtype=np.uint8)
-        opts = native.default_opts(device=device, max_seqs=max_seqs, max_len=max_len, max_sink=max_sink)
+        opts = native.default_opts(device=device, max_seqs=max_seqs, max_len=max_len, max_sink=max_sink,
+                                   kv_mode=native.KV_FLOAT32 if kv_cache == "float32" else native.KV_INT8)
+        self.kv_cache = kv_cache
         h = C.c_void_p()
         check(lib().needle_cuda_open(ptr(self._archive), self._archive.size, C.byref(opts), C.byref(h)))
         self.h = h
@@ -73,8 +77,22 @@ class CudaEngine:
     def stream(self) -> int:
         return lib().needle_cuda_stream(self.h) or 0
 
-    def reset(self, seq: int, maximum_length: int, sink_length: int = 0):
-        check(lib().needle_cuda_seq_reset(self.h, seq, maximum_length, sink_length))
+    def reset(self, seq: int, maximum_length: int, sink_length: int = 0, collect_confidence: bool = False):
+        check(lib().needle_cuda_seq_reset_ex(self.h, seq, maximum_length, sink_length, int(collect_confidence)))
+
+    def confidence(self, seq: int) -> float:
+        v = C.c_double()
+        check(lib().needle_cuda_confidence(self.h, seq, C.byref(v)))
+        return v.value
+
+    def read_kv_f32(self, seq: int, layer: int):
+        alloc = C.c_int32()
+        check(lib().needle_cuda_read_kv_f32(self.h, seq, layer, None, None, C.byref(alloc)))
+        hk, hd = self.geometry.kv_heads, self.geometry.head_dimension
+        k = np.zeros((hk, alloc.value, hd), dtype=np.float32)
+        v = np.zeros((hk, alloc.value, hd), dtype=np.float32)
+        check(lib().needle_cuda_read_kv_f32(self.h, seq, layer, ptr(k), ptr(v), None))
+        return k, v
 
     def position(self, seq: int) -> int:
         p = C.c_int32()
@@ -191,9 +209,10 @@ class CudaBackend:
     name = "CUDA sm_100a (B200)"
 
     def __init__(self, archive: bytes, device: int = 0, max_seqs: int = 1, max_len: int = 2048,
-                 max_sink: int = 160):
+                 max_sink: int = 160, kv_cache: str = "int8"):
         self.weights = archive
-        self.engine = CudaEngine(archive, device=device, max_seqs=max_seqs, max_len=max_len, max_sink=max_sink)
+        self.engine = CudaEngine(archive, device=device, max_seqs=max_seqs, max_len=max_len, max_sink=max_sink,
+                                 kv_cache=kv_cache)
         self._free = list(range(max_seqs))
 
     def matvec(self, tensor: int, input, range: Optional[dict] = None):
@@ -246,10 +265,14 @@ class CudaResidentSession:
 
     def reset(self, maximum_length: int, sink_length: int = 0, kv_cache: str = "int8",
               collect_confidence: bool = False) -> bool:
-        if kv_cache != "int8":
-            raise NeedleError("BACKEND_UNAVAILABLE", "the CUDA backend implements the int8 KV cache")
-        self.engine.reset(self.slot, maximum_length, sink_length)
+        if kv_cache != self.engine.kv_cache:
+            raise NeedleError("BACKEND_UNAVAILABLE",
+                              f"this CUDA backend context holds a {self.engine.kv_cache} KV cache")
+        self.engine.reset(self.slot, maximum_length, sink_length, collect_confidence)
         return True
+
+    def resident_confidence(self) -> float:
+        return self.engine.confidence(self.slot)
 
     def dispose(self):
         self.backend._free.append(self.slot)
@@ -273,9 +296,14 @@ class NeedleRuntime:
     def maximum_length(self) -> int:
         return self._max
 
-    def reset(self, maximum_length: int, sink_length: int = 0):
-        self.session.reset(maximum_length, sink_length)
+    def reset(self, maximum_length: int, sink_length: int = 0, kv_cache: str = "int8",
+              collect_confidence: bool = False):
+        self.session.reset(maximum_length, sink_length, kv_cache, collect_confidence)
         self._max = maximum_length
+
+    def confidence(self) -> float:
+        """NeedleRuntime.confidence (runtime.ts:634-645): NaN unless collecting."""
+        return self.session.resident_confidence()
 
     def prefill(self, tokens) -> np.ndarray:
         if len(tokens) == 0:

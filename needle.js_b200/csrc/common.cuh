@@ -158,4 +158,7 @@ __device__ __forceinline__ double int_to_double_exact(int v) {
   return __longlong_as_double(0x4338000000000000LL + (long long)v) - 6755399441055744.0;
 }
 
+// v rounded to binary32 (ties to even) and widened back: the value of (double)f32(v).
+__device__ __forceinline__ double round32_cvt(double v) { return (double)__double2float_rn(v); }
+
 }  // namespace needle

@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <limits>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -203,6 +204,9 @@ struct Roles {
   };
   std::vector<E> sites;
   int final_norm;
+  // confidence probe head (manifest code 2): probes, projection, bias; -1 when absent
+  int conf_probes = -1, conf_proj = -1, conf_bias = -1;
+  int64_t conf_count = 0, conf_out = 0;
 };
 
 Roles assign_roles(const Archive& A) {
@@ -255,15 +259,53 @@ Roles assign_roles(const Archive& A) {
     R.sites.push_back(e);
   }
   R.final_norm = take(1, "final norm");
+  // Optional probe-head manifest (cact.ts:537-556): a dense list of codes, 1 contrastive, 2
+  // confidence, each followed by its probes, projection and bias.
+  const int64_t D = A.hdr[6];
+  if (cur < A.rec.size() && (A.rec[cur].dtype == 1 || A.rec[cur].dtype == 2)) {
+    const std::vector<float> manifest = A.dense(int(cur++));
+    for (float raw : manifest) {
+      const double code = std::floor(double(raw) + 0.5);  // Math.round
+      require(code == 1 || code == 2, NEEDLE_UNSUPPORTED_CACT,
+              "Unknown probe-head manifest code " + std::to_string(int64_t(code)));
+      const std::string name = code == 1 ? "contrastive" : "confidence";
+      const int probes = take(1, name + " probes"), proj = take(1, name + " projection"),
+                bias = take(1, name + " bias");
+      auto count_of = [&](int i) {
+        int64_t c = 1;
+        for (int d = 0; d < A.rec[i].rank; d++) c *= A.rec[i].shape[d];
+        return c;
+      };
+      const int64_t n_probes = A.rec[probes].rank > 0 ? A.rec[probes].shape[0] : 0;
+      const int64_t n_out = A.rec[proj].rank > 0 ? A.rec[proj].shape[0] : count_of(bias);
+      require(n_probes > 0 && count_of(probes) == n_probes * D, NEEDLE_INVALID_CACT,
+              name + " probe shape is inconsistent");
+      require(count_of(proj) == n_out * n_probes * D, NEEDLE_INVALID_CACT, name + " projection shape is inconsistent");
+      if (code == 2) {
+        R.conf_probes = probes;
+        R.conf_proj = proj;
+        R.conf_bias = bias;
+        R.conf_count = n_probes;
+        R.conf_out = n_out;
+      }
+    }
+  }
   bool tokenizer = false;
-  for (size_t i = cur; i < A.rec.size(); i++)
-    if (A.rec[i].dtype == 4) tokenizer = true;
+  while (cur < A.rec.size()) {
+    const int i = int(cur++);
+    if (A.rec[i].dtype == 4) {
+      require(!tokenizer, NEEDLE_INVALID_CACT, "Archive contains more than one RAW tokenizer tensor");
+      tokenizer = true;
+    } else {
+      fail(NEEDLE_UNSUPPORTED_CACT, "Unexpected trailing tensor " + std::to_string(i));
+    }
+  }
   require(tokenizer, NEEDLE_INVALID_CACT, "Archive does not contain its RAW SentencePiece tokenizer");
   return R;
 }
 
 struct SlotHost {
-  bool ready = false;
+  bool ready = false, collect = false;
   int32_t max_len = 0, sink = 0, kv_alloc = 0, position = 0;
 };
 
@@ -329,6 +371,8 @@ struct needle_ctx {
   // profiling
   bool profiling = false;
   int64_t launches = 0;  // kernels launched by this context
+  int collecting = 0;    // slots that feed a confidence probe pool
+  double* d_confidence = nullptr;
   std::vector<ProfEntry> prof_pending;
   std::vector<cudaEvent_t> event_pool;
   double prof_ms[kProfClasses] = {0};
@@ -546,6 +590,17 @@ void build_model(needle_ctx& C) {
     m.taps_w = upload_floats(C, taps);
   }
   m.final_norm = upload_floats(C, dense_n(R.final_norm, kDim, "final norm"));
+  if (R.conf_probes >= 0) {
+    require(R.conf_count <= kMaxProbes, NEEDLE_UNSUPPORTED_CACT,
+            "confidence head has more than " + std::to_string(kMaxProbes) + " probes");
+    m.probes = upload_floats(C, A.dense(R.conf_probes));
+    m.probe_proj = upload_floats(C, A.dense(R.conf_proj));
+    std::vector<float> bias = A.dense(R.conf_bias);
+    bias.resize(size_t(R.conf_out), 0.0f);  // rows past the bias length sum from 0 (cq.ts:307)
+    m.probe_bias = upload_floats(C, bias);
+    m.probe_count = int32_t(R.conf_count);
+    m.probe_out = int32_t(R.conf_out);
+  }
   // RoPE angles in binary64 exactly as applyRope (math.ts:104-108) evaluates them.
   {
     const double theta = double(A.rope_theta);
@@ -580,16 +635,28 @@ void build_state(needle_ctx& C) {
   sv.x = C.dalloc<float>(size_t(S) * kLaneWidth);
   sv.ring = C.dalloc<float>(size_t(S) * std::max(1, m.n_sites) * depth * kDim);
   const size_t heads = size_t(S) * L * kKvHeads * capacity;
-  sv.kcodes = C.dalloc<int8_t>(heads * kHeadDim);
-  sv.vcodes = C.dalloc<int8_t>(heads * kHeadDim);
+  sv.kv_f32 = o.kv_mode == NEEDLE_KV_FLOAT32 ? 1 : 0;
+  if (sv.kv_f32) {
+    sv.kf = C.dalloc<float>(heads * kHeadDim);
+    sv.vf = C.dalloc<float>(heads * kHeadDim);
+  } else {
+    sv.kcodes = C.dalloc<int8_t>(heads * kHeadDim);
+    sv.vcodes = C.dalloc<int8_t>(heads * kHeadDim);
+  }
   sv.kscale = C.dalloc<float>(heads);
   sv.vscale = C.dalloc<float>(heads);
   sv.seq = C.dalloc<SeqState>(S);
+  if (m.probe_count > 0) {
+    sv.pool_max = C.dalloc<double>(size_t(S) * m.probe_count);
+    sv.pool_den = C.dalloc<double>(size_t(S) * m.probe_count);
+    sv.pool_w = C.dalloc<double>(size_t(S) * m.probe_count * kDim);
+  }
   C.slots.assign(S, SlotHost{});
   StepView& st = C.stv;
   const size_t B = size_t(S);
   st.items = C.dalloc<DevItem>(B);
   C.d_counts = C.dalloc<int32_t>(8);
+  C.d_confidence = C.dalloc<double>(1);
   st.n_items = C.d_counts;
   st.n_select = C.d_counts + 1;
   const int ns = std::max(1, m.n_sites);
@@ -702,7 +769,13 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
   const SlotView& sv = C.sv;
   const int32_t* n_dev = st.n_items;
   cudaStream_t s0 = lane.main;
+  const bool probes = C.collecting > 0 && m.probe_count > 0;
+  auto probe_add = [&](int source) {
+    cuda_check(launch_probe_add(m, sv, st, source, n_host, s0), "probe pool");
+    C.launches++;
+  };
   C.timed(P_EMBED, [&] { return launch_embed(m, sv, st, n_host, s0); }, s0);
+  if (probes) probe_add(0);
   if (m.n_sites > 0) {
     std::vector<JobSpec> jobs;
     for (int s = 0; s < m.n_sites; s++) {
@@ -716,6 +789,7 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
   for (int l = 0; l <= m.layers; l++) {
     if (l > 0) cuda_check(cudaStreamWaitEvent(s0, lane.join[(l - 1) & 1], 0), "join");
     C.timed(P_LAYER, [&] { return launch_layer(m, sv, st, l, n_host, s0); }, s0);
+    if (probes && l > 0) probe_add(1);  // lanes now hold the output of layer l - 1
     if (l == m.layers) break;
     // Sinkhorn routing of layer l on the side stream, joined before the next k_layer.
     cuda_check(cudaEventRecord(lane.fork[l & 1], s0), "fork");
@@ -858,7 +932,8 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
       needle_cuda_default_opts(&C->opts);
     }
     const needle_opts& o = C->opts;
-    require(o.kv_mode == NEEDLE_KV_INT8, NEEDLE_BACKEND_UNAVAILABLE, "only the int8 KV cache is implemented");
+    require(o.kv_mode == NEEDLE_KV_INT8 || o.kv_mode == NEEDLE_KV_FLOAT32, NEEDLE_BACKEND_UNAVAILABLE,
+            "kv_mode must be NEEDLE_KV_INT8 or NEEDLE_KV_FLOAT32");
     require(o.numerics == NEEDLE_NUMERICS_EXACT, NEEDLE_BACKEND_UNAVAILABLE, "unknown numerics mode");
     require(o.max_seqs >= 1 && o.max_seqs <= 65536, NEEDLE_BACKEND_UNAVAILABLE, "max_seqs out of range");
     require(o.max_sink >= 0 && o.max_len >= 1, NEEDLE_BACKEND_UNAVAILABLE, "max_len / max_sink out of range");
@@ -938,6 +1013,11 @@ int needle_cuda_geometry(const needle_ctx* ctx, needle_geometry* g) {
 }
 
 int needle_cuda_seq_reset(needle_ctx* ctx, int32_t seq, int32_t maximum_length, int32_t sink_length) {
+  return needle_cuda_seq_reset_ex(ctx, seq, maximum_length, sink_length, 0);
+}
+
+int needle_cuda_seq_reset_ex(needle_ctx* ctx, int32_t seq, int32_t maximum_length, int32_t sink_length,
+                             int32_t collect_confidence) {
   return guarded([&] {
     needle_ctx& C = *ctx_of(ctx);
     require(seq >= 0 && seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
@@ -951,14 +1031,19 @@ int needle_cuda_seq_reset(needle_ctx* ctx, int32_t seq, int32_t maximum_length, 
     const int32_t kv_alloc = window > 0 ? std::min(maximum_length, sink + window) : maximum_length;
     require(kv_alloc <= C.sv.capacity, NEEDLE_BACKEND_UNAVAILABLE,
             "sink + window exceeds the context's KV capacity (raise max_sink / max_len)");
+    const bool collect = collect_confidence != 0 && C.mv.probe_count > 0;
     SeqState st{};
     st.position = 0;
     st.sink = sink;
     st.max_len = maximum_length;
     st.kv_alloc = kv_alloc;
+    st.collect = collect ? 1 : 0;
     cuda_check(cudaMemcpyAsync(C.sv.seq + seq, &st, sizeof(st), cudaMemcpyHostToDevice, C.stream), "reset");
+    if (collect) cuda_check(launch_pool_reset(C.mv, C.sv, seq, C.stream), "pool reset");
     cuda_check(cudaStreamSynchronize(C.stream), "reset");
     SlotHost& h = C.slots[seq];
+    C.collecting += int(collect) - int(h.collect);
+    h.collect = collect;
     h.ready = true;
     h.max_len = maximum_length;
     h.sink = sink;
@@ -1100,6 +1185,7 @@ int needle_cuda_read_kv(const needle_ctx* ctx, int32_t seq, int32_t layer, int8_
     require(layer >= 0 && layer < C.mv.layers, NEEDLE_INVALID_CACT, "Layer out of range");
     const SlotHost& h = C.slots[seq];
     require(h.ready, NEEDLE_INVALID_CACT, "KV cache was not allocated");
+    require(!C.sv.kv_f32, NEEDLE_INVALID_CACT, "Int8 KV cache is not allocated");
     if (kv_allocation) *kv_allocation = h.kv_alloc;
     const int cap = C.sv.capacity;
     for (int head = 0; head < kKvHeads; head++) {
@@ -1117,6 +1203,44 @@ int needle_cuda_read_kv(const needle_ctx* ctx, int32_t seq, int32_t layer, int8_
         cuda_check(cudaMemcpy(value_scales + size_t(head) * h.kv_alloc, C.sv.vscale + base, size_t(h.kv_alloc) * 4,
                               cudaMemcpyDeviceToHost), "read_kv");
     }
+  });
+}
+
+int needle_cuda_read_kv_f32(const needle_ctx* ctx, int32_t seq, int32_t layer, float* keys, float* values,
+                            int32_t* kv_allocation) {
+  return guarded([&] {
+    const needle_ctx& C = *ctx_of(const_cast<needle_ctx*>(ctx));
+    require(seq >= 0 && seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
+    require(layer >= 0 && layer < C.mv.layers, NEEDLE_INVALID_CACT, "Layer out of range");
+    const SlotHost& h = C.slots[seq];
+    require(C.sv.kv_f32 && h.ready, NEEDLE_INVALID_CACT, "Float32 KV cache is not allocated");
+    if (kv_allocation) *kv_allocation = h.kv_alloc;
+    cuda_check(cudaStreamSynchronize(C.stream), "read_kv");
+    for (int head = 0; head < kKvHeads; head++) {
+      const int64_t base = ((int64_t(seq) * C.mv.layers + layer) * kKvHeads + head) * C.sv.capacity;
+      const size_t n = size_t(h.kv_alloc) * kHeadDim;
+      if (keys)
+        cuda_check(cudaMemcpy(keys + size_t(head) * n, C.sv.kf + base * kHeadDim, n * 4, cudaMemcpyDeviceToHost),
+                   "read_kv");
+      if (values)
+        cuda_check(cudaMemcpy(values + size_t(head) * n, C.sv.vf + base * kHeadDim, n * 4, cudaMemcpyDeviceToHost),
+                   "read_kv");
+    }
+  });
+}
+
+int needle_cuda_confidence(const needle_ctx* ctx, int32_t seq, double* value) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(const_cast<needle_ctx*>(ctx));
+    require(value != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+    require(seq >= 0 && seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
+    *value = std::numeric_limits<double>::quiet_NaN();
+    if (!C.slots[seq].collect || C.mv.probe_count == 0) return;
+    double* d_out = C.d_confidence;
+    cuda_check(launch_confidence(C.mv, C.sv, seq, d_out, C.stream), "confidence");
+    C.launches++;
+    cuda_check(cudaMemcpyAsync(value, d_out, sizeof(double), cudaMemcpyDeviceToHost, C.stream), "confidence");
+    cuda_check(cudaStreamSynchronize(C.stream), "confidence");
   });
 }
 
@@ -1229,6 +1353,7 @@ int needle_cuda_sched_load(needle_ctx* ctx, int32_t n_slots, const int32_t* prom
     // all slots idle
     cuda_check(cudaMemset(C.sv.seq, 0, size_t(C.opts.max_seqs) * sizeof(SeqState)), "sched init");
     for (auto& h : C.slots) h = SlotHost{};
+    C.collecting = 0;
     SchedView& q = C.sched;
     q.prompt_offsets = d_off;
     q.prompt_ids = d_ids;

@@ -8,6 +8,8 @@
 
 namespace needle {
 
+constexpr int kMaxProbes = 32;  // confidence probes an archive may carry
+
 // A Cactus-Quant matrix in device memory (CqMatrix, packages/needle.js/src/model/cact.ts:61-75).
 struct CqMat {
   const uint8_t* packed = nullptr;
@@ -31,6 +33,11 @@ struct ModelView {
   const float* final_norm;  // [512]
   const double *rope_cos, *rope_sin;  // [max_seq][32], computed on the host in binary64
   Codebook cb;
+  // Confidence probe head (cact.ts probe-head manifest code 2), or probe_count 0.
+  const float* probes;      // [probe_count][512]
+  const float* probe_proj;  // [probe_out][probe_count * 512]
+  const float* probe_bias;  // [probe_out]
+  int32_t probe_count, probe_out;
 };
 
 // Per-slot sequence state (NeedleRuntime fields, runtime.ts:113-133), device-authoritative.
@@ -43,6 +50,7 @@ struct SeqState {
   int32_t hist[3];     // previous tokens, most recent first (engram n-grams, runtime.ts:788-818)
   // device scheduler
   int32_t busy, seq_id, prompt_off, prompt_len, gen_target, gen_done;
+  int32_t collect;     // collectConfidence: feed the probe pool
 };
 
 // Slot-indexed device state.
@@ -51,11 +59,18 @@ struct SlotView {
   int32_t layers;
   float* x;             // [S][4][512] mHC lanes
   float* ring;          // [S][sites][10][512] engram value ring
+  int32_t kv_f32;       // 1: float32 cache (kf / vf), 0: int8 cache (kcodes / vcodes)
   int8_t* kcodes;       // [S][L][4][capacity][64]
   int8_t* vcodes;
-  float* kscale;        // [S][L][4][capacity]
+  float* kf;            // [S][L][4][capacity][64] (float32 mode)
+  float* vf;
+  float* kscale;        // [S][L][4][capacity] (1 in float32 mode)
   float* vscale;
   SeqState* seq;        // [S]
+  // OnlineProbePool per slot (allocated when the archive has a confidence head)
+  double* pool_max;     // [S][probes]
+  double* pool_den;     // [S][probes]
+  double* pool_w;       // [S][probes][512]
 };
 
 // One resolved item of a step (internal order: selecting items first).
@@ -130,6 +145,14 @@ size_t attention_fast_scratch_bytes(int32_t batch, int32_t capacity);
 cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
                                   const float* vs, const int32_t* counts, int32_t batch, int32_t capacity,
                                   float* out, void* scratch, cudaStream_t s);
+// Online probe pool (OnlineProbePool.add, runtime.ts:60-90) of the step's collecting items: source 0
+// is the scaled embedding (lane 0 after k_embed), source 1 the mean of the lanes (after a layer).
+cudaError_t launch_probe_add(const ModelView& m, const SlotView& sv, const StepView& st, int source, int n_host,
+                             cudaStream_t s);
+// Resets one slot's pool (maximum -inf, denominator 0, weighted 0).
+cudaError_t launch_pool_reset(const ModelView& m, const SlotView& sv, int slot, cudaStream_t s);
+// confidence() of one slot: sigmoid(denseMatvec(projection, pooled, bias)[0]) into *out (device).
+cudaError_t launch_confidence(const ModelView& m, const SlotView& sv, int slot, double* out, cudaStream_t s);
 // Records the message returned by needle_cuda_last_error() on this thread (engine.cu).
 void set_last_error(const char* msg);
 inline void set_last_error(const std::string& msg) { set_last_error(msg.c_str()); }

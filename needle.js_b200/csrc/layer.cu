@@ -511,42 +511,16 @@ struct CacheRef {
 };
 
 // Attention of query heads 2h, 2h+1 over one KV head (the #attention loops of runtime.ts:732-784
-// for one kvHead).  q: smem binary32 [2][64]; e: smem binary64 [2][count]; tile: smem staging
+// for one kvHead).  q: smem [2][64] (binary32 values widened to binary64); e: smem binary64 [2][count]; tile: smem staging
 // area (kAttnTile value rows + scales + weights); slot_of(t) maps the t-th visible position to its
 // cache row.  Leaves the gated outputs in out[2][64] (smem).
 constexpr int kAttnTile = 256;
 constexpr size_t kAttnTileBytes = kAttnTile * (kHeadDim + 2 * 8);  // codes, 2 x weight*scale
 
-template <class SlotOf>
-__device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const float* q, double* e,
-                            unsigned char* tile, const float* gate, float* out, double* red) {
+// softmaxInPlace (math.ts:46-60) of both heads' binary32 scores e[2][count]: max (order-free),
+// exp in parallel, sequential total; leaves red[4 + h] = 1 / total (0 for an empty row).
+__device__ __forceinline__ void softmax_pair(double* e, int count, double* red) {
   const int tid = threadIdx.x;
-  // scores[t] = f32((sum_i q_i * code_i * keyScale) / 8)  (runtime.ts:736-757)
-  for (int t = tid; t < count; t += kAttnThreads) {
-    const int sl = slot_of(t);
-    const double ks = (double)C.ks[sl];
-    const uint4* kr = reinterpret_cast<const uint4*>(C.kc + (int64_t)sl * kHeadDim);
-    uint4 u[4];
-#pragma unroll
-    for (int w4 = 0; w4 < 4; w4++) u[w4] = __ldg(kr + w4);
-    double d0 = 0.0, d1 = 0.0;
-#pragma unroll
-    for (int w4 = 0; w4 < 4; w4++) {
-      const uint32_t words[4] = {u[w4].x, u[w4].y, u[w4].z, u[w4].w};
-#pragma unroll
-      for (int k = 0; k < 16; k++) {
-        const int i = w4 * 16 + k;
-        const double code = int_to_double_exact((int)(int8_t)((words[k >> 2] >> ((k & 3) * 8)) & 0xff));
-        d0 = d0 + ((double)q[i] * code) * ks;
-        d1 = d1 + ((double)q[kHeadDim + i] * code) * ks;
-      }
-    }
-    const double inverse_root = 1.0 / sqrt((double)kHeadDim);
-    e[t] = (double)f32(d0 * inverse_root);
-    e[count + t] = (double)f32(d1 * inverse_root);
-  }
-  __syncthreads();
-  // softmaxInPlace (math.ts:46-60): max (order-free), exp in parallel, sequential total.
   {
     const int hh = tid >> 6, lane64 = tid & 63;
     double mx = -INFINITY;
@@ -558,15 +532,57 @@ __device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const 
     __syncthreads();
     for (int t = lane64; t < count; t += 64) e[hh * count + t] = exp(e[hh * count + t] - mx);
     __syncthreads();
-    if (lane64 == 0) {
+    if (lane64 == 0) {  // sequential total; the values are read eight at a time ahead of the adds
       const double* eh = e + hh * count;
       double total = 0.0;
-#pragma unroll 8
-      for (int t = 0; t < count; t++) total = total + eh[t];
+      int t = 0;
+      for (; t + 8 <= count; t += 8) {
+        double v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = eh[t + k];
+#pragma unroll
+        for (int k = 0; k < 8; k++) total = total + v[k];
+      }
+      for (; t < count; t++) total = total + eh[t];
       red[4 + hh] = total > 0.0 ? 1.0 / total : 0.0;
     }
     __syncthreads();
   }
+}
+
+template <class SlotOf>
+__device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const double* q, double* e,
+                            unsigned char* tile, const float* gate, float* out, double* red) {
+  const int tid = threadIdx.x;
+  // scores[t] = f32((sum_i q_i * code_i * keyScale) / 8)  (runtime.ts:736-757)
+  for (int t = tid; t < count; t += kAttnThreads) {
+    const int sl = slot_of(t);
+    const double ks = (double)C.ks[sl];
+    const uint4* kr = reinterpret_cast<const uint4*>(C.kc + (int64_t)sl * kHeadDim);
+    uint4 u[4];
+#pragma unroll
+    for (int w4 = 0; w4 < 4; w4++) u[w4] = __ldg(kr + w4);
+    // q * code * keyScale: q * code is exact in binary64 and so is code * keyScale, so
+    // (q * code) * keyScale and q * (code * keyScale) are both the one rounding of the same real
+    // product; the second form shares code * keyScale between the two heads.
+    double d0 = 0.0, d1 = 0.0;
+#pragma unroll
+    for (int w4 = 0; w4 < 4; w4++) {
+      const uint32_t words[4] = {u[w4].x, u[w4].y, u[w4].z, u[w4].w};
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        const int i = w4 * 16 + k;
+        const double cks = int_to_double_exact((int)(int8_t)((words[k >> 2] >> ((k & 3) * 8)) & 0xff)) * ks;
+        d0 = d0 + q[i] * cks;
+        d1 = d1 + q[kHeadDim + i] * cks;
+      }
+    }
+    const double inverse_root = 1.0 / sqrt((double)kHeadDim);
+    e[t] = round32_cvt(d0 * inverse_root);
+    e[count + t] = round32_cvt(d1 * inverse_root);
+  }
+  __syncthreads();
+  softmax_pair(e, count, red);
   // output[i] += weight * code * valueScale, sequentially in t with binary32 storage (760-782).
   // Value rows, scales and weights are staged tile by tile in shared memory so the sequential
   // chain reads only shared memory.
@@ -576,7 +592,7 @@ __device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const 
   int8_t* vt = reinterpret_cast<int8_t*>(tile);                                   // [tile][64]
   double* wvt = reinterpret_cast<double*>(tile + kAttnTile * kHeadDim);           // [2][tile]
   const int hh = tid >> 6, i = tid & 63;
-  float o = 0.0f;
+  double o = 0.0;  // a binary32 value, kept widened (round32 after every step)
   for (int t0 = 0; t0 < count; t0 += kAttnTile) {
     const int n = min(kAttnTile, count - t0);
     for (int k = tid; k < n * 4; k += kAttnThreads) {
@@ -587,18 +603,55 @@ __device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const 
     }
     for (int k = tid; k < 2 * n; k += kAttnThreads) {
       const int h2 = k / n, t = k - h2 * n;
-      const double w = (double)f32((double)f32(e[h2 * count + t0 + t]) * red[4 + h2]);
+      const double w = round32_cvt(round32_cvt(e[h2 * count + t0 + t]) * red[4 + h2]);
       wvt[h2 * kAttnTile + t] = w * (double)C.vs[slot_of(t0 + t)];
     }
     __syncthreads();
     const double* wv = wvt + hh * kAttnTile;
 #pragma unroll 8
-    for (int t = 0; t < n; t++)
-      o = f32((double)o + int_to_double_exact(vt[t * kHeadDim + i]) * wv[t]);
+    for (int t = 0; t < n; t++) o = round32_cvt(o + int_to_double_exact(vt[t * kHeadDim + i]) * wv[t]);
     __syncthreads();
   }
   // attentionOutput * sigmoid(gate) (runtime.ts:503-504)
-  out[hh * kHeadDim + i] = gate ? f32((double)o * sigmoid_d((double)gate[hh * kHeadDim + i])) : o;
+  out[hh * kHeadDim + i] = gate ? f32(o * sigmoid_d((double)gate[hh * kHeadDim + i])) : (float)o;
+  __syncthreads();
+}
+
+// attend_pair over the float32 cache (runtime.ts:744-748, 768-772): keys and values are read as
+// stored, and query * key and weight * value are exact binary64 products, so each accumulation is
+// one fused multiply-add.  The weights are formed once per position in e (binary32 values), and
+// the value chain reads the cache directly (the two heads share each row).
+template <class SlotOf>
+__device__ void attend_pair_f32(const float* kf, const float* vf, int count, SlotOf slot_of, const double* q,
+                                double* e, const float* gate, float* out, double* red) {
+  const int tid = threadIdx.x;
+  const double inverse_root = 1.0 / sqrt((double)kHeadDim);
+  for (int t = tid; t < count; t += kAttnThreads) {
+    const float4* kr = reinterpret_cast<const float4*>(kf + (int64_t)slot_of(t) * kHeadDim);
+    double d0 = 0.0, d1 = 0.0;
+#pragma unroll 4
+    for (int w4 = 0; w4 < kHeadDim / 4; w4++) {
+      const float4 k4 = __ldg(kr + w4);
+      const float kk[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        d0 = fma(q[4 * w4 + c], (double)kk[c], d0);
+        d1 = fma(q[kHeadDim + 4 * w4 + c], (double)kk[c], d1);
+      }
+    }
+    e[t] = round32_cvt(d0 * inverse_root);
+    e[count + t] = round32_cvt(d1 * inverse_root);
+  }
+  __syncthreads();
+  softmax_pair(e, count, red);
+  for (int k = tid; k < 2 * count; k += kAttnThreads) e[k] = round32_cvt(round32_cvt(e[k]) * red[4 + k / count]);
+  __syncthreads();
+  const int hh = tid >> 6, i = tid & 63;
+  const double* w = e + hh * count;
+  double o = 0.0;  // a binary32 value, kept widened
+#pragma unroll 4
+  for (int t = 0; t < count; t++) o = round32_cvt(fma(w[t], (double)__ldg(vf + (int64_t)slot_of(t) * kHeadDim + i), o));
+  out[hh * kHeadDim + i] = gate ? f32(o * sigmoid_d((double)gate[hh * kHeadDim + i])) : (float)o;
   __syncthreads();
 }
 
@@ -670,13 +723,24 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
     const double key_scale = fmax(1e-12, fmax(amax[0], amax[1])) / 127.0;
     const double value_scale = fmax(1e-12, fmax(amax[4], amax[5])) / 127.0;
     const int sl = kv_slot(p);
-    if (tid < kHeadDim) {
-      sv.kcodes[(head_base + sl) * kHeadDim + tid] = (int8_t)round_ties_even((double)kv[tid] / key_scale);
-      sv.vcodes[(head_base + sl) * kHeadDim + tid] = (int8_t)round_ties_even((double)vv[tid] / value_scale);
-    }
-    if (tid == 0) {
-      sv.kscale[head_base + sl] = f32(key_scale);
-      sv.vscale[head_base + sl] = f32(value_scale);
+    if (sv.kv_f32) {  // float32 cache: values as given, scales 1 (runtime.ts:686-693)
+      if (tid < kHeadDim) {
+        sv.kf[(head_base + sl) * kHeadDim + tid] = kv[tid];
+        sv.vf[(head_base + sl) * kHeadDim + tid] = vv[tid];
+      }
+      if (tid == 0) {
+        sv.kscale[head_base + sl] = 1.0f;
+        sv.vscale[head_base + sl] = 1.0f;
+      }
+    } else {
+      if (tid < kHeadDim) {
+        sv.kcodes[(head_base + sl) * kHeadDim + tid] = (int8_t)round_ties_even((double)kv[tid] / key_scale);
+        sv.vcodes[(head_base + sl) * kHeadDim + tid] = (int8_t)round_ties_even((double)vv[tid] / value_scale);
+      }
+      if (tid == 0) {
+        sv.kscale[head_base + sl] = f32(key_scale);
+        sv.vscale[head_base + sl] = f32(value_scale);
+      }
     }
     __syncthreads();
   }
@@ -684,12 +748,20 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
   const int prefix = min(sink, p + 1);
   const int recent_low = window > 0 ? max(prefix, p + 1 - window) : prefix;
   const int count = prefix + (p - recent_low + 1);
-  CacheRef C{sv.kcodes + head_base * kHeadDim, sv.vcodes + head_base * kHeadDim, sv.kscale + head_base,
-             sv.vscale + head_base};
   unsigned char* tile = smem_raw;
   double* e = reinterpret_cast<double*>(smem_raw + kAttnTileBytes);
   auto slot_of = [&](int t) { return kv_slot(t < prefix ? t : recent_low + (t - prefix)); };
-  attend_pair(C, count, slot_of, qv, e, tile, gt, outv, red);
+  __shared__ double qd[2 * kHeadDim];
+  qd[tid] = (double)qv[tid];
+  __syncthreads();
+  if (sv.kv_f32) {
+    attend_pair_f32(sv.kf + head_base * kHeadDim, sv.vf + head_base * kHeadDim, count, slot_of, qd, e, gt, outv,
+                    red);
+  } else {
+    CacheRef C{sv.kcodes + head_base * kHeadDim, sv.vcodes + head_base * kHeadDim, sv.kscale + head_base,
+               sv.vscale + head_base};
+    attend_pair(C, count, slot_of, qd, e, tile, gt, outv, red);
+  }
   // prepareCqActivation of the output projection: heads 2h, 2h+1 are exactly input group h.
   fwht_smem(outv, kGroup, 1);
   st.prep_o[(int64_t)b * kDim + h * kGroup + tid] = f32((double)outv[tid] * (1.0 / sqrt((double)kGroup)));
@@ -703,11 +775,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention_dev(const float* __r
                                                                const int32_t* counts, int32_t capacity,
                                                                float* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ float qv[2 * kHeadDim], outv[2 * kHeadDim];
+  __shared__ double qd[2 * kHeadDim];
+  __shared__ float outv[2 * kHeadDim];
   __shared__ double red[8];
   const int b = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x;
-  qv[tid] = q[(int64_t)b * kHeads * kHeadDim + 2 * h * kHeadDim + tid];
+  qd[tid] = (double)q[(int64_t)b * kHeads * kHeadDim + 2 * h * kHeadDim + tid];
   __syncthreads();
   const int count = min(max(counts[b], 0), capacity);
   const int64_t head_base = ((int64_t)b * kKvHeads + h) * capacity;
@@ -715,7 +788,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention_dev(const float* __r
   unsigned char* tile = smem_raw;
   double* e = reinterpret_cast<double*>(smem_raw + kAttnTileBytes);
   auto slot_of = [](int t) { return t; };
-  attend_pair(C, count, slot_of, qv, e, tile, nullptr, outv, red);
+  attend_pair(C, count, slot_of, qd, e, tile, nullptr, outv, red);
   out[(int64_t)b * kHeads * kHeadDim + 2 * h * kHeadDim + tid] = outv[tid];
 }
 
@@ -825,6 +898,88 @@ __global__ void __launch_bounds__(kFinishThreads) k_finish(const ModelView m, co
   }
 }
 
+// ------------------------------------------------------------------ confidence probe pool
+
+// OnlineProbePool.add (runtime.ts:60-90) for the step's collecting items, one CTA of kDim threads
+// per item.  cell: the scaled embedding (source 0: lane 0 right after k_embed, which holds it) or
+// the mean of the lanes (source 1: f32(sum of lanes / lanes), runtime.ts:551-560).  score_p =
+// (sum_i cell_i * probe_pi) / sqrt(d) sequentially in i (exact products: fused); then the pool's
+// online softmax update in binary64 with separate roundings, as the reference writes it.
+__global__ void __launch_bounds__(kDim) k_probe_add(const ModelView m, const SlotView sv, const StepView st,
+                                                    int source) {
+  __shared__ double cell[kDim];
+  __shared__ double score[kMaxProbes];
+  const int b = blockIdx.x;
+  if (b >= *st.n_items) return;
+  const int slot = st.items[b].slot;
+  if (!sv.seq[slot].collect) return;
+  const int tid = threadIdx.x, P = m.probe_count;
+  const float* x = sv.x + (int64_t)slot * kLaneWidth;
+  if (source == 0) {
+    cell[tid] = (double)x[tid];
+  } else {
+    double sum = 0.0;
+#pragma unroll
+    for (int lane = 0; lane < kLanes; lane++) sum = sum + (double)x[lane * kDim + tid];
+    cell[tid] = round32_cvt(sum / (double)kLanes);
+  }
+  __syncthreads();
+  if (tid < P) {
+    const float* pr = m.probes + (int64_t)tid * kDim;
+    double sc = 0.0;
+    for (int i = 0; i < kDim; i++) sc = fma(cell[i], (double)__ldg(pr + i), sc);
+    score[tid] = sc * (1.0 / sqrt((double)kDim));
+  }
+  __syncthreads();
+  double* mx = sv.pool_max + (int64_t)slot * P;
+  double* den = sv.pool_den + (int64_t)slot * P;
+  double* w = sv.pool_w + (int64_t)slot * P * kDim;
+  for (int p = 0; p < P; p++) {
+    const double sc = score[p], prev = mx[p];
+    double* wp = w + (int64_t)p * kDim + tid;
+    if (sc <= prev) {
+      const double weight = exp(sc - prev);
+      *wp = *wp + weight * cell[tid];
+      if (tid == 0) den[p] = den[p] + weight;
+    } else {
+      const double old = isfinite(prev) ? exp(prev - sc) : 0.0;
+      *wp = *wp * old + cell[tid];
+      if (tid == 0) den[p] = den[p] * old + 1.0;
+    }
+  }
+  __syncthreads();  // every thread has read the old maxima
+  if (tid < P && score[tid] > mx[tid]) mx[tid] = score[tid];
+}
+
+// Pool of one slot back to its constructor state (runtime.ts:52-58).
+__global__ void k_pool_reset(const ModelView m, const SlotView sv, int slot) {
+  const int P = m.probe_count;
+  for (int k = threadIdx.x; k < P * kDim; k += blockDim.x) sv.pool_w[(int64_t)slot * P * kDim + k] = 0.0;
+  if (threadIdx.x < P) {
+    sv.pool_max[(int64_t)slot * P + threadIdx.x] = -INFINITY;
+    sv.pool_den[(int64_t)slot * P + threadIdx.x] = 0.0;
+  }
+}
+
+// confidence (runtime.ts:634-645): pooled = f32(weighted / max(denominator, 1e-30)) (runtime.ts:
+// 92-104), denseMatvec of the projection with bias (cq.ts:297-318: binary64 sum from the bias,
+// exact products, sequential over the columns), sigmoid of output 0.
+__global__ void __launch_bounds__(kDim) k_confidence(const ModelView m, const SlotView sv, int slot, double* out) {
+  extern __shared__ float pooled[];  // [P * kDim]
+  const int tid = threadIdx.x, P = m.probe_count;
+  for (int p = 0; p < P; p++) {
+    const double den = fmax(sv.pool_den[(int64_t)slot * P + p], 1e-30);
+    pooled[p * kDim + tid] = f32(sv.pool_w[((int64_t)slot * P + p) * kDim + tid] / den);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const int n = P * kDim;
+    double sum = (double)m.probe_bias[0];
+    for (int c = 0; c < n; c++) sum = fma((double)__ldg(m.probe_proj + c), (double)pooled[c], sum);
+    *out = sigmoid_d((double)f32(sum));
+  }
+}
+
 // ------------------------------------------------------------------ device scheduler
 
 // Admission: every idle slot takes the next queued sequence (reset as runtime.ts:150-225 with
@@ -851,6 +1006,7 @@ __global__ void k_sched_admit(const SlotView sv, const SchedView q, int window) 
   seq->prompt_len = len;
   seq->gen_target = gen;
   seq->gen_done = 0;
+  seq->collect = 0;
   seq->busy = 1;
 }
 
@@ -984,6 +1140,25 @@ cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView
   SchedView q{};
   if (sched) q = *sched;
   k_finish<<<n_host, kFinishThreads, 0, s>>>(m, sv, st, q, sched ? 1 : 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_probe_add(const ModelView& m, const SlotView& sv, const StepView& st, int source, int n_host,
+                             cudaStream_t s) {
+  if (n_host <= 0 || m.probe_count <= 0) return cudaSuccess;
+  k_probe_add<<<n_host, kDim, 0, s>>>(m, sv, st, source);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pool_reset(const ModelView& m, const SlotView& sv, int slot, cudaStream_t s) {
+  if (m.probe_count <= 0) return cudaSuccess;
+  k_pool_reset<<<1, 256, 0, s>>>(m, sv, slot);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_confidence(const ModelView& m, const SlotView& sv, int slot, double* out, cudaStream_t s) {
+  if (m.probe_count <= 0) return cudaSuccess;
+  k_confidence<<<1, kDim, sizeof(float) * m.probe_count * kDim, s>>>(m, sv, slot, out);
   return cudaGetLastError();
 }
 

@@ -18,6 +18,8 @@ CODES = ["INVALID_CACT", "UNSUPPORTED_CACT", "WEIGHTS_NOT_FOUND", "WEIGHTS_INTEG
          "WEBGPU_UNAVAILABLE", "BACKEND_UNAVAILABLE", "CONTEXT_OVERFLOW", "INVALID_TOOL_SCHEMA",
          "GRAMMAR_DEAD_END", "GENERATION_ABORTED"]
 TOKEN_PENDING = -1
+KV_INT8 = 0
+KV_FLOAT32 = 1
 NOALLOC_MAX_FLOATS = 1 << 20  # NEEDLE_NOALLOC_MAX_FLOATS
 
 
@@ -67,12 +69,16 @@ EXPORTS = {
     "needle_cuda_close": (C.c_int, [C.c_void_p]),
     "needle_cuda_geometry": (C.c_int, [C.c_void_p, C.POINTER(Geometry)]),
     "needle_cuda_seq_reset": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32]),
+    "needle_cuda_seq_reset_ex": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    "needle_cuda_confidence": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_double)]),
     "needle_cuda_seq_position": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
     "needle_cuda_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_size_t,
                                    C.c_void_p, C.c_void_p]),
     "needle_cuda_prefill": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_void_p]),
     "needle_cuda_read_kv": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p, C.POINTER(C.c_int32)]),
+    "needle_cuda_read_kv_f32": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
+                                          C.POINTER(C.c_int32)]),
     "needle_cuda_read_lanes": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p]),
     "needle_cuda_matvec": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                      C.c_int32, C.c_void_p]),

@@ -1461,6 +1461,17 @@ int ref_runtime_read_kv(const ref_runtime* rt, int32_t layer, int8_t* key_codes,
   });
 }
 
+int ref_runtime_read_kv_f32(const ref_runtime* rt, int32_t layer, float* keys, float* values) {
+  return guard([&] {
+    const Geometry& g = rt->G();
+    invariant(layer >= 0 && layer < g.numberOfLayers, INVALID_CACT, "Layer out of range");
+    invariant(rt->kvMode == 1 && rt->maximumLength > 0, INVALID_CACT, "Float32 KV cache is not allocated");
+    const int64_t n = int64_t(g.numberOfKVHeads) * rt->kvAllocation * g.headDimension;
+    if (keys) std::copy_n(rt->keyFloat.data() + layer * n, n, keys);
+    if (values) std::copy_n(rt->valueFloat.data() + layer * n, n, values);
+  });
+}
+
 int ref_runtime_read_lanes(const ref_runtime* rt, float* lanes) {
   return guard([&] {
     const Geometry& g = rt->G();

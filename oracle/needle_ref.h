@@ -87,6 +87,8 @@ int ref_runtime_step_selected(ref_runtime* rt, int32_t token, const uint32_t* al
  * [kv_heads][alloc].  Any pointer may be NULL. */
 int ref_runtime_read_kv(const ref_runtime* rt, int32_t layer, int8_t* key_codes,
                         int8_t* value_codes, float* key_scales, float* value_scales);
+/* Copies one layer of the float32 cache (kv_mode 1): keys / values [kv_heads][alloc][head_dim]. */
+int ref_runtime_read_kv_f32(const ref_runtime* rt, int32_t layer, float* keys, float* values);
 /* Lane state x: lanes * model_dimension floats. */
 int ref_runtime_read_lanes(const ref_runtime* rt, float* lanes);
 /* Confidence (runtime.ts:634-645); returns NaN through *value when unavailable. */

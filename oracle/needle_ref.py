@@ -249,6 +249,14 @@ class Runtime:
         _check(lib().ref_runtime_read_kv(self.h, C.c_int32(layer), _p(kc), _p(vc), _p(ks), _p(vs)))
         return kc, vc, ks, vs
 
+    def read_kv_f32(self, layer):
+        alloc = self.kv_allocation
+        hk, hd = self.model.kv_heads, self.model.head_dim
+        k = np.zeros((hk, alloc, hd), dtype=np.float32)
+        v = np.zeros((hk, alloc, hd), dtype=np.float32)
+        _check(lib().ref_runtime_read_kv_f32(self.h, C.c_int32(layer), _p(k), _p(v)))
+        return k, v
+
     def read_lanes(self):
         out = np.zeros(self.model.lanes * self.model.dim, dtype=np.float32)
         _check(lib().ref_runtime_read_lanes(self.h, _p(out)))
