@@ -208,7 +208,8 @@ def _time_calls(torch, stream, fn, n_sets, warmup, iters):
 
 def bench_qmatvec(args, peaks):
     """isolated quantised matvec, every projection shape + 8192x8192, batch
-    1/8/32/128; indices uniform, fp16 norms |N(0,1)|*0.01, activations N(0,1) (seed 2)."""
+    1/8/32/128; indices uniform, fp16 norms |N(0,1)|*0.01, activations N(0,1) (seed 2: generator
+    2000 + shape index per shape)."""
     import ctypes as C
     import torch
     from needle_b200 import native, synth
@@ -216,9 +217,12 @@ def bench_qmatvec(args, peaks):
     torch.cuda.set_device(0)
     stream = torch.cuda.current_stream()
     cb = synth.lloyd_max_codebook()
-    gen = torch.Generator(device="cuda").manual_seed(2)
     results, launches = [], 0
-    for name, rows, inputs, bits in QMATVEC_SHAPES:
+    batches = [int(b) for b in args.batches.split(",")] if args.batches else [1, 8, 32, 128]
+    for si, (name, rows, inputs, bits) in enumerate(QMATVEC_SHAPES):
+        if args.cases and args.cases not in name:
+            continue
+        gen = torch.Generator(device="cuda").manual_seed(2000 + si)  # seed 2, one stream per shape
         pad = -(-inputs // 128) * 128
         row_bytes = pad * (2 if bits == 5 else bits) // 8
         mbytes = rows * row_bytes + rows * (pad // 128) * 2
@@ -227,13 +231,15 @@ def bench_qmatvec(args, peaks):
         norms = (torch.randn((n_sets, rows * (pad // 128)), device="cuda", generator=gen).abs() * 0.01).half()
         descs = [native.CqMatrixDesc(packed[i].data_ptr(), norms[i].data_ptr(), rows, inputs, 128, bits)
                  for i in range(n_sets)]
-        for batch in (1, 8, 32, 128):
+        for batch in batches:
             x = torch.randn((batch, inputs), device="cuda", generator=gen)
             y = torch.empty((batch, rows), device="cuda")
             lib = native.lib()
-            modes = [("exact", lib.needle_cuda_cq_matvec_dev, 3 if (batch <= 8 and pad // 128 >= 16) else 2)]
-            if bits in (2, 4, 5):
-                modes.append(("fast", lib.needle_cuda_cq_matvec_dev_fast, -(-batch // 8)))
+            modes = []
+            if args.numerics in ("both", "exact"):
+                modes.append(("exact", lib.needle_cuda_cq_matvec_dev, 3 if (batch <= 8 and pad // 128 >= 16) else 2))
+            if bits in (2, 4, 5) and args.numerics in ("both", "fast"):
+                modes.append(("fast", lib.needle_cuda_cq_matvec_dev_fast, 2 * -(-batch // 8)))
             for mode, fn, kernels in modes:
                 def call(i, strm, fn=fn):
                     native.check(fn(C.byref(descs[i]), native.ptr(cb), x.data_ptr(), batch, y.data_ptr(), strm))
@@ -245,7 +251,8 @@ def bench_qmatvec(args, peaks):
                                 "gbs": round(alg / (ms * 1e-3) / 1e9, 1), "bytes": alg, "kernels_per_call": kernels})
         del packed, norms
         torch.cuda.empty_cache()
-    head = next(r for r in results if r["shape"].startswith("stress") and r["batch"] == 1 and r["numerics"] == "fast")
+    head = next((r for r in results if r["shape"].startswith("stress") and r["batch"] == 1 and r["numerics"] == "fast"),
+                results[0])
     peak, src = _peak(peaks)
     line = {"metric": "qmatvec HBM GB/s", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
             "steps": max(20, min(args.steps, 200)), "warmup": max(3, args.warmup), "ms_per_step": head["us"] / 1e3,
@@ -253,9 +260,12 @@ def bench_qmatvec(args, peaks):
             "data": "synthetic", "config": {"workload": "isolated quantised matvec (BASELINE config 2), headline 8192x8192 CQ4 batch 1, "
                                    "fast numerics; exact-numerics rows alongside",
                        "l2": f"operand sets rotated over > {ROTATE_BYTES >> 20} MB", "cases": results},
-            "roofline": {"kernel": "k_cq_gemv_table", "bound": "hbm",
+            "roofline": {"kernel": "k_cq_gemv_table (+ k_cq_fast_reduce)", "bound": "hbm",
                          "achieved": head["gbs"], "peak": peak, "peak_source": src, "unit": "GB/s",
-                         "frac": round(head["gbs"] / peak, 4), "traffic": None},
+                         "frac": round(head["gbs"] / peak, 4),
+                         # DRAM read + write of one table-kernel launch of the headline case (ncu)
+                         "traffic": 33612544 if head["shape"].startswith("stress") and head["batch"] == 1 else None,
+                         "traffic_source": "profiles/qmatvec_table_8192x8192_cq4_batch1.md"},
             "gpu_launches": launches}
     print(json.dumps(line), flush=True)
 
@@ -263,16 +273,17 @@ def bench_qmatvec(args, peaks):
 def bench_attention(args, peaks):
     """isolated int8-KV decode attention, batch 64, 8 query / 4 KV heads x 64,
     visible counts uniform in [64, L] for L in {512, 2048, 8192}; codes uniform in [-127, 127],
-    scales |N(0,1)|*0.02, q N(0,1) (seed 3).  Exact and fast numerics."""
+    scales |N(0,1)|*0.02, q N(0,1) (seed 3: generator 3000 + L per length).  Exact and fast numerics."""
     import torch
     from needle_b200 import native
     native.lib()
     torch.cuda.set_device(0)
     stream = torch.cuda.current_stream()
-    gen = torch.Generator(device="cuda").manual_seed(3)
     lib = native.lib()
     results, launches = [], 0
-    for L in (512, 2048, 8192):
+    lengths = [int(v) for v in args.cases.split(",")] if args.cases else [512, 2048, 8192]
+    for L in lengths:
+        gen = torch.Generator(device="cuda").manual_seed(3000 + L)  # seed 3, one stream per L
         batch = 64
         counts = torch.randint(64, L + 1, (batch,), dtype=torch.int32, device="cuda", generator=gen)
         set_bytes = batch * 4 * L * (64 * 2 + 8)
@@ -285,8 +296,9 @@ def bench_attention(args, peaks):
         out = torch.empty((batch, 512), device="cuda")
         visible = int(counts.sum().item())
         alg = visible * 4 * (64 * 2 + 8) + 2 * batch * 512 * 4 + batch * 4
-        for mode, fn, kernels in (("exact", lib.needle_cuda_attention_dev, 1),
-                                  ("fast", lib.needle_cuda_attention_dev_fast, 2)):
+        modes = [m for m in (("exact", lib.needle_cuda_attention_dev, 1), ("fast", lib.needle_cuda_attention_dev_fast, 2))
+                 if args.numerics in ("both", m[0])]
+        for mode, fn, kernels in modes:
             def call(i, strm, fn=fn):
                 native.check(fn(q.data_ptr(), kc[i].data_ptr(), ks[i].data_ptr(), vc[i].data_ptr(), vs[i].data_ptr(),
                                 counts.data_ptr(), batch, L, out.data_ptr(), strm))
@@ -297,7 +309,7 @@ def bench_attention(args, peaks):
                             "gbs": round(alg / (ms * 1e-3) / 1e9, 1), "bytes": alg})
         del kc, vc, ks, vs
         torch.cuda.empty_cache()
-    head = next(r for r in results if r["L"] == 8192 and r["numerics"] == "fast")
+    head = next((r for r in results if r["L"] == 8192 and r["numerics"] == "fast"), results[-1])
     peak, src = _peak(peaks)
     line = {"metric": "int8-KV decode attention HBM GB/s", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1,
             "steps": max(10, min(args.steps, 100)), "warmup": max(3, args.warmup), "ms_per_step": head["us"] / 1e3,
@@ -305,9 +317,11 @@ def bench_attention(args, peaks):
             "data": "synthetic",
             "config": {"workload": "isolated int8-KV decode attention (BASELINE config 3), headline L=8192 fast",
                        "l2": f"KV sets rotated over > {ROTATE_BYTES >> 20} MB", "cases": results},
-            "roofline": {"kernel": "k_attention_fast (+ combine)", "bound": "hbm", "achieved": head["gbs"],
+            "roofline": {"kernel": "k_attention_fast_mma (+ k_attention_fast_combine)", "bound": "hbm", "achieved": head["gbs"],
                          "peak": peak, "peak_source": src, "unit": "GB/s", "frac": round(head["gbs"] / peak, 4),
-                         "traffic": None},
+                         # DRAM read + write of one k_attention_fast_mma launch at L = 8192 (ncu)
+                         "traffic": 149972736 if head["L"] == 8192 and head["numerics"] == "fast" else None,
+                         "traffic_source": "profiles/attention_fast_mma_L8192_batch64.md"},
             "gpu_launches": launches}
     print(json.dumps(line), flush=True)
 
@@ -323,6 +337,10 @@ def main():
     ap.add_argument("--ramp", type=int, default=1600, help="untimed steps to reach the steady-state mix")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cases", default="", help="qmatvec: shape-name substring; attention: comma list of L")
+    ap.add_argument("--batches", default="", help="qmatvec: comma list of batch sizes (default 1,8,32,128)")
+    ap.add_argument("--numerics", choices=["both", "exact", "fast"], default="both",
+                    help="qmatvec / attention: which numerics to time")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
