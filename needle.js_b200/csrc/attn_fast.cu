@@ -196,11 +196,9 @@ __global__ void __launch_bounds__(kFastThreads) k_attention_fast(
 
 // Merges the splits of every (item, KV head): out = sum_s 2^(m_s - M) acc_s / sum_s 2^(m_s - M) l_s,
 // in one pass with a running maximum (the loads of all splits are independent, so they overlap).
-// Launched as a programmatic dependent of the split kernel: it waits for that grid before reading.
 __global__ void __launch_bounds__(kFastThreads) k_attention_fast_combine(const Partial* __restrict__ partials,
                                                                          int32_t splits, float* __restrict__ out,
                                                                          const int32_t* __restrict__ status) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int b = blockIdx.x, h = blockIdx.y;
   if (status && *status) {  // a bounded wait ran out: report NaN rather than a partial sum
     out[(int64_t)b * kHeads * kHeadDim + h * 2 * kHeadDim + threadIdx.x] = NAN;
@@ -360,14 +358,12 @@ __global__ void __launch_bounds__(kMmaThreads) k_attention_fast_mma(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const float* __restrict__ q,
     const float* __restrict__ ks, const float* __restrict__ vs, const int32_t* __restrict__ counts,
     int32_t capacity, int32_t splits, int32_t n_items, Partial* __restrict__ partials, int32_t* __restrict__ status,
-    int32_t* __restrict__ work) {
+    int32_t* __restrict__ work, int32_t* __restrict__ done) {
   extern __shared__ unsigned char smem_raw[];
   MmaStage* stage = reinterpret_cast<MmaStage*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[kMmaStages], empty[kMmaStages];
   __shared__ Partial warp_part[kMmaConsumers];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // The combine kernel may be scheduled at once: its griddepcontrol.wait still waits for this grid.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) {
     for (int i = 0; i < kMmaStages; i++) {
       mbar_init(&full[i], 1);
@@ -437,6 +433,14 @@ __global__ void __launch_bounds__(kMmaThreads) k_attention_fast_mma(
       // for the last tile issued into each stage.
       for (int i = max(0, seq - kMmaStages); i < seq; i++)
         if (!mbar_wait(&full[i % kMmaStages], (i / kMmaStages) & 1)) atomicExch(status, 1);
+      // The last CTA to stop claiming work resets the counters for the next call (no CTA claims
+      // any more once its claim failed, so nothing races with the reset).
+      __threadfence();
+      if (atomicAdd(done, 1) == (int)(gridDim.x - 1)) {
+        *work = 0;
+        *done = 0;
+        __threadfence();
+      }
     }
     return;
   }
@@ -666,7 +670,7 @@ bool encode_rows_map(CUtensorMap* map, const int8_t* base, int64_t rows) {
 
 size_t attention_fast_scratch_bytes(int32_t batch, int32_t capacity) {
   const int splits = (capacity + kSplit - 1) / kSplit;
-  return 16 + sizeof(Partial) * (size_t)batch * kKvHeads * splits;  // status, work counter, partials
+  return 16 + sizeof(Partial) * (size_t)batch * kKvHeads * splits;  // status and counters, partials
 }
 
 cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
@@ -676,8 +680,10 @@ cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float*
   const int splits = (capacity + kSplit - 1) / kSplit;
   int32_t* status = static_cast<int32_t*>(scratch);
   Partial* parts = reinterpret_cast<Partial*>(static_cast<char*>(scratch) + 16);
-  cudaError_t e = cudaMemsetAsync(status, 0, 2 * sizeof(int32_t), s);  // status, work counter
-  if (e != cudaSuccess) return e;
+  // status (sticky: once a bounded wait has run out the operator reports NaN), work counter and
+  // done counter live at the start of the scratch, zeroed when it was allocated; the persistent
+  // kernel leaves the counters at zero.
+  cudaError_t e = cudaSuccess;
   // The tensor and bulk copies need 16-byte aligned sources and sizes: rows are 64 bytes, and the
   // scale copies are whole 16-byte units when capacity is a multiple of 4.
   const int64_t rows_total = (int64_t)batch * kKvHeads * capacity;
@@ -706,23 +712,15 @@ cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float*
     const int n_items = batch * kKvHeads * splits;
     const int grid = std::max(1, std::min(n_items, sms * per_sm[device & 63]));
     k_attention_fast_mma<<<grid, kMmaThreads, smem, s>>>(kmap, vmap, q, ks, vs, counts, capacity, splits, n_items,
-                                                         parts, status, status + 1);
+                                                         parts, status, status + 1, status + 2);
   } else {
     k_attention_fast<<<dim3(batch, kKvHeads, splits), kFastThreads, 0, s>>>(q, kc, ks, vc, vs, counts, capacity,
                                                                            splits, parts);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(batch, kKvHeads);
-  cfg.blockDim = dim3(kFastThreads);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_attention_fast_combine, (const Partial*)parts, splits, out, (const int32_t*)status);
+  k_attention_fast_combine<<<dim3(batch, kKvHeads), kFastThreads, 0, s>>>(parts, splits, out, status);
+  return cudaGetLastError();
 }
 
 }  // namespace needle

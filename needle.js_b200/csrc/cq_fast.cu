@@ -24,14 +24,18 @@
 // j mod 32 whatever b is; lanes walk their chunks and bytes from lane-specific starting points,
 // which makes the 32 lanes of every step read 32 different j -- no bank conflicts for any weights.
 //
-// Reduction: each block writes the group dot per (group, row) to scratch, and k_cq_fast_reduce --
-// a programmatic dependent launch, so its launch overlaps the GEMV's tail -- sums norm * dot over
-// the groups of every row in a fixed order; the result does not depend on scheduling.
+// Reduction: each block writes the group dot per (group, row) to scratch, and k_cq_fast_reduce sums
+// norm * dot over the groups of every row in a fixed order; the result does not depend on
+// scheduling.  (Fusing it behind a grid barrier in a cooperative launch measured slower: the
+// cooperative launch costs more than the second kernel.)
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 
 #include "cq.cuh"
 
@@ -42,6 +46,10 @@ namespace {
 constexpr int kTabThreads = 256;                 // 8 warps, two CTAs per SM
 constexpr int kTabStride = 64;                   // floats per table byte-row
 constexpr int kTabFloats = 256 * kTabStride;     // 64 KB
+constexpr int kRing = 3;                         // 32-row weight blocks per warp in its copy ring
+constexpr int kSlotBytes = 2048;                 // one block: 32 rows x 64 bytes (CQ4) or 32 bytes
+constexpr int kRingBytes = kRing * kSlotBytes * (kTabThreads / 32);  // 48 KB per CTA
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a copy wait gives up after 2 s
 
 template <int BITS>
 struct TabGeom {
@@ -162,15 +170,47 @@ __device__ __forceinline__ float lookup16(const char* __restrict__ Tc, const uin
   return lo + hi;
 }
 
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase with the given parity; false once kWaitLimitNs has passed without it.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t start;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
+  for (;;) {
+    for (int i = 0; i < 32; i++)
+      if (mbar_try_wait(bar, parity)) return true;
+    uint64_t now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (now - start > kWaitLimitNs) return false;
+  }
+}
+
 template <int BITS>
 __global__ void __launch_bounds__(kTabThreads, 2) k_cq_gemv_table(
-    const uint8_t* __restrict__ packed, int32_t rows, int32_t input_size, int32_t in_pad, int32_t row_bytes,
+    const __grid_constant__ CUtensorMap wmap, int32_t rows, int32_t input_size, int32_t in_pad,
     const float* __restrict__ x, int32_t x_stride, Codebook cb, float* __restrict__ partials) {
   using G = TabGeom<BITS>;
   constexpr int NCH = G::chunks;
   constexpr int kWarps = kTabThreads / 32;
-  extern __shared__ __align__(16) float T[];  // kTabFloats
+  constexpr uint32_t kBlockBytes = 32u * G::group_bytes;
+  // Dynamic shared memory: the warps' weight rings (512-byte aligned, as the swizzled copies need),
+  // then the table.
+  extern __shared__ __align__(16) unsigned char dyn_smem[];
   __shared__ float lut[16];
+  __shared__ __align__(8) uint64_t full[kWarps][kRing];
+  float* T = reinterpret_cast<float*>(dyn_smem + ((((smem_u32(dyn_smem) + 511u) & ~511u) - smem_u32(dyn_smem)) +
+                                                  kRingBytes));  // kTabFloats
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int item = blockIdx.y;
   const int groups = in_pad / kGroup;
@@ -194,9 +234,23 @@ __global__ void __launch_bounds__(kTabThreads, 2) k_cq_gemv_table(
     lut[tid] = v;
   }
 
-  // The dependent reduction may be scheduled at once: its griddepcontrol.wait still waits for this
-  // whole grid to complete, and this grid is a single wave, so its CTAs only take spare slots.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (lane == 0) {
+    for (int r = 0; r < kRing; r++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[warp][r])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // Per-warp ring of 32-row weight blocks filled by the tensor-copy engine (box: the group's bytes
+  // of 32 rows; rows past the matrix read as zeros).  Lane i reads row i: 16-byte chunk c sits at
+  // slot c ^ ((i >> 1) & 3) (64-byte swizzle, CQ4) or c ^ ((i >> 2) & 1) (32-byte swizzle, CQ2 /
+  // ternary), so the chunk reads of eight consecutive lanes hit eight distinct bank groups.
+  const uint32_t ring0 = (smem_u32(dyn_smem) + 511u) & ~511u;
+  const uint32_t ring_base = ring0 + (uint32_t)warp * kRing * kSlotBytes;
+  const uint32_t row_off = (uint32_t)lane * G::group_bytes;
+  const int swz = BITS == 4 ? (lane >> 1) & 3 : (lane >> 2) & 1;
+  // Blocks this warp has issued / consumed, in the same order: block n uses ring slot n % kRing and
+  // completes that slot's phase (n / kRing) & 1.
+  int issued = 0, uses = 0;
+  bool failed = false;
 
   // Lane geometry (constant for the kernel).  Lane i owns row i of a 32-row block: its NCH 16-byte
   // chunks of the group, walked in the order (i + p) mod NCH, each starting at byte rot = i / 2.
@@ -223,52 +277,69 @@ __global__ void __launch_bounds__(kTabThreads, 2) k_cq_gemv_table(
     const int g = (int)(seg / nblk);
     const int64_t seg_end = min(b_end, (int64_t)(g + 1) * nblk);
     const int rb0 = (int)(seg - (int64_t)g * nblk), nseg = (int)(seg_end - seg);
-    const uint8_t* gbase = packed + g * G::group_bytes;
-    // this lane's chunks of block k in walking order; the last block's missing rows read row
-    // rows - 1 (in bounds, never stored)
-    auto load = [&](int k, uint4* c) {
-      const int row = min((rb0 + k) * 32 + lane, rows - 1);
-      const uint4* src = reinterpret_cast<const uint4*>(gbase + (int64_t)row * row_bytes);
-#pragma unroll
-      for (int ph = 0; ph < NCH; ph++) c[ph] = __ldg(src + (lane + ph) % NCH);
+    // lane 0 copies the warp's j-th block of the segment (block warp + j * kWarps) into the next
+    // ring slot; that slot's previous block has been read by every lane (the __syncwarp before)
+    auto issue = [&](int j) {
+      const int k = warp + j * kWarps;
+      if (k >= nseg || failed) return;
+      const int slot = issued % kRing;
+      issued++;
+      if (lane != 0) return;
+      const uint32_t bar = smem_u32(&full[warp][slot]);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kBlockBytes) : "memory");
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+              ring_base + (uint32_t)slot * kSlotBytes),
+          "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(g * G::group_bytes), "r"((rb0 + k) * 32), "r"(bar)
+          : "memory");
     };
-    auto process = [&](int k, const uint4* c) {
-      float sum = 0.0f;
 #pragma unroll
-      for (int ph = 0; ph < NCH; ph++) {
-        uint32_t o[4];
-        rotate16(c[ph], rot, o);
-        sum += lookup16(Tc, o, pk[ph]);
-      }
-      const int row = (rb0 + k) * 32 + lane;
-      if (row < rows) part[(int64_t)g * rows + row] = sum;
-    };
-    uint4 A[NCH], B[NCH];
-    int k = warp;
-    if (k < nseg) load(k, A);  // in flight during the table build
+    for (int j = 0; j < kRing - 1; j++) issue(j);  // in flight during the table build
     float xv[4];
     prepare_group(x, input_size, g, xv);
-    __syncthreads();  // every warp is done with the previous table (and lut is written)
+    __syncthreads();  // every warp is done with the previous table (and lut / barriers are set)
     build_table<BITS>(xv, lut, T);
     __syncthreads();
-    // two register buffers in turn: the next block is in flight while one is looked up
-    while (k < nseg) {
-      if (k + kWarps < nseg) load(k + kWarps, B);
-      process(k, A);
-      k += kWarps;
-      if (k >= nseg) break;
-      if (k + kWarps < nseg) load(k + kWarps, A);
-      process(k, B);
-      k += kWarps;
+    for (int j = 0; warp + j * kWarps < nseg; j++) {
+      __syncwarp();
+      issue(j + kRing - 1);
+      const int slot = uses % kRing;
+      // A copy that has not landed within kWaitLimitNs stops this warp's copies; its remaining
+      // rows get NaN partials, so the row totals report the failure instead of stale values.
+      if (!failed) failed = !__all_sync(0xffffffffu, mbar_wait(&full[warp][slot], (uint32_t)((uses / kRing) & 1)));
+      float sum = NAN;
+      if (!failed) {
+        uses++;
+        const uint32_t src = ring_base + (uint32_t)slot * kSlotBytes + row_off;
+        sum = 0.0f;
+#pragma unroll
+        for (int ph = 0; ph < NCH; ph++) {
+          const int c = (lane + ph) % NCH;
+          uint4 v;
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                       : "r"(src + 16u * (uint32_t)(c ^ swz))
+                       : "memory");
+          uint32_t o[4];
+          rotate16(v, rot, o);
+          sum += lookup16(Tc, o, pk[ph]);
+        }
+      }
+      const int row = (rb0 + warp + j * kWarps) * 32 + lane;
+      if (row < rows) part[(int64_t)g * rows + row] = sum;
     }
     seg = seg_end;
+  }
+  if (failed && lane == 0) {
+    // Copies still landing in this warp's ring must finish before the CTA retires: wait (bounded)
+    // for the blocks issued and not consumed.
+    for (int n = uses; n < issued; n++) mbar_wait(&full[warp][n % kRing], (uint32_t)((n / kRing) & 1));
   }
 }
 
 // Row totals: y[row] = sum_g norm16[row][g] * partials[g][row], groups in a fixed order (four
-// interleaved chains combined in a fixed order).  Launched as a programmatic dependent of
-// k_cq_gemv_table: it is scheduled while that grid drains and waits for its completion before
-// reading.
+// interleaved chains combined in a fixed order).
 constexpr int kReduceRows = 64;
 constexpr int kReduceThreads = 256;
 __global__ void __launch_bounds__(kReduceThreads) k_cq_fast_reduce(const float* __restrict__ partials,
@@ -276,7 +347,6 @@ __global__ void __launch_bounds__(kReduceThreads) k_cq_fast_reduce(const float* 
                                                                    int32_t groups, float* __restrict__ y,
                                                                    int32_t y_stride) {
   __shared__ float red[kReduceThreads];
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   constexpr int kSub = kReduceThreads / kReduceRows;
   const int tid = threadIdx.x, item = blockIdx.y;
   const int r = blockIdx.x * kReduceRows + (tid % kReduceRows), sub = tid / kReduceRows;
@@ -284,10 +354,14 @@ __global__ void __launch_bounds__(kReduceThreads) k_cq_fast_reduce(const float* 
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   if (r < rows) {
     const uint16_t* nr = norms + (int64_t)r * groups;
-    int gg = sub, k = 0;
-#pragma unroll 4
-    for (; gg < groups; gg += kSub, k++)
-      acc[k & 3] += __half2float(__ushort_as_half(__ldg(nr + gg))) * __ldcg(part + (int64_t)gg * rows + r);
+    for (int gg = sub; gg < groups; gg += 4 * kSub) {
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int gk = gg + k * kSub;
+        if (gk < groups)
+          acc[k] += __half2float(__ushort_as_half(__ldg(nr + gk))) * __ldcg(part + (int64_t)gk * rows + r);
+      }
+    }
   }
   red[tid] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   __syncthreads();
@@ -299,17 +373,41 @@ __global__ void __launch_bounds__(kReduceThreads) k_cq_fast_reduce(const float* 
   }
 }
 
+// 2D map of a packed CQ matrix [rows][row_bytes] with boxes of one group's bytes x 32 rows, 64-byte
+// (CQ4) or 32-byte (CQ2 / ternary) swizzle.  The encoder comes from the driver through the
+// runtime's entry-point query.
+bool encode_weight_map(CUtensorMap* map, const uint8_t* packed, int64_t rows, int64_t row_bytes, int group_bytes) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult found{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &found) == cudaSuccess &&
+        found == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)group_bytes, 32u};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(packed), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, group_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BITS>
 cudaError_t launch_table(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
                          int32_t in_pad, const float* x, int32_t batch, float* y, const Codebook& cb,
                          float* partials, cudaStream_t s) {
+  using G = TabGeom<BITS>;
   static std::atomic<uint64_t> configured{0};
   static int per_sm[64] = {0};
   int device = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return e;
-  const size_t smem = sizeof(float) * kTabFloats;
+  const size_t smem = sizeof(float) * kTabFloats + kRingBytes + 512;  // + ring alignment slack
   const uint64_t bit = 1ull << (device & 63);
   if (!(configured.load() & bit)) {
     e = cudaFuncSetAttribute(k_cq_gemv_table<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -323,6 +421,8 @@ cudaError_t launch_table(const uint8_t* packed, const uint16_t* norms, int32_t r
   const int64_t total = (int64_t)groups * ((rows + 31) / 32);
   const int pb = BITS == kTernaryBits ? 2 : BITS;
   const int row_bytes = in_pad * pb / 8;
+  CUtensorMap wmap;
+  if (!encode_weight_map(&wmap, packed, rows, row_bytes, G::group_bytes)) return cudaErrorInvalidValue;
   for (int b0 = 0; b0 < batch; b0 += kFastMaxItems) {
     const int nb = std::min(kFastMaxItems, batch - b0);
     const int slots = sms * per_sm[device & 63];
@@ -330,22 +430,15 @@ cudaError_t launch_table(const uint8_t* packed, const uint16_t* norms, int32_t r
     // each) and, beyond that, at least one block per warp
     const int64_t want = std::max<int64_t>(groups, (total + kTabThreads / 32 - 1) / (kTabThreads / 32));
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>({total, want, (int64_t)std::max(1, slots / nb)}));
+    const float* xb = x + (int64_t)b0 * input_size;
     float* yb = y + (int64_t)b0 * rows;
-    k_cq_gemv_table<BITS><<<dim3(grid, nb), kTabThreads, smem, s>>>(
-        packed, rows, input_size, in_pad, row_bytes, x + (int64_t)b0 * input_size, input_size, cb, partials);
+    k_cq_gemv_table<BITS><<<dim3(grid, nb), kTabThreads, smem, s>>>(wmap, rows, input_size, in_pad, xb,
+                                                                     input_size, cb, partials);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((rows + kReduceRows - 1) / kReduceRows, nb);
-    cfg.blockDim = dim3(kReduceThreads);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, k_cq_fast_reduce, (const float*)partials, norms, rows, groups, yb, rows);
+    k_cq_fast_reduce<<<dim3((rows + kReduceRows - 1) / kReduceRows, nb), kReduceThreads, 0, s>>>(
+        partials, norms, rows, groups, yb, rows);
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

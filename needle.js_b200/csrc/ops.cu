@@ -57,6 +57,7 @@ cudaError_t attn_scratch_for(int device, size_t bytes, void** out) {
       s.floats = 0;
     }
     cudaError_t e = cudaMalloc(&s.ptr, floats * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(s.ptr, 0, 16);  // status and work counters start at zero
     if (e != cudaSuccess) return e;
     s.floats = floats;
   }
@@ -255,7 +256,8 @@ extern "C" int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const f
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   float* partials = nullptr;
-  if (e == cudaSuccess) e = scratch_for(device, cq_gemv_fast_partial_floats(m->rows, in_pad), &partials);
+  const size_t floats = cq_gemv_fast_partial_floats(m->rows, in_pad);
+  if (e == cudaSuccess) e = scratch_for(device, floats, &partials);
   if (e == cudaSuccess)
     e = launch_cq_gemv_fast(m->packed, m->norms, m->rows, m->input_size, m->bits, x, batch, y, cb, partials, s);
   if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));

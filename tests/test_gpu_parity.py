@@ -398,3 +398,4 @@ def test_cq_matvec_dev_fast_within_tolerance(torch_cuda, oracle, bits, rows, inp
         want = m.matvec(x[b]).astype(np.float64)
         tol = 2e-6 * np.sqrt(inputs) * np.max(np.abs(want)) + 1e-6
         assert np.max(np.abs(y[b] - want)) <= tol, (b, np.max(np.abs(y[b] - want)), tol)
+
