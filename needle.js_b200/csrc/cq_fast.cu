@@ -338,18 +338,20 @@ __global__ void __launch_bounds__(kTabThreads, 2) k_cq_gemv_table(
   }
 }
 
-// Row totals: y[row] = sum_g norm16[row][g] * partials[g][row], groups in a fixed order (four
-// interleaved chains combined in a fixed order).
-constexpr int kReduceRows = 64;
+// Row totals: y[row] = sum_g norm16[row][g] * partials[g][row].  16 rows per CTA, 16 threads per row
+// each summing every 16th group (so a 64-group row costs each thread four independent loads), the
+// 16 partial sums combined in a fixed order: the result does not depend on scheduling.
+constexpr int kReduceRows = 16;
 constexpr int kReduceThreads = 256;
 __global__ void __launch_bounds__(kReduceThreads) k_cq_fast_reduce(const float* __restrict__ partials,
                                                                    const uint16_t* __restrict__ norms, int32_t rows,
                                                                    int32_t groups, float* __restrict__ y,
                                                                    int32_t y_stride) {
-  __shared__ float red[kReduceThreads];
   constexpr int kSub = kReduceThreads / kReduceRows;
+  __shared__ float red[kSub][kReduceRows];
   const int tid = threadIdx.x, item = blockIdx.y;
-  const int r = blockIdx.x * kReduceRows + (tid % kReduceRows), sub = tid / kReduceRows;
+  const int rl = tid % kReduceRows, sub = tid / kReduceRows;
+  const int r = blockIdx.x * kReduceRows + rl;
   const float* part = partials + (int64_t)item * groups * rows;
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   if (r < rows) {
@@ -363,12 +365,12 @@ __global__ void __launch_bounds__(kReduceThreads) k_cq_fast_reduce(const float* 
       }
     }
   }
-  red[tid] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  red[sub][rl] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   __syncthreads();
   if (sub == 0 && r < rows) {
-    float v = red[tid];
+    float v = red[0][rl];
 #pragma unroll
-    for (int k = 1; k < kSub; k++) v += red[tid + k * kReduceRows];
+    for (int k = 1; k < kSub; k++) v += red[k][rl];
     y[(int64_t)item * y_stride + r] = v;
   }
 }
