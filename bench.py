@@ -206,6 +206,19 @@ def _time_calls(torch, stream, fn, n_sets, warmup, iters):
     return e0.elapsed_time(e1) / iters
 
 
+def fast_matvec_kernels(rows: int, inputs: int, batch: int, sms: int = 148) -> int:
+    """Kernel launches of one needle_cuda_cq_matvec_dev_fast call: table GEMV + row totals per 8
+    items below 16 items; from 16 items the tensor-core GEMM: activation prepare + GEMM (+ split-K
+    sum when the groups are split across CTAs) per 128 items."""
+    if batch < 16:
+        return 2 * -(-batch // 8)
+    m_tiles, groups = -(-rows // 128), -(-inputs // 128)
+    splits = max(1, min(groups, sms // m_tiles))
+    per = -(-groups // splits)
+    used = -(-groups // per)
+    return (3 if used > 1 else 2) * -(-batch // 128)
+
+
 def bench_qmatvec(args, peaks):
     """isolated quantised matvec, every projection shape + 8192x8192, batch
     1/8/32/128; indices uniform, fp16 norms |N(0,1)|*0.01, activations N(0,1) (seed 2: generator
@@ -239,7 +252,7 @@ def bench_qmatvec(args, peaks):
             if args.numerics in ("both", "exact"):
                 modes.append(("exact", lib.needle_cuda_cq_matvec_dev, 3 if (batch <= 8 and pad // 128 >= 16) else 2))
             if bits in (2, 4, 5) and args.numerics in ("both", "fast"):
-                modes.append(("fast", lib.needle_cuda_cq_matvec_dev_fast, 2 * -(-batch // 8)))
+                modes.append(("fast", lib.needle_cuda_cq_matvec_dev_fast, fast_matvec_kernels(rows, inputs, batch)))
             for mode, fn, kernels in modes:
                 def call(i, strm, fn=fn):
                     native.check(fn(C.byref(descs[i]), native.ptr(cb), x.data_ptr(), batch, y.data_ptr(), strm))

@@ -17,7 +17,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libneedle_cuda.so")
-SOURCES = ["engine.cu", "cq.cu", "layer.cu", "ops.cu", "attn_fast.cu", "cq_fast.cu"]
+SOURCES = ["engine.cu", "cq.cu", "layer.cu", "ops.cu", "attn_fast.cu", "cq_fast.cu", "cq_gemm_tc.cu"]
 HEADERS = ["common.cuh", "cq.cuh", "engine.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "--fmad=false", "-std=c++17", "--extended-lambda", "-Xcompiler", "-fPIC",

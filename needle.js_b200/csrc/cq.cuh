@@ -60,6 +60,15 @@ size_t cq_gemv_fast_partial_floats(int32_t rows, int32_t in_pad);
 cudaError_t launch_cq_gemv_fast(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
                                 int32_t bits, const float* x, int32_t batch, float* y, const Codebook& cb,
                                 float* partials, cudaStream_t s);
+// Batched fast-numerics matvec on the tensor cores (cq_gemm_tc.cu): bf16 head/tail split GEMM,
+// record widths 2, 4 and ternary.  Scratch (cq_gemm_tc_scratch_bytes, 256-byte aligned): the
+// prepared activations and split-K partials; up to 128 items per pass.
+constexpr int kTcMinBatch = 16;
+bool cq_gemm_tc_supported(int32_t bits);
+size_t cq_gemm_tc_scratch_bytes(int32_t rows, int32_t input_size, int32_t batch, int32_t sms);
+cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
+                              int32_t bits, const float* x, int32_t batch, float* y, const Codebook& cb, void* scratch,
+                              int32_t sms, cudaStream_t s);
 cudaError_t launch_cq_rows(const uint8_t* packed, const uint16_t* norms, int32_t bits,
                            int32_t row_bytes, int32_t in_pad, int32_t input_size,
                            const int32_t* rows, int32_t n_rows, float* out, int32_t out_stride,
@@ -98,6 +107,39 @@ __device__ __forceinline__ double cq_level(const float* cb28, int bits, int inde
   }
   const int base = bits == 2 ? 0 : bits == 3 ? 4 : 12;
   return (double)cb28[base + index];
+}
+
+// x' of one group: zero padding, FWHT (binary32 butterflies, strides 1, 2, 4, ...), times
+// 1/sqrt(128) in binary64 rounded to binary32 (prepareCqActivation, cq.ts:30-46).  Every warp
+// computes it (four values per lane: lane l holds x'[4l .. 4l+3]), so no barrier is needed.
+__device__ __forceinline__ void prepare_group_warp(const float* __restrict__ x, int input_size, int g, float v[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int col = g * kGroup + 4 * lane + k;
+    v[k] = col < input_size ? __ldg(x + col) : 0.0f;
+  }
+  // strides 1 and 2 inside the lane
+  {
+    const float a0 = __fadd_rn(v[0], v[1]), a1 = __fsub_rn(v[0], v[1]);
+    const float a2 = __fadd_rn(v[2], v[3]), a3 = __fsub_rn(v[2], v[3]);
+    v[0] = __fadd_rn(a0, a2);
+    v[2] = __fsub_rn(a0, a2);
+    v[1] = __fadd_rn(a1, a3);
+    v[3] = __fsub_rn(a1, a3);
+  }
+  // strides 4 .. 64 across lanes
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[k], m);
+      v[k] = (lane & m) ? __fsub_rn(other, v[k]) : __fadd_rn(v[k], other);
+    }
+  }
+  const double inverse_root = 1.0 / sqrt((double)kGroup);
+#pragma unroll
+  for (int k = 0; k < 4; k++) v[k] = f32((double)v[k] * inverse_root);
 }
 
 }  // namespace needle

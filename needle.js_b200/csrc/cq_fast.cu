@@ -58,39 +58,6 @@ struct TabGeom {
   static constexpr int chunks = group_bytes / 16;                // 16-byte chunks per group row: 4 or 2
 };
 
-// x' of one group: zero padding, FWHT (binary32 butterflies, strides 1, 2, 4, ...), times
-// 1/sqrt(128) in binary64 rounded to binary32 (prepareCqActivation, cq.ts:30-46).  Every warp
-// computes it (four values per lane: lane l holds x'[4l .. 4l+3]), so no barrier is needed.
-__device__ __forceinline__ void prepare_group(const float* __restrict__ x, int input_size, int g, float v[4]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int k = 0; k < 4; k++) {
-    const int col = g * kGroup + 4 * lane + k;
-    v[k] = col < input_size ? __ldg(x + col) : 0.0f;
-  }
-  // strides 1 and 2 inside the lane
-  {
-    const float a0 = __fadd_rn(v[0], v[1]), a1 = __fsub_rn(v[0], v[1]);
-    const float a2 = __fadd_rn(v[2], v[3]), a3 = __fsub_rn(v[2], v[3]);
-    v[0] = __fadd_rn(a0, a2);
-    v[2] = __fsub_rn(a0, a2);
-    v[1] = __fadd_rn(a1, a3);
-    v[3] = __fsub_rn(a1, a3);
-  }
-  // strides 4 .. 64 across lanes
-#pragma unroll
-  for (int m = 1; m < 32; m <<= 1) {
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const float other = __shfl_xor_sync(0xffffffffu, v[k], m);
-      v[k] = (lane & m) ? __fsub_rn(other, v[k]) : __fadd_rn(v[k], other);
-    }
-  }
-  const double inverse_root = 1.0 / sqrt((double)kGroup);
-#pragma unroll
-  for (int k = 0; k < 4; k++) v[k] = f32((double)v[k] * inverse_root);
-}
-
 template <int BITS>
 __device__ __forceinline__ void build_table(const float v[4], const float* __restrict__ lut, float* __restrict__ T) {
   const int t = threadIdx.x;
@@ -297,7 +264,7 @@ __global__ void __launch_bounds__(kTabThreads, 2) k_cq_gemv_table(
 #pragma unroll
     for (int j = 0; j < kRing - 1; j++) issue(j);  // in flight during the table build
     float xv[4];
-    prepare_group(x, input_size, g, xv);
+    prepare_group_warp(x, input_size, g, xv);
     __syncthreads();  // every warp is done with the previous table (and lut / barriers are set)
     build_table<BITS>(xv, lut, T);
     __syncthreads();

@@ -1,0 +1,498 @@
+// cq_gemm_tc.cu -- batched fast-numerics Cactus-Quant matvec on the 5th-generation tensor cores
+// (tcgen05.mma, weight operand and accumulator in tensor memory).  cqMatvec
+// (packages/needle.js/src/backends/cq.ts:233-240) for a batch of B vectors, in binary32 accuracy:
+//
+//   y[b][r] = sum_g norm16[r][g] * sum_{k in g} level(code[r][k]) * x'[b][k]
+//
+// is a GEMM with A = the dequantised weights (rows x inputs; each element is level * norm of its
+// group, folded in while decoding) and B = the prepared activations x' (B x inputs).  The tensor
+// cores multiply bf16; to keep binary32-level accuracy each operand is split into a bf16 head and
+// a bf16 tail (v = hi + lo up to 2^-17 |v|) and the product is accumulated as
+// A_hi B_hi + A_hi B_lo + A_lo B_hi in fp32 (the dropped A_lo B_lo term is below 2^-16 relative).
+// Two MMAs per K-step do it: A_hi x [B_hi; B_lo] (N' = 2N: columns [0, N) get A_hi B_hi and
+// [N, 2N) A_hi B_lo) and A_lo x B_hi into columns [0, N); the epilogue adds the two column blocks.
+//
+// Kernels.  k_cq_prep_bf16 writes x' of every (group, item) as bf16 head and tail rows already in
+// the shared-memory layout the MMA reads (K-major, 128-byte swizzle; per group and 64-column half
+// the N head rows then the N tail rows), so the GEMM fetches a group's activations with one bulk
+// copy.  k_cq_gemm_tc: one CTA per (128-row tile, range of groups) and SM; the groups are split
+// across CTAs (split-K) when there are fewer row tiles than SMs, and k_splitk_sum adds the splits'
+// partial results in a fixed order.
+//
+// k_cq_gemm_tc is warp-specialised around a ring of group slots (A operand in tensor memory,
+// activations in shared memory; 3 slots for N <= 64, 2 above):
+//   * decode warps 0-11, three teams of four (team t takes groups t, t + S, ... for S slots, so that
+//     each slot is used in one team's program order; warp w serves tensor-memory lanes
+//     32 (w % 4) ..+31, one tile row per thread).  Per group a thread turns its
+//     row's norm into a 16-entry table of split values (level * norm as bf16 head | tail), decodes
+//     the row's 128 weights with one table read each and writes the head and tail words into tensor
+//     memory (tcgen05.st); its packed bytes were loaded two of its groups earlier.
+//   * warp 12 (one elected lane, the warp converged) issues a group's 8 K-steps x 2 MMAs and commits
+//     them to the slot's "empty" barrier, which frees the slot for the decoders and the producer.
+//   * warp 13 (one thread) bulk-copies the groups' activation tiles into the ring.
+// Every mbarrier wait gives up after 2 s and marks the tile failed (its outputs become NaN).  The
+// epilogue reads the accumulator with tcgen05.ld (decode warps, one row per lane).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "cq.cuh"
+
+namespace needle {
+
+namespace {
+
+constexpr int kTcTeams = 3;                 // decode teams of 4 warps (one per tensor-memory lane quarter)
+constexpr int kTcDecodeWarps = 4 * kTcTeams;
+constexpr int kTcDecodeThreads = kTcDecodeWarps * 32;
+constexpr int kTcMmaWarp = kTcDecodeWarps, kTcCopyWarp = kTcDecodeWarps + 1;
+constexpr int kTcThreads = kTcDecodeThreads + 64;
+constexpr int kTcM = 128;                   // rows per tile (MMA M)
+constexpr int kTcMaxN = 128;                // items per pass (MMA N, multiple of 16)
+constexpr int kTcMaxSlots = 3;
+constexpr uint32_t kTcCols = 512;           // tensor memory: accumulator, then the A slots (128 columns)
+constexpr int kTcPrefetch = 2;              // groups of packed bytes in flight per decode thread
+constexpr uint64_t kTcWaitNs = 2000000000ull;  // an mbarrier wait gives up after 2 s
+constexpr size_t kTcTableBytes = 16 * kTcDecodeThreads * 4;  // per-thread split tables [code][thread]
+// Smallest dynamic shared memory per CTA: more than half an SM's, so that no two CTAs share an SM
+// (each holds all 512 tensor-memory columns).
+constexpr size_t kTcMinSmem = 120 * 1024;
+
+// Accumulator columns (2N rounded up) and ring slots for N items.
+__host__ __device__ __forceinline__ int tc_acc_cols(int N) { return N <= 64 ? 128 : 256; }
+__host__ __device__ __forceinline__ int tc_slots(int N) { return N <= 64 ? 3 : 2; }
+
+// Byte offset of bf16 element (row, k) (k < 64) in a K-major, 128-byte-swizzled tile.
+__host__ __device__ __forceinline__ uint32_t sw128(int row, int k) {
+  return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + (((k >> 3) ^ (row & 7)) << 4) + (k & 7) * 2);
+}
+
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart,
+// descriptor version 1.  The K offset inside the swizzle atom advances the start address.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t a) {
+  return (uint64_t)((a >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
+         ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: bf16 x bf16 -> fp32, A and B K-major, M = 128, N = n.
+__device__ __forceinline__ uint32_t bf16_idesc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
+}
+
+// D (tensor memory) (+)= A (tensor memory, 128 lanes x 8 columns = 16 bf16 per row) x B^T (shared),
+// issued by one elected lane of a converged warp.
+__device__ __forceinline__ void mma_ts_elect(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
+// Arrive on `bar` once every MMA the warp's elected lane issued so far has completed.
+__device__ __forceinline__ void mma_commit_elect(uint64_t* bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(saddr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void bar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void bar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = saddr(bar);
+  uint64_t start = 0;
+  for (int it = 0;; it++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    uint64_t now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (it == 0) start = now;
+    else if (now - start > kTcWaitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(saddr(bar))
+               : "memory");
+}
+
+// 8 consecutive 32-bit tensor-memory columns of this thread's lane <- v[0..7].
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
+// v[0..7] <- 8 consecutive 32-bit tensor-memory columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// bf16 head and tail of two binary32 values, as bf16x2 words (first value in the low half).
+__device__ __forceinline__ void split2(float v0, float v1, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  const float r0 = __fsub_rn(v0, __uint_as_float(hi << 16));
+  const float r1 = __fsub_rn(v1, __uint_as_float(hi & 0xffff0000u));
+  const __nv_bfloat162 l = __floats2bfloat162_rn(r0, r1);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// x' of (group g, item n) as bf16 head and tail, in the GEMM's activation layout
+// [group][half (2)][2N rows: N head rows, N tail rows][128 bytes], rows swizzled as the MMA's
+// K-major 128-byte layout.  One warp per (group, item); items nb <= n < N are zeros.
+__global__ void __launch_bounds__(256) k_cq_prep_bf16(const float* __restrict__ x, int32_t input_size, int32_t groups,
+                                                      int32_t nb, int32_t N, uint8_t* __restrict__ act) {
+  const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w >= groups * N) return;
+  const int g = w / N, n = w - g * N;
+  float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (n < nb) prepare_group_warp(x + (int64_t)n * input_size, input_size, g, v);
+  uint32_t hi[2], lo[2];
+  split2(v[0], v[1], hi[0], lo[0]);
+  split2(v[2], v[3], hi[1], lo[1]);
+  const int c = 4 * lane, half = c >> 6, k = c & 63;
+  uint8_t* tile = act + ((size_t)g * 2 + half) * (size_t)(2 * N) * 128;
+  *reinterpret_cast<uint2*>(tile + sw128(n, k)) = make_uint2(hi[0], hi[1]);
+  *reinterpret_cast<uint2*>(tile + sw128(N + n, k)) = make_uint2(lo[0], lo[1]);
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
+    const uint8_t* __restrict__ packed, const uint16_t* __restrict__ norms, int32_t rows, int32_t groups,
+    int32_t row_bytes, const uint8_t* __restrict__ act, int32_t N, int32_t nb, int32_t groups_per_split,
+    float* __restrict__ out, int32_t out_stride, int64_t split_stride, Codebook cb) {
+  constexpr int kCodes = BITS == 4 ? 16 : 4;
+  constexpr int kGroupWords = BITS == 4 ? 16 : 8;  // packed 32-bit words of one row's group
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t a_full[kTcMaxSlots];  // 4 decode-warp arrivals
+  __shared__ __align__(8) uint64_t b_full[kTcMaxSlots];  // producer arrival + copied bytes
+  __shared__ __align__(8) uint64_t empty[kTcMaxSlots];   // MMA commit: slot read
+  __shared__ __align__(8) uint64_t acc_full;             // MMA commit: accumulator final
+  __shared__ uint32_t tmem_base;
+  __shared__ float lut[16];
+  __shared__ int s_failed;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int mt = blockIdx.x, split = blockIdx.y;
+  const int g_begin = split * groups_per_split, g_end = min(groups, g_begin + groups_per_split);
+  const int ng = g_end - g_begin;
+  const int nslots = tc_slots(N);
+  const uint32_t acc_cols = (uint32_t)tc_acc_cols(N);
+  const uint32_t half_bytes = (uint32_t)(2 * N) * 128;  // activation tile of one 64-column half
+  const uint32_t group_bytes = 2 * half_bytes;
+  // shared memory: activation ring [slot][half][head rows | tail rows] (1024-aligned), split tables
+  const uint32_t b_sm = (saddr(smem_raw) + 1023u) & ~1023u;
+  uint32_t* table = reinterpret_cast<uint32_t*>(smem_raw + (b_sm - saddr(smem_raw)) + (size_t)nslots * group_bytes);
+
+  if (tid < 16) {
+    float v = 0.0f;
+    if constexpr (BITS == 4) {
+#pragma unroll
+      for (int k = 0; k < 16; k++) v = tid == k ? cb.v[12 + k] : v;
+    } else if constexpr (BITS == 2) {
+#pragma unroll
+      for (int k = 0; k < 4; k++) v = tid == k ? cb.v[k] : v;
+    } else {
+      // ternary crumbs 0..3 are the trits 0, +c, 0, -c (cq_index / cq_level)
+      const float c = f32(kTernaryCentroid * (1.0 / sqrt((double)kGroup)));
+      v = tid == 1 ? c : tid == 3 ? -c : 0.0f;
+    }
+    lut[tid] = v;
+  }
+  if (tid == 0) {
+    for (int i = 0; i < kTcMaxSlots; i++) {
+      bar_init(&a_full[i], 4);
+      bar_init(&b_full[i], 1);
+      bar_init(&empty[i], 1);
+    }
+    bar_init(&acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_failed = 0;
+  }
+  if (warp == kTcMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base)),
+                 "r"(kTcCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+
+  if (warp == kTcCopyWarp) {
+    // ---- producer: activations of group g_begin + gi into slot gi % nslots
+    if (lane == 0) {
+      bool failed = false;
+      int issued = 0;
+      for (int gi = 0; gi < ng; gi++) {
+        const int sl = gi % nslots;
+        if (gi >= nslots && !bar_wait(&empty[sl], (uint32_t)((gi / nslots - 1) & 1))) {
+          failed = true;
+          break;
+        }
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(&b_full[sl])),
+                     "r"(group_bytes)
+                     : "memory");
+        bulk_load(b_sm + sl * group_bytes, act + (size_t)(g_begin + gi) * group_bytes, group_bytes, &b_full[sl]);
+        issued = gi + 1;
+      }
+      if (failed) {
+        atomicExch(&s_failed, 1);
+        // copies may still be landing: wait for the last one of each slot (bounded) before retiring
+        for (int gi = max(0, issued - nslots); gi < issued; gi++)
+          bar_wait(&b_full[gi % nslots], (uint32_t)((gi / nslots) & 1));
+      }
+    }
+    __syncwarp();
+  } else if (warp == kTcMmaWarp) {
+    // ---- MMA issue: the whole warp runs the loop (it stays converged); one elected lane issues
+    const uint32_t idesc2 = bf16_idesc(2 * N), idesc1 = bf16_idesc(N);
+    bool failed = false;
+    for (int gi = 0; gi < ng; gi++) {
+      const int sl = gi % nslots;
+      const uint32_t par = (uint32_t)((gi / nslots) & 1);
+      const bool ok = bar_wait(&b_full[sl], par) && bar_wait(&a_full[sl], par);
+      if (!__all_sync(0xffffffffu, ok)) {
+        failed = true;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a_hi = tmem + acc_cols + sl * 128, a_lo = a_hi + 64;
+      const uint64_t d0 = sw128_desc(b_sm + sl * group_bytes);
+      // K-step kk: 8 A columns; activation half kk / 4 at 32 bytes (2 descriptor units) per step
+#pragma unroll
+      for (int kk = 0; kk < kGroup / 16; kk++) {
+        const uint64_t bd = d0 + (uint64_t)((kk >> 2) * (half_bytes >> 4) + (kk & 3) * 2);
+        mma_ts_elect(tmem, a_hi + kk * 8, bd, idesc2, (gi > 0 || kk > 0) ? 1u : 0u);  // [hh | hl]
+        mma_ts_elect(tmem, a_lo + kk * 8, bd, idesc1, 1u);                            // += lh
+      }
+      mma_commit_elect(&empty[sl]);
+    }
+    if (failed && lane == 0) atomicExch(&s_failed, 1);
+    mma_commit_elect(&acc_full);  // arrives once every MMA issued above has completed
+    __syncwarp();
+  } else {
+    // ---- decode: team t takes groups t, t + teams, ...; thread = one tile row
+    const int team = warp >> 2, quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int grow = mt * kTcM + row;
+    const bool row_ok = grow < rows;
+    const uint8_t* rowp = packed + (int64_t)(row_ok ? grow : 0) * row_bytes;
+    const uint16_t* nrow = norms + (int64_t)(row_ok ? grow : 0) * groups;
+    uint32_t* tab = table + tid;  // entry c of this thread's table at tab[c * kTcDecodeThreads]
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    // one team per ring slot (3, or 2 for N > 64: team 2 then only joins the epilogue), so that the
+    // uses of a slot, and the phases of its barriers, follow one team's program order
+    const int teams = nslots;
+    const int n_mine = team < teams && ng > team ? (ng - team + teams - 1) / teams : 0;
+    uint32_t wr[kTcPrefetch][kGroupWords];
+    float nr[kTcPrefetch];
+    auto load_group = [&](int d, int j) {
+      const int g = g_begin + team + teams * j;
+      const uint4* src = reinterpret_cast<const uint4*>(rowp + (int64_t)g * (kGroupWords * 4));
+#pragma unroll
+      for (int q = 0; q < kGroupWords / 4; q++) {
+        const uint4 u = row_ok ? __ldg(src + q) : make_uint4(0, 0, 0, 0);
+        wr[d][4 * q] = u.x;
+        wr[d][4 * q + 1] = u.y;
+        wr[d][4 * q + 2] = u.z;
+        wr[d][4 * q + 3] = u.w;
+      }
+      nr[d] = row_ok ? __half2float(__ushort_as_half(__ldg(nrow + g))) : 0.0f;
+    };
+#pragma unroll
+    for (int d = 0; d < kTcPrefetch; d++)
+      if (d < n_mine) load_group(d, d);
+    bool failed = false;
+    for (int j0 = 0; j0 < n_mine && !failed; j0 += kTcPrefetch) {
+#pragma unroll
+      for (int d = 0; d < kTcPrefetch; d++) {
+        const int j = j0 + d;
+        if (j >= n_mine || failed) break;
+        const int gi = team + teams * j, sl = team;
+        // split table of this row's group: level * norm as bf16 head | tail, two codes at a time
+#pragma unroll
+        for (int c = 0; c < kCodes; c += 2) {
+          uint32_t h2, l2;
+          split2(__fmul_rn(lut[c], nr[d]), __fmul_rn(lut[c + 1], nr[d]), h2, l2);
+          tab[c * kTcDecodeThreads] = __byte_perm(h2, l2, 0x5410);
+          tab[(c + 1) * kTcDecodeThreads] = __byte_perm(h2, l2, 0x7632);
+        }
+        // pairs 8q .. 8q + 7 (columns 16q .. 16q + 15) of the group as head and tail words
+        auto decode8 = [&](int q, uint32_t* hi, uint32_t* lo) {
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const int p = 8 * q + i;
+            int c0, c1;
+            if constexpr (BITS == 4) {
+              const uint32_t byte = (wr[d][p >> 2] >> (8 * (p & 3))) & 0xFFu;
+              c0 = byte & 15;
+              c1 = byte >> 4;
+            } else {
+              const uint32_t quad = (wr[d][p >> 3] >> (4 * (p & 7))) & 0xFu;
+              c0 = quad & 3;
+              c1 = quad >> 2;
+            }
+            const uint32_t t0 = tab[c0 * kTcDecodeThreads], t1 = tab[c1 * kTcDecodeThreads];
+            hi[i] = __byte_perm(t0, t1, 0x5410);
+            lo[i] = __byte_perm(t0, t1, 0x7632);
+          }
+        };
+        const uint32_t col = lane_addr + acc_cols + sl * 128;
+        uint32_t hi[8], lo[8];
+        decode8(0, hi, lo);
+        if (gi >= nslots) failed = !bar_wait(&empty[sl], (uint32_t)((gi / nslots - 1) & 1));
+        failed = __any_sync(0xffffffffu, failed);  // warp-uniform: tcgen05.st is a warp instruction
+        if (failed) break;
+        tmem_st8(col, hi);
+        tmem_st8(col + 64, lo);
+#pragma unroll
+        for (int q = 1; q < 8; q++) {
+          decode8(q, hi, lo);
+          tmem_st8(col + 8 * q, hi);
+          tmem_st8(col + 64 + 8 * q, lo);
+        }
+        if (j + kTcPrefetch < n_mine) load_group(d, j + kTcPrefetch);  // wr[d] fully used
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) bar_arrive(&a_full[sl]);
+      }
+    }
+    if (failed) atomicExch(&s_failed, 1);
+    // epilogue: wait for the last MMA; this warp's 32 rows x every third 8-column chunk, y = [0, N) + [N, 2N)
+    const bool acc_ok = bar_wait(&acc_full, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    __syncwarp();
+    const bool bad = !acc_ok || *(volatile int*)&s_failed != 0;
+    float* o = out + (int64_t)split * split_stride;
+    for (int c0 = team * 8; c0 < N; c0 += kTcTeams * 8) {
+      uint32_t v[8], w[8];
+      tmem_ld8(lane_addr + (uint32_t)c0, v);
+      tmem_ld8(lane_addr + (uint32_t)(N + c0), w);
+      if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          if (c0 + j < nb)
+            o[(int64_t)(c0 + j) * out_stride + grow] = bad ? NAN : __fadd_rn(__uint_as_float(v[j]), __uint_as_float(w[j]));
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == kTcMmaWarp) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcCols) : "memory");
+  }
+}
+
+// y[n][r] = sum over splits s, in order, of part[s][n][r].
+__global__ void k_splitk_sum(const float* __restrict__ part, int32_t splits, int64_t split_stride, int32_t rows,
+                             int32_t nb, float* __restrict__ y, int32_t y_stride) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)rows * nb) return;
+  const int n = (int)(i / rows), r = (int)(i - (int64_t)n * rows);
+  float v = __ldg(part + i);
+  for (int s = 1; s < splits; s++) v = __fadd_rn(v, __ldg(part + (int64_t)s * split_stride + i));
+  y[(int64_t)n * y_stride + r] = v;
+}
+
+struct TcPlan {
+  int m_tiles, groups, per, used;
+};
+
+TcPlan plan_for(int32_t rows, int32_t in_pad, int sms) {
+  TcPlan p;
+  p.m_tiles = (rows + kTcM - 1) / kTcM;
+  p.groups = in_pad / kGroup;
+  const int splits = std::max(1, std::min(p.groups, sms / p.m_tiles));
+  p.per = (p.groups + splits - 1) / splits;
+  p.used = (p.groups + p.per - 1) / p.per;
+  return p;
+}
+
+}  // namespace
+
+bool cq_gemm_tc_supported(int32_t bits) { return bits == 2 || bits == 4 || bits == kTernaryBits; }
+
+size_t cq_gemm_tc_scratch_bytes(int32_t rows, int32_t input_size, int32_t batch, int32_t sms) {
+  const int in_pad = (input_size + kGroup - 1) / kGroup * kGroup;
+  const int nb = std::min(batch, kTcMaxN);
+  const int N = (nb + 15) / 16 * 16;
+  const TcPlan p = plan_for(rows, in_pad, sms);
+  const size_t act = (size_t)p.groups * 2 * (2 * N) * 128;
+  const size_t part = p.used > 1 ? (size_t)p.used * nb * rows * 4 : 0;
+  return act + part;
+}
+
+cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
+                              int32_t bits, const float* x, int32_t batch, float* y, const Codebook& cb, void* scratch,
+                              int32_t sms, cudaStream_t s) {
+  if (batch <= 0 || rows <= 0) return cudaSuccess;
+  const int in_pad = (input_size + kGroup - 1) / kGroup * kGroup;
+  const int pb = bits == kTernaryBits ? 2 : bits;
+  const int row_bytes = in_pad * pb / 8;
+  const TcPlan p = plan_for(rows, in_pad, sms);
+  uint8_t* act = static_cast<uint8_t*>(scratch);
+  cudaError_t e = cudaSuccess;
+  for (int b0 = 0; b0 < batch; b0 += kTcMaxN) {
+    const int nb = std::min(kTcMaxN, batch - b0);
+    const int N = (nb + 15) / 16 * 16;
+    const size_t act_bytes = (size_t)p.groups * 2 * (2 * N) * 128;
+    const int warps = p.groups * N;
+    k_cq_prep_bf16<<<(warps + 7) / 8, 256, 0, s>>>(x + (int64_t)b0 * input_size, input_size, p.groups, nb, N, act);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    float* part = reinterpret_cast<float*>(act + act_bytes);
+    const int64_t split_stride = (int64_t)nb * rows;
+    const size_t smem = std::max(kTcMinSmem, (size_t)tc_slots(N) * 2 * (2 * N) * 128 + kTcTableBytes + 1024);
+    auto launch = [&](auto kernel) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return;
+      float* o = p.used > 1 ? part : y + (int64_t)b0 * rows;
+      kernel<<<dim3(p.m_tiles, p.used), kTcThreads, smem, s>>>(packed, norms, rows, p.groups, row_bytes, act, N, nb,
+                                                              p.per, o, rows, split_stride, cb);
+      e = cudaGetLastError();
+    };
+    if (bits == 4) launch(k_cq_gemm_tc<4>);
+    else if (bits == 2) launch(k_cq_gemm_tc<2>);
+    else if (bits == kTernaryBits) launch(k_cq_gemm_tc<kTernaryBits>);
+    else return cudaErrorInvalidValue;
+    if (e != cudaSuccess) return e;
+    if (p.used > 1) {
+      const int64_t n = (int64_t)rows * nb;
+      k_splitk_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, p.used, split_stride, rows, nb,
+                                                              y + (int64_t)b0 * rows, rows);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+    }
+  }
+  return cudaSuccess;
+}
+
+}  // namespace needle

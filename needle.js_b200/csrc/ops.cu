@@ -255,6 +255,18 @@ extern "C" int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const f
   for (int i = 0; i < 28; i++) cb.v[i] = codebook[i];
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
+  if (batch >= kTcMinBatch && cq_gemm_tc_supported(m->bits)) {
+    // a real dense contraction: tensor-core GEMM
+    int sms = 0;
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    float* scratch = nullptr;
+    const size_t bytes = cq_gemm_tc_scratch_bytes(m->rows, m->input_size, batch, sms);
+    if (e == cudaSuccess) e = scratch_for(device, (bytes + 3) / 4, &scratch);
+    if (e == cudaSuccess)
+      e = launch_cq_gemm_tc(m->packed, m->norms, m->rows, m->input_size, m->bits, x, batch, y, cb, scratch, sms, s);
+    if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+    return NEEDLE_OK;
+  }
   float* partials = nullptr;
   const size_t floats = cq_gemv_fast_partial_floats(m->rows, in_pad);
   if (e == cudaSuccess) e = scratch_for(device, floats, &partials);
