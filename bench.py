@@ -208,9 +208,9 @@ def _time_calls(torch, stream, fn, n_sets, warmup, iters):
 
 def fast_matvec_kernels(rows: int, inputs: int, batch: int, sms: int = 148) -> int:
     """Kernel launches of one needle_cuda_cq_matvec_dev_fast call: table GEMV + row totals per 8
-    items below 16 items; from 16 items the tensor-core GEMM: activation prepare + GEMM (+ split-K
-    sum when the groups are split across CTAs) per 128 items."""
-    if batch < 16:
+    items below 16 items (6 for matrices of 4M weights and more); above, the tensor-core GEMM:
+    activation prepare + GEMM (+ split-K sum when the groups are split across CTAs) per 128 items."""
+    if batch < 16 and not (batch >= 6 and rows * (-(-inputs // 128) * 128) >= 1 << 22):
         return 2 * -(-batch // 8)
     m_tiles, groups = -(-rows // 128), -(-inputs // 128)
     splits = max(1, min(groups, sms // m_tiles))

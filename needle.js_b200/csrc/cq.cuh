@@ -65,6 +65,7 @@ cudaError_t launch_cq_gemv_fast(const uint8_t* packed, const uint16_t* norms, in
 // prepared activations and split-K partials; up to 128 items per pass.
 constexpr int kTcMinBatch = 16;
 bool cq_gemm_tc_supported(int32_t bits);
+bool cq_gemm_tc_preferred(int32_t rows, int32_t input_size, int32_t batch);
 size_t cq_gemm_tc_scratch_bytes(int32_t rows, int32_t input_size, int32_t batch, int32_t sms);
 cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
                               int32_t bits, const float* x, int32_t batch, float* y, const Codebook& cb, void* scratch,

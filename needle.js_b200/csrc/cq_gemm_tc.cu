@@ -9,8 +9,9 @@
 // cores multiply bf16; to keep binary32-level accuracy each operand is split into a bf16 head and
 // a bf16 tail (v = hi + lo up to 2^-17 |v|) and the product is accumulated as
 // A_hi B_hi + A_hi B_lo + A_lo B_hi in fp32 (the dropped A_lo B_lo term is below 2^-16 relative).
-// Two MMAs per K-step do it: A_hi x [B_hi; B_lo] (N' = 2N: columns [0, N) get A_hi B_hi and
-// [N, 2N) A_hi B_lo) and A_lo x B_hi into columns [0, N); the epilogue adds the two column blocks.
+// For N <= 64 two MMAs per K-step do it: A_hi x [B_hi; B_lo] (N' = 2N: columns [0, N) get A_hi B_hi
+// and [N, 2N) A_hi B_lo) and A_lo x B_hi into columns [0, N), and the epilogue adds the two column
+// blocks; above, three MMAs of N columns accumulate into [0, N).
 //
 // Kernels.  k_cq_prep_bf16 writes x' of every (group, item) as bf16 head and tail rows already in
 // the shared-memory layout the MMA reads (K-major, 128-byte swizzle; per group and 64-column half
@@ -19,16 +20,16 @@
 // across CTAs (split-K) when there are fewer row tiles than SMs, and k_splitk_sum adds the splits'
 // partial results in a fixed order.
 //
-// k_cq_gemm_tc is warp-specialised around a ring of group slots (A operand in tensor memory,
-// activations in shared memory; 3 slots for N <= 64, 2 above):
-//   * decode warps 0-11, three teams of four (team t takes groups t, t + S, ... for S slots, so that
+// k_cq_gemm_tc is warp-specialised around a ring of 3 group slots (A operand in tensor memory,
+// activations in shared memory):
+//   * decode warps 0-11, three teams of four (team t takes groups t, t + 3, ... into slot t, so that
 //     each slot is used in one team's program order; warp w serves tensor-memory lanes
 //     32 (w % 4) ..+31, one tile row per thread).  Per group a thread turns its
 //     row's norm into a 16-entry table of split values (level * norm as bf16 head | tail), decodes
 //     the row's 128 weights with one table read each and writes the head and tail words into tensor
 //     memory (tcgen05.st); its packed bytes were loaded two of its groups earlier.
-//   * warp 12 (one elected lane, the warp converged) issues a group's 8 K-steps x 2 MMAs and commits
-//     them to the slot's "empty" barrier, which frees the slot for the decoders and the producer.
+//   * warp 12 (one elected lane) issues a group's 8 K-steps x 2 (or 3) MMAs and commits them to the slot's
+//     "empty" barrier, which frees the slot for the decoders and the producer.
 //   * warp 13 (one thread) bulk-copies the groups' activation tiles into the ring.
 // Every mbarrier wait gives up after 2 s and marks the tile failed (its outputs become NaN).  The
 // epilogue reads the accumulator with tcgen05.ld (decode warps, one row per lane).
@@ -61,9 +62,9 @@ constexpr size_t kTcTableBytes = 16 * kTcDecodeThreads * 4;  // per-thread split
 // (each holds all 512 tensor-memory columns).
 constexpr size_t kTcMinSmem = 120 * 1024;
 
-// Accumulator columns (2N rounded up) and ring slots for N items.
-__host__ __device__ __forceinline__ int tc_acc_cols(int N) { return N <= 64 ? 128 : 256; }
-__host__ __device__ __forceinline__ int tc_slots(int N) { return N <= 64 ? 3 : 2; }
+// Ring slots (one per decode team); accumulator columns [0, 128) then 3 A slots of 128 columns.
+constexpr int kTcSlotsUsed = 3;
+constexpr uint32_t kTcAccCols = 128;
 
 // Byte offset of bf16 element (row, k) (k < 64) in a K-major, 128-byte-swizzled tile.
 __host__ __device__ __forceinline__ uint32_t sw128(int row, int k) {
@@ -86,23 +87,28 @@ __device__ __forceinline__ uint32_t bf16_idesc(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
 }
 
-// D (tensor memory) (+)= A (tensor memory, 128 lanes x 8 columns = 16 bf16 per row) x B^T (shared),
-// issued by one elected lane of a converged warp.
-__device__ __forceinline__ void mma_ts_elect(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                             uint32_t accumulate) {
+// D (tensor memory) (+)= A (tensor memory, 128 lanes x 8 columns = 16 bf16 per row) x B^T (shared);
+// issued by one thread.
+__device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
   asm volatile(
-      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
-      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
 
-// Arrive on `bar` once every MMA the warp's elected lane issued so far has completed.
-__device__ __forceinline__ void mma_commit_elect(uint64_t* bar) {
-  asm volatile(
-      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
-      " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(saddr(bar))
-      : "memory");
+// Arrive on `bar` once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
+               : "memory");
+}
+
+// True in one lane of the (converged) warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n" : "=r"(e));
+  return e != 0;
 }
 
 __device__ __forceinline__ void bar_init(uint64_t* bar, uint32_t count) {
@@ -137,11 +143,14 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                : "memory");
 }
 
-// 8 consecutive 32-bit tensor-memory columns of this thread's lane <- v[0..7].
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(v[0]),
-               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-               : "memory");
+// 16 consecutive 32-bit tensor-memory columns of this thread's lane <- v[0..15].
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
 }
 
 // v[0..7] <- 8 consecutive 32-bit tensor-memory columns of this thread's lane.
@@ -188,6 +197,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
     float* __restrict__ out, int32_t out_stride, int64_t split_stride, Codebook cb) {
   constexpr int kCodes = BITS == 4 ? 16 : 4;
   constexpr int kGroupWords = BITS == 4 ? 16 : 8;  // packed 32-bit words of one row's group
+  constexpr int kPairsPerWord = BITS == 4 ? 4 : 8;  // column pairs (two codes) per packed word
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t a_full[kTcMaxSlots];  // 4 decode-warp arrivals
   __shared__ __align__(8) uint64_t b_full[kTcMaxSlots];  // producer arrival + copied bytes
@@ -200,8 +210,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
   const int mt = blockIdx.x, split = blockIdx.y;
   const int g_begin = split * groups_per_split, g_end = min(groups, g_begin + groups_per_split);
   const int ng = g_end - g_begin;
-  const int nslots = tc_slots(N);
-  const uint32_t acc_cols = (uint32_t)tc_acc_cols(N);
+  const int nslots = kTcSlotsUsed;
+  const uint32_t acc_cols = kTcAccCols;
+  const bool doubled = N <= 64;  // A_hi x [B_hi; B_lo] as one MMA of 2N columns
   const uint32_t half_bytes = (uint32_t)(2 * N) * 128;  // activation tile of one 64-column half
   const uint32_t group_bytes = 2 * half_bytes;
   // shared memory: activation ring [slot][half][head rows | tail rows] (1024-aligned), split tables
@@ -270,31 +281,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
     }
     __syncwarp();
   } else if (warp == kTcMmaWarp) {
-    // ---- MMA issue: the whole warp runs the loop (it stays converged); one elected lane issues
+    // ---- MMA issue: the whole warp waits (converged); the elected lane issues a group's MMAs back to
+    // back from precomputed operands, so that the warp spends few issue slots next to the decoders
     const uint32_t idesc2 = bf16_idesc(2 * N), idesc1 = bf16_idesc(N);
+    const bool leader = elect_one();
+    const uint64_t half_units = half_bytes >> 4;  // descriptor start-address units of one half
     bool failed = false;
     for (int gi = 0; gi < ng; gi++) {
       const int sl = gi % nslots;
       const uint32_t par = (uint32_t)((gi / nslots) & 1);
-      const bool ok = bar_wait(&b_full[sl], par) && bar_wait(&a_full[sl], par);
+      // the leader polls (many polling lanes would only add shared-memory traffic)
+      const bool ok = !leader || (bar_wait(&b_full[sl], par) && bar_wait(&a_full[sl], par));
       if (!__all_sync(0xffffffffu, ok)) {
         failed = true;
         break;
       }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a_hi = tmem + acc_cols + sl * 128, a_lo = a_hi + 64;
-      const uint64_t d0 = sw128_desc(b_sm + sl * group_bytes);
-      // K-step kk: 8 A columns; activation half kk / 4 at 32 bytes (2 descriptor units) per step
+      if (leader) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_hi = tmem + acc_cols + sl * 128, a_lo = a_hi + 64;
+        const uint64_t d0 = sw128_desc(b_sm + sl * group_bytes), d1 = d0 + half_units;
+        // K-step kk: 8 A columns; activation half kk / 4 at 32 bytes (2 descriptor units) per step
 #pragma unroll
-      for (int kk = 0; kk < kGroup / 16; kk++) {
-        const uint64_t bd = d0 + (uint64_t)((kk >> 2) * (half_bytes >> 4) + (kk & 3) * 2);
-        mma_ts_elect(tmem, a_hi + kk * 8, bd, idesc2, (gi > 0 || kk > 0) ? 1u : 0u);  // [hh | hl]
-        mma_ts_elect(tmem, a_lo + kk * 8, bd, idesc1, 1u);                            // += lh
+        for (int kk = 0; kk < kGroup / 16; kk++) {
+          const uint64_t bd = (kk < 4 ? d0 : d1) + (uint64_t)((kk & 3) * 2);
+          const uint32_t first = (gi > 0 || kk > 0) ? 1u : 0u;
+          if (doubled) {
+            mma_ts(tmem, a_hi + kk * 8, bd, idesc2, first);  // [hh | hl] in columns [0, 2N)
+          } else {
+            mma_ts(tmem, a_hi + kk * 8, bd, idesc1, first);                    // hh
+            mma_ts(tmem, a_hi + kk * 8, bd + (uint64_t)(N * 8), idesc1, 1u);  // += hl (tail rows N..2N-1)
+          }
+          mma_ts(tmem, a_lo + kk * 8, bd, idesc1, 1u);  // += lh
+        }
+        mma_commit(&empty[sl]);
       }
-      mma_commit_elect(&empty[sl]);
+      __syncwarp();
     }
     if (failed && lane == 0) atomicExch(&s_failed, 1);
-    mma_commit_elect(&acc_full);  // arrives once every MMA issued above has completed
+    if (leader) mma_commit(&acc_full);  // arrives once every MMA issued above has completed
     __syncwarp();
   } else {
     // ---- decode: team t takes groups t, t + teams, ...; thread = one tile row
@@ -306,8 +330,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
     const uint16_t* nrow = norms + (int64_t)(row_ok ? grow : 0) * groups;
     uint32_t* tab = table + tid;  // entry c of this thread's table at tab[c * kTcDecodeThreads]
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-    // one team per ring slot (3, or 2 for N > 64: team 2 then only joins the epilogue), so that the
-    // uses of a slot, and the phases of its barriers, follow one team's program order
+    // one team per ring slot, so that the uses of a slot, and the phases of its barriers, follow one
+    // team's program order
     const int teams = nslots;
     const int n_mine = team < teams && ng > team ? (ng - team + teams - 1) / teams : 0;
     uint32_t wr[kTcPrefetch][kGroupWords];
@@ -334,7 +358,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
       for (int d = 0; d < kTcPrefetch; d++) {
         const int j = j0 + d;
         if (j >= n_mine || failed) break;
-        const int gi = team + teams * j, sl = team;
+        const int sl = team;  // group team + teams * j
         // split table of this row's group: level * norm as bf16 head | tail, two codes at a time
 #pragma unroll
         for (int c = 0; c < kCodes; c += 2) {
@@ -343,39 +367,46 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
           tab[c * kTcDecodeThreads] = __byte_perm(h2, l2, 0x5410);
           tab[(c + 1) * kTcDecodeThreads] = __byte_perm(h2, l2, 0x7632);
         }
-        // pairs 8q .. 8q + 7 (columns 16q .. 16q + 15) of the group as head and tail words
-        auto decode8 = [&](int q, uint32_t* hi, uint32_t* lo) {
+        // pairs 16q .. 16q + 15 (columns 32q .. 32q + 31) of the group as head and tail words; the
+        // low and high codes of each packed byte are first split into separate byte lanes
+        auto decode16 = [&](int q, uint32_t* hi, uint32_t* lo) {
 #pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const int p = 8 * q + i;
-            int c0, c1;
-            if constexpr (BITS == 4) {
-              const uint32_t byte = (wr[d][p >> 2] >> (8 * (p & 3))) & 0xFFu;
-              c0 = byte & 15;
-              c1 = byte >> 4;
-            } else {
-              const uint32_t quad = (wr[d][p >> 3] >> (4 * (p & 7))) & 0xFu;
-              c0 = quad & 3;
-              c1 = quad >> 2;
+          for (int wi = 0; wi < 16 / kPairsPerWord; wi++) {
+            const uint32_t w = wr[d][q * (16 / kPairsPerWord) + wi];
+#pragma unroll
+            for (int i = 0; i < kPairsPerWord; i++) {
+              uint32_t c0, c1;
+              if constexpr (BITS == 4) {
+                const uint32_t t = w & 0x0F0F0F0Fu, u = (w >> 4) & 0x0F0F0F0Fu;
+                c0 = __byte_perm(t, 0, 0x4440 | i);
+                c1 = __byte_perm(u, 0, 0x4440 | i);
+              } else {
+                const uint32_t t = w & 0x33333333u, u = (w >> 2) & 0x33333333u;
+                c0 = (t >> (4 * i)) & 3u;
+                c1 = (u >> (4 * i)) & 3u;
+              }
+              const uint32_t t0 = tab[c0 * kTcDecodeThreads], t1 = tab[c1 * kTcDecodeThreads];
+              hi[wi * kPairsPerWord + i] = __byte_perm(t0, t1, 0x5410);
+              lo[wi * kPairsPerWord + i] = __byte_perm(t0, t1, 0x7632);
             }
-            const uint32_t t0 = tab[c0 * kTcDecodeThreads], t1 = tab[c1 * kTcDecodeThreads];
-            hi[i] = __byte_perm(t0, t1, 0x5410);
-            lo[i] = __byte_perm(t0, t1, 0x7632);
           }
         };
         const uint32_t col = lane_addr + acc_cols + sl * 128;
-        uint32_t hi[8], lo[8];
-        decode8(0, hi, lo);
-        if (gi >= nslots) failed = !bar_wait(&empty[sl], (uint32_t)((gi / nslots - 1) & 1));
-        failed = __any_sync(0xffffffffu, failed);  // warp-uniform: tcgen05.st is a warp instruction
+        uint32_t hi[16], lo[16];
+        decode16(0, hi, lo);
+        // lane 0 waits for the MMAs that last read this slot; the verdict is made warp-uniform
+        // (tcgen05.st is a warp instruction)
+        if (j > 0 && lane == 0) failed = !bar_wait(&empty[sl], (uint32_t)((j - 1) & 1));
+        failed = __any_sync(0xffffffffu, failed);
         if (failed) break;
-        tmem_st8(col, hi);
-        tmem_st8(col + 64, lo);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        tmem_st16(col, hi);
+        tmem_st16(col + 64, lo);
 #pragma unroll
-        for (int q = 1; q < 8; q++) {
-          decode8(q, hi, lo);
-          tmem_st8(col + 8 * q, hi);
-          tmem_st8(col + 64 + 8 * q, lo);
+        for (int q = 1; q < 4; q++) {
+          decode16(q, hi, lo);
+          tmem_st16(col + 16 * q, hi);
+          tmem_st16(col + 64 + 16 * q, lo);
         }
         if (j + kTcPrefetch < n_mine) load_group(d, j + kTcPrefetch);  // wr[d] fully used
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -385,16 +416,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
       }
     }
     if (failed) atomicExch(&s_failed, 1);
-    // epilogue: wait for the last MMA; this warp's 32 rows x every third 8-column chunk, y = [0, N) + [N, 2N)
-    const bool acc_ok = bar_wait(&acc_full, 0);
+    // epilogue: wait for the last MMA; this warp's 32 rows x every third 8-column chunk (y = columns
+    // [0, N), plus [N, 2N) when the head x tail products went there)
+    const bool acc_ok = __all_sync(0xffffffffu, lane != 0 || bar_wait(&acc_full, 0));
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    __syncwarp();
     const bool bad = !acc_ok || *(volatile int*)&s_failed != 0;
     float* o = out + (int64_t)split * split_stride;
     for (int c0 = team * 8; c0 < N; c0 += kTcTeams * 8) {
-      uint32_t v[8], w[8];
+      uint32_t v[8], w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       tmem_ld8(lane_addr + (uint32_t)c0, v);
-      tmem_ld8(lane_addr + (uint32_t)(N + c0), w);
+      if (doubled) tmem_ld8(lane_addr + (uint32_t)(N + c0), w);
       if (row_ok) {
 #pragma unroll
         for (int j = 0; j < 8; j++)
@@ -440,6 +471,13 @@ TcPlan plan_for(int32_t rows, int32_t in_pad, int sms) {
 
 bool cq_gemm_tc_supported(int32_t bits) { return bits == 2 || bits == 4 || bits == kTernaryBits; }
 
+// From 16 items the GEMM beats the table GEMV (one weight pass per 8 items) on every shape; for
+// matrices of 4M weights and more already from 6 items (measured on the config-2 shapes).
+bool cq_gemm_tc_preferred(int32_t rows, int32_t input_size, int32_t batch) {
+  const int64_t in_pad = (input_size + kGroup - 1) / kGroup * kGroup;
+  return batch >= kTcMinBatch || (batch >= 6 && (int64_t)rows * in_pad >= (int64_t(1) << 22));
+}
+
 size_t cq_gemm_tc_scratch_bytes(int32_t rows, int32_t input_size, int32_t batch, int32_t sms) {
   const int in_pad = (input_size + kGroup - 1) / kGroup * kGroup;
   const int nb = std::min(batch, kTcMaxN);
@@ -470,7 +508,7 @@ cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int3
     if (e != cudaSuccess) return e;
     float* part = reinterpret_cast<float*>(act + act_bytes);
     const int64_t split_stride = (int64_t)nb * rows;
-    const size_t smem = std::max(kTcMinSmem, (size_t)tc_slots(N) * 2 * (2 * N) * 128 + kTcTableBytes + 1024);
+    const size_t smem = std::max(kTcMinSmem, (size_t)kTcSlotsUsed * 2 * (2 * N) * 128 + kTcTableBytes + 1024);
     auto launch = [&](auto kernel) {
       e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return;

@@ -255,7 +255,7 @@ extern "C" int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const f
   for (int i = 0; i < 28; i++) cb.v[i] = codebook[i];
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
-  if (batch >= kTcMinBatch && cq_gemm_tc_supported(m->bits)) {
+  if (cq_gemm_tc_supported(m->bits) && cq_gemm_tc_preferred(m->rows, m->input_size, batch)) {
     // a real dense contraction: tensor-core GEMM
     int sms = 0;
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
