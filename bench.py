@@ -277,9 +277,22 @@ def bench_qmatvec(args, peaks):
                          "achieved": head["gbs"], "peak": peak, "peak_source": src, "unit": "GB/s",
                          "frac": round(head["gbs"] / peak, 4),
                          # DRAM read + write of one table-kernel launch of the headline case (ncu)
-                         "traffic": 33612544 if head["shape"].startswith("stress") and head["batch"] == 1 else None,
+                         "traffic": 33613312 if head["shape"].startswith("stress") and head["batch"] == 1 else None,
                          "traffic_source": "profiles/qmatvec_table_8192x8192_cq4_batch1.md"},
             "gpu_launches": launches}
+    big = next((r for r in results if r["shape"].startswith("stress") and r["batch"] == 128 and r["numerics"] == "fast"),
+               None)
+    if big is not None:
+        # the batched case runs on the tensor cores: algorithmic flops 2 * B * rows * in_pad against the
+        # measured dense bf16 peak; the pipe executes three bf16 products per weight x activation pair
+        tflops = 2 * 128 * 8192 * 8192 / (big["us"] * 1e-6) / 1e12
+        tpeak = float((peaks or {}).get("bf16_tflops") or 1590.0)
+        line["roofline_batched"] = {"kernel": "k_cq_gemm_tc (+ k_cq_prep_bf16, k_splitk_sum)", "bound": "tensor",
+                                    "case": "stress 8192x8192 CQ4 batch 128", "achieved": round(tflops, 1),
+                                    "executed": round(3 * tflops, 1), "peak": tpeak,
+                                    "peak_source": "measured" if (peaks or {}).get("bf16_tflops") else "fallback",
+                                    "unit": "TFLOP/s", "frac": round(tflops / tpeak, 4),
+                                    "source": "profiles/qmatvec_gemm_tc_8192x8192_cq4.md"}
     print(json.dumps(line), flush=True)
 
 
@@ -333,7 +346,7 @@ def bench_attention(args, peaks):
             "roofline": {"kernel": "k_attention_fast_mma (+ k_attention_fast_combine)", "bound": "hbm", "achieved": head["gbs"],
                          "peak": peak, "peak_source": src, "unit": "GB/s", "frac": round(head["gbs"] / peak, 4),
                          # DRAM read + write of one k_attention_fast_mma launch at L = 8192 (ncu)
-                         "traffic": 149972736 if head["L"] == 8192 and head["numerics"] == "fast" else None,
+                         "traffic": 150667520 if head["L"] == 8192 and head["numerics"] == "fast" else None,
                          "traffic_source": "profiles/attention_fast_mma_L8192_batch64.md"},
             "gpu_launches": launches}
     print(json.dumps(line), flush=True)

@@ -188,10 +188,12 @@ typedef struct needle_cq_matrix {
 int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float* codebook, const float* x,
                               int32_t batch, float* y, void* stream);
 
-/* The same matvec in fast numerics (binary32 FMAs, tree reductions; record widths 2, 4 and
- * ternary): results agree with cqMatvec within binary32 rounding, not bit for bit.  Weights are
- * streamed once with coalesced 16-byte loads.  Same arguments and scratch as
- * needle_cuda_cq_matvec_dev; 3-bit matrices return UNSUPPORTED_CACT. */
+/* The same matvec in fast numerics (record widths 2, 4 and ternary): results agree with cqMatvec
+ * within binary32 rounding, not bit for bit.  Up to 15 items (5 for matrices of 4M weights and
+ * more) it runs the table GEMV (binary32 per-group byte tables, weights streamed once per 8 items);
+ * above, the tensor-core GEMM (bf16 head/tail split, fp32 accumulation, up to 128 items per pass).
+ * Same arguments and scratch as needle_cuda_cq_matvec_dev; 3-bit matrices return
+ * UNSUPPORTED_CACT. */
 int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const float* codebook, const float* x,
                                    int32_t batch, float* y, void* stream);
 
