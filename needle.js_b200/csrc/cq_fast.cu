@@ -50,6 +50,9 @@ constexpr int kRing = 3;                         // 32-row weight blocks per war
 constexpr int kSlotBytes = 2048;                 // one block: 32 rows x 64 bytes (CQ4) or 32 bytes
 constexpr int kRingBytes = kRing * kSlotBytes * (kTabThreads / 32);  // 48 KB per CTA
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a copy wait gives up after 2 s
+// A table build (inputs, FWHT, 64 KB of stores, barriers) costs about as much time as this many
+// 32-row blocks of lookups (measured: CTAs with a second table ran ~2 us = ~18 blocks longer).
+constexpr int kTableCost = 18;
 
 template <int BITS>
 struct TabGeom {
@@ -182,8 +185,16 @@ __global__ void __launch_bounds__(kTabThreads, 2) k_cq_gemv_table(
   const int item = blockIdx.y;
   const int groups = in_pad / kGroup;
   const int nblk = (rows + 31) / 32;  // 32-row blocks per group
-  const int64_t total = (int64_t)groups * nblk;
-  const int64_t b_begin = total * blockIdx.x / gridDim.x, b_end = total * (blockIdx.x + 1) / gridDim.x;
+  // Contiguous block ranges of equal cost: every group of many blocks is counted as kTableCost
+  // blocks longer (its table build), so a CTA whose range crosses into another group gets that many
+  // fewer blocks.  (Groups of few blocks are split evenly: there every CTA builds one table.)
+  const int64_t tcost = nblk >= 128 ? kTableCost : 0;
+  const int64_t per_group = nblk + tcost, cost = (int64_t)groups * per_group;
+  auto block_at = [&](int64_t p) {
+    const int64_t gq = p / per_group;
+    return gq * nblk + max((int64_t)0, p - gq * per_group - tcost);
+  };
+  const int64_t b_begin = block_at(cost * blockIdx.x / gridDim.x), b_end = block_at(cost * (blockIdx.x + 1) / gridDim.x);
   x += (int64_t)item * x_stride;
   float* part = partials + (int64_t)item * groups * rows;
   if (tid < 16) {
