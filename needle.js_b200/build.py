@@ -17,7 +17,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libneedle_cuda.so")
-SOURCES = ["engine.cu", "cq.cu", "layer.cu", "ops.cu", "attn_fast.cu", "cq_fast.cu", "cq_gemm_tc.cu"]
+SOURCES = ["engine.cu", "cq.cu", "layer.cu", "ops.cu", "attn_fast.cu", "cq_fast.cu", "cq_gemm_tc.cu", "grammar.cpp"]
 HEADERS = ["common.cuh", "cq.cuh", "engine.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "--fmad=false", "-std=c++17", "--extended-lambda", "-Xcompiler", "-fPIC",
@@ -41,11 +41,12 @@ def _stale(target: str, deps) -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     """Compiles every source (in parallel) and links the shared library; returns its path."""
     os.makedirs(BUILD, exist_ok=True)
-    headers = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", "needle_cuda.h")]
+    headers = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", h)
+                                                          for h in ("needle_cuda.h", "needle_grammar.h")]
     objs, jobs = [], []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
-        o = os.path.join(BUILD, src.replace(".cu", ".o"))
+        o = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
         objs.append(o)
         if force or _stale(o, [s] + headers):
             jobs.append([nvcc(), *ARCH, *FLAGS, "-c", s, "-o", o])

@@ -104,6 +104,20 @@ EXPORTS = {
     "needle_cuda_profile_read": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_char_p),
                                            C.POINTER(C.c_double), C.POINTER(C.c_int64),
                                            C.POINTER(C.c_int32)]),
+    # include/needle_grammar.h
+    "needle_grammar_tools": (C.c_int, [C.c_char_p, C.c_int32, C.POINTER(C.c_void_p)]),
+    "needle_grammar_schema": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "needle_grammar_clone": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "needle_grammar_free": (None, [C.c_void_p]),
+    "needle_grammar_feed": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int32, C.POINTER(C.c_int32)]),
+    "needle_grammar_complete": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
+    "needle_grammar_result": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int32, C.POINTER(C.c_int32)]),
+    "needle_vocab_open": (C.c_int, [C.c_char_p, C.POINTER(C.c_int32), C.c_int32, C.POINTER(C.c_void_p)]),
+    "needle_vocab_free": (None, [C.c_void_p]),
+    "needle_grammar_allowed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.POINTER(C.c_uint32), C.c_int32,
+                                         C.POINTER(C.c_int32)]),
+    "needle_grammar_allowed_batch": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_int64), C.c_int32, C.c_void_p,
+                                               C.c_int32, C.POINTER(C.c_uint32), C.c_int32, C.POINTER(C.c_int32)]),
 }
 
 _lib = None

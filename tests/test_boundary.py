@@ -1,5 +1,5 @@
 """CPU-side checks of the drop-in boundary: the C-ABI library builds, loads without a GPU, and
-exports every function include/needle_cuda.h declares; error codes follow NeedleErrorCode."""
+exports every function the headers under include/ declare; error codes follow NeedleErrorCode."""
 import ctypes
 import os
 import re
@@ -10,9 +10,15 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def declared_functions():
-    text = open(os.path.join(ROOT, "include", "needle_cuda.h")).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(needle_cuda_\w+)\s*\(", text)))
+    """Every function the headers under include/ declare (needle_cuda_*, needle_grammar_*, needle_vocab_*)."""
+    names = set()
+    for header in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if not header.endswith(".h"):
+            continue
+        text = open(os.path.join(ROOT, "include", header)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names.update(re.findall(r"\b(needle_(?:cuda|grammar|vocab)_\w+)\s*\(", text))
+    return sorted(names)
 
 
 @pytest.fixture(scope="module")
