@@ -352,10 +352,108 @@ def bench_attention(args, peaks):
     print(json.dumps(line), flush=True)
 
 
+TOOLCALL_PROMPT = 256
+TOOLCALL_MAX_NEW = 256
+
+
+def bench_toolcall(args, rank, world, local_rank):
+    """constrained tool-call decode, data-parallel.  --sequences sequences (4096)
+    split evenly over the GPUs; each a 256-token prompt of random ids (seed 5 + rank), then the
+    constrained phase directly after the prompt (random weights never emit <tool_call>), greedy until
+    the grammar completes or 256 constrained tokens, over the synthetic schema (3 tools x 2-5
+    parameters of string / integer / boolean / enum, seed 5).  256 slots per GPU with continuous
+    admission; the allowed ids come from the C++ grammar's byte-trie scan on 16 host threads."""
+    import torch
+    from needle_b200 import build as nbuild
+    from needle_b200 import grammar, synth, toolcall
+    from needle_b200.backend import CudaEngine
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=900))
+    torch.cuda.set_device(local_rank)
+    if rank == 0:
+        nbuild.build()
+    if dist:
+        dist.barrier()
+    archive = synth.build_archive(0)
+    pieces, types, _ = synth.tokenizer_pieces(8192, 0)
+    vocab = grammar.Vocabulary(pieces, types)
+    tools = toolcall.synthetic_tools(5)
+    n_local = args.sequences // world + (1 if rank < args.sequences % world else 0)
+    ids = synth.integers(5 + 1000 * rank, n_local * TOOLCALL_PROMPT + 1, 8192, stream=7).astype(np.int32)
+    prompts = [ids[k * TOOLCALL_PROMPT:(k + 1) * TOOLCALL_PROMPT] for k in range(n_local)]
+    eng = CudaEngine(archive, device=local_rank, max_seqs=SLOTS, max_len=TOOLCALL_PROMPT + TOOLCALL_MAX_NEW + 8,
+                     max_sink=16)
+    threads = max(1, min(16, cpu_threads() // max(1, world)))
+    dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=TOOLCALL_MAX_NEW, threads=threads)
+    dec.run(prompts[:min(8, n_local)], max_steps=max(3, args.warmup))  # warm-up steps (untimed)
+    stream = torch.cuda.ExternalStream(eng.stream, device=local_rank)
+    l0 = eng.kernel_launches()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    results, st = dec.run(prompts)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    launches = eng.kernel_launches() - l0
+    import ctypes
+    from needle_b200 import native
+    h2d = st.items * ctypes.sizeof(native.StepItem) + 4 * st.allowed_ids
+    d2h = st.items * ctypes.sizeof(native.Selected)
+    local = [ms, st.constrained_tokens, st.prompt_tokens, sum(r.complete for r in results),
+             sum(r.dead_end for r in results), st.steps, st.grammar_seconds, launches, len(results), h2d, d2h]
+    if dist:
+        t = torch.tensor(local, dtype=torch.float64)
+        mx = t.clone()
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = t.tolist()
+        tot[0], tot[5], tot[6] = mx[0].item(), mx[5].item(), mx[6].item()
+    else:
+        tot = local
+    if rank == 0:
+        ms_max, cons, prompt_toks, done, dead, steps, gsec, launch_all, seqs, h2d_all, d2h_all = tot
+        secs = ms_max / 1e3
+        line = {"metric": "constrained tool-call tokens/s", "value": round(cons / secs, 1), "unit": "tokens/s",
+                "n_gpus": world, "steps": int(steps), "warmup": max(3, args.warmup),
+                "ms_per_step": round(ms_max / max(steps, 1), 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+                "config": {"workload": "constrained tool-call decode (BASELINE config 5)", "sequences": int(seqs),
+                           "prompt_len": TOOLCALL_PROMPT, "max_new_tokens": TOOLCALL_MAX_NEW, "slots_per_gpu": SLOTS,
+                           "tools": [{"name": t["name"], "parameters": list(t["parameters"]["properties"])}
+                                     for t in tools],
+                           "completed_calls": int(done), "dead_ends": int(dead),
+                           "processed_tokens_per_s": round((cons + prompt_toks) / secs, 1),
+                           "sequences_per_s": round(seqs / secs, 2),
+                           "host_grammar_seconds_max_rank": round(gsec, 3), "host_grammar_threads": threads,
+                           "numerics": "exact (tokens bit-identical to the CPU backend with the same masks)",
+                           "parallelism": f"dp{world} (independent sequences per GPU, no collectives)"},
+                # the whole run goes through needle_cuda_step with host buffers (items, allowed ids in;
+                # selections out), so the measured value is end to end
+                "e2e": {"value": round(cons / secs, 1), "unit": "tokens/s",
+                        "h2d_bytes_per_step": int(h2d_all / max(steps * world, 1)),
+                        "d2h_bytes_per_step": int(d2h_all / max(steps * world, 1))},
+                "gpu_launches": int(launch_all)}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["decode", "qmatvec", "attention"], default="decode",
-                    help="decode: BASELINE config 4 (default); qmatvec / attention: configs 2 / 3 (1 GPU)")
+    ap.add_argument("--workload", choices=["decode", "qmatvec", "attention", "toolcall"], default="decode",
+                    help="decode: BASELINE config 4 (default); qmatvec / attention: configs 2 / 3 (1 GPU); "
+                         "toolcall: config 5 (constrained tool-call decode, data-parallel)")
+    ap.add_argument("--sequences", type=int, default=4096, help="toolcall: sequences over all GPUs")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
@@ -380,7 +478,11 @@ def main():
               "parallelism": f"dp{args.gpus} (independent sequences per GPU, no collectives)"}
     metric, unit = "decode tokens/s", "tokens/s"
 
-    if args.workload != "decode" and args.impl == "cuda":
+    if args.workload == "toolcall" and args.impl == "cuda":
+        bench_toolcall(args, rank, world, local_rank)
+        return
+
+    if args.workload in ("qmatvec", "attention") and args.impl == "cuda":
         if rank != 0:
             return
         peaks = None

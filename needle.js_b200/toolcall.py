@@ -1,0 +1,172 @@
+"""Batched constrained tool-call decoding over the engine's slots.
+
+The constrained loop of `Needle.complete` (packages/needle.js/src/tools/agent.ts:157-210), run for
+many sequences at once: each step, every sequence in its constrained phase asks its
+`ToolCallGrammar` for the ids that may come next (the host-side scan, here a byte-trie walk on host
+threads, include/needle_grammar.h), the engine feeds the pending token and picks the best allowed
+id on the device (needle_cuda_step with an allowed list: the fused mask + argmax, ties to the
+first id of the list as selectToken does), and the chosen piece is fed to the grammar.  When the
+grammar completes, the chosen token is fed once more without a selection (agent.ts:193-196) and the
+slot is freed for the next sequence.  Prompts are fed one token per step through the same batched
+steps; the constrained phase starts directly after the prompt, its pending token being the prompt's
+last token (random weights never emit <tool_call>).
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+from .backend import StepRequest
+from .grammar import MAX_OUTPUT_BYTES, ToolCallGrammar, Vocabulary, allowed_batch
+
+
+def synthetic_tools(seed: int = 5, n_tools: int = 3):
+    """BASELINE config 5's schema: 3 tools with 2-5 parameters each, names of 4-12 random lowercase
+    letters, parameter types drawn from string / integer / boolean / enum (2-4 random words); every
+    parameter required."""
+    rng = np.random.default_rng(seed)
+
+    def word():
+        return "".join(chr(97 + int(c)) for c in rng.integers(0, 26, int(rng.integers(4, 13))))
+
+    tools, names = [], set()
+    while len(tools) < n_tools:
+        name = word()
+        if name in names:
+            continue
+        names.add(name)
+        props = {}
+        for _ in range(int(rng.integers(2, 6))):
+            kind = ("string", "integer", "boolean", "enum")[int(rng.integers(0, 4))]
+            key = word()
+            while key in props:
+                key = word()
+            if kind == "enum":
+                props[key] = {"type": "string", "enum": [word() for _ in range(int(rng.integers(2, 5)))]}
+            else:
+                props[key] = {"type": kind}
+        tools.append({"name": name, "description": "synthetic tool",
+                      "parameters": {"type": "object", "properties": props, "required": list(props)}})
+    return tools
+
+
+@dataclass
+class ToolCallResult:
+    ids: List[int] = field(default_factory=list)      # constrained tokens, in order
+    text: bytes = b""
+    calls: list = field(default_factory=list)
+    complete: bool = False
+    dead_end: bool = False
+
+
+@dataclass
+class DecodeStats:
+    steps: int = 0
+    prompt_tokens: int = 0
+    constrained_tokens: int = 0
+    seconds: float = 0.0
+    grammar_seconds: float = 0.0
+    engine_seconds: float = 0.0
+    items: int = 0        # step items sent to the engine
+    allowed_ids: int = 0  # allowed ids sent with them
+
+
+class ConstrainedDecoder:
+    def __init__(self, engine, vocab: Vocabulary, tools: Sequence[dict], maximum_calls: int = 4,
+                 maximum_new_tokens: int = 256, threads: int = 8):
+        self.engine = engine
+        self.vocab = vocab
+        self.tools = list(tools)
+        self.maximum_calls = maximum_calls
+        self.maximum_new = max(1, maximum_new_tokens)
+        self.threads = threads
+        self.template = ToolCallGrammar(self.tools, maximum_calls)  # validates the tools once
+
+    def run(self, prompts: Sequence[np.ndarray], slots: Optional[int] = None,
+            max_steps: Optional[int] = None) -> tuple[List[ToolCallResult], DecodeStats]:
+        eng = self.engine
+        slots = min(slots or eng.max_seqs, eng.max_seqs)
+        results = [ToolCallResult() for _ in prompts]
+        stats = DecodeStats()
+        queue = list(range(len(prompts)))[::-1]
+        state = [None] * slots  # per slot: dict(seq, pos, phase, grammar, out_bytes, pending)
+        t_start = time.perf_counter()
+        while True:
+            for s in range(slots):  # admit
+                if state[s] is None and queue:
+                    k = queue.pop()
+                    p = np.asarray(prompts[k], dtype=np.int32)
+                    eng.reset(s, int(p.size) + self.maximum_new + 1, 0)
+                    state[s] = {"seq": k, "pos": 0, "phase": "prompt", "prompt": p,
+                                "grammar": self.template.clone(), "out": 0, "pending": -1}
+            live = [s for s in range(slots) if state[s] is not None]
+            if not live or (max_steps is not None and stats.steps >= max_steps):
+                break
+            requests, selecting = [], []
+            for s in live:
+                st = state[s]
+                if st["phase"] == "prompt":
+                    last = st["pos"] == st["prompt"].size - 1
+                    requests.append(StepRequest(s, int(st["prompt"][st["pos"]]), last))
+                    if last:
+                        selecting.append(len(requests) - 1)
+                    stats.prompt_tokens += 1
+                elif st["phase"] == "call":
+                    requests.append(StepRequest(s, st["pending"], True))
+                    selecting.append(len(requests) - 1)
+                else:  # "final": the completed call's last token, no selection
+                    requests.append(StepRequest(s, st["pending"], False))
+            t0 = time.perf_counter()
+            masks = allowed_batch([state[requests[i].seq]["grammar"] for i in selecting],
+                                  [state[requests[i].seq]["out"] for i in selecting], self.vocab, self.threads)
+            stats.grammar_seconds += time.perf_counter() - t0
+            for i, ids in zip(selecting, masks):
+                requests[i].allowed = ids
+            dead = {requests[i].seq for i, ids in zip(selecting, masks) if ids.size == 0}
+            if dead:  # GRAMMAR_DEAD_END: no token can continue; the sequence stops here
+                for s in dead:
+                    results[state[s]["seq"]].dead_end = True
+                    state[s] = None
+                requests = [r for r in requests if r.seq not in dead]
+            if not requests:
+                continue
+            stats.items += len(requests)
+            stats.allowed_ids += sum(int(r.allowed.size) for r in requests if r.allowed is not None)
+            t0 = time.perf_counter()
+            chosen, _ = eng.step(requests)
+            stats.engine_seconds += time.perf_counter() - t0
+            stats.steps += 1
+            for r, sel in zip(requests, chosen):
+                st = state[r.seq]
+                if st["phase"] == "final":
+                    state[r.seq] = None
+                    continue
+                if st["phase"] == "prompt" and not r.select:
+                    st["pos"] += 1
+                    continue
+                tok = int(sel[0])
+                res = results[st["seq"]]
+                piece = self.vocab.piece[tok]
+                t0 = time.perf_counter()
+                accepted = st["grammar"].feed(piece)
+                stats.grammar_seconds += time.perf_counter() - t0
+                if not accepted:  # the device picked outside the mask: a contract violation
+                    raise RuntimeError(f"selected disallowed token {tok}")
+                res.ids.append(tok)
+                res.text += piece
+                st["out"] += len(piece)
+                st["pending"] = tok
+                st["phase"] = "call"
+                stats.constrained_tokens += 1
+                if st["grammar"].complete:
+                    res.complete = True
+                    res.calls = st["grammar"].calls
+                    st["phase"] = "final"
+                elif len(res.ids) >= self.maximum_new or st["out"] >= MAX_OUTPUT_BYTES:
+                    res.calls = st["grammar"].calls
+                    state[r.seq] = None
+        stats.seconds = time.perf_counter() - t_start
+        return results, stats

@@ -1,0 +1,74 @@
+"""GPU parity of batched constrained tool-call decoding (BASELINE config 5's loop).
+
+`ConstrainedDecoder` runs several sequences through the engine at once, each with its own
+`ToolCallGrammar` and allowed-id masks; the oracle replays every sequence alone, token by token,
+selecting like selectToken over the same allowed lists (packages/needle.js/src/model/runtime.ts:
+880-899: the first id of the list wins a tie) with its own logits.  Token ids must agree exactly,
+and every completed call must parse as calls of the schema's tools.
+"""
+import json
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def setup(oracle):
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import needle_b200.build
+    needle_b200.build.build()
+    from needle_b200 import grammar, synth, toolcall
+    archive = synth.build_archive(0)
+    pieces, types, _ = synth.tokenizer_pieces(8192, 0)
+    vocab = grammar.Vocabulary(pieces, types)
+    tools = toolcall.synthetic_tools(5)
+    return archive, vocab, tools, oracle.Model(archive)
+
+
+def oracle_constrained(oracle, model, vocab, tools, prompt, maximum_new):
+    from needle_b200 import grammar
+    rt = oracle.Runtime(model)
+    rt.reset(len(prompt) + maximum_new + 1, 0)
+    logits = None
+    for i, t in enumerate(prompt):
+        logits = rt.step(int(t), want_logits=(i == len(prompt) - 1))
+    g = grammar.ToolCallGrammar(tools, 4)
+    ids, out = [], 0
+    for _ in range(maximum_new):
+        allowed = grammar.allowed(g, vocab, out)
+        if allowed.size == 0:
+            return ids, False, True
+        tok = int(allowed[int(np.argmax(logits[allowed]))])
+        ids.append(tok)
+        assert g.feed(vocab.piece[tok])
+        out += len(vocab.piece[tok])
+        if g.complete:
+            return ids, True, False
+        logits = rt.step(tok, want_logits=True)
+    return ids, False, False
+
+
+def test_constrained_decoding_matches_oracle(setup, oracle):
+    from needle_b200.backend import CudaEngine
+    from needle_b200 import toolcall
+    archive, vocab, tools, model = setup
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, 8192, n).astype(np.int32) for n in (40, 33, 57, 21, 48)]
+    maximum_new = 48
+    with CudaEngine(archive, device=0, max_seqs=3, max_len=160, max_sink=16) as eng:
+        dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=maximum_new, threads=4)
+        results, stats = dec.run(prompts)  # 5 sequences through 3 slots: admission into freed slots
+    assert stats.constrained_tokens == sum(len(r.ids) for r in results)
+    names = {t["name"] for t in tools}
+    for k, (p, res) in enumerate(zip(prompts, results)):
+        ids, complete, dead = oracle_constrained(oracle, model, vocab, tools, p, maximum_new)
+        assert res.ids == ids, k
+        assert res.complete == complete and res.dead_end == dead, k
+        assert res.text == b"".join(vocab.piece[i] for i in ids)
+        if res.complete:
+            calls = json.loads(res.text.decode())
+            assert calls == res.calls and all(c["name"] in names for c in calls)
