@@ -408,18 +408,20 @@ def bench_toolcall(args, rank, world, local_rank):
     h2d = st.items * ctypes.sizeof(native.StepItem) + 4 * st.allowed_ids
     d2h = st.items * ctypes.sizeof(native.Selected)
     local = [ms, st.constrained_tokens, st.prompt_tokens, sum(r.complete for r in results),
-             sum(r.dead_end for r in results), st.steps, st.grammar_seconds, launches, len(results), h2d, d2h]
+             sum(r.dead_end for r in results), st.steps, st.grammar_seconds, launches, len(results), h2d, d2h,
+             st.engine_seconds, st.seconds]
     if dist:
         t = torch.tensor(local, dtype=torch.float64)
         mx = t.clone()
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         tot = t.tolist()
-        tot[0], tot[5], tot[6] = mx[0].item(), mx[5].item(), mx[6].item()
+        for k in (0, 5, 6, 11, 12):
+            tot[k] = mx[k].item()
     else:
         tot = local
     if rank == 0:
-        ms_max, cons, prompt_toks, done, dead, steps, gsec, launch_all, seqs, h2d_all, d2h_all = tot
+        ms_max, cons, prompt_toks, done, dead, steps, gsec, launch_all, seqs, h2d_all, d2h_all, esec, wall = tot
         secs = ms_max / 1e3
         line = {"metric": "constrained tool-call tokens/s", "value": round(cons / secs, 1), "unit": "tokens/s",
                 "n_gpus": world, "steps": int(steps), "warmup": max(3, args.warmup),
@@ -433,6 +435,8 @@ def bench_toolcall(args, rank, world, local_rank):
                            "processed_tokens_per_s": round((cons + prompt_toks) / secs, 1),
                            "sequences_per_s": round(seqs / secs, 2),
                            "host_grammar_seconds_max_rank": round(gsec, 3), "host_grammar_threads": threads,
+                           "engine_call_seconds_max_rank": round(esec, 3),
+                           "host_loop_seconds_max_rank": round(max(wall - gsec - esec, 0.0), 3),
                            "numerics": "exact (tokens bit-identical to the CPU backend with the same masks)",
                            "parallelism": f"dp{world} (independent sequences per GPU, no collectives)"},
                 # the whole run goes through needle_cuda_step with host buffers (items, allowed ids in;

@@ -1078,19 +1078,21 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, 
       seen[it.seq] = 1;
       const SlotHost& h = C.slots[it.seq];
       require(h.ready, NEEDLE_INVALID_CACT, "Call runtime.reset() before decoding");
-      require(h.position < h.max_len, NEEDLE_CONTEXT_OVERFLOW,
-              "Position " + std::to_string(h.position) + " reached runtime limit " + std::to_string(h.max_len));
-      require(it.token == NEEDLE_TOKEN_PENDING || (it.token >= 0 && it.token < V), NEEDLE_INVALID_CACT,
-              "Token " + std::to_string(it.token) + " is outside the vocabulary");
+      // messages are built only on failure: this loop runs for every item of every step
+      if (h.position >= h.max_len)
+        fail(NEEDLE_CONTEXT_OVERFLOW,
+             "Position " + std::to_string(h.position) + " reached runtime limit " + std::to_string(h.max_len));
+      if (!(it.token == NEEDLE_TOKEN_PENDING || (it.token >= 0 && it.token < V)))
+        fail(NEEDLE_INVALID_CACT, "Token " + std::to_string(it.token) + " is outside the vocabulary");
       if (it.select) {
         require(out_selected != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "selection requested without output");
         if (it.allowed_count >= 0) {
           require(it.allowed_count > 0, NEEDLE_INVALID_CACT, "Allowed token set is empty");
           require(allowed_ids != nullptr && uint64_t(it.allowed_offset) + uint64_t(it.allowed_count) <= allowed_total,
                   NEEDLE_INVALID_CACT, "allowed ids out of range");
+          const uint32_t* ids = allowed_ids + it.allowed_offset;
           for (int32_t k = 0; k < it.allowed_count; k++)
-            require(allowed_ids[it.allowed_offset + k] < uint32_t(V), NEEDLE_INVALID_CACT,
-                    "Token " + std::to_string(allowed_ids[it.allowed_offset + k]) + " is outside logits");
+            if (ids[k] >= uint32_t(V)) fail(NEEDLE_INVALID_CACT, "Token " + std::to_string(ids[k]) + " is outside logits");
         }
         n_sel++;
         any_sel = true;

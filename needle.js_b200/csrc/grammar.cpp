@@ -17,7 +17,10 @@
 // Allowed tokens.  The reference clones the grammar and feeds every piece of the vocabulary at
 // every step.  Here the pieces form a byte trie: a clone is fed one trie edge at a time and a
 // rejected byte prunes the whole subtree, so the work is the number of trie nodes the grammar
-// accepts rather than the vocabulary times the piece length.  The result is the same id list
+// accepts rather than the vocabulary times the piece length.  Inside a string's content every byte
+// other than a quote, a backslash or a control byte is accepted and only appended, so those
+// subtrees are walked without copying the grammar at all (most steps of a tool call are spent in
+// argument strings, where nearly the whole vocabulary is allowed).  The result is the same id list
 // (ascending, as the reference's Map of candidates).
 #include <algorithm>
 #include <atomic>
@@ -129,6 +132,31 @@ bool valid_utf8(const std::string& s) {
   }
   return true;
 }
+
+// valid_utf8 one byte at a time: ok() after the last byte tells whether the whole input was valid.
+struct Utf8Check {
+  int need = 0;  // continuation bytes still expected
+  uint32_t cp = 0, min = 0;
+  bool bad = false;
+  void feed(uint8_t c) {
+    if (bad) return;
+    if (need > 0) {
+      if ((c & 0xC0) != 0x80) {
+        bad = true;
+        return;
+      }
+      cp = (cp << 6) | (c & 0x3F);
+      if (--need == 0 && (cp < min || cp > 0x10FFFF || (cp >= 0xD800 && cp <= 0xDFFF))) bad = true;
+      return;
+    }
+    if (c < 0x80) return;
+    if (c >= 0xC2 && c <= 0xDF) need = 1, cp = c & 0x1F, min = 0x80;
+    else if (c >= 0xE0 && c <= 0xEF) need = 2, cp = c & 0x0F, min = 0x800;
+    else if (c >= 0xF0 && c <= 0xF4) need = 3, cp = c & 0x07, min = 0x10000;
+    else bad = true;
+  }
+  bool ok() const { return !bad && need == 0; }
+};
 
 // Number::toString (ECMA-262 6.1.6.1.20): the shortest decimal that reads back as the same double.
 std::string js_number(double x) {
@@ -404,6 +432,14 @@ const Json& empty_schema() {
   return e;
 }
 
+// A schema inside `owner` (a subschema, or `{}` when absent), sharing owner's lifetime instead of
+// copying it.
+SchemaPtr subschema(const SchemaPtr& owner, const Json* child) {
+  if (child) return SchemaPtr(owner, child);
+  static const SchemaPtr empty(std::shared_ptr<const Json>(), &empty_schema());
+  return empty;
+}
+
 // resolveReference (grammar.ts:121-144): a local "#/..." ref, merged as { ...target, ...local }.
 SchemaPtr resolve_reference(const SchemaPtr& schema, const Json& root) {
   const Json* ref = schema->get("$ref");
@@ -446,7 +482,7 @@ void schema_alternatives(const SchemaPtr& schema, const Json& root, std::vector<
     return;
   }
   if (choices->kind != Json::Array) throw SchemaError("oneOf / anyOf must be an array");
-  for (const Json& c : choices->arr) schema_alternatives(std::make_shared<Json>(c), root, out);
+  for (const Json& c : choices->arr) schema_alternatives(subschema(resolved, &c), root, out);
 }
 
 const char* json_type(const Json& v) {
@@ -688,6 +724,134 @@ class SchemaGrammar {
     return nullptr;
   }
 
+  // True while the next byte goes to the content of a started string (not after a backslash, not
+  // inside the hex digits of \u): every byte >= 0x20 other than '"' and '\\' is then accepted and
+  // only appended to the string's bytes, which the allowed-token walk exploits.
+  bool in_string_content() const {
+    if (complete_ || stack_.empty()) return false;
+    const Frame& f = stack_.back();
+    return f.kind == Frame::String && f.started && !f.escaped && f.unicode_remaining == 0;
+  }
+
+  // True when feed_byte(byte) would certainly return false, judged from the top frame without
+  // changing anything; false means "feed a copy to find out".  Each case restates the first check
+  // feed_byte makes for that frame.
+  bool rejects(int byte) const {
+    if (complete_ || stack_.empty()) return true;
+    const Frame& f = stack_.back();
+    switch (f.kind) {
+      case Frame::String:
+        if (!f.started) return byte != 0x22;
+        if (f.unicode_remaining > 0)
+          return !((byte >= 0x30 && byte <= 0x39) || (byte >= 0x41 && byte <= 0x46) || (byte >= 0x61 && byte <= 0x66));
+        if (f.escaped) {
+          static const int ok[] = {0x22, 0x5c, 0x2f, 0x62, 0x66, 0x6e, 0x72, 0x74, 0x75};
+          return std::find(std::begin(ok), std::end(ok), byte) == std::end(ok);
+        }
+        return byte < 0x20;
+      case Frame::Number: {
+        const char c = (char)byte;
+        if ((c >= '0' && c <= '9') || c == 'e' || c == 'E' || c == '+' || c == '-' || c == '.')
+          return !is_number_prefix(f.text + c);
+        return !is_complete_number(f.text);
+      }
+      case Frame::Literal:
+        return byte != (unsigned char)f.literal[f.offset];
+      case Frame::Choice:
+        for (const auto& c : f.candidates)
+          if (c.offset == (int)c.bytes.size() || (unsigned char)c.bytes[c.offset] == byte) return false;
+        return true;
+      case Frame::Key:
+        for (const auto& c : f.candidates)
+          if (byte == 0x22 ? c.offset == (int)c.bytes.size()
+                           : c.offset < (int)c.bytes.size() && (unsigned char)c.bytes[c.offset] == byte)
+            return false;
+        return true;
+      case Frame::Array:
+        if (f.phase == Frame::Open) return byte != 0x5b;
+        if (f.phase == Frame::AfterValue) return byte != 0x2c && byte != 0x5d;
+        return false;
+      case Frame::Object:
+        if (f.phase == Frame::Open) return byte != 0x7b;
+        if (f.phase == Frame::KeyOrEnd) return byte != 0x22 && byte != 0x7d;
+        if (f.phase == Frame::KeyRequired) return byte != 0x22;
+        if (f.phase == Frame::Colon) return byte != 0x3a;
+        if (f.phase == Frame::AfterValue) return byte != 0x2c && byte != 0x7d;
+        return false;
+      case Frame::Value:
+        return false;
+    }
+    return false;
+  }
+
+  // True while the top frame is a number that is not the whole document.  A byte of the number's
+  // charset then only extends number_text() (when the result is still a number prefix); any other
+  // byte ends the number (end_number) and goes to the frame below.
+  bool in_number() const { return !complete_ && stack_.size() >= 2 && stack_.back().kind == Frame::Number; }
+  const std::string& number_text() const { return stack_.back().text; }
+  void append_number(const char* bytes, size_t n) { stack_.back().text.append(bytes, n); }
+
+  // Ends the number on top of the stack as a following byte outside its charset does: false when
+  // the text is not a complete number or the value fails the schema.
+  bool end_number() {
+    const Frame& frame = stack_.back();
+    if (!is_complete_number(frame.text)) return false;
+    const double value = strtod(frame.text.c_str(), nullptr);
+    if (!validate_number(value, *frame.schema)) return false;
+    Json v;
+    v.kind = Json::Number;
+    v.num = value;
+    finish(std::move(v));
+    return true;
+  }
+
+  // Closing the current string (in_string_content) after more content bytes, decided without
+  // feeding: prepared once for a state, then asked about many byte runs.  The literal's bytes so far
+  // hold no unescaped quote and end outside an escape, and the run holds only content bytes, so
+  // JSON.parse of the closed literal is the content decoded so far followed by the run, and the UTF-8
+  // check continues from where the bytes so far left it.
+  struct StringClose {
+    Utf8Check utf8;
+    std::string decoded;
+    const Json* schema = nullptr;
+    bool constrained = false;  // the schema checks strings beyond their type
+    bool usable = false;
+    // Whether feeding `bytes` and then '"' is accepted.
+    bool accepts(const char* bytes, size_t n) const {
+      Utf8Check u = utf8;
+      for (size_t k = 0; k < n; k++) u.feed((uint8_t)bytes[k]);
+      u.feed(0x22);
+      if (!u.ok()) return false;
+      if (!constrained) return true;
+      std::string value = decoded;
+      value.append(bytes, n);
+      return validate_string(value, *schema);
+    }
+  };
+
+  StringClose string_close() const {
+    StringClose c;
+    const Frame& f = stack_.back();
+    for (unsigned char b : f.bytes) c.utf8.feed(b);
+    try {
+      Parser p{f.bytes + "\""};
+      Json v = p.document();
+      if (v.kind != Json::String) return c;
+      c.decoded = std::move(v.str);
+    } catch (const SchemaError&) {
+      return c;
+    }
+    c.schema = f.schema.get();
+    for (const char* key : {"minLength", "maxLength", "pattern", "format", "enum", "const"})
+      if (f.schema->get(key)) c.constrained = true;
+    c.usable = true;
+    return c;
+  }
+
+  // The same as feeding `bytes` one at a time (each >= 0x20, none '"' or '\\') while
+  // in_string_content().
+  void append_string_content(const char* bytes, size_t n) { stack_.back().bytes.append(bytes, n); }
+
   bool feed_byte(int byte) {
     if (complete_) return false;
     for (int retry = 0; retry < 16; retry++) {
@@ -817,13 +981,7 @@ class SchemaGrammar {
             frame.text = std::move(next);
             return true;
           }
-          if (!is_complete_number(frame.text)) return false;
-          const double value = strtod(frame.text.c_str(), nullptr);
-          if (!validate_number(value, *frame.schema)) return false;
-          Json v;
-          v.kind = Json::Number;
-          v.num = value;
-          finish(std::move(v));
+          if (!end_number()) return false;
           continue;
         }
         case Frame::Literal: {
@@ -871,13 +1029,13 @@ class SchemaGrammar {
             }
             if (count >= maximum) return false;
             frame.phase = Frame::InValue;
-            push_value(items ? std::make_shared<Json>(*items) : std::make_shared<Json>(empty_schema()));
+            push_value(subschema(frame.schema, items));
             continue;
           }
           if (frame.phase == Frame::AfterValue) {
             if (byte == 0x2c && count < maximum) {
               frame.phase = Frame::InValue;
-              push_value(items ? std::make_shared<Json>(*items) : std::make_shared<Json>(empty_schema()));
+              push_value(subschema(frame.schema, items));
               return true;
             }
             if (byte == 0x5d && count >= minimum) {
@@ -947,9 +1105,7 @@ class SchemaGrammar {
             frame.phase = Frame::InValue;
             const Json* p = properties ? properties->get(frame.current_key) : nullptr;
             const Json* extra = frame.schema->get("additionalProperties");
-            SchemaPtr child = p ? std::make_shared<Json>(*p)
-                                : (extra && extra->kind == Json::Object ? std::make_shared<Json>(*extra)
-                                                                        : std::make_shared<Json>(empty_schema()));
+            SchemaPtr child = subschema(frame.schema, p ? p : (extra && extra->kind == Json::Object ? extra : nullptr));
             push_value(std::move(child));
             return true;
           }
@@ -1128,10 +1284,40 @@ class ToolGrammar {
 
   bool complete() const { return phase_ == Done; }
   const std::vector<ToolCall>& calls() const { return calls_; }
+  bool in_string_content() const { return phase_ == Arguments && arguments_ && arguments_->in_string_content(); }
+
+  // As SchemaGrammar::rejects: feed_byte's first check for the current phase, without feeding.
+  bool rejects(int byte) const {
+    switch (phase_) {
+      case ArrayOpen: return byte != 0x5b;
+      case CallOpen: return byte != 0x7b;
+      case NameLiteral: return byte != (unsigned char)kName[literal_offset_];
+      case ToolName:
+        for (const auto& c : names_) {
+          const std::string& n = (*tools_)[c.first].name;
+          if (byte == 0x22 ? c.second == (int)n.size() : c.second < (int)n.size() && (unsigned char)n[c.second] == byte)
+            return false;
+        }
+        return true;
+      case ArgumentsLiteral: return byte != (unsigned char)kArguments[literal_offset_];
+      case Arguments:
+        if (!arguments_) return true;
+        if (arguments_->complete()) return byte != 0x7d;
+        return arguments_->rejects(byte);
+      case CallClose: return byte != 0x7d;
+      case AfterCall: return byte != 0x5d && byte != 0x2c;
+      case Done: return true;
+    }
+    return false;
+  }
+  void append_string_content(const char* bytes, size_t n) { arguments_->append_string_content(bytes, n); }
+  SchemaGrammar::StringClose string_close() const { return arguments_->string_close(); }
+  bool in_number() const { return phase_ == Arguments && arguments_ && arguments_->in_number(); }
+  const std::string& number_text() const { return arguments_->number_text(); }
+  void append_number(const char* bytes, size_t n) { arguments_->append_number(bytes, n); }
+  bool end_number() { return arguments_->end_number(); }
 
   bool feed_byte(int byte) {
-    static const std::string kName = "\"name\":\"";
-    static const std::string kArguments = ",\"arguments\":";
     for (int retry = 0; retry < 8; retry++) {
       switch (phase_) {
         case ArrayOpen:
@@ -1146,7 +1332,7 @@ class ToolGrammar {
         case NameLiteral:
           if (byte != (unsigned char)kName[literal_offset_]) return false;
           literal_offset_++;
-          if (literal_offset_ == (int)kName.size()) {
+          if (literal_offset_ == kNameLength) {
             phase_ = ToolName;
             names_.clear();
             for (int k = 0; k < (int)tools_->size(); k++)
@@ -1179,7 +1365,7 @@ class ToolGrammar {
         case ArgumentsLiteral:
           if (byte != (unsigned char)kArguments[literal_offset_]) return false;
           literal_offset_++;
-          if (literal_offset_ == (int)kArguments.size()) {
+          if (literal_offset_ == kArgumentsLength) {
             if (current_ < 0 || current_ >= (int)tools_->size()) return false;
             arguments_ = std::make_unique<SchemaGrammar>((*tools_)[current_].parameters);
             phase_ = Arguments;
@@ -1223,7 +1409,29 @@ class ToolGrammar {
         names_(o.names_), current_(o.current_), used_(o.used_),
         arguments_(o.arguments_ ? std::make_unique<SchemaGrammar>(*o.arguments_) : nullptr), calls_(o.calls_) {}
 
+  // Copy-assignment keeps this object's buffers (strings, vectors, the argument grammar) and only
+  // overwrites their contents, which is what the allowed-token walk's per-depth scratch relies on.
+  ToolGrammar& operator=(const ToolGrammar& o) {
+    if (this == &o) return *this;
+    tools_ = o.tools_;
+    maximum_calls_ = o.maximum_calls_;
+    phase_ = o.phase_;
+    literal_offset_ = o.literal_offset_;
+    names_ = o.names_;
+    current_ = o.current_;
+    used_ = o.used_;
+    if (!o.arguments_) arguments_.reset();
+    else if (arguments_) *arguments_ = *o.arguments_;
+    else arguments_ = std::make_unique<SchemaGrammar>(*o.arguments_);
+    calls_ = o.calls_;
+    return *this;
+  }
+
  private:
+  static constexpr const char kName[] = "\"name\":\"";
+  static constexpr int kNameLength = sizeof(kName) - 1;
+  static constexpr const char kArguments[] = ",\"arguments\":";
+  static constexpr int kArgumentsLength = sizeof(kArguments) - 1;
   enum Phase : uint8_t { ArrayOpen, CallOpen, NameLiteral, ToolName, ArgumentsLiteral, Arguments, CallClose, AfterCall, Done };
   std::shared_ptr<const std::vector<Tool>> tools_;
   int maximum_calls_;
@@ -1263,6 +1471,44 @@ struct Trie {
     nodes[cur].ids.push_back(id);
     max_len = std::max(max_len, n);
   }
+
+  // String content.  Inside a string every byte >= 0x20 other than '"' and '\\' is accepted and
+  // only appended, so from a string state at the root: every piece made only of such bytes is
+  // accepted (`plain`), a piece with a control byte before any quote or backslash is rejected, and
+  // the rest depend on the grammar from their first quote or backslash on (`exits`: the node below
+  // that byte, the byte, its depth and the plain bytes before it in `exit_bytes`).
+  struct Exit {
+    int32_t node, depth, prefix_offset, prefix_length;
+    uint8_t byte;
+  };
+  std::vector<uint8_t> plain;
+  std::vector<Exit> exits;
+  std::string exit_bytes;
+
+  void index_string_content(int32_t vocab_size) {
+    plain.assign(vocab_size, 0);
+    exits.clear();
+    exit_bytes.clear();
+    std::string path;
+    index_from(0, path);
+  }
+
+ private:
+  void index_from(int32_t node, std::string& path) {
+    for (uint32_t id : nodes[node].ids) plain[id] = 1;
+    for (const auto& edge : nodes[node].children) {
+      const uint8_t b = edge.first;
+      if (b < 0x20) continue;
+      if (b == 0x22 || b == 0x5c) {
+        exits.push_back({edge.second, (int32_t)path.size() + 1, (int32_t)exit_bytes.size(), (int32_t)path.size(), b});
+        exit_bytes += path;
+        continue;
+      }
+      path.push_back((char)b);
+      index_from(edge.second, path);
+      path.pop_back();
+    }
+  }
 };
 
 }  // namespace
@@ -1278,6 +1524,7 @@ struct needle_grammar {
 
 struct needle_vocab {
   Trie trie;
+  int32_t size = 0;  // ids are below this
 };
 
 namespace {
@@ -1287,26 +1534,173 @@ int fail(int code, const std::string& msg) {
   return code;
 }
 
+// The trie walk.  `mark` collects accepted ids; `pending` holds the string-content bytes fed since
+// walk_string's `base`, `number` the whole text of the number walk_number is extending.
+struct Walk {
+  const Trie& trie;
+  int32_t limit;
+  std::vector<uint8_t>& mark;
+  std::string pending;
+  std::string number;
+};
+
+inline void mark_ids(Walk& w, int32_t node) {
+  for (uint32_t id : w.trie.nodes[node].ids) w.mark[id] = 1;
+}
+
+inline bool number_byte(uint8_t c) {
+  return (c >= '0' && c <= '9') || c == 'e' || c == 'E' || c == '+' || c == '-' || c == '.';
+}
+
+// Grammars per trie depth, per thread, kept across calls: copying a state into one by assignment
+// reuses its buffers instead of allocating a new copy for every trie edge.  Tag 0 holds the state
+// after an edge, tag 1 the state after a number ended at a node.
+template <class G, int Tag>
+G& scratch(int32_t depth, const G& from) {
+  thread_local std::vector<std::unique_ptr<G>> slots;
+  if ((int32_t)slots.size() <= depth) slots.resize(depth + 1);
+  if (!slots[depth]) slots[depth] = std::make_unique<G>(from);
+  else *slots[depth] = from;
+  return *slots[depth];
+}
+
 template <class G>
-void walk(const Trie& t, int32_t node, const G& g, int32_t depth, int32_t limit, std::vector<uint32_t>& out) {
-  for (const auto& edge : t.nodes[node].children) {
-    if (depth + 1 > limit) break;
-    G next(g);
+void descend(Walk& w, int32_t node, const G& g, int32_t depth);
+
+// The general case: every edge the grammar does not reject outright is fed to a copy.
+template <class G>
+void walk(Walk& w, int32_t node, const G& g, int32_t depth) {
+  for (const auto& edge : w.trie.nodes[node].children) {
+    if (depth + 1 > w.limit) break;
+    if (g.rejects(edge.first)) continue;
+    G& next = scratch<G, 0>(depth + 1, g);
     if (!next.feed_byte(edge.first)) continue;
-    const auto& ids = t.nodes[edge.second].ids;
-    out.insert(out.end(), ids.begin(), ids.end());
-    walk(t, edge.second, next, depth + 1, limit, out);
+    mark_ids(w, edge.second);
+    descend(w, edge.second, next, depth + 1);
   }
 }
 
-void allowed(const needle_grammar& g, const Trie& t, int64_t output_bytes, std::vector<uint32_t>& out) {
+// `base` is inside a string's content and the bytes on the path since then are in w.pending.
+// Content bytes (>= 0x20, not '"' or '\\') are accepted without looking at the grammar, so the
+// subtree below them is walked without copying it; a quote or backslash edge applies the pending
+// bytes to a copy and continues from there.  Control bytes are rejected in a string.
+template <class G>
+void walk_string(Walk& w, int32_t node, const G& base, int32_t depth) {
+  if (node == 0 && w.limit >= w.trie.max_len) {  // from the root: the index built at vocab open
+    for (size_t id = 0; id < w.mark.size(); id++) w.mark[id] |= w.trie.plain[id];
+    // A closing quote is judged by StringClose; what follows it in the piece goes to the frame
+    // below the string, whose first check does not depend on the string's value, so `closed` (the
+    // state after any accepted close) rejects most continuations without a copy.
+    const auto close = base.string_close();
+    const G* closed = nullptr;
+    for (const auto& e : w.trie.exits) {
+      const char* prefix = w.trie.exit_bytes.data() + e.prefix_offset;
+      const auto& children = w.trie.nodes[e.node].children;
+      if (e.byte == 0x22 && close.usable) {
+        if (!close.accepts(prefix, e.prefix_length)) continue;
+        mark_ids(w, e.node);
+        bool more = false;
+        for (const auto& c : children)
+          if (!closed || !closed->rejects(c.first)) {
+            more = true;
+            break;
+          }
+        if (!more) continue;
+      }
+      G& next = scratch<G, 0>(e.depth, base);
+      next.append_string_content(prefix, e.prefix_length);
+      if (!next.feed_byte(e.byte)) continue;
+      mark_ids(w, e.node);
+      if (e.byte == 0x22 && !closed) closed = &scratch<G, 2>(0, next);
+      descend(w, e.node, next, e.depth);
+    }
+    return;
+  }
+  for (const auto& edge : w.trie.nodes[node].children) {
+    if (depth + 1 > w.limit) break;
+    const uint8_t b = edge.first;
+    if (b < 0x20) continue;
+    if (b != 0x22 && b != 0x5c) {
+      mark_ids(w, edge.second);
+      w.pending.push_back((char)b);
+      walk_string(w, edge.second, base, depth + 1);
+      w.pending.pop_back();
+      continue;
+    }
+    G& next = scratch<G, 0>(depth + 1, base);
+    next.append_string_content(w.pending.data(), w.pending.size());
+    if (!next.feed_byte(b)) continue;
+    mark_ids(w, edge.second);
+    descend(w, edge.second, next, depth + 1);
+  }
+}
+
+// `base` is inside a number whose text, with the path's bytes since `base`, is w.number (the first
+// `base_length` bytes are base's own).  A number byte is accepted when the text stays a number
+// prefix, with no copy; the other bytes end the number once per node, on a copy, and are fed to
+// what lies below it.
+template <class G>
+void walk_number(Walk& w, int32_t node, const G& base, size_t base_length, int32_t depth) {
+  const G* ended = nullptr;
+  bool tried = false;
+  for (const auto& edge : w.trie.nodes[node].children) {
+    if (depth + 1 > w.limit) break;
+    const uint8_t b = edge.first;
+    if (number_byte(b)) {
+      w.number.push_back((char)b);
+      if (is_number_prefix(w.number)) {
+        mark_ids(w, edge.second);
+        walk_number(w, edge.second, base, base_length, depth + 1);
+      }
+      w.number.pop_back();
+      continue;
+    }
+    if (!tried) {
+      tried = true;
+      if (is_complete_number(w.number)) {
+        G& e = scratch<G, 1>(depth, base);
+        e.append_number(w.number.data() + base_length, w.number.size() - base_length);
+        if (e.end_number()) ended = &e;
+      }
+    }
+    if (!ended || ended->rejects(b)) continue;
+    G& next = scratch<G, 0>(depth + 1, *ended);
+    if (!next.feed_byte(b)) continue;
+    mark_ids(w, edge.second);
+    descend(w, edge.second, next, depth + 1);
+  }
+}
+
+// Walks the subtree below `node` from grammar state `g` with the walk that suits the state.
+template <class G>
+void descend(Walk& w, int32_t node, const G& g, int32_t depth) {
+  if (g.in_string_content()) {
+    std::string saved;
+    saved.swap(w.pending);
+    walk_string(w, node, g, depth);
+    w.pending.swap(saved);
+  } else if (g.in_number()) {
+    std::string saved(g.number_text());
+    saved.swap(w.number);
+    walk_number(w, node, g, w.number.size(), depth);
+    w.number.swap(saved);
+  } else {
+    walk(w, node, g, depth);
+  }
+}
+
+// Ascending ids whose piece the grammar accepts; `mark` is scratch of the vocabulary's size.
+void allowed(const needle_grammar& g, const needle_vocab& v, int64_t output_bytes, std::vector<uint8_t>& mark,
+             std::vector<uint32_t>& out) {
   out.clear();
   const int64_t room = 65536 - output_bytes;  // agent.ts:171: output bytes stay within 64 KiB
   if (room <= 0) return;
-  const int32_t limit = (int32_t)std::min<int64_t>(room, t.max_len);
-  if (g.schema) walk(t, 0, *g.schema, 0, limit, out);
-  else walk(t, 0, *g.tools, 0, limit, out);
-  std::sort(out.begin(), out.end());
+  mark.assign(v.size, 0);
+  Walk w{v.trie, (int32_t)std::min<int64_t>(room, v.trie.max_len), mark, {}, {}};
+  if (g.schema) descend(w, 0, *g.schema, 0);
+  else descend(w, 0, *g.tools, 0);
+  for (int32_t id = 0; id < v.size; id++)
+    if (mark[id]) out.push_back((uint32_t)id);
 }
 
 }  // namespace
@@ -1404,11 +1798,13 @@ int needle_grammar_result(const needle_grammar* g, char* buf, int32_t capacity, 
 int needle_vocab_open(const uint8_t* bytes, const int32_t* offsets, int32_t n, needle_vocab** out) {
   if (!out || n < 0 || (n > 0 && (!bytes || !offsets))) return fail(NEEDLE_INVALID_TOOL_SCHEMA, "null argument");
   auto v = std::make_unique<needle_vocab>();
+  v->size = n;
   for (int32_t id = 0; id < n; id++) {
     const int32_t len = offsets[id + 1] - offsets[id];
     if (len < 0) return fail(NEEDLE_INVALID_TOOL_SCHEMA, "offsets must not decrease");
     if (len > 0) v->trie.insert(bytes + offsets[id], len, (uint32_t)id);
   }
+  v->trie.index_string_content(n);
   *out = v.release();
   return NEEDLE_OK;
 }
@@ -1419,8 +1815,9 @@ int needle_grammar_allowed(const needle_grammar* g, const needle_vocab* v, int64
                            int32_t capacity, int32_t* count) {
   if (!g || !v || !count) return fail(NEEDLE_INVALID_TOOL_SCHEMA, "null argument");
   try {
+    std::vector<uint8_t> mark;
     std::vector<uint32_t> out;
-    allowed(*g, v->trie, output_bytes, out);
+    allowed(*g, *v, output_bytes, mark, out);
     *count = (int32_t)out.size();
     if ((int32_t)out.size() > capacity) return fail(NEEDLE_INVALID_TOOL_SCHEMA, "id buffer too small");
     if (!out.empty()) memcpy(ids, out.data(), out.size() * sizeof(uint32_t));
@@ -1439,6 +1836,7 @@ int needle_grammar_allowed_batch(const needle_grammar* const* grammars, const in
   std::atomic<int> status{NEEDLE_OK};
   std::string message;
   auto work = [&]() {
+    std::vector<uint8_t> mark;
     std::vector<uint32_t> out;
     for (int k; (k = next.fetch_add(1)) < n;) {
       try {
@@ -1446,7 +1844,7 @@ int needle_grammar_allowed_batch(const needle_grammar* const* grammars, const in
           counts[k] = 0;
           continue;
         }
-        allowed(*grammars[k], v->trie, output_bytes[k], out);
+        allowed(*grammars[k], *v, output_bytes[k], mark, out);
         counts[k] = (int32_t)out.size();
         if ((int32_t)out.size() > capacity_each) {
           status.store(NEEDLE_INVALID_TOOL_SCHEMA);

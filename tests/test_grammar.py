@@ -178,3 +178,41 @@ def test_output_limit(G):
     assert G.allowed(g, v, 65_536).size == 0
     near = G.allowed(g, v, 65_535)
     assert near.size > 0 and all(len(v.piece[i]) == 1 for i in near)
+
+
+@pytest.mark.parametrize("case", range(5))
+def test_walk_shortcuts_equal_clone_and_feed_scan(G, case):
+    """String content (the vocabulary-wide index, the closing-quote check, the byte pieces that break
+    UTF-8) and number text are walked without feeding every edge: the ids must still be exactly
+    those a clone accepts."""
+    schema, opening = [
+        ({"type": "array", "items": {"type": "string"}, "maxItems": 3}, b'["'),
+        ({"type": "object", "properties": {"a": {"type": "string", "maxLength": 6}, "b": {"type": "integer"}}},
+         b'{"a":"'),
+        ({"type": "object", "properties": {"k": {"type": "string", "minLength": 3, "pattern": "^[a-z0-9 ]*$"},
+                                           "n": {"type": "number"}}, "required": ["k"]}, b'{"k":"'),
+        ({"type": "array", "items": {"type": "string", "enum": ["ab", "ab cd", "x\u00e9"]}, "uniqueItems": True},
+         b'["'),
+        ({"type": "array", "items": {"type": "number", "minimum": -5, "maximum": 5000}}, b"[1"),
+    ][case]
+    v = _vocab(G)
+    g = G.JsonSchemaGrammar(schema)
+    assert g.feed(opening)
+    rng = np.random.default_rng(case)
+    text = opening
+    simple = set(b"abcdefghijklmnopqrstuvwxyz0123456789 ")
+    for step in range(30):
+        ids = G.allowed(g, v, len(text))
+        scan = [i for i in range(v.size) if v.piece[i] and g.clone().feed(v.piece[i])]
+        np.testing.assert_array_equal(ids, np.array(scan, dtype=np.uint32), err_msg=f"{text!r}")
+        if ids.size == 0 or g.complete:
+            break
+        # mostly simple text (so patterns and lengths can still pass), sometimes a piece that closes
+        # the current string or number, sometimes anything (bytes that break UTF-8 included)
+        closing = [i for i in ids if any(b in v.piece[i] for b in (b'",]' if case == 4 else b'"'))]
+        plain = [i for i in ids if set(v.piece[i]) <= simple]
+        r = rng.random()
+        pool = closing if closing and r < (0.08 if case == 4 else 0.2) else plain if plain and r < 0.8 else ids
+        pick = int(pool[rng.integers(0, len(pool))])
+        assert g.feed(v.piece[pick])
+        text += v.piece[pick]
