@@ -139,6 +139,18 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n,
                      const uint32_t* allowed_ids, size_t allowed_total,
                      needle_selected* out_selected, float* out_logits);
 
+/* needle_cuda_step in two halves, for constrained decoding, where the allowed ids of a step depend
+ * only on tokens already chosen and can be computed on the host while the step's layers run.
+ * needle_cuda_step_begin checks the items and enqueues every layer and the vocabulary projection,
+ * then returns without waiting; needle_cuda_step_end takes the same items (same slots and tokens in
+ * the same order; a select may be cleared, e.g. for a grammar dead end, but not set) with their
+ * allowed lists, selects, waits and advances the slots, exactly as needle_cuda_step with those items
+ * would have.  No other call may use the context in between (BACKEND_UNAVAILABLE).  If step_end
+ * fails, the step is dropped: the slots keep their positions.  Logits are not returned. */
+int needle_cuda_step_begin(needle_ctx* ctx, const needle_step_item* items, int32_t n);
+int needle_cuda_step_end(needle_ctx* ctx, const needle_step_item* items, int32_t n, const uint32_t* allowed_ids,
+                         size_t allowed_total, needle_selected* out_selected);
+
 /* NeedleRuntime.prefill (runtime.ts:227-243) for one slot: n steps, logits of the last one
  * written to out_logits (vocabulary floats) when non-NULL. */
 int needle_cuda_prefill(needle_ctx* ctx, int32_t seq, const int32_t* ids, int32_t n, float* out_logits);

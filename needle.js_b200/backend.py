@@ -99,8 +99,8 @@ class CudaEngine:
         check(lib().needle_cuda_seq_position(self.h, seq, C.byref(p)))
         return p.value
 
-    def step(self, requests: Sequence[StepRequest], want_logits: bool = False):
-        """One batched step; returns (selected list of (id, logprob) or None per request, logits)."""
+    @staticmethod
+    def _items(requests: Sequence[StepRequest]):
         n = len(requests)
         items = (native.StepItem * max(n, 1))()
         allowed_parts, offset = [], 0
@@ -118,6 +118,12 @@ class CudaEngine:
                 items[i].allowed_count = -1
                 items[i].allowed_offset = 0
         allowed = np.concatenate(allowed_parts) if allowed_parts else None
+        return items, allowed
+
+    def step(self, requests: Sequence[StepRequest], want_logits: bool = False):
+        """One batched step; returns (selected list of (id, logprob) or None per request, logits)."""
+        n = len(requests)
+        items, allowed = self._items(requests)
         sel = (native.Selected * max(n, 1))()
         logits = np.zeros((n, self.vocab), dtype=np.float32) if want_logits else None
         check(lib().needle_cuda_step(self.h, C.cast(items, C.c_void_p), n, ptr(allowed),
@@ -125,6 +131,22 @@ class CudaEngine:
                                      ptr(logits)))
         out = [(sel[i].id, sel[i].log_probability) if r.select else None for i, r in enumerate(requests)]
         return out, logits
+
+    def step_begin(self, requests: Sequence[StepRequest]):
+        """First half of a step (needle_cuda_step_begin): the layers are enqueued and this returns at
+        once; the requests' allowed lists are not read.  step_end must follow before any other call."""
+        items, _ = self._items(requests)
+        check(lib().needle_cuda_step_begin(self.h, C.cast(items, C.c_void_p), len(requests)))
+
+    def step_end(self, requests: Sequence[StepRequest]):
+        """Second half: the same requests (a select may be cleared), now with their allowed lists;
+        returns the selections as step does."""
+        n = len(requests)
+        items, allowed = self._items(requests)
+        sel = (native.Selected * max(n, 1))()
+        check(lib().needle_cuda_step_end(self.h, C.cast(items, C.c_void_p), n, ptr(allowed),
+                                         0 if allowed is None else allowed.size, C.cast(sel, C.c_void_p)))
+        return [(sel[i].id, sel[i].log_probability) if r.select else None for i, r in enumerate(requests)]
 
     def prefill(self, seq: int, ids, want_logits: bool = True):
         ids = np.ascontiguousarray(ids, dtype=np.int32)

@@ -357,6 +357,14 @@ struct needle_ctx {
   double* h_logprob = nullptr;
   uint32_t* d_allowed = nullptr;
   size_t allowed_cap = 0;
+  DevItem* h_items_end = nullptr;  // the items as needle_cuda_step_end re-uploads them
+  // a step begun by needle_cuda_step_begin and not yet ended
+  struct PendingStep {
+    bool active = false;
+    int n = 0, n_sel = 0;
+    std::vector<int> order;
+    std::vector<needle_step_item> items;
+  } pending;
   // scheduler
   SchedView sched{};
   bool sched_loaded = false;
@@ -678,6 +686,7 @@ void build_state(needle_ctx& C) {
   C.d_allowed = C.dalloc<uint32_t>(C.allowed_cap);
   st.allowed = C.d_allowed;
   cuda_check(cudaMallocHost(&C.h_items, B * sizeof(DevItem)), "cudaMallocHost");
+  cuda_check(cudaMallocHost(&C.h_items_end, B * sizeof(DevItem)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_counts, 4 * sizeof(int32_t)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_ids, B * sizeof(int32_t)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_logprob, B * sizeof(double)), "cudaMallocHost");
@@ -764,7 +773,7 @@ StepView half_view(const needle_ctx& C, int offset, const int32_t* n_items, cons
 // The kernel sequence of one batched step for up to n_host items of view `st` (device counts in
 // st.n_items / st.n_select), on the lane's streams.
 void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select, const SchedView* sched,
-                  const Lane& lane) {
+                  const Lane& lane, bool finish = true) {
   const ModelView& m = C.mv;
   const SlotView& sv = C.sv;
   const int32_t* n_dev = st.n_items;
@@ -809,7 +818,7 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
   if (any_select)
     run_gemv(C, P_GEMV_VOCAB, {{m.embedding, 0, m.vocab, st.prep_f, kDim, st.logits, m.vocab}}, n_host,
              st.n_select, s0);
-  C.timed(P_FINISH, [&] { return launch_finish(m, sv, st, n_host, sched, s0); }, s0);
+  if (finish) C.timed(P_FINISH, [&] { return launch_finish(m, sv, st, n_host, sched, s0); }, s0);
 }
 
 Lane lane_a(needle_ctx& C) { return Lane{C.stream, C.side, C.fork_ev, C.join_ev}; }
@@ -839,8 +848,12 @@ void enqueue_sched_step(needle_ctx& C) {
   cuda_check(cudaStreamWaitEvent(C.stream, C.merge_ev, 0), "merge");
 }
 
+// The context of every call except needle_cuda_step_end and needle_cuda_close: none may run while a
+// step begun by needle_cuda_step_begin is waiting for its end.
 needle_ctx* ctx_of(needle_ctx* c) {
   require(c != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null needle context");
+  require(!c->pending.active, NEEDLE_BACKEND_UNAVAILABLE,
+          "needle_cuda_step_begin was called; needle_cuda_step_end must come first");
   cuda_check(cudaSetDevice(c->device), "cudaSetDevice");
   return c;
 }
@@ -862,6 +875,7 @@ void destroy(needle_ctx* C) {
   if (C->d_rows) cudaFree(C->d_rows);
   if (C->d_row_out) cudaFree(C->d_row_out);
   if (C->h_items) cudaFreeHost(C->h_items);
+  if (C->h_items_end) cudaFreeHost(C->h_items_end);
   if (C->h_counts) cudaFreeHost(C->h_counts);
   if (C->h_ids) cudaFreeHost(C->h_ids);
   if (C->h_logprob) cudaFreeHost(C->h_logprob);
@@ -900,6 +914,125 @@ void ensure_mv(needle_ctx& C, size_t floats) {
 }  // namespace
 
 // ------------------------------------------------------------------ C-ABI
+
+namespace {
+
+// Checks one item's allowed list against the vocabulary (selectToken, runtime.ts:880-899).
+void check_allowed(const needle_step_item& it, const uint32_t* allowed_ids, size_t allowed_total, int V) {
+  if (it.allowed_count < 0) return;
+  require(it.allowed_count > 0, NEEDLE_INVALID_CACT, "Allowed token set is empty");
+  require(allowed_ids != nullptr && uint64_t(it.allowed_offset) + uint64_t(it.allowed_count) <= allowed_total,
+          NEEDLE_INVALID_CACT, "allowed ids out of range");
+  const uint32_t* ids = allowed_ids + it.allowed_offset;
+  for (int32_t k = 0; k < it.allowed_count; k++)
+    if (ids[k] >= uint32_t(V)) fail(NEEDLE_INVALID_CACT, "Token " + std::to_string(ids[k]) + " is outside logits");
+}
+
+// Validates the items of a step (allowed lists too when `allowed` is set); returns the number that
+// select.
+int check_items(needle_ctx& C, const needle_step_item* items, int32_t n, bool allowed, const uint32_t* allowed_ids,
+                size_t allowed_total, bool have_selected) {
+  require(n >= 0 && n <= C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "item count out of range");
+  require(n == 0 || items != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null items");
+  std::vector<char> seen(C.opts.max_seqs, 0);
+  const int V = C.mv.vocab;
+  int n_sel = 0;
+  for (int i = 0; i < n; i++) {
+    const needle_step_item& it = items[i];
+    require(it.seq >= 0 && it.seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
+    require(!seen[it.seq], NEEDLE_BACKEND_UNAVAILABLE, "a slot appears twice in one step");
+    seen[it.seq] = 1;
+    const SlotHost& h = C.slots[it.seq];
+    require(h.ready, NEEDLE_INVALID_CACT, "Call runtime.reset() before decoding");
+    // messages are built only on failure: this loop runs for every item of every step
+    if (h.position >= h.max_len)
+      fail(NEEDLE_CONTEXT_OVERFLOW,
+           "Position " + std::to_string(h.position) + " reached runtime limit " + std::to_string(h.max_len));
+    if (!(it.token == NEEDLE_TOKEN_PENDING || (it.token >= 0 && it.token < V)))
+      fail(NEEDLE_INVALID_CACT, "Token " + std::to_string(it.token) + " is outside the vocabulary");
+    if (it.select) {
+      require(have_selected, NEEDLE_BACKEND_UNAVAILABLE, "selection requested without output");
+      if (allowed) check_allowed(it, allowed_ids, allowed_total, V);
+      n_sel++;
+    }
+  }
+  return n_sel;
+}
+
+// The device items in internal order (items that need logits first) into `dst`; order[i] is item
+// i's row.
+void stage_items(needle_ctx& C, const needle_step_item* items, int32_t n, int n_sel, bool all_logits,
+                 std::vector<int>& order, DevItem* dst) {
+  int pos_sel = 0, pos_rest = all_logits ? 0 : n_sel;
+  order.resize(n);
+  for (int i = 0; i < n; i++) {
+    const needle_step_item& it = items[i];
+    const bool first = all_logits || it.select;
+    const int k = all_logits ? pos_sel++ : (first ? pos_sel++ : pos_rest++);
+    order[i] = k;
+    DevItem d{};
+    d.slot = it.seq;
+    d.token = it.token;
+    d.select = it.select ? 1 : 0;
+    d.allowed_count = it.select ? it.allowed_count : -1;
+    d.allowed_offset = it.allowed_offset;
+    d.position = C.slots[it.seq].position;
+    d.out_index = i;
+    dst[k] = d;
+  }
+}
+
+void upload_allowed(needle_ctx& C, const uint32_t* allowed_ids, size_t allowed_total) {
+  if (allowed_total == 0 || !allowed_ids) return;
+  if (allowed_total > C.allowed_cap) {
+    uint32_t* p = nullptr;
+    cuda_check(cudaMalloc(&p, allowed_total * 4), "cudaMalloc");
+    C.allocs.push_back(p);
+    C.d_allowed = p;
+    C.allowed_cap = allowed_total;
+    C.stv.allowed = p;
+  }
+  cuda_check(cudaMemcpyAsync(C.d_allowed, allowed_ids, allowed_total * 4, cudaMemcpyHostToDevice, C.stream),
+             "allowed upload");
+}
+
+void upload_items(needle_ctx& C, const DevItem* src, int n, int rows) {
+  C.h_counts[0] = n;
+  C.h_counts[1] = rows;
+  C.timed(P_COPY, [&] {
+    cudaError_t e = cudaMemcpyAsync(C.stv.items, src, size_t(n) * sizeof(DevItem), cudaMemcpyHostToDevice, C.stream);
+    if (e != cudaSuccess) return e;
+    return cudaMemcpyAsync(C.d_counts, C.h_counts, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, C.stream);
+  });
+}
+
+// Reads the selections (and logits) back, waits for the step and advances the slots.
+void complete_step(needle_ctx& C, const needle_step_item* items, int32_t n, int rows, const std::vector<int>& order,
+                   needle_selected* out_selected, float* out_logits) {
+  const int V = C.mv.vocab;
+  if (rows > 0) {
+    cuda_check(cudaMemcpyAsync(C.h_ids, C.stv.out_id, size_t(rows) * 4, cudaMemcpyDeviceToHost, C.stream), "readback");
+    cuda_check(cudaMemcpyAsync(C.h_logprob, C.stv.out_logprob, size_t(rows) * 8, cudaMemcpyDeviceToHost, C.stream),
+               "readback");
+  }
+  if (out_logits) {
+    for (int i = 0; i < n; i++)
+      cuda_check(cudaMemcpyAsync(out_logits + size_t(i) * V, C.stv.logits + size_t(order[i]) * V, size_t(V) * 4,
+                                 cudaMemcpyDeviceToHost, C.stream),
+                 "logits readback");
+  }
+  cuda_check(cudaStreamSynchronize(C.stream), "step");
+  for (int i = 0; i < n; i++) {
+    C.slots[items[i].seq].position++;
+    if (items[i].select) {
+      out_selected[i].id = C.h_ids[order[i]];
+      out_selected[i].reserved = 0;
+      out_selected[i].log_probability = C.h_logprob[order[i]];
+    }
+  }
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -1064,101 +1197,84 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, 
                      size_t allowed_total, needle_selected* out_selected, float* out_logits) {
   return guarded([&] {
     needle_ctx& C = *ctx_of(ctx);
-    require(n >= 0 && n <= C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "item count out of range");
+    const int n_sel = check_items(C, items, n, true, allowed_ids, allowed_total, out_selected != nullptr);
     if (n == 0) return;
-    require(items != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null items");
-    std::vector<char> seen(C.opts.max_seqs, 0);
+    const bool all_logits = out_logits != nullptr;
+    std::vector<int> order;
+    stage_items(C, items, n, n_sel, all_logits, order, C.h_items);
+    upload_allowed(C, allowed_ids, allowed_total);
+    const int rows = all_logits ? n : n_sel;
+    upload_items(C, C.h_items, n, rows);
+    enqueue_step(C, C.stv, n, n_sel > 0 || all_logits, nullptr, lane_a(C));
+    complete_step(C, items, n, rows, order, out_selected, out_logits);
+  });
+}
+
+int needle_cuda_step_begin(needle_ctx* ctx, const needle_step_item* items, int32_t n) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    const int n_sel = check_items(C, items, n, false, nullptr, 0, true);
+    require(n > 0, NEEDLE_BACKEND_UNAVAILABLE, "a split step needs at least one item");
+    auto& P = C.pending;
+    stage_items(C, items, n, n_sel, false, P.order, C.h_items);
+    upload_items(C, C.h_items, n, n_sel);
+    enqueue_step(C, C.stv, n, n_sel > 0, nullptr, lane_a(C), /*finish=*/false);
+    P.items.assign(items, items + n);
+    P.n = n;
+    P.n_sel = n_sel;
+    P.active = true;
+  });
+}
+
+int needle_cuda_step_end(needle_ctx* ctx, const needle_step_item* items, int32_t n, const uint32_t* allowed_ids,
+                         size_t allowed_total, needle_selected* out_selected) {
+  return guarded([&] {
+    require(ctx != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null needle context");
+    needle_ctx& C = *ctx;
+    auto& P = C.pending;
+    require(P.active, NEEDLE_BACKEND_UNAVAILABLE, "needle_cuda_step_end without needle_cuda_step_begin");
+    cuda_check(cudaSetDevice(C.device), "cudaSetDevice");
+    // On any failure below the begun work is drained and the step is dropped: the slots keep
+    // their positions, so their next step rewrites the K/V this one appended.
+    struct Drop {
+      needle_ctx& C;
+      bool armed = true;
+      ~Drop() {
+        if (!armed) return;
+        cudaStreamSynchronize(C.stream);
+        C.pending.active = false;
+      }
+    } drop{C};
+    require(n == P.n && items != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "step_end items differ from step_begin's");
     const int V = C.mv.vocab;
-    int n_sel = 0;
-    bool any_sel = out_logits != nullptr;
     for (int i = 0; i < n; i++) {
       const needle_step_item& it = items[i];
-      require(it.seq >= 0 && it.seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
-      require(!seen[it.seq], NEEDLE_BACKEND_UNAVAILABLE, "a slot appears twice in one step");
-      seen[it.seq] = 1;
-      const SlotHost& h = C.slots[it.seq];
-      require(h.ready, NEEDLE_INVALID_CACT, "Call runtime.reset() before decoding");
-      // messages are built only on failure: this loop runs for every item of every step
-      if (h.position >= h.max_len)
-        fail(NEEDLE_CONTEXT_OVERFLOW,
-             "Position " + std::to_string(h.position) + " reached runtime limit " + std::to_string(h.max_len));
-      if (!(it.token == NEEDLE_TOKEN_PENDING || (it.token >= 0 && it.token < V)))
-        fail(NEEDLE_INVALID_CACT, "Token " + std::to_string(it.token) + " is outside the vocabulary");
+      const needle_step_item& b = P.items[i];
+      require(it.seq == b.seq && it.token == b.token && (!it.select || b.select), NEEDLE_BACKEND_UNAVAILABLE,
+              "step_end items differ from step_begin's (only select may be cleared)");
       if (it.select) {
         require(out_selected != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "selection requested without output");
-        if (it.allowed_count >= 0) {
-          require(it.allowed_count > 0, NEEDLE_INVALID_CACT, "Allowed token set is empty");
-          require(allowed_ids != nullptr && uint64_t(it.allowed_offset) + uint64_t(it.allowed_count) <= allowed_total,
-                  NEEDLE_INVALID_CACT, "allowed ids out of range");
-          const uint32_t* ids = allowed_ids + it.allowed_offset;
-          for (int32_t k = 0; k < it.allowed_count; k++)
-            if (ids[k] >= uint32_t(V)) fail(NEEDLE_INVALID_CACT, "Token " + std::to_string(ids[k]) + " is outside logits");
-        }
-        n_sel++;
-        any_sel = true;
+        check_allowed(it, allowed_ids, allowed_total, V);
       }
     }
-    // internal order: items that need logits first
-    const bool all_logits = out_logits != nullptr;
-    int pos_sel = 0, pos_rest = all_logits ? 0 : n_sel;
-    std::vector<int> order(n);
+    // the allowed fields (and cleared selects) go in with a second copy of the items, ordered after
+    // the layers that read the first
     for (int i = 0; i < n; i++) {
-      const needle_step_item& it = items[i];
-      const bool first = all_logits || it.select;
-      const int k = all_logits ? pos_sel++ : (first ? pos_sel++ : pos_rest++);
-      order[i] = k;
-      DevItem d{};
-      d.slot = it.seq;
-      d.token = it.token;
-      d.select = it.select ? 1 : 0;
-      d.allowed_count = it.select ? it.allowed_count : -1;
-      d.allowed_offset = it.allowed_offset;
-      d.position = C.slots[it.seq].position;
-      d.out_index = i;
-      C.h_items[k] = d;
+      DevItem d = C.h_items[P.order[i]];
+      d.select = items[i].select ? 1 : 0;
+      d.allowed_count = items[i].select ? items[i].allowed_count : -1;
+      d.allowed_offset = items[i].allowed_offset;
+      C.h_items_end[P.order[i]] = d;
     }
-    if (allowed_total > 0 && allowed_ids) {
-      if (allowed_total > C.allowed_cap) {
-        uint32_t* p = nullptr;
-        cuda_check(cudaMalloc(&p, allowed_total * 4), "cudaMalloc");
-        C.allocs.push_back(p);
-        C.d_allowed = p;
-        C.allowed_cap = allowed_total;
-        C.stv.allowed = p;
-      }
-      cuda_check(cudaMemcpyAsync(C.d_allowed, allowed_ids, allowed_total * 4, cudaMemcpyHostToDevice, C.stream),
-                 "allowed upload");
-    }
-    C.h_counts[0] = n;
-    C.h_counts[1] = all_logits ? n : n_sel;
+    upload_allowed(C, allowed_ids, allowed_total);
     C.timed(P_COPY, [&] {
-      cudaError_t e = cudaMemcpyAsync(C.stv.items, C.h_items, size_t(n) * sizeof(DevItem), cudaMemcpyHostToDevice,
-                                      C.stream);
-      if (e != cudaSuccess) return e;
-      return cudaMemcpyAsync(C.d_counts, C.h_counts, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, C.stream);
+      return cudaMemcpyAsync(C.stv.items, C.h_items_end, size_t(n) * sizeof(DevItem), cudaMemcpyHostToDevice,
+                             C.stream);
     });
-    enqueue_step(C, C.stv, n, any_sel, nullptr, lane_a(C));
-    if (n_sel > 0 || all_logits) {
-      const int ns = all_logits ? n : n_sel;
-      cuda_check(cudaMemcpyAsync(C.h_ids, C.stv.out_id, size_t(ns) * 4, cudaMemcpyDeviceToHost, C.stream), "readback");
-      cuda_check(cudaMemcpyAsync(C.h_logprob, C.stv.out_logprob, size_t(ns) * 8, cudaMemcpyDeviceToHost, C.stream),
-                 "readback");
-    }
-    if (all_logits) {
-      for (int i = 0; i < n; i++)
-        cuda_check(cudaMemcpyAsync(out_logits + size_t(i) * V, C.stv.logits + size_t(order[i]) * V, size_t(V) * 4,
-                                   cudaMemcpyDeviceToHost, C.stream),
-                   "logits readback");
-    }
-    cuda_check(cudaStreamSynchronize(C.stream), "step");
-    for (int i = 0; i < n; i++) {
-      C.slots[items[i].seq].position++;
-      if (items[i].select) {
-        out_selected[i].id = C.h_ids[order[i]];
-        out_selected[i].reserved = 0;
-        out_selected[i].log_probability = C.h_logprob[order[i]];
-      }
-    }
+    C.timed(P_FINISH, [&] { return launch_finish(C.mv, C.sv, C.stv, n, nullptr, C.stream); }, C.stream);
+    complete_step(C, items, n, P.n_sel, P.order, out_selected, nullptr);
+    drop.armed = false;
+    P.active = false;
   });
 }
 

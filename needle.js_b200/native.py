@@ -74,6 +74,8 @@ EXPORTS = {
     "needle_cuda_seq_position": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
     "needle_cuda_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_size_t,
                                    C.c_void_p, C.c_void_p]),
+    "needle_cuda_step_begin": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
+    "needle_cuda_step_end": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_size_t, C.c_void_p]),
     "needle_cuda_prefill": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_void_p]),
     "needle_cuda_read_kv": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p, C.POINTER(C.c_int32)]),

@@ -4,8 +4,10 @@ The constrained loop of `Needle.complete` (packages/needle.js/src/tools/agent.ts
 many sequences at once: each step, every sequence in its constrained phase asks its
 `ToolCallGrammar` for the ids that may come next (the host-side scan, here a byte-trie walk on host
 threads, include/needle_grammar.h), the engine feeds the pending token and picks the best allowed
-id on the device (needle_cuda_step with an allowed list: the fused mask + argmax, ties to the
-first id of the list as selectToken does), and the chosen piece is fed to the grammar.  When the
+id on the device (an allowed list per item: the fused mask + argmax, ties to the first id of the
+list as selectToken does), and the chosen piece is fed to the grammar.  The scan runs while the
+step's layers run on the GPU (needle_cuda_step_begin / needle_cuda_step_end): the allowed ids only
+depend on tokens already chosen.  When the
 grammar completes, the chosen token is fed once more without a selection (agent.ts:193-196) and the
 slot is freed for the next sequence.  Prompts are fed one token per step through the same batched
 steps; the constrained phase starts directly after the prompt, its pending token being the prompt's
@@ -119,29 +121,30 @@ class ConstrainedDecoder:
                     selecting.append(len(requests) - 1)
                 else:  # "final": the completed call's last token, no selection
                     requests.append(StepRequest(s, st["pending"], False))
+            # The step's layers run on the GPU while the host computes the allowed ids, which depend
+            # only on tokens already chosen (needle_cuda_step_begin / _end).
             t0 = time.perf_counter()
+            eng.step_begin(requests)
+            t1 = time.perf_counter()
             masks = allowed_batch([state[requests[i].seq]["grammar"] for i in selecting],
                                   [state[requests[i].seq]["out"] for i in selecting], self.vocab, self.threads)
-            stats.grammar_seconds += time.perf_counter() - t0
+            t2 = time.perf_counter()
+            stats.grammar_seconds += t2 - t1
             for i, ids in zip(selecting, masks):
                 requests[i].allowed = ids
-            dead = {requests[i].seq for i, ids in zip(selecting, masks) if ids.size == 0}
-            if dead:  # GRAMMAR_DEAD_END: no token can continue; the sequence stops here
-                for s in dead:
-                    results[state[s]["seq"]].dead_end = True
-                    state[s] = None
-                requests = [r for r in requests if r.seq not in dead]
-            if not requests:
-                continue
+                if ids.size == 0:  # GRAMMAR_DEAD_END: no token can continue; the sequence stops here
+                    requests[i].select = False
+                    requests[i].allowed = None
+                    results[state[requests[i].seq]["seq"]].dead_end = True
+                    state[requests[i].seq]["phase"] = "dead"
             stats.items += len(requests)
             stats.allowed_ids += sum(int(r.allowed.size) for r in requests if r.allowed is not None)
-            t0 = time.perf_counter()
-            chosen, _ = eng.step(requests)
-            stats.engine_seconds += time.perf_counter() - t0
+            chosen = eng.step_end(requests)
+            stats.engine_seconds += (t1 - t0) + (time.perf_counter() - t2)
             stats.steps += 1
             for r, sel in zip(requests, chosen):
                 st = state[r.seq]
-                if st["phase"] == "final":
+                if st["phase"] in ("final", "dead"):
                     state[r.seq] = None
                     continue
                 if st["phase"] == "prompt" and not r.select:

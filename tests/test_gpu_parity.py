@@ -296,6 +296,42 @@ def test_masked_selection_matches_select_token(engine, oracle, ref_model):
         tok = gid
 
 
+def test_split_step_matches_step(engine, ref_model):
+    """needle_cuda_step_begin / _end (the host computes allowed ids while the layers run) select
+    exactly as needle_cuda_step; no other call may come in between; a failed end drops the step;
+    a select cleared at the end (a grammar dead end) just advances the slot."""
+    from needle_b200.backend import StepRequest
+    from needle_b200.native import NeedleError
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(0, ref_model.vocab, 9).astype(np.int32)
+    for s in (4, 5, 7):
+        engine.reset(s, 64, 0)
+        engine.prefill(s, prompt[:-1], want_logits=False)
+    tok = int(prompt[-1])
+    for k in range(5):
+        allowed = np.sort(rng.choice(ref_model.vocab, size=int(rng.integers(1, 3000)), replace=False)).astype(np.uint32)
+        want, _ = engine.step([StepRequest(4, tok, True, allowed)])
+        reqs = [StepRequest(7, int(prompt[k]), False), StepRequest(5, tok, True, None)]
+        engine.step_begin(reqs)
+        reqs[1].allowed = allowed
+        got = engine.step_end(reqs)
+        assert got[0] is None and got[1][0] == want[0][0] and got[1][1] == want[0][1]
+        tok = want[0][0]
+    assert engine.position(4) == engine.position(5) == len(prompt) - 1 + 5
+    pos = engine.position(5)
+    engine.step_begin([StepRequest(5, tok, True)])
+    with pytest.raises(NeedleError) as e:
+        engine.step([StepRequest(4, tok, False)])
+    assert e.value.code == "BACKEND_UNAVAILABLE"
+    with pytest.raises(NeedleError) as e:
+        engine.step_end([StepRequest(5, tok + 1, True, np.arange(5, dtype=np.uint32))])
+    assert e.value.code == "BACKEND_UNAVAILABLE"
+    assert engine.position(5) == pos  # dropped
+    engine.step_begin([StepRequest(5, tok, True)])
+    assert engine.step_end([StepRequest(5, tok, False)]) == [None]  # select cleared
+    assert engine.position(5) == pos + 1
+
+
 def test_sink_and_window_crossing(engine, oracle, ref_model):
     """A sequence longer than the 256-token window with 8 pinned sink tokens
     (runtime.ts:659-664, 723-728): tokens and cached codes stay exact past the wrap."""
