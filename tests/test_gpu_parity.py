@@ -332,6 +332,69 @@ def test_split_step_matches_step(engine, ref_model):
     assert engine.position(5) == pos + 1
 
 
+def test_wide_host_steps_match_single_steps(torch_cuda, archive, ref_model):
+    """80 sequences stepped together (needle_cuda_step and the begin / end split alike, with a mix
+    of prompt items, masked and unmasked selections) must select exactly what each selects stepped
+    alone (single-item steps are the path checked against the oracle above)."""
+    from needle_b200.backend import CudaEngine, StepRequest
+    rng = np.random.default_rng(13)
+    n, steps = 80, 6
+    prompts = [rng.integers(0, ref_model.vocab, int(rng.integers(1, 5))).astype(np.int32) for _ in range(n)]
+    masks = [[None if rng.random() < 0.5 else
+              np.sort(rng.choice(ref_model.vocab, size=int(rng.integers(1, 2000)), replace=False)).astype(np.uint32)
+              for _ in range(steps)] for _ in range(n)]
+    with CudaEngine(archive, device=0, max_seqs=n, max_len=32, max_sink=16) as eng:
+        def together(split):
+            for s in range(n):
+                eng.reset(s, 32, 0)
+            out = [[] for _ in range(n)]
+            pending = [None] * n
+            for t in range(max(p.size for p in prompts) + steps):
+                reqs = []
+                for s in range(n):
+                    p = prompts[s]
+                    if t < p.size:
+                        reqs.append(StepRequest(s, int(p[t]), t == p.size - 1, masks[s][0] if t == p.size - 1 else None))
+                    elif t - p.size + 1 < steps:
+                        k = t - p.size + 1
+                        reqs.append(StepRequest(s, pending[s], True, masks[s][k]))
+                if not reqs:
+                    break
+                if split:
+                    keep = [r.allowed for r in reqs]
+                    for r in reqs:
+                        r.allowed = None
+                    eng.step_begin(reqs)
+                    for r, a in zip(reqs, keep):
+                        r.allowed = a
+                    sel = eng.step_end(reqs)
+                else:
+                    sel, _ = eng.step(reqs)
+                for r, x in zip(reqs, sel):
+                    if x is not None:
+                        out[r.seq].append(x)
+                        pending[r.seq] = x[0]
+            return out
+
+        def alone():
+            out = [[] for _ in range(n)]
+            for s in range(n):
+                eng.reset(s, 32, 0)
+                p = prompts[s]
+                for t in range(p.size - 1):
+                    eng.step([StepRequest(s, int(p[t]))])
+                tok = int(p[-1])
+                for k in range(steps):
+                    sel, _ = eng.step([StepRequest(s, tok, True, masks[s][k])])
+                    out[s].append(sel[0])
+                    tok = sel[0][0]
+            return out
+
+        want = alone()
+        assert together(False) == want
+        assert together(True) == want
+
+
 def test_sink_and_window_crossing(engine, oracle, ref_model):
     """A sequence longer than the 256-token window with 8 pinned sink tokens
     (runtime.ts:659-664, 723-728): tokens and cached codes stay exact past the wrap."""
