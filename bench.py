@@ -97,6 +97,14 @@ def clocks_summary(proc):
     return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def load_peaks():
+    """MEASURED_PEAKS.json (the pool's measured HBM copy bandwidth and bf16 GEMM rates), or None."""
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        return None
+
+
 def cpu_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -356,6 +364,55 @@ TOOLCALL_PROMPT = 256
 TOOLCALL_MAX_NEW = 256
 
 
+def cpu_toolcall(vocab, tools, prompts):
+    """BASELINE config 5 on the host cores: the oracle runtime (the C++ restatement of the CPU
+    backend) drives the constrained loop of agent.ts:157-210 for one workload sequence per thread
+    (its calls release the GIL), selecting like selectToken over the allowed ids.  The allowed ids
+    come from this repository's trie scan, which is faster than the reference's clone-and-feed scan,
+    so the figure favours the CPU.  Throughput is the renewal-reward estimate
+    threads * constrained tokens / per-sequence seconds."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import needle_ref
+    from needle_b200 import grammar, synth
+    needle_ref.build()
+    model = needle_ref.Model(synth.build_archive(0))
+    threads = cpu_threads()
+
+    def one(prompt):
+        t0 = time.perf_counter()
+        rt = needle_ref.Runtime(model)
+        rt.reset(prompt.size + TOOLCALL_MAX_NEW + 1, 0)
+        logits = None
+        for i, t in enumerate(prompt):
+            logits = rt.step(int(t), want_logits=(i == prompt.size - 1))
+        g = grammar.ToolCallGrammar(tools, 4)
+        out = made = 0
+        for _ in range(TOOLCALL_MAX_NEW):
+            ids = grammar.allowed(g, vocab, out)
+            if ids.size == 0:
+                break
+            tok = int(ids[int(np.argmax(logits[ids]))])
+            g.feed(vocab.piece[tok])
+            out += len(vocab.piece[tok])
+            made += 1
+            if g.complete:
+                rt.step(tok, want_logits=False)
+                break
+            logits = rt.step(tok, want_logits=True)
+        return made, time.perf_counter() - t0
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as pool:
+        runs = list(pool.map(one, prompts[:threads]))
+    wall = time.perf_counter() - t0
+    made = sum(r[0] for r in runs)
+    secs = sum(r[1] for r in runs)
+    return {"value": round(threads * made / secs, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{len(runs)} workload sequences, one per thread ({made} constrained tokens after "
+                      f"{len(runs)} x {TOOLCALL_PROMPT} prompt tokens, {wall:.1f} s wall); allowed ids from "
+                      "this repository's trie scan (faster than the reference's clone-and-feed scan)"}
+
+
 def bench_toolcall(args, rank, world, local_rank):
     """constrained tool-call decode, data-parallel.  --sequences sequences (4096)
     split evenly over the GPUs; each a 256-token prompt of random ids (seed 5 + rank), then the
@@ -393,6 +450,8 @@ def bench_toolcall(args, rank, world, local_rank):
     dec.run(prompts[:min(8, n_local)], max_steps=max(3, args.warmup))  # warm-up steps (untimed)
     stream = torch.cuda.ExternalStream(eng.stream, device=local_rank)
     l0 = eng.kernel_launches()
+    smi = sample_clocks(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
+                        if "CUDA_VISIBLE_DEVICES" in os.environ and world == 1 else local_rank)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -402,7 +461,20 @@ def bench_toolcall(args, rank, world, local_rank):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
+    clocks = clocks_summary(smi)
     launches = eng.kernel_launches() - l0
+
+    # per-kernel-class timing for the roofline, after the timed run: 10 steps of the constrained
+    # phase (every slot past its prompt), events around every launch
+    prof_steps = 10
+
+    def profile_hook(step):
+        if step == TOOLCALL_PROMPT + 4:
+            eng.profile(True)
+
+    dec.run(prompts[:SLOTS], max_steps=TOOLCALL_PROMPT + 4 + prof_steps, hook=profile_hook)
+    prof = {k: v for k, v in eng.profile_read().items() if v[1] > 0}
+    eng.profile(False)
     import ctypes
     from needle_b200 import native
     h2d = st.items * ctypes.sizeof(native.StepItem) + 4 * st.allowed_ids
@@ -444,7 +516,12 @@ def bench_toolcall(args, rank, world, local_rank):
                 "e2e": {"value": round(cons / secs, 1), "unit": "tokens/s",
                         "h2d_bytes_per_step": int(h2d_all / max(steps * world, 1)),
                         "d2h_bytes_per_step": int(d2h_all / max(steps * world, 1))},
-                "gpu_launches": int(launch_all)}
+                "gpu_launches": int(launch_all),
+                "roofline": roofline_for(prof, SLOTS, load_peaks()),
+                "kernel_ms_per_step": {k: round(v[0] / prof_steps, 4) for k, v in prof.items()},
+                "clocks": clocks}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_toolcall(vocab, tools, prompts)
         print(json.dumps(line), flush=True)
     eng.close()
     if dist:
@@ -489,11 +566,7 @@ def main():
     if args.workload in ("qmatvec", "attention") and args.impl == "cuda":
         if rank != 0:
             return
-        peaks = None
-        try:
-            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        except (OSError, ValueError):
-            pass
+        peaks = load_peaks()
         from needle_b200 import build as nbuild
         nbuild.build()
         (bench_qmatvec if args.workload == "qmatvec" else bench_attention)(args, peaks)
@@ -533,11 +606,7 @@ def main():
     if dist:
         dist.barrier()
     archive = synth.build_archive(0)
-    peaks = None
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except (OSError, ValueError):
-        pass
+    peaks = load_peaks()
 
     n_seqs = SLOTS * 12
     prompts, gens = workload(rank, n_seqs)

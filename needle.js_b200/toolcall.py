@@ -17,7 +17,7 @@ from __future__ import annotations
 
 import time
 from dataclasses import dataclass, field
-from typing import List, Optional, Sequence
+from typing import Callable, List, Optional, Sequence
 
 import numpy as np
 
@@ -87,8 +87,10 @@ class ConstrainedDecoder:
         self.threads = threads
         self.template = ToolCallGrammar(self.tools, maximum_calls)  # validates the tools once
 
-    def run(self, prompts: Sequence[np.ndarray], slots: Optional[int] = None,
-            max_steps: Optional[int] = None) -> tuple[List[ToolCallResult], DecodeStats]:
+    def run(self, prompts: Sequence[np.ndarray], slots: Optional[int] = None, max_steps: Optional[int] = None,
+            hook: Optional[Callable[[int], None]] = None) -> tuple[List[ToolCallResult], DecodeStats]:
+        """Decodes every prompt's tool call through at most `slots` engine slots; `hook(step)` is
+        called before each step (e.g. to switch the engine's kernel profiling on)."""
         eng = self.engine
         slots = min(slots or eng.max_seqs, eng.max_seqs)
         results = [ToolCallResult() for _ in prompts]
@@ -121,6 +123,8 @@ class ConstrainedDecoder:
                     selecting.append(len(requests) - 1)
                 else:  # "final": the completed call's last token, no selection
                     requests.append(StepRequest(s, st["pending"], False))
+            if hook is not None:
+                hook(stats.steps)
             # The step's layers run on the GPU while the host computes the allowed ids, which depend
             # only on tokens already chosen (needle_cuda_step_begin / _end).
             t0 = time.perf_counter()
