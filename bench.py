@@ -364,6 +364,110 @@ TOOLCALL_PROMPT = 256
 TOOLCALL_MAX_NEW = 256
 
 
+REFERENCE_CPU_TOKENS_PER_S = 45.3  # pure-TS CPU backend, Apple M4: 13-token prompt, 32 greedy tokens
+
+
+def bench_single(args):
+    """BASELINE config 1 (PR1 ref): one sequence, a --prompt-len prompt of uniform random ids
+    (seed 1; 128 by default) fed to prefill, then --new-tokens greedy steps (64; no EOS stop), int8
+    KV, sink 0.  `value` is generated tokens over the whole time, prefill included, as
+    GenerationResult.tokensPerSecond (model.ts:142-151).  With --prompt-len 13 --new-tokens 32
+    (the reference's published setup) `vs_baseline` compares with its 45.3 tok/s on the CPU backend
+    (Apple M4).  Every step is a host step through the C-ABI (the selected id stays on the device
+    as the next step's pending token), so `e2e` is the same number."""
+    import torch
+    from needle_b200 import build as nbuild
+    from needle_b200 import synth
+    from needle_b200.backend import CudaEngine, StepRequest
+    nbuild.build()
+    torch.cuda.set_device(0)
+    archive = synth.build_archive(0)
+    P, G = args.prompt_len, args.new_tokens
+    prompt = synth.integers(1, P, 8192, stream=0).astype(np.int32)
+    eng = CudaEngine(archive, device=0, max_seqs=1, max_len=P + G + 8, max_sink=0)
+    stream = torch.cuda.ExternalStream(eng.stream, device=0)
+
+    def generate():
+        eng.reset(0, P + G, 0)
+        if P > 1:
+            eng.prefill(0, prompt[:-1], want_logits=False)
+        ids = []
+        for k in range(G):
+            sel, _ = eng.step([StepRequest(0, int(prompt[-1]) if k == 0 else -1, True)])
+            ids.append(sel[0][0])
+        return ids
+
+    for _ in range(max(3, args.warmup)):
+        generate()
+    smi = sample_clocks(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]))
+    runs = max(1, min(args.steps, 10))
+    l0 = eng.kernel_launches()
+    times, prefill_ms = [], []
+    for _ in range(runs):
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        torch.cuda.synchronize()
+        e0.record(stream)
+        eng.reset(0, P + G, 0)
+        if P > 1:
+            eng.prefill(0, prompt[:-1], want_logits=False)
+        e1.record(stream)
+        for k in range(G):
+            eng.step([StepRequest(0, int(prompt[-1]) if k == 0 else -1, True)])
+        e2.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e2))
+        prefill_ms.append(e0.elapsed_time(e1))
+    clocks = clocks_summary(smi)
+    launches = (eng.kernel_launches() - l0) // runs
+    ms = float(np.median(times))
+    # per-kernel-class times of 10 decode steps, events around every launch
+    eng.reset(0, P + G, 0)
+    if P > 1:
+        eng.prefill(0, prompt[:-1], want_logits=False)
+    eng.profile(True)
+    for k in range(min(10, G)):
+        eng.step([StepRequest(0, int(prompt[-1]) if k == 0 else -1, True)])
+    prof = {k: v for k, v in eng.profile_read().items() if v[1] > 0}
+    eng.profile(False)
+    eng.close()
+    value = G / (ms / 1e3)
+    published = (P, G) == (13, 32)
+    import ctypes
+    from needle_b200 import native
+    line = {"metric": "batch-1 greedy decode tokens/s (prefill included)", "value": round(value, 2),
+            "unit": "tokens/s", "n_gpus": 1, "steps": runs, "warmup": max(3, args.warmup),
+            "ms_per_step": round(ms / (P - 1 + G), 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": round(value / REFERENCE_CPU_TOKENS_PER_S, 2) if published else None,
+            "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "single sequence greedy decode (BASELINE config 1)" +
+                                   (", the reference's published setup" if published else ""),
+                       "prompt_len": P, "new_tokens": G, "seed": 1, "kv_cache": "int8", "sink": 0,
+                       "ms_per_generation": round(ms, 3), "prefill_ms": round(float(np.median(prefill_ms)), 3),
+                       "decode_ms_per_token": round((ms - float(np.median(prefill_ms))) / G, 4),
+                       "runs": runs, "statistic": "median over runs",
+                       "numerics": "exact (tokens, logits and int8 KV as the CPU backend's)",
+                       "vs_baseline_basis": "the reference's pure-TS CPU backend, 45.3 tok/s on an Apple M4 "
+                                            "(13-token prompt, 32 greedy tokens, real weights)" if published else None,
+                       "parallelism": "one sequence, one GPU"},
+            "e2e": {"value": round(value, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": ctypes.sizeof(native.StepItem),
+                    "d2h_bytes_per_step": ctypes.sizeof(native.Selected)},
+            "gpu_launches": int(launches),
+            "roofline": roofline_for(prof, 1, load_peaks()),
+            "kernel_ms_per_step": {k: round(v[0] / min(10, G), 4) for k, v in prof.items()},
+            "clocks": clocks}
+    if not args.no_cpu_baseline:
+        from oracle import needle_ref
+        needle_ref.build()
+        model = needle_ref.Model(archive)
+        t0 = time.perf_counter()
+        model.generate_greedy(prompt, G, 0, want_logits=False)
+        secs = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(G / secs, 3), "unit": "tokens/s", "cores": 1, "kind": "port",
+                                "sample": f"the whole workload ({P}-token prompt, {G} greedy tokens) on one core"}
+    print(json.dumps(line), flush=True)
+
+
 def cpu_toolcall(vocab, tools, prompts):
     """BASELINE config 5 on the host cores: the oracle runtime (the C++ restatement of the CPU
     backend) drives the constrained loop of agent.ts:157-210 for one workload sequence per thread
@@ -531,9 +635,12 @@ def bench_toolcall(args, rank, world, local_rank):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["decode", "qmatvec", "attention", "toolcall"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "qmatvec", "attention", "toolcall", "single"], default="decode",
                     help="decode: BASELINE config 4 (default); qmatvec / attention: configs 2 / 3 (1 GPU); "
-                         "toolcall: config 5 (constrained tool-call decode, data-parallel)")
+                         "toolcall: config 5 (constrained tool-call decode, data-parallel); "
+                         "single: config 1 (one sequence, batch-1 latency)")
+    ap.add_argument("--prompt-len", type=int, default=128, help="single: prompt tokens")
+    ap.add_argument("--new-tokens", type=int, default=64, help="single: greedy tokens")
     ap.add_argument("--sequences", type=int, default=4096, help="toolcall: sequences over all GPUs")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -559,6 +666,10 @@ def main():
               "parallelism": f"dp{args.gpus} (independent sequences per GPU, no collectives)"}
     metric, unit = "decode tokens/s", "tokens/s"
 
+    if args.workload == "single" and args.impl == "cuda":
+        if rank == 0:
+            bench_single(args)
+        return
     if args.workload == "toolcall" and args.impl == "cuda":
         bench_toolcall(args, rank, world, local_rank)
         return
