@@ -1,0 +1,160 @@
+"""The batched constrained decoder's host logic on the CPU (needle_b200.toolcall.ConstrainedDecoder).
+
+A fake engine stands in for the GPU: its logits for a slot are a fixed pseudo-random function of
+the tokens fed to that slot since its reset, so any scheduling of sequences over slots must give
+each sequence the same tokens as running it alone.  The reference for one sequence is the loop of
+packages/needle.js/src/tools/agent.ts:157-210 restated directly: scan the allowed ids, feed the
+pending token and select among them (the first maximum wins, runtime.ts:880-899), feed the chosen
+piece to the grammar, and after the grammar completes feed the chosen token once more.
+"""
+import json
+
+import numpy as np
+import pytest
+
+from needle_b200.backend import StepRequest
+
+
+def fake_logits(history, vocab):
+    rng = np.random.default_rng(hash(tuple(history)) % (1 << 32))
+    return rng.standard_normal(vocab)
+
+
+def select(logits, allowed):
+    return int(allowed[int(np.argmax(logits[allowed]))])
+
+
+class FakeEngine:
+    """The engine contract the decoder relies on: reset, step_begin / step_end with the same
+    items, distinct slots per step, selections only for items that select."""
+
+    def __init__(self, max_seqs, vocab):
+        self.max_seqs, self.vocab = max_seqs, vocab
+        self.hist = [None] * max_seqs
+        self.pending = None
+        self.steps = 0
+
+    def reset(self, slot, maximum_length, sink_length=0):
+        assert 0 <= slot < self.max_seqs and self.pending is None
+        self.hist[slot] = []
+
+    def step_begin(self, requests):
+        assert self.pending is None and requests
+        slots = [r.seq for r in requests]
+        assert len(set(slots)) == len(slots)
+        self.pending = [(r.seq, r.token, r.select) for r in requests]
+
+    def step_end(self, requests):
+        assert [(r.seq, r.token) for r in requests] == [(s, t) for s, t, _ in self.pending]
+        out = []
+        for r, (_, _, began_select) in zip(requests, self.pending):
+            assert began_select or not r.select  # a select may be cleared, not set
+            self.hist[r.seq].append(r.token)
+            if r.select:
+                assert r.allowed is not None and r.allowed.size > 0
+                out.append((select(fake_logits(self.hist[r.seq], self.vocab), r.allowed), 0.0))
+            else:
+                out.append(None)
+        self.pending = None
+        self.steps += 1
+        return out
+
+
+def reference(prompt, vocab, pieces, tools, maximum_new, grammar):
+    """One sequence alone: (ids, complete, dead_end, tokens fed)."""
+    g = grammar.ToolCallGrammar(tools, 4)
+    fed = [int(t) for t in prompt[:-1]]
+    pending, ids, out = int(prompt[-1]), [], 0
+    for _ in range(maximum_new):
+        allowed = grammar.allowed(g, vocab, out)
+        if allowed.size == 0:
+            return ids, False, True, fed
+        fed.append(pending)
+        tok = select(fake_logits(fed, vocab.size), allowed)
+        ids.append(tok)
+        assert g.feed(pieces[tok])
+        out += len(pieces[tok])
+        if g.complete:
+            fed.append(tok)
+            return ids, True, False, fed
+        pending = tok
+    return ids, False, False, fed
+
+
+@pytest.fixture(scope="module")
+def env():
+    import needle_b200.build
+    needle_b200.build.build()
+    from needle_b200 import grammar, synth, toolcall
+    pieces, types, _ = synth.tokenizer_pieces(8192, 0)
+    vocab = grammar.Vocabulary(pieces, types)
+    return grammar, toolcall, vocab
+
+
+def test_batched_decoder_matches_one_sequence_at_a_time(env):
+    grammar, toolcall, vocab = env
+    tools = toolcall.synthetic_tools(5)
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, vocab.size, int(rng.integers(2, 7))).astype(np.int32) for _ in range(7)]
+    maximum_new = 200
+    eng = FakeEngine(3, vocab.size)
+    dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=maximum_new, threads=3)
+    results, stats = dec.run(prompts)  # 7 sequences through 3 slots
+    assert stats.constrained_tokens == sum(len(r.ids) for r in results)
+    assert stats.prompt_tokens == sum(p.size for p in prompts)
+    assert stats.steps == eng.steps
+    for p, r in zip(prompts, results):
+        ids, complete, dead, _ = reference(p, vocab, vocab.piece, tools, maximum_new, grammar)
+        assert r.ids == ids and r.complete == complete and r.dead_end == dead
+        assert r.text == b"".join(vocab.piece[i] for i in ids)
+        if complete:
+            assert json.loads(r.text.decode()) == r.calls
+            assert {c["name"] for c in r.calls} <= {t["name"] for t in tools}
+    assert any(r.complete for r in results)
+
+
+def test_slots_are_reused_and_histories_match(env):
+    """After a sequence ends its slot is reset for the next one; what each sequence fed is exactly
+    the reference loop's (prompt, pending tokens, the final token of a completed call)."""
+    grammar, toolcall, vocab = env
+    tools = toolcall.synthetic_tools(5)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, vocab.size, 3).astype(np.int32) for _ in range(4)]
+
+    class Recording(FakeEngine):
+        def __init__(self, *a):
+            super().__init__(*a)
+            self.finished = []
+
+        def reset(self, slot, maximum_length, sink_length=0):
+            if self.hist[slot] is not None:
+                self.finished.append(list(self.hist[slot]))
+            super().reset(slot, maximum_length, sink_length)
+
+    eng = Recording(1, vocab.size)  # one slot: strictly one sequence after another
+    results, _ = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=30).run(prompts)
+    eng.finished.append(list(eng.hist[0]))
+    for p, r, fed in zip(prompts, results, eng.finished):
+        ids, complete, dead, want = reference(p, vocab, vocab.piece, tools, 30, grammar)
+        assert r.ids == ids
+        assert fed == want
+
+
+def test_dead_end_and_maximum_new_tokens(env):
+    grammar, toolcall, _ = env
+    tools = toolcall.synthetic_tools(5)
+    # a vocabulary that can open the call but never write `"name"`: a dead end after "[{"
+    pieces = ["<unk>", "[", "{", "a"]
+    small = grammar.Vocabulary(pieces, [grammar.UNKNOWN, grammar.NORMAL, grammar.NORMAL, grammar.NORMAL])
+    eng = FakeEngine(2, small.size)
+    results, _ = toolcall.ConstrainedDecoder(eng, small, tools, maximum_new_tokens=10).run(
+        [np.array([3, 1], dtype=np.int32), np.array([2], dtype=np.int32)])
+    for r in results:
+        assert r.dead_end and not r.complete and r.text == b"[{"
+    # a budget too small to finish: stops after exactly maximum_new constrained tokens
+    _, toolcall_mod, vocab = env
+    eng = FakeEngine(2, vocab.size)
+    results, _ = toolcall_mod.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=3).run(
+        [np.array([5, 6, 7], dtype=np.int32)])
+    assert len(results[0].ids) == 3 and not results[0].complete and not results[0].dead_end
+    assert results[0].text.startswith(b"[")
