@@ -71,20 +71,38 @@ struct Stage {
   static constexpr int kSize = kGroupsPerChunk * kTileRows * kStride;
 };
 
+// Both staging loops issue eight global loads before the first shared-memory store: a store
+// waits for its load, so one word at a time would pay a full L2 round trip per word.
+constexpr int kStageBatch = 8;
+
 template <int BITS>
 __device__ __forceinline__ void stage_weights(uint8_t* wt, const CqJob& job, int tile, int g0, int gn) {
   constexpr int kWords = Stage<BITS>::kBytes / 4;
   const int total = gn * kTileRows * kWords;
-  for (int idx = threadIdx.x; idx < total; idx += kGemvThreads) {
-    const int gq = idx / (kTileRows * kWords);
-    const int rem = idx - gq * kTileRows * kWords;
-    const int row = rem / kWords, w = rem - row * kWords;
-    const int r_local = tile * kTileRows + row;
-    uint32_t v = 0;
-    if (r_local < job.rows)
-      v = __ldg(reinterpret_cast<const uint32_t*>(job.packed + ((int64_t)job.row_start + r_local) * job.row_bytes +
-                                                  (int64_t)(g0 + gq) * Stage<BITS>::kBytes) + w);
-    *reinterpret_cast<uint32_t*>(wt + (gq * kTileRows + row) * Stage<BITS>::kStride + 4 * w) = v;
+  for (int base = threadIdx.x; base < total; base += kStageBatch * kGemvThreads) {
+    uint32_t v[kStageBatch];
+#pragma unroll
+    for (int k = 0; k < kStageBatch; k++) {
+      const int idx = base + k * kGemvThreads;
+      const int gq = idx / (kTileRows * kWords);
+      const int rem = idx - gq * kTileRows * kWords;
+      const int row = rem / kWords, w = rem - row * kWords;
+      const int r_local = tile * kTileRows + row;
+      v[k] = 0;
+      if (idx < total && r_local < job.rows)
+        v[k] = __ldg(reinterpret_cast<const uint32_t*>(job.packed + ((int64_t)job.row_start + r_local) * job.row_bytes +
+                                                       (int64_t)(g0 + gq) * Stage<BITS>::kBytes) + w);
+    }
+#pragma unroll
+    for (int k = 0; k < kStageBatch; k++) {
+      const int idx = base + k * kGemvThreads;
+      if (idx < total) {
+        const int gq = idx / (kTileRows * kWords);
+        const int rem = idx - gq * kTileRows * kWords;
+        const int row = rem / kWords, w = rem - row * kWords;
+        *reinterpret_cast<uint32_t*>(wt + (gq * kTileRows + row) * Stage<BITS>::kStride + 4 * w) = v[k];
+      }
+    }
   }
 }
 
@@ -211,10 +229,24 @@ __device__ __forceinline__ void fill_gemv_lut(double* lut, const Codebook& cb, i
 
 // Stages the chunk's inputs of items [b0, b0 + nb) as binary64 (exact widening).
 __device__ __forceinline__ void stage_inputs(double* xs, const CqJob& job, int b0, int nb, int g0, int gn) {
-  for (int idx = threadIdx.x; idx < nb * gn * kGroup; idx += kGemvThreads) {
-    const int b = idx / (gn * kGroup);
-    const int c = idx - b * gn * kGroup;
-    xs[b * 512 + c] = (double)job.x[(int64_t)(b0 + b) * job.x_stride + g0 * kGroup + c];
+  const int total = nb * gn * kGroup;
+  for (int base = threadIdx.x; base < total; base += kStageBatch * kGemvThreads) {
+    float v[kStageBatch];
+#pragma unroll
+    for (int k = 0; k < kStageBatch; k++) {
+      const int idx = base + k * kGemvThreads;
+      const int b = idx / (gn * kGroup);
+      const int c = idx - b * gn * kGroup;
+      v[k] = idx < total ? job.x[(int64_t)(b0 + b) * job.x_stride + g0 * kGroup + c] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < kStageBatch; k++) {
+      const int idx = base + k * kGemvThreads;
+      if (idx < total) {
+        const int b = idx / (gn * kGroup);
+        xs[b * 512 + (idx - b * gn * kGroup)] = (double)v[k];
+      }
+    }
   }
 }
 

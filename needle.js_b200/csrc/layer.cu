@@ -295,7 +295,13 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
   const DevItem it = st.items[b];
   const int slot = it.slot, p = it.position;
   float* xg = sv.x + (int64_t)slot * kLaneWidth;
-  for (int i = tid; i < kLaneWidth; i += kThreads) S.xl[i] = xg[i];
+  {
+    float v[kLaneWidth / kThreads];  // all loads in flight before the first store
+#pragma unroll
+    for (int k = 0; k < kLaneWidth / kThreads; k++) v[k] = xg[tid + k * kThreads];
+#pragma unroll
+    for (int k = 0; k < kLaneWidth / kThreads; k++) S.xl[tid + k * kThreads] = v[k];
+  }
   if (layer == 0 && m.n_sites > 0) engram_mix(m, sv, st, b, slot, p);
 
   const double inv_root_128 = 1.0 / sqrt((double)kGroup);
