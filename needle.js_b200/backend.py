@@ -101,23 +101,21 @@ class CudaEngine:
 
     @staticmethod
     def _items(requests: Sequence[StepRequest]):
+        """The requests as a needle_step_item array (int32 seq, token, select, allowed_count,
+        uint32 allowed_offset; filled column by column) and their allowed ids, concatenated."""
         n = len(requests)
-        items = (native.StepItem * max(n, 1))()
-        allowed_parts, offset = [], 0
-        for i, r in enumerate(requests):
-            items[i].seq = r.seq
-            items[i].token = r.token
-            items[i].select = 1 if r.select else 0
-            if r.select and r.allowed is not None:
-                a = np.ascontiguousarray(r.allowed, dtype=np.uint32)
-                items[i].allowed_count = a.size
-                items[i].allowed_offset = offset
-                allowed_parts.append(a)
-                offset += a.size
-            else:
-                items[i].allowed_count = -1
-                items[i].allowed_offset = 0
-        allowed = np.concatenate(allowed_parts) if allowed_parts else None
+        items = np.zeros((max(n, 1), 5), dtype=np.int32)
+        if n:
+            items[:n, 0] = [r.seq for r in requests]
+            items[:n, 1] = [r.token for r in requests]
+            masked = [r.select and r.allowed is not None for r in requests]
+            items[:n, 2] = [1 if r.select else 0 for r in requests]
+            counts = np.array([r.allowed.size if m else -1 for r, m in zip(requests, masked)], dtype=np.int64)
+            items[:n, 3] = counts
+            sizes = np.maximum(counts, 0)
+            items[:n, 4] = (np.cumsum(sizes) - sizes).astype(np.int32)
+        parts = [np.asarray(r.allowed, dtype=np.uint32) for r, m in zip(requests, masked) if m] if n else []
+        allowed = np.ascontiguousarray(np.concatenate(parts)) if parts else None
         return items, allowed
 
     def step(self, requests: Sequence[StepRequest], want_logits: bool = False):
@@ -126,7 +124,7 @@ class CudaEngine:
         items, allowed = self._items(requests)
         sel = (native.Selected * max(n, 1))()
         logits = np.zeros((n, self.vocab), dtype=np.float32) if want_logits else None
-        check(lib().needle_cuda_step(self.h, C.cast(items, C.c_void_p), n, ptr(allowed),
+        check(lib().needle_cuda_step(self.h, ptr(items), n, ptr(allowed),
                                      0 if allowed is None else allowed.size, C.cast(sel, C.c_void_p),
                                      ptr(logits)))
         out = [(sel[i].id, sel[i].log_probability) if r.select else None for i, r in enumerate(requests)]
@@ -136,7 +134,7 @@ class CudaEngine:
         """First half of a step (needle_cuda_step_begin): the layers are enqueued and this returns at
         once; the requests' allowed lists are not read.  step_end must follow before any other call."""
         items, _ = self._items(requests)
-        check(lib().needle_cuda_step_begin(self.h, C.cast(items, C.c_void_p), len(requests)))
+        check(lib().needle_cuda_step_begin(self.h, ptr(items), len(requests)))
 
     def step_end(self, requests: Sequence[StepRequest]):
         """Second half: the same requests (a select may be cleared), now with their allowed lists;
@@ -144,7 +142,7 @@ class CudaEngine:
         n = len(requests)
         items, allowed = self._items(requests)
         sel = (native.Selected * max(n, 1))()
-        check(lib().needle_cuda_step_end(self.h, C.cast(items, C.c_void_p), n, ptr(allowed),
+        check(lib().needle_cuda_step_end(self.h, ptr(items), n, ptr(allowed),
                                          0 if allowed is None else allowed.size, C.cast(sel, C.c_void_p)))
         return [(sel[i].id, sel[i].log_probability) if r.select else None for i, r in enumerate(requests)]
 

@@ -90,14 +90,39 @@ class ConstrainedDecoder:
     def run(self, prompts: Sequence[np.ndarray], slots: Optional[int] = None, max_steps: Optional[int] = None,
             hook: Optional[Callable[[int], None]] = None) -> tuple[List[ToolCallResult], DecodeStats]:
         """Decodes every prompt's tool call through at most `slots` engine slots; `hook(step)` is
-        called before each step (e.g. to switch the engine's kernel profiling on)."""
+        called before each step (e.g. to switch the engine's kernel profiling on).
+
+        A step's items need only tokens: the token chosen at the previous step is fed whether or not
+        it completed the grammar (agent.ts:193-196 feeds it once more when it did), and only the
+        select flag depends on the grammar, which needle_cuda_step_end may clear.  So each step is
+        begun first, and the previous step's chosen pieces are fed to the grammars, completions
+        detected and the next allowed ids scanned while its layers run."""
         eng = self.engine
         slots = min(slots or eng.max_seqs, eng.max_seqs)
         results = [ToolCallResult() for _ in prompts]
         stats = DecodeStats()
         queue = list(range(len(prompts)))[::-1]
-        state = [None] * slots  # per slot: dict(seq, pos, phase, grammar, out_bytes, pending)
+        # per slot: seq, phase ("prompt" | "call" | "final"), prompt, pos, grammar, out (bytes
+        # chosen so far), pending (the token the next step feeds), unfed (chosen but not yet fed
+        # to the grammar)
+        state = [None] * slots
         t_start = time.perf_counter()
+
+        def feed(st, tok):
+            t0 = time.perf_counter()
+            accepted = st["grammar"].feed(self.vocab.piece[tok])
+            complete = accepted and st["grammar"].complete
+            stats.grammar_seconds += time.perf_counter() - t0
+            if not accepted:  # the device picked outside the mask: a contract violation
+                raise RuntimeError(f"selected disallowed token {tok}")
+            res = results[st["seq"]]
+            if complete:
+                res.complete = True
+                res.calls = st["grammar"].calls
+                st["phase"] = "final"
+            st["unfed"] = None
+            return complete
+
         while True:
             for s in range(slots):  # admit
                 if state[s] is None and queue:
@@ -105,35 +130,35 @@ class ConstrainedDecoder:
                     p = np.asarray(prompts[k], dtype=np.int32)
                     eng.reset(s, int(p.size) + self.maximum_new + 1, 0)
                     state[s] = {"seq": k, "pos": 0, "phase": "prompt", "prompt": p,
-                                "grammar": self.template.clone(), "out": 0, "pending": -1}
+                                "grammar": self.template.clone(), "out": 0, "pending": -1, "unfed": None}
             live = [s for s in range(slots) if state[s] is not None]
             if not live or (max_steps is not None and stats.steps >= max_steps):
                 break
-            requests, selecting = [], []
+            if hook is not None:
+                hook(stats.steps)
+            requests = []
             for s in live:
                 st = state[s]
                 if st["phase"] == "prompt":
                     last = st["pos"] == st["prompt"].size - 1
                     requests.append(StepRequest(s, int(st["prompt"][st["pos"]]), last))
-                    if last:
-                        selecting.append(len(requests) - 1)
                     stats.prompt_tokens += 1
-                elif st["phase"] == "call":
-                    requests.append(StepRequest(s, st["pending"], True))
-                    selecting.append(len(requests) - 1)
-                else:  # "final": the completed call's last token, no selection
-                    requests.append(StepRequest(s, st["pending"], False))
-            if hook is not None:
-                hook(stats.steps)
-            # The step's layers run on the GPU while the host computes the allowed ids, which depend
-            # only on tokens already chosen (needle_cuda_step_begin / _end).
+                else:  # "call": the pending token, selecting unless its feed completes the call
+                    requests.append(StepRequest(s, st["pending"], st["phase"] == "call"))
             t0 = time.perf_counter()
             eng.step_begin(requests)
             t1 = time.perf_counter()
+            # while the layers run: the previous choices go to the grammars, then the scans
+            for r in requests:
+                st = state[r.seq]
+                if st["unfed"] is not None and feed(st, st["unfed"]):
+                    r.select = False  # completed: this step is the final feed (no selection)
+            selecting = [i for i, r in enumerate(requests) if r.select]
+            t2 = time.perf_counter()
             masks = allowed_batch([state[requests[i].seq]["grammar"] for i in selecting],
                                   [state[requests[i].seq]["out"] for i in selecting], self.vocab, self.threads)
-            t2 = time.perf_counter()
-            stats.grammar_seconds += t2 - t1
+            t3 = time.perf_counter()
+            stats.grammar_seconds += t3 - t2
             for i, ids in zip(selecting, masks):
                 requests[i].allowed = ids
                 if ids.size == 0:  # GRAMMAR_DEAD_END: no token can continue; the sequence stops here
@@ -144,7 +169,7 @@ class ConstrainedDecoder:
             stats.items += len(requests)
             stats.allowed_ids += sum(int(r.allowed.size) for r in requests if r.allowed is not None)
             chosen = eng.step_end(requests)
-            stats.engine_seconds += (t1 - t0) + (time.perf_counter() - t2)
+            stats.engine_seconds += (t1 - t0) + (time.perf_counter() - t3)
             stats.steps += 1
             for r, sel in zip(requests, chosen):
                 st = state[r.seq]
@@ -156,24 +181,17 @@ class ConstrainedDecoder:
                     continue
                 tok = int(sel[0])
                 res = results[st["seq"]]
-                piece = self.vocab.piece[tok]
-                t0 = time.perf_counter()
-                accepted = st["grammar"].feed(piece)
-                stats.grammar_seconds += time.perf_counter() - t0
-                if not accepted:  # the device picked outside the mask: a contract violation
-                    raise RuntimeError(f"selected disallowed token {tok}")
                 res.ids.append(tok)
-                res.text += piece
-                st["out"] += len(piece)
-                st["pending"] = tok
+                res.text += self.vocab.piece[tok]
+                st["out"] += len(self.vocab.piece[tok])
+                st["pending"] = st["unfed"] = tok
                 st["phase"] = "call"
                 stats.constrained_tokens += 1
-                if st["grammar"].complete:
-                    res.complete = True
-                    res.calls = st["grammar"].calls
-                    st["phase"] = "final"
-                elif len(res.ids) >= self.maximum_new or st["out"] >= MAX_OUTPUT_BYTES:
-                    res.calls = st["grammar"].calls
-                    state[r.seq] = None
+                if len(res.ids) >= self.maximum_new or st["out"] >= MAX_OUTPUT_BYTES:
+                    # the budget is spent: unless this token completes the call (then the next step
+                    # feeds it once more), the sequence ends here
+                    if not feed(st, tok):
+                        res.calls = st["grammar"].calls
+                        state[r.seq] = None
         stats.seconds = time.perf_counter() - t_start
         return results, stats
