@@ -522,8 +522,9 @@ def bench_toolcall(args, rank, world, local_rank):
     split evenly over the GPUs; each a 256-token prompt of random ids (seed 5 + rank), then the
     constrained phase directly after the prompt (random weights never emit <tool_call>), greedy until
     the grammar completes or 256 constrained tokens, over the synthetic schema (3 tools x 2-5
-    parameters of string / integer / boolean / enum, seed 5).  256 slots per GPU with continuous
-    admission; the allowed ids come from the C++ grammar's byte-trie scan on 16 host threads."""
+    parameters of string / integer / boolean / enum, seed 5).  --slots engine slots per GPU (512)
+    with continuous admission; the allowed ids come from the C++ grammar's byte-trie scan on up to
+    16 host threads per GPU."""
     import torch
     from needle_b200 import build as nbuild
     from needle_b200 import grammar, synth, toolcall
@@ -547,7 +548,7 @@ def bench_toolcall(args, rank, world, local_rank):
     n_local = args.sequences // world + (1 if rank < args.sequences % world else 0)
     ids = synth.integers(5 + 1000 * rank, n_local * TOOLCALL_PROMPT + 1, 8192, stream=7).astype(np.int32)
     prompts = [ids[k * TOOLCALL_PROMPT:(k + 1) * TOOLCALL_PROMPT] for k in range(n_local)]
-    eng = CudaEngine(archive, device=local_rank, max_seqs=SLOTS, max_len=TOOLCALL_PROMPT + TOOLCALL_MAX_NEW + 8,
+    eng = CudaEngine(archive, device=local_rank, max_seqs=args.slots, max_len=TOOLCALL_PROMPT + TOOLCALL_MAX_NEW + 8,
                      max_sink=16)
     threads = max(1, min(16, cpu_threads() // max(1, world)))
     dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=TOOLCALL_MAX_NEW, threads=threads)
@@ -576,7 +577,7 @@ def bench_toolcall(args, rank, world, local_rank):
         if step == TOOLCALL_PROMPT + 4:
             eng.profile(True)
 
-    dec.run(prompts[:SLOTS], max_steps=TOOLCALL_PROMPT + 4 + prof_steps, hook=profile_hook)
+    dec.run(prompts[:args.slots], max_steps=TOOLCALL_PROMPT + 4 + prof_steps, hook=profile_hook)
     prof = {k: v for k, v in eng.profile_read().items() if v[1] > 0}
     eng.profile(False)
     import ctypes
@@ -604,7 +605,7 @@ def bench_toolcall(args, rank, world, local_rank):
                 "ms_per_step": round(ms_max / max(steps, 1), 4), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f64", "data": "synthetic",
                 "config": {"workload": "constrained tool-call decode (BASELINE config 5)", "sequences": int(seqs),
-                           "prompt_len": TOOLCALL_PROMPT, "max_new_tokens": TOOLCALL_MAX_NEW, "slots_per_gpu": SLOTS,
+                           "prompt_len": TOOLCALL_PROMPT, "max_new_tokens": TOOLCALL_MAX_NEW, "slots_per_gpu": args.slots,
                            "tools": [{"name": t["name"], "parameters": list(t["parameters"]["properties"])}
                                      for t in tools],
                            "completed_calls": int(done), "dead_ends": int(dead),
@@ -621,7 +622,7 @@ def bench_toolcall(args, rank, world, local_rank):
                         "h2d_bytes_per_step": int(h2d_all / max(steps * world, 1)),
                         "d2h_bytes_per_step": int(d2h_all / max(steps * world, 1))},
                 "gpu_launches": int(launch_all),
-                "roofline": roofline_for(prof, SLOTS, load_peaks()),
+                "roofline": roofline_for(prof, args.slots, load_peaks()),
                 "kernel_ms_per_step": {k: round(v[0] / prof_steps, 4) for k, v in prof.items()},
                 "clocks": clocks}
         if world == 1 and not args.no_cpu_baseline:
@@ -642,6 +643,7 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=128, help="single: prompt tokens")
     ap.add_argument("--new-tokens", type=int, default=64, help="single: greedy tokens")
     ap.add_argument("--sequences", type=int, default=4096, help="toolcall: sequences over all GPUs")
+    ap.add_argument("--slots", type=int, default=512, help="toolcall: engine slots per GPU")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
