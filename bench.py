@@ -171,9 +171,17 @@ def roofline_for(prof, n_items, peaks):
     peak = peaks.get("hbm_gbs") if peaks else None
     src = "measured" if peak else "fallback"
     peak = peak or 6650.0
-    return {"kernel": cls, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_source": src,
-            "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+    # DRAM bytes (read + write) per launch of the 256-slot decode step, from one ncu capture of each
+    # kernel: far below the algorithmic bytes because the KV written by the previous step and the
+    # weights are read from L2
+    traffic = {"attention": 2307840, "layer": 3831808, "gemv_qkvg": 820224, "gemv_o": 703488}
+    line = {"kernel": cls, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_source": src,
+            "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "traffic": traffic.get(cls) if n_items == 256 else None,
             "launch_ms": round(per_launch_ms, 5), "algorithmic_bytes_per_launch": int(bytes_)}
+    if line["traffic"] is not None:
+        line["traffic_source"] = "profiles/exact_kernels_decode_step_256slots.md"
+    return line
 
 
 QMATVEC_SHAPES = [  # (name, rows, inputs, record bits) -- every Needle 2 projection + the stress shape
