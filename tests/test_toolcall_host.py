@@ -158,3 +158,23 @@ def test_dead_end_and_maximum_new_tokens(env):
         [np.array([5, 6, 7], dtype=np.int32)])
     assert len(results[0].ids) == 3 and not results[0].complete and not results[0].dead_end
     assert results[0].text.startswith(b"[")
+
+
+def test_step_items_pack_as_the_c_struct():
+    """CudaEngine._items lays requests out as needle_step_item (include/needle_cuda.h) and
+    concatenates the masks of the selecting items in order."""
+    import ctypes
+    from needle_b200 import native
+    from needle_b200.backend import CudaEngine
+    reqs = [StepRequest(3, 7, True, np.array([1, 5, 9], dtype=np.uint32)), StepRequest(1, -1, False),
+            StepRequest(0, 2, True), StepRequest(2, 4, True, np.array([8], dtype=np.uint32)),
+            StepRequest(4, 6, False, np.array([3], dtype=np.uint32))]  # a mask without select is ignored
+    items, allowed = CudaEngine._items(reqs)
+    assert items.dtype == np.int32 and items.shape[1] * 4 == ctypes.sizeof(native.StepItem)
+    arr = (native.StepItem * len(reqs)).from_buffer_copy(items.tobytes())
+    got = [(a.seq, a.token, a.select, a.allowed_count) for a in arr]
+    assert got == [(3, 7, 1, 3), (1, -1, 0, -1), (0, 2, 1, -1), (2, 4, 1, 1), (4, 6, 0, -1)]
+    assert arr[0].allowed_offset == 0 and arr[3].allowed_offset == 3
+    np.testing.assert_array_equal(allowed, [1, 5, 9, 8])
+    items, allowed = CudaEngine._items([StepRequest(0, 1, False)])
+    assert allowed is None and items[0].tolist() == [0, 1, 0, -1, 0]
