@@ -848,6 +848,44 @@ class SchemaGrammar {
     return c;
   }
 
+  // The bytes feed_byte could accept next, as a 256-bit set: exact when the top frame is a value
+  // whose type is not chosen yet (the bytes that start one of its enum candidates or one of its
+  // types, as feed_byte's Value case decides), every byte otherwise (rejects() covers the rest).
+  void first_bytes(uint64_t (&set)[4]) const {
+    set[0] = set[1] = set[2] = set[3] = ~0ull;
+    if (complete_ || stack_.empty() || stack_.back().kind != Frame::Value) return;
+    try {
+      const Frame& frame = stack_.back();
+      std::vector<SchemaPtr> alternatives;
+      schema_alternatives(frame.schema, *root_, alternatives);
+      bool all_enum = true, any_enum = false;
+      uint64_t enum_set[4] = {0, 0, 0, 0}, type_set[4] = {0, 0, 0, 0};
+      for (const auto& a : alternatives) {
+        const SchemaPtr r = resolve_reference(a, *root_);
+        const Json* c = r->get("const");
+        const Json* e = r->get("enum");
+        if (c) {
+          const std::string t = stringify(*c);
+          enum_set[(uint8_t)t[0] >> 6] |= 1ull << ((uint8_t)t[0] & 63);
+          any_enum = true;
+        } else if (e && e->kind == Json::Array) {
+          for (const Json& v : e->arr) {
+            const std::string t = stringify(v);
+            enum_set[(uint8_t)t[0] >> 6] |= 1ull << ((uint8_t)t[0] & 63);
+            any_enum = true;
+          }
+        }
+        if (!c && !e) all_enum = false;
+        for (const auto& t : possible_types(*r))
+          for (int b = 0; b < 256; b++)
+            if (type_starts_with(t, b)) type_set[b >> 6] |= 1ull << (b & 63);
+      }
+      const uint64_t* chosen = any_enum && all_enum ? enum_set : type_set;
+      for (int k = 0; k < 4; k++) set[k] = chosen[k];
+    } catch (const SchemaError&) {  // feed_byte reports it
+    }
+  }
+
   // The same as feeding `bytes` one at a time (each >= 0x20, none '"' or '\\') while
   // in_string_content().
   void append_string_content(const char* bytes, size_t n) { stack_.back().bytes.append(bytes, n); }
@@ -1312,6 +1350,13 @@ class ToolGrammar {
   }
   void append_string_content(const char* bytes, size_t n) { arguments_->append_string_content(bytes, n); }
   SchemaGrammar::StringClose string_close() const { return arguments_->string_close(); }
+  void first_bytes(uint64_t (&set)[4]) const {
+    if (phase_ == Arguments && arguments_ && !arguments_->complete()) {
+      arguments_->first_bytes(set);
+      return;
+    }
+    set[0] = set[1] = set[2] = set[3] = ~0ull;
+  }
   bool in_number() const { return phase_ == Arguments && arguments_ && arguments_->in_number(); }
   const std::string& number_text() const { return arguments_->number_text(); }
   void append_number(const char* bytes, size_t n) { arguments_->append_number(bytes, n); }
@@ -1570,9 +1615,11 @@ void descend(Walk& w, int32_t node, const G& g, int32_t depth);
 // The general case: every edge the grammar does not reject outright is fed to a copy.
 template <class G>
 void walk(Walk& w, int32_t node, const G& g, int32_t depth) {
+  uint64_t first[4];
+  g.first_bytes(first);
   for (const auto& edge : w.trie.nodes[node].children) {
     if (depth + 1 > w.limit) break;
-    if (g.rejects(edge.first)) continue;
+    if (!((first[edge.first >> 6] >> (edge.first & 63)) & 1) || g.rejects(edge.first)) continue;
     G& next = scratch<G, 0>(depth + 1, g);
     if (!next.feed_byte(edge.first)) continue;
     mark_ids(w, edge.second);
