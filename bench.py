@@ -153,7 +153,8 @@ def roofline_for(prof, n_items, peaks):
     """Roofline of the kernel class with the largest share of step time."""
     cls, (ms, launches) = max(prof.items(), key=lambda kv: kv[1][0])
     per_launch_ms = ms / max(launches, 1)
-    # algorithmic bytes per launch (see DESIGN.md, "Algorithmic bytes")
+    # algorithmic bytes per launch: the bytes the kernel must touch once per item (KV rows of a full
+    # 256-position window, inputs and outputs) plus, for the GEMVs, every weight byte once
     kv_row = 64 + 64 + 4 + 4
     weights = {"gemv_qkvg": (512 + 256 + 256 + 512) * (128 + 8), "gemv_o": 512 * (192 + 8),
                "gemv_vocab": 8192 * (256 + 8)}

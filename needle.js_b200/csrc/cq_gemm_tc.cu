@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
         const uint32_t col = lane_addr + acc_cols + sl * 128;
         uint32_t hi[16], lo[16];
         decode16(0, hi, lo);
-        // lane 0 waits for the MMAs that last read this slot; the verdict is made warp-uniform
+        // lane 0 waits for the MMAs that last read this slot; the outcome is made warp-uniform
         // (tcgen05.st is a warp instruction)
         if (j > 0 && lane == 0) failed = !bar_wait(&empty[sl], (uint32_t)((j - 1) & 1));
         failed = __any_sync(0xffffffffu, failed);

@@ -733,7 +733,7 @@ class SchemaGrammar {
     return f.kind == Frame::String && f.started && !f.escaped && f.unicode_remaining == 0;
   }
 
-  // True when feed_byte(byte) would certainly return false, judged from the top frame without
+  // True when feed_byte(byte) would certainly return false, decided from the top frame without
   // changing anything; false means "feed a copy to find out".  Each case restates the first check
   // feed_byte makes for that frame.
   bool rejects(int byte) const {
@@ -1635,7 +1635,7 @@ template <class G>
 void walk_string(Walk& w, int32_t node, const G& base, int32_t depth) {
   if (node == 0 && w.limit >= w.trie.max_len) {  // from the root: the index built at vocab open
     for (size_t id = 0; id < w.mark.size(); id++) w.mark[id] |= w.trie.plain[id];
-    // A closing quote is judged by StringClose; what follows it in the piece goes to the frame
+    // A closing quote is decided by StringClose; what follows it in the piece goes to the frame
     // below the string, whose first check does not depend on the string's value, so `closed` (the
     // state after any accepted close) rejects most continuations without a copy.
     const auto close = base.string_close();
