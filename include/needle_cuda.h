@@ -151,8 +151,12 @@ int needle_cuda_step_begin(needle_ctx* ctx, const needle_step_item* items, int32
 int needle_cuda_step_end(needle_ctx* ctx, const needle_step_item* items, int32_t n, const uint32_t* allowed_ids,
                          size_t allowed_total, needle_selected* out_selected);
 
-/* NeedleRuntime.prefill (runtime.ts:227-243) for one slot: n steps, logits of the last one
- * written to out_logits (vocabulary floats) when non-NULL. */
+/* NeedleRuntime.prefill (runtime.ts:227-243) for one slot: the n tokens, logits of the last one
+ * written to out_logits (vocabulary floats) when non-NULL.  The result is that of n one-token
+ * steps; the tokens go through the layers in chunks of up to 64, one item per token (K/V of the
+ * whole chunk appended before its items attend), except for a slot that collects confidence, for
+ * positions whose chunk would wrap the KV window, and for the last token when its logits are
+ * wanted. */
 int needle_cuda_prefill(needle_ctx* ctx, int32_t seq, const int32_t* ids, int32_t n, float* out_logits);
 
 /* Copies one layer of a slot's int8 KV cache (layout of runtime.ts:666-677): codes

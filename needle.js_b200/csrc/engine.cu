@@ -309,6 +309,10 @@ struct SlotHost {
   int32_t max_len = 0, sink = 0, kv_alloc = 0, position = 0;
 };
 
+// Prompt tokens of one slot processed together by needle_cuda_prefill (StepView::chunk); the step
+// buffers hold at least this many items.
+constexpr int kPrefillChunk = 64;
+
 struct ProfEntry {
   int cls;
   cudaEvent_t a, b;
@@ -661,8 +665,10 @@ void build_state(needle_ctx& C) {
   }
   C.slots.assign(S, SlotHost{});
   StepView& st = C.stv;
-  const size_t B = size_t(S);
+  const size_t B = size_t(std::max(S, kPrefillChunk));
   st.items = C.dalloc<DevItem>(B);
+  st.chunk = 0;
+  st.lanes = C.dalloc<float>(B * kLaneWidth);
   C.d_counts = C.dalloc<int32_t>(8);
   C.d_confidence = C.dalloc<double>(1);
   st.n_items = C.d_counts;
@@ -778,7 +784,7 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
   const SlotView& sv = C.sv;
   const int32_t* n_dev = st.n_items;
   cudaStream_t s0 = lane.main;
-  const bool probes = C.collecting > 0 && m.probe_count > 0;
+  const bool probes = !st.chunk && C.collecting > 0 && m.probe_count > 0;
   auto probe_add = [&](int source) {
     cuda_check(launch_probe_add(m, sv, st, source, n_host, s0), "probe pool");
     C.launches++;
@@ -812,7 +818,12 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
               {C.lv[l], 0, 256, st.prep_a, kDim, st.qkvg + 768, 1536},
               {C.lg[l], 0, 512, st.prep_a, kDim, st.qkvg + 1024, 1536}},
              n_host, n_dev, s0);
-    C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0); }, s0);
+    if (st.chunk) {  // every item's K/V before any item attends
+      C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 1); }, s0);
+      C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 2); }, s0);
+    } else {
+      C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0); }, s0);
+    }
     run_gemv(C, P_GEMV_O, {{C.lo[l], 0, 512, st.prep_o, kDim, st.proj, kDim}}, n_host, n_dev, s0);
   }
   if (any_select)
@@ -1284,9 +1295,49 @@ int needle_cuda_prefill(needle_ctx* ctx, int32_t seq, const int32_t* ids, int32_
     needle_ctx& C = *ctx_of(ctx);
     require(seq >= 0 && seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
     const SlotHost& h = C.slots[seq];
+    require(h.ready, NEEDLE_INVALID_CACT, "Call runtime.reset() before decoding");
     require(h.max_len - h.position >= n, NEEDLE_CONTEXT_OVERFLOW,
             "Prompt has " + std::to_string(n) + " tokens but runtime holds " + std::to_string(h.max_len));
-    for (int32_t i = 0; i < n; i++) {
+    const int V = C.mv.vocab;
+    for (int32_t i = 0; i < n; i++)
+      if (ids[i] < 0 || ids[i] >= V) fail(NEEDLE_INVALID_CACT, "Token " + std::to_string(ids[i]) + " is outside the vocabulary");
+    // Chunks of up to kPrefillChunk tokens, one item per token (the last token, when its logits
+    // are wanted, is a step of its own).  A slot that feeds a confidence pool goes token by token
+    // (the pool is updated in position order), and no chunk reaches past the KV ring: one of its
+    // items would overwrite the slot of a position an earlier item still attends to.
+    int32_t i = 0;
+    const int32_t chunked_end = n - (out_logits ? 1 : 0);
+    while (!C.slots[seq].collect && i < chunked_end) {
+      SlotHost& hs = C.slots[seq];
+      int k = std::min(kPrefillChunk, chunked_end - i);
+      if (C.mv.kv_window > 0) k = std::min(k, hs.sink + C.mv.kv_window - hs.position);
+      if (k < 2) break;
+      for (int b = 0; b < k; b++) {
+        DevItem d{};
+        d.slot = seq;
+        d.token = ids[i + b];
+        d.select = 0;
+        d.allowed_count = -1;
+        d.position = hs.position + b;
+        d.out_index = b;
+        C.h_items[b] = d;
+      }
+      C.h_counts[0] = k;
+      C.h_counts[1] = 0;
+      C.timed(P_COPY, [&] {
+        cudaError_t e = cudaMemcpyAsync(C.stv.items, C.h_items, size_t(k) * sizeof(DevItem), cudaMemcpyHostToDevice,
+                                        C.stream);
+        if (e != cudaSuccess) return e;
+        return cudaMemcpyAsync(C.d_counts, C.h_counts, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, C.stream);
+      });
+      StepView cv = C.stv;
+      cv.chunk = 1;
+      enqueue_step(C, cv, k, false, nullptr, lane_a(C));
+      cuda_check(cudaStreamSynchronize(C.stream), "prefill chunk");
+      hs.position += k;
+      i += k;
+    }
+    for (; i < n; i++) {
       needle_step_item it{seq, ids[i], 0, -1, 0};
       const bool last = i == n - 1 && out_logits != nullptr;
       const int rc = needle_cuda_step(ctx, &it, 1, nullptr, 0, nullptr, last ? out_logits : nullptr);

@@ -105,6 +105,12 @@ struct StepView {
   float* logits;            // [B][vocab]
   int32_t* out_id;          // [B]
   double* out_logprob;      // [B]
+  // A prefill chunk: items 0..n-1 are the positions p0, p0 + 1, ... of one slot, in order, none
+  // selecting.  Their lanes are per item (`lanes`) instead of per slot, K/V are appended for the
+  // whole chunk before any item attends, and the slot's state (position, token history, engram
+  // ring) advances once, after the chunk.
+  int32_t chunk;
+  float* lanes;             // [B][4][512] (chunk steps)
 };
 
 // Device scheduler queue (needle_cuda_sched_*).
@@ -127,8 +133,10 @@ cudaError_t launch_layer(const ModelView& m, const SlotView& sv, const StepView&
                          int n_host, cudaStream_t s);
 // Sinkhorn routing of the layer's items (reads and writes StepView::route[4..19]).
 cudaError_t launch_route(const StepView& st, int n_host, cudaStream_t s);
+// Chunk steps (StepView::chunk) launch it twice: part 1 appends every item's K/V, part 2 attends;
+// otherwise part 0 does both per item.
 cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
-                             int n_host, cudaStream_t s);
+                             int n_host, cudaStream_t s, int part = 0);
 cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
                           const SchedView* sched, cudaStream_t s);
 // Device scheduler: builds the step's item list and the counts [all, selecting, half A (all,

@@ -63,7 +63,8 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
   DevItem it = st.items[b];
   SeqState* q = sv.seq + it.slot;
   if (tid == 0) {
-    const int p = q->position;
+    // a chunk item's token and position are given (p0 + b); otherwise the slot's
+    const int p = st.chunk ? it.position : q->position;
     const int token = it.token >= 0 ? it.token : q->pending;
     s_token = token;
     s_pos = p;
@@ -73,14 +74,19 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
   __syncthreads();
   const int token = s_token, p = s_pos;
 
-  // #engramLookup (runtime.ts:788-818): history = [..., hist[1], hist[0], token].
+  // #engramLookup (runtime.ts:788-818): history = [..., hist[1], hist[0], token].  In a chunk the
+  // tokens before this item's come from the earlier items, then from the slot's history.
   if (tid < m.n_tables && m.n_sites > 0) {
     const int heads_per_order = m.n_tables / m.n_orders;
     const int oi = tid / heads_per_order, head = tid - oi * heads_per_order;
     const int order = m.orders[oi];
     uint32_t hash = kEngramSeed * (uint32_t)(oi * heads_per_order + head + 1);
     for (int off = 0; off < order; off++) {
-      const uint32_t tok = off > p ? 0u : off == 0 ? (uint32_t)token : (uint32_t)q->hist[off - 1];
+      uint32_t tok;
+      if (off > p) tok = 0u;
+      else if (off == 0) tok = (uint32_t)token;
+      else if (st.chunk && off <= b) tok = (uint32_t)st.items[b - off].token;
+      else tok = (uint32_t)q->hist[st.chunk ? off - b - 1 : off - 1];
       hash = (hash ^ tok) * kEngramPrime;
     }
     hash = hash ^ (hash >> 15);
@@ -88,7 +94,7 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
     evalid[tid] = (order - 1) <= p;
   }
   __syncthreads();
-  if (tid == 0) {
+  if (tid == 0 && !st.chunk) {  // a chunk's history advances in k_finish, after every item read it
     q->hist[2] = q->hist[1];
     q->hist[1] = q->hist[0];
     q->hist[0] = token;
@@ -107,7 +113,7 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
     const double inverse_root = 1.0 / sqrt((double)kGroup);
     const float e = f32((double)v[c] * inverse_root);
     const float scaled = f32((double)e * sqrt((double)kDim));
-    float* x = sv.x + (int64_t)it.slot * kLaneWidth;
+    float* x = st.chunk ? st.lanes + (int64_t)b * kLaneWidth : sv.x + (int64_t)it.slot * kLaneWidth;
 #pragma unroll
     for (int lane = 0; lane < kLanes; lane++) x[lane * kDim + c] = scaled;
     __syncthreads();
@@ -161,15 +167,20 @@ __device__ void engram_mix(const ModelView& m, const SlotView& sv, const StepVie
   // equals the token position: both start at 0 on reset and advance once per step.
   const int c = threadIdx.x;
   const int depth = (m.taps - 1) * m.max_order + 1;
+  // In a chunk the ring is not written here (k_finish writes it after the chunk): a tap inside the
+  // chunk reads that item's value, a tap before it the ring.
   for (int si = 0; si < m.n_sites; si++) {
     const float now = st.engram_kv[(((int64_t)b * m.n_sites + si) * 2 + 1) * kDim + c];
     float* ring = sv.ring + ((int64_t)slot * m.n_sites + si) * depth * kDim;
-    ring[(p % depth) * kDim + c] = now;
+    if (!st.chunk) ring[(p % depth) * kDim + c] = now;
     float mixed = 0.0f;
     for (int tap = 0; tap < m.taps; tap++) {
-      const int prev = p - tap * m.max_order;
+      const int back = tap * m.max_order, prev = p - back;
       if (prev < 0) continue;
-      const float value = tap == 0 ? now : ring[(prev % depth) * kDim + c];
+      float value;
+      if (tap == 0) value = now;
+      else if (st.chunk && back <= b) value = st.engram_kv[((((int64_t)(b - back)) * m.n_sites + si) * 2 + 1) * kDim + c];
+      else value = ring[(prev % depth) * kDim + c];
       mixed = f32((double)mixed + (double)m.taps_w[((int64_t)si * m.taps + tap) * kDim + c] * (double)value);
     }
     st.engram_val[((int64_t)b * m.n_sites + si) * kDim + c] = mixed;
@@ -294,7 +305,7 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
   const int tid = threadIdx.x;
   const DevItem it = st.items[b];
   const int slot = it.slot, p = it.position;
-  float* xg = sv.x + (int64_t)slot * kLaneWidth;
+  float* xg = st.chunk ? st.lanes + (int64_t)b * kLaneWidth : sv.x + (int64_t)slot * kLaneWidth;
   {
     float v[kLaneWidth / kThreads];  // all loads in flight before the first store
 #pragma unroll
@@ -359,6 +370,11 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
   __syncthreads();
 
   if (layer == m.layers) {
+    // a chunk's last item leaves its lanes in the slot (what a one-token step leaves there)
+    if (st.chunk && b == *st.n_items - 1) {
+#pragma unroll
+      for (int lane = 0; lane < kLanes; lane++) sv.x[(int64_t)slot * kLaneWidth + lane * kDim + c] = S.xl[lane * kDim + c];
+    }
     // ---------------- final: lane mean, RMSNorm, prepared vocabulary input (runtime.ts:570-577)
     double sum = 0.0;
 #pragma unroll
@@ -661,8 +677,10 @@ __device__ void attend_pair_f32(const float* kf, const float* vf, int count, Slo
   __syncthreads();
 }
 
+// part 0: append this item's K/V, then attend; part 1: append only; part 2: attend only (a
+// chunk's items attend after all of them appended).
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, const SlotView sv,
-                                                           const StepView st, int l) {
+                                                           const StepView st, int l, int part) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ float qv[2 * kHeadDim], kv[kHeadDim], vv[kHeadDim], gt[2 * kHeadDim], outv[2 * kHeadDim];
   __shared__ double red[8];
@@ -711,7 +729,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
     return sink + (pos - sink) % window;
   };
   const int64_t head_base = (((int64_t)slot * sv.layers + l) * kKvHeads + h) * sv.capacity;
-  {
+  if (part != 2) {
     double mk = 0.0, mv = 0.0;
     if (tid < kHeadDim) {
       mk = fabs((double)kv[tid]);
@@ -750,6 +768,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
     }
     __syncthreads();
   }
+  if (part == 1) return;
   // Visible positions (runtime.ts:723-728): [0, prefix) U [recentLow, p].
   const int prefix = min(sink, p + 1);
   const int recent_low = window > 0 ? max(prefix, p + 1 - window) : prefix;
@@ -885,6 +904,32 @@ __global__ void __launch_bounds__(kFinishThreads) k_finish(const ModelView m, co
       st.out_logprob[b] = (double)lg[chosen] - s_max - log(total);
       seq->pending = chosen;
     }
+  }
+  if (st.chunk) {
+    // a prefill chunk: the engram values of its last ring-depth items enter the ring now that every
+    // item has read its taps (k_layer, layer 0), and the slot advances once, past the last item,
+    // with the chunk's last three tokens as its history
+    const int n = *st.n_items;
+    if (m.n_sites > 0) {
+      const int depth = (m.taps - 1) * m.max_order + 1;
+      if (b >= n - depth) {
+        for (int si = 0; si < m.n_sites; si++) {
+          float* ring = sv.ring + ((int64_t)it.slot * m.n_sites + si) * depth * kDim;
+          for (int c = tid; c < kDim; c += kFinishThreads)
+            ring[(it.position % depth) * kDim + c] = st.engram_kv[(((int64_t)b * m.n_sites + si) * 2 + 1) * kDim + c];
+        }
+      }
+    }
+    if (tid == 0 && b == n - 1) {
+      int h[3];
+#pragma unroll
+      for (int k = 0; k < 3; k++) h[k] = k <= b ? st.items[b - k].token : seq->hist[k - b - 1];
+      seq->hist[0] = h[0];
+      seq->hist[1] = h[1];
+      seq->hist[2] = h[2];
+      seq->position = it.position + 1;
+    }
+    return;
   }
   if (tid == 0) {
     seq->position = it.position + 1;
@@ -1106,10 +1151,10 @@ size_t attention_smem_bytes(int32_t capacity, bool) {
 }
 
 cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
-                             int n_host, cudaStream_t s) {
+                             int n_host, cudaStream_t s, int part) {
   if (n_host <= 0) return cudaSuccess;
   const size_t smem = attention_smem_bytes(sv.capacity, true);
-  k_attention<<<dim3(n_host, kKvHeads), kAttnThreads, smem, s>>>(m, sv, st, layer);
+  k_attention<<<dim3(n_host, kKvHeads), kAttnThreads, smem, s>>>(m, sv, st, layer, part);
   return cudaGetLastError();
 }
 
