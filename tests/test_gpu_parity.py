@@ -395,6 +395,41 @@ def test_wide_host_steps_match_single_steps(torch_cuda, archive, ref_model):
         assert together(True) == want
 
 
+@pytest.mark.parametrize("lengths,sink", [((1,), 0), ((2,), 0), ((64,), 0), ((65,), 0), ((130,), 0),
+                                          ((40, 90), 0), ((3, 61, 5), 0), ((300,), 8)])
+def test_chunked_prefill_matches_token_by_token(engine, ref_model, lengths, sink):
+    """needle_cuda_prefill takes a slot's tokens in chunks (one item per token, K/V of the chunk
+    appended before its items attend, engram taps and token history from the chunk, the slot
+    advanced once); it must leave exactly the state n one-token steps leave: logits, every layer's
+    KV codes and scales, the lanes, and the tokens that follow.  Several prefill calls continue one
+    sequence; 300 tokens with a sink of 8 cross the 256-position window."""
+    from needle_b200.backend import StepRequest
+    rng = np.random.default_rng(sum(lengths) + sink)
+    parts = [rng.integers(0, ref_model.vocab, n).astype(np.int32) for n in lengths]
+    total = sum(lengths)
+    a, b = 2, 3
+    for s in (a, b):
+        engine.reset(s, total + 8, sink)
+    for k, part in enumerate(parts):
+        last = k == len(parts) - 1
+        got = engine.prefill(a, part, want_logits=last)
+        for i, t in enumerate(part):
+            _, lg = engine.step([StepRequest(b, int(t))], want_logits=last and i == part.size - 1)
+        if last:
+            np.testing.assert_array_equal(got, lg[0])
+    assert engine.position(a) == engine.position(b) == total
+    for layer in range(engine.geometry.layers):
+        for x, y in zip(engine.read_kv(a, layer), engine.read_kv(b, layer)):
+            np.testing.assert_array_equal(x, y, err_msg=f"layer {layer}")
+    np.testing.assert_array_equal(engine.read_lanes(a), engine.read_lanes(b))
+    tok = int(rng.integers(0, ref_model.vocab))
+    for _ in range(3):
+        sa, _ = engine.step([StepRequest(a, tok, True)])
+        sb, _ = engine.step([StepRequest(b, tok, True)])
+        assert sa == sb
+        tok = sa[0][0]
+
+
 def test_sink_and_window_crossing(engine, oracle, ref_model):
     """A sequence longer than the 256-token window with 8 pinned sink tokens
     (runtime.ts:659-664, 723-728): tokens and cached codes stay exact past the wrap."""
