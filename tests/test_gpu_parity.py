@@ -420,7 +420,8 @@ def test_chunked_prefill_matches_token_by_token(engine, ref_model, lengths, sink
     assert engine.position(a) == engine.position(b) == total
     for layer in range(engine.geometry.layers):
         for x, y in zip(engine.read_kv(a, layer), engine.read_kv(b, layer)):
-            np.testing.assert_array_equal(x, y, err_msg=f"layer {layer}")
+            written = min(total, x.shape[1])  # cache slots written so far (the rest hold old data)
+            np.testing.assert_array_equal(x[:, :written], y[:, :written], err_msg=f"layer {layer}")
     np.testing.assert_array_equal(engine.read_lanes(a), engine.read_lanes(b))
     tok = int(rng.integers(0, ref_model.vocab))
     for _ in range(3):
