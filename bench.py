@@ -526,6 +526,28 @@ def cpu_toolcall(vocab, tools, prompts):
                       "this repository's trie scan (faster than the reference's clone-and-feed scan)"}
 
 
+# Indices of the per-rank config-5 totals that combine by maximum over ranks (times, steps); the
+# rest are summed (tokens, calls, launches, bytes).
+TOOLCALL_MAX_FIELDS = (0, 5, 6, 11, 12)
+
+
+def aggregate_toolcall(local, dist=None):
+    """Whole-job config-5 totals from this rank's [ms, constrained, prompt, completed, dead ends,
+    steps, grammar s, launches, sequences, h2d, d2h, engine s, wall s]: every rank takes the same two
+    all-reduces (sum and max over the process group)."""
+    import torch
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return [float(v) for v in local]
+    t = torch.tensor([float(v) for v in local], dtype=torch.float64)
+    mx = t.clone()
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    tot = t.tolist()
+    for k in TOOLCALL_MAX_FIELDS:
+        tot[k] = mx[k].item()
+    return tot
+
+
 def bench_toolcall(args, rank, world, local_rank):
     """constrained tool-call decode, data-parallel.  --sequences sequences (4096)
     split evenly over the GPUs; each a 256-token prompt of random ids (seed 5 + rank), then the
@@ -596,16 +618,7 @@ def bench_toolcall(args, rank, world, local_rank):
     local = [ms, st.constrained_tokens, st.prompt_tokens, sum(r.complete for r in results),
              sum(r.dead_end for r in results), st.steps, st.grammar_seconds, launches, len(results), h2d, d2h,
              st.engine_seconds, st.seconds]
-    if dist:
-        t = torch.tensor(local, dtype=torch.float64)
-        mx = t.clone()
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        tot = t.tolist()
-        for k in (0, 5, 6, 11, 12):
-            tot[k] = mx[k].item()
-    else:
-        tot = local
+    tot = aggregate_toolcall(local, dist)
     if rank == 0:
         ms_max, cons, prompt_toks, done, dead, steps, gsec, launch_all, seqs, h2d_all, d2h_all, esec, wall = tot
         secs = ms_max / 1e3
