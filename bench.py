@@ -477,6 +477,100 @@ def bench_single(args):
     print(json.dumps(line), flush=True)
 
 
+def reference_arm(args):
+    """`--impl reference` for the workloads other than the default: the C++ restatement of the
+    reference's CPU path (oracle/) on this host's cores, on the CUDA arm's workload, metric and unit,
+    each a bounded sample.  One JSON line with "impl": "reference"."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import needle_ref
+    from needle_b200 import synth
+    needle_ref.build()
+    threads = cpu_threads()
+
+    def emit(metric, value, unit, config, sample, cores, ms_per_step):
+        line = {"metric": metric, "value": round(value, 3), "unit": unit, "impl": "reference", "n_gpus": args.gpus,
+                "steps": 1, "warmup": 0, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": config,
+                "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": cores, "kind": "port", "sample": sample},
+                "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+
+    if args.workload == "single":
+        P, G = args.prompt_len, args.new_tokens
+        model = needle_ref.Model(synth.build_archive(0))
+        prompt = synth.integers(1, P, 8192, stream=0).astype(np.int32)
+        t0 = time.perf_counter()
+        model.generate_greedy(prompt, G, 0, want_logits=False)
+        secs = time.perf_counter() - t0
+        emit("batch-1 greedy decode tokens/s (prefill included)", G / secs, "tokens/s",
+             {"workload": "single sequence greedy decode (BASELINE config 1)", "prompt_len": P, "new_tokens": G},
+             f"the whole workload ({P}-token prompt, {G} greedy tokens) on one core", 1, 1e3 * secs / (P - 1 + G))
+    elif args.workload == "toolcall":
+        from needle_b200 import grammar, toolcall
+        pieces, types, _ = synth.tokenizer_pieces(8192, 0)
+        vocab = grammar.Vocabulary(pieces, types)
+        tools = toolcall.synthetic_tools(5)
+        ids = synth.integers(5, threads * TOOLCALL_PROMPT + 1, 8192, stream=7).astype(np.int32)
+        prompts = [ids[k * TOOLCALL_PROMPT:(k + 1) * TOOLCALL_PROMPT] for k in range(threads)]
+        r = cpu_toolcall(vocab, tools, prompts)
+        emit("constrained tool-call tokens/s", r["value"], "tokens/s",
+             {"workload": "constrained tool-call decode (BASELINE config 5)", "prompt_len": TOOLCALL_PROMPT,
+              "max_new_tokens": TOOLCALL_MAX_NEW}, r["sample"], r["cores"], 1e3 / r["value"] * r["cores"])
+    elif args.workload == "qmatvec":
+        # the headline case: 8192 x 8192 CQ4, batch 1 (seed 2: generator 2000 + shape index)
+        si = next(i for i, sh in enumerate(QMATVEC_SHAPES) if sh[0].startswith("stress"))
+        _, rows, inputs, bits = QMATVEC_SHAPES[si]
+        rng = np.random.default_rng(2000 + si)
+        pad = -(-inputs // 128) * 128
+        row_bytes = pad * bits // 8
+        packed = rng.integers(0, 256, rows * row_bytes + 64, dtype=np.uint8)
+        norms = (np.abs(rng.standard_normal(rows * (pad // 128))) * 0.01).astype(np.float16)
+        cb = synth.lloyd_max_codebook()
+        M = needle_ref.CqMatrix(rows, inputs, 128, bits, packed, norms, cb[:4], cb[4:12], cb[12:28])
+        xs = [rng.standard_normal(inputs).astype(np.float32) for _ in range(threads)]
+        alg = rows * row_bytes + rows * (pad // 128) * 2 + 4 * (inputs + rows)
+
+        def one(x):
+            t0 = time.perf_counter()
+            M.matvec(x)
+            return time.perf_counter() - t0
+
+        with ThreadPoolExecutor(threads) as pool:
+            secs = list(pool.map(one, xs))
+        gbs = threads * alg / float(np.mean(secs)) / 1e9
+        emit("qmatvec HBM GB/s", gbs, "GB/s", {"workload": "isolated quantised matvec (BASELINE config 2), "
+                                                           "headline 8192x8192 CQ4 batch 1", "numerics": "exact (f64)"},
+             f"{threads} concurrent 8192x8192 CQ4 matvecs, one per host thread (the reference's f64 cqMatvecPrepared)",
+             threads, 1e3 * float(np.mean(secs)))
+    elif args.workload == "attention":
+        # the headline case: batch 64, visible counts uniform in [64, 8192] (seed 3: generator 3000 + L)
+        L, batch = 8192, 64
+        rng = np.random.default_rng(3000 + L)
+        counts = rng.integers(64, L + 1, batch)
+        n = min(batch, max(threads, 8))
+
+        def one(k):
+            c = int(counts[k])
+            kc = rng.integers(-127, 128, (4, c, 64), dtype=np.int8)
+            vc = rng.integers(-127, 128, (4, c, 64), dtype=np.int8)
+            ks = (np.abs(rng.standard_normal((4, c))) * 0.02).astype(np.float32)
+            vs = (np.abs(rng.standard_normal((4, c))) * 0.02).astype(np.float32)
+            q = rng.standard_normal(512).astype(np.float32)
+            t0 = time.perf_counter()
+            needle_ref.attention_int8(q, kc, ks, vc, vs)
+            return time.perf_counter() - t0, c * 4 * (64 * 2 + 8) + 2 * 512 * 4 + 4
+
+        with ThreadPoolExecutor(threads) as pool:
+            runs = list(pool.map(one, range(n)))
+        gbs = threads * sum(r[1] for r in runs) / sum(r[0] for r in runs) / 1e9
+        emit("int8-KV decode attention HBM GB/s", gbs, "GB/s",
+             {"workload": "isolated int8-KV decode attention (BASELINE config 3), headline L=8192", "numerics": "exact (f64)"},
+             f"{n} of the 64 sequences (visible counts uniform in [64, 8192]), one per host thread", threads,
+             1e3 * sum(r[0] for r in runs) / n)
+    else:
+        print(json.dumps({"impl": "reference", "unavailable": f"no reference arm for workload {args.workload}"}))
+
+
 def cpu_toolcall(vocab, tools, prompts):
     """BASELINE config 5 on the host cores: the oracle runtime (the C++ restatement of the CPU
     backend) drives the constrained loop of agent.ts:157-210 for one workload sequence per thread
@@ -707,6 +801,10 @@ def main():
         (bench_qmatvec if args.workload == "qmatvec" else bench_attention)(args, peaks)
         return
 
+    if args.impl == "reference" and args.workload != "decode":
+        if rank == 0:
+            reference_arm(args)
+        return
     if args.impl == "reference":
         if rank != 0:
             return
