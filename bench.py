@@ -297,6 +297,8 @@ def bench_qmatvec(args, peaks):
                          "traffic": 33613312 if head["shape"].startswith("stress") and head["batch"] == 1 else None,
                          "traffic_source": "profiles/qmatvec_table_8192x8192_cq4_batch1.md"},
             "gpu_launches": launches}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = {k: v for k, v in cpu_qmatvec().items() if k != "ms"}
     big = next((r for r in results if r["shape"].startswith("stress") and r["batch"] == 128 and r["numerics"] == "fast"),
                None)
     if big is not None:
@@ -366,6 +368,8 @@ def bench_attention(args, peaks):
                          "traffic": 150667520 if head["L"] == 8192 and head["numerics"] == "fast" else None,
                          "traffic_source": "profiles/attention_fast_mma_L8192_batch64.md"},
             "gpu_launches": launches}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = {k: v for k, v in cpu_attention().items() if k != "ms"}
     print(json.dumps(line), flush=True)
 
 
@@ -517,58 +521,87 @@ def reference_arm(args):
              {"workload": "constrained tool-call decode (BASELINE config 5)", "prompt_len": TOOLCALL_PROMPT,
               "max_new_tokens": TOOLCALL_MAX_NEW}, r["sample"], r["cores"], 1e3 / r["value"] * r["cores"])
     elif args.workload == "qmatvec":
-        # the headline case: 8192 x 8192 CQ4, batch 1 (seed 2: generator 2000 + shape index)
-        si = next(i for i, sh in enumerate(QMATVEC_SHAPES) if sh[0].startswith("stress"))
-        _, rows, inputs, bits = QMATVEC_SHAPES[si]
-        rng = np.random.default_rng(2000 + si)
-        pad = -(-inputs // 128) * 128
-        row_bytes = pad * bits // 8
-        packed = rng.integers(0, 256, rows * row_bytes + 64, dtype=np.uint8)
-        norms = (np.abs(rng.standard_normal(rows * (pad // 128))) * 0.01).astype(np.float16)
-        cb = synth.lloyd_max_codebook()
-        M = needle_ref.CqMatrix(rows, inputs, 128, bits, packed, norms, cb[:4], cb[4:12], cb[12:28])
-        xs = [rng.standard_normal(inputs).astype(np.float32) for _ in range(threads)]
-        alg = rows * row_bytes + rows * (pad // 128) * 2 + 4 * (inputs + rows)
-
-        def one(x):
-            t0 = time.perf_counter()
-            M.matvec(x)
-            return time.perf_counter() - t0
-
-        with ThreadPoolExecutor(threads) as pool:
-            secs = list(pool.map(one, xs))
-        gbs = threads * alg / float(np.mean(secs)) / 1e9
-        emit("qmatvec HBM GB/s", gbs, "GB/s", {"workload": "isolated quantised matvec (BASELINE config 2), "
-                                                           "headline 8192x8192 CQ4 batch 1", "numerics": "exact (f64)"},
-             f"{threads} concurrent 8192x8192 CQ4 matvecs, one per host thread (the reference's f64 cqMatvecPrepared)",
-             threads, 1e3 * float(np.mean(secs)))
+        r = cpu_qmatvec()
+        emit("qmatvec HBM GB/s", r["value"], "GB/s", {"workload": "isolated quantised matvec (BASELINE config 2), "
+                                                                  "headline 8192x8192 CQ4 batch 1", "numerics": "exact (f64)"},
+             r["sample"], r["cores"], r["ms"])
     elif args.workload == "attention":
-        # the headline case: batch 64, visible counts uniform in [64, 8192] (seed 3: generator 3000 + L)
-        L, batch = 8192, 64
-        rng = np.random.default_rng(3000 + L)
-        counts = rng.integers(64, L + 1, batch)
-        n = min(batch, max(threads, 8))
-
-        def one(k):
-            c = int(counts[k])
-            kc = rng.integers(-127, 128, (4, c, 64), dtype=np.int8)
-            vc = rng.integers(-127, 128, (4, c, 64), dtype=np.int8)
-            ks = (np.abs(rng.standard_normal((4, c))) * 0.02).astype(np.float32)
-            vs = (np.abs(rng.standard_normal((4, c))) * 0.02).astype(np.float32)
-            q = rng.standard_normal(512).astype(np.float32)
-            t0 = time.perf_counter()
-            needle_ref.attention_int8(q, kc, ks, vc, vs)
-            return time.perf_counter() - t0, c * 4 * (64 * 2 + 8) + 2 * 512 * 4 + 4
-
-        with ThreadPoolExecutor(threads) as pool:
-            runs = list(pool.map(one, range(n)))
-        gbs = threads * sum(r[1] for r in runs) / sum(r[0] for r in runs) / 1e9
-        emit("int8-KV decode attention HBM GB/s", gbs, "GB/s",
+        r = cpu_attention()
+        emit("int8-KV decode attention HBM GB/s", r["value"], "GB/s",
              {"workload": "isolated int8-KV decode attention (BASELINE config 3), headline L=8192", "numerics": "exact (f64)"},
-             f"{n} of the 64 sequences (visible counts uniform in [64, 8192]), one per host thread", threads,
-             1e3 * sum(r[0] for r in runs) / n)
+             r["sample"], r["cores"], r["ms"])
     else:
         print(json.dumps({"impl": "reference", "unavailable": f"no reference arm for workload {args.workload}"}))
+
+
+def cpu_qmatvec():
+    """BASELINE config 2's headline case (8192 x 8192 CQ4, batch 1; indices uniform, fp16 norms
+    |N(0,1)| * 0.01, x N(0,1), seed 2: generator 2000 + shape index) through the C++ restatement of
+    the reference's f64 cqMatvecPrepared, one matvec per host thread at once; GB/s of the same
+    algorithmic bytes as the CUDA line."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import needle_ref
+    from needle_b200 import synth
+    needle_ref.build()
+    threads = cpu_threads()
+    si = next(i for i, sh in enumerate(QMATVEC_SHAPES) if sh[0].startswith("stress"))
+    _, rows, inputs, bits = QMATVEC_SHAPES[si]
+    rng = np.random.default_rng(2000 + si)
+    pad = -(-inputs // 128) * 128
+    row_bytes = pad * bits // 8
+    packed = rng.integers(0, 256, rows * row_bytes + 64, dtype=np.uint8)
+    norms = (np.abs(rng.standard_normal(rows * (pad // 128))) * 0.01).astype(np.float16)
+    cb = synth.lloyd_max_codebook()
+    M = needle_ref.CqMatrix(rows, inputs, 128, bits, packed, norms, cb[:4], cb[4:12], cb[12:28])
+    xs = [rng.standard_normal(inputs).astype(np.float32) for _ in range(threads)]
+    alg = rows * row_bytes + rows * (pad // 128) * 2 + 4 * (inputs + rows)
+
+    def one(x):
+        t0 = time.perf_counter()
+        M.matvec(x)
+        return time.perf_counter() - t0
+
+    with ThreadPoolExecutor(threads) as pool:
+        secs = list(pool.map(one, xs))
+    mean = float(np.mean(secs))
+    return {"value": round(threads * alg / mean / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{threads} concurrent 8192x8192 CQ4 batch-1 matvecs, one per host thread (the reference's "
+                      "f64 cqMatvecPrepared)", "ms": 1e3 * mean}
+
+
+def cpu_attention():
+    """BASELINE config 3's headline case (batch 64, visible counts uniform in [64, 8192], codes uniform
+    in [-127, 127], scales |N(0,1)| * 0.02, q N(0,1), seed 3: generator 3000 + L) through the C++
+    restatement of the reference's attention, one sequence per host thread; GB/s of the same
+    algorithmic bytes as the CUDA line."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import needle_ref
+    needle_ref.build()
+    threads = cpu_threads()
+    L, batch = 8192, 64
+    rng = np.random.default_rng(3000 + L)
+    counts = rng.integers(64, L + 1, batch)
+    n = min(batch, max(threads, 8))
+    inputs = []
+    for k in range(n):
+        c = int(counts[k])
+        inputs.append((rng.standard_normal(512).astype(np.float32), rng.integers(-127, 128, (4, c, 64), dtype=np.int8),
+                       (np.abs(rng.standard_normal((4, c))) * 0.02).astype(np.float32),
+                       rng.integers(-127, 128, (4, c, 64), dtype=np.int8),
+                       (np.abs(rng.standard_normal((4, c))) * 0.02).astype(np.float32)))
+
+    def one(args_):
+        q, kc, ks, vc, vs = args_
+        t0 = time.perf_counter()
+        needle_ref.attention_int8(q, kc, ks, vc, vs)
+        return time.perf_counter() - t0, kc.shape[1] * 4 * (64 * 2 + 8) + 2 * 512 * 4 + 4
+
+    with ThreadPoolExecutor(threads) as pool:
+        runs = list(pool.map(one, inputs))
+    secs = sum(r[0] for r in runs)
+    return {"value": round(threads * sum(r[1] for r in runs) / secs / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port", "sample": f"{n} of the 64 sequences (visible counts uniform in [64, 8192]), one per host "
+                                      "thread (the reference's attention over int8 KV)", "ms": 1e3 * secs / n}
 
 
 def cpu_toolcall(vocab, tools, prompts):
