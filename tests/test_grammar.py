@@ -216,3 +216,38 @@ def test_walk_shortcuts_equal_clone_and_feed_scan(G, case):
         pick = int(pool[rng.integers(0, len(pool))])
         assert g.feed(v.piece[pick])
         text += v.piece[pick]
+
+
+@pytest.mark.parametrize("case", range(6))
+def test_value_starts_equal_clone_and_feed_scan(G, case):
+    """At the first byte of a value the walk filters edges by the bytes that can start it (enum
+    candidates' first bytes, or its types' first bytes); alternatives, consts, mixed enums, refs and
+    nested containers must still give exactly the clone-and-feed ids."""
+    schema = [
+        {"anyOf": [{"type": "integer"}, {"type": "string", "maxLength": 3}, {"type": "null"}]},
+        {"type": "array", "items": {"enum": [1.5, "x", None, True, {"a": 1}, [2]]}, "maxItems": 4},
+        {"type": "object", "properties": {"k": {"const": "fixed"}, "n": {"oneOf": [{"type": "boolean"},
+                                                                             {"type": "number", "maximum": 9}]}},
+         "required": ["k"]},
+        {"$defs": {"p": {"type": "object", "properties": {"x": {"type": "integer"}, "y": {"$ref": "#/$defs/q"}}},
+                   "q": {"type": ["string", "null"]}},
+         "type": "array", "items": {"$ref": "#/$defs/p"}, "maxItems": 3},
+        {"type": "array", "items": {"type": "array", "items": {"type": ["integer", "boolean"]}, "maxItems": 3},
+         "maxItems": 3},
+        {"enum": ["alpha", "beta", 7, False, None]},
+    ][case]
+    v = _vocab(G)
+    g = G.JsonSchemaGrammar(schema)
+    rng = np.random.default_rng(100 + case)
+    text = b""
+    for step in range(30):
+        ids = G.allowed(g, v, len(text))
+        scan = [i for i in range(v.size) if v.piece[i] and g.clone().feed(v.piece[i])]
+        np.testing.assert_array_equal(ids, np.array(scan, dtype=np.uint32), err_msg=f"{text!r}")
+        if ids.size == 0 or g.complete:
+            break
+        short = [i for i in ids if len(v.piece[i]) <= 2]  # small steps visit more value starts
+        pool = short if short and rng.random() < 0.7 else ids
+        pick = int(pool[rng.integers(0, len(pool))])
+        assert g.feed(v.piece[pick])
+        text += v.piece[pick]
