@@ -151,6 +151,32 @@ int needle_cuda_step_begin(needle_ctx* ctx, const needle_step_item* items, int32
 int needle_cuda_step_end(needle_ctx* ctx, const needle_step_item* items, int32_t n, const uint32_t* allowed_ids,
                          size_t allowed_total, needle_selected* out_selected);
 
+/* ---- ResidentExecutionSession (packages/needle.js/src/backends/backend.ts:66-80) ----
+ * The per-token calls NeedleRuntime.step makes on a resident session (runtime.ts:305-372), with
+ * the arguments it passes them, so an adapter serves an unmodified runtime:
+ *   prepareResidentEngrams({indices, valid, position})  -> kept by the adapter (returns true)
+ *   beginResidentToken(x)                               -> kept by the adapter (returns true)
+ *   forwardResidentToken({position})                    -> needle_cuda_resident_forward
+ *   finishResidentToken(wantLogits)                     -> needle_cuda_resident_finish
+ *   finishResidentTokenForSelection()                   -> nothing (the vocabulary projection ran)
+ *   selectResidentToken(allowed?)                       -> needle_cuda_resident_select
+ * needle_cuda_resident_forward enqueues every layer and the vocabulary projection for slot `seq`
+ * from the runtime's lanes (x: mhc_lanes * model_dimension floats, the scaled embedding row in each
+ * lane, runtime.ts:305-313) and its engram lookup (engram_tables table indices and valid flags from
+ * #engramLookup, runtime.ts:788-818; NULL / 0 for an archive without engram sites), then returns
+ * without waiting.  `position` and `engram_position` must equal the slot's position.  The token
+ * then ends with exactly one of needle_cuda_resident_finish (logits, vocabulary floats, written
+ * when non-NULL; nothing is selected) or needle_cuda_resident_select (allowed ids; n_allowed -1 for
+ * the whole vocabulary), which wait and advance the slot; no other call may use the context in
+ * between.  If the end fails, the token is dropped and the slot keeps its position.  A slot stepped
+ * this way keeps no token history: its engram lookups always come from the caller. */
+int needle_cuda_resident_forward(needle_ctx* ctx, int32_t seq, int32_t position, const float* lanes,
+                                 const uint32_t* engram_indices, const uint32_t* engram_valid,
+                                 int32_t engram_tables, int32_t engram_position);
+int needle_cuda_resident_finish(needle_ctx* ctx, int32_t seq, float* logits);
+int needle_cuda_resident_select(needle_ctx* ctx, int32_t seq, const uint32_t* allowed_ids, int32_t n_allowed,
+                                needle_selected* out_selected);
+
 /* NeedleRuntime.prefill (runtime.ts:227-243) for one slot: the n tokens, logits of the last one
  * written to out_logits (vocabulary floats) when non-NULL.  The result is that of n one-token
  * steps; the tokens go through the layers in chunks of up to 64, one item per token (K/V of the
@@ -161,7 +187,8 @@ int needle_cuda_prefill(needle_ctx* ctx, int32_t seq, const int32_t* ids, int32_
 
 /* Copies one layer of a slot's int8 KV cache (layout of runtime.ts:666-677): codes
  * [kv_heads][kv_allocation][head_dim], scales [kv_heads][kv_allocation], where kv_allocation is the
- * slot's min(maximum_length, sink + window) (runtime.ts:166-170).  Any pointer may be NULL. */
+ * slot's min(maximum_length, sink + window) (runtime.ts:166-170).  Any pointer may be NULL.  Slots
+ * of a loaded device-scheduler queue are read as the scheduler left them. */
 int needle_cuda_read_kv(const needle_ctx* ctx, int32_t seq, int32_t layer, int8_t* key_codes,
                         int8_t* value_codes, float* key_scales, float* value_scales,
                         int32_t* kv_allocation);
@@ -274,6 +301,19 @@ int needle_cuda_sched_step(needle_ctx* ctx, int32_t steps);
  * sequence its last selected token (n_seqs entries, -1 while unfinished; may be NULL). */
 int needle_cuda_sched_status(needle_ctx* ctx, int64_t* tokens_processed, int64_t* tokens_generated,
                              int32_t* seqs_finished, int32_t* last_ids);
+
+/* Every token the device scheduler has selected, by sequence: sequence s's greedy ids occupy
+ * entries [G(s), G(s) + gen_steps[s]) with G(s) = gen_steps[0] + ... + gen_steps[s - 1], in the
+ * order they were selected; entries not yet generated are -1.  Copies min(n, total) entries
+ * (synchronising first) and reports the total through *total (either pointer may be NULL).  The
+ * per-sequence id stream of NeedleModel.generate's greedy loop (packages/needle.js/src/model/
+ * model.ts:116-137), for checking a scheduled run against one-sequence decodes. */
+int needle_cuda_sched_ids(needle_ctx* ctx, int32_t* ids, size_t n, size_t* total);
+
+/* State of one scheduler slot: the queued sequence it holds or last held (-1 if it never admitted
+ * one), the tokens that sequence has consumed, and whether it is still running.  With
+ * needle_cuda_read_kv on the same slot, this reads a scheduled sequence's int8 KV cache. */
+int needle_cuda_sched_slot(needle_ctx* ctx, int32_t slot, int32_t* seq_id, int32_t* position, int32_t* busy);
 
 /* Number of CUDA kernels this context has launched so far (for launch accounting). */
 int needle_cuda_kernel_launches(const needle_ctx* ctx, int64_t* count);

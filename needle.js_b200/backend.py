@@ -1,7 +1,7 @@
 """Host-side mirror of the needle.js backend interface over libneedle_cuda.so.
 
 needle.js is TypeScript and its runtime cannot run in this environment, so the adapter it would
-use (a bun:ffi `CudaBackend`) is mirrored here in Python with the same names,
+use (a bun:ffi `CudaBackend` over the same C-ABI) is mirrored here in Python with the same names,
 argument meanings and error behaviour:
 
 * `CudaBackend`         -- InferenceBackend (packages/needle.js/src/backends/backend.ts:83-110):
@@ -203,6 +203,20 @@ class CudaEngine:
                                              ptr(last)))
         return tokens.value, generated.value, finished.value, last[:self._n_seqs]
 
+    def sched_ids(self):
+        """Every selected id of the loaded queue, split per sequence (-1 where not generated yet)."""
+        total = C.c_size_t()
+        check(lib().needle_cuda_sched_ids(self.h, None, 0, C.byref(total)))
+        flat = np.zeros(max(total.value, 1), dtype=np.int32)
+        check(lib().needle_cuda_sched_ids(self.h, ptr(flat), total.value, None))
+        return flat[:total.value]
+
+    def sched_slot(self, slot: int):
+        """(sequence id, position, busy) of a scheduler slot."""
+        sid, pos, busy = C.c_int32(), C.c_int32(), C.c_int32()
+        check(lib().needle_cuda_sched_slot(self.h, slot, C.byref(sid), C.byref(pos), C.byref(busy)))
+        return sid.value, pos.value, bool(busy.value)
+
     def kernel_launches(self) -> int:
         n = C.c_int64()
         check(lib().needle_cuda_kernel_launches(self.h, C.byref(n)))
@@ -274,78 +288,243 @@ class CudaBackend:
 
 
 class CudaResidentSession:
-    """ResidentExecutionSession (backend.ts:66-80) bound to one engine slot.  reset() returns True
-    for supported options and raises NeedleError(BACKEND_UNAVAILABLE) otherwise: unlike the
-    reference's optional sessions, this backend never hands the step back to a CPU loop."""
+    """ResidentExecutionSession (backend.ts:66-80) bound to one engine slot, implementing the whole-
+    token calls NeedleRuntime.step makes (runtime.ts:314-372) with the arguments it passes them.
+    reset() returns True for supported options and raises NeedleError(BACKEND_UNAVAILABLE) otherwise:
+    unlike the reference's optional sessions, this backend never hands the step back to a CPU loop.
+    prepareResidentEngrams and beginResidentToken keep their arguments; forwardResidentToken runs the
+    token on the GPU (needle_cuda_resident_forward); finishResidentToken / selectResidentToken end it."""
 
     def __init__(self, backend: CudaBackend, slot: int):
         self.backend = backend
         self.engine = backend.engine
         self.slot = slot
+        self._lanes = None
+        self._engrams = None
 
-    def reset(self, maximum_length: int, sink_length: int = 0, kv_cache: str = "int8",
-              collect_confidence: bool = False) -> bool:
+    def reset(self, options: dict) -> bool:
+        """reset({maximumLength, sinkLength, kvCache, collectConfidence})."""
+        kv_cache = options.get("kvCache", "int8")
         if kv_cache != self.engine.kv_cache:
             raise NeedleError("BACKEND_UNAVAILABLE",
                               f"this CUDA backend context holds a {self.engine.kv_cache} KV cache")
-        self.engine.reset(self.slot, maximum_length, sink_length, collect_confidence)
+        self.engine.reset(self.slot, options["maximumLength"], options.get("sinkLength", 0),
+                          bool(options.get("collectConfidence", False)))
+        self._lanes = self._engrams = None
+        return True
+
+    def forward(self, request):
+        raise NeedleError("BACKEND_UNAVAILABLE", "the CUDA session runs whole tokens (forwardResidentToken)")
+
+    def prepare_resident_engrams(self, request: dict) -> bool:
+        """prepareResidentEngrams({indices, valid, position})."""
+        self._engrams = (np.ascontiguousarray(request["indices"], dtype=np.uint32),
+                         np.ascontiguousarray(request["valid"], dtype=np.uint32), int(request["position"]))
+        return True
+
+    def begin_resident_token(self, lanes) -> bool:
+        """beginResidentToken(x): the token's lanes (mhcLanes copies of the scaled embedding row)."""
+        self._lanes = np.ascontiguousarray(lanes, dtype=np.float32)
+        return True
+
+    def forward_resident_token(self, request: dict) -> None:
+        """forwardResidentToken({position, engramKeys, engramValues}): every layer and the vocabulary
+        projection, enqueued on the GPU."""
+        if self._lanes is None:
+            raise NeedleError("BACKEND_UNAVAILABLE", "beginResidentToken must precede forwardResidentToken")
+        idx, valid, epos = self._engrams if self._engrams is not None else (None, None, int(request["position"]))
+        lanes, self._lanes, self._engrams = self._lanes, None, None
+        check(lib().needle_cuda_resident_forward(self.engine.h, self.slot, int(request["position"]), ptr(lanes),
+                                                 ptr(idx), ptr(valid), 0 if idx is None else idx.size, epos))
+
+    def finish_resident_token(self, want_logits: bool):
+        """finishResidentToken(wantLogits): the logits (or None) and the slot advanced."""
+        logits = np.zeros(self.engine.vocab, dtype=np.float32) if want_logits else None
+        check(lib().needle_cuda_resident_finish(self.engine.h, self.slot, ptr(logits)))
+        return logits
+
+    def finish_resident_token_for_selection(self) -> None:
+        """finishResidentTokenForSelection(): nothing to do, forward already projected the vocabulary."""
+
+    def select_resident_token(self, allowed=None):
+        """selectResidentToken(allowedTokenIds?) -> (id, logProbability)."""
+        a = None if allowed is None else np.ascontiguousarray(allowed, dtype=np.uint32)
+        sel = native.Selected()
+        check(lib().needle_cuda_resident_select(self.engine.h, self.slot, ptr(a), -1 if a is None else a.size,
+                                                C.byref(sel)))
+        return sel.id, sel.log_probability
+
+    def resident_layers_enabled(self) -> bool:
         return True
 
     def resident_confidence(self) -> float:
         return self.engine.confidence(self.slot)
 
+    def read_resident_lanes(self):
+        return self.engine.read_lanes(self.slot)
+
     def dispose(self):
         self.backend._free.append(self.slot)
 
 
-class NeedleRuntime:
-    """NeedleRuntime (runtime.ts:108-583) over a CUDA resident session."""
+ENGRAM_SEED = 0x9E3779B9   # runtime.ts:22
+ENGRAM_PRIME = 0x01000193  # runtime.ts:23
+EMBEDDING = 0              # canonical tensor order: the embedding is record 0 (cact.ts:403-536)
 
-    def __init__(self, backend: CudaBackend):
+
+def _imul(a: int, b: int) -> int:
+    return (a * b) & 0xFFFFFFFF
+
+
+class NeedleRuntime:
+    """NeedleRuntime (runtime.ts:108-583) restated over a resident session: the host side of step()
+    is the reference's -- embedding row through backend.row, the scaled lanes, #engramLookup on the
+    token history -- and every token goes through the session calls in the reference's order
+    (prepareResidentEngrams, beginResidentToken, forwardResidentToken, then finishResidentToken or
+    finishResidentTokenForSelection + selectResidentToken).  prefill runs step once per token, as
+    runtime.ts:227-243 does; `chunked_prefill` (an extension) sends a prompt through the engine's
+    batched prefill (needle_cuda_prefill) instead, with the same result."""
+
+    def __init__(self, backend: CudaBackend, kv_cache: str = "int8", collect_confidence: bool = True):
         self.backend = backend
+        self.options = {"kvCache": kv_cache, "collectConfidence": collect_confidence}
         self.session = backend.create_resident_session()
         self.engine = backend.engine
-        self.slot = self.session.slot
+        g = self.engine.geometry
+        self.dimension, self.lanes = g.model_dimension, g.mhc_lanes
+        self.vocab = g.vocabulary_size
+        self.orders = list(g.engram_orders[:g.engram_order_count])
+        self.tables, self.slots = g.engram_tables, g.engram_slots
+        self.sites = g.engram_site_count
         self._max = 0
+        self._position = 0
+        self._history: list[int] = []
+        self._engram_position = 0
+        self._selection_request = None
+        self._selection_active = False
+        self._selection_result = None
 
     @property
     def position(self) -> int:
-        return self.engine.position(self.slot)
+        return self._position
 
     @property
     def maximum_length(self) -> int:
         return self._max
 
-    def reset(self, maximum_length: int, sink_length: int = 0, kv_cache: str = "int8",
-              collect_confidence: bool = False):
-        self.session.reset(maximum_length, sink_length, kv_cache, collect_confidence)
+    def reset(self, maximum_length: int, sink_length: int = 0):
+        if not (isinstance(maximum_length, int) and 0 < maximum_length <= self.engine.geometry.maximum_sequence_length):
+            raise NeedleError("CONTEXT_OVERFLOW", f"Runtime length {maximum_length} is outside model limit "
+                                                  f"{self.engine.geometry.maximum_sequence_length}")
         self._max = maximum_length
+        sink = min(max(sink_length, 0), maximum_length)
+        self._position = 0
+        self._history = []
+        self._engram_position = 0
+        self._selection_active = False
+        self.session.reset({"maximumLength": maximum_length, "sinkLength": sink, "kvCache": self.options["kvCache"],
+                            "collectConfidence": self.options["collectConfidence"] is not False})
 
     def confidence(self) -> float:
         """NeedleRuntime.confidence (runtime.ts:634-645): NaN unless collecting."""
         return self.session.resident_confidence()
 
-    def prefill(self, tokens) -> np.ndarray:
+    def prefill(self, tokens, chunked_prefill: bool = False) -> np.ndarray:
         if len(tokens) == 0:
             raise NeedleError("INVALID_CACT", "Cannot prefill an empty token sequence")
-        return self.engine.prefill(self.slot, tokens, want_logits=True)
+        if self._max < len(tokens):
+            raise NeedleError("CONTEXT_OVERFLOW", f"Prompt has {len(tokens)} tokens but runtime holds {self._max}")
+        if chunked_prefill:
+            logits = self.engine.prefill(self.slot_index, tokens, want_logits=True)
+            self._history.extend(int(t) for t in tokens)
+            self._position += len(tokens)
+            self._engram_position += len(tokens)
+            return logits
+        logits = None
+        for i, t in enumerate(tokens):
+            logits = self.step(int(t), want_logits=i == len(tokens) - 1)
+        return logits
 
     def prefill_selected(self, tokens, allowed=None):
         if len(tokens) == 0:
             raise NeedleError("INVALID_CACT", "Cannot prefill an empty token sequence")
-        if len(tokens) > 1:
-            self.engine.prefill(self.slot, tokens[:-1], want_logits=False)
-        return self.step_selected(tokens[-1], allowed)
-
-    def step(self, token: int, want_logits: bool = True):
-        _, logits = self.engine.step([StepRequest(self.slot, int(token))], want_logits=want_logits)
-        return None if logits is None else logits[0]
+        for t in tokens[:-1]:
+            self.step(int(t), want_logits=False)
+        return self.step_selected(int(tokens[-1]), allowed)
 
     def step_selected(self, token: int, allowed=None):
-        if allowed is not None and len(allowed) == 0:
-            raise NeedleError("INVALID_CACT", "Allowed token set is empty")
-        sel, _ = self.engine.step([StepRequest(self.slot, int(token), True, allowed)])
-        return sel[0]
+        if self._selection_active:
+            raise NeedleError("BACKEND_UNAVAILABLE", "Selection is already active")
+        self._selection_active = True
+        self._selection_request = None if allowed is None else np.asarray(allowed, dtype=np.uint32)
+        self._selection_result = None
+        try:
+            self.step(token)
+            if self._selection_result is None:
+                raise NeedleError("BACKEND_UNAVAILABLE", "Token selection did not produce a result")
+            return self._selection_result
+        finally:
+            self._selection_active = False
+            self._selection_request = None
+            self._selection_result = None
+
+    def _engram_lookup(self):
+        """#engramLookup (runtime.ts:788-818): per order and head an FNV-style hash of the last
+        `order` tokens of the history (missing tokens hash as 0), valid when the history reaches back
+        that far."""
+        per_order = self.tables // len(self.orders)
+        indices = np.zeros(self.tables, dtype=np.uint32)
+        valid = np.zeros(self.tables, dtype=np.uint32)
+        table = 0
+        for oi, order in enumerate(self.orders):
+            for head in range(per_order):
+                h = _imul(ENGRAM_SEED, oi * per_order + head + 1)
+                ok = True
+                for off in range(order):
+                    hi = len(self._history) - 1 - off
+                    tok = self._history[hi] if hi >= 0 else 0
+                    h = _imul((h ^ tok) & 0xFFFFFFFF, ENGRAM_PRIME)
+                    if off == order - 1:
+                        ok = hi >= 0
+                h = (h ^ (h >> 15)) & 0xFFFFFFFF
+                indices[table] = h % self.slots
+                valid[table] = 1 if ok else 0
+                table += 1
+        return indices, valid
+
+    def step(self, token: int, want_logits: bool = True):
+        if self._max <= 0:
+            raise NeedleError("INVALID_CACT", "Call runtime.reset() before decoding")
+        if self._position >= self._max:
+            raise NeedleError("CONTEXT_OVERFLOW", f"Position {self._position} reached runtime limit {self._max}")
+        if not (0 <= int(token) < self.vocab):
+            raise NeedleError("INVALID_CACT", f"Token {token} is outside the vocabulary")
+        position = self._position
+        self._history.append(int(token))
+        embedding = self.backend.row(EMBEDDING, int(token))
+        scaled = (embedding.astype(np.float64) * np.sqrt(float(self.dimension))).astype(np.float32)
+        x = np.tile(scaled, self.lanes)
+        if self.sites > 0:
+            indices, valid = self._engram_lookup()
+            if self.session.prepare_resident_engrams({"indices": indices, "valid": valid,
+                                                      "position": self._engram_position}):
+                self._engram_position += 1
+        self.session.begin_resident_token(x)
+        self.session.forward_resident_token({"position": position, "engramKeys": [], "engramValues": []})
+        logits = None
+        if self._selection_active:
+            self.session.finish_resident_token_for_selection()
+        else:
+            logits = self.session.finish_resident_token(want_logits is not False)
+        self._position += 1
+        if self._selection_active:
+            self._selection_result = self.session.select_resident_token(self._selection_request)
+            return None
+        return logits if want_logits is not False else None
+
+    @property
+    def slot_index(self) -> int:
+        return self.session.slot
 
     def dispose(self):
         self.session.dispose()

@@ -362,16 +362,21 @@ struct needle_ctx {
   uint32_t* d_allowed = nullptr;
   size_t allowed_cap = 0;
   DevItem* h_items_end = nullptr;  // the items as needle_cuda_step_end re-uploads them
+  float* h_lanes = nullptr;         // a resident-session item's lanes (pinned, kLaneWidth floats)
+  uint32_t* h_engram = nullptr;     // and its engram lookup (pinned, 2 * kMaxTables)
+  uint32_t* d_engram_in = nullptr;  // StepView::engram_in
   // a step begun by needle_cuda_step_begin and not yet ended
   struct PendingStep {
     bool active = false;
     int n = 0, n_sel = 0;
     std::vector<int> order;
     std::vector<needle_step_item> items;
+    bool resident = false;  // begun by needle_cuda_resident_forward
   } pending;
   // scheduler
   SchedView sched{};
   bool sched_loaded = false;
+  int64_t sched_gen_total = 0;  // entries of sched.gen_ids
   std::vector<void*> sched_allocs;
   // matvec API scratch
   float* d_mv_x = nullptr;
@@ -669,6 +674,8 @@ void build_state(needle_ctx& C) {
   st.items = C.dalloc<DevItem>(B);
   st.chunk = 0;
   st.lanes = C.dalloc<float>(B * kLaneWidth);
+  C.d_engram_in = C.dalloc<uint32_t>(B * 2 * kMaxTables);
+  st.engram_in = C.d_engram_in;
   C.d_counts = C.dalloc<int32_t>(8);
   C.d_confidence = C.dalloc<double>(1);
   st.n_items = C.d_counts;
@@ -693,6 +700,8 @@ void build_state(needle_ctx& C) {
   st.allowed = C.d_allowed;
   cuda_check(cudaMallocHost(&C.h_items, B * sizeof(DevItem)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_items_end, B * sizeof(DevItem)), "cudaMallocHost");
+  cuda_check(cudaMallocHost(&C.h_lanes, kLaneWidth * sizeof(float)), "cudaMallocHost");
+  cuda_check(cudaMallocHost(&C.h_engram, 2 * kMaxTables * sizeof(uint32_t)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_counts, 4 * sizeof(int32_t)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_ids, B * sizeof(int32_t)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_logprob, B * sizeof(double)), "cudaMallocHost");
@@ -887,6 +896,8 @@ void destroy(needle_ctx* C) {
   if (C->d_row_out) cudaFree(C->d_row_out);
   if (C->h_items) cudaFreeHost(C->h_items);
   if (C->h_items_end) cudaFreeHost(C->h_items_end);
+  if (C->h_lanes) cudaFreeHost(C->h_lanes);
+  if (C->h_engram) cudaFreeHost(C->h_engram);
   if (C->h_counts) cudaFreeHost(C->h_counts);
   if (C->h_ids) cudaFreeHost(C->h_ids);
   if (C->h_logprob) cudaFreeHost(C->h_logprob);
@@ -927,6 +938,19 @@ void ensure_mv(needle_ctx& C, size_t floats) {
 // ------------------------------------------------------------------ C-ABI
 
 namespace {
+
+// KV allocation of a slot: the host's record for slots reset through needle_cuda_seq_reset, the
+// device's for slots the device scheduler admitted (after a synchronisation).
+int slot_kv_alloc(needle_ctx& C, int seq) {
+  const SlotHost& h = C.slots[seq];
+  if (h.ready) return h.kv_alloc;
+  require(C.sched_loaded, NEEDLE_INVALID_CACT, "KV cache was not allocated");
+  SeqState st{};
+  cuda_check(cudaStreamSynchronize(C.stream), "read_kv");
+  cuda_check(cudaMemcpy(&st, C.sv.seq + seq, sizeof(st), cudaMemcpyDeviceToHost), "read_kv");
+  require(st.kv_alloc > 0, NEEDLE_INVALID_CACT, "KV cache was not allocated");
+  return st.kv_alloc;
+}
 
 // Checks one item's allowed list against the vocabulary (selectToken, runtime.ts:880-899).
 void check_allowed(const needle_step_item& it, const uint32_t* allowed_ids, size_t allowed_total, int V) {
@@ -1041,6 +1065,60 @@ void complete_step(needle_ctx& C, const needle_step_item* items, int32_t n, int 
       out_selected[i].log_probability = C.h_logprob[order[i]];
     }
   }
+}
+
+
+// Second half of a begun step (needle_cuda_step_end, needle_cuda_resident_finish / _select): the
+// same items with their allowed lists (a select may be cleared), selection, readback of the
+// selections and of the logits rows when out_logits is given, and the slots advanced.  On any
+// failure the begun work is drained and the step is dropped: the slots keep their positions, so
+// their next step rewrites the K/V this one appended.
+void end_step(needle_ctx& C, const needle_step_item* items, int32_t n, const uint32_t* allowed_ids,
+              size_t allowed_total, needle_selected* out_selected, float* out_logits) {
+  auto& P = C.pending;
+  require(P.active, NEEDLE_BACKEND_UNAVAILABLE, "needle_cuda_step_end without needle_cuda_step_begin");
+  cuda_check(cudaSetDevice(C.device), "cudaSetDevice");
+  struct Drop {
+    needle_ctx& C;
+    bool armed = true;
+    ~Drop() {
+      if (!armed) return;
+      cudaStreamSynchronize(C.stream);
+      C.pending.active = false;
+      C.pending.resident = false;
+    }
+  } drop{C};
+  require(n == P.n && items != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "step_end items differ from step_begin's");
+  const int V = C.mv.vocab;
+  for (int i = 0; i < n; i++) {
+    const needle_step_item& it = items[i];
+    const needle_step_item& b = P.items[i];
+    require(it.seq == b.seq && it.token == b.token && (!it.select || b.select), NEEDLE_BACKEND_UNAVAILABLE,
+            "step_end items differ from step_begin's (only select may be cleared)");
+    if (it.select) {
+      require(out_selected != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "selection requested without output");
+      check_allowed(it, allowed_ids, allowed_total, V);
+    }
+  }
+  // the allowed fields (and cleared selects) go in with a second copy of the items, ordered after
+  // the layers that read the first
+  for (int i = 0; i < n; i++) {
+    DevItem d = C.h_items[P.order[i]];
+    d.select = items[i].select ? 1 : 0;
+    d.allowed_count = items[i].select ? items[i].allowed_count : -1;
+    d.allowed_offset = items[i].allowed_offset;
+    C.h_items_end[P.order[i]] = d;
+  }
+  upload_allowed(C, allowed_ids, allowed_total);
+  C.timed(P_COPY, [&] {
+    return cudaMemcpyAsync(C.stv.items, C.h_items_end, size_t(n) * sizeof(DevItem), cudaMemcpyHostToDevice,
+                           C.stream);
+  });
+  C.timed(P_FINISH, [&] { return launch_finish(C.mv, C.sv, C.stv, n, nullptr, C.stream); }, C.stream);
+  complete_step(C, items, n, P.n_sel, P.order, out_selected, out_logits);
+  drop.armed = false;
+  P.active = false;
+  P.resident = false;
 }
 
 }  // namespace
@@ -1241,51 +1319,91 @@ int needle_cuda_step_end(needle_ctx* ctx, const needle_step_item* items, int32_t
                          size_t allowed_total, needle_selected* out_selected) {
   return guarded([&] {
     require(ctx != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null needle context");
-    needle_ctx& C = *ctx;
+    require(!ctx->pending.resident, NEEDLE_BACKEND_UNAVAILABLE,
+            "a resident token is in flight; it ends with needle_cuda_resident_finish or _select");
+    end_step(*ctx, items, n, allowed_ids, allowed_total, out_selected, nullptr);
+  });
+}
+
+int needle_cuda_resident_forward(needle_ctx* ctx, int32_t seq, int32_t position, const float* lanes,
+                                 const uint32_t* engram_indices, const uint32_t* engram_valid, int32_t engram_tables,
+                                 int32_t engram_position) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    const ModelView& m = C.mv;
+    require(seq >= 0 && seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
+    const SlotHost& h = C.slots[seq];
+    require(h.ready, NEEDLE_INVALID_CACT, "Call runtime.reset() before decoding");
+    if (h.position >= h.max_len)
+      fail(NEEDLE_CONTEXT_OVERFLOW,
+           "Position " + std::to_string(h.position) + " reached runtime limit " + std::to_string(h.max_len));
+    require(position == h.position, NEEDLE_BACKEND_UNAVAILABLE,
+            "resident token position " + std::to_string(position) + " differs from the session's " +
+                std::to_string(h.position));
+    require(lanes != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "beginResidentToken lanes are missing");
+    int32_t flags = kItemLanes;
+    if (m.n_sites > 0) {
+      require(engram_indices != nullptr && engram_valid != nullptr && engram_tables == m.n_tables,
+              NEEDLE_BACKEND_UNAVAILABLE, "prepareResidentEngrams lookup is missing or has the wrong table count");
+      require(engram_position == position, NEEDLE_BACKEND_UNAVAILABLE,
+              "engram position " + std::to_string(engram_position) + " differs from the token position");
+      for (int t = 0; t < m.n_tables; t++) {
+        require(engram_indices[t] < uint32_t(m.engram_slots), NEEDLE_INVALID_CACT, "engram index outside its table");
+        C.h_engram[t] = engram_indices[t];
+        C.h_engram[kMaxTables + t] = engram_valid[t] ? 1u : 0u;
+      }
+      flags |= kItemEngrams;
+    }
+    std::memcpy(C.h_lanes, lanes, kLaneWidth * sizeof(float));
     auto& P = C.pending;
-    require(P.active, NEEDLE_BACKEND_UNAVAILABLE, "needle_cuda_step_end without needle_cuda_step_begin");
-    cuda_check(cudaSetDevice(C.device), "cudaSetDevice");
-    // On any failure below the begun work is drained and the step is dropped: the slots keep
-    // their positions, so their next step rewrites the K/V this one appended.
-    struct Drop {
-      needle_ctx& C;
-      bool armed = true;
-      ~Drop() {
-        if (!armed) return;
-        cudaStreamSynchronize(C.stream);
-        C.pending.active = false;
-      }
-    } drop{C};
-    require(n == P.n && items != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "step_end items differ from step_begin's");
-    const int V = C.mv.vocab;
-    for (int i = 0; i < n; i++) {
-      const needle_step_item& it = items[i];
-      const needle_step_item& b = P.items[i];
-      require(it.seq == b.seq && it.token == b.token && (!it.select || b.select), NEEDLE_BACKEND_UNAVAILABLE,
-              "step_end items differ from step_begin's (only select may be cleared)");
-      if (it.select) {
-        require(out_selected != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "selection requested without output");
-        check_allowed(it, allowed_ids, allowed_total, V);
-      }
-    }
-    // the allowed fields (and cleared selects) go in with a second copy of the items, ordered after
-    // the layers that read the first
-    for (int i = 0; i < n; i++) {
-      DevItem d = C.h_items[P.order[i]];
-      d.select = items[i].select ? 1 : 0;
-      d.allowed_count = items[i].select ? items[i].allowed_count : -1;
-      d.allowed_offset = items[i].allowed_offset;
-      C.h_items_end[P.order[i]] = d;
-    }
-    upload_allowed(C, allowed_ids, allowed_total);
+    const needle_step_item item{seq, 0, 1, -1, 0};
+    stage_items(C, &item, 1, 1, false, P.order, C.h_items);
+    C.h_items[0].flags = flags;
     C.timed(P_COPY, [&] {
-      return cudaMemcpyAsync(C.stv.items, C.h_items_end, size_t(n) * sizeof(DevItem), cudaMemcpyHostToDevice,
+      cudaError_t e = cudaMemcpyAsync(C.stv.lanes, C.h_lanes, kLaneWidth * sizeof(float), cudaMemcpyHostToDevice,
+                                      C.stream);
+      if (e != cudaSuccess || !(flags & kItemEngrams)) return e;
+      return cudaMemcpyAsync(C.d_engram_in, C.h_engram, 2 * kMaxTables * sizeof(uint32_t), cudaMemcpyHostToDevice,
                              C.stream);
     });
-    C.timed(P_FINISH, [&] { return launch_finish(C.mv, C.sv, C.stv, n, nullptr, C.stream); }, C.stream);
-    complete_step(C, items, n, P.n_sel, P.order, out_selected, nullptr);
-    drop.armed = false;
-    P.active = false;
+    upload_items(C, C.h_items, 1, 1);
+    enqueue_step(C, C.stv, 1, true, nullptr, lane_a(C), /*finish=*/false);
+    P.items.assign(&item, &item + 1);
+    P.n = 1;
+    P.n_sel = 1;
+    P.active = true;
+    P.resident = true;
+  });
+}
+
+namespace {
+// The item a resident token began with, for its end (finish or select).
+needle_ctx& resident_pending(needle_ctx* ctx, int32_t seq) {
+  require(ctx != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null needle context");
+  require(ctx->pending.active && ctx->pending.resident && ctx->pending.items[0].seq == seq,
+          NEEDLE_BACKEND_UNAVAILABLE, "no resident token of this slot is in flight");
+  return *ctx;
+}
+}  // namespace
+
+int needle_cuda_resident_finish(needle_ctx* ctx, int32_t seq, float* logits) {
+  return guarded([&] {
+    needle_ctx& C = resident_pending(ctx, seq);
+    needle_step_item item = C.pending.items[0];
+    item.select = 0;
+    end_step(C, &item, 1, nullptr, 0, nullptr, logits);
+  });
+}
+
+int needle_cuda_resident_select(needle_ctx* ctx, int32_t seq, const uint32_t* allowed_ids, int32_t n_allowed,
+                                needle_selected* out_selected) {
+  return guarded([&] {
+    needle_ctx& C = resident_pending(ctx, seq);
+    require(out_selected != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "selection requested without output");
+    needle_step_item item = C.pending.items[0];
+    item.allowed_count = n_allowed < 0 ? -1 : n_allowed;
+    item.allowed_offset = 0;
+    end_step(C, &item, 1, allowed_ids, n_allowed < 0 ? 0 : size_t(n_allowed), out_selected, nullptr);
   });
 }
 
@@ -1352,24 +1470,23 @@ int needle_cuda_read_kv(const needle_ctx* ctx, int32_t seq, int32_t layer, int8_
     needle_ctx& C = *ctx_of(const_cast<needle_ctx*>(ctx));
     require(seq >= 0 && seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
     require(layer >= 0 && layer < C.mv.layers, NEEDLE_INVALID_CACT, "Layer out of range");
-    const SlotHost& h = C.slots[seq];
-    require(h.ready, NEEDLE_INVALID_CACT, "KV cache was not allocated");
     require(!C.sv.kv_f32, NEEDLE_INVALID_CACT, "Int8 KV cache is not allocated");
-    if (kv_allocation) *kv_allocation = h.kv_alloc;
+    const int kv_alloc = slot_kv_alloc(C, seq);
+    if (kv_allocation) *kv_allocation = kv_alloc;
     const int cap = C.sv.capacity;
     for (int head = 0; head < kKvHeads; head++) {
       const size_t base = ((size_t(seq) * C.mv.layers + layer) * kKvHeads + head) * cap;
       if (key_codes)
-        cuda_check(cudaMemcpy(key_codes + size_t(head) * h.kv_alloc * kHeadDim, C.sv.kcodes + base * kHeadDim,
-                              size_t(h.kv_alloc) * kHeadDim, cudaMemcpyDeviceToHost), "read_kv");
+        cuda_check(cudaMemcpy(key_codes + size_t(head) * kv_alloc * kHeadDim, C.sv.kcodes + base * kHeadDim,
+                              size_t(kv_alloc) * kHeadDim, cudaMemcpyDeviceToHost), "read_kv");
       if (value_codes)
-        cuda_check(cudaMemcpy(value_codes + size_t(head) * h.kv_alloc * kHeadDim, C.sv.vcodes + base * kHeadDim,
-                              size_t(h.kv_alloc) * kHeadDim, cudaMemcpyDeviceToHost), "read_kv");
+        cuda_check(cudaMemcpy(value_codes + size_t(head) * kv_alloc * kHeadDim, C.sv.vcodes + base * kHeadDim,
+                              size_t(kv_alloc) * kHeadDim, cudaMemcpyDeviceToHost), "read_kv");
       if (key_scales)
-        cuda_check(cudaMemcpy(key_scales + size_t(head) * h.kv_alloc, C.sv.kscale + base, size_t(h.kv_alloc) * 4,
+        cuda_check(cudaMemcpy(key_scales + size_t(head) * kv_alloc, C.sv.kscale + base, size_t(kv_alloc) * 4,
                               cudaMemcpyDeviceToHost), "read_kv");
       if (value_scales)
-        cuda_check(cudaMemcpy(value_scales + size_t(head) * h.kv_alloc, C.sv.vscale + base, size_t(h.kv_alloc) * 4,
+        cuda_check(cudaMemcpy(value_scales + size_t(head) * kv_alloc, C.sv.vscale + base, size_t(kv_alloc) * 4,
                               cudaMemcpyDeviceToHost), "read_kv");
     }
   });
@@ -1514,6 +1631,13 @@ int needle_cuda_sched_load(needle_ctx* ctx, int32_t n_slots, const int32_t* prom
     int32_t* d_gen = static_cast<int32_t*>(alloc(size_t(n_seqs) * 4));
     int32_t* d_ctr = static_cast<int32_t*>(alloc(64));
     int32_t* d_last = static_cast<int32_t*>(alloc(size_t(std::max(n_seqs, 1)) * 4));
+    std::vector<int64_t> gen_off(size_t(n_seqs) + 1, 0);
+    for (int s = 0; s < n_seqs; s++) gen_off[s + 1] = gen_off[s] + gen_steps[s];
+    int64_t* d_gen_off = static_cast<int64_t*>(alloc(gen_off.size() * 8));
+    int32_t* d_gen_ids = static_cast<int32_t*>(alloc(size_t(std::max<int64_t>(gen_off[n_seqs], 1)) * 4));
+    cuda_check(cudaMemcpy(d_gen_off, gen_off.data(), gen_off.size() * 8, cudaMemcpyHostToDevice), "sched upload");
+    cuda_check(cudaMemset(d_gen_ids, 0xff, size_t(std::max<int64_t>(gen_off[n_seqs], 1)) * 4), "sched init");
+    C.sched_gen_total = gen_off[n_seqs];
     cuda_check(cudaMemcpy(d_off, prompt_offsets, size_t(n_seqs + 1) * 4, cudaMemcpyHostToDevice), "sched upload");
     if (total) cuda_check(cudaMemcpy(d_ids, prompt_ids, total * 4, cudaMemcpyHostToDevice), "sched upload");
     cuda_check(cudaMemcpy(d_gen, gen_steps, size_t(n_seqs) * 4, cudaMemcpyHostToDevice), "sched upload");
@@ -1534,6 +1658,8 @@ int needle_cuda_sched_load(needle_ctx* ctx, int32_t n_slots, const int32_t* prom
     q.processed = reinterpret_cast<int64_t*>(d_ctr + 2);
     q.generated = reinterpret_cast<int64_t*>(d_ctr + 4);
     q.last_ids = d_last;
+    q.gen_offsets = d_gen_off;
+    q.gen_ids = d_gen_ids;
     C.sched_loaded = true;
     cuda_check(launch_sched_admit(C.sv, q, window, C.stream), "admit");
     cuda_check(cudaStreamSynchronize(C.stream), "sched_load");
@@ -1593,6 +1719,31 @@ int needle_cuda_sched_status(needle_ctx* ctx, int64_t* tokens_processed, int64_t
     if (last_ids && C.sched.n_seqs > 0)
       cuda_check(cudaMemcpy(last_ids, C.sched.last_ids, size_t(C.sched.n_seqs) * 4, cudaMemcpyDeviceToHost),
                  "sched_status");
+  });
+}
+
+int needle_cuda_sched_ids(needle_ctx* ctx, int32_t* ids, size_t n, size_t* total) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    require(C.sched_loaded, NEEDLE_BACKEND_UNAVAILABLE, "no scheduler queue loaded");
+    if (total) *total = size_t(C.sched_gen_total);
+    cuda_check(cudaStreamSynchronize(C.stream), "sched_ids");
+    const size_t k = std::min(n, size_t(C.sched_gen_total));
+    if (ids && k) cuda_check(cudaMemcpy(ids, C.sched.gen_ids, k * 4, cudaMemcpyDeviceToHost), "sched_ids");
+  });
+}
+
+int needle_cuda_sched_slot(needle_ctx* ctx, int32_t slot, int32_t* seq_id, int32_t* position, int32_t* busy) {
+  return guarded([&] {
+    needle_ctx& C = *ctx_of(ctx);
+    require(C.sched_loaded, NEEDLE_BACKEND_UNAVAILABLE, "no scheduler queue loaded");
+    require(slot >= 0 && slot < C.sched.n_slots, NEEDLE_BACKEND_UNAVAILABLE, "slot out of range");
+    SeqState st{};
+    cuda_check(cudaStreamSynchronize(C.stream), "sched_slot");
+    cuda_check(cudaMemcpy(&st, C.sv.seq + slot, sizeof(st), cudaMemcpyDeviceToHost), "sched_slot");
+    if (seq_id) *seq_id = st.kv_alloc > 0 ? st.seq_id : -1;
+    if (position) *position = st.position;
+    if (busy) *busy = st.busy;
   });
 }
 

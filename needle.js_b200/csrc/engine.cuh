@@ -82,8 +82,14 @@ struct DevItem {
   uint32_t allowed_offset;
   int32_t position;         // filled by k_embed
   int32_t out_index;        // caller's index
-  int32_t pad;
+  int32_t flags;            // kItemLanes | kItemEngrams: inputs given by a resident session
 };
+
+// DevItem::flags.  A resident-session item (needle_cuda_resident_forward) brings the lanes that
+// NeedleRuntime built from the embedding row (StepView::lanes, row = item) and the engram lookup it
+// hashed from its token history (StepView::engram_in), instead of a token.
+constexpr int32_t kItemLanes = 1;
+constexpr int32_t kItemEngrams = 2;
 
 // Step scratch, indexed by internal item index.
 struct StepView {
@@ -110,7 +116,8 @@ struct StepView {
   // whole chunk before any item attends, and the slot's state (position, token history, engram
   // ring) advances once, after the chunk.
   int32_t chunk;
-  float* lanes;             // [B][4][512] (chunk steps)
+  float* lanes;             // [B][4][512] (chunk steps; kItemLanes items)
+  const uint32_t* engram_in;  // [B][2][kMaxTables]: table indices, then valid flags (kItemEngrams)
 };
 
 // Device scheduler queue (needle_cuda_sched_*).
@@ -125,6 +132,8 @@ struct SchedView {
   int64_t* processed;             // tokens processed
   int64_t* generated;             // tokens selected (generated)
   int32_t* last_ids;              // [n_seqs]
+  const int64_t* gen_offsets;     // [n_seqs]: start of each sequence's run in gen_ids
+  int32_t* gen_ids;               // [sum of gen_steps]: every selected id, by sequence, in order
 };
 
 cudaError_t launch_embed(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,

@@ -75,8 +75,14 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
   const int token = s_token, p = s_pos;
 
   // #engramLookup (runtime.ts:788-818): history = [..., hist[1], hist[0], token].  In a chunk the
-  // tokens before this item's come from the earlier items, then from the slot's history.
-  if (tid < m.n_tables && m.n_sites > 0) {
+  // tokens before this item's come from the earlier items, then from the slot's history.  A
+  // resident-session item brings the lookup NeedleRuntime computed (prepareResidentEngrams).
+  if (it.flags & kItemEngrams) {
+    if (tid < m.n_tables && m.n_sites > 0) {
+      eidx[tid] = st.engram_in[(int64_t)b * 2 * kMaxTables + tid] % (uint32_t)m.engram_slots;
+      evalid[tid] = st.engram_in[(int64_t)b * 2 * kMaxTables + kMaxTables + tid] != 0u;
+    }
+  } else if (tid < m.n_tables && m.n_sites > 0) {
     const int heads_per_order = m.n_tables / m.n_orders;
     const int oi = tid / heads_per_order, head = tid - oi * heads_per_order;
     const int order = m.orders[oi];
@@ -94,14 +100,19 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
     evalid[tid] = (order - 1) <= p;
   }
   __syncthreads();
-  if (tid == 0 && !st.chunk) {  // a chunk's history advances in k_finish, after every item read it
+  if (tid == 0 && !st.chunk && !(it.flags & kItemEngrams)) {  // a chunk's history advances in k_finish
     q->hist[2] = q->hist[1];
     q->hist[1] = q->hist[0];
     q->hist[0] = token;
   }
 
   // Embedding: dequantizeCqRow(embedding, token) * sqrt(512), broadcast to the lanes (305-313).
-  {
+  // A resident-session item's lanes are beginResidentToken's (built by the runtime the same way).
+  if (it.flags & kItemLanes) {
+    float* x = sv.x + (int64_t)it.slot * kLaneWidth;
+    for (int c = tid; c < kLaneWidth; c += kThreads) x[c] = st.lanes[(int64_t)b * kLaneWidth + c];
+    __syncthreads();
+  } else {
     const CqMat& E = m.embedding;
     const int c = tid;
     const int g = c / kGroup;
@@ -937,6 +948,7 @@ __global__ void __launch_bounds__(kFinishThreads) k_finish(const ModelView m, co
       atomicAdd(reinterpret_cast<unsigned long long*>(q.processed), 1ull);
       if (selecting) {
         atomicAdd(reinterpret_cast<unsigned long long*>(q.generated), 1ull);
+        q.gen_ids[q.gen_offsets[seq->seq_id] + seq->gen_done] = chosen;
         const int done = seq->gen_done + 1;
         seq->gen_done = done;
         if (done >= seq->gen_target) {
@@ -1097,7 +1109,7 @@ __global__ void __launch_bounds__(1024) k_sched(const SlotView sv, const StepVie
     it.allowed_offset = 0;
     it.position = seq.position;
     it.out_index = idx;
-    it.pad = 0;
+    it.flags = 0;
     st.items[idx] = it;
   }
   __syncthreads();

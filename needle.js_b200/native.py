@@ -76,6 +76,10 @@ EXPORTS = {
                                    C.c_void_p, C.c_void_p]),
     "needle_cuda_step_begin": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
     "needle_cuda_step_end": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "needle_cuda_resident_forward": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
+                                               C.c_void_p, C.c_int32, C.c_int32]),
+    "needle_cuda_resident_finish": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p]),
+    "needle_cuda_resident_select": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_void_p]),
     "needle_cuda_prefill": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_void_p]),
     "needle_cuda_read_kv": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p, C.POINTER(C.c_int32)]),
@@ -101,6 +105,9 @@ EXPORTS = {
     "needle_cuda_sched_step": (C.c_int, [C.c_void_p, C.c_int32]),
     "needle_cuda_sched_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64), C.POINTER(C.c_int64),
                                            C.POINTER(C.c_int32), C.c_void_p]),
+    "needle_cuda_sched_ids": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "needle_cuda_sched_slot": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                         C.POINTER(C.c_int32)]),
     "needle_cuda_kernel_launches": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64)]),
     "needle_cuda_profile": (C.c_int, [C.c_void_p, C.c_int32]),
     "needle_cuda_profile_read": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_char_p),
