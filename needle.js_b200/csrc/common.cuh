@@ -161,4 +161,16 @@ __device__ __forceinline__ double int_to_double_exact(int v) {
 // v rounded to binary32 (ties to even) and widened back: the value of (double)f32(v).
 __device__ __forceinline__ double round32_cvt(double v) { return (double)__double2float_rn(v); }
 
+// The same value without the conversion unit (which issues a quarter as many operations per clock
+// as the FP64 add pipe).  With 2^e <= |v| < 2^(e+1) and e clamped to >= -126 (the binary32
+// subnormal spacing below), c = 1.5 * 2^(e+29) is an even number of binary32 ulps of v and one
+// binary64 ulp of v + c is one binary32 ulp of v, so v + c rounds v to binary32 precision with
+// ties to even and subtracting c is exact.  Requires |v| < 2^127 (no binary32 overflow).
+__device__ __forceinline__ double round32_add(double v) {
+  const int hi = __double2hiint(v);
+  const int ch = max(hi & 0x7ff00000, 897 << 20) + ((29 << 20) | 0x00080000);
+  const double c = __hiloint2double(ch, 0);
+  return (v + c) - c;
+}
+
 }  // namespace needle

@@ -334,10 +334,12 @@ struct needle_ctx {
   cudaStream_t stream = nullptr;
   cudaStream_t side = nullptr;             // routing (Sinkhorn) overlapped with attention
   cudaEvent_t fork_ev[2] = {nullptr, nullptr}, join_ev[2] = {nullptr, nullptr};
-  // Second micro-batch of the device-scheduled step (its own main and routing streams).
-  cudaStream_t stream2 = nullptr, side2 = nullptr;
-  cudaEvent_t fork2_ev[2] = {nullptr, nullptr}, join2_ev[2] = {nullptr, nullptr};
-  cudaEvent_t split_ev = nullptr, merge_ev = nullptr;
+  // Micro-batches 1.. of the device-scheduled step (each with its own main and routing streams;
+  // micro-batch 0 runs on stream / side).
+  cudaStream_t mb_main[kMaxMicro] = {}, mb_side[kMaxMicro] = {};
+  cudaEvent_t mb_fork[kMaxMicro][2] = {}, mb_join[kMaxMicro][2] = {}, mb_done[kMaxMicro] = {};
+  cudaEvent_t split_ev = nullptr;
+  int micro = 4;  // micro-batches of a device-scheduled step
   // The device-scheduled step captured as a CUDA graph after one eager step.
   cudaGraphExec_t sched_graph = nullptr;
   int64_t graph_launches = 0;
@@ -676,7 +678,7 @@ void build_state(needle_ctx& C) {
   st.lanes = C.dalloc<float>(B * kLaneWidth);
   C.d_engram_in = C.dalloc<uint32_t>(B * 2 * kMaxTables);
   st.engram_in = C.d_engram_in;
-  C.d_counts = C.dalloc<int32_t>(8);
+  C.d_counts = C.dalloc<int32_t>(2 + 2 * kMaxMicro);
   C.d_confidence = C.dalloc<double>(1);
   st.n_items = C.d_counts;
   st.n_select = C.d_counts + 1;
@@ -842,30 +844,39 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
 }
 
 Lane lane_a(needle_ctx& C) { return Lane{C.stream, C.side, C.fork_ev, C.join_ev}; }
-Lane lane_b(needle_ctx& C) { return Lane{C.stream2, C.side2, C.fork2_ev, C.join2_ev}; }
+Lane lane_k(needle_ctx& C, int k) {
+  return k == 0 ? lane_a(C) : Lane{C.mb_main[k], C.mb_side[k], C.mb_fork[k], C.mb_join[k]};
+}
 
-// One device-scheduled step: admission and item list on the device, then the busy slots as two
-// micro-batches on two stream pairs so the latency-bound k_layer of one overlaps the GEMVs and
-// attention of the other (one batch when profiling, so per-kernel times stay unperturbed).
+// One device-scheduled step: admission and item list on the device, then the busy slots as
+// `micro` micro-batches on their own stream pairs, so the latency-bound kernels of one (k_layer's
+// sequential sums, attention's softmax and value chains) overlap the GEMVs and attention of the
+// others (one batch when profiling, so per-kernel times stay unperturbed).
 void enqueue_sched_step(needle_ctx& C) {
   const int S = C.sched.n_slots;
-  const bool split = S >= 64 && !C.profiling;
-  const int hA = split ? (S + 1) / 2 : S;
+  const int M = C.profiling ? 1 : std::max(1, std::min(C.micro, S / 32));
+  const int h = (S + M - 1) / M;
   C.timed(P_SCHED, [&] {
     cudaError_t e = launch_sched_admit(C.sv, C.sched, C.mv.kv_window, C.stream);
     if (e != cudaSuccess) return e;
-    return launch_sched(C.sv, C.stv, C.sched, C.d_counts, hA, C.stream);
+    return launch_sched(C.sv, C.stv, C.sched, C.d_counts, h, M, C.stream);
   });
-  if (!split) {
+  if (M == 1) {
     enqueue_step(C, half_view(C, 0, C.d_counts, C.d_counts + 1), S, true, &C.sched, lane_a(C));
     return;
   }
   cuda_check(cudaEventRecord(C.split_ev, C.stream), "split");
-  cuda_check(cudaStreamWaitEvent(C.stream2, C.split_ev, 0), "split");
-  enqueue_step(C, half_view(C, 0, C.d_counts + 2, C.d_counts + 3), hA, true, &C.sched, lane_a(C));
-  enqueue_step(C, half_view(C, hA, C.d_counts + 4, C.d_counts + 5), S - hA, true, &C.sched, lane_b(C));
-  cuda_check(cudaEventRecord(C.merge_ev, C.stream2), "merge");
-  cuda_check(cudaStreamWaitEvent(C.stream, C.merge_ev, 0), "merge");
+  for (int k = 1; k < M; k++) cuda_check(cudaStreamWaitEvent(C.mb_main[k], C.split_ev, 0), "split");
+  for (int k = 0; k < M; k++) {
+    const int off = k * h, n = std::min(h, S - off);
+    if (n <= 0) continue;
+    enqueue_step(C, half_view(C, off, C.d_counts + 2 + 2 * k, C.d_counts + 3 + 2 * k), n, true, &C.sched,
+                 lane_k(C, k));
+  }
+  for (int k = 1; k < M; k++) {
+    cuda_check(cudaEventRecord(C.mb_done[k], C.mb_main[k]), "merge");
+    cuda_check(cudaStreamWaitEvent(C.stream, C.mb_done[k], 0), "merge");
+  }
 }
 
 // The context of every call except needle_cuda_step_end and needle_cuda_close: none may run while a
@@ -906,14 +917,16 @@ void destroy(needle_ctx* C) {
     if (C->join_ev[k]) cudaEventDestroy(C->join_ev[k]);
   }
   if (C->sched_graph) cudaGraphExecDestroy(C->sched_graph);
-  for (int k = 0; k < 2; k++) {
-    if (C->fork2_ev[k]) cudaEventDestroy(C->fork2_ev[k]);
-    if (C->join2_ev[k]) cudaEventDestroy(C->join2_ev[k]);
-  }
   if (C->split_ev) cudaEventDestroy(C->split_ev);
-  if (C->merge_ev) cudaEventDestroy(C->merge_ev);
-  if (C->side2) cudaStreamDestroy(C->side2);
-  if (C->stream2) cudaStreamDestroy(C->stream2);
+  for (int k = 1; k < kMaxMicro; k++) {
+    for (int j = 0; j < 2; j++) {
+      if (C->mb_fork[k][j]) cudaEventDestroy(C->mb_fork[k][j]);
+      if (C->mb_join[k][j]) cudaEventDestroy(C->mb_join[k][j]);
+    }
+    if (C->mb_done[k]) cudaEventDestroy(C->mb_done[k]);
+    if (C->mb_side[k]) cudaStreamDestroy(C->mb_side[k]);
+    if (C->mb_main[k]) cudaStreamDestroy(C->mb_main[k]);
+  }
   if (C->side) cudaStreamDestroy(C->side);
   if (C->stream) cudaStreamDestroy(C->stream);
   delete C;
@@ -1177,16 +1190,21 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
             "max_len exceeds the model's maximum sequence length");
     cuda_check(cudaStreamCreateWithFlags(&C->stream, cudaStreamNonBlocking), "cudaStreamCreate");
     cuda_check(cudaStreamCreateWithFlags(&C->side, cudaStreamNonBlocking), "cudaStreamCreate");
-    cuda_check(cudaStreamCreateWithFlags(&C->stream2, cudaStreamNonBlocking), "cudaStreamCreate");
-    cuda_check(cudaStreamCreateWithFlags(&C->side2, cudaStreamNonBlocking), "cudaStreamCreate");
     for (int k = 0; k < 2; k++) {
       cuda_check(cudaEventCreateWithFlags(&C->fork_ev[k], cudaEventDisableTiming), "cudaEventCreate");
       cuda_check(cudaEventCreateWithFlags(&C->join_ev[k], cudaEventDisableTiming), "cudaEventCreate");
-      cuda_check(cudaEventCreateWithFlags(&C->fork2_ev[k], cudaEventDisableTiming), "cudaEventCreate");
-      cuda_check(cudaEventCreateWithFlags(&C->join2_ev[k], cudaEventDisableTiming), "cudaEventCreate");
+    }
+    for (int k = 1; k < kMaxMicro; k++) {
+      cuda_check(cudaStreamCreateWithFlags(&C->mb_main[k], cudaStreamNonBlocking), "cudaStreamCreate");
+      cuda_check(cudaStreamCreateWithFlags(&C->mb_side[k], cudaStreamNonBlocking), "cudaStreamCreate");
+      for (int j = 0; j < 2; j++) {
+        cuda_check(cudaEventCreateWithFlags(&C->mb_fork[k][j], cudaEventDisableTiming), "cudaEventCreate");
+        cuda_check(cudaEventCreateWithFlags(&C->mb_join[k][j], cudaEventDisableTiming), "cudaEventCreate");
+      }
+      cuda_check(cudaEventCreateWithFlags(&C->mb_done[k], cudaEventDisableTiming), "cudaEventCreate");
     }
     cuda_check(cudaEventCreateWithFlags(&C->split_ev, cudaEventDisableTiming), "cudaEventCreate");
-    cuda_check(cudaEventCreateWithFlags(&C->merge_ev, cudaEventDisableTiming), "cudaEventCreate");
+    if (const char* mb = getenv("NEEDLE_MICRO")) C->micro = std::max(1, std::min(kMaxMicro, atoi(mb)));
     build_model(*C);
     build_state(*C);
     cuda_check(cudaDeviceSynchronize(), "upload");

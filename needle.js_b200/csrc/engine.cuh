@@ -9,6 +9,7 @@
 namespace needle {
 
 constexpr int kMaxProbes = 32;  // confidence probes an archive may carry
+constexpr int kMaxMicro = 8;    // micro-batches of a device-scheduled step
 
 // A Cactus-Quant matrix in device memory (CqMatrix, packages/needle.js/src/model/cact.ts:61-75).
 struct CqMat {
@@ -148,10 +149,10 @@ cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepV
                              int n_host, cudaStream_t s, int part = 0);
 cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
                           const SchedView* sched, cudaStream_t s);
-// Device scheduler: builds the step's item list and the counts [all, selecting, half A (all,
-// selecting), half B (all, selecting)] with half A = items [0, half).
-cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts, int half,
-                         cudaStream_t s);
+// Device scheduler: builds the step's item list and the counts [all, selecting, then (all,
+// selecting) of each of `parts` micro-batches], micro-batch k being items [k * part, (k + 1) * part).
+cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts, int part,
+                         int parts, cudaStream_t s);
 cudaError_t launch_sched_admit(const SlotView& sv, const SchedView& q, int window, cudaStream_t s);
 cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
                                  const float* vs, const int32_t* counts, int32_t batch,

@@ -548,6 +548,7 @@ struct CacheRef {
 // area (kAttnTile value rows + scales + weights); slot_of(t) maps the t-th visible position to its
 // cache row.  Leaves the gated outputs in out[2][64] (smem).
 constexpr int kAttnTile = 256;
+constexpr int kAttnSc = 1, kAttnMix = 1, kAttnMc = 0;  // attend_pair variant of the engine
 constexpr size_t kAttnTileBytes = kAttnTile * (kHeadDim + 2 * 8);  // codes, 2 x weight*scale
 
 // softmaxInPlace (math.ts:46-60) of both heads' binary32 scores e[2][count]: max (order-free),
@@ -583,77 +584,142 @@ __device__ __forceinline__ void softmax_pair(double* e, int count, double* red) 
   }
 }
 
-template <class SlotOf>
-__device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const double* q, double* e,
+// Widened int8 code: through the FP64 add pipe (Mc 0, int_to_double_exact) or the conversion unit.
+template <int Mc>
+__device__ __forceinline__ double code_d(int c) {
+  if constexpr (Mc == 0) return int_to_double_exact(c);
+  else return (double)c;
+}
+// round32 of one value-mix step: on the FP64 add pipe (R 0) or through the conversion unit (R 1).
+template <int R>
+__device__ __forceinline__ double round32_r(double v) {
+  if constexpr (R == 0) return round32_add(v);
+  else return round32_cvt(v);
+}
+
+// 16-byte asynchronous global -> shared copy (L2 only); completes at cp_async_wait.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Attention variants (all bit-identical): Sc = key-code widening (0 add pipe, 1 conversion unit);
+// Mix = value-mix layout (0: one chain per thread, conversion rounding; 1: threads 0-63 run both
+// heads' chains of one element, head 0 rounding on the add pipe and head 1 by conversion; 2: both on
+// the add pipe; 3: both by conversion); Mc = value-code widening.
+template <int Sc, int Mix, int Mc, class SlotOf>
+__device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const double* q2, double* e,
                             unsigned char* tile, const float* gate, float* out, double* red) {
   const int tid = threadIdx.x;
-  // scores[t] = f32((sum_i q_i * code_i * keyScale) / 8)  (runtime.ts:736-757)
-  for (int t = tid; t < count; t += kAttnThreads) {
-    const int sl = slot_of(t);
-    const double ks = (double)C.ks[sl];
-    const uint4* kr = reinterpret_cast<const uint4*>(C.kc + (int64_t)sl * kHeadDim);
-    uint4 u[4];
-#pragma unroll
-    for (int w4 = 0; w4 < 4; w4++) u[w4] = __ldg(kr + w4);
-    // q * code * keyScale: q * code is exact in binary64 and so is code * keyScale, so
-    // (q * code) * keyScale and q * (code * keyScale) are both the one rounding of the same real
-    // product; the second form shares code * keyScale between the two heads.
-    double d0 = 0.0, d1 = 0.0;
+  int8_t* vt = reinterpret_cast<int8_t*>(tile);                                 // [tile][64] value codes
+  double2* wvt = reinterpret_cast<double2*>(tile + kAttnTile * kHeadDim);       // [tile] (head 0, head 1)
+  // The first tile of value rows is fetched asynchronously while the scores and the softmax run.
+  const int n0 = min(kAttnTile, count);
+  for (int k = tid; k < n0 * 4; k += kAttnThreads)
+    cp_async16(vt + (k >> 2) * kHeadDim + (k & 3) * 16, C.vc + (int64_t)slot_of(k >> 2) * kHeadDim + (k & 3) * 16);
+  // scores[t] = f32((sum_i q_i * code_i * keyScale) / 8)  (runtime.ts:736-757), two positions per
+  // thread at a time (four independent sums).  q * code * keyScale: q * code is exact in binary64 and
+  // so is code * keyScale, so (q * code) * keyScale and q * (code * keyScale) are both the one rounding
+  // of the same real product; the second form shares code * keyScale between the two heads.
+  const double inverse_root = 1.0 / sqrt((double)kHeadDim);
+  for (int t0 = tid; t0 < count; t0 += 2 * kAttnThreads) {
+    const int t1 = t0 + kAttnThreads;
+    const bool two = t1 < count;
+    const int s0 = slot_of(t0), s1 = two ? slot_of(t1) : s0;
+    const double ks0 = (double)C.ks[s0], ks1 = (double)C.ks[s1];
+    const uint4* k0 = reinterpret_cast<const uint4*>(C.kc + (int64_t)s0 * kHeadDim);
+    const uint4* k1 = reinterpret_cast<const uint4*>(C.kc + (int64_t)s1 * kHeadDim);
+    uint4 u0[4], u1[4];
 #pragma unroll
     for (int w4 = 0; w4 < 4; w4++) {
-      const uint32_t words[4] = {u[w4].x, u[w4].y, u[w4].z, u[w4].w};
+      u0[w4] = __ldg(k0 + w4);
+      u1[w4] = __ldg(k1 + w4);
+    }
+    double a0 = 0.0, a1 = 0.0, b0 = 0.0, b1 = 0.0;
+#pragma unroll
+    for (int w4 = 0; w4 < 4; w4++) {
+      const uint32_t wa[4] = {u0[w4].x, u0[w4].y, u0[w4].z, u0[w4].w};
+      const uint32_t wb[4] = {u1[w4].x, u1[w4].y, u1[w4].z, u1[w4].w};
 #pragma unroll
       for (int k = 0; k < 16; k++) {
         const int i = w4 * 16 + k;
-        const double cks = int_to_double_exact((int)(int8_t)((words[k >> 2] >> ((k & 3) * 8)) & 0xff)) * ks;
-        d0 = d0 + q[i] * cks;
-        d1 = d1 + q[kHeadDim + i] * cks;
+        const double2 qq = reinterpret_cast<const double2*>(q2)[i];
+        const double ca = code_d<Sc>((int)(int8_t)((wa[k >> 2] >> ((k & 3) * 8)) & 0xff)) * ks0;
+        const double cb = code_d<Sc>((int)(int8_t)((wb[k >> 2] >> ((k & 3) * 8)) & 0xff)) * ks1;
+        a0 = a0 + qq.x * ca;
+        a1 = a1 + qq.y * ca;
+        b0 = b0 + qq.x * cb;
+        b1 = b1 + qq.y * cb;
       }
     }
-    const double inverse_root = 1.0 / sqrt((double)kHeadDim);
-    e[t] = round32_cvt(d0 * inverse_root);
-    e[count + t] = round32_cvt(d1 * inverse_root);
+    e[t0] = round32_cvt(a0 * inverse_root);
+    e[count + t0] = round32_cvt(a1 * inverse_root);
+    if (two) {
+      e[t1] = round32_cvt(b0 * inverse_root);
+      e[count + t1] = round32_cvt(b1 * inverse_root);
+    }
   }
   __syncthreads();
   softmax_pair(e, count, red);
   // output[i] += weight * code * valueScale, sequentially in t with binary32 storage (760-782).
-  // Value rows, scales and weights are staged tile by tile in shared memory so the sequential
-  // chain reads only shared memory.
   // weight * code * valueScale == code * (weight * valueScale): weight (binary32) * valueScale
   // (binary32) is exact in binary64, and weight * code is exact too, so both orders are one
   // rounding of the same real product.
-  int8_t* vt = reinterpret_cast<int8_t*>(tile);                                   // [tile][64]
-  double* wvt = reinterpret_cast<double*>(tile + kAttnTile * kHeadDim);           // [2][tile]
-  const int hh = tid >> 6, i = tid & 63;
-  double o = 0.0;  // a binary32 value, kept widened (round32 after every step)
+  const int i = tid & 63;
+  double o0 = 0.0, o1 = 0.0;  // binary32 values, kept widened (rounded after every step)
   for (int t0 = 0; t0 < count; t0 += kAttnTile) {
     const int n = min(kAttnTile, count - t0);
-    for (int k = tid; k < n * 4; k += kAttnThreads) {
-      const int t = k >> 2, part = k & 3;
-      const int sl = slot_of(t0 + t);
-      reinterpret_cast<uint4*>(vt + t * kHeadDim)[part] =
-          __ldg(reinterpret_cast<const uint4*>(C.vc + (int64_t)sl * kHeadDim) + part);
+    if (t0 > 0) {
+      for (int k = tid; k < n * 4; k += kAttnThreads)
+        cp_async16(vt + (k >> 2) * kHeadDim + (k & 3) * 16,
+                   C.vc + (int64_t)slot_of(t0 + (k >> 2)) * kHeadDim + (k & 3) * 16);
     }
-    for (int k = tid; k < 2 * n; k += kAttnThreads) {
-      const int h2 = k / n, t = k - h2 * n;
-      const double w = round32_cvt(round32_cvt(e[h2 * count + t0 + t]) * red[4 + h2]);
-      wvt[h2 * kAttnTile + t] = w * (double)C.vs[slot_of(t0 + t)];
+    for (int t = tid; t < n; t += kAttnThreads) {
+      const double vs = (double)C.vs[slot_of(t0 + t)];
+      const double w0 = round32_cvt(round32_cvt(e[t0 + t]) * red[4]);
+      const double w1 = round32_cvt(round32_cvt(e[count + t0 + t]) * red[5]);
+      wvt[t] = make_double2(w0 * vs, w1 * vs);
     }
+    cp_async_wait_all();
     __syncthreads();
-    const double* wv = wvt + hh * kAttnTile;
+    if constexpr (Mix == 0) {
+      const int hh = tid >> 6;
+      double o = hh ? o1 : o0;
 #pragma unroll 8
-    for (int t = 0; t < n; t++) o = round32_cvt(o + int_to_double_exact(vt[t * kHeadDim + i]) * wv[t]);
+      for (int t = 0; t < n; t++) {
+        const double2 w = wvt[t];
+        o = round32_cvt(o + code_d<Mc>(vt[t * kHeadDim + i]) * (hh ? w.y : w.x));
+      }
+      if (hh) o1 = o; else o0 = o;
+    } else if (tid < 64) {
+      constexpr int R0 = Mix == 3 ? 1 : 0, R1 = Mix == 2 ? 0 : 1;
+#pragma unroll 8
+      for (int t = 0; t < n; t++) {
+        const double c = code_d<Mc>(vt[t * kHeadDim + i]);
+        const double2 w = wvt[t];
+        o0 = round32_r<R0>(o0 + c * w.x);
+        o1 = round32_r<R1>(o1 + c * w.y);
+      }
+    }
     __syncthreads();
   }
   // attentionOutput * sigmoid(gate) (runtime.ts:503-504)
-  out[hh * kHeadDim + i] = gate ? f32(o * sigmoid_d((double)gate[hh * kHeadDim + i])) : (float)o;
+  if constexpr (Mix == 0) {
+    const int hh = tid >> 6;
+    const double o = hh ? o1 : o0;
+    out[hh * kHeadDim + i] = gate ? f32(o * sigmoid_d((double)gate[hh * kHeadDim + i])) : (float)o;
+  } else if (tid < 64) {
+    out[i] = gate ? f32(o0 * sigmoid_d((double)gate[i])) : (float)o0;
+    out[kHeadDim + i] = gate ? f32(o1 * sigmoid_d((double)gate[kHeadDim + i])) : (float)o1;
+  }
   __syncthreads();
 }
 
 // attend_pair over the float32 cache (runtime.ts:744-748, 768-772): keys and values are read as
 // stored, and query * key and weight * value are exact binary64 products, so each accumulation is
 // one fused multiply-add.  The weights are formed once per position in e (binary32 values), and
-// the value chain reads the cache directly (the two heads share each row).
+// the value chain reads the cache directly (the two heads share each row).  q is [i][head].
 template <class SlotOf>
 __device__ void attend_pair_f32(const float* kf, const float* vf, int count, SlotOf slot_of, const double* q,
                                 double* e, const float* gate, float* out, double* red) {
@@ -668,8 +734,8 @@ __device__ void attend_pair_f32(const float* kf, const float* vf, int count, Slo
       const float kk[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
       for (int c = 0; c < 4; c++) {
-        d0 = fma(q[4 * w4 + c], (double)kk[c], d0);
-        d1 = fma(q[kHeadDim + 4 * w4 + c], (double)kk[c], d1);
+        d0 = fma(q[(4 * w4 + c) * 2], (double)kk[c], d0);
+        d1 = fma(q[(4 * w4 + c) * 2 + 1], (double)kk[c], d1);
       }
     }
     e[t] = round32_cvt(d0 * inverse_root);
@@ -690,6 +756,7 @@ __device__ void attend_pair_f32(const float* kf, const float* vf, int count, Slo
 
 // part 0: append this item's K/V, then attend; part 1: append only; part 2: attend only (a
 // chunk's items attend after all of them appended).
+template <int Sc, int Mix, int Mc>
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, const SlotView sv,
                                                            const StepView st, int l, int part) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -787,8 +854,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
   unsigned char* tile = smem_raw;
   double* e = reinterpret_cast<double*>(smem_raw + kAttnTileBytes);
   auto slot_of = [&](int t) { return kv_slot(t < prefix ? t : recent_low + (t - prefix)); };
-  __shared__ double qd[2 * kHeadDim];
-  qd[tid] = (double)qv[tid];
+  __shared__ __align__(16) double qd[2 * kHeadDim];  // [i][head]
+  qd[(tid & 63) * 2 + (tid >> 6)] = (double)qv[tid];
   __syncthreads();
   if (sv.kv_f32) {
     attend_pair_f32(sv.kf + head_base * kHeadDim, sv.vf + head_base * kHeadDim, count, slot_of, qd, e, gt, outv,
@@ -796,7 +863,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
   } else {
     CacheRef C{sv.kcodes + head_base * kHeadDim, sv.vcodes + head_base * kHeadDim, sv.kscale + head_base,
                sv.vscale + head_base};
-    attend_pair(C, count, slot_of, qd, e, tile, gt, outv, red);
+    attend_pair<Sc, Mix, Mc>(C, count, slot_of, qd, e, tile, gt, outv, red);
   }
   // prepareCqActivation of the output projection: heads 2h, 2h+1 are exactly input group h.
   fwht_smem(outv, kGroup, 1);
@@ -811,12 +878,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention_dev(const float* __r
                                                                const int32_t* counts, int32_t capacity,
                                                                float* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ double qd[2 * kHeadDim];
+  __shared__ __align__(16) double qd[2 * kHeadDim];  // [i][head]
   __shared__ float outv[2 * kHeadDim];
   __shared__ double red[8];
   const int b = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x;
-  qd[tid] = (double)q[(int64_t)b * kHeads * kHeadDim + 2 * h * kHeadDim + tid];
+  qd[(tid & 63) * 2 + (tid >> 6)] = (double)q[(int64_t)b * kHeads * kHeadDim + 2 * h * kHeadDim + tid];
   __syncthreads();
   const int count = min(max(counts[b], 0), capacity);
   const int64_t head_base = ((int64_t)b * kKvHeads + h) * capacity;
@@ -824,7 +891,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention_dev(const float* __r
   unsigned char* tile = smem_raw;
   double* e = reinterpret_cast<double*>(smem_raw + kAttnTileBytes);
   auto slot_of = [](int t) { return t; };
-  attend_pair(C, count, slot_of, qd, e, tile, nullptr, outv, red);
+  attend_pair<kAttnSc, kAttnMix, kAttnMc>(C, count, slot_of, qd, e, tile, nullptr, outv, red);
   out[(int64_t)b * kHeads * kHeadDim + 2 * h * kHeadDim + tid] = outv[tid];
 }
 
@@ -1075,10 +1142,10 @@ __global__ void k_sched_admit(const SlotView sv, const SchedView q, int window) 
 
 // Builds the step's item list from the busy slots: selecting items (the last prompt token and
 // every decode step) first, then prefill items.  One CTA.
-// counts: [0] items, [1] selecting items, [2]/[3] the same for items [0, half), [4]/[5] for
-// items [half, n) -- the two micro-batches of the step.
+// counts: [0] items, [1] selecting items, then for micro-batch k (items [k * part, (k + 1) *
+// part)) its items at [2 + 2k] and its selecting items (a prefix of its items) at [3 + 2k].
 __global__ void __launch_bounds__(1024) k_sched(const SlotView sv, const StepView st, const SchedView q,
-                                              int32_t* counts, int half) {
+                                              int32_t* counts, int part, int parts) {
   __shared__ int s_sel;
   const int tid = threadIdx.x;
   if (tid == 0) s_sel = 0;
@@ -1117,16 +1184,25 @@ __global__ void __launch_bounds__(1024) k_sched(const SlotView sv, const StepVie
     const int n = c_sel + c_pre;
     counts[0] = n;
     counts[1] = c_sel;
-    counts[2] = min(n, half);
-    counts[3] = min(c_sel, half);
-    counts[4] = max(0, n - half);
-    counts[5] = max(0, c_sel - half);
+    for (int k = 0; k < parts; k++) {
+      counts[2 + 2 * k] = min(max(n - k * part, 0), part);
+      counts[3 + 2 * k] = min(max(c_sel - k * part, 0), part);
+    }
   }
 }
 
 }  // namespace
 
 // ------------------------------------------------------------------ launchers
+
+// Variant of the engine's attention kernel (an experiment switch: NEEDLE_ATTN_VARIANT, default 7).
+static int attention_variant() {
+  static const int v = [] {
+    const char* s = getenv("NEEDLE_ATTN_VARIANT");
+    return s ? atoi(s) : 7;
+  }();
+  return v;
+}
 
 // The dynamic shared-memory limit is an attribute of the function on the device, shared by every
 // context in the process, so it is raised to the device's opt-in maximum rather than to one
@@ -1166,7 +1242,17 @@ cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepV
                              int n_host, cudaStream_t s, int part) {
   if (n_host <= 0) return cudaSuccess;
   const size_t smem = attention_smem_bytes(sv.capacity, true);
-  k_attention<<<dim3(n_host, kKvHeads), kAttnThreads, smem, s>>>(m, sv, st, layer, part);
+  const dim3 grid(n_host, kKvHeads);
+  switch (attention_variant()) {
+    case 0: k_attention<0, 0, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
+    case 1: k_attention<0, 1, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
+    case 2: k_attention<0, 2, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
+    case 3: k_attention<1, 1, 1><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
+    case 4: k_attention<1, 2, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
+    case 5: k_attention<1, 2, 1><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
+    case 6: k_attention<0, 3, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
+    default: k_attention<1, 1, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
+  }
   return cudaGetLastError();
 }
 
@@ -1192,8 +1278,13 @@ cudaError_t configure_step_kernels(int32_t capacity) {
     return cudaErrorInvalidValue;
   cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(k_layer));
   if (e != cudaSuccess) return e;
-  e = raise_smem_limit(reinterpret_cast<const void*>(k_attention));
-  if (e != cudaSuccess) return e;
+  for (const void* fn : {reinterpret_cast<const void*>(k_attention<0, 0, 0>), reinterpret_cast<const void*>(k_attention<0, 1, 0>),
+                         reinterpret_cast<const void*>(k_attention<0, 2, 0>), reinterpret_cast<const void*>(k_attention<1, 1, 1>),
+                         reinterpret_cast<const void*>(k_attention<1, 2, 0>), reinterpret_cast<const void*>(k_attention<1, 2, 1>),
+                         reinterpret_cast<const void*>(k_attention<0, 3, 0>), reinterpret_cast<const void*>(k_attention<1, 1, 0>)}) {
+    e = raise_smem_limit(fn);
+    if (e != cudaSuccess) return e;
+  }
   return raise_smem_limit(reinterpret_cast<const void*>(k_attention_dev));
 }
 
@@ -1230,9 +1321,10 @@ cudaError_t launch_sched_admit(const SlotView& sv, const SchedView& q, int windo
   return cudaGetLastError();
 }
 
-cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts, int half,
-                         cudaStream_t s) {
-  k_sched<<<1, 1024, 0, s>>>(sv, st, q, counts, half);
+cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts, int part,
+                         int parts, cudaStream_t s) {
+  if (parts < 1 || parts > kMaxMicro) return cudaErrorInvalidValue;
+  k_sched<<<1, 1024, 0, s>>>(sv, st, q, counts, part, parts);
   return cudaGetLastError();
 }
 
