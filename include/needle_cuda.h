@@ -281,6 +281,27 @@ int needle_cuda_attention_dev_fast(const float* q, const int8_t* key_codes, cons
                                    const int32_t* counts, int32_t batch, int32_t capacity,
                                    float* out, void* stream);
 
+/* ---- Bounded device waits ----
+ * The kernels that wait on asynchronous copies or barriers -- the fast attention, the table matvec and
+ * the tensor-core matvec -- give up after 2 s instead of spinning forever.  The outputs of that call
+ * are then NaN, and the kernel records its kind in the device's wait-status word (pinned host memory:
+ * readable without synchronising).  The next needle_cuda_cq_matvec_dev_fast or
+ * needle_cuda_attention_dev_fast call on that device returns BACKEND_UNAVAILABLE, naming the kernels,
+ * and clears the word.  (The reference's GPU path is WebGPU, whose device loss the browser reports;
+ * these statuses play that part.) */
+#define NEEDLE_WAIT_ATTENTION 1u   /* k_attention_fast_mma */
+#define NEEDLE_WAIT_TABLE_GEMV 2u  /* k_cq_gemv_table */
+#define NEEDLE_WAIT_TENSOR_GEMM 4u /* k_cq_gemm_tc */
+#define NEEDLE_WAIT_SELFTEST 8u    /* needle_cuda_wait_selftest */
+
+/* The wait-status bits of `device` (NEEDLE_WAIT_*) through *kinds; clear = 1 resets them. */
+int needle_cuda_wait_status(int32_t device, uint32_t* kinds, int32_t clear);
+
+/* Diagnostic of the path above: one GPU thread of the current device waits, up to limit_ns
+ * (at most 1 s), on a device flag that nothing sets, gives up, records NEEDLE_WAIT_SELFTEST and
+ * returns -- what every waiting kernel does when its wait runs out, without a stalled copy. */
+int needle_cuda_wait_selftest(uint64_t limit_ns, void* stream);
+
 /* ---- Benchmark / device-resident scheduling ---- */
 
 /* Returns the context's CUDA stream (a cudaStream_t) so callers can time on it. */

@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(kMmaThreads) k_attention_fast_mma(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const float* __restrict__ q,
     const float* __restrict__ ks, const float* __restrict__ vs, const int32_t* __restrict__ counts,
     int32_t capacity, int32_t splits, int32_t n_items, Partial* __restrict__ partials, int32_t* __restrict__ status,
-    int32_t* __restrict__ work, int32_t* __restrict__ done) {
+    int32_t* __restrict__ work, int32_t* __restrict__ done, uint32_t* __restrict__ wait_words) {
   extern __shared__ unsigned char smem_raw[];
   MmaStage* stage = reinterpret_cast<MmaStage*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[kMmaStages], empty[kMmaStages];
@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(kMmaThreads) k_attention_fast_mma(
       auto next_stage = [&](int& sidx) -> bool {
         sidx = seq % kMmaStages;
         if (seq >= kMmaStages && !mbar_wait(&empty[sidx], ((seq / kMmaStages) - 1) & 1)) {
-          atomicExch(status, 1);
+          { atomicExch(status, 1); report_wait_timeout(wait_words, kWaitAttention); }
           return false;
         }
         return true;
@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(kMmaThreads) k_attention_fast_mma(
       // The CTA must not retire with copies still landing in its shared memory: wait (bounded)
       // for the last tile issued into each stage.
       for (int i = max(0, seq - kMmaStages); i < seq; i++)
-        if (!mbar_wait(&full[i % kMmaStages], (i / kMmaStages) & 1)) atomicExch(status, 1);
+        if (!mbar_wait(&full[i % kMmaStages], (i / kMmaStages) & 1)) { atomicExch(status, 1); report_wait_timeout(wait_words, kWaitAttention); }
       // The last CTA to stop claiming work resets the counters for the next call (no CTA claims
       // any more once its claim failed, so nothing races with the reset).
       __threadfence();
@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(kMmaThreads) k_attention_fast_mma(
     // Every consumer warp waits on the same stages in the same order, so a bounded wait that runs out
     // runs out for all of them before any item barrier below.
     if (!mbar_wait(&full[sidx], (seq / kMmaStages) & 1)) {
-      atomicExch(status, 1);
+      { atomicExch(status, 1); report_wait_timeout(wait_words, kWaitAttention); }
       break;
     }
     const MmaStage& st = stage[sidx];
@@ -715,7 +715,8 @@ cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float*
     const int n_items = batch * kKvHeads * splits;
     const int grid = std::max(1, std::min(n_items, sms * per_sm[device & 63]));
     k_attention_fast_mma<<<grid, kMmaThreads, smem, s>>>(kmap, vmap, q, ks, vs, counts, capacity, splits, n_items,
-                                                         parts, status, status + 1, status + 2);
+                                                         parts, status, status + 1, status + 2,
+                                                         wait_status_words(device));
   } else {
     k_attention_fast<<<dim3(batch, kKvHeads, splits), kFastThreads, 0, s>>>(q, kc, ks, vc, vs, counts, capacity,
                                                                            splits, parts);

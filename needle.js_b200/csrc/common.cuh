@@ -173,4 +173,18 @@ __device__ __forceinline__ double round32_add(double v) {
   return (v + c) - c;
 }
 
+// Bounded device waits that ran out.  Every kernel that waits on a copy or a barrier gives up
+// after a time limit; it then records its kind in the library's wait-status words of the device
+// (mapped pinned host memory, so the host reads them without synchronising) and its outputs of
+// that call are NaN.  The next operator call on the device reports BACKEND_UNAVAILABLE.
+enum WaitKind { kWaitAttention = 0, kWaitTableGemv = 1, kWaitTensorGemm = 2, kWaitSelftest = 3, kWaitKinds = 4 };
+
+__device__ __forceinline__ void report_wait_timeout(uint32_t* words, int kind) {
+  if (words) *reinterpret_cast<volatile uint32_t*>(words + kind) = 1u;
+}
+
+// The wait-status words of a device (kWaitKinds of them), allocated on first use; nullptr if the
+// pinned mapping cannot be made.
+uint32_t* wait_status_words(int device);
+
 }  // namespace needle

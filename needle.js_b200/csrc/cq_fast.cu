@@ -169,7 +169,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 template <int BITS>
 __global__ void __launch_bounds__(kTabThreads, 2) k_cq_gemv_table(
     const __grid_constant__ CUtensorMap wmap, int32_t rows, int32_t input_size, int32_t in_pad,
-    const float* __restrict__ x, int32_t x_stride, Codebook cb, float* __restrict__ partials) {
+    const float* __restrict__ x, int32_t x_stride, Codebook cb, float* __restrict__ partials,
+    uint32_t* __restrict__ wait_words) {
   using G = TabGeom<BITS>;
   constexpr int NCH = G::chunks;
   constexpr int kWarps = kTabThreads / 32;
@@ -310,6 +311,7 @@ __global__ void __launch_bounds__(kTabThreads, 2) k_cq_gemv_table(
     seg = seg_end;
   }
   if (failed && lane == 0) {
+    report_wait_timeout(wait_words, kWaitTableGemv);
     // Copies still landing in this warp's ring must finish before the CTA retires: wait (bounded)
     // for the blocks issued and not consumed.
     for (int n = uses; n < issued; n++) mbar_wait(&full[warp][n % kRing], (uint32_t)((n / kRing) & 1));
@@ -413,7 +415,8 @@ cudaError_t launch_table(const uint8_t* packed, const uint16_t* norms, int32_t r
     const float* xb = x + (int64_t)b0 * input_size;
     float* yb = y + (int64_t)b0 * rows;
     k_cq_gemv_table<BITS><<<dim3(grid, nb), kTabThreads, smem, s>>>(wmap, rows, input_size, in_pad, xb,
-                                                                     input_size, cb, partials);
+                                                                     input_size, cb, partials,
+                                                                     wait_status_words(device));
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     k_cq_fast_reduce<<<dim3((rows + kReduceRows - 1) / kReduceRows, nb), kReduceThreads, 0, s>>>(

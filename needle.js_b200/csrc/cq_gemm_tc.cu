@@ -194,7 +194,7 @@ template <int BITS>
 __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
     const uint8_t* __restrict__ packed, const uint16_t* __restrict__ norms, int32_t rows, int32_t groups,
     int32_t row_bytes, const uint8_t* __restrict__ act, int32_t N, int32_t nb, int32_t groups_per_split,
-    float* __restrict__ out, int32_t out_stride, int64_t split_stride, Codebook cb) {
+    float* __restrict__ out, int32_t out_stride, int64_t split_stride, Codebook cb, uint32_t* __restrict__ wait_words) {
   constexpr int kCodes = BITS == 4 ? 16 : 4;
   constexpr int kGroupWords = BITS == 4 ? 16 : 8;  // packed 32-bit words of one row's group
   constexpr int kPairsPerWord = BITS == 4 ? 4 : 8;  // column pairs (two codes) per packed word
@@ -421,6 +421,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
     const bool acc_ok = __all_sync(0xffffffffu, lane != 0 || bar_wait(&acc_full, 0));
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const bool bad = !acc_ok || *(volatile int*)&s_failed != 0;
+    if (bad && lane == 0) report_wait_timeout(wait_words, kWaitTensorGemm);
     float* o = out + (int64_t)split * split_stride;
     for (int c0 = team * 8; c0 < N; c0 += kTcTeams * 8) {
       uint32_t v[8], w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -513,8 +514,11 @@ cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int3
       e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return;
       float* o = p.used > 1 ? part : y + (int64_t)b0 * rows;
+      int dev = 0;
+      e = cudaGetDevice(&dev);
+      if (e != cudaSuccess) return;
       kernel<<<dim3(p.m_tiles, p.used), kTcThreads, smem, s>>>(packed, norms, rows, p.groups, row_bytes, act, N, nb,
-                                                              p.per, o, rows, split_stride, cb);
+                                                              p.per, o, rows, split_stride, cb, wait_status_words(dev));
       e = cudaGetLastError();
     };
     if (bits == 4) launch(k_cq_gemm_tc<4>);

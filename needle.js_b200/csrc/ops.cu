@@ -1,6 +1,7 @@
 // ops.cu -- stateless device-pointer operators of the C-ABI (isolated matvec and attention).
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -70,7 +71,94 @@ int op_fail(int code, const std::string& msg) {
   return code;
 }
 
+// Wait-status words of every device: one pinned, mapped host allocation (kWaitKinds words per
+// device), made on the first call that needs it.
+constexpr int kStatusDevices = 64;
+std::mutex g_status_mu;
+uint32_t* g_status_host = nullptr;
+bool g_status_failed = false;
+
+const char* kWaitKindNames[kWaitKinds] = {"fast attention", "table matvec", "tensor-core matvec", "wait self-test"};
+
+// Reports (and clears) the bounded waits of earlier calls on `device` that ran out.
+int check_wait_status(int device) {
+  uint32_t* w = wait_status_words(device);
+  if (!w) return NEEDLE_OK;
+  std::string names;
+  for (int k = 0; k < kWaitKinds; k++) {
+    volatile uint32_t* v = w + k;
+    if (*v) {
+      names += (names.empty() ? "" : ", ") + std::string(kWaitKindNames[k]);
+      *v = 0;
+    }
+  }
+  if (names.empty()) return NEEDLE_OK;
+  return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "a bounded device wait ran out on device " + std::to_string(device) +
+                                                 " (" + names + "); that call's outputs are NaN");
+}
+
+__device__ int g_never_set;  // nothing writes it: the self-test's wait always runs out
+
+__global__ void k_wait_selftest(uint64_t limit_ns, uint32_t* words) {
+  if (threadIdx.x != 0) return;
+  uint64_t start, now;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
+  for (;;) {
+    if (*reinterpret_cast<volatile int*>(&g_never_set) != 0) return;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (now - start > limit_ns) {
+      report_wait_timeout(words, kWaitSelftest);
+      return;
+    }
+    __nanosleep(1000);
+  }
+}
+
 }  // namespace
+
+uint32_t* needle::wait_status_words(int device) {
+  if (device < 0 || device >= kStatusDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  if (!g_status_host && !g_status_failed) {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, sizeof(uint32_t) * kWaitKinds * kStatusDevices, cudaHostAllocMapped | cudaHostAllocPortable) ==
+        cudaSuccess) {
+      std::memset(p, 0, sizeof(uint32_t) * kWaitKinds * kStatusDevices);
+      g_status_host = static_cast<uint32_t*>(p);
+    } else {
+      cudaGetLastError();
+      g_status_failed = true;
+    }
+  }
+  return g_status_host ? g_status_host + kWaitKinds * device : nullptr;
+}
+
+extern "C" int needle_cuda_wait_status(int32_t device, uint32_t* kinds, int32_t clear) {
+  if (!kinds) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+  uint32_t* w = wait_status_words(device);
+  if (!w) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "no wait-status words for device " + std::to_string(device));
+  uint32_t mask = 0;
+  for (int k = 0; k < kWaitKinds; k++) {
+    volatile uint32_t* v = w + k;
+    if (*v) mask |= 1u << k;
+    if (clear) *v = 0;
+  }
+  *kinds = mask;
+  return NEEDLE_OK;
+}
+
+extern "C" int needle_cuda_wait_selftest(uint64_t limit_ns, void* stream) {
+  if (limit_ns > 1000000000ull) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "self-test wait limit above 1 s");
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  uint32_t* w = wait_status_words(device);
+  if (!w) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "no wait-status words");
+  k_wait_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, w);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
+  return NEEDLE_OK;
+}
 
 extern "C" int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float* codebook, const float* x,
                                          int32_t batch, float* y, void* stream) {
@@ -229,6 +317,7 @@ extern "C" int needle_cuda_attention_dev_fast(const float* q, const int8_t* key_
     return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "key/value codes must be 16-byte aligned");
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
+  if (e == cudaSuccess && check_wait_status(device) != NEEDLE_OK) return NEEDLE_BACKEND_UNAVAILABLE;
   void* scratch = nullptr;
   if (e == cudaSuccess) e = attn_scratch_for(device, attention_fast_scratch_bytes(batch, capacity), &scratch);
   if (e == cudaSuccess)
@@ -255,6 +344,7 @@ extern "C" int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const f
   for (int i = 0; i < 28; i++) cb.v[i] = codebook[i];
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
+  if (e == cudaSuccess && check_wait_status(device) != NEEDLE_OK) return NEEDLE_BACKEND_UNAVAILABLE;
   if (cq_gemm_tc_supported(m->bits) && cq_gemm_tc_preferred(m->rows, m->input_size, batch)) {
     // a real dense contraction: tensor-core GEMM
     int sms = 0;

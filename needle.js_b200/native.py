@@ -21,6 +21,7 @@ TOKEN_PENDING = -1
 KV_INT8 = 0
 KV_FLOAT32 = 1
 NOALLOC_MAX_FLOATS = 1 << 20  # NEEDLE_NOALLOC_MAX_FLOATS
+WAIT_ATTENTION, WAIT_TABLE_GEMV, WAIT_TENSOR_GEMM, WAIT_SELFTEST = 1, 2, 4, 8  # NEEDLE_WAIT_*
 
 
 class NeedleError(RuntimeError):
@@ -99,6 +100,8 @@ EXPORTS = {
                                                                 C.c_void_p]),
     "needle_cuda_attention_dev_fast": (C.c_int, [C.c_void_p] * 6 + [C.c_int32, C.c_int32, C.c_void_p,
                                                                      C.c_void_p]),
+    "needle_cuda_wait_status": (C.c_int, [C.c_int32, C.POINTER(C.c_uint32), C.c_int32]),
+    "needle_cuda_wait_selftest": (C.c_int, [C.c_uint64, C.c_void_p]),
     "needle_cuda_stream": (C.c_void_p, [C.c_void_p]),
     "needle_cuda_sched_load": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_int32]),
