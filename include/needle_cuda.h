@@ -55,7 +55,10 @@ typedef struct needle_opts {
   int32_t max_sink;     /* largest sinkLength a slot accepts */
   int32_t kv_mode;      /* NEEDLE_KV_INT8 or NEEDLE_KV_FLOAT32, for every slot of the context */
   int32_t numerics;     /* NEEDLE_NUMERICS_EXACT */
-  int32_t reserved[9];
+  int32_t micro_batches; /* device-scheduled steps run as this many micro-batches on their own
+                            streams (1..8; 0 = the default, 4), so latency-bound kernels of one
+                            overlap the others' */
+  int32_t reserved[8];
 } needle_opts;
 
 typedef struct needle_ctx needle_ctx;

@@ -59,25 +59,28 @@ struct GroupBytes {
   static constexpr int value = BITS == 4 ? 64 : BITS == 3 ? 48 : 32;  // 128 columns
 };
 
-constexpr int kRowsPerThread = 2;
+constexpr int kRowsPerThread = 2;                         // the split-group kernel's tile
 constexpr int kTileRows = kRowsPerTile * kRowsPerThread;  // 64
 
-// A (64-row, 4-group) weight tile staged in shared memory, [group][row][stride]; the stride is the
+// A (32 R-row, 4-group) weight tile staged in shared memory, [group][row][stride]; the stride is the
 // group's bytes + 4, an odd number of words, so the 32 rows a warp reads sit on distinct banks.
-template <int BITS>
+template <int BITS, int R = kRowsPerThread>
 struct Stage {
   static constexpr int kBytes = GroupBytes<BITS>::value;
   static constexpr int kStride = kBytes + 4;
-  static constexpr int kSize = kGroupsPerChunk * kTileRows * kStride;
+  static constexpr int kRows = kRowsPerTile * R;
+  static constexpr int kSize = kGroupsPerChunk * kRows * kStride;
 };
 
 // Both staging loops issue eight global loads before the first shared-memory store: a store
 // waits for its load, so one word at a time would pay a full L2 round trip per word.
 constexpr int kStageBatch = 8;
 
-template <int BITS>
+template <int BITS, int R = kRowsPerThread>
 __device__ __forceinline__ void stage_weights(uint8_t* wt, const CqJob& job, int tile, int g0, int gn) {
-  constexpr int kWords = Stage<BITS>::kBytes / 4;
+  using St = Stage<BITS, R>;
+  constexpr int kWords = St::kBytes / 4;
+  constexpr int kTileRows = St::kRows;
   const int total = gn * kTileRows * kWords;
   for (int base = threadIdx.x; base < total; base += kStageBatch * kGemvThreads) {
     uint32_t v[kStageBatch];
@@ -91,7 +94,7 @@ __device__ __forceinline__ void stage_weights(uint8_t* wt, const CqJob& job, int
       v[k] = 0;
       if (idx < total && r_local < job.rows)
         v[k] = __ldg(reinterpret_cast<const uint32_t*>(job.packed + ((int64_t)job.row_start + r_local) * job.row_bytes +
-                                                       (int64_t)(g0 + gq) * Stage<BITS>::kBytes) + w);
+                                                       (int64_t)(g0 + gq) * St::kBytes) + w);
     }
 #pragma unroll
     for (int k = 0; k < kStageBatch; k++) {
@@ -100,27 +103,30 @@ __device__ __forceinline__ void stage_weights(uint8_t* wt, const CqJob& job, int
         const int gq = idx / (kTileRows * kWords);
         const int rem = idx - gq * kTileRows * kWords;
         const int row = rem / kWords, w = rem - row * kWords;
-        *reinterpret_cast<uint32_t*>(wt + (gq * kTileRows + row) * Stage<BITS>::kStride + 4 * w) = v[k];
+        *reinterpret_cast<uint32_t*>(wt + (gq * kTileRows + row) * St::kStride + 4 * w) = v[k];
       }
     }
   }
 }
 
-// Dot products of one (row pair, group) against kBT items, the chains interleaved across the
-// 2 x kBT (row, item) pairs so that independent binary64 operations issue back to back.  Each
+// Dot products of R rows of one group against BT items, the chains interleaved across the
+// R x BT (row, item) pairs so that independent binary64 operations issue back to back.  Each
 // chain is the reference's: per byte the 4 (2-bit, ternary) or 2 (4-bit) column products summed
 // left to right, then added to the group's dot; 3-bit rows add one product per column.
-// `wrow[r]` points at row r's staged group, `xg` at the group's columns of item 0 of the
-// [kBT][512] binary64 inputs.
-template <int BITS>
-__device__ __forceinline__ void group_dots(const uint8_t* wrow0, const uint8_t* wrow1, const double* lut,
-                                           const double* __restrict__ xg, int nb,
-                                           double (&dot)[kRowsPerThread][kBT]) {
+// Row r's staged group is at wrow0 + r * rstride, `xg` points at the group's columns of item 0 of
+// the [BT][512] binary64 inputs.
+template <int BITS, int R = kRowsPerThread, int BT = kBT>
+__device__ __forceinline__ void group_dots(const uint8_t* wrow0, int rstride, const double* lut,
+                                           const double* __restrict__ xg, int nb, double (&dot)[R][BT]) {
+  constexpr int kRowsPerThread = R;
+  constexpr int kBT = BT;
 #pragma unroll
   for (int r = 0; r < kRowsPerThread; r++)
 #pragma unroll
     for (int b = 0; b < kBT; b++) dot[r][b] = 0.0;
-  const uint8_t* wrow[kRowsPerThread] = {wrow0, wrow1};
+  const uint8_t* wrow[kRowsPerThread];
+#pragma unroll
+  for (int r = 0; r < kRowsPerThread; r++) wrow[r] = wrow0 + r * rstride;
   if constexpr (BITS == 2 || BITS == kTernaryBits || BITS == 4) {
     constexpr int kCols = BITS == 4 ? 2 : 4;  // columns per byte
 #pragma unroll 1
@@ -227,7 +233,7 @@ __device__ __forceinline__ void fill_gemv_lut(double* lut, const Codebook& cb, i
   }
 }
 
-// Stages the chunk's inputs of items [b0, b0 + nb) as binary64 (exact widening).
+// Stages the chunk's inputs of items [b0, b0 + nb) as binary64 (exact widening), [item][512].
 __device__ __forceinline__ void stage_inputs(double* xs, const CqJob& job, int b0, int nb, int g0, int gn) {
   const int total = nb * gn * kGroup;
   for (int base = threadIdx.x; base < total; base += kStageBatch * kGemvThreads) {
@@ -250,14 +256,19 @@ __device__ __forceinline__ void stage_inputs(double* xs, const CqJob& job, int b
   }
 }
 
-template <int BITS>
+// Units of (32 R-row tile, BT-item tile); jobs' tile_begin counts tiles of 32 R rows.
+template <int BITS, int R, int BT>
 __global__ void __launch_bounds__(kGemvThreads)
 k_cq_gemv(const CqJobs jobs, const Codebook cb, int32_t n_host, const int32_t* n_dev) {
+  using St = Stage<BITS, R>;
+  constexpr int kRowsPerThread = R;
+  constexpr int kBT = BT;
+  constexpr int kTileRows = St::kRows;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  double* xs = reinterpret_cast<double*>(smem_raw);                   // [kBT][512]
-  double* dsm = xs + kBT * 512;                                       // [kBT][4][64]
+  double* xs = reinterpret_cast<double*>(smem_raw);                   // [BT][512]
+  double* dsm = xs + kBT * 512;                                       // [BT][4][32 R]
   double* lut = dsm + kBT * kGroupsPerChunk * kTileRows;              // [16]
-  uint8_t* wt = reinterpret_cast<uint8_t*>(lut + 16);                 // Stage<BITS>
+  uint8_t* wt = reinterpret_cast<uint8_t*>(lut + 16);                 // Stage<BITS, R>
   const int n = item_count(n_host, n_dev);
   const int item_tiles = (n + kBT - 1) / kBT;
   const int units = jobs.total_tiles * item_tiles;
@@ -289,12 +300,12 @@ k_cq_gemv(const CqJobs jobs, const Codebook cb, int32_t n_host, const int32_t* n
       const int gn = min(kGroupsPerChunk, groups - g0);
       __syncthreads();  // previous chunk's xs / dsm / wt fully consumed
       stage_inputs(xs, job, b0, nb, g0, gn);
-      stage_weights<BITS>(wt, job, tile, g0, gn);
+      stage_weights<BITS, R>(wt, job, tile, g0, gn);
       __syncthreads();
       double dot[kRowsPerThread][kBT];
       if (gc < gn) {
-        const uint8_t* w0 = wt + (gc * kTileRows + lane) * Stage<BITS>::kStride;
-        group_dots<BITS>(w0, w0 + 32 * Stage<BITS>::kStride, lut, xs + gc * kGroup, nb, dot);
+        const uint8_t* w0 = wt + (gc * kTileRows + lane) * St::kStride;
+        group_dots<BITS, R, BT>(w0, 32 * St::kStride, lut, xs + gc * kGroup, nb, dot);
 #pragma unroll
         for (int r = 0; r < kRowsPerThread; r++)
 #pragma unroll
@@ -364,61 +375,71 @@ cudaError_t launch_cq_prepare(const float* x, int32_t x_stride, int32_t input_si
   return cudaGetLastError();
 }
 
+template <int R, int BT>
 static size_t gemv_smem() {
-  return sizeof(double) * (kBT * 512 + kBT * kGroupsPerChunk * kTileRows + 16) + Stage<4>::kSize;
+  return sizeof(double) * (BT * 512 + BT * kGroupsPerChunk * kRowsPerTile * R + 16) + Stage<4, R>::kSize;
 }
 
-// Opts the GEMV instantiations into more than 48 KB of dynamic shared memory, once per device.
-static cudaError_t configure_gemv() {
+// Per (R, BT) variant: opts the four record widths into their dynamic shared memory (once per
+// device) and returns the CTAs that fit on the device at once (the persistent grid size).
+template <int R, int BT>
+static cudaError_t configure_gemv(int* resident) {
   static std::atomic<uint64_t> done{0};
+  static std::atomic<int> cached[64];
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return e;
   const uint64_t bit = 1ull << (device & 63);
-  if (done.load() & bit) return cudaSuccess;
-  const int smem = (int)gemv_smem();
-  if ((e = cudaFuncSetAttribute(k_cq_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(k_cq_gemv<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(k_cq_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(k_cq_gemv<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
-  done.fetch_or(bit);
+  const int smem = (int)gemv_smem<R, BT>();
+  if (!(done.load() & bit)) {
+    if ((e = cudaFuncSetAttribute(k_cq_gemv<2, R, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+    if ((e = cudaFuncSetAttribute(k_cq_gemv<3, R, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+    if ((e = cudaFuncSetAttribute(k_cq_gemv<4, R, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+    if ((e = cudaFuncSetAttribute(k_cq_gemv<5, R, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+    int per_sm = 0, sms = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_cq_gemv<2, R, BT>, kGemvThreads, smem);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    cached[device & 63].store(std::max(1, per_sm) * std::max(1, sms));
+    done.fetch_or(bit);
+  }
+  *resident = cached[device & 63].load();
   return cudaSuccess;
 }
 
-// CTAs of k_cq_gemv that fit on the device at once (the persistent grid size).
-static int gemv_resident_ctas() {
-  static std::atomic<int> cached[64];
-  int device = 0;
-  cudaGetDevice(&device);
-  int v = cached[device & 63].load();
-  if (v > 0) return v;
-  int per_sm = 0, sms = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_cq_gemv<2>, kGemvThreads, gemv_smem());
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  v = std::max(1, per_sm) * std::max(1, sms);
-  cached[device & 63].store(v);
-  return v;
-}
-
-cudaError_t launch_cq_gemv(const CqJobs& jobs, const Codebook& cb, int32_t n_host,
-                           const int32_t* n_dev, cudaStream_t s) {
-  if (n_host <= 0 || jobs.count <= 0) return cudaSuccess;
-  cudaError_t ce = configure_gemv();
-  if (ce != cudaSuccess) return ce;
-  const int bits = jobs.job[0].bits;
-  for (int k = 1; k < jobs.count; k++)
-    if (jobs.job[k].bits != bits) return cudaErrorInvalidValue;
-  const int units = jobs.total_tiles * ((n_host + kBT - 1) / kBT);
-  dim3 grid(std::min(units, gemv_resident_ctas()));
-  const size_t smem = gemv_smem();
-  switch (bits) {
-    case 2: k_cq_gemv<2><<<grid, kGemvThreads, smem, s>>>(jobs, cb, n_host, n_dev); break;
-    case 3: k_cq_gemv<3><<<grid, kGemvThreads, smem, s>>>(jobs, cb, n_host, n_dev); break;
-    case 4: k_cq_gemv<4><<<grid, kGemvThreads, smem, s>>>(jobs, cb, n_host, n_dev); break;
-    case 5: k_cq_gemv<5><<<grid, kGemvThreads, smem, s>>>(jobs, cb, n_host, n_dev); break;
+template <int R, int BT>
+static cudaError_t launch_gemv_variant(CqJobs J, const Codebook& cb, int32_t n_host, const int32_t* n_dev,
+                                       cudaStream_t s) {
+  int resident = 0;
+  cudaError_t e = configure_gemv<R, BT>(&resident);
+  if (e != cudaSuccess) return e;
+  constexpr int rows_per_tile = kRowsPerTile * R;
+  J.total_tiles = 0;  // tiles of this variant's height
+  for (int k = 0; k < J.count; k++) {
+    J.job[k].tile_begin = J.total_tiles;
+    J.total_tiles += (J.job[k].rows + rows_per_tile - 1) / rows_per_tile;
+  }
+  const int units = J.total_tiles * ((n_host + BT - 1) / BT);
+  dim3 grid(std::min(units, resident));
+  const size_t smem = gemv_smem<R, BT>();
+  switch (J.job[0].bits) {
+    case 2: k_cq_gemv<2, R, BT><<<grid, kGemvThreads, smem, s>>>(J, cb, n_host, n_dev); break;
+    case 3: k_cq_gemv<3, R, BT><<<grid, kGemvThreads, smem, s>>>(J, cb, n_host, n_dev); break;
+    case 4: k_cq_gemv<4, R, BT><<<grid, kGemvThreads, smem, s>>>(J, cb, n_host, n_dev); break;
+    case 5: k_cq_gemv<5, R, BT><<<grid, kGemvThreads, smem, s>>>(J, cb, n_host, n_dev); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+// Tile shape of the batched exact GEMV: two rows per thread (64-row tiles) and four items per
+// tile measured best at 64-256 items (against 1 x 4, 1 x 8 and 2 x 8).
+cudaError_t launch_cq_gemv(const CqJobs& jobs, const Codebook& cb, int32_t n_host,
+                           const int32_t* n_dev, cudaStream_t s) {
+  if (n_host <= 0 || jobs.count <= 0) return cudaSuccess;
+  const int bits = jobs.job[0].bits;
+  for (int k = 1; k < jobs.count; k++)
+    if (jobs.job[k].bits != bits) return cudaErrorInvalidValue;
+  return launch_gemv_variant<2, 4>(jobs, cb, n_host, n_dev, s);
 }
 
 cudaError_t launch_cq_rows(const uint8_t* packed, const uint16_t* norms, int32_t bits,
@@ -467,7 +488,7 @@ k_cq_group_dots(const CqJob job, const Codebook cb, int32_t n, double* __restric
     if (gc >= gn) continue;
     double dot[kRowsPerThread][kBT];
     const uint8_t* w0 = wt + (gc * kTileRows + lane) * Stage<BITS>::kStride;
-    group_dots<BITS>(w0, w0 + 32 * Stage<BITS>::kStride, lut, xs + gc * kGroup, n, dot);
+    group_dots<BITS>(w0, 32 * Stage<BITS>::kStride, lut, xs + gc * kGroup, n, dot);
 #pragma unroll
     for (int r = 0; r < kRowsPerThread; r++) {
       const int r_local = tile * kTileRows + r * 32 + lane;

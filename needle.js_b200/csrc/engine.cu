@@ -339,7 +339,7 @@ struct needle_ctx {
   cudaStream_t mb_main[kMaxMicro] = {}, mb_side[kMaxMicro] = {};
   cudaEvent_t mb_fork[kMaxMicro][2] = {}, mb_join[kMaxMicro][2] = {}, mb_done[kMaxMicro] = {};
   cudaEvent_t split_ev = nullptr;
-  int micro = 4;  // micro-batches of a device-scheduled step
+  int micro = 4;  // micro-batches of a device-scheduled step (needle_opts.micro_batches)
   // The device-scheduled step captured as a CUDA graph after one eager step.
   cudaGraphExec_t sched_graph = nullptr;
   int64_t graph_launches = 0;
@@ -1171,6 +1171,8 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
             "kv_mode must be NEEDLE_KV_INT8 or NEEDLE_KV_FLOAT32");
     require(o.numerics == NEEDLE_NUMERICS_EXACT, NEEDLE_BACKEND_UNAVAILABLE, "unknown numerics mode");
     require(o.max_seqs >= 1 && o.max_seqs <= 65536, NEEDLE_BACKEND_UNAVAILABLE, "max_seqs out of range");
+    require(o.micro_batches >= 0 && o.micro_batches <= kMaxMicro, NEEDLE_BACKEND_UNAVAILABLE,
+            "micro_batches out of range (0..8)");
     require(o.max_sink >= 0 && o.max_len >= 1, NEEDLE_BACKEND_UNAVAILABLE, "max_len / max_sink out of range");
     int devices = 0;
     cuda_check(cudaGetDeviceCount(&devices), "cudaGetDeviceCount");
@@ -1204,7 +1206,7 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
       cuda_check(cudaEventCreateWithFlags(&C->mb_done[k], cudaEventDisableTiming), "cudaEventCreate");
     }
     cuda_check(cudaEventCreateWithFlags(&C->split_ev, cudaEventDisableTiming), "cudaEventCreate");
-    if (const char* mb = getenv("NEEDLE_MICRO")) C->micro = std::max(1, std::min(kMaxMicro, atoi(mb)));
+    if (o.micro_batches > 0) C->micro = std::min(kMaxMicro, int(o.micro_batches));
     build_model(*C);
     build_state(*C);
     cuda_check(cudaDeviceSynchronize(), "upload");

@@ -548,7 +548,7 @@ struct CacheRef {
 // area (kAttnTile value rows + scales + weights); slot_of(t) maps the t-th visible position to its
 // cache row.  Leaves the gated outputs in out[2][64] (smem).
 constexpr int kAttnTile = 256;
-constexpr int kAttnSc = 1, kAttnMix = 1, kAttnMc = 0;  // attend_pair variant of the engine
+constexpr int kAttnSc = 1, kAttnMix = 1, kAttnMc = 0;  // attend_pair variant of the engine (measured best)
 constexpr size_t kAttnTileBytes = kAttnTile * (kHeadDim + 2 * 8);  // codes, 2 x weight*scale
 
 // softmaxInPlace (math.ts:46-60) of both heads' binary32 scores e[2][count]: max (order-free),
@@ -607,7 +607,9 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // Attention variants (all bit-identical): Sc = key-code widening (0 add pipe, 1 conversion unit);
 // Mix = value-mix layout (0: one chain per thread, conversion rounding; 1: threads 0-63 run both
 // heads' chains of one element, head 0 rounding on the add pipe and head 1 by conversion; 2: both on
-// the add pipe; 3: both by conversion); Mc = value-code widening.
+// the add pipe; 3: both by conversion); Mc = value-code widening.  The engine's choice (kAttnSc,
+// kAttnMix, kAttnMc) balances the FP64 pipe against the conversion unit: it measured fastest of the
+// eight combinations at 256 items with full windows (1.15 against 1.26 ms per step for 0, 0, 0).
 template <int Sc, int Mix, int Mc, class SlotOf>
 __device__ void attend_pair(const CacheRef& C, int count, SlotOf slot_of, const double* q2, double* e,
                             unsigned char* tile, const float* gate, float* out, double* red) {
@@ -1195,15 +1197,6 @@ __global__ void __launch_bounds__(1024) k_sched(const SlotView sv, const StepVie
 
 // ------------------------------------------------------------------ launchers
 
-// Variant of the engine's attention kernel (an experiment switch: NEEDLE_ATTN_VARIANT, default 7).
-static int attention_variant() {
-  static const int v = [] {
-    const char* s = getenv("NEEDLE_ATTN_VARIANT");
-    return s ? atoi(s) : 7;
-  }();
-  return v;
-}
-
 // The dynamic shared-memory limit is an attribute of the function on the device, shared by every
 // context in the process, so it is raised to the device's opt-in maximum rather than to one
 // context's need (a smaller later context must not lower it under a larger one).
@@ -1217,7 +1210,6 @@ static cudaError_t raise_smem_limit(const void* fn) {
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)attr.sharedSizeBytes);
   return e;
 }
-
 
 cudaError_t launch_embed(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
                          cudaStream_t s) {
@@ -1242,17 +1234,7 @@ cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepV
                              int n_host, cudaStream_t s, int part) {
   if (n_host <= 0) return cudaSuccess;
   const size_t smem = attention_smem_bytes(sv.capacity, true);
-  const dim3 grid(n_host, kKvHeads);
-  switch (attention_variant()) {
-    case 0: k_attention<0, 0, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
-    case 1: k_attention<0, 1, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
-    case 2: k_attention<0, 2, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
-    case 3: k_attention<1, 1, 1><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
-    case 4: k_attention<1, 2, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
-    case 5: k_attention<1, 2, 1><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
-    case 6: k_attention<0, 3, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
-    default: k_attention<1, 1, 0><<<grid, kAttnThreads, smem, s>>>(m, sv, st, layer, part); break;
-  }
+  k_attention<kAttnSc, kAttnMix, kAttnMc><<<dim3(n_host, kKvHeads), kAttnThreads, smem, s>>>(m, sv, st, layer, part);
   return cudaGetLastError();
 }
 
@@ -1278,13 +1260,8 @@ cudaError_t configure_step_kernels(int32_t capacity) {
     return cudaErrorInvalidValue;
   cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(k_layer));
   if (e != cudaSuccess) return e;
-  for (const void* fn : {reinterpret_cast<const void*>(k_attention<0, 0, 0>), reinterpret_cast<const void*>(k_attention<0, 1, 0>),
-                         reinterpret_cast<const void*>(k_attention<0, 2, 0>), reinterpret_cast<const void*>(k_attention<1, 1, 1>),
-                         reinterpret_cast<const void*>(k_attention<1, 2, 0>), reinterpret_cast<const void*>(k_attention<1, 2, 1>),
-                         reinterpret_cast<const void*>(k_attention<0, 3, 0>), reinterpret_cast<const void*>(k_attention<1, 1, 0>)}) {
-    e = raise_smem_limit(fn);
-    if (e != cudaSuccess) return e;
-  }
+  e = raise_smem_limit(reinterpret_cast<const void*>(k_attention<kAttnSc, kAttnMix, kAttnMc>));
+  if (e != cudaSuccess) return e;
   return raise_smem_limit(reinterpret_cast<const void*>(k_attention_dev));
 }
 
