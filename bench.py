@@ -303,10 +303,11 @@ def bench_qmatvec(args, peaks):
                None)
     if big is not None:
         # the batched case runs on the tensor cores: algorithmic flops 2 * B * rows * in_pad against the
-        # measured dense bf16 peak; the pipe executes three bf16 products per weight x activation pair
+        # measured dense bf16 GEMM peak (fp16 runs at the same rate); the pipe executes three fp16 products
+        # per weight x activation pair
         tflops = 2 * 128 * 8192 * 8192 / (big["us"] * 1e-6) / 1e12
         tpeak = float((peaks or {}).get("bf16_tflops") or 1590.0)
-        line["roofline_batched"] = {"kernel": "k_cq_gemm_tc (+ k_cq_prep_bf16, k_splitk_sum)", "bound": "tensor",
+        line["roofline_batched"] = {"kernel": "k_cq_gemm_tc (+ k_cq_prep_f16, k_splitk_sum)", "bound": "tensor",
                                     "case": "stress 8192x8192 CQ4 batch 128", "achieved": round(tflops, 1),
                                     "executed": round(3 * tflops, 1), "peak": tpeak,
                                     "peak_source": "measured" if (peaks or {}).get("bf16_tflops") else "fallback",

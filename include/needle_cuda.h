@@ -43,6 +43,10 @@ typedef enum needle_status {
 
 enum {
   NEEDLE_NUMERICS_EXACT = 0, /* binary64 in reference order: bit-faithful to the CPU backend */
+  NEEDLE_NUMERICS_FAST = 1,  /* the projections (Q|K|V|gate, output, engram K|V, vocabulary) as
+                                tcgen05 tensor-core GEMMs over the step's items, fp16 head/tail
+                                split with fp32 accumulation (binary32-level accuracy); everything
+                                else as in exact numerics; int8 KV cache only */
   NEEDLE_KV_INT8 = 0,        /* RuntimeOptions.kvCache "int8" (runtime.ts:30-32) */
   NEEDLE_KV_FLOAT32 = 1      /* RuntimeOptions.kvCache "float32": keys / values stored as given */
 };
@@ -54,7 +58,7 @@ typedef struct needle_opts {
   int32_t max_len;      /* largest maximumLength a slot accepts (<= geometry max sequence) */
   int32_t max_sink;     /* largest sinkLength a slot accepts */
   int32_t kv_mode;      /* NEEDLE_KV_INT8 or NEEDLE_KV_FLOAT32, for every slot of the context */
-  int32_t numerics;     /* NEEDLE_NUMERICS_EXACT */
+  int32_t numerics;     /* NEEDLE_NUMERICS_EXACT or NEEDLE_NUMERICS_FAST */
   int32_t micro_batches; /* device-scheduled steps run as this many micro-batches on their own
                             streams (1..8; 0 = the default, 4), so latency-bound kernels of one
                             overlap the others' */
@@ -237,7 +241,7 @@ int needle_cuda_cq_matvec_dev(const needle_cq_matrix* m, const float* codebook, 
 /* The same matvec in fast numerics (record widths 2, 4 and ternary): results agree with cqMatvec
  * within binary32 rounding, not bit for bit.  Up to 15 items (5 for matrices of 4M weights and
  * more) it runs the table GEMV (binary32 per-group byte tables, weights streamed once per 8 items);
- * above, the tensor-core GEMM (bf16 head/tail split, fp32 accumulation, up to 128 items per pass).
+ * above, the tensor-core GEMM (fp16 head/tail split, fp32 accumulation, up to 128 items per pass).
  * Same arguments and scratch as needle_cuda_cq_matvec_dev; 3-bit matrices return
  * UNSUPPORTED_CACT. */
 int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const float* codebook, const float* x,

@@ -39,12 +39,17 @@ class CudaEngine:
     """One engine context on one GPU (needle_cuda_open .. needle_cuda_close)."""
 
     def __init__(self, archive: bytes, device: int = 0, max_seqs: int = 1, max_len: int = 2048,
-                 max_sink: int = 160, kv_cache: str = "int8"):
+                 max_sink: int = 160, kv_cache: str = "int8", numerics: str = "exact", micro_batches: int = 0):
         if kv_cache not in ("int8", "float32"):
             raise NeedleError("BACKEND_UNAVAILABLE", f"unknown kvCache {kv_cache!r}")
+        if numerics not in ("exact", "fast"):
+            raise NeedleError("BACKEND_UNAVAILABLE", f"unknown numerics {numerics!r}")
         self._archive = np.frombuffer(archive, dtype=np.uint8)
         opts = native.default_opts(device=device, max_seqs=max_seqs, max_len=max_len, max_sink=max_sink,
-                                   kv_mode=native.KV_FLOAT32 if kv_cache == "float32" else native.KV_INT8)
+                                   kv_mode=native.KV_FLOAT32 if kv_cache == "float32" else native.KV_INT8,
+                                   numerics=native.NUMERICS_FAST if numerics == "fast" else native.NUMERICS_EXACT,
+                                   micro_batches=micro_batches)
+        self.numerics = numerics
         self.kv_cache = kv_cache
         h = C.c_void_p()
         check(lib().needle_cuda_open(ptr(self._archive), self._archive.size, C.byref(opts), C.byref(h)))

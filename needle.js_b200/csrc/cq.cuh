@@ -60,16 +60,20 @@ size_t cq_gemv_fast_partial_floats(int32_t rows, int32_t in_pad);
 cudaError_t launch_cq_gemv_fast(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
                                 int32_t bits, const float* x, int32_t batch, float* y, const Codebook& cb,
                                 float* partials, cudaStream_t s);
-// Batched fast-numerics matvec on the tensor cores (cq_gemm_tc.cu): bf16 head/tail split GEMM,
-// record widths 2, 4 and ternary.  Scratch (cq_gemm_tc_scratch_bytes, 256-byte aligned): the
+// Batched fast-numerics matvec on the tensor cores (cq_gemm_tc.cu): fp16 head/tail split GEMM,
+// record widths 2, 3, 4 and ternary.  Scratch (cq_gemm_tc_scratch_bytes, 256-byte aligned): the
 // prepared activations and split-K partials; up to 128 items per pass.
 constexpr int kTcMinBatch = 16;
 bool cq_gemm_tc_supported(int32_t bits);
+// Split-K factor of the GEMM for a matrix (1: no partials and no split-K sum kernel).
+int cq_gemm_tc_splits(int32_t rows, int32_t input_size, int32_t sms);
 bool cq_gemm_tc_preferred(int32_t rows, int32_t input_size, int32_t batch);
 size_t cq_gemm_tc_scratch_bytes(int32_t rows, int32_t input_size, int32_t batch, int32_t sms);
+// x: rows of x_stride floats, raw (prepared = 0: each group is prepared here) or already prepared
+// (x', input padded to whole groups); y: rows of y_stride floats.  Record widths 2, 3, 4, ternary.
 cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
-                              int32_t bits, const float* x, int32_t batch, float* y, const Codebook& cb, void* scratch,
-                              int32_t sms, cudaStream_t s);
+                              int32_t bits, const float* x, int32_t x_stride, int32_t prepared, int32_t batch, float* y,
+                              int32_t y_stride, const Codebook& cb, void* scratch, int32_t sms, cudaStream_t s);
 cudaError_t launch_cq_rows(const uint8_t* packed, const uint16_t* norms, int32_t bits,
                            int32_t row_bytes, int32_t in_pad, int32_t input_size,
                            const int32_t* rows, int32_t n_rows, float* out, int32_t out_stride,

@@ -6,14 +6,19 @@
 //
 // is a GEMM with A = the dequantised weights (rows x inputs; each element is level * norm of its
 // group, folded in while decoding) and B = the prepared activations x' (B x inputs).  The tensor
-// cores multiply bf16; to keep binary32-level accuracy each operand is split into a bf16 head and
-// a bf16 tail (v = hi + lo up to 2^-17 |v|) and the product is accumulated as
-// A_hi B_hi + A_hi B_lo + A_lo B_hi in fp32 (the dropped A_lo B_lo term is below 2^-16 relative).
+// cores multiply fp16; to keep binary32-level accuracy each operand is split into an fp16 head and
+// an fp16 tail (v = hi + lo up to 2^-22 |v|) and the four products A_hi B_hi + A_hi B_lo +
+// A_lo B_hi + A_lo B_lo are accumulated in fp32.
+// fp16 rather than bf16 (8-bit significands, 2^-16 per operand) because the decode step amplifies
+// the projections' relative error about 500-fold over 27 layers: with bf16 heads and tails the
+// logits drifted 3e-3 from the reference, with fp16 ones they stay well inside 1e-3.  The weights
+// are scaled by 2^10 (exactly; undone in the epilogue) so that the tails of small level * norm
+// values stay clear of fp16's subnormal range; activations (prepared, O(1)) are split unscaled.
 // For N <= 64 two MMAs per K-step do it: A_hi x [B_hi; B_lo] (N' = 2N: columns [0, N) get A_hi B_hi
-// and [N, 2N) A_hi B_lo) and A_lo x B_hi into columns [0, N), and the epilogue adds the two column
-// blocks; above, three MMAs of N columns accumulate into [0, N).
+// and [N, 2N) A_hi B_lo) and A_lo x [B_hi; B_lo] into the same columns, and the epilogue adds the two
+// column blocks; above, four MMAs of N columns accumulate into [0, N).
 //
-// Kernels.  k_cq_prep_bf16 writes x' of every (group, item) as bf16 head and tail rows already in
+// Kernels.  k_cq_prep_f16 writes x' of every (group, item) as fp16 head and tail rows already in
 // the shared-memory layout the MMA reads (K-major, 128-byte swizzle; per group and 64-column half
 // the N head rows then the N tail rows), so the GEMM fetches a group's activations with one bulk
 // copy.  k_cq_gemm_tc: one CTA per (128-row tile, range of groups) and SM; the groups are split
@@ -25,7 +30,7 @@
 //   * decode warps 0-11, three teams of four (team t takes groups t, t + 3, ... into slot t, so that
 //     each slot is used in one team's program order; warp w serves tensor-memory lanes
 //     32 (w % 4) ..+31, one tile row per thread).  Per group a thread turns its
-//     row's norm into a 16-entry table of split values (level * norm as bf16 head | tail), decodes
+//     row's norm into a 16-entry table of split values (level * norm as fp16 head | tail), decodes
 //     the row's 128 weights with one table read each and writes the head and tail words into tensor
 //     memory (tcgen05.st); its packed bytes were loaded two of its groups earlier.
 //   * warp 12 (one elected lane) issues a group's 8 K-steps x 2 (or 3) MMAs and commits them to the slot's
@@ -34,7 +39,6 @@
 // Every mbarrier wait gives up after 2 s and marks the tile failed (its outputs become NaN).  The
 // epilogue reads the accumulator with tcgen05.ld (decode warps, one row per lane).
 #include <cuda.h>
-#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -66,7 +70,7 @@ constexpr size_t kTcMinSmem = 120 * 1024;
 constexpr int kTcSlotsUsed = 3;
 constexpr uint32_t kTcAccCols = 128;
 
-// Byte offset of bf16 element (row, k) (k < 64) in a K-major, 128-byte-swizzled tile.
+// Byte offset of 16-bit element (row, k) (k < 64) in a K-major, 128-byte-swizzled tile.
 __host__ __device__ __forceinline__ uint32_t sw128(int row, int k) {
   return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + (((k >> 3) ^ (row & 7)) << 4) + (k & 7) * 2);
 }
@@ -82,12 +86,15 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t a) {
          ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor: bf16 x bf16 -> fp32, A and B K-major, M = 128, N = n.
-__device__ __forceinline__ uint32_t bf16_idesc(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
+// Instruction descriptor: fp16 x fp16 -> fp32 (A and B type fields 0 = f16, both), A and B
+// K-major, M = 128, N = n.
+__device__ __forceinline__ uint32_t f16_idesc(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
 }
 
-// D (tensor memory) (+)= A (tensor memory, 128 lanes x 8 columns = 16 bf16 per row) x B^T (shared);
+constexpr float kTcWeightScale = 1024.0f;  // 2^10: A = level * norm * 2^10, undone in the epilogue
+
+// D (tensor memory) (+)= A (tensor memory, 128 lanes x 8 columns = 16 fp16 per row) x B^T (shared);
 // issued by one thread.
 __device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -161,26 +168,39 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// bf16 head and tail of two binary32 values, as bf16x2 words (first value in the low half).
+// fp16 head and tail of two binary32 values, as half2 words (first value in the low half).  The
+// head is fp16(v); v - head is exact in binary32 and its fp16 rounding is the tail.
 __device__ __forceinline__ void split2(float v0, float v1, uint32_t& hi, uint32_t& lo) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+  const __half2 h = __floats2half2_rn(v0, v1);
   hi = *reinterpret_cast<const uint32_t*>(&h);
-  const float r0 = __fsub_rn(v0, __uint_as_float(hi << 16));
-  const float r1 = __fsub_rn(v1, __uint_as_float(hi & 0xffff0000u));
-  const __nv_bfloat162 l = __floats2bfloat162_rn(r0, r1);
+  const float r0 = __fsub_rn(v0, __low2float(h));
+  const float r1 = __fsub_rn(v1, __high2float(h));
+  const __half2 l = __floats2half2_rn(r0, r1);
   lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
-// x' of (group g, item n) as bf16 head and tail, in the GEMM's activation layout
+// x' of (group g, item n) as fp16 head and tail, in the GEMM's activation layout
 // [group][half (2)][2N rows: N head rows, N tail rows][128 bytes], rows swizzled as the MMA's
 // K-major 128-byte layout.  One warp per (group, item); items nb <= n < N are zeros.
-__global__ void __launch_bounds__(256) k_cq_prep_bf16(const float* __restrict__ x, int32_t input_size, int32_t groups,
-                                                      int32_t nb, int32_t N, uint8_t* __restrict__ act) {
+// `prepared` inputs are x' already (padded to whole groups); otherwise each group is prepared here.
+__global__ void __launch_bounds__(256) k_cq_prep_f16(const float* __restrict__ x, int32_t x_stride, int32_t input_size,
+                                                      int32_t groups, int32_t nb, int32_t N, int32_t prepared,
+                                                      uint8_t* __restrict__ act) {
   const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (w >= groups * N) return;
   const int g = w / N, n = w - g * N;
   float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  if (n < nb) prepare_group_warp(x + (int64_t)n * input_size, input_size, g, v);
+  if (n < nb) {
+    if (prepared) {
+      const float4 p4 = __ldg(reinterpret_cast<const float4*>(x + (int64_t)n * x_stride + g * kGroup + 4 * lane));
+      v[0] = p4.x;
+      v[1] = p4.y;
+      v[2] = p4.z;
+      v[3] = p4.w;
+    } else {
+      prepare_group_warp(x + (int64_t)n * x_stride, input_size, g, v);
+    }
+  }
   uint32_t hi[2], lo[2];
   split2(v[0], v[1], hi[0], lo[0]);
   split2(v[2], v[3], hi[1], lo[1]);
@@ -195,9 +215,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
     const uint8_t* __restrict__ packed, const uint16_t* __restrict__ norms, int32_t rows, int32_t groups,
     int32_t row_bytes, const uint8_t* __restrict__ act, int32_t N, int32_t nb, int32_t groups_per_split,
     float* __restrict__ out, int32_t out_stride, int64_t split_stride, Codebook cb, uint32_t* __restrict__ wait_words) {
-  constexpr int kCodes = BITS == 4 ? 16 : 4;
-  constexpr int kGroupWords = BITS == 4 ? 16 : 8;  // packed 32-bit words of one row's group
-  constexpr int kPairsPerWord = BITS == 4 ? 4 : 8;  // column pairs (two codes) per packed word
+  constexpr int kCodes = BITS == 4 ? 16 : BITS == 3 ? 8 : 4;
+  constexpr int kGroupWords = BITS == 4 ? 16 : BITS == 3 ? 12 : 8;  // packed 32-bit words of one row's group
+  constexpr int kPairsPerWord = BITS == 4 ? 4 : 8;  // column pairs (two codes) per packed word (2, 4 bits)
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t a_full[kTcMaxSlots];  // 4 decode-warp arrivals
   __shared__ __align__(8) uint64_t b_full[kTcMaxSlots];  // producer arrival + copied bytes
@@ -224,6 +244,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
     if constexpr (BITS == 4) {
 #pragma unroll
       for (int k = 0; k < 16; k++) v = tid == k ? cb.v[12 + k] : v;
+    } else if constexpr (BITS == 3) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) v = tid == k ? cb.v[4 + k] : v;
     } else if constexpr (BITS == 2) {
 #pragma unroll
       for (int k = 0; k < 4; k++) v = tid == k ? cb.v[k] : v;
@@ -283,7 +306,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
   } else if (warp == kTcMmaWarp) {
     // ---- MMA issue: the whole warp waits (converged); the elected lane issues a group's MMAs back to
     // back from precomputed operands, so that the warp spends few issue slots next to the decoders
-    const uint32_t idesc2 = bf16_idesc(2 * N), idesc1 = bf16_idesc(N);
+    const uint32_t idesc2 = f16_idesc(2 * N), idesc1 = f16_idesc(N);
     const bool leader = elect_one();
     const uint64_t half_units = half_bytes >> 4;  // descriptor start-address units of one half
     bool failed = false;
@@ -307,11 +330,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
           const uint32_t first = (gi > 0 || kk > 0) ? 1u : 0u;
           if (doubled) {
             mma_ts(tmem, a_hi + kk * 8, bd, idesc2, first);  // [hh | hl] in columns [0, 2N)
+            mma_ts(tmem, a_lo + kk * 8, bd, idesc2, 1u);     // += [lh | ll]
           } else {
             mma_ts(tmem, a_hi + kk * 8, bd, idesc1, first);                    // hh
             mma_ts(tmem, a_hi + kk * 8, bd + (uint64_t)(N * 8), idesc1, 1u);  // += hl (tail rows N..2N-1)
+            mma_ts(tmem, a_lo + kk * 8, bd, idesc1, 1u);                       // += lh
+            mma_ts(tmem, a_lo + kk * 8, bd + (uint64_t)(N * 8), idesc1, 1u);  // += ll
           }
-          mma_ts(tmem, a_lo + kk * 8, bd, idesc1, 1u);  // += lh
         }
         mma_commit(&empty[sl]);
       }
@@ -359,17 +384,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
         const int j = j0 + d;
         if (j >= n_mine || failed) break;
         const int sl = team;  // group team + teams * j
-        // split table of this row's group: level * norm as bf16 head | tail, two codes at a time
+        // split table of this row's group: level * norm * 2^10 as fp16 head | tail, two codes at a time
 #pragma unroll
         for (int c = 0; c < kCodes; c += 2) {
           uint32_t h2, l2;
-          split2(__fmul_rn(lut[c], nr[d]), __fmul_rn(lut[c + 1], nr[d]), h2, l2);
+          split2(__fmul_rn(__fmul_rn(lut[c], nr[d]), kTcWeightScale),
+                 __fmul_rn(__fmul_rn(lut[c + 1], nr[d]), kTcWeightScale), h2, l2);
           tab[c * kTcDecodeThreads] = __byte_perm(h2, l2, 0x5410);
           tab[(c + 1) * kTcDecodeThreads] = __byte_perm(h2, l2, 0x7632);
         }
         // pairs 16q .. 16q + 15 (columns 32q .. 32q + 31) of the group as head and tail words; the
         // low and high codes of each packed byte are first split into separate byte lanes
         auto decode16 = [&](int q, uint32_t* hi, uint32_t* lo) {
+          if constexpr (BITS == 3) {
+            // 3-bit bitstream: pairs 16q .. 16q + 15 are the 96 bits of words 3q .. 3q + 2, pair j the
+            // 6-bit field at bit 6j (low code first)
+            const uint32_t* w3 = &wr[d][3 * q];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+              const int bit = 6 * j, wi = bit >> 5, sh = bit & 31;
+              const uint32_t field = wi < 2 ? __funnelshift_r(w3[wi], w3[wi + 1], sh) : (w3[2] >> sh);
+              const uint32_t t0 = tab[(field & 7u) * kTcDecodeThreads], t1 = tab[((field >> 3) & 7u) * kTcDecodeThreads];
+              hi[j] = __byte_perm(t0, t1, 0x5410);
+              lo[j] = __byte_perm(t0, t1, 0x7632);
+            }
+            return;
+          }
 #pragma unroll
           for (int wi = 0; wi < 16 / kPairsPerWord; wi++) {
             const uint32_t w = wr[d][q * (16 / kPairsPerWord) + wi];
@@ -431,7 +471,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
 #pragma unroll
         for (int j = 0; j < 8; j++)
           if (c0 + j < nb)
-            o[(int64_t)(c0 + j) * out_stride + grow] = bad ? NAN : __fadd_rn(__uint_as_float(v[j]), __uint_as_float(w[j]));
+            o[(int64_t)(c0 + j) * out_stride + grow] =
+                bad ? NAN : __fmul_rn(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(w[j])), 1.0f / kTcWeightScale);
       }
     }
   }
@@ -470,7 +511,11 @@ TcPlan plan_for(int32_t rows, int32_t in_pad, int sms) {
 
 }  // namespace
 
-bool cq_gemm_tc_supported(int32_t bits) { return bits == 2 || bits == 4 || bits == kTernaryBits; }
+int cq_gemm_tc_splits(int32_t rows, int32_t input_size, int32_t sms) {
+  return plan_for(rows, (input_size + kGroup - 1) / kGroup * kGroup, sms).used;
+}
+
+bool cq_gemm_tc_supported(int32_t bits) { return bits == 2 || bits == 3 || bits == 4 || bits == kTernaryBits; }
 
 // From 16 items the GEMM beats the table GEMV (one weight pass per 8 items) on every shape; for
 // matrices of 4M weights and more already from 6 items (measured on the config-2 shapes).
@@ -490,21 +535,25 @@ size_t cq_gemm_tc_scratch_bytes(int32_t rows, int32_t input_size, int32_t batch,
 }
 
 cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int32_t rows, int32_t input_size,
-                              int32_t bits, const float* x, int32_t batch, float* y, const Codebook& cb, void* scratch,
-                              int32_t sms, cudaStream_t s) {
+                              int32_t bits, const float* x, int32_t x_stride, int32_t prepared, int32_t batch, float* y,
+                              int32_t y_stride, const Codebook& cb, void* scratch, int32_t sms, cudaStream_t s) {
   if (batch <= 0 || rows <= 0) return cudaSuccess;
   const int in_pad = (input_size + kGroup - 1) / kGroup * kGroup;
   const int pb = bits == kTernaryBits ? 2 : bits;
   const int row_bytes = in_pad * pb / 8;
   const TcPlan p = plan_for(rows, in_pad, sms);
   uint8_t* act = static_cast<uint8_t*>(scratch);
-  cudaError_t e = cudaSuccess;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  uint32_t* wait_words = wait_status_words(dev);
   for (int b0 = 0; b0 < batch; b0 += kTcMaxN) {
     const int nb = std::min(kTcMaxN, batch - b0);
     const int N = (nb + 15) / 16 * 16;
     const size_t act_bytes = (size_t)p.groups * 2 * (2 * N) * 128;
     const int warps = p.groups * N;
-    k_cq_prep_bf16<<<(warps + 7) / 8, 256, 0, s>>>(x + (int64_t)b0 * input_size, input_size, p.groups, nb, N, act);
+    k_cq_prep_f16<<<(warps + 7) / 8, 256, 0, s>>>(x + (int64_t)b0 * x_stride, x_stride, input_size, p.groups, nb, N,
+                                                  prepared, act);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     float* part = reinterpret_cast<float*>(act + act_bytes);
@@ -513,15 +562,14 @@ cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int3
     auto launch = [&](auto kernel) {
       e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return;
-      float* o = p.used > 1 ? part : y + (int64_t)b0 * rows;
-      int dev = 0;
-      e = cudaGetDevice(&dev);
-      if (e != cudaSuccess) return;
+      float* o = p.used > 1 ? part : y + (int64_t)b0 * y_stride;
       kernel<<<dim3(p.m_tiles, p.used), kTcThreads, smem, s>>>(packed, norms, rows, p.groups, row_bytes, act, N, nb,
-                                                              p.per, o, rows, split_stride, cb, wait_status_words(dev));
+                                                              p.per, o, p.used > 1 ? rows : y_stride, split_stride, cb,
+                                                              wait_words);
       e = cudaGetLastError();
     };
     if (bits == 4) launch(k_cq_gemm_tc<4>);
+    else if (bits == 3) launch(k_cq_gemm_tc<3>);
     else if (bits == 2) launch(k_cq_gemm_tc<2>);
     else if (bits == kTernaryBits) launch(k_cq_gemm_tc<kTernaryBits>);
     else return cudaErrorInvalidValue;
@@ -529,7 +577,7 @@ cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int3
     if (p.used > 1) {
       const int64_t n = (int64_t)rows * nb;
       k_splitk_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, p.used, split_stride, rows, nb,
-                                                              y + (int64_t)b0 * rows, rows);
+                                                              y + (int64_t)b0 * y_stride, y_stride);
       e = cudaGetLastError();
       if (e != cudaSuccess) return e;
     }

@@ -354,6 +354,13 @@ struct needle_ctx {
   StepView stv{};
   std::vector<CqMat> lq, lk, lv, lg, lo;
   std::vector<CqMat> ek, ev;
+  // Fast numerics (NEEDLE_NUMERICS_FAST): Q|K|V|gate of each layer and K|V of each engram site as
+  // one matrix each (one GEMM per shared input), and per micro-batch lane the GEMM's scratch.
+  bool fast = false;
+  int sms = 0;
+  std::vector<CqMat> lqkvg, ekv;
+  void* gemm_scratch[kMaxMicro] = {};
+  size_t gemm_scratch_bytes = 0;
   int32_t* d_counts = nullptr;  // [0] n_items, [1] n_select
   std::vector<SlotHost> slots;
   // pinned staging
@@ -467,6 +474,33 @@ CqMat upload_cq(needle_ctx& C, int i) {
   return m;
 }
 
+// Matrices of equal record width and input length stacked row-wise into one (packed rows, then
+// fp16 norms, as the archive lays out one matrix), copied on the device.
+CqMat stack_rows(needle_ctx& C, std::initializer_list<CqMat> parts) {
+  const CqMat& f = *parts.begin();
+  int rows = 0;
+  for (const CqMat& p : parts) {
+    require(p.bits == f.bits && p.in_pad == f.in_pad && p.input_size == f.input_size, NEEDLE_UNSUPPORTED_CACT,
+            "fast numerics needs the projections that share an input to share a record width");
+    rows += p.rows;
+  }
+  const int groups = f.in_pad / kGroup;
+  uint8_t* packed = C.dalloc<uint8_t>(size_t(rows) * f.row_bytes + 64);
+  uint16_t* norms = C.dalloc<uint16_t>(size_t(rows) * groups + 8, false);
+  size_t r0 = 0;
+  for (const CqMat& p : parts) {
+    cuda_check(cudaMemcpy(packed + r0 * f.row_bytes, p.packed, size_t(p.rows) * f.row_bytes, cudaMemcpyDeviceToDevice),
+               "stack");
+    cuda_check(cudaMemcpy(norms + r0 * groups, p.norms, size_t(p.rows) * groups * 2, cudaMemcpyDeviceToDevice), "stack");
+    r0 += p.rows;
+  }
+  CqMat m = f;
+  m.packed = packed;
+  m.norms = norms;
+  m.rows = rows;
+  return m;
+}
+
 const float* upload_floats(needle_ctx& C, const std::vector<float>& v) {
   float* d = C.dalloc<float>(v.size(), false);
   cuda_check(cudaMemcpy(d, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice), "upload");
@@ -571,6 +605,10 @@ void build_model(needle_ctx& C) {
     C.lv.push_back(C.cq[Lr.v]);
     C.lg.push_back(C.cq[Lr.gate]);
     C.lo.push_back(C.cq[Lr.o]);
+  }
+  if (C.fast) {
+    for (int l = 0; l < L; l++) C.lqkvg.push_back(stack_rows(C, {C.lq[l], C.lk[l], C.lv[l], C.lg[l]}));
+    for (int s = 0; s < m.n_sites; s++) C.ekv.push_back(stack_rows(C, {C.ek[s], C.ev[s]}));
   }
   m.norm_input = upload_floats(C, pack_layers(C, &Roles::L::norm_input, kDim));
   m.query_norm = upload_floats(C, pack_layers(C, &Roles::L::qn, kHeadDim));
@@ -708,6 +746,14 @@ void build_state(needle_ctx& C) {
   cuda_check(cudaMallocHost(&C.h_ids, B * sizeof(int32_t)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_logprob, B * sizeof(double)), "cudaMallocHost");
   cuda_check(configure_step_kernels(capacity), "cudaFuncSetAttribute");
+  if (C.fast) {
+    size_t bytes = 0;
+    for (const CqMat* M : std::initializer_list<const CqMat*>{&C.lqkvg[0], &C.lo[0], &m.embedding})
+      bytes = std::max(bytes, cq_gemm_tc_scratch_bytes(M->rows, M->input_size, int(B), C.sms));
+    if (!C.ekv.empty()) bytes = std::max(bytes, cq_gemm_tc_scratch_bytes(C.ekv[0].rows, C.ekv[0].input_size, int(B), C.sms));
+    C.gemm_scratch_bytes = (bytes + 255) & ~size_t(255);
+    for (int k = 0; k < kMaxMicro; k++) C.gemm_scratch[k] = C.dalloc<uint8_t>(C.gemm_scratch_bytes, false);
+  }
 }
 
 // Builds the GEMV job list for matrices sharing one input (same bits per launch).
@@ -738,10 +784,27 @@ struct JobSpec {
   int y_stride;
 };
 
-// Launches the jobs grouped by record width (one GEMV launch per width present).
+// Launches the jobs grouped by record width (one GEMV launch per width present).  In fast numerics
+// every job is a tensor-core GEMM over the lane's n_host item rows (rows past the device count hold
+// stale inputs; their outputs are never read).
 void run_gemv(needle_ctx& C, int cls, const std::vector<JobSpec>& specs, int n_host, const int32_t* n_dev,
-              cudaStream_t strm = nullptr) {
+              cudaStream_t strm = nullptr, int lane = 0) {
   if (!strm) strm = C.stream;
+  if (C.fast) {
+    for (const auto& sp : specs) {
+      const CqMat& M = sp.M;
+      const int passes = (n_host + 127) / 128;
+      const int splits = cq_gemm_tc_splits(M.rows, M.input_size, C.sms);
+      C.launches += passes * (splits > 1 ? 3 : 2) - 1;  // timed() counts one
+      C.timed(cls, [&] {
+        return launch_cq_gemm_tc(M.packed + int64_t(sp.row_start) * M.row_bytes,
+                                 M.norms + int64_t(sp.row_start) * (M.in_pad / kGroup), sp.rows, M.input_size, M.bits,
+                                 sp.x, sp.x_stride, 1, n_host, sp.y, sp.y_stride, C.mv.cb, C.gemm_scratch[lane], C.sms,
+                                 strm);
+      }, strm);
+    }
+    return;
+  }
   for (int bits : {2, 3, 4, 5}) {
     CqJobs J{};
     for (const auto& s : specs)
@@ -760,6 +823,7 @@ struct Lane {
   cudaStream_t main, side;
   cudaEvent_t* fork;
   cudaEvent_t* join;
+  int index;  // micro-batch lane (its own GEMM scratch in fast numerics)
 };
 
 // A view of the step scratch for the items [offset, ...) with their own device counts.
@@ -805,12 +869,17 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
   if (m.n_sites > 0) {
     std::vector<JobSpec> jobs;
     for (int s = 0; s < m.n_sites; s++) {
+      if (C.fast) {  // K and V rows of the site as one matrix: outputs [site][K | V]
+        jobs.push_back({C.ekv[s], 0, 1024, st.prep_engram + s * kDim, m.n_sites * kDim,
+                        st.engram_kv + (s * 2) * kDim, m.n_sites * 2 * kDim});
+        continue;
+      }
       jobs.push_back({C.ek[s], 0, 512, st.prep_engram + s * kDim, m.n_sites * kDim,
                       st.engram_kv + (s * 2) * kDim, m.n_sites * 2 * kDim});
       jobs.push_back({C.ev[s], 0, 512, st.prep_engram + s * kDim, m.n_sites * kDim,
                       st.engram_kv + (s * 2 + 1) * kDim, m.n_sites * 2 * kDim});
     }
-    run_gemv(C, P_GEMV_ENGRAM, jobs, n_host, n_dev, s0);
+    run_gemv(C, P_GEMV_ENGRAM, jobs, n_host, n_dev, s0, lane.index);
   }
   for (int l = 0; l <= m.layers; l++) {
     if (l > 0) cuda_check(cudaStreamWaitEvent(s0, lane.join[(l - 1) & 1], 0), "join");
@@ -823,29 +892,33 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
     cuda_check(launch_route(st, n_host, lane.side), "route");
     C.launches++;
     cuda_check(cudaEventRecord(lane.join[l & 1], lane.side), "join");
-    run_gemv(C, P_GEMV_QKVG,
-             {{C.lq[l], 0, 512, st.prep_a, kDim, st.qkvg, 1536},
-              {C.lk[l], 0, 256, st.prep_a, kDim, st.qkvg + 512, 1536},
-              {C.lv[l], 0, 256, st.prep_a, kDim, st.qkvg + 768, 1536},
-              {C.lg[l], 0, 512, st.prep_a, kDim, st.qkvg + 1024, 1536}},
-             n_host, n_dev, s0);
+    if (C.fast)
+      run_gemv(C, P_GEMV_QKVG, {{C.lqkvg[l], 0, 1536, st.prep_a, kDim, st.qkvg, 1536}}, n_host, n_dev, s0,
+               lane.index);
+    else
+      run_gemv(C, P_GEMV_QKVG,
+               {{C.lq[l], 0, 512, st.prep_a, kDim, st.qkvg, 1536},
+                {C.lk[l], 0, 256, st.prep_a, kDim, st.qkvg + 512, 1536},
+                {C.lv[l], 0, 256, st.prep_a, kDim, st.qkvg + 768, 1536},
+                {C.lg[l], 0, 512, st.prep_a, kDim, st.qkvg + 1024, 1536}},
+               n_host, n_dev, s0);
     if (st.chunk) {  // every item's K/V before any item attends
       C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 1); }, s0);
       C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 2); }, s0);
     } else {
       C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0); }, s0);
     }
-    run_gemv(C, P_GEMV_O, {{C.lo[l], 0, 512, st.prep_o, kDim, st.proj, kDim}}, n_host, n_dev, s0);
+    run_gemv(C, P_GEMV_O, {{C.lo[l], 0, 512, st.prep_o, kDim, st.proj, kDim}}, n_host, n_dev, s0, lane.index);
   }
   if (any_select)
     run_gemv(C, P_GEMV_VOCAB, {{m.embedding, 0, m.vocab, st.prep_f, kDim, st.logits, m.vocab}}, n_host,
-             st.n_select, s0);
+             st.n_select, s0, lane.index);
   if (finish) C.timed(P_FINISH, [&] { return launch_finish(m, sv, st, n_host, sched, s0); }, s0);
 }
 
-Lane lane_a(needle_ctx& C) { return Lane{C.stream, C.side, C.fork_ev, C.join_ev}; }
+Lane lane_a(needle_ctx& C) { return Lane{C.stream, C.side, C.fork_ev, C.join_ev, 0}; }
 Lane lane_k(needle_ctx& C, int k) {
-  return k == 0 ? lane_a(C) : Lane{C.mb_main[k], C.mb_side[k], C.mb_fork[k], C.mb_join[k]};
+  return k == 0 ? lane_a(C) : Lane{C.mb_main[k], C.mb_side[k], C.mb_fork[k], C.mb_join[k], k};
 }
 
 // One device-scheduled step: admission and item list on the device, then the busy slots as
@@ -1054,6 +1127,23 @@ void upload_items(needle_ctx& C, const DevItem* src, int n, int rows) {
   });
 }
 
+// Fails the call (BACKEND_UNAVAILABLE) when a bounded wait of a fast-numerics kernel ran out during
+// the work just synchronised (its outputs are NaN); the wait status is cleared.
+void check_device_waits(needle_ctx& C) {
+  if (!C.fast) return;
+  uint32_t* w = wait_status_words(C.device);
+  if (!w) return;
+  bool any = false;
+  for (int k = 0; k < kWaitKinds; k++) {
+    volatile uint32_t* v = w + k;
+    if (*v) {
+      any = true;
+      *v = 0;
+    }
+  }
+  require(!any, NEEDLE_BACKEND_UNAVAILABLE, "a bounded device wait ran out in a fast-numerics kernel (outputs are NaN)");
+}
+
 // Reads the selections (and logits) back, waits for the step and advances the slots.
 void complete_step(needle_ctx& C, const needle_step_item* items, int32_t n, int rows, const std::vector<int>& order,
                    needle_selected* out_selected, float* out_logits) {
@@ -1070,6 +1160,7 @@ void complete_step(needle_ctx& C, const needle_step_item* items, int32_t n, int 
                  "logits readback");
   }
   cuda_check(cudaStreamSynchronize(C.stream), "step");
+  check_device_waits(C);
   for (int i = 0; i < n; i++) {
     C.slots[items[i].seq].position++;
     if (items[i].select) {
@@ -1169,7 +1260,10 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
     const needle_opts& o = C->opts;
     require(o.kv_mode == NEEDLE_KV_INT8 || o.kv_mode == NEEDLE_KV_FLOAT32, NEEDLE_BACKEND_UNAVAILABLE,
             "kv_mode must be NEEDLE_KV_INT8 or NEEDLE_KV_FLOAT32");
-    require(o.numerics == NEEDLE_NUMERICS_EXACT, NEEDLE_BACKEND_UNAVAILABLE, "unknown numerics mode");
+    require(o.numerics == NEEDLE_NUMERICS_EXACT || o.numerics == NEEDLE_NUMERICS_FAST, NEEDLE_BACKEND_UNAVAILABLE,
+            "unknown numerics mode");
+    require(o.numerics == NEEDLE_NUMERICS_EXACT || o.kv_mode == NEEDLE_KV_INT8, NEEDLE_BACKEND_UNAVAILABLE,
+            "fast numerics runs on the int8 KV cache");
     require(o.max_seqs >= 1 && o.max_seqs <= 65536, NEEDLE_BACKEND_UNAVAILABLE, "max_seqs out of range");
     require(o.micro_batches >= 0 && o.micro_batches <= kMaxMicro, NEEDLE_BACKEND_UNAVAILABLE,
             "micro_batches out of range (0..8)");
@@ -1207,6 +1301,8 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
     }
     cuda_check(cudaEventCreateWithFlags(&C->split_ev, cudaEventDisableTiming), "cudaEventCreate");
     if (o.micro_batches > 0) C->micro = std::min(kMaxMicro, int(o.micro_batches));
+    C->fast = o.numerics == NEEDLE_NUMERICS_FAST;
+    cuda_check(cudaDeviceGetAttribute(&C->sms, cudaDevAttrMultiProcessorCount, C->device), "device attribute");
     build_model(*C);
     build_state(*C);
     cuda_check(cudaDeviceSynchronize(), "upload");
@@ -1728,6 +1824,7 @@ int needle_cuda_sched_status(needle_ctx* ctx, int64_t* tokens_processed, int64_t
     needle_ctx& C = *ctx_of(ctx);
     require(C.sched_loaded, NEEDLE_BACKEND_UNAVAILABLE, "no scheduler queue loaded");
     cuda_check(cudaStreamSynchronize(C.stream), "sched_status");
+    check_device_waits(C);
     int32_t ctr[6];
     cuda_check(cudaMemcpy(ctr, C.sched.next_seq, 24, cudaMemcpyDeviceToHost), "sched_status");
     int64_t processed = 0, generated = 0;

@@ -332,8 +332,8 @@ extern "C" int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const f
   if (!m || !codebook || (batch > 0 && (!x || !y)))
     return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "null argument");
   if (m->group_size != kGroup) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "CQ group size 128 only");
-  if (!cq_gemv_fast_supported(m->bits))
-    return op_fail(NEEDLE_UNSUPPORTED_CACT, "fast matvec supports record widths 2, 4 and ternary");
+  if (!cq_gemv_fast_supported(m->bits) && !cq_gemm_tc_supported(m->bits))
+    return op_fail(NEEDLE_UNSUPPORTED_CACT, "unsupported CQ record width");
   if (m->rows < 0 || m->input_size <= 0 || batch < 0) return op_fail(NEEDLE_INVALID_CACT, "bad matrix shape");
   if ((reinterpret_cast<uintptr_t>(m->packed) & 15) != 0)
     return op_fail(NEEDLE_BACKEND_UNAVAILABLE, "packed rows must be 16-byte aligned");
@@ -345,7 +345,8 @@ extern "C" int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const f
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e == cudaSuccess && check_wait_status(device) != NEEDLE_OK) return NEEDLE_BACKEND_UNAVAILABLE;
-  if (cq_gemm_tc_supported(m->bits) && cq_gemm_tc_preferred(m->rows, m->input_size, batch)) {
+  if (cq_gemm_tc_supported(m->bits) &&
+      (cq_gemm_tc_preferred(m->rows, m->input_size, batch) || !cq_gemv_fast_supported(m->bits))) {
     // a real dense contraction: tensor-core GEMM
     int sms = 0;
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
@@ -353,7 +354,8 @@ extern "C" int needle_cuda_cq_matvec_dev_fast(const needle_cq_matrix* m, const f
     const size_t bytes = cq_gemm_tc_scratch_bytes(m->rows, m->input_size, batch, sms);
     if (e == cudaSuccess) e = scratch_for(device, (bytes + 3) / 4, &scratch);
     if (e == cudaSuccess)
-      e = launch_cq_gemm_tc(m->packed, m->norms, m->rows, m->input_size, m->bits, x, batch, y, cb, scratch, sms, s);
+      e = launch_cq_gemm_tc(m->packed, m->norms, m->rows, m->input_size, m->bits, x, m->input_size, 0, batch, y,
+                            m->rows, cb, scratch, sms, s);
     if (e != cudaSuccess) return op_fail(NEEDLE_BACKEND_UNAVAILABLE, cudaGetErrorString(e));
     return NEEDLE_OK;
   }

@@ -514,12 +514,15 @@ def test_errors_follow_needle_error_codes(engine, ref_model):
                                                     # batch >= 16: the tensor-core GEMM (bf16 head/tail split)
                                                     (4, 512, 512, 16), (2, 1000, 8192, 32), (5, 300, 2048, 40),
                                                     (4, 64, 20000, 17), (4, 700, 1000, 130), (4, 4096, 4096, 128),
-                                                    (2, 8192, 512, 64), (4, 2048, 2048, 6)])
+                                                    (2, 8192, 512, 64), (4, 2048, 2048, 6),
+                                                    # 3-bit rows always take the tensor-core GEMM
+                                                    (3, 512, 512, 1), (3, 512, 512, 64), (3, 1000, 8192, 17),
+                                                    (3, 300, 2048, 130)])
 def test_cq_matvec_dev_fast_within_tolerance(torch_cuda, oracle, bits, rows, inputs, batch):
     """Fast numerics (binary32) vs the oracle's binary64 cqMatvec: |got - want| <= 1e-5 * sum of
     |terms| bound, taken as 2e-6 * sqrt(inputs) * max|want| + 1e-6.  Batches of 16 and more (6 and
-    more for 4M weights) take the tensor-core path (130 = two passes, the second of 2 items padded
-    to 16)."""
+    more for 4M weights), and 3-bit matrices at any batch, take the tensor-core path (130 = two
+    passes, the second of 2 items padded to 16)."""
     torch = torch_cuda
     from needle_b200 import native, synth
     packed, norms = synth.random_cq_matrix(rows, inputs, bits, seed=6)
