@@ -41,6 +41,9 @@ import __graft_entry__  # noqa: E402  (registers the needle.js_b200/ package as 
 
 __graft_entry__.load()
 
+# DRAM bytes of one 256-item k_attention launch in the benchmarked state (set from the committed
+# steady-state capture; None until one exists)
+ATTENTION_TRAFFIC_BYTES = 30582272
 SLOTS = 256
 PROMPT = (32, 1024)
 GEN = (16, 128)
@@ -149,20 +152,37 @@ def aggregate(local_stats, dist=None):
             float(allst[:, 3].max()), float(allst[:, 4].sum()), int(allst[:, 5].sum()))
 
 
-def roofline_for(prof, n_items, peaks):
-    """Roofline of the kernel class with the largest share of step time."""
+# Binary64 operations the reference performs per unit (its own expressions, not this engine's):
+# attention, per visible position, head element and query head: q * code * keyScale (2 multiplies)
+# and the add of the score dot, weight * code * valueScale (2) and the add of the value mix -> 6;
+# a 2-bit matvec byte (4 weights): 1 multiply + 3 multiply-adds + 1 add = 5 (4-bit: 3 per byte;
+# 3-bit: 1 multiply-add per weight).
+FP64_OPS_ATTENTION = 6
+# FP64 lanes per SM per clock on B200 (spec: 37-40 TFLOP/s FP64 = 148 SMs x 64 FMA lanes x ~2 GHz);
+# no FP64 peak is measured on this pool, so the spec-derived figure at the sampled clock is used.
+FP64_LANES_PER_SM = 64
+SMS = 148
+
+
+def roofline_for(prof, n_items, peaks, visible=None, sm_mhz=None):
+    """Roofline of the kernel class with the largest share of step time.  `visible` is the number of
+    visible KV positions summed over the step's items (from the slots' positions), else full
+    256-position windows are assumed."""
     cls, (ms, launches) = max(prof.items(), key=lambda kv: kv[1][0])
     per_launch_ms = ms / max(launches, 1)
-    # algorithmic bytes per launch: the bytes the kernel must touch once per item (KV rows of a full
-    # 256-position window, inputs and outputs) plus, for the GEMVs, every weight byte once
+    # algorithmic bytes per launch: the bytes the kernel must touch once per item (KV rows of the
+    # visible positions, inputs and outputs) plus, for the GEMVs, every weight byte once
     kv_row = 64 + 64 + 4 + 4
     weights = {"gemv_qkvg": (512 + 256 + 256 + 512) * (128 + 8), "gemv_o": 512 * (192 + 8),
                "gemv_vocab": 8192 * (256 + 8)}
+    positions = visible if visible is not None else n_items * 256
+    fp64_ops = None
     if cls == "layer":
         per_item = 2 * 2048 * 4 + 24 * (1024 + 32) + 5 * 2048 + 80 * 2
         bytes_ = n_items * per_item + 12 * 2048
     elif cls == "attention":
-        bytes_ = n_items * (4 * 256 * kv_row + 1536 * 4 + 512 * 4)
+        bytes_ = 4 * positions * kv_row + n_items * (1536 * 4 + 512 * 4)
+        fp64_ops = FP64_OPS_ATTENTION * 8 * 64 * positions  # 8 query heads x 64 elements
     elif cls in weights:
         ins = {"gemv_qkvg": (512, 1536), "gemv_o": (512, 512), "gemv_vocab": (512, 8192)}[cls]
         bytes_ = weights[cls] + n_items * 4 * (ins[0] + ins[1])
@@ -172,16 +192,27 @@ def roofline_for(prof, n_items, peaks):
     peak = peaks.get("hbm_gbs") if peaks else None
     src = "measured" if peak else "fallback"
     peak = peak or 6650.0
-    # DRAM bytes (read + write) per launch of the 256-slot decode step, from one ncu capture of each
-    # kernel: far below the algorithmic bytes because the KV written by the previous step and the
-    # weights are read from L2
-    traffic = {"attention": 2307840, "layer": 3831808, "gemv_qkvg": 820224, "gemv_o": 703488}
+    # DRAM bytes (read + write) of one launch of the kernel in the benchmarked state (ncu, 1 pass,
+    # bench.py --steps 20 --warmup 5 --no-cpu-baseline --e2e-steps 2 --no-fast: the first
+    # 256-item launches after the ramp; profiles/attention_exact_decode_step_steady_state.md)
+    traffic = {"attention": ATTENTION_TRAFFIC_BYTES}
     line = {"kernel": cls, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_source": src,
             "unit": "GB/s", "frac": round(achieved / peak, 4),
             "traffic": traffic.get(cls) if n_items == 256 else None,
             "launch_ms": round(per_launch_ms, 5), "algorithmic_bytes_per_launch": int(bytes_)}
     if line["traffic"] is not None:
-        line["traffic_source"] = "profiles/exact_kernels_decode_step_256slots.md"
+        line["traffic_source"] = "profiles/attention_exact_decode_step_steady_state.md"
+    if visible is not None:
+        line["visible_positions_per_launch"] = int(visible)
+    if fp64_ops is not None:
+        mhz = sm_mhz or 1965.0
+        fpeak = SMS * FP64_LANES_PER_SM * mhz * 1e6
+        line["fp64"] = {"bound": "fp64", "ops_per_launch": int(fp64_ops),
+                        "achieved_gops": round(fp64_ops / (per_launch_ms * 1e-3) / 1e9, 1),
+                        "peak_gops": round(fpeak / 1e9, 1), "frac": round(fp64_ops / (per_launch_ms * 1e-3) / fpeak, 4),
+                        "peak_source": "spec lanes (148 SMs x 64 FP64 lanes) x sampled SM clock, not measured",
+                        "ops": "the reference's binary64 multiplies and adds per visible position (6 per element "
+                               "and query head)"}
     return line
 
 
@@ -801,6 +832,7 @@ def main():
     ap.add_argument("--ramp", type=int, default=1600, help="untimed steps to reach the steady-state mix")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fast", action="store_true", help="decode: skip the fast-numerics measurement")
     ap.add_argument("--cases", default="", help="qmatvec: shape-name substring; attention: comma list of L")
     ap.add_argument("--batches", default="", help="qmatvec: comma list of batch sizes (default 1,8,32,128)")
     ap.add_argument("--numerics", choices=["both", "exact", "fast"], default="both",
@@ -904,7 +936,10 @@ def main():
     gen_tokens = g1 - g0
     processed = p1 - p0
 
-    # per-kernel-class timing (events around every launch) for the roofline, after the timed run
+    # per-kernel-class timing (events around every launch) for the roofline, after the timed run;
+    # the visible KV positions of the profiled steps from the slots' positions (window 256, sink 0)
+    slots = [eng.sched_slot(k) for k in range(SLOTS)]
+    visible = sum(min(pos + 1 + k, 256) for (_, pos, busy) in slots if busy for k in range(10)) / 10.0
     eng.profile(True)
     eng.sched_step(10)
     prof = {k: v for k, v in eng.profile_read().items() if v[1] > 0}
@@ -916,6 +951,48 @@ def main():
 
     ms_max, gen_all, proc_all, e2e_ms, e2e_gen, launches_all = aggregate(
         [ms, gen_tokens, processed, e2e["ms"], e2e["generated"], launches], dist)
+    eng.close()
+
+    # ---------------- the same workload in fast numerics: every projection a tcgen05 GEMM over the
+    # step's items (fp16 head/tail operands, fp32 accumulation); device-resident like `value`
+    fast = None
+    if not args.no_fast:
+        feng = CudaEngine(archive, device=device, max_seqs=SLOTS, max_len=PROMPT[1] + GEN[1], max_sink=0,
+                          numerics="fast")
+        fstream = torch.cuda.ExternalStream(feng.stream, device=device)
+        feng.sched_load(SLOTS, prompts, gens)
+        feng.sched_step(args.ramp + args.warmup)
+        fp0, fg0, _, _ = feng.sched_status()
+        fl0 = feng.kernel_launches()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(fstream)
+        feng.sched_step(args.steps)
+        f1.record(fstream)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        fms = f0.elapsed_time(f1)
+        fp1, fg1, _, _ = feng.sched_status()
+        flaunch = feng.kernel_launches() - fl0
+        feng.profile(True)
+        feng.sched_step(10)
+        fprof = {k: v for k, v in feng.profile_read().items() if v[1] > 0}
+        feng.profile(False)
+        feng.close()
+        fms_max, fgen_all, fproc_all, _, _, flaunch_all = aggregate([fms, fg1 - fg0, fp1 - fp0, 0.0, 0, flaunch], dist)
+        fast = {"value": round(fgen_all / (fms_max / 1e3), 1), "unit": unit, "ms_per_step": round(fms_max / args.steps, 4),
+                "processed_tokens_per_s": round(fproc_all / (fms_max / 1e3), 1), "generated_tokens": int(fgen_all),
+                "gpu_launches": flaunch_all,
+                "numerics": "fast: projections (Q|K|V|gate, output, engram K|V, vocabulary) as tcgen05 GEMMs with "
+                            "fp16 head/tail operands and fp32 accumulation; norms, attention, routing and selection "
+                            "binary64 as in exact; greedy ids equal to the CPU reference, logits within 1e-3 "
+                            "(tests/test_gpu_fast_engine.py)",
+                "dtype": "fp16x2 (head/tail) -> fp32 GEMMs; f64 elsewhere",
+                "kernel_ms_per_step": {k: round(v[0] / 10, 4) for k, v in fprof.items()},
+                "roofline_gemm": gemm_roofline(fprof, SLOTS, peaks)}
     if rank == 0:
         value = gen_all / (ms_max / 1e3)
         line = {"metric": metric, "value": round(value, 1), "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
@@ -926,9 +1003,14 @@ def main():
                 "e2e": {"value": round(e2e_gen / (e2e_ms / 1e3), 1), "unit": unit,
                         "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"], "steps": e2e_steps},
                 "gpu_launches": launches_all,
-                "roofline": roofline_for(prof, SLOTS, peaks),
+                "roofline": roofline_for(prof, SLOTS, peaks, visible=visible,
+                                         sm_mhz=(clocks or {}).get("sm_mhz")),
                 "kernel_ms_per_step": {k: round(v[0] / 10, 4) for k, v in prof.items()},
+                "kernel_ms_per_step_note": "event-timed per launch with the micro-batches run one after another "
+                                           "(their sum exceeds ms_per_step, where they overlap)",
                 "clocks": clocks}
+        if fast is not None:
+            line["fast"] = fast
         if world == 1 and not args.no_cpu_baseline:
             r = cpu_reference()
             line["cpu_baseline"] = {"value": round(r["value"], 3), "unit": unit, "cores": r["threads"], "kind": "port",
@@ -936,10 +1018,27 @@ def main():
                                               f"({r['processed']} tokens, {r['seconds']:.1f} s wall), C++ restatement "
                                               f"of the reference CPU backend"}
         print(json.dumps(line), flush=True)
-    eng.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def gemm_roofline(prof, n_items, peaks):
+    """Tensor roofline of the fast step's GEMMs: algorithmic flops per step (2 x rows x 512 inputs x
+    items for Q|K|V|gate and the output projection of every layer, the engram K|V and the vocabulary)
+    over their event-timed time per step, against the measured dense bf16 GEMM peak (fp16 runs at the
+    same rate; the pipe executes four fp16 products per weight x activation pair)."""
+    layers, sites = 27, 2
+    flops = 2 * n_items * 512 * (layers * (1536 + 512) + sites * 1024 + 8192)
+    ms = sum(prof.get(k, (0.0, 0))[0] for k in ("gemv_qkvg", "gemv_o", "gemv_engram", "gemv_vocab")) / 10
+    if ms <= 0:
+        return None
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak = float((peaks or {}).get("bf16_tflops") or 1590.0)
+    return {"kernel": "k_cq_gemm_tc (+ k_cq_prep_f16, k_splitk_sum)", "bound": "tensor", "achieved": round(tflops, 2),
+            "executed": round(4 * tflops, 2), "peak": peak,
+            "peak_source": "measured" if (peaks or {}).get("bf16_tflops") else "fallback", "unit": "TFLOP/s",
+            "frac": round(tflops / peak, 5), "gemm_ms_per_step": round(ms, 4), "flops_per_step": flops}
 
 
 def host_driven(eng, stream, prompts, gens, ramp, warmup, steps):
