@@ -45,8 +45,12 @@ enum {
   NEEDLE_NUMERICS_EXACT = 0, /* binary64 in reference order: bit-faithful to the CPU backend */
   NEEDLE_NUMERICS_FAST = 1,  /* the projections (Q|K|V|gate, output, engram K|V, vocabulary) as
                                 tcgen05 tensor-core GEMMs over the step's items, fp16 head/tail
-                                split with fp32 accumulation (binary32-level accuracy); everything
-                                else as in exact numerics; int8 KV cache only */
+                                split with fp32 accumulation (binary32-level accuracy), and the
+                                layer's norm sums as block reductions; attention, routing and
+                                selection as in exact numerics; int8 KV cache only.  Same greedy
+                                ids as the CPU backend, logits within 1e-3 */
+  NEEDLE_NUMERICS_FAST_ATTENTION = 2, /* NEEDLE_NUMERICS_FAST plus attention on the int8-MMA kernel
+                                (binary32 online softmax over the int8 cache): logits within 3e-3 */
   NEEDLE_KV_INT8 = 0,        /* RuntimeOptions.kvCache "int8" (runtime.ts:30-32) */
   NEEDLE_KV_FLOAT32 = 1      /* RuntimeOptions.kvCache "float32": keys / values stored as given */
 };
@@ -58,7 +62,7 @@ typedef struct needle_opts {
   int32_t max_len;      /* largest maximumLength a slot accepts (<= geometry max sequence) */
   int32_t max_sink;     /* largest sinkLength a slot accepts */
   int32_t kv_mode;      /* NEEDLE_KV_INT8 or NEEDLE_KV_FLOAT32, for every slot of the context */
-  int32_t numerics;     /* NEEDLE_NUMERICS_EXACT or NEEDLE_NUMERICS_FAST */
+  int32_t numerics;     /* NEEDLE_NUMERICS_EXACT, _FAST or _FAST_ATTENTION */
   int32_t micro_batches; /* device-scheduled steps run as this many micro-batches on their own
                             streams (1..8; 0 = the default, 4), so latency-bound kernels of one
                             overlap the others' */

@@ -42,12 +42,14 @@ class CudaEngine:
                  max_sink: int = 160, kv_cache: str = "int8", numerics: str = "exact", micro_batches: int = 0):
         if kv_cache not in ("int8", "float32"):
             raise NeedleError("BACKEND_UNAVAILABLE", f"unknown kvCache {kv_cache!r}")
-        if numerics not in ("exact", "fast"):
+        modes = {"exact": native.NUMERICS_EXACT, "fast": native.NUMERICS_FAST,
+                 "fast_attention": native.NUMERICS_FAST_ATTENTION}
+        if numerics not in modes:
             raise NeedleError("BACKEND_UNAVAILABLE", f"unknown numerics {numerics!r}")
         self._archive = np.frombuffer(archive, dtype=np.uint8)
         opts = native.default_opts(device=device, max_seqs=max_seqs, max_len=max_len, max_sink=max_sink,
                                    kv_mode=native.KV_FLOAT32 if kv_cache == "float32" else native.KV_INT8,
-                                   numerics=native.NUMERICS_FAST if numerics == "fast" else native.NUMERICS_EXACT,
+                                   numerics=modes[numerics],
                                    micro_batches=micro_batches)
         self.numerics = numerics
         self.kv_cache = kv_cache

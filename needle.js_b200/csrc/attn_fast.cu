@@ -57,7 +57,7 @@ __device__ __forceinline__ void codes16(const uint4 u, float* out) {
 __global__ void __launch_bounds__(kFastThreads) k_attention_fast(
     const float* __restrict__ q, const int8_t* __restrict__ kc, const float* __restrict__ ks,
     const int8_t* __restrict__ vc, const float* __restrict__ vs, const int32_t* __restrict__ counts,
-    int32_t capacity, int32_t splits, Partial* __restrict__ partials) {
+    int32_t capacity, int32_t splits, Partial* __restrict__ partials, const int64_t* __restrict__ row_base) {
   __shared__ Partial warp_part[kFastThreads / 32];
   const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
   const int count = min(max(counts[b], 0), capacity);
@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(kFastThreads) k_attention_fast(
 #pragma unroll
     for (int d = 0; d < 16; d++) qr[hh][d] = qb[hh * kHeadDim + d] * (0.125f * kLog2e);
 
-  const int64_t head_row = ((int64_t)b * kKvHeads + h) * capacity;
+  const int64_t head_row = (row_base ? row_base[b] : (int64_t)b * kKvHeads * capacity) + (int64_t)h * capacity;
   const uint4* krows = reinterpret_cast<const uint4*>(kc + head_row * kHeadDim);
   const uint4* vrows = reinterpret_cast<const uint4*>(vc + head_row * kHeadDim);
   const float* ksc = ks + head_row;
@@ -361,7 +361,8 @@ __global__ void __launch_bounds__(kMmaThreads) k_attention_fast_mma(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const float* __restrict__ q,
     const float* __restrict__ ks, const float* __restrict__ vs, const int32_t* __restrict__ counts,
     int32_t capacity, int32_t splits, int32_t n_items, Partial* __restrict__ partials, int32_t* __restrict__ status,
-    int32_t* __restrict__ work, int32_t* __restrict__ done, uint32_t* __restrict__ wait_words) {
+    int32_t* __restrict__ work, int32_t* __restrict__ done, uint32_t* __restrict__ wait_words,
+    const int64_t* __restrict__ row_base) {
   extern __shared__ unsigned char smem_raw[];
   MmaStage* stage = reinterpret_cast<MmaStage*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[kMmaStages], empty[kMmaStages];
@@ -402,7 +403,8 @@ __global__ void __launch_bounds__(kMmaThreads) k_attention_fast_mma(
         }
         const int t_end = min(count, t_begin + kSplit);
         const int ntiles = (t_end - t_begin + kMmaTile - 1) / kMmaTile;
-        const int64_t head_row = (int64_t)bh * capacity;
+        const int64_t head_row =
+            (row_base ? row_base[b] : (int64_t)b * kKvHeads * capacity) + (int64_t)(bh % kKvHeads) * capacity;
         for (int ti = 0; ti < ntiles && ok; ti++, seq++) {
           int sidx;
           if (!(ok = next_stage(sidx))) break;
@@ -678,7 +680,8 @@ size_t attention_fast_scratch_bytes(int32_t batch, int32_t capacity) {
 
 cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
                                   const float* vs, const int32_t* counts, int32_t batch, int32_t capacity,
-                                  float* out, void* scratch, cudaStream_t s) {
+                                  float* out, void* scratch, cudaStream_t s, const int64_t* row_base,
+                                  int64_t cache_rows) {
   if (batch <= 0) return cudaSuccess;
   const int splits = (capacity + kSplit - 1) / kSplit;
   int32_t* status = static_cast<int32_t*>(scratch);
@@ -689,7 +692,7 @@ cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float*
   cudaError_t e = cudaSuccess;
   // The tensor and bulk copies need 16-byte aligned sources and sizes: rows are 64 bytes, and the
   // scale copies are whole 16-byte units when capacity is a multiple of 4.
-  const int64_t rows_total = (int64_t)batch * kKvHeads * capacity;
+  const int64_t rows_total = row_base ? cache_rows : (int64_t)batch * kKvHeads * capacity;
   const bool aligned = capacity % 4 == 0 && rows_total < (1ll << 31) &&
                        ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc) |
                          reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs) |
@@ -716,10 +719,10 @@ cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float*
     const int grid = std::max(1, std::min(n_items, sms * per_sm[device & 63]));
     k_attention_fast_mma<<<grid, kMmaThreads, smem, s>>>(kmap, vmap, q, ks, vs, counts, capacity, splits, n_items,
                                                          parts, status, status + 1, status + 2,
-                                                         wait_status_words(device));
+                                                         wait_status_words(device), row_base);
   } else {
     k_attention_fast<<<dim3(batch, kKvHeads, splits), kFastThreads, 0, s>>>(q, kc, ks, vc, vs, counts, capacity,
-                                                                           splits, parts);
+                                                                           splits, parts, row_base);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;

@@ -62,11 +62,11 @@ cudaError_t launch_cq_gemv_fast(const uint8_t* packed, const uint16_t* norms, in
                                 float* partials, cudaStream_t s);
 // Batched fast-numerics matvec on the tensor cores (cq_gemm_tc.cu): fp16 head/tail split GEMM,
 // record widths 2, 3, 4 and ternary.  Scratch (cq_gemm_tc_scratch_bytes, 256-byte aligned): the
-// prepared activations and split-K partials; up to 128 items per pass.
+// split activations and split-K partials; items are tiled over CTAs (tiles of 16-128).
 constexpr int kTcMinBatch = 16;
 bool cq_gemm_tc_supported(int32_t bits);
 // Split-K factor of the GEMM for a matrix (1: no partials and no split-K sum kernel).
-int cq_gemm_tc_splits(int32_t rows, int32_t input_size, int32_t sms);
+int cq_gemm_tc_splits(int32_t rows, int32_t input_size, int32_t batch, int32_t sms);
 bool cq_gemm_tc_preferred(int32_t rows, int32_t input_size, int32_t batch);
 size_t cq_gemm_tc_scratch_bytes(int32_t rows, int32_t input_size, int32_t batch, int32_t sms);
 // x: rows of x_stride floats, raw (prepared = 0: each group is prepared here) or already prepared

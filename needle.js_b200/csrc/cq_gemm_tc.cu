@@ -183,22 +183,27 @@ __device__ __forceinline__ void split2(float v0, float v1, uint32_t& hi, uint32_
 // [group][half (2)][2N rows: N head rows, N tail rows][128 bytes], rows swizzled as the MMA's
 // K-major 128-byte layout.  One warp per (group, item); items nb <= n < N are zeros.
 // `prepared` inputs are x' already (padded to whole groups); otherwise each group is prepared here.
+// Items form tiles of N (the GEMM's item tiles), tile t at act + t * groups * 2 * 2N * 128; items
+// past `batch` in the last tile are zeros.  One warp per (item slot, group).
 __global__ void __launch_bounds__(256) k_cq_prep_f16(const float* __restrict__ x, int32_t x_stride, int32_t input_size,
-                                                      int32_t groups, int32_t nb, int32_t N, int32_t prepared,
-                                                      uint8_t* __restrict__ act) {
+                                                      int32_t groups, int32_t batch, int32_t N, int32_t tiles,
+                                                      int32_t prepared, uint8_t* __restrict__ act_all) {
   const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (w >= groups * N) return;
-  const int g = w / N, n = w - g * N;
+  if (w >= groups * N * tiles) return;
+  const int item = w / groups, g = w - item * groups;
+  const int t = item / N, n = item - t * N;
+  uint8_t* act = act_all + (size_t)t * groups * 2 * (2 * N) * 128;
   float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  if (n < nb) {
+  if (item < batch) {
+    x += (int64_t)item * x_stride;
     if (prepared) {
-      const float4 p4 = __ldg(reinterpret_cast<const float4*>(x + (int64_t)n * x_stride + g * kGroup + 4 * lane));
+      const float4 p4 = __ldg(reinterpret_cast<const float4*>(x + g * kGroup + 4 * lane));
       v[0] = p4.x;
       v[1] = p4.y;
       v[2] = p4.z;
       v[3] = p4.w;
     } else {
-      prepare_group_warp(x + (int64_t)n * x_stride, input_size, g, v);
+      prepare_group_warp(x, input_size, g, v);
     }
   }
   uint32_t hi[2], lo[2];
@@ -213,7 +218,7 @@ __global__ void __launch_bounds__(256) k_cq_prep_f16(const float* __restrict__ x
 template <int BITS>
 __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
     const uint8_t* __restrict__ packed, const uint16_t* __restrict__ norms, int32_t rows, int32_t groups,
-    int32_t row_bytes, const uint8_t* __restrict__ act, int32_t N, int32_t nb, int32_t groups_per_split,
+    int32_t row_bytes, const uint8_t* __restrict__ act_all, int32_t N, int32_t batch, int32_t groups_per_split,
     float* __restrict__ out, int32_t out_stride, int64_t split_stride, Codebook cb, uint32_t* __restrict__ wait_words) {
   constexpr int kCodes = BITS == 4 ? 16 : BITS == 3 ? 8 : 4;
   constexpr int kGroupWords = BITS == 4 ? 16 : BITS == 3 ? 12 : 8;  // packed 32-bit words of one row's group
@@ -227,7 +232,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
   __shared__ float lut[16];
   __shared__ int s_failed;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int mt = blockIdx.x, split = blockIdx.y;
+  const int mt = blockIdx.x, split = blockIdx.y, zt = blockIdx.z;  // row tile, K split, item tile
+  const int nb = min(N, batch - zt * N);                              // items of this tile
+  const uint8_t* act = act_all + (size_t)zt * groups * 2 * (2 * N) * 128;
   const int g_begin = split * groups_per_split, g_end = min(groups, g_begin + groups_per_split);
   const int ng = g_end - g_begin;
   const int nslots = kTcSlotsUsed;
@@ -462,7 +469,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const bool bad = !acc_ok || *(volatile int*)&s_failed != 0;
     if (bad && lane == 0) report_wait_timeout(wait_words, kWaitTensorGemm);
-    float* o = out + (int64_t)split * split_stride;
+    float* o = out + (int64_t)split * split_stride + (int64_t)zt * N * out_stride;
     for (int c0 = team * 8; c0 < N; c0 += kTcTeams * 8) {
       uint32_t v[8], w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       tmem_ld8(lane_addr + (uint32_t)c0, v);
@@ -496,14 +503,39 @@ __global__ void k_splitk_sum(const float* __restrict__ part, int32_t splits, int
 }
 
 struct TcPlan {
-  int m_tiles, groups, per, used;
+  int m_tiles, groups, per, used;  // row tiles, groups, groups per split, splits
+  int N, z;                        // items per tile (MMA N) and item tiles
 };
 
-TcPlan plan_for(int32_t rows, int32_t in_pad, int sms) {
+// Rows of at most kTcGroupSplitMax groups (the engine's 512-input projections) accumulate each
+// group separately -- one group per CTA, split-K -- and k_splitk_sum adds the groups' partials with
+// IEEE binary32 adds in a fixed order: the tensor pipe's fp32 accumulation over a whole 512-input row
+// (32 MMAs into one accumulator) measured 1.9e-6 relative error against 1.2e-7 per group, and the
+// decode step amplifies that difference past the 1e-3 logits bar.  The item tile (16, 32, 64, 128)
+// is then the smallest that keeps the grid within one CTA per SM.  Longer rows take all items in
+// one tile (up to 128; a second tile would decode every weight again) and split K over the SMs.
+constexpr int kTcGroupSplitMax = 8;
+
+TcPlan plan_for(int32_t rows, int32_t in_pad, int32_t batch, int sms) {
   TcPlan p;
   p.m_tiles = (rows + kTcM - 1) / kTcM;
   p.groups = in_pad / kGroup;
-  const int splits = std::max(1, std::min(p.groups, sms / p.m_tiles));
+  int splits;
+  if (p.groups <= kTcGroupSplitMax) {
+    const int64_t per_tile = (int64_t)p.m_tiles * p.groups;
+    p.N = kTcMaxN;
+    for (int n = 16; n <= kTcMaxN; n *= 2)
+      if (per_tile * ((batch + n - 1) / n) <= sms) {
+        p.N = n;
+        break;
+      }
+    splits = p.groups;
+  } else {
+    p.N = kTcMaxN;
+    splits = std::max(1, std::min(p.groups, sms / p.m_tiles));
+  }
+  p.N = std::min(p.N, std::max(16, (batch + 15) / 16 * 16));
+  p.z = (batch + p.N - 1) / p.N;
   p.per = (p.groups + splits - 1) / splits;
   p.used = (p.groups + p.per - 1) / p.per;
   return p;
@@ -511,8 +543,8 @@ TcPlan plan_for(int32_t rows, int32_t in_pad, int sms) {
 
 }  // namespace
 
-int cq_gemm_tc_splits(int32_t rows, int32_t input_size, int32_t sms) {
-  return plan_for(rows, (input_size + kGroup - 1) / kGroup * kGroup, sms).used;
+int cq_gemm_tc_splits(int32_t rows, int32_t input_size, int32_t batch, int32_t sms) {
+  return plan_for(rows, (input_size + kGroup - 1) / kGroup * kGroup, batch, sms).used;
 }
 
 bool cq_gemm_tc_supported(int32_t bits) { return bits == 2 || bits == 3 || bits == 4 || bits == kTernaryBits; }
@@ -526,11 +558,9 @@ bool cq_gemm_tc_preferred(int32_t rows, int32_t input_size, int32_t batch) {
 
 size_t cq_gemm_tc_scratch_bytes(int32_t rows, int32_t input_size, int32_t batch, int32_t sms) {
   const int in_pad = (input_size + kGroup - 1) / kGroup * kGroup;
-  const int nb = std::min(batch, kTcMaxN);
-  const int N = (nb + 15) / 16 * 16;
-  const TcPlan p = plan_for(rows, in_pad, sms);
-  const size_t act = (size_t)p.groups * 2 * (2 * N) * 128;
-  const size_t part = p.used > 1 ? (size_t)p.used * nb * rows * 4 : 0;
+  const TcPlan p = plan_for(rows, in_pad, batch, sms);
+  const size_t act = (size_t)p.z * p.groups * 2 * (2 * p.N) * 128;
+  const size_t part = p.used > 1 ? (size_t)p.used * batch * rows * 4 : 0;
   return act + part;
 }
 
@@ -541,46 +571,42 @@ cudaError_t launch_cq_gemm_tc(const uint8_t* packed, const uint16_t* norms, int3
   const int in_pad = (input_size + kGroup - 1) / kGroup * kGroup;
   const int pb = bits == kTernaryBits ? 2 : bits;
   const int row_bytes = in_pad * pb / 8;
-  const TcPlan p = plan_for(rows, in_pad, sms);
+  const TcPlan p = plan_for(rows, in_pad, batch, sms);
+  const int N = p.N;
   uint8_t* act = static_cast<uint8_t*>(scratch);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   uint32_t* wait_words = wait_status_words(dev);
-  for (int b0 = 0; b0 < batch; b0 += kTcMaxN) {
-    const int nb = std::min(kTcMaxN, batch - b0);
-    const int N = (nb + 15) / 16 * 16;
-    const size_t act_bytes = (size_t)p.groups * 2 * (2 * N) * 128;
-    const int warps = p.groups * N;
-    k_cq_prep_f16<<<(warps + 7) / 8, 256, 0, s>>>(x + (int64_t)b0 * x_stride, x_stride, input_size, p.groups, nb, N,
-                                                  prepared, act);
+  const int64_t warps = (int64_t)p.groups * N * p.z;
+  k_cq_prep_f16<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(x, x_stride, input_size, p.groups, batch, N, p.z, prepared,
+                                                           act);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const size_t act_bytes = (size_t)p.z * p.groups * 2 * (2 * N) * 128;
+  float* part = reinterpret_cast<float*>(act + act_bytes);
+  const int64_t split_stride = (int64_t)batch * rows;  // partials [split][item][row]
+  const size_t smem = std::max(kTcMinSmem, (size_t)kTcSlotsUsed * 2 * (2 * N) * 128 + kTcTableBytes + 1024);
+  auto launch = [&](auto kernel) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return;
+    float* o = p.used > 1 ? part : y;
+    kernel<<<dim3(p.m_tiles, p.used, p.z), kTcThreads, smem, s>>>(packed, norms, rows, p.groups, row_bytes, act, N, batch,
+                                                                 p.per, o, p.used > 1 ? rows : y_stride, split_stride, cb,
+                                                                 wait_words);
+    e = cudaGetLastError();
+  };
+  if (bits == 4) launch(k_cq_gemm_tc<4>);
+  else if (bits == 3) launch(k_cq_gemm_tc<3>);
+  else if (bits == 2) launch(k_cq_gemm_tc<2>);
+  else if (bits == kTernaryBits) launch(k_cq_gemm_tc<kTernaryBits>);
+  else return cudaErrorInvalidValue;
+  if (e != cudaSuccess) return e;
+  if (p.used > 1) {
+    const int64_t n = (int64_t)rows * batch;
+    k_splitk_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, p.used, split_stride, rows, batch, y, y_stride);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    float* part = reinterpret_cast<float*>(act + act_bytes);
-    const int64_t split_stride = (int64_t)nb * rows;
-    const size_t smem = std::max(kTcMinSmem, (size_t)kTcSlotsUsed * 2 * (2 * N) * 128 + kTcTableBytes + 1024);
-    auto launch = [&](auto kernel) {
-      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return;
-      float* o = p.used > 1 ? part : y + (int64_t)b0 * y_stride;
-      kernel<<<dim3(p.m_tiles, p.used), kTcThreads, smem, s>>>(packed, norms, rows, p.groups, row_bytes, act, N, nb,
-                                                              p.per, o, p.used > 1 ? rows : y_stride, split_stride, cb,
-                                                              wait_words);
-      e = cudaGetLastError();
-    };
-    if (bits == 4) launch(k_cq_gemm_tc<4>);
-    else if (bits == 3) launch(k_cq_gemm_tc<3>);
-    else if (bits == 2) launch(k_cq_gemm_tc<2>);
-    else if (bits == kTernaryBits) launch(k_cq_gemm_tc<kTernaryBits>);
-    else return cudaErrorInvalidValue;
-    if (e != cudaSuccess) return e;
-    if (p.used > 1) {
-      const int64_t n = (int64_t)rows * nb;
-      k_splitk_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, p.used, split_stride, rows, nb,
-                                                              y + (int64_t)b0 * y_stride, y_stride);
-      e = cudaGetLastError();
-      if (e != cudaSuccess) return e;
-    }
   }
   return cudaSuccess;
 }

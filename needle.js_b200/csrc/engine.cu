@@ -357,10 +357,12 @@ struct needle_ctx {
   // Fast numerics (NEEDLE_NUMERICS_FAST): Q|K|V|gate of each layer and K|V of each engram site as
   // one matrix each (one GEMM per shared input), and per micro-batch lane the GEMM's scratch.
   bool fast = false;
+  bool fast_attention = false;  // NEEDLE_NUMERICS_FAST_ATTENTION: also the int8-MMA attention
   int sms = 0;
   std::vector<CqMat> lqkvg, ekv;
   void* gemm_scratch[kMaxMicro] = {};
   size_t gemm_scratch_bytes = 0;
+  void* attn_scratch[kMaxMicro] = {};  // the int8-MMA attention's partials and counters, per lane
   int32_t* d_counts = nullptr;  // [0] n_items, [1] n_select
   std::vector<SlotHost> slots;
   // pinned staging
@@ -606,6 +608,7 @@ void build_model(needle_ctx& C) {
     C.lg.push_back(C.cq[Lr.gate]);
     C.lo.push_back(C.cq[Lr.o]);
   }
+  m.fast = C.fast ? 1 : 0;
   if (C.fast) {
     for (int l = 0; l < L; l++) C.lqkvg.push_back(stack_rows(C, {C.lq[l], C.lk[l], C.lv[l], C.lg[l]}));
     for (int s = 0; s < m.n_sites; s++) C.ekv.push_back(stack_rows(C, {C.ek[s], C.ev[s]}));
@@ -747,12 +750,24 @@ void build_state(needle_ctx& C) {
   cuda_check(cudaMallocHost(&C.h_logprob, B * sizeof(double)), "cudaMallocHost");
   cuda_check(configure_step_kernels(capacity), "cudaFuncSetAttribute");
   if (C.fast) {
+    // the GEMM's tiling depends on the item count: size for every count a launch can have
+    std::vector<const CqMat*> mats{&C.lqkvg[0], &C.lo[0], &m.embedding};
+    if (!C.ekv.empty()) mats.push_back(&C.ekv[0]);
     size_t bytes = 0;
-    for (const CqMat* M : std::initializer_list<const CqMat*>{&C.lqkvg[0], &C.lo[0], &m.embedding})
-      bytes = std::max(bytes, cq_gemm_tc_scratch_bytes(M->rows, M->input_size, int(B), C.sms));
-    if (!C.ekv.empty()) bytes = std::max(bytes, cq_gemm_tc_scratch_bytes(C.ekv[0].rows, C.ekv[0].input_size, int(B), C.sms));
+    for (const CqMat* M : mats)
+      for (int n = 1; n <= int(B); n++) bytes = std::max(bytes, cq_gemm_tc_scratch_bytes(M->rows, M->input_size, n, C.sms));
     C.gemm_scratch_bytes = (bytes + 255) & ~size_t(255);
     for (int k = 0; k < kMaxMicro; k++) C.gemm_scratch[k] = C.dalloc<uint8_t>(C.gemm_scratch_bytes, false);
+  }
+  if (C.fast_attention) {
+    // int8-MMA attention: rotated queries, visible counts, cache rows, outputs; per lane its scratch
+    // (status and work counters zeroed here, left at zero by every call)
+    st.qrope = C.dalloc<float>(B * kDim);
+    st.attn_out = C.dalloc<float>(B * kDim);
+    st.attn_count = C.dalloc<int32_t>(B);
+    st.attn_row = C.dalloc<int64_t>(B);
+    for (int k = 0; k < kMaxMicro; k++)
+      C.attn_scratch[k] = C.dalloc<uint8_t>(attention_fast_scratch_bytes(int32_t(B), capacity));
   }
 }
 
@@ -793,9 +808,8 @@ void run_gemv(needle_ctx& C, int cls, const std::vector<JobSpec>& specs, int n_h
   if (C.fast) {
     for (const auto& sp : specs) {
       const CqMat& M = sp.M;
-      const int passes = (n_host + 127) / 128;
-      const int splits = cq_gemm_tc_splits(M.rows, M.input_size, C.sms);
-      C.launches += passes * (splits > 1 ? 3 : 2) - 1;  // timed() counts one
+      const int splits = cq_gemm_tc_splits(sp.rows, M.input_size, n_host, C.sms);
+      C.launches += (splits > 1 ? 3 : 2) - 1;  // prepare, GEMM, split-K sum; timed() counts one
       C.timed(cls, [&] {
         return launch_cq_gemm_tc(M.packed + int64_t(sp.row_start) * M.row_bytes,
                                  M.norms + int64_t(sp.row_start) * (M.in_pad / kGroup), sp.rows, M.input_size, M.bits,
@@ -848,6 +862,12 @@ StepView half_view(const needle_ctx& C, int offset, const int32_t* n_items, cons
   v.logits = st.logits + o * C.mv.vocab;
   v.out_id = st.out_id + o;
   v.out_logprob = st.out_logprob + o;
+  if (st.qrope) {
+    v.qrope = st.qrope + o * kDim;
+    v.attn_out = st.attn_out + o * kDim;
+    v.attn_count = st.attn_count + o;
+    v.attn_row = st.attn_row + o;
+  }
   return v;
 }
 
@@ -902,7 +922,20 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
                 {C.lv[l], 0, 256, st.prep_a, kDim, st.qkvg + 768, 1536},
                 {C.lg[l], 0, 512, st.prep_a, kDim, st.qkvg + 1024, 1536}},
                n_host, n_dev, s0);
-    if (st.chunk) {  // every item's K/V before any item attends
+    if (C.fast_attention) {
+      // append every item's K/V (and leave its rotated query, count and cache row), then the
+      // int8-MMA attention over the cache and the gate
+      const int64_t cache_rows = int64_t(C.opts.max_seqs) * m.layers * kKvHeads * sv.capacity;
+      C.launches += 3;  // + persistent attention, combine, gate (timed() counts the append)
+      C.timed(P_ATTN, [&] {
+        cudaError_t e = launch_attention(m, sv, st, l, n_host, s0, 1);
+        if (e == cudaSuccess)
+          e = launch_attention_fast(st.qrope, sv.kcodes, sv.kscale, sv.vcodes, sv.vscale, st.attn_count, n_host,
+                                    sv.capacity, st.attn_out, C.attn_scratch[lane.index], s0, st.attn_row, cache_rows);
+        if (e == cudaSuccess) e = launch_attention_gate(st, n_host, s0);
+        return e;
+      }, s0);
+    } else if (st.chunk) {  // every item's K/V before any item attends
       C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 1); }, s0);
       C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 2); }, s0);
     } else {
@@ -1260,8 +1293,9 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
     const needle_opts& o = C->opts;
     require(o.kv_mode == NEEDLE_KV_INT8 || o.kv_mode == NEEDLE_KV_FLOAT32, NEEDLE_BACKEND_UNAVAILABLE,
             "kv_mode must be NEEDLE_KV_INT8 or NEEDLE_KV_FLOAT32");
-    require(o.numerics == NEEDLE_NUMERICS_EXACT || o.numerics == NEEDLE_NUMERICS_FAST, NEEDLE_BACKEND_UNAVAILABLE,
-            "unknown numerics mode");
+    require(o.numerics == NEEDLE_NUMERICS_EXACT || o.numerics == NEEDLE_NUMERICS_FAST ||
+                o.numerics == NEEDLE_NUMERICS_FAST_ATTENTION,
+            NEEDLE_BACKEND_UNAVAILABLE, "unknown numerics mode");
     require(o.numerics == NEEDLE_NUMERICS_EXACT || o.kv_mode == NEEDLE_KV_INT8, NEEDLE_BACKEND_UNAVAILABLE,
             "fast numerics runs on the int8 KV cache");
     require(o.max_seqs >= 1 && o.max_seqs <= 65536, NEEDLE_BACKEND_UNAVAILABLE, "max_seqs out of range");
@@ -1301,7 +1335,8 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
     }
     cuda_check(cudaEventCreateWithFlags(&C->split_ev, cudaEventDisableTiming), "cudaEventCreate");
     if (o.micro_batches > 0) C->micro = std::min(kMaxMicro, int(o.micro_batches));
-    C->fast = o.numerics == NEEDLE_NUMERICS_FAST;
+    C->fast = o.numerics == NEEDLE_NUMERICS_FAST || o.numerics == NEEDLE_NUMERICS_FAST_ATTENTION;
+    C->fast_attention = o.numerics == NEEDLE_NUMERICS_FAST_ATTENTION;
     cuda_check(cudaDeviceGetAttribute(&C->sms, cudaDevAttrMultiProcessorCount, C->device), "device attribute");
     build_model(*C);
     build_state(*C);

@@ -39,6 +39,7 @@ struct ModelView {
   const float* probe_proj;  // [probe_out][probe_count * 512]
   const float* probe_bias;  // [probe_out]
   int32_t probe_count, probe_out;
+  int32_t fast;             // NEEDLE_NUMERICS_FAST: block-reduced sums in k_layer
 };
 
 // Per-slot sequence state (NeedleRuntime fields, runtime.ts:113-133), device-authoritative.
@@ -116,6 +117,11 @@ struct StepView {
   // selecting.  Their lanes are per item (`lanes`) instead of per slot, K/V are appended for the
   // whole chunk before any item attends, and the slot's state (position, token history, engram
   // ring) advances once, after the chunk.
+  // fast numerics: what the append pass (k_attention part 1) leaves for the int8-MMA attention
+  float* qrope;             // [B][512] normalised, rotated queries
+  float* attn_out;          // [B][512] attention output (before the gate)
+  int32_t* attn_count;      // [B] visible cache slots: slots 0 .. count-1 in the ring layout
+  int64_t* attn_row;        // [B] cache row of (item, layer, KV head 0)
   int32_t chunk;
   float* lanes;             // [B][4][512] (chunk steps; kItemLanes items)
   const uint32_t* engram_in;  // [B][2][kMaxTables]: table indices, then valid flags (kItemEngrams)
@@ -160,9 +166,16 @@ cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* 
 size_t attention_smem_bytes(int32_t capacity, bool ring);
 // Fast-numerics attention (attn_fast.cu): scratch holds the split partials.
 size_t attention_fast_scratch_bytes(int32_t batch, int32_t capacity);
+// row_base (optional, per item): the cache row of (item, KV head 0), head h at + h * capacity, in
+// a cache of cache_rows rows of 64 codes (the engine's [slot][layer][head][capacity] blocks);
+// without it item b's rows are b * kv_heads * capacity onwards.
 cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
                                   const float* vs, const int32_t* counts, int32_t batch, int32_t capacity,
-                                  float* out, void* scratch, cudaStream_t s);
+                                  float* out, void* scratch, cudaStream_t s, const int64_t* row_base = nullptr,
+                                  int64_t cache_rows = 0);
+// Fast numerics, after launch_attention (part 1) and launch_attention_fast: attention output times
+// sigmoid(gate) and the output projection's prepared input, per (item, KV head).
+cudaError_t launch_attention_gate(const StepView& st, int n_host, cudaStream_t s);
 // Online probe pool (OnlineProbePool.add, runtime.ts:60-90) of the step's collecting items: source 0
 // is the scaled embedding (lane 0 after k_embed), source 1 the mean of the lanes (after a layer).
 cudaError_t launch_probe_add(const ModelView& m, const SlotView& sv, const StepView& st, int source, int n_host,

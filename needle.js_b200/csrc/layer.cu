@@ -170,6 +170,7 @@ struct LayerSmem {
   float hpre[kLanes], hpost[kLanes], routing[16];
   double red[4];
   double sk[16];            // routing logits (Float64Array of the Float32Array, math.ts:64)
+  double part[kThreads / 32];  // block reductions (fast numerics)
 };
 
 __device__ void engram_mix(const ModelView& m, const SlotView& sv, const StepView& st, int b,
@@ -307,6 +308,33 @@ __device__ __forceinline__ double inverse_rms_of(const double* terms, int n) {
   return 1.0 / sqrt(sum_seq(terms, n) / (double)n + 1e-6);
 }
 
+// Fast numerics: the same sums as binary64 tree reductions over the whole block (every thread
+// calls it; `part` is kThreads / 32 doubles of shared scratch).  They differ from the sequential
+// sums only in the last bits of a binary64 value (~1e-16 relative).
+__device__ __forceinline__ double block_sum(const double* terms, int n, double* part) {
+  const int tid = threadIdx.x;
+  double v = 0.0;
+  for (int i = tid; i < n; i += kThreads) v += terms[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((tid & 31) == 0) part[tid >> 5] = v;
+  __syncthreads();
+  double t = 0.0;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; w++) t += part[w];
+  return t;
+}
+
+// One binary64 sum of a k_layer phase: the reference's sequential sum by thread 0 (exact
+// numerics; result valid in thread 0) or a block reduction (fast; result valid in every thread).
+template <bool Fast>
+__device__ __forceinline__ double phase_sum(const double* terms, int n, double* part) {
+  if constexpr (Fast) return block_sum(terms, n, part);
+  else return threadIdx.x == 0 ? sum_seq(terms, n) : 0.0;
+}
+
+template <bool Fast>
 __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const SlotView sv, const StepView st,
                                                   int layer) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -342,7 +370,10 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
     }
     S.sq[c] = (double)projected * (double)projected;
     __syncthreads();
-    if (tid == 0) S.red[0] = inverse_rms_of(S.sq, kDim);
+    {
+      const double sum_ = phase_sum<Fast>(S.sq, kDim, S.part);
+      if (tid == 0) S.red[0] = 1.0 / sqrt(sum_ / (double)kDim + 1e-6);
+    }
     __syncthreads();
     // #attentionDelta (runtime.ts:585-611)
     const float normalized =
@@ -351,7 +382,10 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
     const float after = f32((double)blk + attention_scale * (double)normalized);
     S.sq[c] = (double)after * (double)after;
     __syncthreads();
-    if (tid == 0) S.red[1] = inverse_rms_of(S.sq, kDim);
+    {
+      const double sum_ = phase_sum<Fast>(S.sq, kDim, S.part);
+      if (tid == 0) S.red[1] = 1.0 / sqrt(sum_ / (double)kDim + 1e-6);
+    }
     __syncthreads();
     const float pre = f32((1.0 + (double)m.pre_had_norm[(int64_t)l * kDim + c]) * (double)after * S.red[1]);
     // hadamardMlp (math.ts:117-138)
@@ -393,7 +427,10 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
     const float mean = f32(sum / (double)kLanes);
     S.sq[c] = (double)mean * (double)mean;
     __syncthreads();
-    if (tid == 0) S.red[0] = inverse_rms_of(S.sq, kDim);
+    {
+      const double sum_ = phase_sum<Fast>(S.sq, kDim, S.part);
+      if (tid == 0) S.red[0] = 1.0 / sqrt(sum_ / (double)kDim + 1e-6);
+    }
     __syncthreads();
     float f = f32((1.0 + (double)m.final_norm[c]) * (double)mean * S.red[0]);
     f = fwht_reg(f, S.fw, kGroup, kThreads);
@@ -415,7 +452,10 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
     S.lut[which][lev] = lut_level(m.cb.v, bits, lev);
   }
   __syncthreads();
-  if (tid == 0) S.red[2] = inverse_rms_of(S.sq, kLaneWidth);
+  {
+      const double sum_ = phase_sum<Fast>(S.sq, kLaneWidth, S.part);
+      if (tid == 0) S.red[2] = 1.0 / sqrt(sum_ / (double)kLaneWidth + 1e-6);
+    }
   __syncthreads();
   // prepareCqActivation of the phi input: FWHT of each 128-group, * 1/sqrt(128)
 #pragma unroll
@@ -487,14 +527,26 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
     S.sq[c] = (double)upd * (double)upd;
     S.sq2[c] = (double)key * (double)key;
     __syncthreads();
-    if (tid == 0) S.red[0] = inverse_rms_of(S.sq, kDim);
-    if (tid == 32) S.red[1] = inverse_rms_of(S.sq2, kDim);
+    if constexpr (Fast) {
+      const double a_ = block_sum(S.sq, kDim, S.part);
+      const double b_ = block_sum(S.sq2, kDim, S.part);
+      if (tid == 0) {
+        S.red[0] = 1.0 / sqrt(a_ / (double)kDim + 1e-6);
+        S.red[1] = 1.0 / sqrt(b_ / (double)kDim + 1e-6);
+      }
+    } else {
+      if (tid == 0) S.red[0] = inverse_rms_of(S.sq, kDim);
+      if (tid == 32) S.red[1] = inverse_rms_of(S.sq2, kDim);
+    }
     __syncthreads();
     const float ni = f32((double)upd * S.red[0]);
     const float nk = f32((double)key * S.red[1]);
     S.sq[c] = (double)ni * (double)nk;
     __syncthreads();
-    if (tid == 0) S.red[3] = sigmoid_d(sum_seq(S.sq, kDim) / sqrt((double)kDim));
+    {
+      const double dot_ = phase_sum<Fast>(S.sq, kDim, S.part);
+      if (tid == 0) S.red[3] = sigmoid_d(dot_ / sqrt((double)kDim));
+    }
     __syncthreads();
     const float value = st.engram_val[((int64_t)b * m.n_sites + site) * kDim + c];
     blk = f32((double)upd + S.red[3] * (double)value);
@@ -503,7 +555,10 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
   st.block[(int64_t)b * kDim + c] = blk;
   S.sq[c] = (double)blk * (double)blk;
   __syncthreads();
-  if (tid == 0) S.red[0] = inverse_rms_of(S.sq, kDim);
+  {
+      const double sum_ = phase_sum<Fast>(S.sq, kDim, S.part);
+      if (tid == 0) S.red[0] = 1.0 / sqrt(sum_ / (double)kDim + 1e-6);
+    }
   __syncthreads();
   // rmsNorm(blockInput, normInput) then prepareCqActivation for Q/K/V/gate (runtime.ts:441, 465)
   float a = f32((1.0 + (double)m.norm_input[(int64_t)l * kDim + c]) * (double)blk * S.red[0]);
@@ -848,7 +903,20 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
     }
     __syncthreads();
   }
-  if (part == 1) return;
+  if (part == 1) {
+    // fast numerics attends with the int8-MMA kernel next: leave it the rotated queries, the visible
+    // count (slots 0 .. count-1 of the ring hold exactly the visible positions) and the cache row
+    if (st.qrope) {
+      st.qrope[(int64_t)b * kDim + 2 * h * kHeadDim + tid] = qv[tid];
+      if (h == 0 && tid == 0) {
+        const int prefix = min(sink, p + 1);
+        const int recent_low = window > 0 ? max(prefix, p + 1 - window) : prefix;
+        st.attn_count[b] = prefix + (p - recent_low + 1);
+        st.attn_row[b] = head_base;  // KV head 0 of this item's (slot, layer)
+      }
+    }
+    return;
+  }
   // Visible positions (runtime.ts:723-728): [0, prefix) U [recentLow, p].
   const int prefix = min(sink, p + 1);
   const int recent_low = window > 0 ? max(prefix, p + 1 - window) : prefix;
@@ -868,6 +936,21 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
     attend_pair<Sc, Mix, Mc>(C, count, slot_of, qd, e, tile, gt, outv, red);
   }
   // prepareCqActivation of the output projection: heads 2h, 2h+1 are exactly input group h.
+  fwht_smem(outv, kGroup, 1);
+  st.prep_o[(int64_t)b * kDim + h * kGroup + tid] = f32((double)outv[tid] * (1.0 / sqrt((double)kGroup)));
+}
+
+// Fast numerics: attentionOutput * sigmoid(gate) (runtime.ts:503-504) of the int8-MMA attention's
+// output, and the output projection's prepared input (heads 2h, 2h+1 are input group h).
+__global__ void __launch_bounds__(kAttnThreads) k_attention_gate(const StepView st) {
+  __shared__ float outv[2 * kHeadDim];
+  const int b = blockIdx.x, h = blockIdx.y;
+  if (b >= *st.n_items) return;
+  const int tid = threadIdx.x;
+  const float o = st.attn_out[(int64_t)b * kDim + 2 * h * kHeadDim + tid];
+  const float g = st.qkvg[(int64_t)b * 1536 + 1024 + 2 * h * kHeadDim + tid];
+  outv[tid] = f32((double)o * sigmoid_d((double)g));
+  __syncthreads();
   fwht_smem(outv, kGroup, 1);
   st.prep_o[(int64_t)b * kDim + h * kGroup + tid] = f32((double)outv[tid] * (1.0 / sqrt((double)kGroup)));
 }
@@ -1222,7 +1305,10 @@ cudaError_t launch_layer(const ModelView& m, const SlotView& sv, const StepView&
                          int n_host, cudaStream_t s) {
   if (n_host <= 0) return cudaSuccess;
   const size_t smem = sizeof(LayerSmem);
-  k_layer<<<n_host, kThreads, smem, s>>>(m, sv, st, layer);
+  if (m.fast)
+    k_layer<true><<<n_host, kThreads, smem, s>>>(m, sv, st, layer);
+  else
+    k_layer<false><<<n_host, kThreads, smem, s>>>(m, sv, st, layer);
   return cudaGetLastError();
 }
 
@@ -1249,6 +1335,12 @@ cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* 
   return cudaGetLastError();
 }
 
+cudaError_t launch_attention_gate(const StepView& st, int n_host, cudaStream_t s) {
+  if (n_host <= 0) return cudaSuccess;
+  k_attention_gate<<<dim3(n_host, kKvHeads), kAttnThreads, 0, s>>>(st);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_route(const StepView& st, int n_host, cudaStream_t s) {
   if (n_host <= 0) return cudaSuccess;
   k_route<<<n_host, 32, 0, s>>>(st);
@@ -1258,7 +1350,9 @@ cudaError_t launch_route(const StepView& st, int n_host, cudaStream_t s) {
 cudaError_t configure_step_kernels(int32_t capacity) {
   if (sizeof(LayerSmem) > 200 * 1024 || attention_smem_bytes(capacity, true) > 200 * 1024)
     return cudaErrorInvalidValue;
-  cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(k_layer));
+  cudaError_t e = raise_smem_limit(reinterpret_cast<const void*>(k_layer<false>));
+  if (e != cudaSuccess) return e;
+  e = raise_smem_limit(reinterpret_cast<const void*>(k_layer<true>));
   if (e != cudaSuccess) return e;
   e = raise_smem_limit(reinterpret_cast<const void*>(k_attention<kAttnSc, kAttnMix, kAttnMc>));
   if (e != cudaSuccess) return e;

@@ -22,6 +22,7 @@ KV_INT8 = 0
 KV_FLOAT32 = 1
 NUMERICS_EXACT = 0
 NUMERICS_FAST = 1
+NUMERICS_FAST_ATTENTION = 2
 NOALLOC_MAX_FLOATS = 1 << 20  # NEEDLE_NOALLOC_MAX_FLOATS
 WAIT_ATTENTION, WAIT_TABLE_GEMV, WAIT_TENSOR_GEMM, WAIT_SELFTEST = 1, 2, 4, 8  # NEEDLE_WAIT_*
 

@@ -42,7 +42,15 @@ def ref_model(oracle, archive):
     return oracle.Model(archive)
 
 
-def test_config1_fast_logits_and_greedy_ids(archive, oracle, ref_model):
+# NEEDLE_NUMERICS_FAST_ATTENTION also runs attention on the int8-MMA kernel (binary32 online
+# softmax, query and weights as 21-bit integer digits): its outputs differ from the binary64 chain by
+# about 1e-6 relative, which the int8 cache and the layers amplify to about 2.4e-3 in the logits;
+# its stated bar is 3e-3, with the same greedy ids.
+MODES = [("fast", LOGIT_TOL, 0.98), ("fast_attention", 3e-3, 0.95)]
+
+
+@pytest.mark.parametrize("numerics,tol,kv_equal", MODES)
+def test_config1_fast_logits_and_greedy_ids(archive, oracle, ref_model, numerics, tol, kv_equal):
     """128-token prompt (seed 1) prefilled in chunks, 64 greedy steps; the
     oracle's tokens are fed back (teacher forcing) so every step's logits are compared at the same
     state, and the greedy ids of a free run must equal the oracle's."""
@@ -51,7 +59,7 @@ def test_config1_fast_logits_and_greedy_ids(archive, oracle, ref_model):
     prompt = synth.integers(1, 128, ref_model.vocab, stream=0).astype(np.int32)
     steps = 64
     ids_ref, _, logits_ref = ref_model.generate_greedy(prompt, steps, sink=0, want_logits=True)
-    with CudaEngine(archive, device=0, max_seqs=2, max_len=512, max_sink=0, numerics="fast") as eng:
+    with CudaEngine(archive, device=0, max_seqs=2, max_len=512, max_sink=0, numerics=numerics) as eng:
         # teacher forced
         eng.reset(0, len(prompt) + steps, 0)
         lg = eng.prefill(0, prompt, want_logits=True)
@@ -62,7 +70,7 @@ def test_config1_fast_logits_and_greedy_ids(archive, oracle, ref_model):
             if s + 1 < steps:
                 _, l2 = eng.step([StepRequest(0, int(ids_ref[s]), False)], want_logits=True)
                 lg = l2[0]
-        assert worst <= LOGIT_TOL, worst
+        assert worst <= tol, worst
         # free-running greedy with selection on the device
         eng.reset(1, len(prompt) + steps, 0)
         eng.prefill(1, prompt[:-1], want_logits=False)
@@ -83,8 +91,8 @@ def test_config1_fast_logits_and_greedy_ids(archive, oracle, ref_model):
             rkc, rvc, _, _ = rt.read_kv(layer)
             same += int(np.sum(kc == rkc) + np.sum(vc == rvc))
             total += kc.size + vc.size
-        print(f"fast numerics: worst logits max-abs-rel {worst:.2e}, KV codes equal {same / total:.4%}")
-        assert same / total > 0.98
+        print(f"{numerics}: worst logits max-abs-rel {worst:.2e}, KV codes equal {same / total:.4%}")
+        assert same / total > kv_equal
 
 
 def test_scheduler_fast_ids_equal_except_at_near_ties(archive, oracle, ref_model):
