@@ -692,8 +692,9 @@ TOOLCALL_MAX_FIELDS = (0, 5, 6, 11, 12)
 
 def aggregate_toolcall(local, dist=None):
     """Whole-job config-5 totals from this rank's [ms, constrained, prompt, completed, dead ends,
-    steps, grammar s, launches, sequences, h2d, d2h, engine s, wall s]: every rank takes the same two
-    all-reduces (sum and max over the process group)."""
+    steps, grammar s, launches, sequences, h2d, d2h, engine s, wall s, masks put, masked selections,
+    allowed ids sent]: every rank takes the same two all-reduces (sum and max over the process
+    group)."""
     import torch
     if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
         return [float(v) for v in local]
@@ -741,7 +742,8 @@ def bench_toolcall(args, rank, world, local_rank):
     eng = CudaEngine(archive, device=local_rank, max_seqs=args.slots, max_len=TOOLCALL_PROMPT + TOOLCALL_MAX_NEW + 8,
                      max_sink=16)
     threads = max(1, min(16, cpu_threads() // max(1, world)))
-    dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=TOOLCALL_MAX_NEW, threads=threads)
+    dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=TOOLCALL_MAX_NEW, threads=threads,
+                                      mask_cache=args.mask_cache)
     dec.run(prompts[:min(8, n_local)], max_steps=max(3, args.warmup))  # warm-up steps (untimed)
     stream = torch.cuda.ExternalStream(eng.stream, device=local_rank)
     l0 = eng.kernel_launches()
@@ -772,14 +774,16 @@ def bench_toolcall(args, rank, world, local_rank):
     eng.profile(False)
     import ctypes
     from needle_b200 import native
-    h2d = st.items * ctypes.sizeof(native.StepItem) + 4 * st.allowed_ids
+    mask_bytes = 4 * (vocab.size + 31) // 32 + 4  # one mask and its slot number
+    h2d = st.items * ctypes.sizeof(native.StepItem) + 4 * st.allowed_ids + st.masks_put * mask_bytes
     d2h = st.items * ctypes.sizeof(native.Selected)
     local = [ms, st.constrained_tokens, st.prompt_tokens, sum(r.complete for r in results),
              sum(r.dead_end for r in results), st.steps, st.grammar_seconds, launches, len(results), h2d, d2h,
-             st.engine_seconds, st.seconds]
+             st.engine_seconds, st.seconds, st.masks_put, st.masked_items, st.allowed_ids]
     tot = aggregate_toolcall(local, dist)
     if rank == 0:
-        ms_max, cons, prompt_toks, done, dead, steps, gsec, launch_all, seqs, h2d_all, d2h_all, esec, wall = tot
+        (ms_max, cons, prompt_toks, done, dead, steps, gsec, launch_all, seqs, h2d_all, d2h_all, esec, wall,
+         masks_put, masked_items, allowed_ids) = tot
         secs = ms_max / 1e3
         line = {"metric": "constrained tool-call tokens/s", "value": round(cons / secs, 1), "unit": "tokens/s",
                 "n_gpus": world, "steps": int(steps), "warmup": max(3, args.warmup),
@@ -795,10 +799,14 @@ def bench_toolcall(args, rank, world, local_rank):
                            "host_grammar_seconds_max_rank": round(gsec, 3), "host_grammar_threads": threads,
                            "engine_call_seconds_max_rank": round(esec, 3),
                            "host_loop_seconds_max_rank": round(max(wall - gsec - esec, 0.0), 3),
+                           "allowed": (f"device mask pool, masks cached per grammar state ({args.mask_cache} slots "
+                                       f"per GPU)" if args.mask_cache else "id lists per step"),
+                           "masks_put": int(masks_put), "masked_selections": int(masked_items),
+                           "allowed_ids_sent": int(allowed_ids),
                            "numerics": "exact (tokens bit-identical to the CPU backend with the same masks)",
                            "parallelism": f"dp{world} (independent sequences per GPU, no collectives)"},
-                # the whole run goes through needle_cuda_step with host buffers (items, allowed ids in;
-                # selections out), so the measured value is end to end
+                # the whole run goes through needle_cuda_step with host buffers (items, allowed masks or
+                # ids in; selections out), so the measured value is end to end
                 "e2e": {"value": round(cons / secs, 1), "unit": "tokens/s",
                         "h2d_bytes_per_step": int(h2d_all / max(steps * world, 1)),
                         "d2h_bytes_per_step": int(d2h_all / max(steps * world, 1))},
@@ -825,6 +833,9 @@ def main():
     ap.add_argument("--new-tokens", type=int, default=64, help="single: greedy tokens")
     ap.add_argument("--sequences", type=int, default=4096, help="toolcall: sequences over all GPUs")
     ap.add_argument("--slots", type=int, default=512, help="toolcall: engine slots per GPU")
+    ap.add_argument("--mask-cache", type=int, default=4096,
+                    help="toolcall: allowed masks cached per grammar state in a device pool of this many "
+                         "slots (0: id lists per step)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)

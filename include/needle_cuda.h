@@ -88,11 +88,14 @@ typedef struct needle_step_item {
   int32_t token;          /* token consumed at the slot's current position;
                              NEEDLE_TOKEN_PENDING takes the slot's last selected id */
   int32_t select;         /* 1: select a token after this step (argmax / masked argmax) */
-  int32_t allowed_count;  /* -1: unmasked; >0: mask = allowed_ids[allowed_offset, +count) */
+  int32_t allowed_count;  /* -1: unmasked; >0: mask = allowed_ids[allowed_offset, +count);
+                             NEEDLE_ALLOWED_MASK: mask = slot allowed_offset of the device mask
+                             pool (needle_cuda_mask_pool / needle_cuda_masks_put) */
   uint32_t allowed_offset;
 } needle_step_item;
 
 #define NEEDLE_TOKEN_PENDING (-1)
+#define NEEDLE_ALLOWED_MASK (-2)
 
 /* SelectedToken (backend.ts:41-44). */
 typedef struct needle_selected {
@@ -156,11 +159,25 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n,
  * then returns without waiting; needle_cuda_step_end takes the same items (same slots and tokens in
  * the same order; a select may be cleared, e.g. for a grammar dead end, but not set) with their
  * allowed lists, selects, waits and advances the slots, exactly as needle_cuda_step with those items
- * would have.  No other call may use the context in between (BACKEND_UNAVAILABLE).  If step_end
- * fails, the step is dropped: the slots keep their positions.  Logits are not returned. */
+ * would have.  No other call may use the context in between (BACKEND_UNAVAILABLE), except
+ * needle_cuda_masks_put.  If step_end fails, the step is dropped: the slots keep their positions.
+ * Logits are not returned. */
 int needle_cuda_step_begin(needle_ctx* ctx, const needle_step_item* items, int32_t n);
 int needle_cuda_step_end(needle_ctx* ctx, const needle_step_item* items, int32_t n, const uint32_t* allowed_ids,
                          size_t allowed_total, needle_selected* out_selected);
+
+/* Device-resident allowed-id masks.  An item with allowed_count = NEEDLE_ALLOWED_MASK selects among
+ * the ids set in slot allowed_offset of the context's mask pool (bit id % 32 of word id / 32,
+ * ceil(vocab / 32) words per slot), with the same result as the ascending id list of those ids: the
+ * best logit, ties to the lowest id.  The masks cross PCIe once per new grammar state instead of as
+ * an id list at every step (a needle_mask_cache keeps them per state, include/needle_grammar.h).
+ * needle_cuda_mask_pool (re)allocates a pool of `capacity` empty slots.  needle_cuda_masks_put
+ * copies the masks of the `n` listed slots from `table` (a host table indexed by slot, [capacity]
+ * [words], as needle_mask_cache_table gives) into the pool, ordered before every later step on the
+ * context (it may run between needle_cuda_step_begin and needle_cuda_step_end).  An item naming a
+ * slot whose last put was empty, or never put, fails as an empty allowed set. */
+int needle_cuda_mask_pool(needle_ctx* ctx, int32_t capacity);
+int needle_cuda_masks_put(needle_ctx* ctx, const int32_t* slots, int32_t n, const uint32_t* table);
 
 /* ---- ResidentExecutionSession (packages/needle.js/src/backends/backend.ts:66-80) ----
  * The per-token calls NeedleRuntime.step makes on a resident session (runtime.ts:305-372), with

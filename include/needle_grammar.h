@@ -64,6 +64,36 @@ int needle_grammar_allowed_batch(const needle_grammar* const* grammars, const in
                                  const needle_vocab* vocab, int32_t threads, uint32_t* ids,
                                  int32_t capacity_each, int32_t* counts);
 
+/* Allowed-token masks per grammar state.  Many sequences of a batch sit in the same grammar state
+ * (inside the free content of an argument string, after the same key, at the same separator), and
+ * one sequence revisits states; the scan above (agent.ts:165-176) depends only on that state and on
+ * the room left under the 64 KiB limit, so its result is kept, as a bit mask over the vocabulary,
+ * under a key of both.  The reference rescans the vocabulary at every step and has no counterpart;
+ * a mask holds exactly the ids needle_grammar_allowed returns for the same grammar (bit id % 32 of
+ * word id / 32).  The masks live in a table of `capacity` slots, reused least recently used first;
+ * the slot numbers are meant to index a copy of the table on the device (needle_cuda_masks_put),
+ * so a step's items can name a mask instead of carrying an id list.
+ *
+ * A cache serves the clones of one template grammar (it keeps a clone of it) and one vocabulary
+ * (which must outlive it).  Not thread-safe. */
+typedef struct needle_mask_cache needle_mask_cache;
+int needle_mask_cache_open(const needle_grammar* template_grammar, const needle_vocab* vocab, int32_t capacity,
+                           needle_mask_cache** out);
+void needle_mask_cache_free(needle_mask_cache* cache);
+/* The host table: capacity x words uint32, words = ceil(vocabulary size / 32); valid until the
+ * cache is freed. */
+int needle_mask_cache_table(const needle_mask_cache* cache, const uint32_t** table, int32_t* words);
+/* For `n` grammars (clones of the template; null entries give slot -1 and count 0): slots[k] is the
+ * table slot of grammar k's mask and counts[k] its number of ids (0: no token can continue).  States
+ * not in the table are scanned on up to `threads` host threads into slots taken least recently used
+ * first; those slots are listed in filled[0 .. *n_filled) (at most n entries; their contents
+ * changed).  No slot that one call uses is evicted by the same call, so `capacity` must be at least
+ * the number of distinct states in one call (NEEDLE_INVALID_TOOL_SCHEMA otherwise). */
+int needle_mask_cache_lookup(needle_mask_cache* cache, const needle_grammar* const* grammars,
+                             const int64_t* output_bytes, int32_t n, int32_t threads, int32_t* slots,
+                             int32_t* counts, int32_t* filled, int32_t* n_filled);
+int needle_mask_cache_stats(const needle_mask_cache* cache, int64_t* hits, int64_t* misses, int64_t* evictions);
+
 #ifdef __cplusplus
 }
 #endif

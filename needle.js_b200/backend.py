@@ -33,6 +33,7 @@ class StepRequest:
     token: int = native.TOKEN_PENDING
     select: bool = False
     allowed: Optional[np.ndarray] = None  # None: unmasked argmax
+    mask_slot: Optional[int] = None       # a slot of the device mask pool instead of `allowed`
 
 
 class CudaEngine:
@@ -115,12 +116,17 @@ class CudaEngine:
         if n:
             items[:n, 0] = [r.seq for r in requests]
             items[:n, 1] = [r.token for r in requests]
-            masked = [r.select and r.allowed is not None for r in requests]
+            masked = [r.select and r.allowed is not None and r.mask_slot is None for r in requests]
+            pooled = [r.select and r.mask_slot is not None for r in requests]
             items[:n, 2] = [1 if r.select else 0 for r in requests]
             counts = np.array([r.allowed.size if m else -1 for r, m in zip(requests, masked)], dtype=np.int64)
-            items[:n, 3] = counts
             sizes = np.maximum(counts, 0)
-            items[:n, 4] = (np.cumsum(sizes) - sizes).astype(np.int32)
+            offsets = np.cumsum(sizes) - sizes
+            for i, p in enumerate(pooled):
+                if p:
+                    counts[i], offsets[i] = native.ALLOWED_MASK, requests[i].mask_slot
+            items[:n, 3] = counts
+            items[:n, 4] = offsets.astype(np.uint32).view(np.int32)
         parts = [np.asarray(r.allowed, dtype=np.uint32) for r, m in zip(requests, masked) if m] if n else []
         allowed = np.ascontiguousarray(np.concatenate(parts)) if parts else None
         return items, allowed
@@ -152,6 +158,19 @@ class CudaEngine:
         check(lib().needle_cuda_step_end(self.h, ptr(items), n, ptr(allowed),
                                          0 if allowed is None else allowed.size, C.cast(sel, C.c_void_p)))
         return [(sel[i].id, sel[i].log_probability) if r.select else None for i, r in enumerate(requests)]
+
+    def mask_pool(self, capacity: int):
+        """(Re)allocates the device mask pool (needle_cuda_mask_pool): `capacity` empty slots."""
+        check(lib().needle_cuda_mask_pool(self.h, int(capacity)))
+
+    def masks_put(self, slots, table: np.ndarray):
+        """Copies the listed slots' masks from `table` ([capacity][words] uint32, indexed by slot) into
+        the device pool (needle_cuda_masks_put); allowed between step_begin and step_end."""
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        if slots.size == 0:
+            return
+        table = np.ascontiguousarray(table, dtype=np.uint32)
+        check(lib().needle_cuda_masks_put(self.h, ptr(slots), slots.size, ptr(table)))
 
     def prefill(self, seq: int, ids, want_logits: bool = True):
         ids = np.ascontiguousarray(ids, dtype=np.int32)

@@ -372,6 +372,13 @@ struct needle_ctx {
   double* h_logprob = nullptr;
   uint32_t* d_allowed = nullptr;
   size_t allowed_cap = 0;
+  // allowed-id bit masks (needle_cuda_mask_pool / needle_cuda_masks_put)
+  uint32_t* d_masks = nullptr;     // [mask_capacity][mask_words]
+  int32_t mask_capacity = 0, mask_words = 0;
+  std::vector<int32_t> mask_count;  // ids set in each slot's mask as last put (0: empty or never put)
+  uint32_t* h_mask_stage = nullptr;  // pinned: max_seqs slot numbers, then max_seqs masks
+  uint32_t* d_mask_stage = nullptr;
+  cudaEvent_t mask_staged = nullptr;  // recorded after the last staging copy
   DevItem* h_items_end = nullptr;  // the items as needle_cuda_step_end re-uploads them
   float* h_lanes = nullptr;         // a resident-session item's lanes (pinned, kLaneWidth floats)
   uint32_t* h_engram = nullptr;     // and its engram lookup (pinned, 2 * kMaxTables)
@@ -1018,6 +1025,10 @@ void destroy(needle_ctx* C) {
   if (C->h_counts) cudaFreeHost(C->h_counts);
   if (C->h_ids) cudaFreeHost(C->h_ids);
   if (C->h_logprob) cudaFreeHost(C->h_logprob);
+  if (C->h_mask_stage) cudaFreeHost(C->h_mask_stage);
+  if (C->d_masks) cudaFree(C->d_masks);
+  if (C->d_mask_stage) cudaFree(C->d_mask_stage);
+  if (C->mask_staged) cudaEventDestroy(C->mask_staged);
   for (int k = 0; k < 2; k++) {
     if (C->fork_ev[k]) cudaEventDestroy(C->fork_ev[k]);
     if (C->join_ev[k]) cudaEventDestroy(C->join_ev[k]);
@@ -1071,8 +1082,17 @@ int slot_kv_alloc(needle_ctx& C, int seq) {
   return st.kv_alloc;
 }
 
-// Checks one item's allowed list against the vocabulary (selectToken, runtime.ts:880-899).
-void check_allowed(const needle_step_item& it, const uint32_t* allowed_ids, size_t allowed_total, int V) {
+// Checks one item's allowed list against the vocabulary (selectToken, runtime.ts:880-899), or its
+// mask slot against the pool.
+void check_allowed(const needle_ctx& C, const needle_step_item& it, const uint32_t* allowed_ids,
+                   size_t allowed_total, int V) {
+  if (it.allowed_count == NEEDLE_ALLOWED_MASK) {
+    require(C.d_masks != nullptr && it.allowed_offset < uint32_t(C.mask_capacity), NEEDLE_INVALID_CACT,
+            "allowed mask slot out of range");
+    require(C.mask_count[it.allowed_offset] > 0, NEEDLE_INVALID_CACT, "Allowed token set is empty");
+    return;
+  }
+  require(it.allowed_count >= -1, NEEDLE_INVALID_CACT, "allowed_count must be -1, NEEDLE_ALLOWED_MASK or a count");
   if (it.allowed_count < 0) return;
   require(it.allowed_count > 0, NEEDLE_INVALID_CACT, "Allowed token set is empty");
   require(allowed_ids != nullptr && uint64_t(it.allowed_offset) + uint64_t(it.allowed_count) <= allowed_total,
@@ -1106,7 +1126,7 @@ int check_items(needle_ctx& C, const needle_step_item* items, int32_t n, bool al
       fail(NEEDLE_INVALID_CACT, "Token " + std::to_string(it.token) + " is outside the vocabulary");
     if (it.select) {
       require(have_selected, NEEDLE_BACKEND_UNAVAILABLE, "selection requested without output");
-      if (allowed) check_allowed(it, allowed_ids, allowed_total, V);
+      if (allowed) check_allowed(C, it, allowed_ids, allowed_total, V);
       n_sel++;
     }
   }
@@ -1234,7 +1254,7 @@ void end_step(needle_ctx& C, const needle_step_item* items, int32_t n, const uin
             "step_end items differ from step_begin's (only select may be cleared)");
     if (it.select) {
       require(out_selected != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "selection requested without output");
-      check_allowed(it, allowed_ids, allowed_total, V);
+      check_allowed(C, it, allowed_ids, allowed_total, V);
     }
   }
   // the allowed fields (and cleared selects) go in with a second copy of the items, ordered after
@@ -1463,6 +1483,84 @@ int needle_cuda_step_begin(needle_ctx* ctx, const needle_step_item* items, int32
     P.n = n;
     P.n_sel = n_sel;
     P.active = true;
+  });
+}
+
+static_assert(kAllowedMask == NEEDLE_ALLOWED_MASK, "device and C-ABI mask markers differ");
+
+int needle_cuda_mask_pool(needle_ctx* ctx, int32_t capacity) {
+  return guarded([&] {
+    require(ctx != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null context");
+    needle_ctx& C = *ctx;
+    require(capacity > 0 && capacity <= (1 << 20), NEEDLE_BACKEND_UNAVAILABLE, "mask pool capacity out of range");
+    require(!C.pending.active, NEEDLE_BACKEND_UNAVAILABLE, "a begun step is pending");
+    cuda_check(cudaSetDevice(C.device), "cudaSetDevice");
+    cuda_check(cudaStreamSynchronize(C.stream), "cudaStreamSynchronize");
+    if (C.d_masks) cudaFree(C.d_masks);
+    if (C.d_mask_stage) cudaFree(C.d_mask_stage);
+    if (C.h_mask_stage) cudaFreeHost(C.h_mask_stage);
+    C.d_masks = C.d_mask_stage = C.h_mask_stage = nullptr;
+    C.mask_capacity = 0;
+    const int words = (C.mv.vocab + 31) / 32;
+    const size_t stage = size_t(C.opts.max_seqs) * (1 + words);
+    cuda_check(cudaMalloc(&C.d_masks, size_t(capacity) * words * 4), "cudaMalloc");
+    cuda_check(cudaMemsetAsync(C.d_masks, 0, size_t(capacity) * words * 4, C.stream), "cudaMemsetAsync");
+    cuda_check(cudaMalloc(&C.d_mask_stage, stage * 4), "cudaMalloc");
+    cuda_check(cudaHostAlloc(&C.h_mask_stage, stage * 4, cudaHostAllocDefault), "cudaHostAlloc");
+    if (!C.mask_staged) cuda_check(cudaEventCreateWithFlags(&C.mask_staged, cudaEventDisableTiming), "cudaEventCreate");
+    cuda_check(cudaEventRecord(C.mask_staged, C.stream), "cudaEventRecord");
+    C.mask_capacity = capacity;
+    C.mask_words = words;
+    C.mask_count.assign(capacity, 0);
+    C.stv.masks = C.d_masks;
+    C.stv.mask_words = words;
+  });
+}
+
+int needle_cuda_masks_put(needle_ctx* ctx, const int32_t* slots, int32_t n, const uint32_t* table) {
+  return guarded([&] {
+    require(ctx != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null context");
+    needle_ctx& C = *ctx;
+    require(C.d_masks != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "no mask pool (needle_cuda_mask_pool)");
+    require(n >= 0 && (n == 0 || (slots != nullptr && table != nullptr)), NEEDLE_BACKEND_UNAVAILABLE,
+            "null argument");
+    cuda_check(cudaSetDevice(C.device), "cudaSetDevice");
+    const int words = C.mask_words, V = C.mv.vocab;
+    const int per = C.opts.max_seqs;
+    const uint32_t tail = (V & 31) ? ~((1u << (V & 31)) - 1u) : 0u;  // bits of ids >= V in the last word
+    std::vector<int32_t> set(per);
+    for (int32_t base = 0; base < n; base += per) {
+      const int m = std::min<int32_t>(per, n - base);
+      for (int k = 0; k < m; k++) {
+        const int32_t s = slots[base + k];
+        require(s >= 0 && s < C.mask_capacity, NEEDLE_BACKEND_UNAVAILABLE, "mask slot out of range");
+        const uint32_t* w = table + size_t(s) * words;
+        require(!(w[words - 1] & tail), NEEDLE_INVALID_CACT, "a mask sets an id outside the vocabulary");
+        int c = 0;
+        for (int j = 0; j < words; j++) c += __builtin_popcount(w[j]);
+        set[k] = c;
+      }
+      // the staging buffer is free once the previous put's copy has run
+      cuda_check(cudaEventSynchronize(C.mask_staged), "cudaEventSynchronize");
+      for (int k = 0; k < m; k++) {
+        const int32_t s = slots[base + k];
+        C.h_mask_stage[k] = uint32_t(s);
+        memcpy(C.h_mask_stage + per + size_t(k) * words, table + size_t(s) * words, size_t(words) * 4);
+      }
+      C.timed(P_COPY, [&] {
+        cudaError_t e = cudaMemcpyAsync(C.d_mask_stage, C.h_mask_stage, size_t(m) * 4, cudaMemcpyHostToDevice,
+                                        C.stream);
+        if (e != cudaSuccess) return e;
+        return cudaMemcpyAsync(C.d_mask_stage + per, C.h_mask_stage + per, size_t(m) * words * 4,
+                               cudaMemcpyHostToDevice, C.stream);
+      });
+      cuda_check(cudaEventRecord(C.mask_staged, C.stream), "cudaEventRecord");
+      C.timed(P_FINISH, [&] {
+        return launch_mask_scatter(C.d_mask_stage + per, reinterpret_cast<const int32_t*>(C.d_mask_stage), m, words,
+                                   C.d_masks, C.stream);
+      });
+      for (int k = 0; k < m; k++) C.mask_count[slots[base + k]] = set[k];
+    }
   });
 }
 

@@ -80,7 +80,7 @@ struct DevItem {
   int32_t slot;
   int32_t token;            // >= 0, or NEEDLE_TOKEN_PENDING (-1) until k_embed resolves it
   int32_t select;
-  int32_t allowed_count;    // -1 unmasked
+  int32_t allowed_count;    // -1 unmasked, >0 ids at allowed_offset, kAllowedMask: pool slot
   uint32_t allowed_offset;
   int32_t position;         // filled by k_embed
   int32_t out_index;        // caller's index
@@ -93,12 +93,18 @@ struct DevItem {
 constexpr int32_t kItemLanes = 1;
 constexpr int32_t kItemEngrams = 2;
 
+// DevItem::allowed_count of an item whose allowed ids are a bit mask of the mask pool
+// (StepView::masks, slot allowed_offset): NEEDLE_ALLOWED_MASK.
+constexpr int32_t kAllowedMask = -2;
+
 // Step scratch, indexed by internal item index.
 struct StepView {
   DevItem* items;
   const int32_t* n_items;   // device count (all items)
   const int32_t* n_select;  // device count of selecting items (a prefix of items)
   const uint32_t* allowed;  // allowed ids
+  const uint32_t* masks;    // [pool slots][mask_words] allowed-id bit masks (bit id % 32 of word id / 32)
+  int32_t mask_words;
   float* prep_engram;       // [B][sites][512]
   float* engram_kv;         // [B][sites][2][512]  (K projection, V projection)
   float* engram_val;        // [B][sites][512]      convolved values
@@ -155,6 +161,9 @@ cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepV
                              int n_host, cudaStream_t s, int part = 0);
 cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
                           const SchedView* sched, cudaStream_t s);
+// Copies staged masks into the mask pool: mask k of `staged` ([n][words]) to slot slots[k].
+cudaError_t launch_mask_scatter(const uint32_t* staged, const int32_t* slots, int n, int words, uint32_t* pool,
+                                cudaStream_t s);
 // Device scheduler: builds the step's item list and the counts [all, selecting, then (all,
 // selecting) of each of `parts` micro-batches], micro-batch k being items [k * part, (k + 1) * part).
 cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts, int part,

@@ -34,6 +34,7 @@
 #include <stdexcept>
 #include <string>
 #include <thread>
+#include <unordered_map>
 #include <utility>
 #include <vector>
 
@@ -670,6 +671,14 @@ bool parse_string_literal(const std::string& bytes, std::string& out) {
 
 // ------------------------------------------------------------------ JsonSchemaGrammar
 
+// State keys (the allowed-token mask cache): fixed-width integers and length-prefixed strings, so
+// that distinct field sequences never concatenate to the same bytes.
+void key_int(std::string& k, int64_t v) { k.append(reinterpret_cast<const char*>(&v), sizeof v); }
+void key_str(std::string& k, const std::string& s) {
+  key_int(k, (int64_t)s.size());
+  k += s;
+}
+
 struct Candidate {
   std::string bytes;  // choice: JSON text of the value; key: the property name
   Json value;
@@ -683,6 +692,7 @@ struct Frame {
   std::string bytes;
   bool started = false, escaped = false;
   int unicode_remaining = 0;
+  Utf8Check utf8;  // over `bytes` so far (the state key needs it without rescanning them)
   // number
   std::string text;
   // literal
@@ -832,7 +842,7 @@ class SchemaGrammar {
   StringClose string_close() const {
     StringClose c;
     const Frame& f = stack_.back();
-    for (unsigned char b : f.bytes) c.utf8.feed(b);
+    c.utf8 = f.utf8;
     try {
       Parser p{f.bytes + "\""};
       Json v = p.document();
@@ -888,7 +898,94 @@ class SchemaGrammar {
 
   // The same as feeding `bytes` one at a time (each >= 0x20, none '"' or '\\') while
   // in_string_content().
-  void append_string_content(const char* bytes, size_t n) { stack_.back().bytes.append(bytes, n); }
+  void append_string_content(const char* bytes, size_t n) {
+    Frame& f = stack_.back();
+    f.bytes.append(bytes, n);
+    for (size_t k = 0; k < n; k++) f.utf8.feed((uint8_t)bytes[k]);
+  }
+
+  // Appends a key of this state.  Two grammars cloned from one template whose keys are equal accept
+  // the same byte strings from here on, so they allow the same tokens.  The key keeps what
+  // feed_byte can still read -- each frame's kind, schema, phase and progress -- and drops what no
+  // later check reads: the content of a string or an array whose value nothing inspects any more
+  // (no enum, const or uniqueItems on it or around it, and for a string no constraint of its own)
+  // shrinks to the UTF-8 decoder's state or the item count.  A string's close then depends only on
+  // that state: JSON.parse of bytes that feed_byte accepted fails only on invalid UTF-8 (lone
+  // surrogate escapes decode).  Schemas inside the template's document are named by address (the
+  // cache keeps the template alive); a schema outside it (a $ref merged into a new object) by its
+  // JSON text.
+  void state_key(std::string& k) const {
+    if (complete_) {
+      k += 'C';
+      k += (char)value_.kind;
+      return;
+    }
+    key_int(k, (int64_t)stack_.size());
+    bool read_later = false;  // an enclosing value's content is checked when it closes
+    for (const Frame& f : stack_) {
+      k += (char)f.kind;
+      key_schema(k, f.schema);
+      const Json* s = f.schema.get();
+      const bool checked = s && (s->get("enum") || s->get("const") || (f.kind == Frame::Array && s->get("uniqueItems")));
+      switch (f.kind) {
+        case Frame::Value:
+          break;
+        case Frame::String: {
+          k += (char)((f.started ? 1 : 0) | (f.escaped ? 2 : 0));
+          key_int(k, f.unicode_remaining);
+          bool content = read_later;
+          for (const char* key : {"minLength", "maxLength", "pattern", "format", "enum", "const"})
+            if (s && s->get(key)) content = true;
+          if (content) {
+            key_str(k, f.bytes);
+          } else {
+            k += (char)(f.utf8.bad ? 1 : 0);
+            key_int(k, f.utf8.need);
+            if (f.utf8.need > 0) {
+              key_int(k, f.utf8.cp);
+              key_int(k, f.utf8.min);
+            }
+          }
+          break;
+        }
+        case Frame::Number:
+          key_str(k, f.text);
+          break;
+        case Frame::Literal:
+          key_str(k, f.literal);
+          key_int(k, f.offset);
+          break;
+        case Frame::Choice:
+        case Frame::Key:
+          key_int(k, (int64_t)f.candidates.size());
+          for (const auto& c : f.candidates) {
+            key_str(k, c.bytes);
+            key_int(k, c.offset);
+          }
+          break;
+        case Frame::Array:
+          k += (char)f.phase;
+          key_int(k, (int64_t)f.value.arr.size());
+          if (read_later || checked) key_str(k, stringify(f.value));
+          break;
+        case Frame::Object: {
+          k += (char)f.phase;
+          k += (char)(f.has_key ? 1 : 0);
+          key_str(k, f.current_key);
+          std::vector<std::string> used(f.used);  // only membership is read
+          std::sort(used.begin(), used.end());
+          key_int(k, (int64_t)used.size());
+          for (const auto& u : used) key_str(k, u);
+          if (read_later || checked) key_str(k, stringify(f.value));
+          break;
+        }
+      }
+      read_later = read_later || checked;
+    }
+  }
+
+  // The template this grammar was cloned from (shared by all its clones).
+  const void* template_id() const { return root_.get(); }
 
   bool feed_byte(int byte) {
     if (complete_) return false;
@@ -977,6 +1074,7 @@ class SchemaGrammar {
             if (byte != 0x22) return false;
             frame.started = true;
             frame.bytes += (char)byte;
+            frame.utf8.feed((uint8_t)byte);
             return true;
           }
           if (frame.unicode_remaining > 0) {
@@ -984,6 +1082,7 @@ class SchemaGrammar {
               return false;
             frame.unicode_remaining--;
             frame.bytes += (char)byte;
+            frame.utf8.feed((uint8_t)byte);
             return true;
           }
           if (frame.escaped) {
@@ -992,15 +1091,18 @@ class SchemaGrammar {
             frame.escaped = false;
             if (byte == 0x75) frame.unicode_remaining = 4;
             frame.bytes += (char)byte;
+            frame.utf8.feed((uint8_t)byte);
             return true;
           }
           if (byte == 0x5c) {
             frame.escaped = true;
             frame.bytes += (char)byte;
+            frame.utf8.feed((uint8_t)byte);
             return true;
           }
           if (byte < 0x20) return false;
           frame.bytes += (char)byte;
+          frame.utf8.feed((uint8_t)byte);
           if (byte != 0x22) return true;
           std::string value;
           if (!parse_string_literal(frame.bytes, value)) return false;
@@ -1199,6 +1301,20 @@ class SchemaGrammar {
     stack_.push_back(std::move(f));
   }
 
+  void key_schema(std::string& k, const SchemaPtr& s) const {
+    if (!s) {
+      k += 'N';
+    } else if (s.get() == &empty_schema()) {
+      k += 'E';
+    } else if (!s.owner_before(root_) && !root_.owner_before(s)) {
+      k += 'P';
+      key_int(k, (int64_t)(uintptr_t)s.get());
+    } else {
+      k += 'J';
+      key_str(k, stringify(*s));
+    }
+  }
+
   void finish(Json value) {
     stack_.pop_back();
     if (stack_.empty()) {
@@ -1361,6 +1477,43 @@ class ToolGrammar {
   const std::string& number_text() const { return arguments_->number_text(); }
   void append_number(const char* bytes, size_t n) { arguments_->append_number(bytes, n); }
   bool end_number() { return arguments_->end_number(); }
+
+  // As SchemaGrammar::state_key.  The calls made so far are read only through the tools they used
+  // (a used tool's name is not offered again; their number bounds further calls); the arguments
+  // grammar is keyed while it is being fed or checked.
+  void state_key(std::string& k) const {
+    k += (char)phase_;
+    std::vector<int> used(used_);
+    std::sort(used.begin(), used.end());
+    key_int(k, (int64_t)used.size());
+    for (int u : used) key_int(k, u);
+    switch (phase_) {
+      case NameLiteral:
+        key_int(k, literal_offset_);
+        break;
+      case ToolName:
+        key_int(k, (int64_t)names_.size());
+        for (const auto& c : names_) {
+          key_int(k, c.first);
+          key_int(k, c.second);
+        }
+        break;
+      case ArgumentsLiteral:
+        key_int(k, literal_offset_);
+        key_int(k, current_);
+        break;
+      case Arguments:
+      case CallClose:
+        key_int(k, current_);
+        if (arguments_) arguments_->state_key(k);
+        else k += 'X';
+        break;
+      default:
+        break;
+    }
+  }
+  const void* template_id() const { return tools_.get(); }
+  int maximum_calls() const { return maximum_calls_; }
 
   bool feed_byte(int byte) {
     for (int retry = 0; retry < 8; retry++) {
@@ -1572,6 +1725,26 @@ struct needle_vocab {
   int32_t size = 0;  // ids are below this
 };
 
+// Allowed-token masks per grammar state (needle_mask_cache_*): a fixed table of `capacity` bit
+// masks, reused least-recently-used first, indexed by the state key of the grammar and the walk's
+// length limit.
+struct needle_mask_cache {
+  std::unique_ptr<needle_grammar> keep;  // a clone of the template: keeps its schemas alive
+  const void* template_id = nullptr;
+  int maximum_calls = 0;
+  const needle_vocab* vocab = nullptr;
+  int32_t capacity = 0, words = 0;
+  std::vector<uint32_t> table;   // [capacity][words]
+  std::vector<int32_t> count;    // ids set in each mask
+  std::vector<std::string> key;  // "" = free
+  std::vector<int32_t> prev, next;
+  int32_t head = -1, tail = -1;  // most / least recently used
+  std::vector<uint64_t> used_in;  // the lookup that last used each slot
+  uint64_t lookups = 0;
+  std::unordered_map<std::string, int32_t> index;
+  int64_t hits = 0, misses = 0, evictions = 0;
+};
+
 namespace {
 
 int fail(int code, const std::string& msg) {
@@ -1736,23 +1909,206 @@ void descend(Walk& w, int32_t node, const G& g, int32_t depth) {
   }
 }
 
+// The longest piece the walk may take: agent.ts:171 keeps the output within 64 KiB; 0 when no piece
+// fits.
+int32_t walk_limit(const needle_vocab& v, int64_t output_bytes) {
+  const int64_t room = 65536 - output_bytes;
+  return room <= 0 ? 0 : (int32_t)std::min<int64_t>(room, v.trie.max_len);
+}
+
+// mark[id] = 1 for each id whose piece the grammar accepts; `mark` is resized to the vocabulary.
+void mark_allowed(const needle_grammar& g, const needle_vocab& v, int64_t output_bytes, std::vector<uint8_t>& mark) {
+  mark.assign(v.size, 0);
+  const int32_t limit = walk_limit(v, output_bytes);
+  if (limit == 0) return;
+  Walk w{v.trie, limit, mark, {}, {}};
+  if (g.schema) descend(w, 0, *g.schema, 0);
+  else descend(w, 0, *g.tools, 0);
+}
+
 // Ascending ids whose piece the grammar accepts; `mark` is scratch of the vocabulary's size.
 void allowed(const needle_grammar& g, const needle_vocab& v, int64_t output_bytes, std::vector<uint8_t>& mark,
              std::vector<uint32_t>& out) {
   out.clear();
-  const int64_t room = 65536 - output_bytes;  // agent.ts:171: output bytes stay within 64 KiB
-  if (room <= 0) return;
-  mark.assign(v.size, 0);
-  Walk w{v.trie, (int32_t)std::min<int64_t>(room, v.trie.max_len), mark, {}, {}};
-  if (g.schema) descend(w, 0, *g.schema, 0);
-  else descend(w, 0, *g.tools, 0);
+  mark_allowed(g, v, output_bytes, mark);
   for (int32_t id = 0; id < v.size; id++)
     if (mark[id]) out.push_back((uint32_t)id);
+}
+
+std::string grammar_key(const needle_grammar& g, int32_t limit) {
+  std::string k;
+  key_int(k, limit);
+  if (limit > 0) {
+    if (g.schema) g.schema->state_key(k);
+    else g.tools->state_key(k);
+  }
+  return k;
+}
+
+bool same_template(const needle_grammar& g, const needle_mask_cache& c) {
+  if (g.schema) return g.schema->template_id() == c.template_id;
+  return g.tools->template_id() == c.template_id && g.tools->maximum_calls() == c.maximum_calls;
+}
+
+void lru_unlink(needle_mask_cache& c, int32_t s) {
+  if (c.prev[s] >= 0) c.next[c.prev[s]] = c.next[s];
+  else c.head = c.next[s];
+  if (c.next[s] >= 0) c.prev[c.next[s]] = c.prev[s];
+  else c.tail = c.prev[s];
+  c.prev[s] = c.next[s] = -1;
+}
+
+void lru_front(needle_mask_cache& c, int32_t s) {
+  if (c.head == s) return;
+  if (c.prev[s] >= 0) lru_unlink(c, s);  // linked (every linked slot but the head has a prev)
+  c.next[s] = c.head;
+  if (c.head >= 0) c.prev[c.head] = s;
+  c.head = s;
+  if (c.tail < 0) c.tail = s;
+}
+
+// Empties slots whose key was taken but whose mask was not written.
+void drop_slots(needle_mask_cache& c, const std::vector<int32_t>& slots) {
+  for (int32_t s : slots) {
+    c.index.erase(c.key[s]);
+    c.key[s].clear();
+    c.count[s] = 0;
+  }
 }
 
 }  // namespace
 
 extern "C" {
+
+int needle_mask_cache_open(const needle_grammar* template_grammar, const needle_vocab* vocab, int32_t capacity,
+                           needle_mask_cache** out) {
+  if (!template_grammar || !vocab || !out) return fail(NEEDLE_INVALID_TOOL_SCHEMA, "null argument");
+  if (capacity < 1) return fail(NEEDLE_INVALID_TOOL_SCHEMA, "mask cache capacity must be positive");
+  auto c = std::make_unique<needle_mask_cache>();
+  c->keep = std::make_unique<needle_grammar>();
+  if (template_grammar->schema) {
+    c->keep->schema = std::make_unique<SchemaGrammar>(*template_grammar->schema);
+    c->template_id = c->keep->schema->template_id();
+  } else {
+    c->keep->tools = std::make_unique<ToolGrammar>(*template_grammar->tools);
+    c->template_id = c->keep->tools->template_id();
+    c->maximum_calls = c->keep->tools->maximum_calls();
+  }
+  c->vocab = vocab;
+  c->capacity = capacity;
+  c->words = (vocab->size + 31) / 32;
+  c->table.assign((size_t)capacity * c->words, 0u);
+  c->count.assign(capacity, 0);
+  c->key.assign(capacity, std::string());
+  c->prev.assign(capacity, -1);
+  c->next.assign(capacity, -1);
+  c->used_in.assign(capacity, 0);
+  for (int32_t s = 0; s < capacity; s++) lru_front(*c, s);  // slot 0 ends last: taken first
+  *out = c.release();
+  return NEEDLE_OK;
+}
+
+void needle_mask_cache_free(needle_mask_cache* cache) { delete cache; }
+
+int needle_mask_cache_table(const needle_mask_cache* cache, const uint32_t** table, int32_t* words) {
+  if (!cache || !table || !words) return fail(NEEDLE_INVALID_TOOL_SCHEMA, "null argument");
+  *table = cache->table.data();
+  *words = cache->words;
+  return NEEDLE_OK;
+}
+
+int needle_mask_cache_stats(const needle_mask_cache* cache, int64_t* hits, int64_t* misses, int64_t* evictions) {
+  if (!cache || !hits || !misses || !evictions) return fail(NEEDLE_INVALID_TOOL_SCHEMA, "null argument");
+  *hits = cache->hits;
+  *misses = cache->misses;
+  *evictions = cache->evictions;
+  return NEEDLE_OK;
+}
+
+int needle_mask_cache_lookup(needle_mask_cache* cache, const needle_grammar* const* grammars,
+                             const int64_t* output_bytes, int32_t n, int32_t threads, int32_t* slots,
+                             int32_t* counts, int32_t* filled, int32_t* n_filled) {
+  if (!cache || !n_filled || n < 0 || (n > 0 && (!grammars || !output_bytes || !slots || !counts || !filled)))
+    return fail(NEEDLE_INVALID_TOOL_SCHEMA, "null argument");
+  needle_mask_cache& c = *cache;
+  *n_filled = 0;
+  for (int32_t k = 0; k < n; k++)
+    if (grammars[k] && !same_template(*grammars[k], c))
+      return fail(NEEDLE_INVALID_TOOL_SCHEMA, "grammar is not a clone of the mask cache's template");
+  std::vector<int32_t> fill_slot, fill_from;
+  const uint64_t lookup = ++c.lookups;
+  try {
+    for (int32_t k = 0; k < n; k++) {
+      if (!grammars[k]) {
+        slots[k] = -1;
+        counts[k] = 0;
+        continue;
+      }
+      std::string key = grammar_key(*grammars[k], walk_limit(*c.vocab, output_bytes[k]));
+      int32_t slot;
+      if (auto it = c.index.find(key); it != c.index.end()) {
+        slot = it->second;
+        c.hits++;
+      } else {
+        slot = c.tail;
+        if (slot < 0 || c.used_in[slot] == lookup) {
+          drop_slots(c, fill_slot);
+          return fail(NEEDLE_INVALID_TOOL_SCHEMA, "mask cache capacity is below the distinct states of one lookup");
+        }
+        if (!c.key[slot].empty()) {
+          c.index.erase(c.key[slot]);
+          c.evictions++;
+        }
+        c.key[slot] = key;
+        c.index.emplace(std::move(key), slot);
+        c.misses++;
+        fill_slot.push_back(slot);
+        fill_from.push_back(k);
+      }
+      c.used_in[slot] = lookup;
+      lru_front(c, slot);
+      slots[k] = slot;
+    }
+  } catch (const std::exception& e) {
+    drop_slots(c, fill_slot);
+    return fail(NEEDLE_INVALID_TOOL_SCHEMA, e.what());
+  }
+  std::atomic<int> next{0};
+  std::atomic<bool> bad{false};
+  auto work = [&]() {
+    std::vector<uint8_t> mark;
+    for (int j; (j = next.fetch_add(1)) < (int)fill_slot.size();) {
+      try {
+        const int32_t k = fill_from[j], slot = fill_slot[j];
+        mark_allowed(*grammars[k], *c.vocab, output_bytes[k], mark);
+        uint32_t* w = c.table.data() + (size_t)slot * c.words;
+        std::fill(w, w + c.words, 0u);
+        int32_t set = 0;
+        for (int32_t id = 0; id < c.vocab->size; id++)
+          if (mark[id]) {
+            w[id >> 5] |= 1u << (id & 31);
+            set++;
+          }
+        c.count[slot] = set;
+      } catch (const std::exception&) {
+        bad.store(true);
+      }
+    }
+  };
+  const int t = std::max(1, std::min<int>(threads, (int)fill_slot.size()));
+  std::vector<std::thread> pool;
+  for (int k = 1; k < t; k++) pool.emplace_back(work);
+  work();
+  for (auto& th : pool) th.join();
+  if (bad.load()) {
+    drop_slots(c, fill_slot);
+    return fail(NEEDLE_INVALID_TOOL_SCHEMA, "grammar enumeration failed (schema error)");
+  }
+  for (int32_t k = 0; k < n; k++) counts[k] = slots[k] < 0 ? 0 : c.count[slots[k]];
+  for (size_t j = 0; j < fill_slot.size(); j++) filled[j] = fill_slot[j];
+  *n_filled = (int32_t)fill_slot.size();
+  return NEEDLE_OK;
+}
 
 int needle_grammar_tools(const char* tools_json, int32_t maximum_calls, needle_grammar** out) {
   if (!tools_json || !out) return fail(NEEDLE_INVALID_TOOL_SCHEMA, "null argument");

@@ -1006,12 +1006,16 @@ __global__ void __launch_bounds__(kFinishThreads) k_finish(const ModelView m, co
   int chosen = -1;
   if (selecting) {
     const float* lg = st.logits + (int64_t)b * m.vocab;
-    // masked argmax / argmax (selectToken, runtime.ts:880-899; argmax, math.ts:140-151)
+    // masked argmax / argmax (selectToken, runtime.ts:880-899; argmax, math.ts:140-151).  An id list
+    // is ascending, so its earliest best entry is its lowest best id, as with a bit mask over ids.
     const bool masked = it.allowed_count >= 0;
+    const uint32_t* mask =
+        it.allowed_count == kAllowedMask ? st.masks + (int64_t)it.allowed_offset * st.mask_words : nullptr;
     const int n = masked ? it.allowed_count : m.vocab;
     float bv = -INFINITY;
     int bk = 0x7fffffff;
     for (int k = tid; k < n; k += kFinishThreads) {
+      if (mask && !((mask[k >> 5] >> (k & 31)) & 1u)) continue;
       const int id = masked ? (int)st.allowed[it.allowed_offset + k] : k;
       const float v = lg[id];
       if (bk == 0x7fffffff || v > bv) {  // ascending k: strict > keeps the earliest
@@ -1040,6 +1044,7 @@ __global__ void __launch_bounds__(kFinishThreads) k_finish(const ModelView m, co
           v0 = sv_[w];
           k0 = sk_[w];
         }
+      if (k0 == 0x7fffffff) k0 = 0;  // an empty mask: the host refuses those before the step
       s_id = masked ? (int)st.allowed[it.allowed_offset + k0] : k0;
     }
     // logSoftmaxAt (math.ts:153-160): max, then sum of exp(logit - max) as a binary64 tree sum.
@@ -1365,6 +1370,21 @@ cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView
   SchedView q{};
   if (sched) q = *sched;
   k_finish<<<n_host, kFinishThreads, 0, s>>>(m, sv, st, q, sched ? 1 : 0);
+  return cudaGetLastError();
+}
+
+// One block per staged mask: a coalesced copy of its words into its pool slot.
+__global__ void k_mask_scatter(const uint32_t* __restrict__ staged, const int32_t* __restrict__ slots, int words,
+                               uint32_t* __restrict__ pool) {
+  const uint32_t* src = staged + (int64_t)blockIdx.x * words;
+  uint32_t* dst = pool + (int64_t)slots[blockIdx.x] * words;
+  for (int k = threadIdx.x; k < words; k += blockDim.x) dst[k] = src[k];
+}
+
+cudaError_t launch_mask_scatter(const uint32_t* staged, const int32_t* slots, int n, int words, uint32_t* pool,
+                                cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  k_mask_scatter<<<n, 256, 0, s>>>(staged, slots, words, pool);
   return cudaGetLastError();
 }
 

@@ -151,3 +151,54 @@ def allowed_batch(grammars: Sequence[Optional[_Grammar]], output_bytes: Sequence
                                              ids.ctypes.data_as(C.POINTER(C.c_uint32)), vocab.size,
                                              counts.ctypes.data_as(C.POINTER(C.c_int32))))
     return [ids[k, :counts[k]].copy() for k in range(n)]
+
+
+class MaskCache:
+    """Allowed-token masks per grammar state (needle_mask_cache_*, include/needle_grammar.h) for the
+    clones of one template grammar: `lookup` gives each grammar's table slot and allowed count,
+    scanning only states not seen before; `table` is the [capacity][words] host table the slots
+    index (the masks a device pool copies, CudaEngine.masks_put)."""
+
+    def __init__(self, template: _Grammar, vocab: Vocabulary, capacity: int = 4096):
+        out = C.c_void_p()
+        check(lib().needle_mask_cache_open(template.handle, vocab._h, int(capacity), C.byref(out)))
+        self._h = out
+        self._vocab = vocab  # the cache reads it: keep it alive as long as the cache
+        self.capacity = int(capacity)
+        p = C.POINTER(C.c_uint32)()
+        words = C.c_int32()
+        check(lib().needle_mask_cache_table(self._h, C.byref(p), C.byref(words)))
+        self.words = words.value
+        self.table = np.ctypeslib.as_array(p, shape=(self.capacity, self.words))
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            self.table = None
+            lib().needle_mask_cache_free(h)
+            self._h = None
+
+    def lookup(self, grammars: Sequence[Optional[_Grammar]], output_bytes: Sequence[int], threads: int = 8):
+        """(slots, counts, filled): per grammar its table slot (-1 for None) and allowed count, and the
+        slots this call (re)filled."""
+        n = len(grammars)
+        slots = np.empty(max(n, 1), dtype=np.int32)
+        counts = np.empty(max(n, 1), dtype=np.int32)
+        filled = np.empty(max(n, 1), dtype=np.int32)
+        n_filled = C.c_int32()
+        hs = (C.c_void_p * max(n, 1))(*[g.handle if g is not None else None for g in grammars])
+        ob = (C.c_int64 * max(n, 1))(*[int(v) for v in output_bytes])
+        check(lib().needle_mask_cache_lookup(self._h, hs, ob, n, int(threads), slots.ctypes.data,
+                                             counts.ctypes.data, filled.ctypes.data, C.byref(n_filled)))
+        return slots[:n], counts[:n], filled[:n_filled.value].copy()
+
+    def ids(self, slot: int) -> np.ndarray:
+        """The ascending ids of a slot's mask."""
+        bits = np.unpackbits(self.table[slot].view(np.uint8), bitorder="little")
+        return np.flatnonzero(bits[:self._vocab.size]).astype(np.uint32)
+
+    @property
+    def stats(self):
+        h, m, e = C.c_int64(), C.c_int64(), C.c_int64()
+        check(lib().needle_mask_cache_stats(self._h, C.byref(h), C.byref(m), C.byref(e)))
+        return {"hits": h.value, "misses": m.value, "evictions": e.value}

@@ -18,6 +18,7 @@ CODES = ["INVALID_CACT", "UNSUPPORTED_CACT", "WEIGHTS_NOT_FOUND", "WEIGHTS_INTEG
          "WEBGPU_UNAVAILABLE", "BACKEND_UNAVAILABLE", "CONTEXT_OVERFLOW", "INVALID_TOOL_SCHEMA",
          "GRAMMAR_DEAD_END", "GENERATION_ABORTED"]
 TOKEN_PENDING = -1
+ALLOWED_MASK = -2  # NEEDLE_ALLOWED_MASK: allowed_offset names a slot of the device mask pool
 KV_INT8 = 0
 KV_FLOAT32 = 1
 NUMERICS_EXACT = 0
@@ -114,6 +115,8 @@ EXPORTS = {
     "needle_cuda_sched_ids": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t)]),
     "needle_cuda_sched_slot": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
                                          C.POINTER(C.c_int32)]),
+    "needle_cuda_mask_pool": (C.c_int, [C.c_void_p, C.c_int32]),
+    "needle_cuda_masks_put": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p]),
     "needle_cuda_kernel_launches": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64)]),
     "needle_cuda_profile": (C.c_int, [C.c_void_p, C.c_int32]),
     "needle_cuda_profile_read": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_char_p),
@@ -133,6 +136,13 @@ EXPORTS = {
                                          C.POINTER(C.c_int32)]),
     "needle_grammar_allowed_batch": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_int64), C.c_int32, C.c_void_p,
                                                C.c_int32, C.POINTER(C.c_uint32), C.c_int32, C.POINTER(C.c_int32)]),
+    "needle_mask_cache_open": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.POINTER(C.c_void_p)]),
+    "needle_mask_cache_free": (None, [C.c_void_p]),
+    "needle_mask_cache_table": (C.c_int, [C.c_void_p, C.POINTER(C.POINTER(C.c_uint32)), C.POINTER(C.c_int32)]),
+    "needle_mask_cache_lookup": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_int64), C.c_int32,
+                                           C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_int32)]),
+    "needle_mask_cache_stats": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64), C.POINTER(C.c_int64),
+                                          C.POINTER(C.c_int64)]),
 }
 
 _lib = None

@@ -9,7 +9,14 @@ list as selectToken does), and the chosen piece is fed to the grammar.  The scan
 step's layers run on the GPU (needle_cuda_step_begin / needle_cuda_step_end): the allowed ids only
 depend on tokens already chosen.  When the
 grammar completes, the chosen token is fed once more without a selection (agent.ts:193-196) and the
-slot is freed for the next sequence.  Prompts are fed one token per step through the same batched
+slot is freed for the next sequence.
+
+With a mask cache (`mask_cache` slots), the scan runs once per grammar state instead of once per
+sequence and step (needle_mask_cache_lookup, include/needle_grammar.h): sequences in the same state
+(the free content of a string, the same separator or key) share one mask, and a state seen before is
+not scanned again.  The masks live in a pool on the device (needle_cuda_mask_pool); only the masks of
+new states cross PCIe (needle_cuda_masks_put, one per state) and the items name their slot, so the
+selections are the same as with id lists (the best logit, ties to the lowest id).  Prompts are fed one token per step through the same batched
 steps; the constrained phase starts directly after the prompt, its pending token being the prompt's
 last token (random weights never emit <tool_call>).
 """
@@ -22,7 +29,7 @@ from typing import Callable, List, Optional, Sequence
 import numpy as np
 
 from .backend import StepRequest
-from .grammar import MAX_OUTPUT_BYTES, ToolCallGrammar, Vocabulary, allowed_batch
+from .grammar import MAX_OUTPUT_BYTES, MaskCache, ToolCallGrammar, Vocabulary, allowed_batch
 
 
 def synthetic_tools(seed: int = 5, n_tools: int = 3):
@@ -73,12 +80,16 @@ class DecodeStats:
     grammar_seconds: float = 0.0
     engine_seconds: float = 0.0
     items: int = 0        # step items sent to the engine
-    allowed_ids: int = 0  # allowed ids sent with them
+    allowed_ids: int = 0  # allowed ids sent with them as id lists
+    masked_items: int = 0  # selections over a device mask (mask cache)
+    masks_put: int = 0     # masks copied to the device (new grammar states)
 
 
 class ConstrainedDecoder:
     def __init__(self, engine, vocab: Vocabulary, tools: Sequence[dict], maximum_calls: int = 4,
-                 maximum_new_tokens: int = 256, threads: int = 8):
+                 maximum_new_tokens: int = 256, threads: int = 8, mask_cache: int = 0):
+        """`mask_cache` > 0: keep allowed masks per grammar state in a cache of that many slots and
+        a device pool of the same size (at least the engine's slot count); 0: id lists per step."""
         self.engine = engine
         self.vocab = vocab
         self.tools = list(tools)
@@ -86,6 +97,12 @@ class ConstrainedDecoder:
         self.maximum_new = max(1, maximum_new_tokens)
         self.threads = threads
         self.template = ToolCallGrammar(self.tools, maximum_calls)  # validates the tools once
+        self.cache = None
+        if mask_cache:
+            if mask_cache < engine.max_seqs:
+                raise ValueError("mask_cache needs at least one slot per engine slot")
+            self.cache = MaskCache(self.template, vocab, mask_cache)
+            engine.mask_pool(mask_cache)
 
     def run(self, prompts: Sequence[np.ndarray], slots: Optional[int] = None, max_steps: Optional[int] = None,
             hook: Optional[Callable[[int], None]] = None) -> tuple[List[ToolCallResult], DecodeStats]:
@@ -155,19 +172,33 @@ class ConstrainedDecoder:
                     r.select = False  # completed: this step is the final feed (no selection)
             selecting = [i for i, r in enumerate(requests) if r.select]
             t2 = time.perf_counter()
-            masks = allowed_batch([state[requests[i].seq]["grammar"] for i in selecting],
-                                  [state[requests[i].seq]["out"] for i in selecting], self.vocab, self.threads)
-            t3 = time.perf_counter()
+            grammars = [state[requests[i].seq]["grammar"] for i in selecting]
+            outs = [state[requests[i].seq]["out"] for i in selecting]
+            if self.cache is not None:
+                mslots, counts, filled = self.cache.lookup(grammars, outs, self.threads)
+                t3 = time.perf_counter()
+                eng.masks_put(filled, self.cache.table)
+                stats.masks_put += int(filled.size)
+                sizes = counts.tolist()
+                for i, slot in zip(selecting, mslots.tolist()):
+                    requests[i].mask_slot = slot
+            else:
+                masks = allowed_batch(grammars, outs, self.vocab, self.threads)
+                t3 = time.perf_counter()
+                sizes = [int(m.size) for m in masks]
+                for i, ids in zip(selecting, masks):
+                    requests[i].allowed = ids
             stats.grammar_seconds += t3 - t2
-            for i, ids in zip(selecting, masks):
-                requests[i].allowed = ids
-                if ids.size == 0:  # GRAMMAR_DEAD_END: no token can continue; the sequence stops here
+            for i, size in zip(selecting, sizes):
+                if size == 0:  # GRAMMAR_DEAD_END: no token can continue; the sequence stops here
                     requests[i].select = False
                     requests[i].allowed = None
+                    requests[i].mask_slot = None
                     results[state[requests[i].seq]["seq"]].dead_end = True
                     state[requests[i].seq]["phase"] = "dead"
             stats.items += len(requests)
             stats.allowed_ids += sum(int(r.allowed.size) for r in requests if r.allowed is not None)
+            stats.masked_items += sum(1 for r in requests if r.select and r.mask_slot is not None)
             chosen = eng.step_end(requests)
             stats.engine_seconds += (t1 - t0) + (time.perf_counter() - t3)
             stats.steps += 1

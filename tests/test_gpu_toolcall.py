@@ -72,3 +72,35 @@ def test_constrained_decoding_matches_oracle(setup, oracle):
         if res.complete:
             calls = json.loads(res.text.decode())
             assert calls == res.calls and all(c["name"] in names for c in calls)
+
+
+def test_device_masks_match_oracle(setup, oracle):
+    """The same decode with allowed masks kept per grammar state in a device pool (the items name a
+    pool slot; only new states' masks are copied): the same token ids as the oracle's id lists, with
+    a table small enough to evict."""
+    from needle_b200.backend import CudaEngine, StepRequest
+    from needle_b200 import toolcall
+    from needle_b200.native import NeedleError
+    archive, vocab, tools, model = setup
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, 8192, n).astype(np.int32) for n in (40, 33, 57, 21, 48)]
+    maximum_new = 48
+    with CudaEngine(archive, device=0, max_seqs=3, max_len=160, max_sink=16) as eng:
+        dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=maximum_new, threads=4,
+                                          mask_cache=12)
+        results, stats = dec.run(prompts)
+        assert stats.allowed_ids == 0 and stats.masked_items == stats.constrained_tokens
+        assert 0 < stats.masks_put < stats.masked_items
+        assert dec.cache.stats["evictions"] > 0
+        # an item naming a slot that holds no mask is refused before anything runs
+        eng.mask_pool(4)
+        eng.reset(0, 16, 0)
+        with pytest.raises(NeedleError) as e:
+            eng.step([StepRequest(0, 5, True, mask_slot=2)])
+        assert e.value.code == "INVALID_CACT"
+        with pytest.raises(NeedleError):
+            eng.step([StepRequest(0, 5, True, mask_slot=4)])
+    for k, (p, res) in enumerate(zip(prompts, results)):
+        ids, complete, dead = oracle_constrained(oracle, model, vocab, tools, p, maximum_new)
+        assert res.ids == ids, k
+        assert res.complete == complete and res.dead_end == dead, k

@@ -33,6 +33,20 @@ class FakeEngine:
         self.hist = [None] * max_seqs
         self.pending = None
         self.steps = 0
+        self.pool = None
+
+    def mask_pool(self, capacity):
+        self.pool = np.zeros((capacity, (self.vocab + 31) // 32), dtype=np.uint32)
+
+    def masks_put(self, slots, table):  # between step_begin and step_end, as the decoder calls it
+        for s in np.asarray(slots).tolist():
+            self.pool[s] = table[s]
+
+    def _allowed(self, r):
+        if r.mask_slot is None:
+            return r.allowed
+        bits = np.unpackbits(self.pool[r.mask_slot].view(np.uint8), bitorder="little")[:self.vocab]
+        return np.flatnonzero(bits)
 
     def reset(self, slot, maximum_length, sink_length=0):
         assert 0 <= slot < self.max_seqs and self.pending is None
@@ -51,8 +65,9 @@ class FakeEngine:
             assert began_select or not r.select  # a select may be cleared, not set
             self.hist[r.seq].append(r.token)
             if r.select:
-                assert r.allowed is not None and r.allowed.size > 0
-                out.append((select(fake_logits(self.hist[r.seq], self.vocab), r.allowed), 0.0))
+                allowed = self._allowed(r)
+                assert allowed is not None and allowed.size > 0
+                out.append((select(fake_logits(self.hist[r.seq], self.vocab), allowed), 0.0))
             else:
                 out.append(None)
         self.pending = None
@@ -113,6 +128,29 @@ def test_batched_decoder_matches_one_sequence_at_a_time(env):
     assert any(r.complete for r in results)
 
 
+@pytest.mark.parametrize("capacity", [6, 512])
+def test_mask_cache_decodes_the_same_tokens(env, capacity):
+    """Masks per grammar state in a device pool (a table far smaller than the states visited, and
+    one that holds them all) select exactly the tokens of per-step id lists."""
+    grammar, toolcall, vocab = env
+    tools = toolcall.synthetic_tools(5)
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, vocab.size, int(rng.integers(2, 5))).astype(np.int32) for _ in range(9)]
+    plain, _ = toolcall.ConstrainedDecoder(FakeEngine(4, vocab.size), vocab, tools, maximum_new_tokens=120,
+                                           threads=3).run(prompts)
+    eng = FakeEngine(4, vocab.size)
+    dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=120, threads=3, mask_cache=capacity)
+    cached, stats = dec.run(prompts)
+    for a, b in zip(plain, cached):
+        assert a.ids == b.ids and a.complete == b.complete and a.dead_end == b.dead_end and a.calls == b.calls
+    assert stats.allowed_ids == 0 and stats.masked_items == stats.constrained_tokens
+    assert 0 < stats.masks_put < stats.masked_items  # states repeat across sequences and steps
+    if capacity == 6:
+        assert dec.cache.stats["evictions"] > 0
+    with pytest.raises(ValueError):
+        toolcall.ConstrainedDecoder(FakeEngine(4, vocab.size), vocab, tools, mask_cache=3)
+
+
 def test_slots_are_reused_and_histories_match(env):
     """After a sequence ends its slot is reset for the next one; what each sequence fed is exactly
     the reference loop's (prompt, pending tokens, the final token of a completed call)."""
@@ -168,13 +206,15 @@ def test_step_items_pack_as_the_c_struct():
     from needle_b200.backend import CudaEngine
     reqs = [StepRequest(3, 7, True, np.array([1, 5, 9], dtype=np.uint32)), StepRequest(1, -1, False),
             StepRequest(0, 2, True), StepRequest(2, 4, True, np.array([8], dtype=np.uint32)),
-            StepRequest(4, 6, False, np.array([3], dtype=np.uint32))]  # a mask without select is ignored
+            StepRequest(4, 6, False, np.array([3], dtype=np.uint32)),  # a mask without select is ignored
+            StepRequest(5, 1, True, mask_slot=17), StepRequest(6, 2, False, mask_slot=4)]
     items, allowed = CudaEngine._items(reqs)
     assert items.dtype == np.int32 and items.shape[1] * 4 == ctypes.sizeof(native.StepItem)
     arr = (native.StepItem * len(reqs)).from_buffer_copy(items.tobytes())
     got = [(a.seq, a.token, a.select, a.allowed_count) for a in arr]
-    assert got == [(3, 7, 1, 3), (1, -1, 0, -1), (0, 2, 1, -1), (2, 4, 1, 1), (4, 6, 0, -1)]
-    assert arr[0].allowed_offset == 0 and arr[3].allowed_offset == 3
+    assert got == [(3, 7, 1, 3), (1, -1, 0, -1), (0, 2, 1, -1), (2, 4, 1, 1), (4, 6, 0, -1),
+                   (5, 1, 1, native.ALLOWED_MASK), (6, 2, 0, -1)]
+    assert arr[0].allowed_offset == 0 and arr[3].allowed_offset == 3 and arr[5].allowed_offset == 17
     np.testing.assert_array_equal(allowed, [1, 5, 9, 8])
     items, allowed = CudaEngine._items([StepRequest(0, 1, False)])
     assert allowed is None and items[0].tolist() == [0, 1, 0, -1, 0]
