@@ -29,7 +29,16 @@ def _matrix(torch, rows, inputs, bits):
     packed, norms = synth.random_cq_matrix(rows, inputs, bits, seed=12)
     d_packed = torch.from_numpy(packed.copy()).cuda()
     d_norms = torch.from_numpy(norms.view(np.int16).copy()).cuda()
-    return native.CqMatrixDesc(d_packed.data_ptr(), d_norms.data_ptr(), rows, inputs, 128, bits), (d_packed, d_norms)
+    desc = native.CqMatrixDesc(d_packed.data_ptr(), d_norms.data_ptr(), rows, inputs, 128, bits)
+    return desc, (d_packed, d_norms, packed, norms)
+
+
+def _oracle_rows(oracle, desc, keep, x):
+    """The oracle's matvec of every batch row (the CPU restatement of the reference's CQ matvec)."""
+    from needle_b200 import synth
+    cb = synth.lloyd_max_codebook()
+    m = oracle.CqMatrix(desc.rows, desc.input_size, 128, desc.bits, keep[2], keep[3], cb[:4], cb[4:12], cb[12:])
+    return np.stack([m.matvec(row) for row in x])
 
 
 def _run(torch, fn, desc, x):
@@ -42,7 +51,7 @@ def _run(torch, fn, desc, x):
     return d_y.cpu().numpy()
 
 
-def test_noalloc_matches_allocating_entry_point_twice_in_a_row(cuda):
+def test_noalloc_matches_allocating_entry_point_twice_in_a_row(cuda, oracle):
     from needle_b200 import native, synth
     lib = native.lib()
     desc, keep = _matrix(cuda, 1000, 2048, 4)
@@ -56,6 +65,9 @@ def test_noalloc_matches_allocating_entry_point_twice_in_a_row(cuda):
     want2 = _run(cuda, lib.needle_cuda_cq_matvec_dev, desc2, x2)
     np.testing.assert_array_equal(got1, want1)  # the exact kernels are bitwise deterministic
     np.testing.assert_array_equal(got2, want2)
+    # and both are the oracle's, bit for bit
+    np.testing.assert_array_equal(got1, _oracle_rows(oracle, desc, keep, x1))
+    np.testing.assert_array_equal(got2, _oracle_rows(oracle, desc2, keep2, x2))
 
 
 def test_noalloc_rejects_batches_beyond_its_scratch(cuda):
