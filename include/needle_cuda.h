@@ -66,7 +66,14 @@ typedef struct needle_opts {
   int32_t micro_batches; /* device-scheduled steps run as this many micro-batches on their own
                             streams (1..8; 0 = the default, 4), so latency-bound kernels of one
                             overlap the others' */
-  int32_t reserved[8];
+  int32_t sched_chunk;   /* device-scheduled steps: up to this many prompt positions of a slot that
+                            is still reading its prompt go into one step, as a chunk of items (2..64;
+                            0 or 1 = one position per slot and step, the default).  A chunk never
+                            reaches past the slot's KV window (prompt positions beyond it go one
+                            per step) and holds no selecting position; the results are the same */
+  int32_t sched_items;   /* device-scheduled steps with chunks: items one step may hold, spread over
+                            the micro-batches with whole chunks (>= max_seqs; 0 = 2 x max_seqs) */
+  int32_t reserved[6];
 } needle_opts;
 
 typedef struct needle_ctx needle_ctx;

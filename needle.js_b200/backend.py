@@ -40,7 +40,8 @@ class CudaEngine:
     """One engine context on one GPU (needle_cuda_open .. needle_cuda_close)."""
 
     def __init__(self, archive: bytes, device: int = 0, max_seqs: int = 1, max_len: int = 2048,
-                 max_sink: int = 160, kv_cache: str = "int8", numerics: str = "exact", micro_batches: int = 0):
+                 max_sink: int = 160, kv_cache: str = "int8", numerics: str = "exact", micro_batches: int = 0,
+                 sched_chunk: int = 0, sched_items: int = 0):
         if kv_cache not in ("int8", "float32"):
             raise NeedleError("BACKEND_UNAVAILABLE", f"unknown kvCache {kv_cache!r}")
         modes = {"exact": native.NUMERICS_EXACT, "fast": native.NUMERICS_FAST,
@@ -51,7 +52,8 @@ class CudaEngine:
         opts = native.default_opts(device=device, max_seqs=max_seqs, max_len=max_len, max_sink=max_sink,
                                    kv_mode=native.KV_FLOAT32 if kv_cache == "float32" else native.KV_INT8,
                                    numerics=modes[numerics],
-                                   micro_batches=micro_batches)
+                                   micro_batches=micro_batches, sched_chunk=sched_chunk,
+                                   sched_items=sched_items)
         self.numerics = numerics
         self.kv_cache = kv_cache
         h = C.c_void_p()

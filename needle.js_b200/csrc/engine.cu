@@ -340,6 +340,8 @@ struct needle_ctx {
   cudaEvent_t mb_fork[kMaxMicro][2] = {}, mb_join[kMaxMicro][2] = {}, mb_done[kMaxMicro] = {};
   cudaEvent_t split_ev = nullptr;
   int micro = 4;  // micro-batches of a device-scheduled step (needle_opts.micro_batches)
+  int sched_chunk = 0;  // prompt positions per slot and scheduled step (needle_opts.sched_chunk; 0: one)
+  int sched_items = 0;  // items a scheduled step with chunks may hold (needle_opts.sched_items)
   // The device-scheduled step captured as a CUDA graph after one eager step.
   cudaGraphExec_t sched_graph = nullptr;
   int64_t graph_launches = 0;
@@ -720,7 +722,8 @@ void build_state(needle_ctx& C) {
   }
   C.slots.assign(S, SlotHost{});
   StepView& st = C.stv;
-  const size_t B = size_t(std::max(S, kPrefillChunk));
+  // scheduled steps with chunks use item rows up to ceil(sched_items / M) * M < sched_items + kMaxMicro
+  const size_t B = size_t(std::max({S, kPrefillChunk, C.sched_items > 0 ? C.sched_items + kMaxMicro : 0}));
   st.items = C.dalloc<DevItem>(B);
   st.chunk = 0;
   st.lanes = C.dalloc<float>(B * kLaneWidth);
@@ -853,6 +856,7 @@ StepView half_view(const needle_ctx& C, int offset, const int32_t* n_items, cons
   const int64_t o = offset, ns = C.mv.n_sites;
   StepView v = st;
   v.items = st.items + o;
+  v.lanes = st.lanes + o * kLaneWidth;
   v.n_items = n_items;
   v.n_select = n_select;
   v.prep_engram = st.prep_engram + o * ns * kDim;
@@ -942,9 +946,9 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
         if (e == cudaSuccess) e = launch_attention_gate(st, n_host, s0);
         return e;
       }, s0);
-    } else if (st.chunk) {  // every item's K/V before any item attends
-      C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 1); }, s0);
-      C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 2); }, s0);
+    } else if (st.chunk) {  // every chunk item's K/V before any of them attends
+      C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 3); }, s0);
+      C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0, 4); }, s0);
     } else {
       C.timed(P_ATTN, [&] { return launch_attention(m, sv, st, l, n_host, s0); }, s0);
     }
@@ -969,21 +973,32 @@ void enqueue_sched_step(needle_ctx& C) {
   const int S = C.sched.n_slots;
   const int M = C.profiling ? 1 : std::max(1, std::min(C.micro, S / 32));
   const int h = (S + M - 1) / M;
+  // with prompt chunks, micro-batch k holds slots [k * h, (k + 1) * h) in item rows [k * hi, ...)
+  const bool chunks = C.sched_chunk >= 2;
+  const int hi = chunks ? (C.sched_items + M - 1) / M : h;
   C.timed(P_SCHED, [&] {
     cudaError_t e = launch_sched_admit(C.sv, C.sched, C.mv.kv_window, C.stream);
     if (e != cudaSuccess) return e;
+    if (chunks)
+      return launch_sched_chunked(C.sv, C.stv, C.sched, C.d_counts, h, hi, M, C.sched_chunk, C.mv.kv_window,
+                                  C.stream);
     return launch_sched(C.sv, C.stv, C.sched, C.d_counts, h, M, C.stream);
   });
+  auto view = [&](int off, const int32_t* n_items, const int32_t* n_select) {
+    StepView v = half_view(C, off, n_items, n_select);
+    v.chunk = chunks ? 1 : 0;
+    return v;
+  };
   if (M == 1) {
-    enqueue_step(C, half_view(C, 0, C.d_counts, C.d_counts + 1), S, true, &C.sched, lane_a(C));
+    enqueue_step(C, view(0, C.d_counts, C.d_counts + 1), hi, true, &C.sched, lane_a(C));
     return;
   }
   cuda_check(cudaEventRecord(C.split_ev, C.stream), "split");
   for (int k = 1; k < M; k++) cuda_check(cudaStreamWaitEvent(C.mb_main[k], C.split_ev, 0), "split");
   for (int k = 0; k < M; k++) {
-    const int off = k * h, n = std::min(h, S - off);
-    if (n <= 0) continue;
-    enqueue_step(C, half_view(C, off, C.d_counts + 2 + 2 * k, C.d_counts + 3 + 2 * k), n, true, &C.sched,
+    const int n = chunks ? hi : std::min(h, S - k * h);
+    if (n <= 0 || k * h >= S) continue;
+    enqueue_step(C, view(k * hi, C.d_counts + 2 + 2 * k, C.d_counts + 3 + 2 * k), n, true, &C.sched,
                  lane_k(C, k));
   }
   for (int k = 1; k < M; k++) {
@@ -1321,6 +1336,10 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
     require(o.max_seqs >= 1 && o.max_seqs <= 65536, NEEDLE_BACKEND_UNAVAILABLE, "max_seqs out of range");
     require(o.micro_batches >= 0 && o.micro_batches <= kMaxMicro, NEEDLE_BACKEND_UNAVAILABLE,
             "micro_batches out of range (0..8)");
+    require(o.sched_chunk >= 0 && o.sched_chunk <= kPrefillChunk, NEEDLE_BACKEND_UNAVAILABLE,
+            "sched_chunk out of range (0..64)");
+    require(o.sched_items == 0 || (o.sched_items >= o.max_seqs && o.sched_items <= 8 * o.max_seqs + kPrefillChunk),
+            NEEDLE_BACKEND_UNAVAILABLE, "sched_items out of range (max_seqs .. 8 x max_seqs + 64)");
     require(o.max_sink >= 0 && o.max_len >= 1, NEEDLE_BACKEND_UNAVAILABLE, "max_len / max_sink out of range");
     int devices = 0;
     cuda_check(cudaGetDeviceCount(&devices), "cudaGetDeviceCount");
@@ -1355,6 +1374,10 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
     }
     cuda_check(cudaEventCreateWithFlags(&C->split_ev, cudaEventDisableTiming), "cudaEventCreate");
     if (o.micro_batches > 0) C->micro = std::min(kMaxMicro, int(o.micro_batches));
+    if (o.sched_chunk >= 2) {
+      C->sched_chunk = o.sched_chunk;
+      C->sched_items = o.sched_items > 0 ? o.sched_items : 2 * o.max_seqs;
+    }
     C->fast = o.numerics == NEEDLE_NUMERICS_FAST || o.numerics == NEEDLE_NUMERICS_FAST_ATTENTION;
     C->fast_attention = o.numerics == NEEDLE_NUMERICS_FAST_ATTENTION;
     cuda_check(cudaDeviceGetAttribute(&C->sms, cudaDevAttrMultiProcessorCount, C->device), "device attribute");
@@ -1687,6 +1710,8 @@ int needle_cuda_prefill(needle_ctx* ctx, int32_t seq, const int32_t* ids, int32_
         d.allowed_count = -1;
         d.position = hs.position + b;
         d.out_index = b;
+        d.chunk_index = b;
+        d.chunk_len = k;
         C.h_items[b] = d;
       }
       C.h_counts[0] = k;
@@ -1845,6 +1870,8 @@ int needle_cuda_sched_load(needle_ctx* ctx, int32_t n_slots, const int32_t* prom
   return guarded([&] {
     needle_ctx& C = *ctx_of(ctx);
     require(n_slots >= 1 && n_slots <= C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "n_slots out of range");
+    require(C.sched_chunk < 2 || n_slots <= 1024, NEEDLE_BACKEND_UNAVAILABLE,
+            "prompt chunks (sched_chunk) schedule at most 1024 slots");
     require(n_seqs >= 0 && prompt_offsets && gen_steps && (n_seqs == 0 || prompt_ids), NEEDLE_BACKEND_UNAVAILABLE,
             "bad queue");
     const int window = C.mv.kv_window;

@@ -85,6 +85,13 @@ struct DevItem {
   int32_t position;         // filled by k_embed
   int32_t out_index;        // caller's index
   int32_t flags;            // kItemLanes | kItemEngrams: inputs given by a resident session
+  // A prefill chunk: chunk_len (>= 2) consecutive positions of one slot as consecutive items, this
+  // one at chunk_index; 0 for an item of its own.  The chunk's items get their positions and tokens
+  // from the item, their lanes per item (StepView::lanes), read the engram taps and token history
+  // of the chunk's earlier items, append K/V before any of them attends (StepView::chunk), and the
+  // slot advances once, at the chunk's last item.
+  int32_t chunk_index;
+  int32_t chunk_len;
 };
 
 // DevItem::flags.  A resident-session item (needle_cuda_resident_forward) brings the lanes that
@@ -128,8 +135,8 @@ struct StepView {
   float* attn_out;          // [B][512] attention output (before the gate)
   int32_t* attn_count;      // [B] visible cache slots: slots 0 .. count-1 in the ring layout
   int64_t* attn_row;        // [B] cache row of (item, layer, KV head 0)
-  int32_t chunk;
-  float* lanes;             // [B][4][512] (chunk steps; kItemLanes items)
+  int32_t chunk;            // the step may hold chunk items (DevItem::chunk_len): K/V append first
+  float* lanes;             // [B][4][512] (chunk items; kItemLanes items)
   const uint32_t* engram_in;  // [B][2][kMaxTables]: table indices, then valid flags (kItemEngrams)
 };
 
@@ -155,8 +162,8 @@ cudaError_t launch_layer(const ModelView& m, const SlotView& sv, const StepView&
                          int n_host, cudaStream_t s);
 // Sinkhorn routing of the layer's items (reads and writes StepView::route[4..19]).
 cudaError_t launch_route(const StepView& st, int n_host, cudaStream_t s);
-// Chunk steps (StepView::chunk) launch it twice: part 1 appends every item's K/V, part 2 attends;
-// otherwise part 0 does both per item.
+// Steps that may hold chunk items (StepView::chunk) launch it twice: part 3 appends the chunk
+// items' K/V, part 4 attends (and appends for the other items); otherwise part 0 does both per item.
 cudaError_t launch_attention(const ModelView& m, const SlotView& sv, const StepView& st, int layer,
                              int n_host, cudaStream_t s, int part = 0);
 cudaError_t launch_finish(const ModelView& m, const SlotView& sv, const StepView& st, int n_host,
@@ -168,6 +175,11 @@ cudaError_t launch_mask_scatter(const uint32_t* staged, const int32_t* slots, in
 // selecting) of each of `parts` micro-batches], micro-batch k being items [k * part, (k + 1) * part).
 cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts, int part,
                          int parts, cudaStream_t s);
+// The same with prompt chunks: micro-batch k holds slots [k * slots_per_part, ...) and item rows
+// [k * items_per_part, ...); a prefilling slot takes up to chunk_max prompt positions (n_slots <= 1024).
+cudaError_t launch_sched_chunked(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts,
+                                 int slots_per_part, int items_per_part, int parts, int chunk_max, int window,
+                                 cudaStream_t s);
 cudaError_t launch_sched_admit(const SlotView& sv, const SchedView& q, int window, cudaStream_t s);
 cudaError_t launch_attention_dev(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
                                  const float* vs, const int32_t* counts, int32_t batch,

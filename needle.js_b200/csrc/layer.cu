@@ -63,8 +63,8 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
   DevItem it = st.items[b];
   SeqState* q = sv.seq + it.slot;
   if (tid == 0) {
-    // a chunk item's token and position are given (p0 + b); otherwise the slot's
-    const int p = st.chunk ? it.position : q->position;
+    // a chunk item's token and position are given (p0 + chunk_index); otherwise the slot's
+    const int p = it.chunk_len ? it.position : q->position;
     const int token = it.token >= 0 ? it.token : q->pending;
     s_token = token;
     s_pos = p;
@@ -91,8 +91,8 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
       uint32_t tok;
       if (off > p) tok = 0u;
       else if (off == 0) tok = (uint32_t)token;
-      else if (st.chunk && off <= b) tok = (uint32_t)st.items[b - off].token;
-      else tok = (uint32_t)q->hist[st.chunk ? off - b - 1 : off - 1];
+      else if (it.chunk_len && off <= it.chunk_index) tok = (uint32_t)st.items[b - off].token;
+      else tok = (uint32_t)q->hist[it.chunk_len ? off - it.chunk_index - 1 : off - 1];
       hash = (hash ^ tok) * kEngramPrime;
     }
     hash = hash ^ (hash >> 15);
@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
     evalid[tid] = (order - 1) <= p;
   }
   __syncthreads();
-  if (tid == 0 && !st.chunk && !(it.flags & kItemEngrams)) {  // a chunk's history advances in k_finish
+  if (tid == 0 && !it.chunk_len && !(it.flags & kItemEngrams)) {  // a chunk's history advances in k_finish
     q->hist[2] = q->hist[1];
     q->hist[1] = q->hist[0];
     q->hist[0] = token;
@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kThreads) k_embed(const ModelView m, const Slo
     const double inverse_root = 1.0 / sqrt((double)kGroup);
     const float e = f32((double)v[c] * inverse_root);
     const float scaled = f32((double)e * sqrt((double)kDim));
-    float* x = st.chunk ? st.lanes + (int64_t)b * kLaneWidth : sv.x + (int64_t)it.slot * kLaneWidth;
+    float* x = it.chunk_len ? st.lanes + (int64_t)b * kLaneWidth : sv.x + (int64_t)it.slot * kLaneWidth;
 #pragma unroll
     for (int lane = 0; lane < kLanes; lane++) x[lane * kDim + c] = scaled;
     __syncthreads();
@@ -174,7 +174,8 @@ struct LayerSmem {
 };
 
 __device__ void engram_mix(const ModelView& m, const SlotView& sv, const StepView& st, int b,
-                           int slot, int p) {
+                           const DevItem& it) {
+  const int slot = it.slot, p = it.position;
   // #engramStep ring write and causal tap convolution (runtime.ts:854-873).  The engram position
   // equals the token position: both start at 0 on reset and advance once per step.
   const int c = threadIdx.x;
@@ -184,14 +185,15 @@ __device__ void engram_mix(const ModelView& m, const SlotView& sv, const StepVie
   for (int si = 0; si < m.n_sites; si++) {
     const float now = st.engram_kv[(((int64_t)b * m.n_sites + si) * 2 + 1) * kDim + c];
     float* ring = sv.ring + ((int64_t)slot * m.n_sites + si) * depth * kDim;
-    if (!st.chunk) ring[(p % depth) * kDim + c] = now;
+    if (!it.chunk_len) ring[(p % depth) * kDim + c] = now;
     float mixed = 0.0f;
     for (int tap = 0; tap < m.taps; tap++) {
       const int back = tap * m.max_order, prev = p - back;
       if (prev < 0) continue;
       float value;
       if (tap == 0) value = now;
-      else if (st.chunk && back <= b) value = st.engram_kv[((((int64_t)(b - back)) * m.n_sites + si) * 2 + 1) * kDim + c];
+      else if (it.chunk_len && back <= it.chunk_index)
+        value = st.engram_kv[((((int64_t)(b - back)) * m.n_sites + si) * 2 + 1) * kDim + c];
       else value = ring[(prev % depth) * kDim + c];
       mixed = f32((double)mixed + (double)m.taps_w[((int64_t)si * m.taps + tap) * kDim + c] * (double)value);
     }
@@ -344,7 +346,7 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
   const int tid = threadIdx.x;
   const DevItem it = st.items[b];
   const int slot = it.slot, p = it.position;
-  float* xg = st.chunk ? st.lanes + (int64_t)b * kLaneWidth : sv.x + (int64_t)slot * kLaneWidth;
+  float* xg = it.chunk_len ? st.lanes + (int64_t)b * kLaneWidth : sv.x + (int64_t)slot * kLaneWidth;
   {
     float v[kLaneWidth / kThreads];  // all loads in flight before the first store
 #pragma unroll
@@ -352,7 +354,7 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
 #pragma unroll
     for (int k = 0; k < kLaneWidth / kThreads; k++) S.xl[tid + k * kThreads] = v[k];
   }
-  if (layer == 0 && m.n_sites > 0) engram_mix(m, sv, st, b, slot, p);
+  if (layer == 0 && m.n_sites > 0) engram_mix(m, sv, st, b, it);
 
   const double inv_root_128 = 1.0 / sqrt((double)kGroup);
   const int c = tid;
@@ -416,7 +418,7 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
 
   if (layer == m.layers) {
     // a chunk's last item leaves its lanes in the slot (what a one-token step leaves there)
-    if (st.chunk && b == *st.n_items - 1) {
+    if (it.chunk_len && it.chunk_index == it.chunk_len - 1) {
 #pragma unroll
       for (int lane = 0; lane < kLanes; lane++) sv.x[(int64_t)slot * kLaneWidth + lane * kDim + c] = S.xl[lane * kDim + c];
     }
@@ -811,8 +813,10 @@ __device__ void attend_pair_f32(const float* kf, const float* vf, int count, Slo
   __syncthreads();
 }
 
-// part 0: append this item's K/V, then attend; part 1: append only; part 2: attend only (a
-// chunk's items attend after all of them appended).
+// part 0: append this item's K/V, then attend; part 1: append only (fast numerics attends with
+// another kernel); part 2: attend only; part 3: append the chunk items only; part 4: the chunk items
+// attend, every other item appends and attends.  A step that holds chunk items runs parts 3 and 4:
+// every item of a chunk appends before any of them attends.
 template <int Sc, int Mix, int Mc>
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, const SlotView sv,
                                                            const StepView st, int l, int part) {
@@ -824,6 +828,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
   if (b >= *st.n_items) return;
   const int tid = threadIdx.x;
   const DevItem it = st.items[b];
+  const bool chunk_item = it.chunk_len > 0;
+  if (part == 3 && !chunk_item) return;
+  const bool append = part == 0 || part == 1 || part == 3 || (part == 4 && !chunk_item);
+  const bool attend = part == 0 || part == 2 || part == 4;
   const int slot = it.slot, p = it.position;
   const SeqState seq = sv.seq[slot];
   const float* qkvg = st.qkvg + (int64_t)b * 1536;
@@ -864,7 +872,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
     return sink + (pos - sink) % window;
   };
   const int64_t head_base = (((int64_t)slot * sv.layers + l) * kKvHeads + h) * sv.capacity;
-  if (part != 2) {
+  if (append) {
     double mk = 0.0, mv = 0.0;
     if (tid < kHeadDim) {
       mk = fabs((double)kv[tid]);
@@ -903,10 +911,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
     }
     __syncthreads();
   }
-  if (part == 1) {
+  if (!attend) {
     // fast numerics attends with the int8-MMA kernel next: leave it the rotated queries, the visible
     // count (slots 0 .. count-1 of the ring hold exactly the visible positions) and the cache row
-    if (st.qrope) {
+    if (part == 1 && st.qrope) {
       st.qrope[(int64_t)b * kDim + 2 * h * kHeadDim + tid] = qv[tid];
       if (h == 0 && tid == 0) {
         const int prefix = min(sink, p + 1);
@@ -1073,14 +1081,14 @@ __global__ void __launch_bounds__(kFinishThreads) k_finish(const ModelView m, co
       seq->pending = chosen;
     }
   }
-  if (st.chunk) {
+  if (it.chunk_len) {
     // a prefill chunk: the engram values of its last ring-depth items enter the ring now that every
     // item has read its taps (k_layer, layer 0), and the slot advances once, past the last item,
     // with the chunk's last three tokens as its history
-    const int n = *st.n_items;
+    const int n = it.chunk_len, ci = it.chunk_index;
     if (m.n_sites > 0) {
       const int depth = (m.taps - 1) * m.max_order + 1;
-      if (b >= n - depth) {
+      if (ci >= n - depth) {
         for (int si = 0; si < m.n_sites; si++) {
           float* ring = sv.ring + ((int64_t)it.slot * m.n_sites + si) * depth * kDim;
           for (int c = tid; c < kDim; c += kFinishThreads)
@@ -1088,14 +1096,15 @@ __global__ void __launch_bounds__(kFinishThreads) k_finish(const ModelView m, co
         }
       }
     }
-    if (tid == 0 && b == n - 1) {
+    if (tid == 0 && ci == n - 1) {
       int h[3];
 #pragma unroll
-      for (int k = 0; k < 3; k++) h[k] = k <= b ? st.items[b - k].token : seq->hist[k - b - 1];
+      for (int k = 0; k < 3; k++) h[k] = k <= ci ? st.items[b - k].token : seq->hist[k - ci - 1];
       seq->hist[0] = h[0];
       seq->hist[1] = h[1];
       seq->hist[2] = h[2];
       seq->position = it.position + 1;
+      if (has_sched) atomicAdd(reinterpret_cast<unsigned long long*>(q.processed), (unsigned long long)n);
     }
     return;
   }
@@ -1267,6 +1276,8 @@ __global__ void __launch_bounds__(1024) k_sched(const SlotView sv, const StepVie
     it.position = seq.position;
     it.out_index = idx;
     it.flags = 0;
+    it.chunk_index = 0;
+    it.chunk_len = 0;
     st.items[idx] = it;
   }
   __syncthreads();
@@ -1278,6 +1289,131 @@ __global__ void __launch_bounds__(1024) k_sched(const SlotView sv, const StepVie
       counts[2 + 2 * k] = min(max(n - k * part, 0), part);
       counts[3 + 2 * k] = min(max(c_sel - k * part, 0), part);
     }
+  }
+}
+
+// Exclusive prefix sum of `v` over the block (a multiple of 32 threads, at most 1024); *total gets
+// the block's sum.  Every thread of the block calls it.
+__device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int t = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane < nw) warp_sums[lane] = t;
+  }
+  __syncthreads();
+  const int before = (w > 0 ? warp_sums[w - 1] : 0) + x - v;
+  *total = warp_sums[nw - 1];
+  __syncthreads();
+  return before;
+}
+
+// The step's items with prompt chunks (needle_opts.sched_chunk).  Micro-batch k owns slots
+// [k * slots_per_part, ...) and item rows [k * items_per_part, ...): its selecting items first
+// (the last prompt position and every decode step), then its prefilling slots' items.  Each busy
+// slot gets one item; a prefilling slot may take up to chunk_max consecutive prompt positions as a
+// chunk -- never its last prompt position (that one selects) nor past its KV window (sink 0 here:
+// positions beyond `window` would overwrite ring entries an earlier item of the chunk still reads)
+// -- while the micro-batch's rows last, in slot order.  One CTA, one thread per slot (n_slots <= 1024).
+__global__ void __launch_bounds__(1024) k_sched_chunked(const SlotView sv, const StepView st, const SchedView q,
+                                                      int32_t* counts, int slots_per_part, int items_per_part,
+                                                      int parts, int chunk_max, int window) {
+  __shared__ int warp_sums[32];
+  __shared__ int first_sel[kMaxMicro + 1], first_extra[kMaxMicro + 1], first_rows[kMaxMicro + 1];
+  __shared__ int n_sel[kMaxMicro], n_pre[kMaxMicro], n_rows[kMaxMicro];
+  const int s = threadIdx.x;
+  const bool live = s < q.n_slots;
+  const int part = live ? s / slots_per_part : 0;
+  if (s < kMaxMicro) {
+    n_sel[s] = 0;
+    n_pre[s] = 0;
+    n_rows[s] = 0;
+  }
+  __syncthreads();
+  SeqState seq{};
+  if (live) seq = sv.seq[s];
+  const bool busy = live && seq.busy;
+  const bool sel = busy && seq.position >= seq.prompt_len - 1;
+  const bool pre = busy && !sel;
+  int want = 1;
+  if (pre) {
+    want = min(chunk_max, seq.prompt_len - 1 - seq.position);
+    if (window > 0) want = min(want, window - seq.position);
+    want = max(want, 1);
+  }
+  if (sel) atomicAdd(&n_sel[part], 1);
+  if (pre) atomicAdd(&n_pre[part], 1);
+  int total;
+  const int sel_before = block_exclusive_scan(sel ? 1 : 0, warp_sums, &total);
+  const int extra_before = block_exclusive_scan(pre ? want - 1 : 0, warp_sums, &total);
+  // the scans' values at each micro-batch's first slot
+  if (live && s % slots_per_part == 0) {
+    first_sel[part] = sel_before;
+    first_extra[part] = extra_before;
+  }
+  __syncthreads();
+  const int budget = items_per_part - n_sel[part] - n_pre[part];
+  const int extra_in_part = extra_before - first_extra[part];
+  const int grant = pre ? max(0, min(want - 1, budget - extra_in_part)) : 0;
+  const int rows = pre ? 1 + grant : 0;
+  const int rows_before = block_exclusive_scan(rows, warp_sums, &total);
+  if (live && s % slots_per_part == 0) first_rows[part] = rows_before;
+  if (pre) atomicAdd(&n_rows[part], rows);
+  __syncthreads();
+  const int base = part * items_per_part;
+  if (sel) {
+    const int idx = base + sel_before - first_sel[part];
+    DevItem it;
+    it.slot = s;
+    it.token = seq.position < seq.prompt_len ? q.prompt_ids[seq.prompt_off + seq.position] : -1;
+    it.select = 1;
+    it.allowed_count = -1;
+    it.allowed_offset = 0;
+    it.position = seq.position;
+    it.out_index = idx;
+    it.flags = 0;
+    it.chunk_index = 0;
+    it.chunk_len = 0;
+    st.items[idx] = it;
+  } else if (pre) {
+    const int first = base + n_sel[part] + rows_before - first_rows[part];
+    for (int j = 0; j < rows; j++) {
+      DevItem it;
+      it.slot = s;
+      it.token = q.prompt_ids[seq.prompt_off + seq.position + j];
+      it.select = 0;
+      it.allowed_count = -1;
+      it.allowed_offset = 0;
+      it.position = seq.position + j;
+      it.out_index = first + j;
+      it.flags = 0;
+      it.chunk_index = rows > 1 ? j : 0;
+      it.chunk_len = rows > 1 ? rows : 0;
+      st.items[first + j] = it;
+    }
+  }
+  if (s == 0) {
+    int all = 0, all_sel = 0;
+    for (int k = 0; k < parts; k++) {
+      counts[2 + 2 * k] = n_sel[k] + n_rows[k];
+      counts[3 + 2 * k] = n_sel[k];
+      all += n_sel[k] + n_rows[k];
+      all_sel += n_sel[k];
+    }
+    counts[0] = all;
+    counts[1] = all_sel;
   }
 }
 
@@ -1416,6 +1552,14 @@ cudaError_t launch_sched(const SlotView& sv, const StepView& st, const SchedView
                          int parts, cudaStream_t s) {
   if (parts < 1 || parts > kMaxMicro) return cudaErrorInvalidValue;
   k_sched<<<1, 1024, 0, s>>>(sv, st, q, counts, part, parts);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sched_chunked(const SlotView& sv, const StepView& st, const SchedView& q, int32_t* counts,
+                                 int slots_per_part, int items_per_part, int parts, int chunk_max, int window,
+                                 cudaStream_t s) {
+  if (q.n_slots > 1024 || parts > kMaxMicro) return cudaErrorInvalidValue;
+  k_sched_chunked<<<1, 1024, 0, s>>>(sv, st, q, counts, slots_per_part, items_per_part, parts, chunk_max, window);
   return cudaGetLastError();
 }
 

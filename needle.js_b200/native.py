@@ -39,7 +39,8 @@ class NeedleError(RuntimeError):
 class Opts(C.Structure):
     _fields_ = [("struct_size", C.c_uint32), ("device", C.c_int32), ("max_seqs", C.c_int32),
                 ("max_len", C.c_int32), ("max_sink", C.c_int32), ("kv_mode", C.c_int32),
-                ("numerics", C.c_int32), ("micro_batches", C.c_int32), ("reserved", C.c_int32 * 8)]
+                ("numerics", C.c_int32), ("micro_batches", C.c_int32), ("sched_chunk", C.c_int32),
+                ("sched_items", C.c_int32), ("reserved", C.c_int32 * 6)]
 
 
 class Geometry(C.Structure):

@@ -9,6 +9,11 @@ the window among the first admissions, and the shortest admitted into reused slo
 the oracle's one-sequence decode (NeedleModel.generate's greedy loop, packages/needle.js/src/model/
 model.ts:88-153; window and slots as runtime.ts:659-786), and a running slot's int8 K/V codes and
 scales, every layer, must equal the oracle runtime's after the same tokens.
+
+The same run again with prompt chunks (needle_opts.sched_chunk = 16, 512 items per step): slots
+still reading their prompts take up to 16 positions per step as a chunk of items beside the other
+slots' single items, until their window would wrap.  The reference reads a prompt one token at a
+time (runtime.ts:227-243), so the streams and the K/V must not change.
 """
 import concurrent.futures
 import os
@@ -22,8 +27,9 @@ STEPS = 600
 SLOTS = 256
 
 
-@pytest.fixture(scope="module")
-def run(oracle):
+@pytest.fixture(scope="module", params=[{}, {"sched_chunk": 16, "sched_items": 512}],
+                ids=["one-position", "prompt-chunks"])
+def run(oracle, request):
     torch = pytest.importorskip("torch")
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
@@ -34,7 +40,8 @@ def run(oracle):
     needle_b200.build.build()
     archive = synth.build_archive(0)
     prompts, gens = bench.workload(0, SLOTS * 12)
-    with CudaEngine(archive, device=0, max_seqs=SLOTS, max_len=bench.PROMPT[1] + bench.GEN[1], max_sink=0) as eng:
+    with CudaEngine(archive, device=0, max_seqs=SLOTS, max_len=bench.PROMPT[1] + bench.GEN[1], max_sink=0,
+                    **request.param) as eng:
         eng.sched_load(SLOTS, prompts, gens)
         eng.sched_step(1)       # eager
         eng.sched_step(STEPS - 1)  # captured once, then replayed
@@ -48,7 +55,8 @@ def run(oracle):
         kv = [eng.read_kv(slot, layer) for layer in range(eng.layers)]
     offs = np.concatenate([[0], np.cumsum(gens)]).astype(np.int64)
     yield dict(prompts=prompts, gens=gens, tokens=tokens, generated=generated, finished=finished, last=last,
-               ids=ids, offs=offs, kv_slot=(slot, sid, pos, kv), model=oracle.Model(archive))
+               ids=ids, offs=offs, kv_slot=(slot, sid, pos, kv), model=oracle.Model(archive),
+               chunks=bool(request.param))
 
 
 def _stream(r, i):
@@ -66,7 +74,10 @@ def test_counters_and_finished_streams_are_complete(run):
         assert np.all(s >= 0) and s[-1] == run["last"][i]
     assert run["generated"] == int(np.sum(run["ids"] >= 0))
     assert any(i >= SLOTS for i in done), "no sequence finished in a reused slot"
-    assert run["tokens"] == STEPS * SLOTS  # every slot stays busy: the queue is far from empty
+    if run["chunks"]:  # prompt chunks: more than one position per slot and step while prompts last
+        assert run["tokens"] > STEPS * SLOTS
+    else:
+        assert run["tokens"] == STEPS * SLOTS  # every slot stays busy: the queue is far from empty
 
 
 def test_finished_id_streams_match_oracle(run):
