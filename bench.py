@@ -41,9 +41,14 @@ import __graft_entry__  # noqa: E402  (registers the needle.js_b200/ package as 
 
 __graft_entry__.load()
 
-# DRAM bytes of one 256-item k_attention launch in the benchmarked state (set from the committed
-# steady-state capture; None until one exists)
-ATTENTION_TRAFFIC_BYTES = 30582272
+# DRAM bytes (read + write) per timed launch of a kernel class in the benchmarked state, from the
+# committed steady-state captures (ncu, one pass), with the sched_chunk they were taken at.  With
+# prompt chunks an attention "launch" is the pair of launches of one layer (chunk append, attend).
+STEADY_TRAFFIC = {
+    "attention": {"bytes": 1054208 + 35696640, "sched_chunk": 8,
+                  "source": "profiles/attention_exact_decode_step_steady_state.md"},
+    "layer": {"bytes": 5684224, "sched_chunk": 8, "source": "profiles/layer_exact_decode_step_steady_state.md"},
+}
 SLOTS = 256
 PROMPT = (32, 1024)
 GEN = (16, 128)
@@ -164,10 +169,37 @@ FP64_LANES_PER_SM = 64
 SMS = 148
 
 
-def roofline_for(prof, n_items, peaks, visible=None, sm_mhz=None):
-    """Roofline of the kernel class with the largest share of step time.  `visible` is the number of
-    visible KV positions summed over the step's items (from the slots' positions), else full
-    256-position windows are assumed."""
+def visible_positions(slots, prompts, chunk, items, steps, window=256):
+    """(visible, distinct) KV positions per step over the next `steps` scheduled steps, from the
+    slots' (sequence, position, busy): visible summed over the step's items, distinct counted once per
+    slot (a chunk's items read one window).  One item per busy slot, or, with prompt chunks, up to
+    `chunk` prompt positions of a prefilling slot (never its last, never past the window) while the
+    step's `items` last, in slot order (admissions and retirements in between are ignored)."""
+    pos = {k: p for k, (sid, p, busy) in enumerate(slots) if busy}
+    plen = {k: len(prompts[slots[k][0]]) for k in pos}
+    total = distinct = 0
+    for _ in range(steps):
+        budget = (items if chunk >= 2 else len(pos)) - len(pos)
+        for k in sorted(pos):
+            p = pos[k]
+            n = 1
+            if chunk >= 2 and p < plen[k] - 1:
+                want = max(1, min(chunk, plen[k] - 1 - p, window - p))
+                n = 1 + max(0, min(want - 1, budget))
+                budget -= n - 1
+            total += sum(min(q + 1, window) for q in range(p, p + n))
+            distinct += min(p + n, window + n - 1)
+            pos[k] = p + n
+    return total / steps, distinct / steps
+
+
+def roofline_for(prof, n_items, peaks, visible=None, sm_mhz=None, state_chunk=None, unique=None):
+    """Roofline of the kernel class with the largest share of step time.  `n_items` is the items of
+    one launch, `visible` the number of visible KV positions summed over them (from the slots'
+    positions), else full 256-position windows are assumed; `unique` the distinct KV positions among
+    them (the items of one chunk share their slot's window), else `visible`.  `state_chunk`: the
+    sched_chunk of a config-4 run, whose committed steady-state DRAM capture then applies (None: no
+    capture applies)."""
     cls, (ms, launches) = max(prof.items(), key=lambda kv: kv[1][0])
     per_launch_ms = ms / max(launches, 1)
     # algorithmic bytes per launch: the bytes the kernel must touch once per item (KV rows of the
@@ -176,12 +208,13 @@ def roofline_for(prof, n_items, peaks, visible=None, sm_mhz=None):
     weights = {"gemv_qkvg": (512 + 256 + 256 + 512) * (128 + 8), "gemv_o": 512 * (192 + 8),
                "gemv_vocab": 8192 * (256 + 8)}
     positions = visible if visible is not None else n_items * 256
+    distinct = unique if unique is not None else positions
     fp64_ops = None
     if cls == "layer":
         per_item = 2 * 2048 * 4 + 24 * (1024 + 32) + 5 * 2048 + 80 * 2
         bytes_ = n_items * per_item + 12 * 2048
     elif cls == "attention":
-        bytes_ = 4 * positions * kv_row + n_items * (1536 * 4 + 512 * 4)
+        bytes_ = 4 * distinct * kv_row + n_items * (1536 * 4 + 512 * 4)
         fp64_ops = FP64_OPS_ATTENTION * 8 * 64 * positions  # 8 query heads x 64 elements
     elif cls in weights:
         ins = {"gemv_qkvg": (512, 1536), "gemv_o": (512, 512), "gemv_vocab": (512, 8192)}[cls]
@@ -195,15 +228,18 @@ def roofline_for(prof, n_items, peaks, visible=None, sm_mhz=None):
     # DRAM bytes (read + write) of one launch of the kernel in the benchmarked state (ncu, 1 pass,
     # bench.py --steps 20 --warmup 5 --no-cpu-baseline --e2e-steps 2 --no-fast: the first
     # 256-item launches after the ramp; profiles/attention_exact_decode_step_steady_state.md)
-    traffic = {"attention": ATTENTION_TRAFFIC_BYTES}
+    t = STEADY_TRAFFIC.get(cls)
+    if t is not None and (state_chunk is None or max(state_chunk, 1) != max(t["sched_chunk"], 1)):
+        t = None
     line = {"kernel": cls, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_source": src,
             "unit": "GB/s", "frac": round(achieved / peak, 4),
-            "traffic": traffic.get(cls) if n_items == 256 else None,
+            "traffic": t["bytes"] if t else None,
             "launch_ms": round(per_launch_ms, 5), "algorithmic_bytes_per_launch": int(bytes_)}
-    if line["traffic"] is not None:
-        line["traffic_source"] = "profiles/attention_exact_decode_step_steady_state.md"
+    if t:
+        line["traffic_source"] = t["source"]
     if visible is not None:
         line["visible_positions_per_launch"] = int(visible)
+        line["distinct_kv_positions_per_launch"] = int(distinct)
     if fp64_ops is not None:
         mhz = sm_mhz or 1965.0
         fpeak = SMS * FP64_LANES_PER_SM * mhz * 1e6
@@ -833,6 +869,9 @@ def main():
     ap.add_argument("--new-tokens", type=int, default=64, help="single: greedy tokens")
     ap.add_argument("--sequences", type=int, default=4096, help="toolcall: sequences over all GPUs")
     ap.add_argument("--slots", type=int, default=512, help="toolcall: engine slots per GPU")
+    ap.add_argument("--sched-chunk", type=int, default=8,
+                    help="decode: prompt positions a prefilling slot may take per scheduled step (0: one)")
+    ap.add_argument("--sched-items", type=int, default=384, help="decode: items per scheduled step with chunks")
     ap.add_argument("--mask-cache", type=int, default=4096,
                     help="toolcall: allowed masks cached per grammar state in a device pool of this many "
                          "slots (0: id lists per step)")
@@ -858,7 +897,12 @@ def main():
               "numerics": "exact (binary64 in reference order; tokens and int8 KV bit-identical to the CPU backend)",
               "kv_cache": "int8", "l2": "inputs larger than L2: the per-step KV working set is ~1 GB; the 13.7 MB "
                                         "of CQ weights stay L2-resident as in deployment",
-              "parallelism": f"dp{args.gpus} (independent sequences per GPU, no collectives)"}
+              "parallelism": f"dp{args.gpus} (independent sequences per GPU, no collectives)",
+              "prompt_chunks": ({"sched_chunk": args.sched_chunk, "sched_items": args.sched_items,
+                                 "note": "a slot still reading its prompt takes up to sched_chunk positions per "
+                                         "step (until its KV window would wrap) beside the other slots' single "
+                                         "items, at most sched_items items per step; the same ids and KV"}
+                                if args.sched_chunk >= 2 else "one position per slot and step")}
     metric, unit = "decode tokens/s", "tokens/s"
 
     if args.workload == "single" and args.impl == "cuda":
@@ -920,7 +964,8 @@ def main():
 
     n_seqs = SLOTS * 12
     prompts, gens = workload(rank, n_seqs)
-    eng = CudaEngine(archive, device=device, max_seqs=SLOTS, max_len=PROMPT[1] + GEN[1], max_sink=0)
+    chunking = dict(sched_chunk=args.sched_chunk, sched_items=args.sched_items if args.sched_chunk >= 2 else 0)
+    eng = CudaEngine(archive, device=device, max_seqs=SLOTS, max_len=PROMPT[1] + GEN[1], max_sink=0, **chunking)
     stream = torch.cuda.ExternalStream(eng.stream, device=device)
 
     # ---------------- device-resident run
@@ -950,11 +995,13 @@ def main():
     # per-kernel-class timing (events around every launch) for the roofline, after the timed run;
     # the visible KV positions of the profiled steps from the slots' positions (window 256, sink 0)
     slots = [eng.sched_slot(k) for k in range(SLOTS)]
-    visible = sum(min(pos + 1 + k, 256) for (_, pos, busy) in slots if busy for k in range(10)) / 10.0
+    visible, unique = visible_positions(slots, prompts, args.sched_chunk, args.sched_items, 10)
+    pp0 = eng.sched_status()[0]
     eng.profile(True)
     eng.sched_step(10)
     prof = {k: v for k, v in eng.profile_read().items() if v[1] > 0}
     eng.profile(False)
+    items_per_launch = (eng.sched_status()[0] - pp0) / 10.0  # profiling runs one micro-batch per step
 
     # ---------------- end-to-end through the host C-ABI step
     e2e_steps = args.e2e_steps or max(20, min(args.steps, 100))
@@ -969,7 +1016,7 @@ def main():
     fast = None
     if not args.no_fast:
         feng = CudaEngine(archive, device=device, max_seqs=SLOTS, max_len=PROMPT[1] + GEN[1], max_sink=0,
-                          numerics="fast")
+                          numerics="fast", **chunking)
         fstream = torch.cuda.ExternalStream(feng.stream, device=device)
         feng.sched_load(SLOTS, prompts, gens)
         feng.sched_step(args.ramp + args.warmup)
@@ -1014,8 +1061,9 @@ def main():
                 "e2e": {"value": round(e2e_gen / (e2e_ms / 1e3), 1), "unit": unit,
                         "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"], "steps": e2e_steps},
                 "gpu_launches": launches_all,
-                "roofline": roofline_for(prof, SLOTS, peaks, visible=visible,
-                                         sm_mhz=(clocks or {}).get("sm_mhz")),
+                "roofline": roofline_for(prof, items_per_launch, peaks, visible=visible,
+                                         sm_mhz=(clocks or {}).get("sm_mhz"),
+                                         state_chunk=args.sched_chunk, unique=unique),
                 "kernel_ms_per_step": {k: round(v[0] / 10, 4) for k, v in prof.items()},
                 "kernel_ms_per_step_note": "event-timed per launch with the micro-batches run one after another "
                                            "(their sum exceeds ms_per_step, where they overlap)",
