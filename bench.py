@@ -1007,6 +1007,9 @@ def main():
     e2e_steps = args.e2e_steps or max(20, min(args.steps, 100))
     e2e = host_driven(eng, stream, prompts, gens, args.ramp, args.warmup, e2e_steps)
 
+    if world > 1:  # this rank's own figures (stderr: stdout carries rank 0's one line)
+        print(json.dumps({"rank": rank, "device": device, "ms": round(ms, 3), "generated": int(gen_tokens),
+                          "processed": int(processed), "e2e_ms": round(e2e["ms"], 3)}), file=sys.stderr, flush=True)
     ms_max, gen_all, proc_all, e2e_ms, e2e_gen, launches_all = aggregate(
         [ms, gen_tokens, processed, e2e["ms"], e2e["generated"], launches], dist)
     eng.close()
