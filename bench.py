@@ -1005,7 +1005,8 @@ def main():
 
     # ---------------- end-to-end through the host C-ABI step
     e2e_steps = args.e2e_steps or max(20, min(args.steps, 100))
-    e2e = host_driven(eng, stream, prompts, gens, args.ramp, args.warmup, e2e_steps)
+    e2e = host_driven(eng, stream, prompts, gens, args.ramp, args.warmup, e2e_steps, args.sched_chunk,
+                      args.sched_items)
 
     if world > 1:  # this rank's own figures (stderr: stdout carries rank 0's one line)
         print(json.dumps({"rank": rank, "device": device, "ms": round(ms, 3), "generated": int(gen_tokens),
@@ -1103,8 +1104,11 @@ def gemm_roofline(prof, n_items, peaks):
             "frac": round(tflops / peak, 5), "gemm_ms_per_step": round(ms, 4), "flops_per_step": flops}
 
 
-def host_driven(eng, stream, prompts, gens, ramp, warmup, steps):
-    """Continuous batching driven from the host through needle_cuda_step (host buffers)."""
+def host_driven(eng, stream, prompts, gens, ramp, warmup, steps, chunk=0, items=0):
+    """Continuous batching driven from the host through needle_cuda_step (host buffers).  With
+    `chunk` >= 2 a slot still reading its prompt sends up to `chunk` prompt positions as consecutive
+    items (a prompt chunk: never its last position, never past the 256-position window), at most
+    `items` items per step, in slot order, as the device scheduler does."""
     import torch
     from needle_b200.backend import StepRequest
     n_slots = eng.max_seqs
@@ -1123,6 +1127,7 @@ def host_driven(eng, stream, prompts, gens, ramp, warmup, steps):
     def one_step():
         admit()
         reqs = []
+        budget = items - sum(1 for st in state if st is not None) if chunk >= 2 else 0
         for s in range(n_slots):
             st = state[s]
             if st is None:
@@ -1130,6 +1135,14 @@ def host_driven(eng, stream, prompts, gens, ramp, warmup, steps):
             q, pos, done = st
             p = prompts[q]
             sel = pos >= len(p) - 1
+            n = 1
+            if chunk >= 2 and not sel:
+                want = max(1, min(chunk, len(p) - 1 - pos, 256 - pos))
+                n = 1 + max(0, min(want - 1, budget))
+                budget -= n - 1
+            if n > 1:
+                reqs.extend(StepRequest(s, int(p[pos + j]), False) for j in range(n))
+                continue
             tok = int(p[pos]) if pos < len(p) else -1
             reqs.append(StepRequest(s, tok, sel))
         if not reqs:

@@ -89,7 +89,11 @@ typedef struct needle_geometry {
   int32_t kv_capacity; /* KV slots per sequence allocated by this context */
 } needle_geometry;
 
-/* One sequence's work in a batched step (NeedleRuntime.step / stepSelected, runtime.ts:257-583). */
+/* One sequence's work in a batched step (NeedleRuntime.step / stepSelected, runtime.ts:257-583).  A
+ * slot appears once per step, or as a prompt chunk: consecutive items of the slot with their tokens
+ * (no NEEDLE_TOKEN_PENDING), none selecting, for positions p, p + 1, ... -- the same result as that
+ * many one-token steps (runtime.ts:227-243), provided the chunk does not reach past the slot's KV
+ * window (INVALID_CACT otherwise) and no slot of the context collects confidence. */
 typedef struct needle_step_item {
   int32_t seq;            /* slot in [0, max_seqs) prepared with needle_cuda_seq_reset */
   int32_t token;          /* token consumed at the slot's current position;

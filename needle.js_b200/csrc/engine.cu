@@ -342,6 +342,7 @@ struct needle_ctx {
   int micro = 4;  // micro-batches of a device-scheduled step (needle_opts.micro_batches)
   int sched_chunk = 0;  // prompt positions per slot and scheduled step (needle_opts.sched_chunk; 0: one)
   int sched_items = 0;  // items a scheduled step with chunks may hold (needle_opts.sched_items)
+  int step_capacity = 0;  // items one step's buffers hold
   // The device-scheduled step captured as a CUDA graph after one eager step.
   cudaGraphExec_t sched_graph = nullptr;
   int64_t graph_launches = 0;
@@ -724,6 +725,7 @@ void build_state(needle_ctx& C) {
   StepView& st = C.stv;
   // scheduled steps with chunks use item rows up to ceil(sched_items / M) * M < sched_items + kMaxMicro
   const size_t B = size_t(std::max({S, kPrefillChunk, C.sched_items > 0 ? C.sched_items + kMaxMicro : 0}));
+  C.step_capacity = int(B);
   st.items = C.dalloc<DevItem>(B);
   st.chunk = 0;
   st.lanes = C.dalloc<float>(B * kLaneWidth);
@@ -1122,20 +1124,42 @@ void check_allowed(const needle_ctx& C, const needle_step_item& it, const uint32
 
 // Validates the items of a step (allowed lists too when `allowed` is set); returns the number that
 // select.
+// A slot's items in one step are one item, or a prompt chunk: consecutive items with given tokens,
+// none selecting (positions p, p + 1, ...; the slot advances past all of them).  Returns the number
+// of selecting items; *chunks is set when the step holds a chunk.
 int check_items(needle_ctx& C, const needle_step_item* items, int32_t n, bool allowed, const uint32_t* allowed_ids,
-                size_t allowed_total, bool have_selected) {
-  require(n >= 0 && n <= C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "item count out of range");
+                size_t allowed_total, bool have_selected, bool* chunks = nullptr) {
+  require(n >= 0 && n <= C.step_capacity, NEEDLE_BACKEND_UNAVAILABLE, "item count out of range");
   require(n == 0 || items != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null items");
   std::vector<char> seen(C.opts.max_seqs, 0);
   const int V = C.mv.vocab;
   int n_sel = 0;
+  bool any_chunk = false;
   for (int i = 0; i < n; i++) {
     const needle_step_item& it = items[i];
     require(it.seq >= 0 && it.seq < C.opts.max_seqs, NEEDLE_BACKEND_UNAVAILABLE, "sequence slot out of range");
-    require(!seen[it.seq], NEEDLE_BACKEND_UNAVAILABLE, "a slot appears twice in one step");
+    const bool cont = i > 0 && items[i - 1].seq == it.seq;
+    require(cont || !seen[it.seq], NEEDLE_BACKEND_UNAVAILABLE,
+            "a slot appears twice in one step (a prompt chunk's items must be consecutive)");
     seen[it.seq] = 1;
     const SlotHost& h = C.slots[it.seq];
     require(h.ready, NEEDLE_INVALID_CACT, "Call runtime.reset() before decoding");
+    if (cont || (i + 1 < n && items[i + 1].seq == it.seq)) {  // an item of a prompt chunk
+      any_chunk = true;
+      require(!it.select && it.token >= 0, NEEDLE_INVALID_CACT,
+              "a prompt chunk's items carry their tokens and do not select");
+      if (!cont) {
+        int k = 1;
+        while (i + k < n && items[i + k].seq == it.seq) k++;
+        if (h.position + k > h.max_len)
+          fail(NEEDLE_CONTEXT_OVERFLOW, "Position " + std::to_string(h.position + k) + " exceeds runtime limit " +
+                                            std::to_string(h.max_len));
+        require(C.mv.kv_window == 0 || h.position + k <= h.sink + C.mv.kv_window, NEEDLE_INVALID_CACT,
+                "a prompt chunk may not reach past the KV window");
+        require(C.collecting == 0, NEEDLE_INVALID_CACT,
+                "prompt chunks are not taken while a slot collects confidence");
+      }
+    }
     // messages are built only on failure: this loop runs for every item of every step
     if (h.position >= h.max_len)
       fail(NEEDLE_CONTEXT_OVERFLOW,
@@ -1148,6 +1172,7 @@ int check_items(needle_ctx& C, const needle_step_item* items, int32_t n, bool al
       n_sel++;
     }
   }
+  if (chunks) *chunks = any_chunk;
   return n_sel;
 }
 
@@ -1157,10 +1182,16 @@ void stage_items(needle_ctx& C, const needle_step_item* items, int32_t n, int n_
                  std::vector<int>& order, DevItem* dst) {
   int pos_sel = 0, pos_rest = all_logits ? 0 : n_sel;
   order.resize(n);
+  int run_start = 0, run_len = 1;  // the prompt chunk (or single item) item i belongs to
   for (int i = 0; i < n; i++) {
     const needle_step_item& it = items[i];
+    if (i == 0 || items[i - 1].seq != it.seq) {
+      run_start = i;
+      run_len = 1;
+      while (i + run_len < n && items[i + run_len].seq == it.seq) run_len++;
+    }
     const bool first = all_logits || it.select;
-    const int k = all_logits ? pos_sel++ : (first ? pos_sel++ : pos_rest++);
+    const int k = all_logits ? pos_sel++ : (first ? pos_sel++ : pos_rest++);  // chunks stay in order
     order[i] = k;
     DevItem d{};
     d.slot = it.seq;
@@ -1168,8 +1199,12 @@ void stage_items(needle_ctx& C, const needle_step_item* items, int32_t n, int n_
     d.select = it.select ? 1 : 0;
     d.allowed_count = it.select ? it.allowed_count : -1;
     d.allowed_offset = it.allowed_offset;
-    d.position = C.slots[it.seq].position;
+    d.position = C.slots[it.seq].position + (i - run_start);
     d.out_index = i;
+    if (run_len > 1) {
+      d.chunk_index = i - run_start;
+      d.chunk_len = run_len;
+    }
     dst[k] = d;
   }
 }
@@ -1483,7 +1518,8 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, 
                      size_t allowed_total, needle_selected* out_selected, float* out_logits) {
   return guarded([&] {
     needle_ctx& C = *ctx_of(ctx);
-    const int n_sel = check_items(C, items, n, true, allowed_ids, allowed_total, out_selected != nullptr);
+    bool chunks = false;
+    const int n_sel = check_items(C, items, n, true, allowed_ids, allowed_total, out_selected != nullptr, &chunks);
     if (n == 0) return;
     const bool all_logits = out_logits != nullptr;
     std::vector<int> order;
@@ -1491,7 +1527,9 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, 
     upload_allowed(C, allowed_ids, allowed_total);
     const int rows = all_logits ? n : n_sel;
     upload_items(C, C.h_items, n, rows);
-    enqueue_step(C, C.stv, n, n_sel > 0 || all_logits, nullptr, lane_a(C));
+    StepView v = C.stv;
+    v.chunk = chunks ? 1 : 0;
+    enqueue_step(C, v, n, n_sel > 0 || all_logits, nullptr, lane_a(C));
     complete_step(C, items, n, rows, order, out_selected, out_logits);
   });
 }
@@ -1499,12 +1537,15 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, 
 int needle_cuda_step_begin(needle_ctx* ctx, const needle_step_item* items, int32_t n) {
   return guarded([&] {
     needle_ctx& C = *ctx_of(ctx);
-    const int n_sel = check_items(C, items, n, false, nullptr, 0, true);
+    bool chunks = false;
+    const int n_sel = check_items(C, items, n, false, nullptr, 0, true, &chunks);
     require(n > 0, NEEDLE_BACKEND_UNAVAILABLE, "a split step needs at least one item");
     auto& P = C.pending;
     stage_items(C, items, n, n_sel, false, P.order, C.h_items);
     upload_items(C, C.h_items, n, n_sel);
-    enqueue_step(C, C.stv, n, n_sel > 0, nullptr, lane_a(C), /*finish=*/false);
+    StepView v = C.stv;
+    v.chunk = chunks ? 1 : 0;
+    enqueue_step(C, v, n, n_sel > 0, nullptr, lane_a(C), /*finish=*/false);
     P.items.assign(items, items + n);
     P.n = n;
     P.n_sel = n_sel;

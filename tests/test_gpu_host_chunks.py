@@ -1,0 +1,94 @@
+"""Prompt chunks in host-driven steps (needle_cuda_step with consecutive items of one slot).
+
+A slot still reading its prompt may send several of its next prompt positions in one step, as
+consecutive items that carry their tokens and do not select; the slot advances past all of them.
+The reference reads a prompt one token per step (packages/needle.js/src/model/runtime.ts:227-243),
+so the same sequences driven with chunks and one position at a time must select the same ids and
+leave the same int8 K/V, bit for bit.  Chunks that select, that are not consecutive, or that
+would reach past the KV window are refused before anything runs.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def archive():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import needle_b200.build
+    needle_b200.build.build()
+    from needle_b200 import synth
+    return synth.build_archive(0)
+
+
+def _drive(eng, prompts, gens, chunk):
+    """Every slot s decodes prompts[s] then gens[s] greedy ids; returns the ids per slot."""
+    from needle_b200.backend import StepRequest
+    n = len(prompts)
+    for s in range(n):
+        eng.reset(s, len(prompts[s]) + gens[s] + 1, 0)
+    pos = [0] * n
+    ids = [[] for _ in range(n)]
+    while any(len(ids[s]) < gens[s] for s in range(n)):
+        reqs = []
+        for s in range(n):
+            if len(ids[s]) >= gens[s]:
+                continue
+            p = prompts[s]
+            if pos[s] < len(p) - 1:
+                k = min(chunk, len(p) - 1 - pos[s]) if chunk > 1 else 1
+                reqs.extend(StepRequest(s, int(p[pos[s] + j]), False) for j in range(k))
+            elif pos[s] == len(p) - 1:
+                reqs.append(StepRequest(s, int(p[-1]), True))
+            else:
+                reqs.append(StepRequest(s, -1, True))
+        out, _ = eng.step(reqs)
+        for r, o in zip(reqs, out):
+            pos[r.seq] += 1
+            if r.select:
+                ids[r.seq].append(int(o[0]))
+    return ids, pos
+
+
+def test_host_chunks_match_one_position_steps(archive):
+    from needle_b200.backend import CudaEngine
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, 8192, n).astype(np.int32) for n in (41, 10, 29, 3)]
+    gens = [6, 9, 4, 7]
+    results = []
+    for chunk in (1, 8):
+        with CudaEngine(archive, device=0, max_seqs=4, max_len=96, max_sink=0) as eng:
+            ids, pos = _drive(eng, prompts, gens, chunk)
+            kv = [[eng.read_kv(s, layer) for layer in (0, 13, eng.layers - 1)] for s in range(4)]
+            results.append((ids, pos, kv))
+    (ids_a, pos_a, kv_a), (ids_b, pos_b, kv_b) = results
+    assert ids_a == ids_b and pos_a == pos_b
+    for s in range(4):
+        for a, b in zip(kv_a[s], kv_b[s]):
+            for x, y in zip(a, b):
+                np.testing.assert_array_equal(x, y, err_msg=f"slot {s}")
+
+
+def test_host_chunks_refused(archive):
+    from needle_b200.backend import CudaEngine, StepRequest
+    from needle_b200.native import NeedleError
+    with CudaEngine(archive, device=0, max_seqs=2, max_len=300, max_sink=0) as eng:
+        eng.reset(0, 300, 0)
+        eng.reset(1, 300, 0)
+        with pytest.raises(NeedleError) as e:  # a chunk item that selects
+            eng.step([StepRequest(0, 5, False), StepRequest(0, 6, True)])
+        assert e.value.code == "INVALID_CACT"
+        with pytest.raises(NeedleError):  # a slot twice, not consecutively
+            eng.step([StepRequest(0, 5, False), StepRequest(1, 6, False), StepRequest(0, 7, False)])
+        with pytest.raises(NeedleError):  # a chunk item without its token
+            eng.step([StepRequest(0, 5, False), StepRequest(0, -1, False)])
+        assert eng.position(0) == 0 and eng.position(1) == 0  # nothing ran
+        eng.prefill(0, np.arange(250, dtype=np.int32) % 8192, want_logits=False)
+        with pytest.raises(NeedleError) as e:  # positions 250..257 would wrap the 256-position window
+            eng.step([StepRequest(0, 9, False) for _ in range(8)])
+        assert e.value.code == "INVALID_CACT"
+        eng.step([StepRequest(0, 9, False) for _ in range(6)])  # up to the window is fine
+        assert eng.position(0) == 256
