@@ -347,6 +347,10 @@ struct needle_ctx {
   cudaGraphExec_t sched_graph = nullptr;
   int64_t graph_launches = 0;
   int sched_eager_steps = 0;
+  // host steps as micro-batches (needle_cuda_step): the captured step and its shape
+  cudaGraphExec_t host_graph = nullptr;
+  int64_t host_graph_launches = 0;
+  int host_eager_steps = 0, host_m = 0, host_cap = 0;
   std::vector<uint8_t> bytes;  // archive copy (host)
   Archive A;
   Roles roles;
@@ -757,7 +761,7 @@ void build_state(needle_ctx& C) {
   cuda_check(cudaMallocHost(&C.h_items_end, B * sizeof(DevItem)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_lanes, kLaneWidth * sizeof(float)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_engram, 2 * kMaxTables * sizeof(uint32_t)), "cudaMallocHost");
-  cuda_check(cudaMallocHost(&C.h_counts, 4 * sizeof(int32_t)), "cudaMallocHost");
+  cuda_check(cudaMallocHost(&C.h_counts, (2 + 2 * kMaxMicro) * sizeof(int32_t)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_ids, B * sizeof(int32_t)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_logprob, B * sizeof(double)), "cudaMallocHost");
   cuda_check(configure_step_kernels(capacity), "cudaFuncSetAttribute");
@@ -1012,6 +1016,96 @@ void enqueue_sched_step(needle_ctx& C) {
   }
 }
 
+// Host steps of many items run as micro-batches, like device-scheduled steps: micro-batch k holds
+// item rows [k * cap, (k + 1) * cap) with its own device counts, its selecting items first, and a
+// slot's items (a prompt chunk) stay in one micro-batch.  Fills dst, order (item i's row) and
+// h_counts; false when the items do not fit that shape.
+bool stage_items_mb(needle_ctx& C, const needle_step_item* items, int32_t n, int M, int cap, std::vector<int>& order,
+                    DevItem* dst) {
+  std::vector<int> part(n);
+  const int target = (n + M - 1) / M;
+  int k = 0, fill = 0;
+  for (int i = 0; i < n;) {
+    int len = 1;
+    while (i + len < n && items[i + len].seq == items[i].seq) len++;
+    if (fill > 0 && (fill + len > cap || (fill >= target && k < M - 1))) {
+      k++;
+      fill = 0;
+    }
+    if (k >= M || len > cap) return false;
+    for (int j = 0; j < len; j++) part[i + j] = k;
+    fill += len;
+    i += len;
+  }
+  std::vector<int> n_sel(M, 0), n_all(M, 0);
+  for (int i = 0; i < n; i++) {
+    n_all[part[i]]++;
+    if (items[i].select) n_sel[part[i]]++;
+  }
+  std::vector<int> next_sel(M), next_rest(M);
+  for (int q = 0; q < M; q++) {
+    next_sel[q] = q * cap;
+    next_rest[q] = q * cap + n_sel[q];
+  }
+  order.resize(n);
+  int run_start = 0, run_len = 1;
+  for (int i = 0; i < n; i++) {
+    const needle_step_item& it = items[i];
+    if (i == 0 || items[i - 1].seq != it.seq) {
+      run_start = i;
+      run_len = 1;
+      while (i + run_len < n && items[i + run_len].seq == it.seq) run_len++;
+    }
+    const int row = it.select ? next_sel[part[i]]++ : next_rest[part[i]]++;
+    order[i] = row;
+    DevItem d{};
+    d.slot = it.seq;
+    d.token = it.token;
+    d.select = it.select ? 1 : 0;
+    d.allowed_count = it.select ? it.allowed_count : -1;
+    d.allowed_offset = it.allowed_offset;
+    d.position = C.slots[it.seq].position + (i - run_start);
+    d.out_index = i;
+    if (run_len > 1) {
+      d.chunk_index = i - run_start;
+      d.chunk_len = run_len;
+    }
+    dst[row] = d;
+  }
+  int sel_all = 0;
+  for (int q = 0; q < M; q++) {
+    C.h_counts[2 + 2 * q] = n_all[q];
+    C.h_counts[3 + 2 * q] = n_sel[q];
+    sel_all += n_sel[q];
+  }
+  C.h_counts[0] = n;
+  C.h_counts[1] = sel_all;
+  return true;
+}
+
+// The kernels of a micro-batched host step (every micro-batch sized `cap` rows; the device counts
+// say how many each holds), forked from and joined back to the context stream.
+void enqueue_host_mb(needle_ctx& C, int M, int cap) {
+  cuda_check(cudaEventRecord(C.split_ev, C.stream), "split");
+  for (int k = 1; k < M; k++) cuda_check(cudaStreamWaitEvent(C.mb_main[k], C.split_ev, 0), "split");
+  for (int k = 0; k < M; k++) {
+    StepView v = half_view(C, k * cap, C.d_counts + 2 + 2 * k, C.d_counts + 3 + 2 * k);
+    v.chunk = 1;
+    enqueue_step(C, v, cap, true, nullptr, lane_k(C, k));
+  }
+  for (int k = 1; k < M; k++) {
+    cuda_check(cudaEventRecord(C.mb_done[k], C.mb_main[k]), "merge");
+    cuda_check(cudaStreamWaitEvent(C.stream, C.mb_done[k], 0), "merge");
+  }
+}
+
+// Drops the captured host step (its kernels hold buffer addresses that are about to change).
+void drop_host_graph(needle_ctx& C) {
+  if (C.host_graph) cudaGraphExecDestroy(C.host_graph);
+  C.host_graph = nullptr;
+  C.host_eager_steps = 0;
+}
+
 // The context of every call except needle_cuda_step_end and needle_cuda_close: none may run while a
 // step begun by needle_cuda_step_begin is waiting for its end.
 needle_ctx* ctx_of(needle_ctx* c) {
@@ -1054,6 +1148,7 @@ void destroy(needle_ctx* C) {
     if (C->join_ev[k]) cudaEventDestroy(C->join_ev[k]);
   }
   if (C->sched_graph) cudaGraphExecDestroy(C->sched_graph);
+  if (C->host_graph) cudaGraphExecDestroy(C->host_graph);
   if (C->split_ev) cudaEventDestroy(C->split_ev);
   for (int k = 1; k < kMaxMicro; k++) {
     for (int j = 0; j < 2; j++) {
@@ -1212,6 +1307,7 @@ void stage_items(needle_ctx& C, const needle_step_item* items, int32_t n, int n_
 void upload_allowed(needle_ctx& C, const uint32_t* allowed_ids, size_t allowed_total) {
   if (allowed_total == 0 || !allowed_ids) return;
   if (allowed_total > C.allowed_cap) {
+    drop_host_graph(C);
     uint32_t* p = nullptr;
     cuda_check(cudaMalloc(&p, allowed_total * 4), "cudaMalloc");
     C.allocs.push_back(p);
@@ -1523,6 +1619,54 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, 
     if (n == 0) return;
     const bool all_logits = out_logits != nullptr;
     std::vector<int> order;
+    // Many items: micro-batches on their own stream pairs, the step replayed as a CUDA graph after
+    // its first (eager) run, as device-scheduled steps are.
+    if (!all_logits && C.collecting == 0 && !C.profiling && C.micro >= 2 && n >= 64) {
+      const int M = C.micro, cap = C.step_capacity / C.micro;
+      if (stage_items_mb(C, items, n, M, cap, order, C.h_items)) {
+        upload_allowed(C, allowed_ids, allowed_total);
+        if (C.host_m != M || C.host_cap != cap) {
+          drop_host_graph(C);
+          C.host_m = M;
+          C.host_cap = cap;
+        }
+        C.timed(P_COPY, [&] {
+          cudaError_t e = cudaMemcpyAsync(C.stv.items, C.h_items, size_t(M) * cap * sizeof(DevItem),
+                                          cudaMemcpyHostToDevice, C.stream);
+          if (e != cudaSuccess) return e;
+          return cudaMemcpyAsync(C.d_counts, C.h_counts, size_t(2 + 2 * M) * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                 C.stream);
+        });
+        if (C.host_eager_steps < 1) {
+          enqueue_host_mb(C, M, cap);
+          C.host_eager_steps++;
+        } else {
+          if (!C.host_graph) {
+            cuda_check(cudaStreamBeginCapture(C.stream, cudaStreamCaptureModeThreadLocal), "capture");
+            const int64_t l0 = C.launches;
+            try {
+              enqueue_host_mb(C, M, cap);
+            } catch (...) {
+              cudaGraph_t broken = nullptr;
+              cudaStreamEndCapture(C.stream, &broken);
+              if (broken) cudaGraphDestroy(broken);
+              throw;
+            }
+            C.host_graph_launches = C.launches - l0;
+            C.launches = l0;
+            cudaGraph_t g = nullptr;
+            cuda_check(cudaStreamEndCapture(C.stream, &g), "capture");
+            const cudaError_t e = cudaGraphInstantiate(&C.host_graph, g, 0);
+            cudaGraphDestroy(g);
+            cuda_check(e, "cudaGraphInstantiate");
+          }
+          cuda_check(cudaGraphLaunch(C.host_graph, C.stream), "cudaGraphLaunch");
+          C.launches += C.host_graph_launches;
+        }
+        complete_step(C, items, n, M * cap, order, out_selected, nullptr);
+        return;
+      }
+    }
     stage_items(C, items, n, n_sel, all_logits, order, C.h_items);
     upload_allowed(C, allowed_ids, allowed_total);
     const int rows = all_logits ? n : n_sel;
@@ -1563,6 +1707,7 @@ int needle_cuda_mask_pool(needle_ctx* ctx, int32_t capacity) {
     require(!C.pending.active, NEEDLE_BACKEND_UNAVAILABLE, "a begun step is pending");
     cuda_check(cudaSetDevice(C.device), "cudaSetDevice");
     cuda_check(cudaStreamSynchronize(C.stream), "cudaStreamSynchronize");
+    drop_host_graph(C);
     if (C.d_masks) cudaFree(C.d_masks);
     if (C.d_mask_stage) cudaFree(C.d_mask_stage);
     if (C.h_mask_stage) cudaFreeHost(C.h_mask_stage);

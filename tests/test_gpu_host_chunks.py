@@ -92,3 +92,52 @@ def test_host_chunks_refused(archive):
         assert e.value.code == "INVALID_CACT"
         eng.step([StepRequest(0, 9, False) for _ in range(6)])  # up to the window is fine
         assert eng.position(0) == 256
+
+
+def test_many_items_run_as_micro_batches(archive):
+    """A host step of 64 items or more runs as micro-batches (replayed as a CUDA graph from its
+    second step on): the same ids and K/V as one batch, with chunks, decode slots and slots that
+    finish and are reset in between."""
+    from needle_b200.backend import CudaEngine, StepRequest
+    rng = np.random.default_rng(12)
+    n_slots = 96
+    prompts = [rng.integers(0, 8192, int(n)).astype(np.int32) for n in rng.integers(2, 40, n_slots)]
+    gens = [int(g) for g in rng.integers(1, 6, n_slots)]
+    runs = []
+    for micro in (1, 4):
+        with CudaEngine(archive, device=0, max_seqs=n_slots, max_len=64, max_sink=0, micro_batches=micro,
+                        sched_chunk=8, sched_items=160) as eng:
+            for s in range(n_slots):
+                eng.reset(s, len(prompts[s]) + gens[s] + 1, 0)
+            pos, got, trace = [0] * n_slots, [[] for _ in range(n_slots)], []
+            for step in range(24):
+                reqs, budget = [], 160 - n_slots
+                for s in range(n_slots):
+                    p = prompts[s]
+                    if len(got[s]) >= gens[s]:  # finished: start over with the same prompt
+                        eng.reset(s, len(p) + gens[s] + 1, 0)
+                        pos[s], got[s] = 0, []
+                    if pos[s] < len(p) - 1:
+                        k = 1 + max(0, min(min(8, len(p) - 1 - pos[s]) - 1, budget))
+                        budget -= k - 1
+                        reqs.extend(StepRequest(s, int(p[pos[s] + j]), False) for j in range(k))
+                    else:
+                        reqs.append(StepRequest(s, int(p[-1]) if pos[s] == len(p) - 1 else -1, True))
+                assert len(reqs) >= 64
+                out, _ = eng.step(reqs)
+                sel = []
+                for r, o in zip(reqs, out):
+                    pos[r.seq] += 1
+                    if r.select:
+                        got[r.seq].append(int(o[0]))
+                        sel.append((r.seq, int(o[0]), o[1]))
+                trace.append(sel)
+            kv = [eng.read_kv(s, 0) for s in (0, 17, 95)]
+            runs.append((trace, pos, kv))
+    (ta, pa, ka), (tb, pb, kb) = runs
+    assert pa == pb
+    for step, (a, b) in enumerate(zip(ta, tb)):
+        assert a == b, f"step {step}"
+    for a, b in zip(ka, kb):
+        for x, y in zip(a, b):
+            np.testing.assert_array_equal(x, y)
