@@ -110,6 +110,7 @@ def test_many_items_run_as_micro_batches(archive):
             for s in range(n_slots):
                 eng.reset(s, len(prompts[s]) + gens[s] + 1, 0)
             pos, got, trace = [0] * n_slots, [[] for _ in range(n_slots)], []
+            l0 = eng.kernel_launches()
             for step in range(24):
                 reqs, budget = [], 160 - n_slots
                 for s in range(n_slots):
@@ -133,8 +134,9 @@ def test_many_items_run_as_micro_batches(archive):
                         sel.append((r.seq, int(o[0]), o[1]))
                 trace.append(sel)
             kv = [eng.read_kv(s, 0) for s in (0, 17, 95)]
-            runs.append((trace, pos, kv))
-    (ta, pa, ka), (tb, pb, kb) = runs
+            runs.append((trace, pos, kv, eng.kernel_launches() - l0))
+    (ta, pa, ka, la), (tb, pb, kb, lb) = runs
+    assert lb > 3 * la  # four micro-batches: the kernels of each launched per micro-batch
     assert pa == pb
     for step, (a, b) in enumerate(zip(ta, tb)):
         assert a == b, f"step {step}"
