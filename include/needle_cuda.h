@@ -154,12 +154,15 @@ int needle_cuda_confidence(const needle_ctx* ctx, int32_t seq, double* value);
 /* Position (tokens consumed) of a slot. */
 int needle_cuda_seq_position(const needle_ctx* ctx, int32_t seq, int32_t* position);
 
-/* One ragged batched decode step over n items (distinct slots).  For every item the slot's token
- * runs through all layers at the slot's position, its K/V are appended to the int8 cache, and the
- * position advances (runtime.ts:280-583).  Items with select=1 write out_selected[i]
- * (selectToken, runtime.ts:880-899).  out_logits (n * vocabulary floats, row i for item i) may be
- * NULL; when given, every item's logits are written (step with wantLogits).  The call is
- * synchronous: results are in host memory on return. */
+/* One ragged batched decode step over n items (distinct slots, or a slot's prompt chunk).  For
+ * every item the slot's token runs through all layers at the slot's position, its K/V are appended
+ * to the int8 cache, and the position advances (runtime.ts:280-583).  Items with select=1 write
+ * out_selected[i] (selectToken, runtime.ts:880-899).  out_logits (n * vocabulary floats, row i for
+ * item i) may be NULL; when given, every item's logits are written (step with wantLogits).  The
+ * call is synchronous: results are in host memory on return.  A step of 64 items or more without
+ * out_logits runs as needle_opts.micro_batches micro-batches on their own streams, and from the
+ * second such step on as a replay of a CUDA graph the engine captures on its own stream; results
+ * are the same as one batch's. */
 int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n,
                      const uint32_t* allowed_ids, size_t allowed_total,
                      needle_selected* out_selected, float* out_logits);
