@@ -240,6 +240,18 @@ def roofline_for(prof, n_items, peaks, visible=None, sm_mhz=None, state_chunk=No
     if visible is not None:
         line["visible_positions_per_launch"] = int(visible)
         line["distinct_kv_positions_per_launch"] = int(distinct)
+    if cls == "layer":
+        # k_layer's bound is the dependent binary64 adds of its sequential sums (512 + 512 + 2048 +
+        # 512 terms per item in the reference's order, about 11 cycles each, measured by phase
+        # stamps); every item's CTA is resident at once at these counts, so one chain is the floor
+        mhz = sm_mhz or 1965.0
+        chain_adds, cycles_per_add = 512 + 512 + 2048 + 512, 11
+        floor_ms = chain_adds * cycles_per_add / (mhz * 1e3)
+        line["latency"] = {"bound": "dependent binary64 adds (sequential sums)", "chain_adds_per_item": chain_adds,
+                           "cycles_per_add": cycles_per_add, "floor_ms": round(floor_ms, 5),
+                           "frac": round(floor_ms / per_launch_ms, 4),
+                           "note": "floor = one item's chain at the sampled clock; the rest is the FWHTs, phi "
+                                   "dots and barriers around the chains and the CTAs' contention for the SMs"}
     if fp64_ops is not None:
         mhz = sm_mhz or 1965.0
         fpeak = SMS * FP64_LANES_PER_SM * mhz * 1e6
