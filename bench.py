@@ -1117,29 +1117,31 @@ def gemm_roofline(prof, n_items, peaks):
 
 
 def host_driven(eng, stream, prompts, gens, ramp, warmup, steps, chunk=0, items=0):
-    """Continuous batching driven from the host through needle_cuda_step (host buffers).  With
-    `chunk` >= 2 a slot still reading its prompt sends up to `chunk` prompt positions as consecutive
-    items (a prompt chunk: never its last position, never past the 256-position window), at most
-    `items` items per step, in slot order, as the device scheduler does."""
+    """Continuous batching driven from the host through the C-ABI with host buffers
+    (needle_cuda_step_begin / _end: the layers of step t run while the host plans step t + 1, which
+    needs no result of step t -- a decode item takes its slot's pending token on the device, and
+    the host knows how many tokens each sequence generates).  With `chunk` >= 2 a slot still reading
+    its prompt sends up to `chunk` prompt positions as consecutive items (a prompt chunk: never its
+    last position, never past the 256-position window), at most `items` items per step, in slot
+    order, as the device scheduler does."""
     import torch
     from needle_b200.backend import StepRequest
     n_slots = eng.max_seqs
     queue = 0
-    state = [None] * n_slots  # (seq index, position, generated)
-    max_len = PROMPT[1] + GEN[1]
+    state = [None] * n_slots  # [seq index, position, generated] after every planned step
 
-    def admit():
+    def plan():
+        """The next step from the planned state: (slot resets to make first, requests, generated)."""
         nonlocal queue
+        resets = []
         for s in range(n_slots):
             if state[s] is None and queue < len(prompts):
-                eng.reset(s, len(prompts[queue]) + int(gens[queue]), 0)
+                resets.append((s, len(prompts[queue]) + int(gens[queue])))
                 state[s] = [queue, 0, 0]
                 queue += 1
-
-    def one_step():
-        admit()
         reqs = []
         budget = items - sum(1 for st in state if st is not None) if chunk >= 2 else 0
+        gen = 0
         for s in range(n_slots):
             st = state[s]
             if st is None:
@@ -1154,39 +1156,45 @@ def host_driven(eng, stream, prompts, gens, ramp, warmup, steps, chunk=0, items=
                 budget -= n - 1
             if n > 1:
                 reqs.extend(StepRequest(s, int(p[pos + j]), False) for j in range(n))
-                continue
-            tok = int(p[pos]) if pos < len(p) else -1
-            reqs.append(StepRequest(s, tok, sel))
-        if not reqs:
-            return 0, 0, 0
-        out, _ = eng.step(reqs)
-        gen = 0
-        for r, o in zip(reqs, out):
-            st = state[r.seq]
-            st[1] += 1
-            if r.select:
+            else:
+                reqs.append(StepRequest(s, int(p[pos]) if pos < len(p) else -1, sel))
+            st[1] += n
+            if sel:
                 gen += 1
                 st[2] += 1
-                if st[2] >= gens[st[0]]:
-                    state[r.seq] = None
-        n_sel = sum(1 for r in reqs if r.select)
-        return gen, len(reqs) * 20 + 8, n_sel * 12
+                if st[2] >= gens[q]:
+                    state[s] = None
+        return resets, reqs, gen
 
-    for _ in range(ramp + warmup):
-        one_step()
-    torch.cuda.synchronize()
+    def begin(resets, reqs):
+        for s, max_len in resets:
+            eng.reset(s, max_len, 0)
+        if reqs:
+            eng.step_begin(reqs)
+
+    total = ramp + warmup + steps
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
     gen, h2d, d2h = 0, 0, 0
-    for _ in range(steps):
-        g, a, b = one_step()
-        gen += g
-        h2d += a
-        d2h += b
+    resets, reqs, g = plan()
+    begin(resets, reqs)
+    for i in range(total):
+        nxt = plan() if i + 1 < total else None
+        if reqs:
+            eng.step_end(reqs)
+        if i >= ramp + warmup:
+            gen += g
+            n_sel = sum(1 for r in reqs if r.select)
+            h2d += 2 * (len(reqs) * 20) + 8
+            d2h += n_sel * 12
+        if i + 1 == ramp + warmup:
+            torch.cuda.synchronize()
+            e0.record(stream)
+        if nxt is not None:
+            resets, reqs, g = nxt
+            begin(resets, reqs)
     e1.record(stream)
     torch.cuda.synchronize()
     return {"ms": e0.elapsed_time(e1), "generated": gen, "h2d": int(h2d / steps), "d2h": int(d2h / steps)}
-
 
 if __name__ == "__main__":
     main()

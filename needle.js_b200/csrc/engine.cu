@@ -348,8 +348,9 @@ struct needle_ctx {
   int64_t graph_launches = 0;
   int sched_eager_steps = 0;
   // host steps as micro-batches (needle_cuda_step): the captured step and its shape
-  cudaGraphExec_t host_graph = nullptr;
-  int64_t host_graph_launches = 0;
+  cudaGraphExec_t host_graph = nullptr;        // whole step
+  cudaGraphExec_t host_graph_begin = nullptr;  // needle_cuda_step_begin's part (no selection)
+  int64_t host_graph_launches = 0, host_begin_launches = 0;
   int host_eager_steps = 0, host_m = 0, host_cap = 0;
   std::vector<uint8_t> bytes;  // archive copy (host)
   Archive A;
@@ -397,6 +398,7 @@ struct needle_ctx {
     std::vector<int> order;
     std::vector<needle_step_item> items;
     bool resident = false;  // begun by needle_cuda_resident_forward
+    int mb = 0, cap = 0;    // begun as mb micro-batches of cap rows (0: one batch)
   } pending;
   // scheduler
   SchedView sched{};
@@ -1084,14 +1086,15 @@ bool stage_items_mb(needle_ctx& C, const needle_step_item* items, int32_t n, int
 }
 
 // The kernels of a micro-batched host step (every micro-batch sized `cap` rows; the device counts
-// say how many each holds), forked from and joined back to the context stream.
-void enqueue_host_mb(needle_ctx& C, int M, int cap) {
+// say how many each holds), forked from and joined back to the context stream; without selection
+// when `finish` is false (needle_cuda_step_begin).
+void enqueue_host_mb(needle_ctx& C, int M, int cap, bool finish = true) {
   cuda_check(cudaEventRecord(C.split_ev, C.stream), "split");
   for (int k = 1; k < M; k++) cuda_check(cudaStreamWaitEvent(C.mb_main[k], C.split_ev, 0), "split");
   for (int k = 0; k < M; k++) {
     StepView v = half_view(C, k * cap, C.d_counts + 2 + 2 * k, C.d_counts + 3 + 2 * k);
     v.chunk = 1;
-    enqueue_step(C, v, cap, true, nullptr, lane_k(C, k));
+    enqueue_step(C, v, cap, true, nullptr, lane_k(C, k), finish);
   }
   for (int k = 1; k < M; k++) {
     cuda_check(cudaEventRecord(C.mb_done[k], C.mb_main[k]), "merge");
@@ -1099,11 +1102,64 @@ void enqueue_host_mb(needle_ctx& C, int M, int cap) {
   }
 }
 
-// Drops the captured host step (its kernels hold buffer addresses that are about to change).
+// Drops the captured host steps (their kernels hold buffer addresses that are about to change).
 void drop_host_graph(needle_ctx& C) {
+  if (!C.host_graph && !C.host_graph_begin) return;
+  cudaStreamSynchronize(C.stream);
   if (C.host_graph) cudaGraphExecDestroy(C.host_graph);
-  C.host_graph = nullptr;
+  if (C.host_graph_begin) cudaGraphExecDestroy(C.host_graph_begin);
+  C.host_graph = C.host_graph_begin = nullptr;
   C.host_eager_steps = 0;
+}
+
+// Runs a micro-batched host step's kernels: eagerly the first time, then as a replay of the step
+// captured on the context stream (`graph` / `launches` hold the capture).
+void run_host_mb(needle_ctx& C, int M, int cap, bool finish, cudaGraphExec_t& graph, int64_t& launches) {
+  if (C.host_eager_steps < 1) {
+    enqueue_host_mb(C, M, cap, finish);
+    C.host_eager_steps++;
+    return;
+  }
+  if (!graph) {
+    cuda_check(cudaStreamBeginCapture(C.stream, cudaStreamCaptureModeThreadLocal), "capture");
+    const int64_t l0 = C.launches;
+    try {
+      enqueue_host_mb(C, M, cap, finish);
+    } catch (...) {
+      cudaGraph_t broken = nullptr;
+      cudaStreamEndCapture(C.stream, &broken);
+      if (broken) cudaGraphDestroy(broken);
+      throw;
+    }
+    launches = C.launches - l0;
+    C.launches = l0;
+    cudaGraph_t g = nullptr;
+    cuda_check(cudaStreamEndCapture(C.stream, &g), "capture");
+    const cudaError_t e = cudaGraphInstantiate(&graph, g, 0);
+    cudaGraphDestroy(g);
+    cuda_check(e, "cudaGraphInstantiate");
+  }
+  cuda_check(cudaGraphLaunch(graph, C.stream), "cudaGraphLaunch");
+  C.launches += launches;
+}
+
+// Whether a host step of n items runs as micro-batches, and in what shape.
+bool host_mb_shape(const needle_ctx& C, int32_t n, bool all_logits, int* M, int* cap) {
+  if (all_logits || C.collecting != 0 || C.profiling || C.micro < 2 || n < 64) return false;
+  *M = C.micro;
+  *cap = C.step_capacity / C.micro;
+  return true;
+}
+
+// Uploads a micro-batched step's item rows and per-micro-batch counts.
+void upload_items_mb(needle_ctx& C, const DevItem* src, int M, int cap) {
+  C.timed(P_COPY, [&] {
+    cudaError_t e = cudaMemcpyAsync(C.stv.items, src, size_t(M) * cap * sizeof(DevItem), cudaMemcpyHostToDevice,
+                                    C.stream);
+    if (e != cudaSuccess) return e;
+    return cudaMemcpyAsync(C.d_counts, C.h_counts, size_t(2 + 2 * M) * sizeof(int32_t), cudaMemcpyHostToDevice,
+                           C.stream);
+  });
 }
 
 // The context of every call except needle_cuda_step_end and needle_cuda_close: none may run while a
@@ -1149,6 +1205,7 @@ void destroy(needle_ctx* C) {
   }
   if (C->sched_graph) cudaGraphExecDestroy(C->sched_graph);
   if (C->host_graph) cudaGraphExecDestroy(C->host_graph);
+  if (C->host_graph_begin) cudaGraphExecDestroy(C->host_graph_begin);
   if (C->split_ev) cudaEventDestroy(C->split_ev);
   for (int k = 1; k < kMaxMicro; k++) {
     for (int j = 0; j < 2; j++) {
@@ -1416,12 +1473,24 @@ void end_step(needle_ctx& C, const needle_step_item* items, int32_t n, const uin
     C.h_items_end[P.order[i]] = d;
   }
   upload_allowed(C, allowed_ids, allowed_total);
-  C.timed(P_COPY, [&] {
-    return cudaMemcpyAsync(C.stv.items, C.h_items_end, size_t(n) * sizeof(DevItem), cudaMemcpyHostToDevice,
-                           C.stream);
-  });
-  C.timed(P_FINISH, [&] { return launch_finish(C.mv, C.sv, C.stv, n, nullptr, C.stream); }, C.stream);
-  complete_step(C, items, n, P.n_sel, P.order, out_selected, out_logits);
+  if (P.mb > 0) {  // micro-batched: every micro-batch's rows, then its selection
+    C.timed(P_COPY, [&] {
+      return cudaMemcpyAsync(C.stv.items, C.h_items_end, size_t(P.mb) * P.cap * sizeof(DevItem),
+                             cudaMemcpyHostToDevice, C.stream);
+    });
+    for (int k = 0; k < P.mb; k++) {
+      const StepView v = half_view(C, k * P.cap, C.d_counts + 2 + 2 * k, C.d_counts + 3 + 2 * k);
+      C.timed(P_FINISH, [&] { return launch_finish(C.mv, C.sv, v, P.cap, nullptr, C.stream); }, C.stream);
+    }
+    complete_step(C, items, n, P.mb * P.cap, P.order, out_selected, out_logits);
+  } else {
+    C.timed(P_COPY, [&] {
+      return cudaMemcpyAsync(C.stv.items, C.h_items_end, size_t(n) * sizeof(DevItem), cudaMemcpyHostToDevice,
+                             C.stream);
+    });
+    C.timed(P_FINISH, [&] { return launch_finish(C.mv, C.sv, C.stv, n, nullptr, C.stream); }, C.stream);
+    complete_step(C, items, n, P.n_sel, P.order, out_selected, out_logits);
+  }
   drop.armed = false;
   P.active = false;
   P.resident = false;
@@ -1621,51 +1690,18 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, 
     std::vector<int> order;
     // Many items: micro-batches on their own stream pairs, the step replayed as a CUDA graph after
     // its first (eager) run, as device-scheduled steps are.
-    if (!all_logits && C.collecting == 0 && !C.profiling && C.micro >= 2 && n >= 64) {
-      const int M = C.micro, cap = C.step_capacity / C.micro;
-      if (stage_items_mb(C, items, n, M, cap, order, C.h_items)) {
-        upload_allowed(C, allowed_ids, allowed_total);
-        if (C.host_m != M || C.host_cap != cap) {
-          drop_host_graph(C);
-          C.host_m = M;
-          C.host_cap = cap;
-        }
-        C.timed(P_COPY, [&] {
-          cudaError_t e = cudaMemcpyAsync(C.stv.items, C.h_items, size_t(M) * cap * sizeof(DevItem),
-                                          cudaMemcpyHostToDevice, C.stream);
-          if (e != cudaSuccess) return e;
-          return cudaMemcpyAsync(C.d_counts, C.h_counts, size_t(2 + 2 * M) * sizeof(int32_t), cudaMemcpyHostToDevice,
-                                 C.stream);
-        });
-        if (C.host_eager_steps < 1) {
-          enqueue_host_mb(C, M, cap);
-          C.host_eager_steps++;
-        } else {
-          if (!C.host_graph) {
-            cuda_check(cudaStreamBeginCapture(C.stream, cudaStreamCaptureModeThreadLocal), "capture");
-            const int64_t l0 = C.launches;
-            try {
-              enqueue_host_mb(C, M, cap);
-            } catch (...) {
-              cudaGraph_t broken = nullptr;
-              cudaStreamEndCapture(C.stream, &broken);
-              if (broken) cudaGraphDestroy(broken);
-              throw;
-            }
-            C.host_graph_launches = C.launches - l0;
-            C.launches = l0;
-            cudaGraph_t g = nullptr;
-            cuda_check(cudaStreamEndCapture(C.stream, &g), "capture");
-            const cudaError_t e = cudaGraphInstantiate(&C.host_graph, g, 0);
-            cudaGraphDestroy(g);
-            cuda_check(e, "cudaGraphInstantiate");
-          }
-          cuda_check(cudaGraphLaunch(C.host_graph, C.stream), "cudaGraphLaunch");
-          C.launches += C.host_graph_launches;
-        }
-        complete_step(C, items, n, M * cap, order, out_selected, nullptr);
-        return;
+    int M = 0, cap = 0;
+    if (host_mb_shape(C, n, all_logits, &M, &cap) && stage_items_mb(C, items, n, M, cap, order, C.h_items)) {
+      upload_allowed(C, allowed_ids, allowed_total);
+      if (C.host_m != M || C.host_cap != cap) {
+        drop_host_graph(C);
+        C.host_m = M;
+        C.host_cap = cap;
       }
+      upload_items_mb(C, C.h_items, M, cap);
+      run_host_mb(C, M, cap, true, C.host_graph, C.host_graph_launches);
+      complete_step(C, items, n, M * cap, order, out_selected, nullptr);
+      return;
     }
     stage_items(C, items, n, n_sel, all_logits, order, C.h_items);
     upload_allowed(C, allowed_ids, allowed_total);
@@ -1685,11 +1721,25 @@ int needle_cuda_step_begin(needle_ctx* ctx, const needle_step_item* items, int32
     const int n_sel = check_items(C, items, n, false, nullptr, 0, true, &chunks);
     require(n > 0, NEEDLE_BACKEND_UNAVAILABLE, "a split step needs at least one item");
     auto& P = C.pending;
-    stage_items(C, items, n, n_sel, false, P.order, C.h_items);
-    upload_items(C, C.h_items, n, n_sel);
-    StepView v = C.stv;
-    v.chunk = chunks ? 1 : 0;
-    enqueue_step(C, v, n, n_sel > 0, nullptr, lane_a(C), /*finish=*/false);
+    int M = 0, cap = 0;
+    P.mb = P.cap = 0;
+    if (host_mb_shape(C, n, false, &M, &cap) && stage_items_mb(C, items, n, M, cap, P.order, C.h_items)) {
+      if (C.host_m != M || C.host_cap != cap) {
+        drop_host_graph(C);
+        C.host_m = M;
+        C.host_cap = cap;
+      }
+      upload_items_mb(C, C.h_items, M, cap);
+      run_host_mb(C, M, cap, false, C.host_graph_begin, C.host_begin_launches);
+      P.mb = M;
+      P.cap = cap;
+    } else {
+      stage_items(C, items, n, n_sel, false, P.order, C.h_items);
+      upload_items(C, C.h_items, n, n_sel);
+      StepView v = C.stv;
+      v.chunk = chunks ? 1 : 0;
+      enqueue_step(C, v, n, n_sel > 0, nullptr, lane_a(C), /*finish=*/false);
+    }
     P.items.assign(items, items + n);
     P.n = n;
     P.n_sel = n_sel;
@@ -1832,6 +1882,7 @@ int needle_cuda_resident_forward(needle_ctx* ctx, int32_t seq, int32_t position,
     P.items.assign(&item, &item + 1);
     P.n = 1;
     P.n_sel = 1;
+    P.mb = P.cap = 0;
     P.active = true;
     P.resident = true;
   });

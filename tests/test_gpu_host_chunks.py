@@ -96,15 +96,16 @@ def test_host_chunks_refused(archive):
 
 def test_many_items_run_as_micro_batches(archive):
     """A host step of 64 items or more runs as micro-batches (replayed as a CUDA graph from its
-    second step on): the same ids and K/V as one batch, with chunks, decode slots and slots that
-    finish and are reset in between."""
+    second step on), through needle_cuda_step and through needle_cuda_step_begin / _end: the same
+    ids and K/V as one batch, with chunks, decode slots and slots that finish and are reset in
+    between."""
     from needle_b200.backend import CudaEngine, StepRequest
     rng = np.random.default_rng(12)
     n_slots = 96
     prompts = [rng.integers(0, 8192, int(n)).astype(np.int32) for n in rng.integers(2, 40, n_slots)]
     gens = [int(g) for g in rng.integers(1, 6, n_slots)]
     runs = []
-    for micro in (1, 4):
+    for micro, split in ((1, False), (4, False), (4, True)):
         with CudaEngine(archive, device=0, max_seqs=n_slots, max_len=64, max_sink=0, micro_batches=micro,
                         sched_chunk=8, sched_items=160) as eng:
             for s in range(n_slots):
@@ -125,7 +126,11 @@ def test_many_items_run_as_micro_batches(archive):
                     else:
                         reqs.append(StepRequest(s, int(p[-1]) if pos[s] == len(p) - 1 else -1, True))
                 assert len(reqs) >= 64
-                out, _ = eng.step(reqs)
+                if split:
+                    eng.step_begin(reqs)
+                    out = eng.step_end(reqs)
+                else:
+                    out, _ = eng.step(reqs)
                 sel = []
                 for r, o in zip(reqs, out):
                     pos[r.seq] += 1
@@ -135,11 +140,12 @@ def test_many_items_run_as_micro_batches(archive):
                 trace.append(sel)
             kv = [eng.read_kv(s, 0) for s in (0, 17, 95)]
             runs.append((trace, pos, kv, eng.kernel_launches() - l0))
-    (ta, pa, ka, la), (tb, pb, kb, lb) = runs
-    assert lb > 3 * la  # four micro-batches: the kernels of each launched per micro-batch
-    assert pa == pb
-    for step, (a, b) in enumerate(zip(ta, tb)):
-        assert a == b, f"step {step}"
-    for a, b in zip(ka, kb):
-        for x, y in zip(a, b):
-            np.testing.assert_array_equal(x, y)
+    (ta, pa, ka, la) = runs[0]
+    for tb, pb, kb, lb in runs[1:]:
+        assert lb > 3 * la  # four micro-batches: the kernels of each launched per micro-batch
+        assert pa == pb
+        for step, (a, b) in enumerate(zip(ta, tb)):
+            assert a == b, f"step {step}"
+        for a, b in zip(ka, kb):
+            for x, y in zip(a, b):
+                np.testing.assert_array_equal(x, y)

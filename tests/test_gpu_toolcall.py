@@ -104,3 +104,20 @@ def test_device_masks_match_oracle(setup, oracle):
         ids, complete, dead = oracle_constrained(oracle, model, vocab, tools, p, maximum_new)
         assert res.ids == ids, k
         assert res.complete == complete and res.dead_end == dead, k
+
+
+def test_many_slots_split_steps_match_one_batch(setup):
+    """Config 5's loop with 80 slots: its split steps (64 items or more) run as micro-batches; the
+    tokens are those of one batch."""
+    from needle_b200.backend import CudaEngine
+    from needle_b200 import toolcall
+    archive, vocab, tools, model = setup
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, 8192, int(n)).astype(np.int32) for n in rng.integers(3, 12, 80)]
+    outs = []
+    for micro in (1, 4):
+        with CudaEngine(archive, device=0, max_seqs=80, max_len=64, max_sink=0, micro_batches=micro) as eng:
+            dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=24, threads=4, mask_cache=256)
+            results, stats = dec.run(prompts)
+            outs.append([(r.ids, r.complete, r.dead_end) for r in results])
+    assert outs[0] == outs[1]
