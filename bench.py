@@ -1061,10 +1061,11 @@ def main():
                 "processed_tokens_per_s": round(fproc_all / (fms_max / 1e3), 1), "generated_tokens": int(fgen_all),
                 "gpu_launches": flaunch_all,
                 "numerics": "fast: projections (Q|K|V|gate, output, engram K|V, vocabulary) as tcgen05 GEMMs with "
-                            "fp16 head/tail operands and fp32 accumulation; norms, attention, routing and selection "
-                            "binary64 as in exact; greedy ids equal to the CPU reference, logits within 1e-3 "
+                            "fp16 head/tail operands and fp32 accumulation; attention in binary32 over the int8 "
+                            "cache; norm sums as block reductions; K/V append, routing and selection binary64 as in "
+                            "exact; greedy ids equal to the CPU reference, logits within 1e-3 "
                             "(tests/test_gpu_fast_engine.py)",
-                "dtype": "fp16x2 (head/tail) -> fp32 GEMMs; f64 elsewhere",
+                "dtype": "fp16x2 (head/tail) -> fp32 GEMMs; f32 attention; f64 elsewhere",
                 "kernel_ms_per_step": {k: round(v[0] / 10, 4) for k, v in fprof.items()},
                 "roofline_gemm": gemm_roofline(fprof, SLOTS, peaks)}
     if rank == 0:

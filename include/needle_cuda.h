@@ -46,11 +46,12 @@ enum {
   NEEDLE_NUMERICS_FAST = 1,  /* the projections (Q|K|V|gate, output, engram K|V, vocabulary) as
                                 tcgen05 tensor-core GEMMs over the step's items, fp16 head/tail
                                 split with fp32 accumulation (binary32-level accuracy), and the
-                                layer's norm sums as block reductions; attention, routing and
-                                selection as in exact numerics; int8 KV cache only.  Same greedy
+                                layer's norm sums as block reductions; attention in binary32 (online
+                                softmax over the int8 cache, CUDA cores); the K/V append, routing
+                                and selection as in exact numerics; int8 KV cache only.  Same greedy
                                 ids as the CPU backend, logits within 1e-3 */
-  NEEDLE_NUMERICS_FAST_ATTENTION = 2, /* NEEDLE_NUMERICS_FAST plus attention on the int8-MMA kernel
-                                (binary32 online softmax over the int8 cache): logits within 3e-3 */
+  NEEDLE_NUMERICS_FAST_ATTENTION = 2, /* NEEDLE_NUMERICS_FAST with attention on the int8-MMA kernel
+                                (integer-digit tensor-core products): logits within 3e-3 */
   NEEDLE_KV_INT8 = 0,        /* RuntimeOptions.kvCache "int8" (runtime.ts:30-32) */
   NEEDLE_KV_FLOAT32 = 1      /* RuntimeOptions.kvCache "float32": keys / values stored as given */
 };

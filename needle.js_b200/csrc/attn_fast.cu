@@ -681,7 +681,7 @@ size_t attention_fast_scratch_bytes(int32_t batch, int32_t capacity) {
 cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
                                   const float* vs, const int32_t* counts, int32_t batch, int32_t capacity,
                                   float* out, void* scratch, cudaStream_t s, const int64_t* row_base,
-                                  int64_t cache_rows) {
+                                  int64_t cache_rows, bool tensor) {
   if (batch <= 0) return cudaSuccess;
   const int splits = (capacity + kSplit - 1) / kSplit;
   int32_t* status = static_cast<int32_t*>(scratch);
@@ -698,7 +698,8 @@ cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float*
                          reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs) |
                          reinterpret_cast<uintptr_t>(q)) & 15) == 0;
   CUtensorMap kmap, vmap;
-  const bool mma = aligned && encode_rows_map(&kmap, kc, rows_total) && encode_rows_map(&vmap, vc, rows_total);
+  const bool mma = tensor && aligned && encode_rows_map(&kmap, kc, rows_total) &&
+                   encode_rows_map(&vmap, vc, rows_total);
   if (mma) {
     const size_t smem = sizeof(MmaStage) * kMmaStages + 1024;  // + alignment slack
     static std::atomic<uint64_t> configured{0};

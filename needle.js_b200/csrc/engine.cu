@@ -365,12 +365,12 @@ struct needle_ctx {
   // Fast numerics (NEEDLE_NUMERICS_FAST): Q|K|V|gate of each layer and K|V of each engram site as
   // one matrix each (one GEMM per shared input), and per micro-batch lane the GEMM's scratch.
   bool fast = false;
-  bool fast_attention = false;  // NEEDLE_NUMERICS_FAST_ATTENTION: also the int8-MMA attention
+  bool fast_attention = false;  // NEEDLE_NUMERICS_FAST_ATTENTION: int8-MMA attention (else binary32)
   int sms = 0;
   std::vector<CqMat> lqkvg, ekv;
   void* gemm_scratch[kMaxMicro] = {};
   size_t gemm_scratch_bytes = 0;
-  void* attn_scratch[kMaxMicro] = {};  // the int8-MMA attention's partials and counters, per lane
+  void* attn_scratch[kMaxMicro] = {};  // the fast attention's partials and counters, per lane
   int32_t* d_counts = nullptr;  // [0] n_items, [1] n_select
   std::vector<SlotHost> slots;
   // pinned staging
@@ -777,8 +777,8 @@ void build_state(needle_ctx& C) {
     C.gemm_scratch_bytes = (bytes + 255) & ~size_t(255);
     for (int k = 0; k < kMaxMicro; k++) C.gemm_scratch[k] = C.dalloc<uint8_t>(C.gemm_scratch_bytes, false);
   }
-  if (C.fast_attention) {
-    // int8-MMA attention: rotated queries, visible counts, cache rows, outputs; per lane its scratch
+  if (C.fast) {
+    // fast attention: rotated queries, visible counts, cache rows, outputs; per lane its scratch
     // (status and work counters zeroed here, left at zero by every call)
     st.qrope = C.dalloc<float>(B * kDim);
     st.attn_out = C.dalloc<float>(B * kDim);
@@ -941,16 +941,18 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
                 {C.lv[l], 0, 256, st.prep_a, kDim, st.qkvg + 768, 1536},
                 {C.lg[l], 0, 512, st.prep_a, kDim, st.qkvg + 1024, 1536}},
                n_host, n_dev, s0);
-    if (C.fast_attention) {
-      // append every item's K/V (and leave its rotated query, count and cache row), then the
-      // int8-MMA attention over the cache and the gate
+    if (C.fast) {
+      // append every item's K/V (and leave its rotated query, count and cache row), then attention
+      // over the cache -- binary32 on the CUDA cores (NEEDLE_NUMERICS_FAST) or int8 MMAs
+      // (NEEDLE_NUMERICS_FAST_ATTENTION) -- and the gate
       const int64_t cache_rows = int64_t(C.opts.max_seqs) * m.layers * kKvHeads * sv.capacity;
       C.launches += 3;  // + persistent attention, combine, gate (timed() counts the append)
       C.timed(P_ATTN, [&] {
         cudaError_t e = launch_attention(m, sv, st, l, n_host, s0, 1);
         if (e == cudaSuccess)
           e = launch_attention_fast(st.qrope, sv.kcodes, sv.kscale, sv.vcodes, sv.vscale, st.attn_count, n_host,
-                                    sv.capacity, st.attn_out, C.attn_scratch[lane.index], s0, st.attn_row, cache_rows);
+                                    sv.capacity, st.attn_out, C.attn_scratch[lane.index], s0, st.attn_row, cache_rows,
+                                    C.fast_attention);
         if (e == cudaSuccess) e = launch_attention_gate(st, n_host, s0);
         return e;
       }, s0);

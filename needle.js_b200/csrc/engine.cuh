@@ -189,11 +189,12 @@ size_t attention_smem_bytes(int32_t capacity, bool ring);
 size_t attention_fast_scratch_bytes(int32_t batch, int32_t capacity);
 // row_base (optional, per item): the cache row of (item, KV head 0), head h at + h * capacity, in
 // a cache of cache_rows rows of 64 codes (the engine's [slot][layer][head][capacity] blocks);
-// without it item b's rows are b * kv_heads * capacity onwards.
+// without it item b's rows are b * kv_heads * capacity onwards.  `tensor`: the int8-MMA kernel
+// where the cache allows it (false: the binary32 CUDA-core kernel).
 cudaError_t launch_attention_fast(const float* q, const int8_t* kc, const float* ks, const int8_t* vc,
                                   const float* vs, const int32_t* counts, int32_t batch, int32_t capacity,
                                   float* out, void* scratch, cudaStream_t s, const int64_t* row_base = nullptr,
-                                  int64_t cache_rows = 0);
+                                  int64_t cache_rows = 0, bool tensor = true);
 // Fast numerics, after launch_attention (part 1) and launch_attention_fast: attention output times
 // sigmoid(gate) and the output projection's prepared input, per (item, KV head).
 cudaError_t launch_attention_gate(const StepView& st, int n_host, cudaStream_t s);

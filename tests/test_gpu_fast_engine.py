@@ -3,8 +3,9 @@
 Fast numerics computes every projection of a step -- Q|K|V|gate, the output projection, the engram
 key|value projections and the tied vocabulary head -- as a tcgen05 tensor-core GEMM over the step's
 items (fp16 head/tail split operands, fp32 accumulation: about 1e-6 relative per projection), and
-prompt chunks go through the same GEMMs (batched prefill).  Norms, attention, routing and selection
-stay as in exact numerics.  Bar (north star): the same greedy token ids as the CPU reference and
+prompt chunks go through the same GEMMs (batched prefill), and attention runs in binary32 over the
+int8 cache (online softmax on the CUDA cores).  The K/V append, routing and selection stay as in
+exact numerics.  Bar (north star): the same greedy token ids as the CPU reference and
 logits within 1e-3 max-abs-relative (max |a - b| / max(|b|, 1) per logits vector).  The margin is
 thin by construction: the int8 KV cache turns last-bit differences of K and V into whole-code
 differences for 1-2 % of the codes of deep layers, and the 27 layers of the random-init model
