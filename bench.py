@@ -787,11 +787,13 @@ def bench_toolcall(args, rank, world, local_rank):
     n_local = args.sequences // world + (1 if rank < args.sequences % world else 0)
     ids = synth.integers(5 + 1000 * rank, n_local * TOOLCALL_PROMPT + 1, 8192, stream=7).astype(np.int32)
     prompts = [ids[k * TOOLCALL_PROMPT:(k + 1) * TOOLCALL_PROMPT] for k in range(n_local)]
+    step_items = args.slots * 3 // 2 if args.sched_chunk >= 2 else args.slots
     eng = CudaEngine(archive, device=local_rank, max_seqs=args.slots, max_len=TOOLCALL_PROMPT + TOOLCALL_MAX_NEW + 8,
-                     max_sink=16)
+                     max_sink=16, sched_chunk=args.sched_chunk, sched_items=step_items if args.sched_chunk >= 2 else 0)
     threads = max(1, min(16, cpu_threads() // max(1, world)))
     dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=TOOLCALL_MAX_NEW, threads=threads,
-                                      mask_cache=args.mask_cache)
+                                      mask_cache=args.mask_cache, prompt_chunk=args.sched_chunk,
+                                      step_items=step_items)
     dec.run(prompts[:min(8, n_local)], max_steps=max(3, args.warmup))  # warm-up steps (untimed)
     stream = torch.cuda.ExternalStream(eng.stream, device=local_rank)
     l0 = eng.kernel_launches()
@@ -849,6 +851,8 @@ def bench_toolcall(args, rank, world, local_rank):
                            "host_loop_seconds_max_rank": round(max(wall - gsec - esec, 0.0), 3),
                            "allowed": (f"device mask pool, masks cached per grammar state ({args.mask_cache} slots "
                                        f"per GPU)" if args.mask_cache else "id lists per step"),
+                           "prompt_chunks": ({"chunk": args.sched_chunk, "items_per_step": step_items}
+                                             if args.sched_chunk >= 2 else "one position per slot and step"),
                            "masks_put": int(masks_put), "masked_selections": int(masked_items),
                            "allowed_ids_sent": int(allowed_ids),
                            "numerics": "exact (tokens bit-identical to the CPU backend with the same masks)",

@@ -72,8 +72,10 @@ typedef struct needle_opts {
                             0 or 1 = one position per slot and step, the default).  A chunk never
                             reaches past the slot's KV window (prompt positions beyond it go one
                             per step) and holds no selecting position; the results are the same */
-  int32_t sched_items;   /* device-scheduled steps with chunks: items one step may hold, spread over
-                            the micro-batches with whole chunks (>= max_seqs; 0 = 2 x max_seqs) */
+  int32_t sched_items;   /* with sched_chunk >= 2: the items one step may hold -- a device-scheduled
+                            step, spread over the micro-batches with whole chunks, or a host step
+                            (needle_cuda_step, _begin) with prompt chunks (>= max_seqs; 0 = 2 x
+                            max_seqs); without it a step holds max(max_seqs, 64) items */
   int32_t reserved[6];
 } needle_opts;
 

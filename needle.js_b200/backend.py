@@ -65,6 +65,7 @@ class CudaEngine:
         self.vocab = g.vocabulary_size
         self.layers = g.layers
         self.max_seqs = max_seqs
+        self.kv_window = g.kv_window
 
     def close(self):
         if getattr(self, "h", None):

@@ -87,9 +87,13 @@ class DecodeStats:
 
 class ConstrainedDecoder:
     def __init__(self, engine, vocab: Vocabulary, tools: Sequence[dict], maximum_calls: int = 4,
-                 maximum_new_tokens: int = 256, threads: int = 8, mask_cache: int = 0):
+                 maximum_new_tokens: int = 256, threads: int = 8, mask_cache: int = 0, prompt_chunk: int = 0,
+                 step_items: int = 0):
         """`mask_cache` > 0: keep allowed masks per grammar state in a cache of that many slots and
-        a device pool of the same size (at least the engine's slot count); 0: id lists per step."""
+        a device pool of the same size (at least the engine's slot count); 0: id lists per step.
+        `prompt_chunk` >= 2: a slot still reading its prompt sends up to that many prompt positions
+        per step as a chunk of items (never the last, which selects), at most `step_items` items per
+        step (0: the engine's slot count), in slot order; the tokens are the same."""
         self.engine = engine
         self.vocab = vocab
         self.tools = list(tools)
@@ -97,6 +101,9 @@ class ConstrainedDecoder:
         self.maximum_new = max(1, maximum_new_tokens)
         self.threads = threads
         self.template = ToolCallGrammar(self.tools, maximum_calls)  # validates the tools once
+        self.prompt_chunk = prompt_chunk
+        self.step_items = step_items or engine.max_seqs
+        self.window = getattr(engine, "kv_window", 0)  # slots are reset with sink 0
         self.cache = None
         if mask_cache:
             if mask_cache < engine.max_seqs:
@@ -154,12 +161,22 @@ class ConstrainedDecoder:
             if hook is not None:
                 hook(stats.steps)
             requests = []
+            budget = self.step_items - len(live)
             for s in live:
                 st = state[s]
                 if st["phase"] == "prompt":
-                    last = st["pos"] == st["prompt"].size - 1
-                    requests.append(StepRequest(s, int(st["prompt"][st["pos"]]), last))
-                    stats.prompt_tokens += 1
+                    p, pos = st["prompt"], st["pos"]
+                    last = pos == p.size - 1
+                    k = 1
+                    if self.prompt_chunk >= 2 and not last:  # a chunk: never past the KV window
+                        want = min(self.prompt_chunk, p.size - 1 - pos)
+                        if self.window > 0:
+                            want = min(want, self.window - pos)
+                        want = max(1, want)
+                        k = 1 + max(0, min(want - 1, budget))
+                        budget -= k - 1
+                    requests.extend(StepRequest(s, int(p[pos + j]), last) for j in range(k))
+                    stats.prompt_tokens += k
                 else:  # "call": the pending token, selecting unless its feed completes the call
                     requests.append(StepRequest(s, st["pending"], st["phase"] == "call"))
             t0 = time.perf_counter()

@@ -30,6 +30,7 @@ class FakeEngine:
 
     def __init__(self, max_seqs, vocab):
         self.max_seqs, self.vocab = max_seqs, vocab
+        self.kv_window = 256
         self.hist = [None] * max_seqs
         self.pending = None
         self.steps = 0
@@ -55,7 +56,12 @@ class FakeEngine:
     def step_begin(self, requests):
         assert self.pending is None and requests
         slots = [r.seq for r in requests]
-        assert len(set(slots)) == len(slots)
+        # a slot appears once, or as consecutive items that do not select (a prompt chunk)
+        runs = [s for i, s in enumerate(slots) if i == 0 or slots[i - 1] != s]
+        assert len(set(runs)) == len(runs)
+        for i in range(1, len(requests)):
+            if slots[i] == slots[i - 1]:
+                assert not requests[i].select and not requests[i - 1].select and requests[i].token >= 0
         self.pending = [(r.seq, r.token, r.select) for r in requests]
 
     def step_end(self, requests):
@@ -149,6 +155,23 @@ def test_mask_cache_decodes_the_same_tokens(env, capacity):
         assert dec.cache.stats["evictions"] > 0
     with pytest.raises(ValueError):
         toolcall.ConstrainedDecoder(FakeEngine(4, vocab.size), vocab, tools, mask_cache=3)
+
+
+def test_prompt_chunks_decode_the_same_tokens(env):
+    """Prompts sent in chunks of up to 8 positions per step (at most 16 items per step over 6
+    slots) feed every slot the same tokens as one position per step, so the calls are the same."""
+    grammar, toolcall, vocab = env
+    tools = toolcall.synthetic_tools(5)
+    rng = np.random.default_rng(13)
+    prompts = [rng.integers(0, vocab.size, int(rng.integers(2, 40))).astype(np.int32) for _ in range(9)]
+    plain, st0 = toolcall.ConstrainedDecoder(FakeEngine(6, vocab.size), vocab, tools,
+                                             maximum_new_tokens=60).run(prompts)
+    eng = FakeEngine(6, vocab.size)
+    chunked, st1 = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=60, prompt_chunk=8,
+                                               step_items=16).run(prompts)
+    for a, b in zip(plain, chunked):
+        assert a.ids == b.ids and a.complete == b.complete and a.calls == b.calls
+    assert st1.prompt_tokens == st0.prompt_tokens and st1.steps < st0.steps
 
 
 def test_slots_are_reused_and_histories_match(env):
