@@ -121,3 +121,23 @@ def test_many_slots_split_steps_match_one_batch(setup):
             results, stats = dec.run(prompts)
             outs.append([(r.ids, r.complete, r.dead_end) for r in results])
     assert outs[0] == outs[1]
+
+
+def test_prompt_chunks_match_oracle(setup, oracle):
+    """The same decode with prompts sent in chunks of up to 8 positions per step (at most 24 items
+    per step): the oracle's ids, fed one token at a time."""
+    from needle_b200.backend import CudaEngine
+    from needle_b200 import toolcall
+    archive, vocab, tools, model = setup
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, 8192, n).astype(np.int32) for n in (40, 33, 57, 21, 48)]
+    maximum_new = 48
+    with CudaEngine(archive, device=0, max_seqs=3, max_len=160, max_sink=16) as eng:
+        dec = toolcall.ConstrainedDecoder(eng, vocab, tools, maximum_new_tokens=maximum_new, threads=4,
+                                          prompt_chunk=8, step_items=24)
+        results, stats = dec.run(prompts)
+    assert stats.prompt_tokens == sum(p.size for p in prompts)
+    for k, (p, res) in enumerate(zip(prompts, results)):
+        ids, complete, dead = oracle_constrained(oracle, model, vocab, tools, p, maximum_new)
+        assert res.ids == ids, k
+        assert res.complete == complete and res.dead_end == dead, k
