@@ -384,6 +384,14 @@ int needle_cuda_sched_slot(needle_ctx* ctx, int32_t slot, int32_t* seq_id, int32
 /* Number of CUDA kernels this context has launched so far (for launch accounting). */
 int needle_cuda_kernel_launches(const needle_ctx* ctx, int64_t* count);
 
+/* Overrun check (no counterpart; the reference has no sanitizer, and compute-sanitizer is not
+ * available where this runs): every device buffer of the context's model, slot state and step
+ * scratch is followed by 256 guard bytes of a fixed pattern; this synchronises the device and
+ * reports through *damaged how many guards no longer hold it (0: no kernel wrote past the end of
+ * those buffers).  With the environment variable NEEDLE_NVTX set (not "0") when the context is
+ * opened, every step and kernel class is also an NVTX range, for profilers that filter by range. */
+int needle_cuda_check_guards(const needle_ctx* ctx, int32_t* damaged);
+
 /* Per-kernel-class timing with CUDA events on the context stream (off by default).  enable=1
  * starts accumulating, enable=0 stops.  read fills up to n entries of (name, total ms, launches)
  * and returns the number of classes through *count. */

@@ -246,6 +246,13 @@ class CudaEngine:
         check(lib().needle_cuda_sched_slot(self.h, slot, C.byref(sid), C.byref(pos), C.byref(busy)))
         return sid.value, pos.value, bool(busy.value)
 
+    def damaged_guards(self) -> int:
+        """Guards after the context's device buffers that no longer hold their pattern (0: no
+        kernel wrote past those buffers; needle_cuda_check_guards)."""
+        n = C.c_int32()
+        check(lib().needle_cuda_check_guards(self.h, C.byref(n)))
+        return n.value
+
     def kernel_launches(self) -> int:
         n = C.c_int64()
         check(lib().needle_cuda_kernel_launches(self.h, C.byref(n)))

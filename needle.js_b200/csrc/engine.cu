@@ -1,10 +1,12 @@
 // engine.cu -- host side of libneedle_cuda.so: `.cact` parsing, weight upload, per-slot state,
 // batched step orchestration, device scheduler, and the C-ABI of include/needle_cuda.h.
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <memory>
@@ -414,6 +416,7 @@ struct needle_ctx {
   float* d_row_out = nullptr;
   // profiling
   bool profiling = false;
+  bool nvtx = false;  // NEEDLE_NVTX set at open: an NVTX range around every step and kernel class
   int64_t launches = 0;  // kernels launched by this context
   int collecting = 0;    // slots that feed a confidence probe pool
   double* d_confidence = nullptr;
@@ -422,12 +425,23 @@ struct needle_ctx {
   double prof_ms[kProfClasses] = {0};
   int64_t prof_n[kProfClasses] = {0};
 
+  // Device buffers carry kGuardBytes of a known pattern after their last byte
+  // (needle_cuda_check_guards reads them back: a kernel that wrote past a buffer is found).
+  static constexpr size_t kGuardBytes = 256;
+  static constexpr int kGuardByte = 0xA5;
+  struct Guard {
+    const uint8_t* at;
+  };
+  std::vector<Guard> guards;
   template <class T>
   T* dalloc(size_t count, bool zero = true) {
     void* p = nullptr;
-    cuda_check(cudaMalloc(&p, std::max<size_t>(count * sizeof(T), 16)), "cudaMalloc");
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    cuda_check(cudaMalloc(&p, bytes + kGuardBytes), "cudaMalloc");
     allocs.push_back(p);
-    if (zero) cuda_check(cudaMemset(p, 0, std::max<size_t>(count * sizeof(T), 16)), "cudaMemset");
+    if (zero) cuda_check(cudaMemset(p, 0, bytes), "cudaMemset");
+    cuda_check(cudaMemset(static_cast<uint8_t*>(p) + bytes, kGuardByte, kGuardBytes), "cudaMemset");
+    guards.push_back({static_cast<const uint8_t*>(p) + bytes});
     return static_cast<T*>(p);
   }
 
@@ -459,6 +473,15 @@ struct needle_ctx {
   void timed(int cls, F&& launch, cudaStream_t s = nullptr) {
     if (!s) s = stream;
     if (cls != P_COPY) launches += cls == P_SCHED ? 2 : 1;
+    struct Range {
+      bool on;
+      Range(bool o, const char* name) : on(o) {
+        if (on) nvtxRangePushA(name);
+      }
+      ~Range() {
+        if (on) nvtxRangePop();
+      }
+    } range(nvtx, kProfNames[cls]);
     if (!profiling) {
       cuda_check(launch(), kProfNames[cls]);
       return;
@@ -1579,6 +1602,7 @@ int needle_cuda_open(const uint8_t* cact, size_t n, const needle_opts* opts, nee
     }
     cuda_check(cudaEventCreateWithFlags(&C->split_ev, cudaEventDisableTiming), "cudaEventCreate");
     if (o.micro_batches > 0) C->micro = std::min(kMaxMicro, int(o.micro_batches));
+    if (const char* v = std::getenv("NEEDLE_NVTX")) C->nvtx = v[0] != 0 && v[0] != '0';
     if (o.sched_chunk >= 2) {
       C->sched_chunk = o.sched_chunk;
       C->sched_items = o.sched_items > 0 ? o.sched_items : 2 * o.max_seqs;
@@ -2263,6 +2287,25 @@ int needle_cuda_sched_slot(needle_ctx* ctx, int32_t slot, int32_t* seq_id, int32
     if (seq_id) *seq_id = st.kv_alloc > 0 ? st.seq_id : -1;
     if (position) *position = st.position;
     if (busy) *busy = st.busy;
+  });
+}
+
+int needle_cuda_check_guards(const needle_ctx* ctx, int32_t* damaged) {
+  return guarded([&] {
+    require(ctx != nullptr && damaged != nullptr, NEEDLE_BACKEND_UNAVAILABLE, "null argument");
+    needle_ctx& C = *ctx_of(const_cast<needle_ctx*>(ctx));
+    cuda_check(cudaDeviceSynchronize(), "check_guards");
+    std::vector<uint8_t> host(needle_ctx::kGuardBytes);
+    int32_t bad = 0;
+    for (const auto& g : C.guards) {
+      cuda_check(cudaMemcpy(host.data(), g.at, host.size(), cudaMemcpyDeviceToHost), "check_guards");
+      for (uint8_t b : host)
+        if (b != needle_ctx::kGuardByte) {
+          bad++;
+          break;
+        }
+    }
+    *damaged = bad;
   });
 }
 

@@ -119,6 +119,7 @@ EXPORTS = {
     "needle_cuda_mask_pool": (C.c_int, [C.c_void_p, C.c_int32]),
     "needle_cuda_masks_put": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p]),
     "needle_cuda_kernel_launches": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64)]),
+    "needle_cuda_check_guards": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
     "needle_cuda_profile": (C.c_int, [C.c_void_p, C.c_int32]),
     "needle_cuda_profile_read": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_char_p),
                                            C.POINTER(C.c_double), C.POINTER(C.c_int64),

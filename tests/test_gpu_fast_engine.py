@@ -117,6 +117,7 @@ def test_scheduler_fast_ids_equal_except_at_near_ties(archive, oracle, ref_model
                 break
         assert finished == n
         ids = eng.sched_ids()
+        assert eng.damaged_guards() == 0  # no kernel (GEMMs, fast attention) wrote past a buffer
     offs = np.concatenate([[0], np.cumsum(gens)])
 
     def check(i):

@@ -139,6 +139,7 @@ def test_many_items_run_as_micro_batches(archive):
                         sel.append((r.seq, int(o[0]), o[1]))
                 trace.append(sel)
             kv = [eng.read_kv(s, 0) for s in (0, 17, 95)]
+            assert eng.damaged_guards() == 0
             runs.append((trace, pos, kv, eng.kernel_launches() - l0))
     (ta, pa, ka, la) = runs[0]
     for tb, pb, kb, lb in runs[1:]:
@@ -149,3 +150,20 @@ def test_many_items_run_as_micro_batches(archive):
         for a, b in zip(ka, kb):
             for x, y in zip(a, b):
                 np.testing.assert_array_equal(x, y)
+
+
+def test_nvtx_ranges_do_not_change_a_step(archive, monkeypatch):
+    """With NEEDLE_NVTX set when the context opens, steps run inside NVTX ranges: same selections."""
+    from needle_b200.backend import CudaEngine, StepRequest
+    outs = []
+    for nvtx in ("0", "1"):
+        monkeypatch.setenv("NEEDLE_NVTX", nvtx)
+        with CudaEngine(archive, device=0, max_seqs=2, max_len=32, max_sink=0) as eng:
+            eng.reset(0, 32, 0)
+            eng.reset(1, 32, 0)
+            got = []
+            for t in range(6):
+                out, _ = eng.step([StepRequest(0, 3 + t, t == 5), StepRequest(1, 7 + t, t == 5)])
+                got.append(out)
+            outs.append(got)
+    assert outs[0] == outs[1]

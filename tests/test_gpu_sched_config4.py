@@ -53,10 +53,11 @@ def run(oracle, request):
         assert running, "no running slot past the window wrap"
         pos, slot, sid = running[0]
         kv = [eng.read_kv(slot, layer) for layer in range(eng.layers)]
+        guards = eng.damaged_guards()
     offs = np.concatenate([[0], np.cumsum(gens)]).astype(np.int64)
     yield dict(prompts=prompts, gens=gens, tokens=tokens, generated=generated, finished=finished, last=last,
                ids=ids, offs=offs, kv_slot=(slot, sid, pos, kv), model=oracle.Model(archive),
-               chunks=bool(request.param))
+               chunks=bool(request.param), guards=guards)
 
 
 def _stream(r, i):
@@ -123,3 +124,9 @@ def test_running_slot_kv_matches_oracle(run):
         np.testing.assert_array_equal(ks, rks, err_msg=f"key scales, layer {layer}")
         np.testing.assert_array_equal(vs, rvs, err_msg=f"value scales, layer {layer}")
     ref.close()
+
+
+def test_no_kernel_wrote_past_a_buffer(run):
+    """Every device buffer of the context is followed by guard bytes; after 600 scheduled steps at
+    this shape none of them has changed."""
+    assert run["guards"] == 0
