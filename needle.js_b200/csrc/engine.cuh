@@ -130,7 +130,7 @@ struct StepView {
   // selecting.  Their lanes are per item (`lanes`) instead of per slot, K/V are appended for the
   // whole chunk before any item attends, and the slot's state (position, token history, engram
   // ring) advances once, after the chunk.
-  // fast numerics: what the append pass (k_attention part 1) leaves for the int8-MMA attention
+  // fast numerics: what the append pass (k_attention part 1) leaves for the fast attention kernel
   float* qrope;             // [B][512] normalised, rotated queries
   float* attn_out;          // [B][512] attention output (before the gate)
   int32_t* attn_count;      // [B] visible cache slots: slots 0 .. count-1 in the ring layout

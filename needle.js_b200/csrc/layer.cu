@@ -814,7 +814,7 @@ __device__ void attend_pair_f32(const float* kf, const float* vf, int count, Slo
 }
 
 // part 0: append this item's K/V, then attend; part 1: append only (fast numerics attends with
-// another kernel); part 2: attend only; part 3: append the chunk items only; part 4: the chunk items
+// the fast attention kernel); part 2: attend only; part 3: append the chunk items only; part 4: the chunk items
 // attend, every other item appends and attends.  A step that holds chunk items runs parts 3 and 4:
 // every item of a chunk appends before any of them attends.
 template <int Sc, int Mix, int Mc>
@@ -912,8 +912,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
     __syncthreads();
   }
   if (!attend) {
-    // fast numerics attends with the int8-MMA kernel next: leave it the rotated queries, the visible
-    // count (slots 0 .. count-1 of the ring hold exactly the visible positions) and the cache row
+    // fast numerics attends with the fast attention kernel next (binary32 or int8-MMA): leave it the
+    // rotated queries, the visible count (slots 0 .. count-1 of the ring hold exactly the visible
+    // positions) and the cache row
     if (part == 1 && st.qrope) {
       st.qrope[(int64_t)b * kDim + 2 * h * kHeadDim + tid] = qv[tid];
       if (h == 0 && tid == 0) {
@@ -948,8 +949,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const ModelView m, c
   st.prep_o[(int64_t)b * kDim + h * kGroup + tid] = f32((double)outv[tid] * (1.0 / sqrt((double)kGroup)));
 }
 
-// Fast numerics: attentionOutput * sigmoid(gate) (runtime.ts:503-504) of the int8-MMA attention's
-// output, and the output projection's prepared input (heads 2h, 2h+1 are input group h).
+// Fast numerics: attentionOutput * sigmoid(gate) (runtime.ts:503-504) of the fast attention's output,
+// and the output projection's prepared input (heads 2h, 2h+1 are input group h).
 __global__ void __launch_bounds__(kAttnThreads) k_attention_gate(const StepView st) {
   __shared__ float outv[2 * kHeadDim];
   const int b = blockIdx.x, h = blockIdx.y;
