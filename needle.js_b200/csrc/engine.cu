@@ -352,7 +352,9 @@ struct needle_ctx {
   // host steps as micro-batches (needle_cuda_step): the captured step and its shape
   cudaGraphExec_t host_graph = nullptr;        // whole step
   cudaGraphExec_t host_graph_begin = nullptr;  // needle_cuda_step_begin's part (no selection)
-  int64_t host_graph_launches = 0, host_begin_launches = 0;
+  cudaGraphExec_t single_graph = nullptr;      // a one-item step (batch-1 decode)
+  int64_t host_graph_launches = 0, host_begin_launches = 0, single_launches = 0;
+  int single_eager_steps = 0;
   int host_eager_steps = 0, host_m = 0, host_cap = 0;
   std::vector<uint8_t> bytes;  // archive copy (host)
   Archive A;
@@ -1129,12 +1131,46 @@ void enqueue_host_mb(needle_ctx& C, int M, int cap, bool finish = true) {
 
 // Drops the captured host steps (their kernels hold buffer addresses that are about to change).
 void drop_host_graph(needle_ctx& C) {
-  if (!C.host_graph && !C.host_graph_begin) return;
+  if (!C.host_graph && !C.host_graph_begin && !C.single_graph) return;
   cudaStreamSynchronize(C.stream);
   if (C.host_graph) cudaGraphExecDestroy(C.host_graph);
   if (C.host_graph_begin) cudaGraphExecDestroy(C.host_graph_begin);
-  C.host_graph = C.host_graph_begin = nullptr;
+  if (C.single_graph) cudaGraphExecDestroy(C.single_graph);
+  C.host_graph = C.host_graph_begin = C.single_graph = nullptr;
   C.host_eager_steps = 0;
+  C.single_eager_steps = 0;
+}
+
+// A one-item host step (the batch-1 decode loop): its ~170 kernels as one graph replay after the
+// first eager run, so the GPU does not wait on launch gaps between the dependent kernels.
+void run_single(needle_ctx& C) {
+  auto enqueue = [&] { enqueue_step(C, C.stv, 1, true, nullptr, lane_a(C)); };
+  if (C.single_eager_steps < 1) {
+    enqueue();
+    C.single_eager_steps++;
+    return;
+  }
+  if (!C.single_graph) {
+    cuda_check(cudaStreamBeginCapture(C.stream, cudaStreamCaptureModeThreadLocal), "capture");
+    const int64_t l0 = C.launches;
+    try {
+      enqueue();
+    } catch (...) {
+      cudaGraph_t broken = nullptr;
+      cudaStreamEndCapture(C.stream, &broken);
+      if (broken) cudaGraphDestroy(broken);
+      throw;
+    }
+    C.single_launches = C.launches - l0;
+    C.launches = l0;
+    cudaGraph_t g = nullptr;
+    cuda_check(cudaStreamEndCapture(C.stream, &g), "capture");
+    const cudaError_t e = cudaGraphInstantiate(&C.single_graph, g, 0);
+    cudaGraphDestroy(g);
+    cuda_check(e, "cudaGraphInstantiate");
+  }
+  cuda_check(cudaGraphLaunch(C.single_graph, C.stream), "cudaGraphLaunch");
+  C.launches += C.single_launches;
 }
 
 // Runs a micro-batched host step's kernels: eagerly the first time, then as a replay of the step
@@ -1231,6 +1267,7 @@ void destroy(needle_ctx* C) {
   if (C->sched_graph) cudaGraphExecDestroy(C->sched_graph);
   if (C->host_graph) cudaGraphExecDestroy(C->host_graph);
   if (C->host_graph_begin) cudaGraphExecDestroy(C->host_graph_begin);
+  if (C->single_graph) cudaGraphExecDestroy(C->single_graph);
   if (C->split_ev) cudaEventDestroy(C->split_ev);
   for (int k = 1; k < kMaxMicro; k++) {
     for (int j = 0; j < 2; j++) {
@@ -1733,6 +1770,11 @@ int needle_cuda_step(needle_ctx* ctx, const needle_step_item* items, int32_t n, 
     upload_allowed(C, allowed_ids, allowed_total);
     const int rows = all_logits ? n : n_sel;
     upload_items(C, C.h_items, n, rows);
+    if (n == 1 && !all_logits && C.collecting == 0 && !C.profiling) {
+      run_single(C);
+      complete_step(C, items, n, rows, order, out_selected, out_logits);
+      return;
+    }
     StepView v = C.stv;
     v.chunk = chunks ? 1 : 0;
     enqueue_step(C, v, n, n_sel > 0 || all_logits, nullptr, lane_a(C));

@@ -167,3 +167,31 @@ def test_nvtx_ranges_do_not_change_a_step(archive, monkeypatch):
                 got.append(out)
             outs.append(got)
     assert outs[0] == outs[1]
+
+
+def test_one_item_steps_replay_a_graph(archive):
+    """One-item host steps (the batch-1 decode loop) run as a graph replay from their second on:
+    the same selections, log-probabilities and K/V as eager steps (steps that return logits run
+    eagerly), across a reset and a different slot."""
+    from needle_b200.backend import CudaEngine, StepRequest
+    rng = np.random.default_rng(14)
+    prompt = rng.integers(0, 8192, 9).astype(np.int32)
+    runs = []
+    for want_logits in (True, False):
+        with CudaEngine(archive, device=0, max_seqs=2, max_len=64, max_sink=0) as eng:
+            got = []
+            for slot in (0, 1, 0):
+                eng.reset(slot, 40, 0)
+                eng.prefill(slot, prompt[:-1], want_logits=False)
+                for k in range(12):
+                    out, _ = eng.step([StepRequest(slot, int(prompt[-1]) if k == 0 else -1, True)],
+                                      want_logits=want_logits)
+                    got.append(out[0])
+            kv = [eng.read_kv(s, layer) for s in (0, 1) for layer in (0, eng.layers - 1)]
+            assert eng.damaged_guards() == 0
+            runs.append((got, kv))
+    (ga, ka), (gb, kb) = runs
+    assert ga == gb
+    for a, b in zip(ka, kb):
+        for x, y in zip(a, b):
+            np.testing.assert_array_equal(x, y)
