@@ -445,7 +445,7 @@ def bench_attention(args, peaks):
             "roofline": {"kernel": "k_attention_fast_mma (+ k_attention_fast_combine)", "bound": "hbm", "achieved": head["gbs"],
                          "peak": peak, "peak_source": src, "unit": "GB/s", "frac": round(head["gbs"] / peak, 4),
                          # DRAM read + write of one k_attention_fast_mma launch at L = 8192 (ncu)
-                         "traffic": 150667520 if head["L"] == 8192 and head["numerics"] == "fast" else None,
+                         "traffic": 152468480 if head["L"] == 8192 and head["numerics"] == "fast" else None,
                          "traffic_source": "profiles/attention_fast_mma_L8192_batch64.md"},
             "gpu_launches": launches}
     if not args.no_cpu_baseline:
