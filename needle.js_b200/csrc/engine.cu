@@ -1141,7 +1141,7 @@ void drop_host_graph(needle_ctx& C) {
   C.single_eager_steps = 0;
 }
 
-// A one-item host step (the batch-1 decode loop): its ~170 kernels as one graph replay after the
+// A one-item host step (the batch-1 decode loop): its 140 kernels as one graph replay after the
 // first eager run, so the GPU does not wait on launch gaps between the dependent kernels.
 void run_single(needle_ctx& C) {
   auto enqueue = [&] { enqueue_step(C, C.stv, 1, true, nullptr, lane_a(C)); };
