@@ -1174,11 +1174,11 @@ def host_driven(eng, stream, prompts, gens, ramp, warmup, steps, chunk=0, items=
                     state[s] = None
         return resets, reqs, gen
 
-    def begin(resets, reqs):
+    def begin(resets, reqs, packed=None):
         for s, max_len in resets:
             eng.reset(s, max_len, 0)
         if reqs:
-            eng.step_begin(reqs)
+            eng.step_begin(reqs, packed)
 
     total = ramp + warmup + steps
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1187,6 +1187,7 @@ def host_driven(eng, stream, prompts, gens, ramp, warmup, steps, chunk=0, items=
     begin(resets, reqs)
     for i in range(total):
         nxt = plan() if i + 1 < total else None
+        packed = eng._items(nxt[1])[0] if nxt is not None and nxt[1] else None  # while step i runs
         if reqs:
             eng.step_end(reqs)
         if i >= ramp + warmup:
@@ -1199,7 +1200,7 @@ def host_driven(eng, stream, prompts, gens, ramp, warmup, steps, chunk=0, items=
             e0.record(stream)
         if nxt is not None:
             resets, reqs, g = nxt
-            begin(resets, reqs)
+            begin(resets, reqs, packed)
     e1.record(stream)
     torch.cuda.synchronize()
     return {"ms": e0.elapsed_time(e1), "generated": gen, "h2d": int(h2d / steps), "d2h": int(d2h / steps)}

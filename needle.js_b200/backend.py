@@ -146,10 +146,12 @@ class CudaEngine:
         out = [(sel[i].id, sel[i].log_probability) if r.select else None for i, r in enumerate(requests)]
         return out, logits
 
-    def step_begin(self, requests: Sequence[StepRequest]):
+    def step_begin(self, requests: Sequence[StepRequest], items: Optional[np.ndarray] = None):
         """First half of a step (needle_cuda_step_begin): the layers are enqueued and this returns at
-        once; the requests' allowed lists are not read.  step_end must follow before any other call."""
-        items, _ = self._items(requests)
+        once; the requests' allowed lists are not read.  step_end must follow before any other call.
+        `items`: the requests already packed by `_items` (e.g. while the previous step ran)."""
+        if items is None:
+            items, _ = self._items(requests)
         check(lib().needle_cuda_step_begin(self.h, ptr(items), len(requests)))
 
     def step_end(self, requests: Sequence[StepRequest]):
