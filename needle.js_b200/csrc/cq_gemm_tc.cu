@@ -415,26 +415,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_cq_gemm_tc(
               hi[j] = __byte_perm(t0, t1, 0x5410);
               lo[j] = __byte_perm(t0, t1, 0x7632);
             }
-            return;
-          }
+          } else {
 #pragma unroll
-          for (int wi = 0; wi < 16 / kPairsPerWord; wi++) {
-            const uint32_t w = wr[d][q * (16 / kPairsPerWord) + wi];
+            for (int wi = 0; wi < 16 / kPairsPerWord; wi++) {
+              const uint32_t w = wr[d][q * (16 / kPairsPerWord) + wi];
 #pragma unroll
-            for (int i = 0; i < kPairsPerWord; i++) {
-              uint32_t c0, c1;
-              if constexpr (BITS == 4) {
-                const uint32_t t = w & 0x0F0F0F0Fu, u = (w >> 4) & 0x0F0F0F0Fu;
-                c0 = __byte_perm(t, 0, 0x4440 | i);
-                c1 = __byte_perm(u, 0, 0x4440 | i);
-              } else {
-                const uint32_t t = w & 0x33333333u, u = (w >> 2) & 0x33333333u;
-                c0 = (t >> (4 * i)) & 3u;
-                c1 = (u >> (4 * i)) & 3u;
+              for (int i = 0; i < kPairsPerWord; i++) {
+                uint32_t c0, c1;
+                if constexpr (BITS == 4) {
+                  const uint32_t t = w & 0x0F0F0F0Fu, u = (w >> 4) & 0x0F0F0F0Fu;
+                  c0 = __byte_perm(t, 0, 0x4440 | i);
+                  c1 = __byte_perm(u, 0, 0x4440 | i);
+                } else {
+                  const uint32_t t = w & 0x33333333u, u = (w >> 2) & 0x33333333u;
+                  c0 = (t >> (4 * i)) & 3u;
+                  c1 = (u >> (4 * i)) & 3u;
+                }
+                const uint32_t t0 = tab[c0 * kTcDecodeThreads], t1 = tab[c1 * kTcDecodeThreads];
+                hi[wi * kPairsPerWord + i] = __byte_perm(t0, t1, 0x5410);
+                lo[wi * kPairsPerWord + i] = __byte_perm(t0, t1, 0x7632);
               }
-              const uint32_t t0 = tab[c0 * kTcDecodeThreads], t1 = tab[c1 * kTcDecodeThreads];
-              hi[wi * kPairsPerWord + i] = __byte_perm(t0, t1, 0x5410);
-              lo[wi * kPairsPerWord + i] = __byte_perm(t0, t1, 0x7632);
             }
           }
         };

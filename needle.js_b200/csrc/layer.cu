@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const Slo
   if (b >= *st.n_items) return;
   const int tid = threadIdx.x;
   const DevItem it = st.items[b];
-  const int slot = it.slot, p = it.position;
+  const int slot = it.slot;
   float* xg = it.chunk_len ? st.lanes + (int64_t)b * kLaneWidth : sv.x + (int64_t)slot * kLaneWidth;
   {
     float v[kLaneWidth / kThreads];  // all loads in flight before the first store
