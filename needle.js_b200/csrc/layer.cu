@@ -336,9 +336,12 @@ __device__ __forceinline__ double phase_sum(const double* terms, int n, double* 
   else return threadIdx.x == 0 ? sum_seq(terms, n) : 0.0;
 }
 
+// Three CTAs per SM (40 registers a thread, a few spilled): with many items per step the CTAs of
+// every micro-batch stay resident together (measured: 76.2 k against 72.4 k processed tokens/s at
+// two CTAs per SM, 72.6 k at four).
 template <bool Fast>
-__global__ void __launch_bounds__(kThreads) k_layer(const ModelView m, const SlotView sv, const StepView st,
-                                                  int layer) {
+__global__ void __launch_bounds__(kThreads, 3) k_layer(const ModelView m, const SlotView sv, const StepView st,
+                                                     int layer) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   LayerSmem& S = *reinterpret_cast<LayerSmem*>(smem_raw);
   const int b = blockIdx.x;
