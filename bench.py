@@ -888,6 +888,7 @@ def main():
     ap.add_argument("--sched-chunk", type=int, default=8,
                     help="decode: prompt positions a prefilling slot may take per scheduled step (0: one)")
     ap.add_argument("--sched-items", type=int, default=384, help="decode: items per scheduled step with chunks")
+    ap.add_argument("--micro-batches", type=int, default=8, help="decode: micro-batches per step (engine option)")
     ap.add_argument("--toolcall-chunk", type=int, default=0,
                     help="toolcall: prompt positions per slot and step (0: one; 512 slots already fill the GPU, "
                          "so chunks of 8 at 768 items per step measured 6 %% slower)")
@@ -917,6 +918,7 @@ def main():
               "kv_cache": "int8", "l2": "inputs larger than L2: the per-step KV working set is ~1 GB; the 13.7 MB "
                                         "of CQ weights stay L2-resident as in deployment",
               "parallelism": f"dp{args.gpus} (independent sequences per GPU, no collectives)",
+              "micro_batches": args.micro_batches,
               "prompt_chunks": ({"sched_chunk": args.sched_chunk, "sched_items": args.sched_items,
                                  "note": "a slot still reading its prompt takes up to sched_chunk positions per "
                                          "step (until its KV window would wrap) beside the other slots' single "
@@ -983,7 +985,8 @@ def main():
 
     n_seqs = SLOTS * 12
     prompts, gens = workload(rank, n_seqs)
-    chunking = dict(sched_chunk=args.sched_chunk, sched_items=args.sched_items if args.sched_chunk >= 2 else 0)
+    chunking = dict(sched_chunk=args.sched_chunk, sched_items=args.sched_items if args.sched_chunk >= 2 else 0,
+                    micro_batches=args.micro_batches)
     eng = CudaEngine(archive, device=device, max_seqs=SLOTS, max_len=PROMPT[1] + GEN[1], max_sink=0, **chunking)
     stream = torch.cuda.ExternalStream(eng.stream, device=device)
 

@@ -10,9 +10,10 @@ the oracle's one-sequence decode (NeedleModel.generate's greedy loop, packages/n
 model.ts:88-153; window and slots as runtime.ts:659-786), and a running slot's int8 K/V codes and
 scales, every layer, must equal the oracle runtime's after the same tokens.
 
-The same run again with prompt chunks (needle_opts.sched_chunk = 16, 512 items per step): slots
-still reading their prompts take up to 16 positions per step as a chunk of items beside the other
-slots' single items, until their window would wrap.  The reference reads a prompt one token at a
+The same run again with prompt chunks (needle_opts.sched_chunk = 16, 512 items per step; and the
+bench's shape: 8 positions, 384 items, eight micro-batches): slots still reading their prompts take
+several positions per step as a chunk of items beside the other slots' single items, until their
+window would wrap.  The reference reads a prompt one token at a
 time (runtime.ts:227-243), so the streams and the K/V must not change.
 """
 import concurrent.futures
@@ -27,8 +28,9 @@ STEPS = 600
 SLOTS = 256
 
 
-@pytest.fixture(scope="module", params=[{}, {"sched_chunk": 16, "sched_items": 512}],
-                ids=["one-position", "prompt-chunks"])
+@pytest.fixture(scope="module", params=[{}, {"sched_chunk": 16, "sched_items": 512},
+                                        {"sched_chunk": 8, "sched_items": 384, "micro_batches": 8}],
+                ids=["one-position", "prompt-chunks", "bench-shape"])
 def run(oracle, request):
     torch = pytest.importorskip("torch")
     if not torch.cuda.is_available():
