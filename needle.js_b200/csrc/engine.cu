@@ -349,6 +349,7 @@ struct needle_ctx {
   cudaGraphExec_t sched_graph = nullptr;
   int64_t graph_launches = 0;
   int sched_eager_steps = 0;
+  bool sched_inflight = false;  // scheduled steps enqueued since the stream was last drained
   // host steps as micro-batches (needle_cuda_step): the captured step and its shape
   cudaGraphExec_t host_graph = nullptr;        // whole step
   cudaGraphExec_t host_graph_begin = nullptr;  // needle_cuda_step_begin's part (no selection)
@@ -392,6 +393,7 @@ struct needle_ctx {
   uint32_t* d_mask_stage = nullptr;
   cudaEvent_t mask_staged = nullptr;  // recorded after the last staging copy
   DevItem* h_items_end = nullptr;  // the items as needle_cuda_step_end re-uploads them
+  SeqState* h_seq_stage = nullptr;  // pinned: each slot's state as needle_cuda_seq_reset uploads it
   float* h_lanes = nullptr;         // a resident-session item's lanes (pinned, kLaneWidth floats)
   uint32_t* h_engram = nullptr;     // and its engram lookup (pinned, 2 * kMaxTables)
   uint32_t* d_engram_in = nullptr;  // StepView::engram_in
@@ -786,6 +788,7 @@ void build_state(needle_ctx& C) {
   st.allowed = C.d_allowed;
   cuda_check(cudaMallocHost(&C.h_items, B * sizeof(DevItem)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_items_end, B * sizeof(DevItem)), "cudaMallocHost");
+  cuda_check(cudaMallocHost(&C.h_seq_stage, size_t(S) * sizeof(SeqState)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_lanes, kLaneWidth * sizeof(float)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_engram, 2 * kMaxTables * sizeof(uint32_t)), "cudaMallocHost");
   cuda_check(cudaMallocHost(&C.h_counts, (2 + 2 * kMaxMicro) * sizeof(int32_t)), "cudaMallocHost");
@@ -1251,6 +1254,7 @@ void destroy(needle_ctx* C) {
   if (C->d_row_out) cudaFree(C->d_row_out);
   if (C->h_items) cudaFreeHost(C->h_items);
   if (C->h_items_end) cudaFreeHost(C->h_items_end);
+  if (C->h_seq_stage) cudaFreeHost(C->h_seq_stage);
   if (C->h_lanes) cudaFreeHost(C->h_lanes);
   if (C->h_engram) cudaFreeHost(C->h_engram);
   if (C->h_counts) cudaFreeHost(C->h_counts);
@@ -1714,7 +1718,16 @@ int needle_cuda_seq_reset_ex(needle_ctx* ctx, int32_t seq, int32_t maximum_lengt
     require(kv_alloc <= C.sv.capacity, NEEDLE_BACKEND_UNAVAILABLE,
             "sink + window exceeds the context's KV capacity (raise max_sink / max_len)");
     const bool collect = collect_confidence != 0 && C.mv.probe_count > 0;
-    SeqState st{};
+    // the slot's state goes in from pinned staging, ordered before every later step on the stream
+    // (no wait here: a host loop resetting slots between steps keeps the GPU busy).  Host steps
+    // end synchronised; scheduled steps may still be queued, and one of them could read this slot
+    // between an earlier reset's copy and this one, so their work is drained first.
+    if (C.sched_inflight) {
+      cuda_check(cudaStreamSynchronize(C.stream), "reset");
+      C.sched_inflight = false;
+    }
+    SeqState& st = C.h_seq_stage[seq];
+    st = SeqState{};
     st.position = 0;
     st.sink = sink;
     st.max_len = maximum_length;
@@ -1722,7 +1735,6 @@ int needle_cuda_seq_reset_ex(needle_ctx* ctx, int32_t seq, int32_t maximum_lengt
     st.collect = collect ? 1 : 0;
     cuda_check(cudaMemcpyAsync(C.sv.seq + seq, &st, sizeof(st), cudaMemcpyHostToDevice, C.stream), "reset");
     if (collect) cuda_check(launch_pool_reset(C.mv, C.sv, seq, C.stream), "pool reset");
-    cuda_check(cudaStreamSynchronize(C.stream), "reset");
     SlotHost& h = C.slots[seq];
     C.collecting += int(collect) - int(h.collect);
     h.collect = collect;
@@ -2254,6 +2266,7 @@ int needle_cuda_sched_step(needle_ctx* ctx, int32_t steps) {
   return guarded([&] {
     needle_ctx& C = *ctx_of(ctx);
     require(C.sched_loaded, NEEDLE_BACKEND_UNAVAILABLE, "no scheduler queue loaded");
+    if (steps > 0) C.sched_inflight = true;
     for (int32_t k = 0; k < steps; k++) {
       if (C.profiling || C.sched_eager_steps < 1) {
         enqueue_sched_step(C);
