@@ -36,4 +36,4 @@ def test_roofline_traffic_and_bounds():
     assert bench.roofline_for(prof, 380, peaks)["traffic"] is None
     layer = bench.roofline_for({"layer": (20.0, 280)}, 380, peaks, sm_mhz=1965.0, state_chunk=8)
     assert layer["latency"]["chain_adds_per_item"] == 512 + 512 + 2048 + 512
-    assert abs(layer["latency"]["floor_ms"] - 3584 * 11 / 1965e3) < 1e-9
+    assert abs(layer["latency"]["floor_ms"] - 3584 * 11 / 1965e3) < 1e-5  # rounded to 5 decimals
