@@ -264,12 +264,14 @@ def roofline_for(prof, n_items, peaks, visible=None, sm_mhz=None, state_chunk=No
     return line
 
 
-QMATVEC_SHAPES = [  # (name, rows, inputs, record bits) -- every Needle 2 projection + the stress shape
+QMATVEC_SHAPES = [  # (name, rows, inputs, record bits) -- every Needle 2 projection, the stress shape and
+    # the four 2-bit projections of a layer stacked (one launch of the exact engine step)
     ("query/gate 512x512 CQ2", 512, 512, 2), ("key/value 256x512 CQ2", 256, 512, 2),
     ("output 512x512 CQ3", 512, 512, 3), ("phi_pre/post layer slice 4x2048 CQ4", 4, 2048, 4),
     ("phi_res layer slice 16x2048 CQ4", 16, 2048, 4), ("phi_pre/post 108x2048 CQ4", 108, 2048, 4),
     ("phi_res 432x2048 CQ4", 432, 2048, 4), ("engram key/value 512x512 ternary", 512, 512, 5),
-    ("vocabulary 8192x512 CQ4", 8192, 512, 4), ("stress 8192x8192 CQ4", 8192, 8192, 4)]
+    ("vocabulary 8192x512 CQ4", 8192, 512, 4), ("stress 8192x8192 CQ4", 8192, 8192, 4),
+    ("query|key|value|gate stacked 1536x512 CQ2", 1536, 512, 2)]
 ROTATE_BYTES = 256 << 20  # rotated operand sets exceed the 126 MB L2 twice over
 
 

@@ -431,15 +431,284 @@ static cudaError_t launch_gemv_variant(CqJobs J, const Codebook& cb, int32_t n_h
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ byte-table GEMV (2-bit, many items)
+//
+// For a 2-bit row the reference's inner step is a whole byte: the four column products of the
+// byte's crumbs, summed left to right, then added to the group's dot (cq.ts:137-153).  That byte
+// term depends only on the byte's value and on the item's four inputs of that column quad, so for
+// one (item, group) a table
+//     T[b][j] = fma(l(c3), x[4j+3], fma(l(c2), x[4j+2], fma(l(c1), x[4j+1], l(c0) * x[4j])))
+// (b = c3 c2 c1 c0 in crumbs, 256 x 32 binary64 = 64 KB) holds every term the rows can need, built
+// with exactly the operations the per-byte chain performs, and a row's group dot becomes 32 table
+// reads and 32 adds in byte order -- the same values in the same order, a quarter of the binary64
+// operations and a third of the instructions.  The table is shared by every row of the launch's
+// jobs, which must therefore read one input (the Q, K, V and gate projections of a layer do).
+//
+// A CTA owns one item and a part of the rows; thread t streams rows t, t + 256, ... of its part.
+// All lanes of a warp would read column j of the table at once, with random bytes b -- a 16-way bank
+// conflict.  So lane l runs d = l mod 16 bytes behind lane l - d: at step i it reads column
+// (i - d) mod 32, and the 16 lanes of each half-warp read 16 different columns (conflict-free).
+// During the block of 32 steps that starts row k, a lane spends its first d steps on the last d
+// bytes of row k - 1 and the rest on the first 32 - d bytes of row k: a 32-byte window at offset
+// 32 - d of the two rows' bytes, rotated into registers once per block.
+namespace {
+
+constexpr int kTableThreads = 256;
+constexpr int kTableMaxRounds = 6;  // rows per thread and part: parts have at most 1536 rows
+constexpr int kTableMinItems = 64;  // below this the tile kernel (more CTAs per item) is faster
+constexpr int kTableBytes = 256 * 32 * 8;
+
+// Row `rr` of the launch (jobs in order; tile_begin holds each job's first row here): its job and
+// matrix row.
+__device__ __forceinline__ const CqJob& table_row(const CqJobs& J, int rr, int& prow, int& local) {
+  int j = 0;
+#pragma unroll 1
+  for (int k = 1; k < J.count; k++)
+    if (rr >= J.job[k].tile_begin) j = k;
+  local = rr - J.job[j].tile_begin;
+  prow = J.job[j].row_start + local;
+  return J.job[j];
+}
+
+// T[b][j] for one item's group.  Thread (j = t mod 32, h = t / 32) holds the group's inputs
+// 4j .. 4j + 3 in xq and writes the 32 bytes whose top three bits are h; the partial sums of the
+// two low crumbs are shared by them.
+__device__ __forceinline__ void build_byte_table(double* __restrict__ T, const float xq[4], const double lut[4]) {
+  const int t = threadIdx.x, j = t & 31, hb = t >> 5;
+  const double x0 = (double)xq[0], x1 = (double)xq[1], x2 = (double)xq[2], x3 = (double)xq[3];
+  double s01[16];  // [c1 * 4 + c0]
+#pragma unroll
+  for (int c0 = 0; c0 < 4; c0++) {
+    const double p0 = lut[c0] * x0;
+#pragma unroll
+    for (int c1 = 0; c1 < 4; c1++) s01[c1 * 4 + c0] = fma(lut[c1], x1, p0);
+  }
+  auto level = [&](int c) { return c == 0 ? lut[0] : c == 1 ? lut[1] : c == 2 ? lut[2] : lut[3]; };
+  const double a3 = level(hb >> 1);
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const double a2 = level(((hb & 1) << 1) | h);
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const double s = fma(a2, x2, s01[k]);
+      T[(((hb << 5) | (h << 4) | k) << 5) + j] = fma(a3, x3, s);
+    }
+  }
+}
+
+// Row `rr` of the launch, group g: its 32 bytes and its raw fp16 norm.  Row-major matrices keep a
+// row's groups together (row_bytes apart per row); group-major ones ([group][row][32 bytes], row_bytes
+// = the stride between groups) keep a group's rows together, so the 32 rows a warp reads are 1 KB.
+template <bool kGroupMajor>
+__device__ __forceinline__ void load_table_row(const CqJobs& J, int rr, int g, int groups, uint4& n0, uint4& n1,
+                                               uint16_t& nn) {
+  int prow, local;
+  const CqJob& jb = table_row(J, rr, prow, local);
+  const int64_t at = kGroupMajor ? (int64_t)g * jb.row_bytes + (int64_t)prow * (kGroup / 4)
+                                 : (int64_t)prow * jb.row_bytes + g * (kGroup / 4);
+  const uint4* p = reinterpret_cast<const uint4*>(jb.packed + at);
+  n0 = __ldg(p);
+  n1 = __ldg(p + 1);
+  nn = __ldg(jb.norms + (int64_t)prow * groups + g);
+}
+
+// w = bytes [e, e + 32) of prev || cur (e in 17..32).
+__device__ __forceinline__ void table_window(const uint32_t prev[8], const uint32_t cur[8], int e, uint32_t w[8]) {
+  uint32_t s[13];  // words 4 .. 16 of prev || cur || 0
+#pragma unroll
+  for (int i = 0; i < 13; i++) s[i] = i < 4 ? prev[4 + i] : i < 12 ? cur[i - 4] : 0u;
+  const int r = (e >> 2) - 4;  // 0 .. 4
+  const uint32_t sh = 8u * uint32_t(e & 3);
+#pragma unroll
+  for (int i = 0; i < 9; i++) s[i] = (r & 4) ? s[i + 4] : s[i];
+#pragma unroll
+  for (int i = 0; i < 11; i++) s[i] = (r & 2) ? s[i + 2] : s[i];
+#pragma unroll
+  for (int i = 0; i < 9; i++) s[i] = (r & 1) ? s[i + 1] : s[i];
+#pragma unroll
+  for (int m = 0; m < 8; m++) w[m] = __funnelshift_r(s[m], s[m + 1], sh);
+}
+
+template <bool kGroupMajor>
+__global__ void __launch_bounds__(kTableThreads, 3)
+k_cq_gemv2_table(const CqJobs J, const Codebook cb, int32_t n_host, const int32_t* n_dev, int32_t parts,
+                 int32_t part_rows) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  double* T = reinterpret_cast<double*>(smem_raw);  // [256][32]
+  const char* Tb = reinterpret_cast<const char*>(smem_raw);
+  const int n = item_count(n_host, n_dev);
+  const int item = blockIdx.x / parts, part = blockIdx.x - item * parts;
+  if (item >= n) return;  // the whole CTA, before any barrier
+  const int t = threadIdx.x, lane = t & 31;
+  const int r0 = part * part_rows, r1 = min(J.total_tiles, r0 + part_rows);
+  const int rounds = (r1 - r0 + kTableThreads - 1) / kTableThreads;  // <= kTableMaxRounds
+  const CqJob& f = J.job[0];
+  const int groups = f.in_pad / kGroup;
+  const float* xi = f.x + (int64_t)item * f.x_stride;
+  double lut[4];
+#pragma unroll
+  for (int c = 0; c < 4; c++) lut[c] = (double)cb.v[c];
+  const int d = lane & 15, e = 32 - d;
+  const uint32_t jd8 = uint32_t((32 - d) & 31) * 8u;  // byte offset of column (i - d) mod 32, at i = 0
+  double tot[kTableMaxRounds];
+#pragma unroll
+  for (int k = 0; k < kTableMaxRounds; k++) tot[k] = 0.0;
+
+  // Every global read is issued a block (a row's bytes and norm) or a group (the table's inputs,
+  // the group's first row) before its use: the lookups hide their latency.
+  const int jq = t & 31;
+  float xq[4];
+#pragma unroll
+  for (int c = 0; c < 4; c++) xq[c] = xi[4 * jq + c];
+  uint4 n0 = make_uint4(0u, 0u, 0u, 0u), n1 = n0;
+  uint16_t nn = 0;  // raw fp16 norm of the row in n0 / n1
+  if (r0 + t < r1) load_table_row<kGroupMajor>(J, r0 + t, 0, groups, n0, n1, nn);
+
+#pragma unroll 1
+  for (int g = 0; g < groups; g++) {
+    if (g > 0) __syncthreads();  // every lookup of the previous group is done
+    build_byte_table(T, xq, lut);
+    __syncthreads();
+    if (g + 1 < groups) {
+#pragma unroll
+      for (int c = 0; c < 4; c++) xq[c] = xi[(g + 1) * kGroup + 4 * jq + c];
+    }
+    uint32_t prev[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    uint16_t norm_prev = 0;
+    double acc_prev = 0.0, acc_cur = 0.0;
+#pragma unroll
+    for (int k = 0; k <= kTableMaxRounds; k++) {
+      if (k > rounds) break;
+      const uint32_t cur[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+      const uint16_t norm_cur = nn;
+      n0 = make_uint4(0u, 0u, 0u, 0u);
+      n1 = n0;
+      nn = 0;
+      const int rn = r0 + t + (k + 1) * kTableThreads;  // next row of this thread
+      if (k + 1 < rounds) {
+        if (rn < r1) load_table_row<kGroupMajor>(J, rn, g, groups, n0, n1, nn);
+      } else if (k == rounds && g + 1 < groups && r0 + t < r1) {
+        load_table_row<kGroupMajor>(J, r0 + t, g + 1, groups, n0, n1, nn);  // the next group's first row
+      }
+      uint32_t w[8];
+      table_window(prev, cur, e, w);
+      acc_cur = 0.0;
+      if (k < rounds) {
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const uint32_t b8 = __byte_perm(w[i >> 2], 0u, 0x4404u | (uint32_t(i & 3) << 4));  // byte << 8
+          const uint32_t off = b8 | ((jd8 + 8u * uint32_t(i)) & 255u);
+          const double v = *reinterpret_cast<const double*>(Tb + off);
+          if (i < 16 && i < d)
+            acc_prev = acc_prev + v;  // the last d bytes of row k - 1
+          else
+            acc_cur = acc_cur + v;
+        }
+      } else {  // drain: the last d bytes of the final row
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const uint32_t b8 = __byte_perm(w[i >> 2], 0u, 0x4404u | (uint32_t(i & 3) << 4));
+          const uint32_t off = b8 | ((jd8 + 8u * uint32_t(i)) & 255u);
+          const double v = *reinterpret_cast<const double*>(Tb + off);
+          if (i < d) acc_prev = acc_prev + v;
+        }
+      }
+      if (k >= 1 && r0 + t + (k - 1) * kTableThreads < r1) {
+        // row k - 1 is complete: fold its group dot into the total (cq.ts:151)
+        const double nrm = (double)__half2float(__ushort_as_half(norm_prev));
+        tot[k - 1] = tot[k - 1] + nrm * acc_prev;
+      }
+      acc_prev = acc_cur;
+      norm_prev = norm_cur;
+#pragma unroll
+      for (int m = 0; m < 8; m++) prev[m] = cur[m];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kTableMaxRounds; k++) {
+    const int rr = r0 + t + k * kTableThreads;
+    if (k < rounds && rr < r1) {
+      int prow, local;
+      const CqJob& jb = table_row(J, rr, prow, local);
+      jb.y[(int64_t)item * jb.y_stride + local] = f32(tot[k]);
+    }
+  }
+}
+
+// The byte-table kernel applies to launches of 2-bit jobs that share one input, with 16-byte
+// aligned rows, from kTableMinItems items.
+bool table_gemv_applies(const CqJobs& J, int32_t n_host) {
+  if (n_host < kTableMinItems || J.count <= 0) return false;
+  const CqJob& f = J.job[0];
+  if (f.in_pad <= 0 || f.in_pad % kGroup) return false;
+  for (int k = 0; k < J.count; k++) {
+    const CqJob& j = J.job[k];
+    if (j.bits != 2 || j.x != f.x || j.x_stride != f.x_stride || j.in_pad != f.in_pad) return false;
+    if (j.row_bytes % 16 || reinterpret_cast<uintptr_t>(j.packed) % 16 || j.row_bytes < f.in_pad / 4) return false;
+  }
+  return true;
+}
+
+template <bool kGroupMajor>
+cudaError_t launch_gemv_table(CqJobs J, const Codebook& cb, int32_t n_host, const int32_t* n_dev, cudaStream_t s) {
+  static std::atomic<uint64_t> configured{0};  // per device: 64 KB dynamic shared memory opt-in
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    e = cudaFuncSetAttribute(k_cq_gemv2_table<kGroupMajor>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTableBytes);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit);
+  }
+  int rows = 0;
+  for (int k = 0; k < J.count; k++) {
+    J.job[k].tile_begin = rows;  // first row of the job in the launch
+    rows += J.job[k].rows;
+  }
+  J.total_tiles = rows;  // rows of the launch
+  if (rows <= 0) return cudaSuccess;
+  constexpr int kPartMax = kTableThreads * kTableMaxRounds;
+  // Two parts per item below two CTAs per SM's worth of items (more CTAs to spread), as long as a
+  // part keeps three rows per thread; more parts only where the rows need them.
+  int parts = (rows + kPartMax - 1) / kPartMax;
+  if (n_host < 296 && rows >= 2 * 3 * kTableThreads) parts = std::max(parts, 2);
+  const int part_rows = (rows + parts - 1) / parts;
+  const int64_t grid = (int64_t)n_host * parts;
+  if (grid > 0x7fffffff) return cudaErrorInvalidValue;
+  k_cq_gemv2_table<kGroupMajor>
+      <<<(unsigned)grid, kTableThreads, kTableBytes, s>>>(J, cb, n_host, n_dev, parts, part_rows);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
 // Tile shape of the batched exact GEMV: two rows per thread (64-row tiles) and four items per
-// tile measured best at 64-256 items (against 1 x 4, 1 x 8 and 2 x 8).
+// tile measured best at 64-256 items (against 1 x 4, 1 x 8 and 2 x 8).  2-bit launches of many
+// items that share one input take the byte-table kernel instead (the same operations in the same
+// order, so the same bits).
 cudaError_t launch_cq_gemv(const CqJobs& jobs, const Codebook& cb, int32_t n_host,
                            const int32_t* n_dev, cudaStream_t s) {
   if (n_host <= 0 || jobs.count <= 0) return cudaSuccess;
   const int bits = jobs.job[0].bits;
   for (int k = 1; k < jobs.count; k++)
     if (jobs.job[k].bits != bits) return cudaErrorInvalidValue;
+  if (table_gemv_applies(jobs, n_host)) return launch_gemv_table<false>(jobs, cb, n_host, n_dev, s);
   return launch_gemv_variant<2, 4>(jobs, cb, n_host, n_dev, s);
+}
+
+bool cq_gemv2_group_major_preferred(int32_t n_host) { return n_host >= kTableMinItems; }
+
+cudaError_t launch_cq_gemv2_group_major(const CqJob& job, const Codebook& cb, int32_t n_host, const int32_t* n_dev,
+                                        cudaStream_t s) {
+  if (n_host <= 0 || job.rows <= 0) return cudaSuccess;
+  if (job.bits != 2 || job.in_pad <= 0 || job.in_pad % kGroup || job.row_bytes % 16 ||
+      job.row_bytes < job.rows * (kGroup / 4) || reinterpret_cast<uintptr_t>(job.packed) % 16)
+    return cudaErrorInvalidValue;
+  CqJobs J{};
+  J.job[0] = job;
+  J.count = 1;
+  return launch_gemv_table<true>(J, cb, n_host, n_dev, s);
 }
 
 cudaError_t launch_cq_rows(const uint8_t* packed, const uint16_t* norms, int32_t bits,

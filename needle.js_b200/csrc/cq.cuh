@@ -46,6 +46,12 @@ cudaError_t launch_cq_prepare(const float* x, int32_t x_stride, int32_t input_si
                               cudaStream_t s);
 cudaError_t launch_cq_gemv(const CqJobs& jobs, const Codebook& cb, int32_t n_host,
                            const int32_t* n_dev, cudaStream_t s);
+// Exact 2-bit GEMV of one group-major matrix ([group][row][32 bytes]; job.row_bytes = the byte
+// stride between groups, at least rows * 32): the byte-table kernel with contiguous row loads.  The
+// engine keeps its Q|K|V|gate projections in this layout too; preferred from the item count on.
+bool cq_gemv2_group_major_preferred(int32_t n_host);
+cudaError_t launch_cq_gemv2_group_major(const CqJob& job, const Codebook& cb, int32_t n_host, const int32_t* n_dev,
+                                        cudaStream_t s);
 // Small-batch path for long rows (cq.cu): per-(row, group) dots of (row tile, group chunk) units
 // into `scratch` (cq_gemv_split_scratch_bytes), then ordered per-row totals.
 bool cq_gemv_prefers_split(const CqJob& job, int32_t n);

@@ -373,6 +373,9 @@ struct needle_ctx {
   bool fast_attention = false;  // NEEDLE_NUMERICS_FAST_ATTENTION: int8-MMA attention (else binary32)
   int sms = 0;
   std::vector<CqMat> lqkvg, ekv;
+  // Exact numerics: Q|K|V|gate of each layer stacked group-major for the byte-table GEMV (empty when
+  // the four are not all 2-bit rows of one input length).
+  std::vector<CqMat> lqkvg_gm;
   void* gemm_scratch[kMaxMicro] = {};
   size_t gemm_scratch_bytes = 0;
   void* attn_scratch[kMaxMicro] = {};  // the fast attention's partials and counters, per lane
@@ -546,6 +549,38 @@ CqMat stack_rows(needle_ctx& C, std::initializer_list<CqMat> parts) {
   return m;
 }
 
+// 2-bit matrices of one input length stacked row-wise in group-major order: [group][row][32 bytes]
+// (row_bytes of the result = the stride between groups), fp16 norms stacked row-major as usual.
+// Returns an empty matrix (rows 0) when the parts do not qualify.
+CqMat stack_group_major(needle_ctx& C, std::initializer_list<CqMat> parts) {
+  const CqMat& f = *parts.begin();
+  int rows = 0;
+  for (const CqMat& p : parts) {
+    if (p.bits != 2 || p.in_pad != f.in_pad || p.input_size != f.input_size || p.row_bytes != p.in_pad / 4)
+      return CqMat{};
+    rows += p.rows;
+  }
+  const int groups = f.in_pad / kGroup;
+  constexpr int kRecord = kGroup / 4;  // bytes of one (row, group) record
+  uint8_t* packed = C.dalloc<uint8_t>(size_t(groups) * rows * kRecord + 64);
+  uint16_t* norms = C.dalloc<uint16_t>(size_t(rows) * groups + 8, false);
+  size_t r0 = 0;
+  for (const CqMat& p : parts) {
+    for (int g = 0; g < groups; g++)
+      cuda_check(cudaMemcpy2D(packed + (size_t(g) * rows + r0) * kRecord, kRecord, p.packed + size_t(g) * kRecord,
+                              size_t(p.row_bytes), kRecord, size_t(p.rows), cudaMemcpyDeviceToDevice),
+                 "group-major stack");
+    cuda_check(cudaMemcpy(norms + r0 * groups, p.norms, size_t(p.rows) * groups * 2, cudaMemcpyDeviceToDevice), "stack");
+    r0 += p.rows;
+  }
+  CqMat m = f;
+  m.packed = packed;
+  m.norms = norms;
+  m.rows = rows;
+  m.row_bytes = rows * kRecord;
+  return m;
+}
+
 const float* upload_floats(needle_ctx& C, const std::vector<float>& v) {
   float* d = C.dalloc<float>(v.size(), false);
   cuda_check(cudaMemcpy(d, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice), "upload");
@@ -655,6 +690,15 @@ void build_model(needle_ctx& C) {
   if (C.fast) {
     for (int l = 0; l < L; l++) C.lqkvg.push_back(stack_rows(C, {C.lq[l], C.lk[l], C.lv[l], C.lg[l]}));
     for (int s = 0; s < m.n_sites; s++) C.ekv.push_back(stack_rows(C, {C.ek[s], C.ev[s]}));
+  } else {
+    for (int l = 0; l < L; l++) {
+      CqMat gm = stack_group_major(C, {C.lq[l], C.lk[l], C.lv[l], C.lg[l]});
+      if (gm.rows == 0) {
+        C.lqkvg_gm.clear();
+        break;
+      }
+      C.lqkvg_gm.push_back(gm);
+    }
   }
   m.norm_input = upload_floats(C, pack_layers(C, &Roles::L::norm_input, kDim));
   m.query_norm = upload_floats(C, pack_layers(C, &Roles::L::qn, kHeadDim));
@@ -962,7 +1006,21 @@ void enqueue_step(needle_ctx& C, const StepView& st, int n_host, bool any_select
     if (C.fast)
       run_gemv(C, P_GEMV_QKVG, {{C.lqkvg[l], 0, 1536, st.prep_a, kDim, st.qkvg, 1536}}, n_host, n_dev, s0,
                lane.index);
-    else
+    else if (!C.lqkvg_gm.empty() && cq_gemv2_group_major_preferred(n_host)) {
+      const CqMat& M = C.lqkvg_gm[l];
+      CqJob j{};
+      j.packed = M.packed;
+      j.norms = M.norms;
+      j.rows = M.rows;
+      j.in_pad = M.in_pad;
+      j.bits = M.bits;
+      j.row_bytes = M.row_bytes;
+      j.x = st.prep_a;
+      j.x_stride = kDim;
+      j.y = st.qkvg;
+      j.y_stride = 1536;
+      C.timed(P_GEMV_QKVG, [&] { return launch_cq_gemv2_group_major(j, C.mv.cb, n_host, n_dev, s0); }, s0);
+    } else
       run_gemv(C, P_GEMV_QKVG,
                {{C.lq[l], 0, 512, st.prep_a, kDim, st.qkvg, 1536},
                 {C.lk[l], 0, 256, st.prep_a, kDim, st.qkvg + 512, 1536},

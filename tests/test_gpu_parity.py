@@ -101,6 +101,34 @@ def test_cq_matvec_dev_long_rows_small_batch_bit_exact(torch_cuda, oracle, bits,
         np.testing.assert_array_equal(y[b], m.matvec(x[b]), err_msg=f"batch item {b}")
 
 
+@pytest.mark.parametrize("rows,inputs,batch", [(1536, 512, 64), (1536, 512, 300), (2000, 128, 100),
+                                               (77, 256, 64), (8192, 512, 70), (5, 384, 65)])
+def test_cq_matvec_dev_byte_table_bit_exact(torch_cuda, oracle, rows, inputs, batch):
+    """2-bit launches of 64 items or more take the byte-table kernel: one item per CTA and up to
+    1536 rows per part (two parts below 296 items; six for 8192 rows), every group dot read from a
+    per-(item, group) table of byte terms with the lanes skewed across the table's columns.  Same
+    bits as the oracle, including rows that end inside a part and parts with fewer rows than
+    threads."""
+    torch = torch_cuda
+    from needle_b200 import native, synth
+    packed, norms = synth.random_cq_matrix(rows, inputs, 2, seed=rows + batch)
+    cb = codebook()
+    x = synth.normal(6, batch * inputs, stream=11).astype(np.float32).reshape(batch, inputs)
+    x[1, :] = 0.0  # an all-zero item: every term and dot is +0
+    d_packed = torch.from_numpy(packed.copy()).cuda()
+    d_norms = torch.from_numpy(norms.view(np.int16).copy()).cuda()
+    d_x = torch.from_numpy(x).cuda()
+    d_y = torch.full((batch, rows), float("nan"), dtype=torch.float32, device="cuda")
+    desc = native.CqMatrixDesc(d_packed.data_ptr(), d_norms.data_ptr(), rows, inputs, 128, 2)
+    native.check(native.lib().needle_cuda_cq_matvec_dev(C.byref(desc), native.ptr(cb), d_x.data_ptr(), batch,
+                                                        d_y.data_ptr(), None))
+    torch.cuda.synchronize()
+    m = oracle.CqMatrix(rows, inputs, 128, 2, packed, norms, cb[:4], cb[4:12], cb[12:])
+    y = d_y.cpu().numpy()
+    for b in range(batch):
+        np.testing.assert_array_equal(y[b], m.matvec(x[b]), err_msg=f"batch item {b}")
+
+
 @pytest.mark.parametrize("cap", [8192, 8190])
 def test_attention_dev_fast_within_tolerance(torch_cuda, oracle, cap):
     """Fast numerics (binary32, online softmax, split positions) vs the oracle's binary64 attention:
