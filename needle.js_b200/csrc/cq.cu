@@ -454,7 +454,7 @@ static cudaError_t launch_gemv_variant(CqJobs J, const Codebook& cb, int32_t n_h
 namespace {
 
 constexpr int kTableThreads = 256;
-constexpr int kTableMaxRounds = 6;  // rows per thread and part: parts have at most 1536 rows
+constexpr int kTableMaxPasses = 6;  // rows per thread and part: parts have at most 1536 rows
 constexpr int kTableMinItems = 64;  // below this the tile kernel (more CTAs per item) is faster
 constexpr int kTableBytes = 256 * 32 * 8;
 
@@ -541,7 +541,7 @@ k_cq_gemv2_table(const CqJobs J, const Codebook cb, int32_t n_host, const int32_
   if (item >= n) return;  // the whole CTA, before any barrier
   const int t = threadIdx.x, lane = t & 31;
   const int r0 = part * part_rows, r1 = min(J.total_tiles, r0 + part_rows);
-  const int rounds = (r1 - r0 + kTableThreads - 1) / kTableThreads;  // <= kTableMaxRounds
+  const int passes = (r1 - r0 + kTableThreads - 1) / kTableThreads;  // <= kTableMaxPasses
   const CqJob& f = J.job[0];
   const int groups = f.in_pad / kGroup;
   const float* xi = f.x + (int64_t)item * f.x_stride;
@@ -550,9 +550,9 @@ k_cq_gemv2_table(const CqJobs J, const Codebook cb, int32_t n_host, const int32_
   for (int c = 0; c < 4; c++) lut[c] = (double)cb.v[c];
   const int d = lane & 15, e = 32 - d;
   const uint32_t jd8 = uint32_t((32 - d) & 31) * 8u;  // byte offset of column (i - d) mod 32, at i = 0
-  double tot[kTableMaxRounds];
+  double tot[kTableMaxPasses];
 #pragma unroll
-  for (int k = 0; k < kTableMaxRounds; k++) tot[k] = 0.0;
+  for (int k = 0; k < kTableMaxPasses; k++) tot[k] = 0.0;
 
   // Every global read is issued a block (a row's bytes and norm) or a group (the table's inputs,
   // the group's first row) before its use: the lookups hide their latency.
@@ -577,23 +577,23 @@ k_cq_gemv2_table(const CqJobs J, const Codebook cb, int32_t n_host, const int32_
     uint16_t norm_prev = 0;
     double acc_prev = 0.0, acc_cur = 0.0;
 #pragma unroll
-    for (int k = 0; k <= kTableMaxRounds; k++) {
-      if (k > rounds) break;
+    for (int k = 0; k <= kTableMaxPasses; k++) {
+      if (k > passes) break;
       const uint32_t cur[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
       const uint16_t norm_cur = nn;
       n0 = make_uint4(0u, 0u, 0u, 0u);
       n1 = n0;
       nn = 0;
       const int rn = r0 + t + (k + 1) * kTableThreads;  // next row of this thread
-      if (k + 1 < rounds) {
+      if (k + 1 < passes) {
         if (rn < r1) load_table_row<kGroupMajor>(J, rn, g, groups, n0, n1, nn);
-      } else if (k == rounds && g + 1 < groups && r0 + t < r1) {
+      } else if (k == passes && g + 1 < groups && r0 + t < r1) {
         load_table_row<kGroupMajor>(J, r0 + t, g + 1, groups, n0, n1, nn);  // the next group's first row
       }
       uint32_t w[8];
       table_window(prev, cur, e, w);
       acc_cur = 0.0;
-      if (k < rounds) {
+      if (k < passes) {
 #pragma unroll
         for (int i = 0; i < 32; i++) {
           const uint32_t b8 = __byte_perm(w[i >> 2], 0u, 0x4404u | (uint32_t(i & 3) << 4));  // byte << 8
@@ -625,9 +625,9 @@ k_cq_gemv2_table(const CqJobs J, const Codebook cb, int32_t n_host, const int32_
     }
   }
 #pragma unroll
-  for (int k = 0; k < kTableMaxRounds; k++) {
+  for (int k = 0; k < kTableMaxPasses; k++) {
     const int rr = r0 + t + k * kTableThreads;
-    if (k < rounds && rr < r1) {
+    if (k < passes && rr < r1) {
       int prow, local;
       const CqJob& jb = table_row(J, rr, prow, local);
       jb.y[(int64_t)item * jb.y_stride + local] = f32(tot[k]);
@@ -668,7 +668,7 @@ cudaError_t launch_gemv_table(CqJobs J, const Codebook& cb, int32_t n_host, cons
   }
   J.total_tiles = rows;  // rows of the launch
   if (rows <= 0) return cudaSuccess;
-  constexpr int kPartMax = kTableThreads * kTableMaxRounds;
+  constexpr int kPartMax = kTableThreads * kTableMaxPasses;
   // Two parts per item below two CTAs per SM's worth of items (more CTAs to spread), as long as a
   // part keeps three rows per thread; more parts only where the rows need them.
   int parts = (rows + kPartMax - 1) / kPartMax;
